@@ -1,0 +1,704 @@
+/*
+ * tvq_oracle.c -- CPU restatement of TokenVector.Inference's post-training-
+ * quantization (PTQ) linear path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the checker for the CUDA path in
+ * tokenvector/inference_b200: only tests/, __graft_entry__.smoke() and the
+ * cpu_baseline / --impl reference legs of bench.py may load it.  The product
+ * never calls it and has no CPU fallback.
+ *
+ * Every function restates one function of the reference (.tkv source, cited as
+ * path:line relative to the reference repository root).  The reference is
+ * written in TokenVector, compiled to .NET IL by an external compiler that is
+ * not available here, so it cannot be run; this file is the executable model.
+ *
+ * Numeric model (the reference compiler's, see docs/HANDOFF.md:3663 "JIT widen
+ * f64, truncate at the typed boundary"): untyped locals and every arithmetic
+ * expression are binary64; a value is rounded to binary32 only where it is
+ * stored into something typed 'f32' (list[f32] elements, f32 fields, f32
+ * parameters and return values).  `round` is .NET Math.Round (half to even),
+ * `int()` truncates and, as on .NET 9+, saturates with NaN -> 0.  The file is
+ * compiled with -ffp-contract=off so no multiply-add is fused.
+ *
+ * Parity pins: calibrate_minmax, quantize/dequantize round trip and the FP8
+ * round trip are pinned by the reference's own tests (tv/tests/gap_tests.tkv:
+ * 159-240); MatMulInteger and DynamicQuantizeLinear by
+ * tv/tests/inference_tests.tkv:847-989.  The INT8 GEMM, per-channel quantize
+ * and the f64 epilogue model have no reference test or fixture: their parity
+ * is unpinned beyond this restatement.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#include <float.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define TVO_API __attribute__((visibility("default")))
+
+/* ---------------------------------------------------------------------- */
+/* .NET-style conversions                                                  */
+/* ---------------------------------------------------------------------- */
+
+/* int(round(v)) with .NET 9+ saturating conversion (NaN -> 0). */
+static inline int64_t net_round_to_i64(double v) {
+    if (isnan(v)) return 0;
+    double r = nearbyint(v);               /* half to even in the default mode */
+    if (r >= 9.2233720368547758e18) return INT64_MAX;
+    if (r <= -9.2233720368547758e18) return INT64_MIN;
+    return (int64_t)r;
+}
+
+static inline int64_t clamp_i64(int64_t v, int64_t lo, int64_t hi) {
+    return v < lo ? lo : (v > hi ? hi : v);
+}
+
+/* ---------------------------------------------------------------------- */
+/* tv/runtime/f32_bits.tkv                                                 */
+/* ---------------------------------------------------------------------- */
+
+/* f64_to_f32_bits, tv/runtime/f32_bits.tkv:6-57.  The loop is kept as the
+ * reference writes it.  Two inputs never finish there: +/-Inf loops forever in
+ * `while a >= 2.0` and NaN falls through to an undefined int(NaN).  For those
+ * this restatement returns the binary32 Inf / quiet-NaN pattern instead, so
+ * that the FP8 encoder below reaches its own ex == 255 branch. */
+TVO_API uint32_t tvo_f64_to_f32_bits(double x) {
+    if (x == 0.0) return 0;                       /* -0.0 also gives 0 */
+    uint32_t s = 0;
+    double a = x;
+    if (isnan(x)) return 0x7FC00000u;
+    if (x < 0.0) { s = 2147483648u; a = 0.0 - x; }
+    if (isinf(a)) return s + 255u * 8388608u;
+    int64_t e = 0;
+    while (a >= 2.0) { a = a / 2.0; e = e + 1; }
+    while (a < 1.0) { a = a * 2.0; e = e - 1; }
+    int64_t ex = e + 127;
+    if (ex >= 255) return s + 255u * 8388608u;
+    if (ex <= 0) {
+        int64_t sh = e + 149;
+        if (sh <= 0) return s;
+        return s + (uint32_t)(int64_t)(a * pow(2.0, (double)sh) + 0.5);
+    }
+    double t = (a - 1.0) * 8388608.0;
+    int64_t f = (int64_t)t;
+    double r = t - (double)f;
+    int64_t m;
+    if (r > 0.5) m = f + 1;
+    else if (r < 0.5) m = f;
+    else { m = f; if (f % 2 != 0) m = f + 1; }
+    if (m > 8388607) {
+        m = 0;
+        ex = ex + 1;
+        if (ex >= 255) return s + 255u * 8388608u;
+    }
+    return s + (uint32_t)ex * 8388608u + (uint32_t)m;
+}
+
+/* f32_bits_to_f64, tv/runtime/f32_bits.tkv:60-74 (ex == 255 gives 2^129,
+ * i.e. +/-Inf after the f32 return boundary). */
+TVO_API double tvo_f32_bits_to_f64(uint32_t b) {
+    uint32_t s = b & 2147483648u;
+    int64_t ex = (b >> 23) & 255;
+    int64_t mant = b & 8388607;
+    double v;
+    if (ex == 0) v = (double)mant * pow(2.0, 0.0 - 149.0);
+    else if (ex == 255) v = pow(2.0, 128.0) * 2.0;
+    else v = (1.0 + (double)mant / 8388608.0) * pow(2.0, (double)(ex - 127));
+    if (s != 0) v = 0.0 - v;
+    return v;
+}
+
+/* ---------------------------------------------------------------------- */
+/* tv/quantization/types.tkv -- FP8 / FP16 codecs                          */
+/* ---------------------------------------------------------------------- */
+
+/* _qt_rne_rshift, tv/quantization/types.tkv:71-93 */
+TVO_API int64_t tvo_rne_rshift(int64_t v, int64_t s) {
+    if (s > 40) return 0;
+    if (s <= 0) return v;
+    int64_t half = (int64_t)1 << (s - 1);
+    int64_t q = v >> s;
+    int64_t rem = v - (q << s);
+    if (rem > half) return q + 1;
+    if (rem < half) return q;
+    if ((q & 1) == 1) return q + 1;
+    return q;
+}
+
+/* _qt_fp8_encode, tv/quantization/types.tkv:154-191 */
+TVO_API int tvo_fp8_encode(float x, int bias, int w, int emax_field, int has_inf, int sat_bits) {
+    uint32_t b = tvo_f64_to_f32_bits((double)x);
+    int64_t sign = (b >> 31) & 1;
+    int64_t ex = (b >> 23) & 255;
+    int64_t man = b & 8388607;
+    if (ex == 255) {
+        if (man != 0) {
+            if (has_inf == 1) return (int)((sign << 7) | sat_bits);
+            return (int)((sign << 7) | 127);
+        }
+        if (has_inf == 1) return (int)((sign << 7) | emax_field);
+        return (int)((sign << 7) | 127);
+    }
+    int64_t e, full;
+    if (ex == 0) { e = -126; full = man; }
+    else { e = ex - 127; full = man | 8388608; }
+    int64_t e8 = e + bias;
+    if (e8 >= emax_field) return (int)((sign << 7) | sat_bits);
+    if (e8 <= 0) {
+        int64_t m = tvo_rne_rshift(full, 24 - w - e8);
+        int64_t lim = ((int64_t)1 << w) - 1;
+        if (m > lim) m = lim;
+        return (int)((sign << 7) | m);
+    }
+    int64_t r = tvo_rne_rshift(full, 23 - w);
+    int64_t base = (int64_t)1 << w;
+    if (r >= base * 2) {
+        r = base;
+        e8 = e8 + 1;
+        if (e8 >= emax_field) return (int)((sign << 7) | sat_bits);
+    }
+    return (int)((sign << 7) | (e8 << w) | (r - base));
+}
+
+/* _qt_fp8_decode, tv/quantization/types.tkv:193-226 (f32 return boundary). */
+TVO_API float tvo_fp8_decode(int v, int bias, int w, int emax_field, int has_inf) {
+    int64_t sign = (v >> 7) & 1;
+    int ebits = (emax_field == 15) ? 4 : 5;
+    int64_t emask = ((int64_t)1 << ebits) - 1;
+    int64_t e8 = (v >> w) & emask;
+    int64_t m8 = v & (((int64_t)1 << w) - 1);
+    int64_t base = (int64_t)1 << w;
+    int64_t e32, man32;
+    if (e8 == emax_field) {
+        if (has_inf == 0) {
+            if (m8 == 7)
+                return (float)tvo_f32_bits_to_f64((uint32_t)((sign << 31) | 2139095040 | 4194304));
+        } else {
+            if (m8 != 0)
+                return (float)tvo_f32_bits_to_f64((uint32_t)((sign << 31) | 2139095040 | 4194304));
+            return (float)tvo_f32_bits_to_f64((uint32_t)((sign << 31) | 2139095040));
+        }
+    }
+    if (e8 == 0) {
+        if (m8 == 0) return (float)tvo_f32_bits_to_f64((uint32_t)(sign << 31));
+        int64_t t = m8, n = 0;
+        while (t < base) { t = t * 2; n = n + 1; }
+        e32 = 127 - bias - n;
+        man32 = (t - base) << (23 - w);
+    } else {
+        e32 = e8 - bias + 127;
+        man32 = m8 << (23 - w);
+    }
+    return (float)tvo_f32_bits_to_f64((uint32_t)((sign << 31) | (e32 << 23) | man32));
+}
+
+/* native_fp8_e4m3_encode / _decode, tv/quantization/types.tkv:228-233 */
+TVO_API int tvo_e4m3_encode(float x) { return tvo_fp8_encode(x, 7, 3, 15, 0, 126); }
+TVO_API float tvo_e4m3_decode(int v) { return tvo_fp8_decode(v, 7, 3, 15, 0); }
+/* native_fp8_e5m2_encode / _decode, tv/quantization/types.tkv:235-240 */
+TVO_API int tvo_e5m2_encode(float x) { return tvo_fp8_encode(x, 15, 2, 31, 1, 252); }
+TVO_API float tvo_e5m2_decode(int v) { return tvo_fp8_decode(v, 15, 2, 31, 1); }
+
+/* native_f16_encode, tv/quantization/types.tkv:95-127 */
+TVO_API int tvo_f16_encode(float x) {
+    uint32_t b = tvo_f64_to_f32_bits((double)x);
+    int64_t sign = (b >> 31) & 1, ex = (b >> 23) & 255, man = b & 8388607;
+    if (ex == 255) {
+        if (man != 0) return (int)((sign << 15) | 31744 | 512);
+        return (int)((sign << 15) | 31744);
+    }
+    int64_t e, full;
+    if (ex == 0) { e = -126; full = man; } else { e = ex - 127; full = man | 8388608; }
+    int64_t e16 = e + 15;
+    if (e16 >= 31) return (int)((sign << 15) | 31744);
+    if (e16 <= 0) {
+        int64_t m = tvo_rne_rshift(full, 24 - 10 - e16);
+        if (m > 1023) m = 1023;
+        return (int)((sign << 15) | m);
+    }
+    int64_t r = tvo_rne_rshift(full, 23 - 10);
+    if (r >= 2048) {
+        r = 1024;
+        e16 = e16 + 1;
+        if (e16 >= 31) return (int)((sign << 15) | 31744);
+    }
+    return (int)((sign << 15) | (e16 << 10) | (r - 1024));
+}
+
+/* native_f16_decode, tv/quantization/types.tkv:129-152 */
+TVO_API float tvo_f16_decode(int v) {
+    int64_t sign = (v >> 15) & 1, e16 = (v >> 10) & 31, m16 = v & 1023, e32, man32;
+    if (e16 == 31) {
+        if (m16 != 0) return (float)tvo_f32_bits_to_f64((uint32_t)((sign << 31) | 2139095040 | 4194304));
+        return (float)tvo_f32_bits_to_f64((uint32_t)((sign << 31) | 2139095040));
+    }
+    if (e16 == 0) {
+        if (m16 == 0) return (float)tvo_f32_bits_to_f64((uint32_t)(sign << 31));
+        int64_t t = m16, n = 0;
+        while (t < 1024) { t = t * 2; n = n + 1; }
+        e32 = 127 - 14 - n;
+        man32 = (t - 1024) << 13;
+    } else {
+        e32 = e16 - 15 + 127;
+        man32 = m16 << 13;
+    }
+    return (float)tvo_f32_bits_to_f64((uint32_t)((sign << 31) | (e32 << 23) | man32));
+}
+
+/* ---------------------------------------------------------------------- */
+/* tv/quantization/engine.tkv -- calibration and INT8 quantize             */
+/* ---------------------------------------------------------------------- */
+
+typedef struct {
+    float scale;          /* QuantParams.scale      'f32' */
+    int64_t zero_point;   /* QuantParams.zero_point 'i64' */
+    float min_val;        /* QuantParams.min_val    'f32' */
+    float max_val;        /* QuantParams.max_val    'f32' */
+} tvo_qparams;
+
+/* _quant_identity, tv/quantization/engine.tkv:9-10 */
+static tvo_qparams quant_identity(void) {
+    tvo_qparams p = {1.0f, 0, -FLT_MAX, FLT_MAX};
+    return p;
+}
+
+/* calibrate_minmax, tv/quantization/engine.tkv:13-36.  Locals are f64; the
+ * QuantParams fields round to f32.  NaN elements compare false and are
+ * skipped unless data[0] is NaN, exactly as the comparison chain does. */
+TVO_API tvo_qparams tvo_calibrate_minmax(const float* data, int64_t n, int symmetric) {
+    if (n == 0) return quant_identity();
+    double mn = data[0], mx = data[0];
+    for (int64_t i = 1; i < n; i++) {
+        double v = data[i];
+        if (v < mn) mn = v;
+        if (v > mx) mx = v;
+    }
+    tvo_qparams p;
+    if (symmetric) {
+        double am = fabs(mx);
+        if (fabs(mn) > am) am = fabs(mn);
+        if (am < 0.00000001) am = 0.00000001;
+        p.scale = (float)(am / 127.0);
+        p.zero_point = 0;
+        p.min_val = (float)(-am);
+        p.max_val = (float)am;
+        return p;
+    }
+    if (fabs(mx - mn) < 0.00000001) mx = mn + 0.00000001;
+    double scale = (mx - mn) / 255.0;
+    int64_t zp = net_round_to_i64(-mn / scale) - 128;
+    zp = clamp_i64(zp, -128, 127);
+    p.scale = (float)scale;
+    p.zero_point = zp;
+    p.min_val = (float)mn;
+    p.max_val = (float)mx;
+    return p;
+}
+
+/* Running calibration over several batches (8 seeded
+ * batches).  calibrate_minmax over the concatenation equals this max-of-maxes,
+ * which is how the caller composes it. */
+TVO_API tvo_qparams tvo_calibrate_minmax_batches(const float* const* batches, const int64_t* sizes,
+                                                 int64_t nb, int symmetric) {
+    int64_t total = 0;
+    for (int64_t b = 0; b < nb; b++) total += sizes[b];
+    float* cat = (float*)malloc(sizeof(float) * (size_t)(total > 0 ? total : 1));
+    int64_t o = 0;
+    for (int64_t b = 0; b < nb; b++) {
+        memcpy(cat + o, batches[b], sizeof(float) * (size_t)sizes[b]);
+        o += sizes[b];
+    }
+    tvo_qparams p = tvo_calibrate_minmax(cat, total, symmetric);
+    free(cat);
+    return p;
+}
+
+/* calibrate_per_channel_minmax, tv/quantization/engine.tkv:202-213.
+ * Returns 0, or -1 for the reference's ValueError cases. */
+TVO_API int tvo_calibrate_per_channel_minmax(const float* data, int64_t len, int64_t rows, int64_t cols,
+                                             int symmetric, tvo_qparams* out) {
+    if (rows <= 0 || cols <= 0) return -1;
+    if (len < rows * cols) return -1;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++) out[r] = tvo_calibrate_minmax(data + r * cols, cols, symmetric);
+    return 0;
+}
+
+/* quantize_int8_symmetric, tv/quantization/engine.tkv:216-226 */
+TVO_API int tvo_quantize_int8_symmetric(const float* src, int64_t n, int8_t* dst, int64_t dst_len, float scale) {
+    if (dst_len < n) return -1;
+    double inv;
+    if ((double)scale > 0.00000001) inv = 1.0 / (double)scale;
+    else inv = 1.0 / 0.00000001;
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; i++) {
+        int64_t q = net_round_to_i64((double)src[i] * inv);
+        dst[i] = (int8_t)clamp_i64(q, -127, 127);
+    }
+    return 0;
+}
+
+/* dequantize_int8_symmetric, tv/quantization/engine.tkv:229-234 */
+TVO_API int tvo_dequantize_int8_symmetric(const int8_t* src, int64_t n, float* dst, int64_t dst_len, float scale) {
+    if (dst_len < n) return -1;
+    for (int64_t i = 0; i < n; i++) dst[i] = (float)((double)src[i] * (double)scale);
+    return 0;
+}
+
+/* quantize_int8_per_channel, tv/quantization/engine.tkv:237-250 */
+TVO_API int tvo_quantize_int8_per_channel(const float* src, int64_t src_len, int8_t* dst, int64_t dst_len,
+                                          int64_t rows, int64_t cols, const float* scales, int64_t n_scales) {
+    if (dst_len < rows * cols || src_len < rows * cols) return -1;
+    if (n_scales < rows) return -1;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++) {
+        double sc = scales[r];
+        if (sc <= 0.00000001) sc = 0.00000001;
+        double inv = 1.0 / sc;
+        for (int64_t c = 0; c < cols; c++) {
+            int64_t i = r * cols + c;
+            dst[i] = (int8_t)clamp_i64(net_round_to_i64((double)src[i] * inv), -127, 127);
+        }
+    }
+    return 0;
+}
+
+/* dequantize_int8_per_channel, tv/quantization/engine.tkv:253-262 */
+TVO_API int tvo_dequantize_int8_per_channel(const int8_t* src, int64_t src_len, float* dst, int64_t dst_len,
+                                            int64_t rows, int64_t cols, const float* scales, int64_t n_scales) {
+    if (dst_len < rows * cols || src_len < rows * cols) return -1;
+    if (n_scales < rows) return -1;
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t c = 0; c < cols; c++) {
+            int64_t i = r * cols + c;
+            dst[i] = (float)((double)src[i] * (double)scales[r]);
+        }
+    return 0;
+}
+
+/* quantize_dynamic_int8_rowwise, tv/quantization/engine.tkv:266-285.  The
+ * stored scale rounds to f32 but the quantizer uses the f64 `sc`. */
+TVO_API int tvo_quantize_dynamic_int8_rowwise(const float* src, int64_t src_len, int8_t* dst, int64_t dst_len,
+                                              int64_t rows, int64_t cols, float* scales_out, int64_t n_scales) {
+    if (dst_len < rows * cols || src_len < rows * cols) return -1;
+    if (n_scales < rows) return -1;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++) {
+        double am = 0.0;
+        for (int64_t c = 0; c < cols; c++) {
+            double a = fabs((double)src[r * cols + c]);
+            if (a > am) am = a;
+        }
+        if (am < 0.00000001) am = 0.00000001;
+        double sc = am / 127.0;
+        scales_out[r] = (float)sc;
+        double inv = 1.0 / sc;
+        for (int64_t c = 0; c < cols; c++) {
+            int64_t i = r * cols + c;
+            dst[i] = (int8_t)clamp_i64(net_round_to_i64((double)src[i] * inv), -127, 127);
+        }
+    }
+    return 0;
+}
+
+/* ---------------------------------------------------------------------- */
+/* tv/quantization/matmul.tkv -- quantized GEMMs                           */
+/* ---------------------------------------------------------------------- */
+
+/* _dot_int8, tv/quantization/matmul.tkv:116-127: K unrolled by 32 with an
+ * i64 accumulator, then the tail. */
+TVO_API int64_t tvo_dot_int8(const int8_t* a, const int8_t* b, int64_t k) {
+    int64_t acc = 0, kk = 0, limit = k - 31;
+    while (kk < limit) {
+        for (int l = 0; l < 32; l++) acc += (int64_t)a[kk + l] * (int64_t)b[kk + l];
+        kk += 32;
+    }
+    while (kk < k) { acc += (int64_t)a[kk] * (int64_t)b[kk]; kk++; }
+    return acc;
+}
+
+/* Raw accumulators acc[m,n] = _dot_int8(A[m,:], W[n,:]) as int32 (exact
+ * for k < 133143), for bit-exact checks of the tensor-core accumulator. */
+TVO_API int tvo_gemm_i8_acc_i32(const int8_t* A, const int8_t* W, int32_t* acc, int64_t m, int64_t n, int64_t k) {
+#pragma omp parallel for schedule(static)
+    for (int64_t mm = 0; mm < m; mm++)
+        for (int64_t nn = 0; nn < n; nn++) acc[mm * n + nn] = (int32_t)tvo_dot_int8(A + mm * k, W + nn * k, k);
+    return 0;
+}
+
+/* matmul_int8_per_channel, tv/quantization/matmul.tkv:17-29:
+ * py = acc * scale_a * scales_w[nn] + bias, evaluated left to right in f64 and
+ * rounded to f32 on the list[f32] store.  n_bias == 0 means "no bias". */
+TVO_API int tvo_matmul_int8_per_channel(const int8_t* A, const int8_t* W, const float* bias, int64_t n_bias,
+                                        float* Y, int64_t m, int64_t n, int64_t k, float scale_a,
+                                        const float* scales_w, int64_t n_scales) {
+    if (n_scales < n) return -1;
+#pragma omp parallel for schedule(static)
+    for (int64_t mm = 0; mm < m; mm++)
+        for (int64_t nn = 0; nn < n; nn++) {
+            int64_t acc = tvo_dot_int8(A + mm * k, W + nn * k, k);
+            double b = (n_bias > 0) ? (double)bias[nn] : 0.0;
+            Y[mm * n + nn] = (float)((double)acc * (double)scale_a * (double)scales_w[nn] + b);
+        }
+    return 0;
+}
+
+/* matmul_int8_symmetric, tv/quantization/matmul.tkv:4-15: s = scale_a*scale_w
+ * is an untyped local (f64, exact product of two f32). */
+TVO_API int tvo_matmul_int8_symmetric(const int8_t* A, const int8_t* W, const float* bias, int64_t n_bias,
+                                      float* Y, int64_t m, int64_t n, int64_t k, float scale_a, float scale_w) {
+    double s = (double)scale_a * (double)scale_w;
+#pragma omp parallel for schedule(static)
+    for (int64_t mm = 0; mm < m; mm++)
+        for (int64_t nn = 0; nn < n; nn++) {
+            int64_t acc = tvo_dot_int8(A + mm * k, W + nn * k, k);
+            double b = (n_bias > 0) ? (double)bias[nn] : 0.0;
+            Y[mm * n + nn] = (float)((double)acc * s + b);
+        }
+    return 0;
+}
+
+/* matmul_int8_asymmetric, tv/quantization/matmul.tkv:31-44 */
+TVO_API int tvo_matmul_int8_asymmetric(const int8_t* A, const int8_t* W, const float* bias, int64_t n_bias,
+                                       float* Y, int64_t m, int64_t n, int64_t k, float scale_a, int64_t zp_a,
+                                       float scale_w, int64_t zp_w) {
+    double s = (double)scale_a * (double)scale_w;
+#pragma omp parallel for schedule(static)
+    for (int64_t mm = 0; mm < m; mm++)
+        for (int64_t nn = 0; nn < n; nn++) {
+            int64_t acc = 0;
+            for (int64_t kk = 0; kk < k; kk++)
+                acc += ((int64_t)A[mm * k + kk] - zp_a) * ((int64_t)W[nn * k + kk] - zp_w);
+            double b = (n_bias > 0) ? (double)bias[nn] : 0.0;
+            Y[mm * n + nn] = (float)((double)acc * s + b);
+        }
+    return 0;
+}
+
+/* Decode table for E4M3 bytes through the restated decoder. */
+static void e4m3_table(double* t) {
+    for (int v = 0; v < 256; v++) t[v] = (double)tvo_e4m3_decode(v);
+}
+
+/* quantize_fp8_e4m3, tv/quantization/matmul.tkv:60-66, storing the encoded
+ * byte itself (the reference stores byte - 128 in a list[i32]; the byte form
+ * is what the tensor cores read, the offset is applied at the boundary). */
+TVO_API int tvo_quantize_fp8_e4m3(const float* src, int64_t n, uint8_t* dst) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; i++) dst[i] = (uint8_t)tvo_e4m3_encode(src[i]);
+    return 0;
+}
+
+/* Scaled FP8 quantize used by BASELINE config 3 (scale = amax/448): the
+ * reference has no scaled FP8 quantizer, so it is composed the way the INT8
+ * quantizer is (engine.tkv:219-224): inv = 1.0/scale in f64, the product is
+ * rounded to f32 at the encoder's 'f32' parameter, then encoded. */
+TVO_API int tvo_quantize_fp8_e4m3_scaled(const float* src, int64_t rows, int64_t cols, uint8_t* dst,
+                                         const float* scales, int per_row) {
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++) {
+        double sc = per_row ? (double)scales[r] : (double)scales[0];
+        double inv = (sc > 0.00000001) ? 1.0 / sc : 1.0 / 0.00000001;
+        for (int64_t c = 0; c < cols; c++) {
+            float v = (float)((double)src[r * cols + c] * inv);
+            dst[r * cols + c] = (uint8_t)tvo_e4m3_encode(v);
+        }
+    }
+    return 0;
+}
+
+/* dequantize_fp8_e4m3, tv/quantization/matmul.tkv:68-73 (byte form) */
+TVO_API int tvo_dequantize_fp8_e4m3(const uint8_t* src, int64_t n, float* dst) {
+    for (int64_t i = 0; i < n; i++) dst[i] = tvo_e4m3_decode(src[i]);
+    return 0;
+}
+
+/* matmul_fp8_e4m3, tv/quantization/matmul.tkv:46-58: two decodes per MAC, f64
+ * accumulator (acc = 0.0), py = acc + bias.  The reference has no scales; the
+ * optional scale_a * scales_w[n] factor multiplies the
+ * accumulator before the bias, mirroring the INT8 epilogue (matmul.tkv:28).
+ * With scale_a == 1 and scales_w == NULL the expression is the reference's. */
+TVO_API int tvo_matmul_fp8_e4m3(const uint8_t* A, const uint8_t* W, const float* bias, int64_t n_bias,
+                                float* Y, int64_t m, int64_t n, int64_t k, float scale_a, const float* scales_w) {
+    double tab[256];
+    e4m3_table(tab);
+    const int scaled = (scales_w != NULL) || scale_a != 1.0f;
+#pragma omp parallel for schedule(static)
+    for (int64_t mm = 0; mm < m; mm++)
+        for (int64_t nn = 0; nn < n; nn++) {
+            double acc = 0.0;
+            for (int64_t kk = 0; kk < k; kk++) acc = acc + tab[A[mm * k + kk]] * tab[W[nn * k + kk]];
+            double b = (n_bias > 0) ? (double)bias[nn] : 0.0;
+            if (scaled) {
+                double sw = scales_w ? (double)scales_w[nn] : 1.0;
+                Y[mm * n + nn] = (float)(acc * (double)scale_a * sw + b);
+            } else {
+                Y[mm * n + nn] = (float)(acc + b);
+            }
+        }
+    return 0;
+}
+
+/* ---------------------------------------------------------------------- */
+/* Activations: tv/optimization/kernels.tkv:14-38, tv/training/tensor.tkv  */
+/* ---------------------------------------------------------------------- */
+
+/* _tanh(x: f32) -> f32, tv/optimization/kernels.tkv:32-38 */
+static float ref_tanh(float x) {
+    if ((double)x > 10.0) return 1.0f;
+    if ((double)x < -10.0) return -1.0f;
+    double e = exp(2.0 * (double)x);
+    return (float)((e - 1.0) / (e + 1.0));
+}
+
+/* apply_activation GELU (tanh form), tv/optimization/kernels.tkv:22-24 */
+TVO_API float tvo_gelu_tanh(float x) {
+    double xd = x;
+    double x3 = xd * xd * xd;
+    float targ = (float)(0.79788456 * (xd + 0.044715 * x3));
+    return (float)(0.5 * xd * (1.0 + (double)ref_tanh(targ)));
+}
+
+/* erf(x: f32) -> f32, Abramowitz-Stegun 7.1.26, tv/training/tensor.tkv:165-187 */
+TVO_API float tvo_erf_as(float x) {
+    double sg = 1.0;
+    if (x < 0.0f) sg = -1.0;
+    double ax = fabs((double)x);
+    double t = 1.0 / (1.0 + 0.3275911 * ax);
+    double poly = 1.061405429;
+    poly = poly * t + -1.453152027;
+    poly = poly * t + 1.421413741;
+    poly = poly * t + -0.284496736;
+    poly = poly * t + 0.254829592;
+    poly = poly * t;
+    return (float)(sg * (1.0 - exp(-ax * ax) * poly));
+}
+
+/* gelu_erf(v: f32) -> f32, tv/training/tensor.tkv:189-190: the argument of
+ * erf rounds to f32 at erf's parameter. */
+TVO_API float tvo_gelu_erf(float v) {
+    float arg = (float)((double)v / 1.4142135623730951);
+    return (float)(0.5 * (double)v * (1.0 + (double)tvo_erf_as(arg)));
+}
+
+TVO_API void tvo_gelu_erf_inplace(float* x, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; i++) x[i] = tvo_gelu_erf(x[i]);
+}
+
+/* ---------------------------------------------------------------------- */
+/* GPT-2 composition pieces, tv/training/gpt2_ref.tkv                      */
+/* ---------------------------------------------------------------------- */
+
+/* gpt2_layernorm interpreted path, tv/training/gpt2_ref.tkv:61-78 (f64
+ * statistics, one rounding to f32 on store). */
+TVO_API void tvo_layernorm(const float* x, const float* g, const float* b, float* out, int64_t n, int64_t h,
+                           double eps) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; i++) {
+        const float* xr = x + i * h;
+        double mu = 0.0;
+        for (int64_t j = 0; j < h; j++) mu = mu + (double)xr[j];
+        mu = mu / (double)h;
+        double v = 0.0;
+        for (int64_t j = 0; j < h; j++) { double d = (double)xr[j] - mu; v = v + d * d; }
+        v = v / (double)h;
+        double rstd = 1.0 / sqrt(v + eps);
+        for (int64_t j = 0; j < h; j++)
+            out[i * h + j] = (float)(((double)xr[j] - mu) * rstd * (double)g[j] + (double)b[j]);
+    }
+}
+
+/* gpt2_embed, tv/training/gpt2_ref.tkv:80-88 */
+TVO_API void tvo_embed(const int64_t* ids, const int64_t* pos, const float* wte, const float* wpe, float* out,
+                       int64_t n, int64_t h) {
+    for (int64_t i = 0; i < n; i++)
+        for (int64_t j = 0; j < h; j++)
+            out[i * h + j] = (float)((double)wte[ids[i] * h + j] + (double)wpe[pos[i] * h + j]);
+}
+
+/* gpt2_attention scalar path, tv/training/gpt2_ref.tkv:360-395 (without the
+ * projection, which is a QuantizedGemm here): qkv rows are [Q | K | V] with
+ * heads contiguous (head_dim = h / nheads); causal within each packed
+ * sequence [seg[s], seg[s+1]).  f64 throughout, ctx rounds to f32. */
+TVO_API void tvo_attention_causal(const float* qkv, float* ctx, int64_t n, int64_t h, int64_t nheads,
+                                  const int64_t* seg, int64_t nseg) {
+    int64_t hd = h / nheads;
+    double inv = 1.0 / sqrt((double)hd);
+    for (int64_t s = 0; s < nseg; s++) {
+        int64_t lo = seg[s], hi = seg[s + 1];
+#pragma omp parallel for schedule(dynamic, 4)
+        for (int64_t t = lo; t < hi; t++) {
+            double* sc = (double*)malloc(sizeof(double) * (size_t)(hi - lo));
+            for (int64_t head = 0; head < nheads; head++) {
+                int64_t ho = head * hd;
+                const float* q = qkv + t * 3 * h + ho;
+                for (int64_t u = lo; u <= t; u++) {
+                    const float* kv = qkv + u * 3 * h + h + ho;
+                    double acc = 0.0;
+                    for (int64_t d = 0; d < hd; d++) acc = acc + (double)q[d] * (double)kv[d];
+                    sc[u - lo] = acc * inv;
+                }
+                double mx = sc[0];
+                for (int64_t u = 1; u <= t - lo; u++) if (sc[u] > mx) mx = sc[u];
+                double tot = 0.0;
+                for (int64_t u = 0; u <= t - lo; u++) { double e = exp(sc[u] - mx); sc[u] = e; tot = tot + e; }
+                double inv_tot = 1.0 / tot;
+                for (int64_t d = 0; d < hd; d++) {
+                    double acc = 0.0;
+                    for (int64_t u = lo; u <= t; u++) acc = acc + sc[u - lo] * (double)qkv[u * 3 * h + 2 * h + ho + d];
+                    ctx[t * h + ho + d] = (float)(acc * inv_tot);
+                }
+            }
+            free(sc);
+        }
+    }
+}
+
+/* residual: out = a + b (f32 store) */
+TVO_API void tvo_add(const float* a, const float* b, float* out, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; i++) out[i] = (float)((double)a[i] + (double)b[i]);
+}
+
+/* LM head with the tied embedding, tv/training/gpt2_ref.tkv:603-610:
+ * logits[i,o] = sum_k x[i,k] * wte[o,k], f64 accumulator. */
+TVO_API void tvo_lm_head(const float* x, const float* wte, float* logits, int64_t n, int64_t vocab, int64_t h) {
+#pragma omp parallel for schedule(static)
+    for (int64_t o = 0; o < vocab; o++)
+        for (int64_t i = 0; i < n; i++) {
+            double acc = 0.0;
+            for (int64_t k = 0; k < h; k++) acc = acc + (double)x[i * h + k] * (double)wte[o * h + k];
+            logits[i * vocab + o] = (float)acc;
+        }
+}
+
+/* _gi_noise, tv/training/gpt2_ref.tkv:1977-1991: LCG + Box-Muller, x0.02 */
+TVO_API void tvo_gi_noise(float* out, int64_t n, int64_t seed, double mult) {
+    int64_t s = seed % 2147483648LL;
+    for (int64_t i = 0; i < n; i++) {
+        s = (s * 1103515245LL + 12345LL) % 2147483648LL;
+        double u1 = ((double)s + 0.5) / 2147483648.0;
+        s = (s * 1103515245LL + 12345LL) % 2147483648LL;
+        double u2 = (double)s / 2147483648.0;
+        out[i] = (float)(sqrt(0.0 - 2.0 * log(u1)) * cos(6.283185307179586 * u2) * mult);
+    }
+}
+
+TVO_API int tvo_num_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+TVO_API void tvo_set_num_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
