@@ -1,0 +1,186 @@
+/*
+ * tvq.h -- C ABI of libtvq, the B200 (sm_100a) implementation of
+ * TokenVector.Inference's post-training-quantized (PTQ) linear path.
+ *
+ * The boundary follows the reference's native-call convention
+ * (docs/SPEC_FUSED_SDPA_BWD.md:89, docs/SIMD_NOTES.md:8-18 of that
+ * repository): plain pointers, int64_t sizes, float scalars, an int status
+ * (0 = OK).  The reference turned a non-zero status into an interpreted
+ * fallback; this library has no fallback -- callers raise on non-zero.
+ *
+ * Two families of entry points:
+ *  - tvq_*      HOST buffers (the reference's list backing arrays).  The call
+ *               stages them to the current CUDA device, runs, copies results
+ *               back and synchronises.  Mirrors tv.quantization.* one to one.
+ *  - tvq_dev_*  DEVICE buffers, asynchronous on the given cudaStream_t
+ *               (NULL = legacy default stream); scales that the GPU produces
+ *               (calibration) are passed by device pointer so that chains of
+ *               calls need no host round trip.
+ * And a session API (tvq_session_*) holding device-resident weights and a
+ * captured launch sequence for a GPT-2-shaped stack of QuantizedGemm layers.
+ *
+ * Semantics of every numeric entry point match the reference bit for bit
+ * (int8 tensors, int32 accumulators, fp32 epilogue outputs) except where a
+ * comment states a tolerance.  Thread safety: each call is independent; a
+ * session handle must not be used from two threads at once.
+ */
+#ifndef TVQ_H_
+#define TVQ_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TVQ_API __attribute__((visibility("default")))
+#else
+#define TVQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes */
+#define TVQ_OK 0
+#define TVQ_ERR_INVALID (-1)     /* null pointer, negative size, bad mode          */
+#define TVQ_ERR_SIZE (-2)        /* a buffer or scale list is too small (ValueError) */
+#define TVQ_ERR_CUDA (-3)        /* CUDA runtime / driver error                     */
+#define TVQ_ERR_TIMEOUT (-4)     /* a device-side bounded wait ran out             */
+#define TVQ_ERR_UNSUPPORTED (-5) /* no sm_100 device, unaligned or unsupported shape */
+#define TVQ_ERR_HANDLE (-6)      /* unknown or destroyed session handle            */
+
+/* ---- activation codes of the GEMM epilogue
+ * tv/optimization/kernels.tkv:2-7 numbers its ActivationFunction enum the same
+ * way for 0..2; GELU_ERF is the erf form used by tv/training/gpt2_ref.tkv. */
+#define TVQ_ACT_NONE 0
+#define TVQ_ACT_RELU 1
+#define TVQ_ACT_GELU_TANH 2 /* ActivationFunction_GELU, kernels.tkv:22-24        */
+#define TVQ_ACT_GELU_ERF 6  /* gelu_erf, tv/training/tensor.tkv:189-190 (fp32 math) */
+
+/* ---- FP8 encoder modes */
+#define TVQ_FP8_REF 0 /* reference encoder, tv/quantization/types.tkv:154-191 (quirks kept) */
+#define TVQ_FP8_HW 1  /* hardware cvt.rn.satfinite (OCP E4M3), not the reference's          */
+
+/* ---- library / device */
+TVQ_API int tvq_version(void);
+/* Copies the last error message of the calling thread (NUL-terminated). */
+TVQ_API int tvq_last_error(char* buf, int64_t len);
+TVQ_API int tvq_device_count(int* n);
+/* Reads and clears the device error word of the current device (bounded
+ * waits record there); returns TVQ_OK or TVQ_ERR_TIMEOUT. */
+TVQ_API int tvq_device_error(void* stream);
+
+/* ================================================================ host buffers
+ * tv/quantization/engine.tkv */
+
+/* calibrate_minmax(data, symmetric), engine.tkv:13-36 -> QuantParams fields. */
+TVQ_API int tvq_calibrate_minmax(const float* data, int64_t n, int symmetric, float* scale, int64_t* zero_point,
+                         float* min_val, float* max_val);
+/* calibrate_minmax over several batches (running min/max), as the caller of
+ * engine.tkv:13-36 does for BASELINE config 1's 8 calibration batches. */
+TVQ_API int tvq_calibrate_minmax_batches(const float* const* batches, const int64_t* sizes, int64_t n_batches,
+                                 int symmetric, float* scale, int64_t* zero_point, float* min_val,
+                                 float* max_val);
+/* calibrate_per_channel_minmax(data, rows, cols, 1), engine.tkv:202-213: the
+ * per-row symmetric scales (fl32(max|W[r,:]|/127), floor 1e-8). */
+TVQ_API int tvq_calibrate_per_channel_minmax(const float* data, int64_t len, int64_t rows, int64_t cols,
+                                     float* scales, int64_t n_scales);
+/* quantize_int8_symmetric, engine.tkv:216-226 */
+TVQ_API int tvq_quantize_int8_symmetric(const float* src, int64_t n, int8_t* dst, int64_t dst_len, float scale);
+/* dequantize_int8_symmetric, engine.tkv:229-234 */
+TVQ_API int tvq_dequantize_int8_symmetric(const int8_t* src, int64_t n, float* dst, int64_t dst_len, float scale);
+/* quantize_int8_per_channel, engine.tkv:237-250 */
+TVQ_API int tvq_quantize_int8_per_channel(const float* src, int64_t src_len, int8_t* dst, int64_t dst_len, int64_t rows,
+                                  int64_t cols, const float* scales, int64_t n_scales);
+/* dequantize_int8_per_channel, engine.tkv:253-262 */
+TVQ_API int tvq_dequantize_int8_per_channel(const int8_t* src, int64_t src_len, float* dst, int64_t dst_len,
+                                    int64_t rows, int64_t cols, const float* scales, int64_t n_scales);
+/* quantize_dynamic_int8_rowwise, engine.tkv:266-285 */
+TVQ_API int tvq_quantize_dynamic_int8_rowwise(const float* src, int64_t src_len, int8_t* dst, int64_t dst_len,
+                                      int64_t rows, int64_t cols, float* scales_out, int64_t n_scales);
+
+/* ================================================================ host buffers
+ * tv/quantization/matmul.tkv -- A int8 [m,k] row-major, W int8 [n,k]
+ * row-major ("TN"), bias f32 [n] (n_bias == 0: none), Y f32 [m,n]. */
+
+/* matmul_int8_per_channel, matmul.tkv:17-29 (+ optional activation, which the
+ * reference's QuantizedGemm node ignores: pass TVQ_ACT_NONE for parity). */
+TVQ_API int tvq_matmul_int8_per_channel(const int8_t* A, const int8_t* W, const float* bias, int64_t n_bias, float* Y,
+                                int64_t m, int64_t n, int64_t k, float scale_a, const float* scales_w,
+                                int64_t n_scales, int act);
+/* matmul_int8_symmetric, matmul.tkv:4-15 */
+TVQ_API int tvq_matmul_int8_symmetric(const int8_t* A, const int8_t* W, const float* bias, int64_t n_bias, float* Y,
+                              int64_t m, int64_t n, int64_t k, float scale_a, float scale_w, int act);
+/* Raw int32 accumulators acc[m,n] = sum_k A[m,k]*W[n,k] (_dot_int8,
+ * matmul.tkv:116-127), for bit-exact verification. */
+TVQ_API int tvq_gemm_i8_acc(const int8_t* A, const int8_t* W, int32_t* acc, int64_t m, int64_t n, int64_t k);
+
+/* quantize_fp8_e4m3, matmul.tkv:60-66 (byte form; mode TVQ_FP8_REF|HW). */
+TVQ_API int tvq_quantize_fp8_e4m3(const float* src, int64_t n, uint8_t* dst, int64_t dst_len, int mode);
+/* Scaled FP8 quantize: dst = encode(fl32(src * (1/scale))),
+ * scales per row (per_row = 1, n_scales >= rows) or one per tensor. */
+TVQ_API int tvq_quantize_fp8_e4m3_scaled(const float* src, int64_t rows, int64_t cols, uint8_t* dst,
+                                 const float* scales, int64_t n_scales, int per_row, int mode);
+/* dequantize_fp8_e4m3, matmul.tkv:68-73 (reference decoder, byte form). */
+TVQ_API int tvq_dequantize_fp8_e4m3(const uint8_t* src, int64_t n, float* dst, int64_t dst_len);
+/* matmul_fp8_e4m3, matmul.tkv:46-58, on E4M3 bytes, with the optional
+ * scale_a * scales_w[n] factor of config 3 (scales_w NULL and scale_a 1 =
+ * the reference's unscaled form).  fp32 tensor-core accumulation: results
+ * agree with the reference's exact f64 sum within the documented FP8
+ * tolerance; subnormal E4M3 operands use the OCP value (the reference
+ * decoder halves them, types.tkv:221). */
+TVQ_API int tvq_matmul_fp8_e4m3(const uint8_t* A, const uint8_t* W, const float* bias, int64_t n_bias, float* Y,
+                        int64_t m, int64_t n, int64_t k, float scale_a, const float* scales_w, int act);
+
+/* ---- list[i32] compatibility forms: the reference stores int8 values in
+ * list[i32] (engine.tkv:216, session.tkv:158-170) and FP8 bytes as
+ * byte - 128 (matmul.tkv:65, :76).  These convert at the boundary. */
+TVQ_API int tvq_quantize_int8_symmetric_i32(const float* src, int64_t n, int32_t* dst, int64_t dst_len, float scale);
+TVQ_API int tvq_matmul_int8_per_channel_i32(const int32_t* A, const int32_t* W, const float* bias, int64_t n_bias,
+                                    float* Y, int64_t m, int64_t n, int64_t k, float scale_a,
+                                    const float* scales_w, int64_t n_scales);
+TVQ_API int tvq_quantize_fp8_e4m3_i32(const float* src, int64_t n, int32_t* dst, int64_t dst_len);
+TVQ_API int tvq_matmul_fp8_e4m3_i32(const int32_t* A, const int32_t* W, const float* bias, int64_t n_bias, float* Y,
+                            int64_t m, int64_t n, int64_t k);
+
+/* ================================================================ device buffers
+ * Asynchronous on `stream`.  minmax_dev is float[2] = {min, max} in an
+ * order-preserving encoding; reset it with tvq_dev_minmax_reset before the
+ * first batch, accumulate any number of batches, then finalize. */
+TVQ_API int tvq_dev_minmax_reset(uint32_t* minmax_dev, void* stream);
+TVQ_API int tvq_dev_minmax_accumulate(const float* x, int64_t n, uint32_t* minmax_dev, float* first_dev, void* stream);
+/* Writes QuantParams {scale, zero_point(as float), min, max} to params_dev[4]. */
+TVQ_API int tvq_dev_minmax_finalize(const uint32_t* minmax_dev, const float* first_dev, int symmetric, float* params_dev,
+                            void* stream);
+/* Per-tensor quantize with a device scale (scale_dev[0]). */
+TVQ_API int tvq_dev_quantize_int8(const float* x, int8_t* q, int64_t n, const float* scale_dev, void* stream);
+/* Per-channel weight calibrate + quantize, fused: scales_dev[r] and q[r,:]. */
+TVQ_API int tvq_dev_calibrate_quantize_per_channel(const float* w, int8_t* q, float* scales_dev, int64_t rows,
+                                           int64_t cols, void* stream);
+TVQ_API int tvq_dev_quantize_int8_per_channel(const float* w, int8_t* q, const float* scales_dev, int64_t rows,
+                                      int64_t cols, void* stream);
+TVQ_API int tvq_dev_quantize_dynamic_rowwise(const float* x, int8_t* q, float* scales_dev, int64_t rows, int64_t cols,
+                                     void* stream);
+TVQ_API int tvq_dev_quantize_fp8(const float* x, uint8_t* q, int64_t rows, int64_t cols, const float* scales_dev,
+                         int scale_mode /*0 none, 1 per tensor, 2 per row*/, int mode, void* stream);
+TVQ_API int tvq_dev_dequantize_fp8(const uint8_t* q, float* y, int64_t n, void* stream);
+
+/* Quantized GEMM on tcgen05 tensor cores.  kind 0 = INT8 (A,W int8), 1 = FP8
+ * E4M3 (A,W bytes).  scale_a_dev: device float[1]; scales_w_dev: device
+ * float[n] (per_channel = 1) or float[1].  Epilogue, in order:
+ *   y = fl32(acc * scale_a * scale_w[n] + bias[n])      (f64, the reference's)
+ *   y = act(y)                                          (TVQ_ACT_*)
+ *   y = fl32(y + residual[m,n])   if residual != NULL
+ *   Y[m,n] = y                    if Y != NULL          (f32, ldy = n)
+ *   Yq[m,n] = clamp(round(y * (1/scale_out)), +-127)   if Yq != NULL
+ *   atomicMax(|y|) into amax_dev  if amax_dev != NULL   (calibration)
+ * k must be a multiple of 16 and pointers 16-byte aligned. */
+TVQ_API int tvq_dev_gemm(int kind, const void* A, const void* W, const float* bias, const float* residual, float* Y,
+                 int8_t* Yq, int64_t m, int64_t n, int64_t k, const float* scale_a_dev,
+                 const float* scales_w_dev, int per_channel, int act, const float* scale_out_dev,
+                 uint32_t* amax_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TVQ_H_ */

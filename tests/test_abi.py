@@ -1,0 +1,64 @@
+"""The C ABI boundary: libtvq.so loads without a GPU and exports exactly what
+include/*.h declares (no compute calls here)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from tokenvector.inference_b200 import _native as N
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    names = set()
+    inc = os.path.join(ROOT, "include")
+    for f in os.listdir(inc):
+        if f.endswith(".h"):
+            src = open(os.path.join(inc, f)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            names |= set(re.findall(r"^\s*(?:TVQ_API\s+)?(?:int|float|void|int64_t)\s+\**(tvq_\w+)\s*\(", src, flags=re.M))
+    return names
+
+
+def test_library_builds_and_loads():
+    from tokenvector.inference_b200 import build
+    build.build()
+    assert os.path.exists(N.LIB_PATH)
+    N.lib()
+
+
+def test_every_declared_symbol_is_exported():
+    decl = _declared()
+    assert len(decl) >= 30
+    lib = ctypes.CDLL(N.LIB_PATH)
+    missing = [s for s in sorted(decl) if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_header():
+    decl = _declared()
+    assert decl == set(N.SIGNATURES), sorted(decl ^ set(N.SIGNATURES))
+
+
+def test_version_and_error_string():
+    assert N.lib().tvq_version() >= 10000
+    buf = ctypes.create_string_buffer(64)
+    assert N.lib().tvq_last_error(buf, 64) == 0
+    assert N.lib().tvq_last_error(None, 0) == N.TVQ_ERR_INVALID
+
+
+def test_argument_errors_need_no_gpu():
+    # size checks come before any device work, as the reference's ValueErrors
+    import numpy as np
+    from tokenvector.inference_b200.quantization import matmul as M, engine as E
+    with pytest.raises(ValueError):
+        M.matmul_int8_per_channel(np.zeros(8, np.int8), np.zeros(12, np.int8), [], np.zeros(6, np.float32),
+                                  2, 3, 4, 1.0, np.ones(2, np.float32))
+    with pytest.raises(ValueError):
+        E.quantize_int8_symmetric(np.zeros(4, np.float32), np.zeros(3, np.int8), 1.0)
+    with pytest.raises(ValueError):
+        E.calibrate_per_channel_minmax(np.zeros(4, np.float32), 0, 4)
+    with pytest.raises(ValueError):
+        E.quantize_int8_per_channel(np.zeros(8, np.float32), np.zeros(8, np.int8), 2, 4, np.ones(1, np.float32))

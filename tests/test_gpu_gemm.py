@@ -1,0 +1,198 @@
+"""GPU parity of the tcgen05 quantized GEMM against the CPU oracle, through
+the C ABI: int32 accumulators and fp32 epilogue outputs bit-exact for INT8;
+the FP8 path within its stated tolerance."""
+import numpy as np
+import pytest
+
+import oracle as O
+from tokenvector.inference_b200 import _native as N
+from tokenvector.inference_b200.quantization import matmul as M
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(1, 1, 1), (3, 5, 7), (1, 64, 16), (17, 33, 100), (128, 128, 128), (130, 250, 300), (200, 96, 768),
+          (129, 257, 1040), (64, 2304, 768), (1024, 3072, 768)]
+
+
+def _mats(m, n, k, seed):
+    rng = np.random.default_rng(seed)
+    A = rng.integers(-127, 128, (m, k)).astype(np.int8)
+    W = rng.integers(-127, 128, (n, k)).astype(np.int8)
+    return A, W
+
+
+def _same(a, b):
+    return np.array_equal(np.asarray(a, np.float32).view(np.uint32), np.asarray(b, np.float32).view(np.uint32))
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_int8_accumulators_exact(m, n, k):
+    A, W = _mats(m, n, k, m * 7 + n)
+    acc = M.gemm_i8_accumulators(A, W, m, n, k)
+    assert np.array_equal(acc, O.gemm_i8_acc(A, W))
+
+
+def test_int8_accumulators_extremes():
+    # all +-127: largest |acc| = 16129 * k
+    for k in [16, 768, 6400]:
+        A = np.full((130, k), -127, np.int8)
+        W = np.full((70, k), 127, np.int8)
+        W[::2] = -127
+        assert np.array_equal(M.gemm_i8_accumulators(A, W, 130, 70, k), O.gemm_i8_acc(A, W))
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_matmul_int8_per_channel_bit_exact(m, n, k):
+    A, W = _mats(m, n, k, m + 3 * n + k)
+    rng = np.random.default_rng(k)
+    bias = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    sa = np.float32(0.0213)
+    sw = (rng.random(n) * 0.003 + 1e-4).astype(np.float32)
+    Y = np.empty(m * n, np.float32)
+    M.matmul_int8_per_channel(A, W, bias, Y, m, n, k, sa, sw)
+    assert _same(Y.reshape(m, n), O.matmul_int8_per_channel(A, W, bias, sa, sw))
+    Y2 = np.empty(m * n, np.float32)
+    M.matmul_int8_per_channel(A, W, [], Y2, m, n, k, sa, sw)
+    assert _same(Y2.reshape(m, n), O.matmul_int8_per_channel(A, W, None, sa, sw))
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES[:6])
+def test_matmul_int8_symmetric_bit_exact(m, n, k):
+    A, W = _mats(m, n, k, 99 + m)
+    bias = np.linspace(-1, 1, n).astype(np.float32)
+    Y = np.empty(m * n, np.float32)
+    M.matmul_int8_symmetric(A, W, bias, Y, m, n, k, 0.011, 0.007)
+    assert _same(Y.reshape(m, n), O.matmul_int8_symmetric(A, W, bias, 0.011, 0.007))
+
+
+def test_matmul_k0_is_bias():
+    Y = np.empty(6, np.float32)
+    bias = np.array([1.5, -2.0, 0.25], np.float32)
+    M.matmul_int8_per_channel(np.zeros(0, np.int8), np.zeros(0, np.int8), bias, Y, 2, 3, 0, 0.5,
+                              np.ones(3, np.float32))
+    assert _same(Y.reshape(2, 3), np.tile(bias, (2, 1)))
+
+
+def test_matmul_list_i32_form():
+    A, W = _mats(9, 11, 40, 1)
+    sw = np.full(11, 0.01, np.float32)
+    Y = np.empty(99, np.float32)
+    M.matmul_int8_per_channel(A.astype(np.int32), W.astype(np.int32), [], Y, 9, 11, 40, 0.02, sw)
+    assert _same(Y.reshape(9, 11), O.matmul_int8_per_channel(A, W, None, 0.02, sw))
+
+
+def test_config1_end_to_end():
+    """calibrate (8 batches), quantize X and W, GEMM."""
+    from tokenvector.inference_b200.quantization import engine as E
+    X = O.gi_noise(1024 * 768, 0, 1.0).reshape(1024, 768)
+    Wf = O.gi_noise(3072 * 768, 100).reshape(3072, 768)
+    bias = O.gi_noise(3072, 200)
+    batches = [X] + [O.gi_noise(1024 * 768, s, 1.0) for s in range(1, 8)]
+    p = E.calibrate_minmax_batches(batches, 1)
+    op = O.calibrate_minmax(np.concatenate([b.ravel() for b in batches]), 1)
+    assert _same(p.scale, op.scale)
+    xq = np.empty(X.size, np.int8)
+    E.quantize_int8_symmetric(X, xq, p.scale)
+    sw = np.array([q.scale for q in E.calibrate_per_channel_minmax(Wf, 3072, 768)], np.float32)
+    wq = np.empty(Wf.size, np.int8)
+    E.quantize_int8_per_channel(Wf, wq, 3072, 768, sw)
+    oxq = O.quantize_int8_symmetric(X, op.scale)
+    osw = O.per_channel_scales(Wf, 3072, 768)
+    owq = O.quantize_int8_per_channel(Wf, 3072, 768, osw)
+    assert np.array_equal(xq.reshape(1024, 768), oxq) and np.array_equal(wq.reshape(3072, 768), owq)
+    Y = np.empty(1024 * 3072, np.float32)
+    M.matmul_int8_per_channel(xq, wq, bias, Y, 1024, 3072, 768, p.scale, sw)
+    assert _same(Y.reshape(1024, 3072), O.matmul_int8_per_channel(oxq, owq, bias, op.scale, osw))
+
+
+def _fp8_operands(m, n, k, seed):
+    rng = np.random.default_rng(seed)
+    X = rng.standard_normal((m, k)).astype(np.float32)
+    idx = rng.choice(m * k, max(1, m * k // 1000), replace=False)
+    X.ravel()[idx] *= 20.0
+    Wf = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    sa = np.array([np.abs(X).max() / 448.0], np.float32)
+    sw = (np.abs(Wf).max(axis=1) / 448.0).astype(np.float32)
+    A = O.quantize_fp8_e4m3_scaled(X, sa, False)
+    W = O.quantize_fp8_e4m3_scaled(Wf, sw, True)
+    return A, W, sa, sw
+
+
+def _fp8_tol(A, W, sa, sw):
+    # |error| <= 2^-20 * sum_k |a_k w_k| * sa * sw[n]  +  the reference's halved
+    # subnormals: sum over subnormal operands of |a w| / 2 (types.tkv:221)
+    da = np.abs(O.dequantize_fp8_e4m3(A).astype(np.float64))
+    dw = np.abs(O.dequantize_fp8_e4m3(W).astype(np.float64))
+    mag = da @ dw.T
+    sub_a = ((A & 0x78) == 0) & ((A & 0x7) != 0)
+    sub_w = ((W & 0x78) == 0) & ((W & 0x7) != 0)
+    sub = (da * sub_a) @ dw.T + da @ (dw * sub_w).T
+    return (mag * 2.0 ** -20 + sub * 1.01 + 1e-30) * float(sa[0]) * sw.astype(np.float64)[None, :]
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 3072, 1024), (16, 4096, 1024), (128, 1024, 4096), (300, 200, 160)])
+def test_matmul_fp8_within_tolerance(m, n, k):
+    A, W, sa, sw = _fp8_operands(m, n, k, m + n)
+    bias = np.zeros(n, np.float32)
+    Y = np.empty(m * n, np.float32)
+    M.matmul_fp8_e4m3(A, W, bias, Y, m, n, k, float(sa[0]), sw)
+    ref = O.matmul_fp8_e4m3(A, W, bias, float(sa[0]), sw).astype(np.float64)
+    err = np.abs(Y.reshape(m, n).astype(np.float64) - ref)
+    tol = _fp8_tol(A, W, sa, sw) + np.abs(ref) * 2.0 ** -23
+    assert np.all(err <= tol), float((err / tol).max())
+
+
+def test_matmul_fp8_unscaled_reference_form():
+    # matmul.tkv:46-58: no scales, y = sum dec(a) dec(w) + bias; normal
+    # operands only, small K -> exact in fp32 too
+    rng = np.random.default_rng(11)
+    A = rng.integers(0x08, 0x78, (33, 64)).astype(np.uint8) | (rng.integers(0, 2, (33, 64)) * 0x80).astype(np.uint8)
+    W = rng.integers(0x08, 0x40, (17, 64)).astype(np.uint8)
+    Y = np.empty(33 * 17, np.float32)
+    M.matmul_fp8_e4m3(A.astype(np.int32) - 128, W.astype(np.int32) - 128, [], Y, 33, 17, 64)
+    ref = O.matmul_fp8_e4m3(A, W, None).astype(np.float64)
+    err = np.abs(Y.reshape(33, 17).astype(np.float64) - ref)
+    tol = _fp8_tol(A, W, np.ones(1, np.float32), np.ones(17, np.float32)) + np.abs(ref) * 2.0 ** -23
+    assert np.all(err <= tol)
+
+
+def test_gemm_errors():
+    with pytest.raises(ValueError):
+        M.matmul_int8_per_channel(np.zeros(8, np.int8), np.zeros(12, np.int8), [], np.zeros(6, np.float32),
+                                  2, 3, 4, 1.0, np.ones(2, np.float32))
+    with pytest.raises(ValueError):
+        M.matmul_int8_per_channel(np.zeros(8, np.int8), np.zeros(12, np.int8), np.ones(2, np.float32),
+                                  np.zeros(6, np.float32), 2, 3, 4, 1.0, np.ones(3, np.float32))
+
+
+def test_device_gemm_fused_epilogue():
+    """tvq_dev_gemm with GELU + residual + int8 output + amax on torch tensors."""
+    import torch
+    m, n, k = 256, 384, 512
+    A, W = _mats(m, n, k, 5)
+    rng = np.random.default_rng(5)
+    bias = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    sw = (rng.random(n) * 0.002 + 1e-4).astype(np.float32)
+    R = rng.standard_normal((m, n)).astype(np.float32)
+    dev = torch.device("cuda:0")
+    tA, tW = torch.from_numpy(A).to(dev), torch.from_numpy(W).to(dev)
+    tb, tsw = torch.from_numpy(bias).to(dev), torch.from_numpy(sw).to(dev)
+    tR = torch.from_numpy(R).to(dev)
+    sa = torch.tensor([0.03], dtype=torch.float32, device=dev)
+    so = torch.tensor([0.05], dtype=torch.float32, device=dev)
+    Y = torch.empty((m, n), dtype=torch.float32, device=dev)
+    Yq = torch.empty((m, n), dtype=torch.int8, device=dev)
+    amax = torch.zeros(1, dtype=torch.int32, device=dev)
+    from tokenvector.inference_b200.quantization import _buf as B
+    N.call("tvq_dev_gemm", N.GEMM_I8, B.ptr(tA), B.ptr(tW), B.ptr(tb), B.ptr(tR), B.ptr(Y), B.ptr(Yq), m, n, k,
+           B.ptr(sa), B.ptr(tsw), 1, N.ACT_GELU_ERF, B.ptr(so), B.ptr(amax), B.stream_of(tA))
+    torch.cuda.synchronize()
+    base = O.matmul_int8_per_channel(A, W, bias, np.float32(0.03), sw)
+    gel = O.gelu_erf_array(base)
+    want = O.add(gel, R)
+    got = Y.cpu().numpy()
+    assert np.allclose(got, want, rtol=2e-6, atol=2e-6)
+    q_ref = O.quantize_int8_symmetric(got, np.float32(0.05))
+    assert np.array_equal(Yq.cpu().numpy(), q_ref)
+    am = amax.cpu().numpy().view(np.float32)[0]
+    assert am == np.abs(got).max()

@@ -1,0 +1,158 @@
+"""GPU parity of the HBM-bound PTQ kernels (calibration, INT8 quantize,
+FP8 codec) against the CPU oracle, through the C ABI.  Bit-exact."""
+import numpy as np
+import pytest
+
+import oracle as O
+from tokenvector.inference_b200.quantization import engine as E
+from tokenvector.inference_b200.quantization import matmul as M
+from tokenvector.inference_b200.quantization import types as T
+
+pytestmark = pytest.mark.gpu
+
+
+def _same_f32(a, b):
+    return np.array_equal(np.asarray(a, np.float32).view(np.uint32), np.asarray(b, np.float32).view(np.uint32))
+
+
+def _data(n, seed, outliers=False):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal(n).astype(np.float32)
+    if outliers and n:
+        idx = rng.choice(n, max(1, n // 1000), replace=False)
+        x[idx] *= 20.0
+    return x
+
+
+@pytest.mark.parametrize("n", [1, 2, 5, 31, 1000, 4097, 786432])
+@pytest.mark.parametrize("sym", [1, 0])
+def test_calibrate_minmax(n, sym):
+    x = _data(n, n, outliers=True)
+    g = E.calibrate_minmax(x, sym)
+    o = O.calibrate_minmax(x, sym)
+    assert _same_f32(g.scale, o.scale) and g.zero_point == o.zero_point
+    assert _same_f32(g.min_val, o.min_val) and _same_f32(g.max_val, o.max_val)
+
+
+def test_calibrate_minmax_edges():
+    for x in [np.zeros(7, np.float32), np.full(9, -3.5, np.float32), np.array([1e-12, -1e-12], np.float32),
+              np.array([np.nan, 1.0, 2.0], np.float32), np.array([1.0, np.nan, -4.0], np.float32),
+              np.array([np.inf, 1.0], np.float32), np.array([-np.inf], np.float32)]:
+        for sym in (1, 0):
+            g = E.calibrate_minmax(x, sym)
+            o = O.calibrate_minmax(x, sym)
+            assert _same_f32(g.scale, o.scale) or (np.isnan(g.scale) and np.isnan(o.scale)), (x, sym, g, o.scale)
+            assert g.zero_point == o.zero_point, (x, sym)
+    g = E.calibrate_minmax(np.zeros(0, np.float32))
+    assert g.scale == 1.0 and g.zero_point == 0
+
+
+def test_calibrate_eight_batches_config1():
+    # scale over 8 seeded [1024,768] batches
+    batches = [O.gi_noise(1024 * 768, s, 1.0) for s in range(8)]
+    g = E.calibrate_minmax_batches(batches, 1)
+    o = O.calibrate_minmax(np.concatenate(batches), 1)
+    assert _same_f32(g.scale, o.scale)
+
+
+def test_quantize_symmetric_bit_exact():
+    x = _data(1 << 20, 3, outliers=True)
+    x[:9] = [np.nan, np.inf, -np.inf, 0.0, -0.0, 1e-30, -1e30, 3.0, -3.0]
+    for scale in [0.0123, 1.0, 0.0, 1e-9, 3.4e38]:
+        q = np.empty(x.size, np.int8)
+        E.quantize_int8_symmetric(x, q, scale)
+        assert np.array_equal(q, O.quantize_int8_symmetric(x, scale)), scale
+    # exact ties: x * (1/scale) lands on k + 0.5
+    t = (np.arange(-300, 300, dtype=np.float32) + 0.5)
+    q = np.empty(t.size, np.int8)
+    E.quantize_int8_symmetric(t, q, 1.0)
+    assert np.array_equal(q, O.quantize_int8_symmetric(t, 1.0))
+    # unaligned / odd sizes and the list[i32] destination
+    for n in [1, 15, 17, 33]:
+        xs = x[3:3 + n].copy()
+        q32 = np.zeros(n, np.int32)
+        E.quantize_int8_symmetric(xs, q32, 0.05)
+        assert np.array_equal(q32, O.quantize_int8_symmetric(xs, 0.05).astype(np.int32))
+
+
+def test_dequantize_bit_exact():
+    rng = np.random.default_rng(4)
+    q = rng.integers(-127, 128, 5000).astype(np.int8)
+    y = np.empty(q.size, np.float32)
+    E.dequantize_int8_symmetric(q, y, 0.0173)
+    assert _same_f32(y, O.dequantize_int8_symmetric(q, 0.0173))
+    sc = (rng.random(50) * 0.1).astype(np.float32)
+    y2 = np.empty(q.size, np.float32)
+    E.dequantize_int8_per_channel(q, y2, 50, 100, sc)
+    assert _same_f32(y2, O.dequantize_int8_per_channel(q, 50, 100, sc))
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 7), (64, 768), (3072, 768), (100, 1001)])
+def test_per_channel_calibrate_and_quantize(rows, cols):
+    w = (O.gi_noise(rows * cols, rows + cols) if rows * cols > 1 else np.array([0.5], np.float32)).reshape(rows, cols)
+    ps = E.calibrate_per_channel_minmax(w, rows, cols)
+    os_ = O.per_channel_scales(w, rows, cols)
+    assert _same_f32([p.scale for p in ps], os_)
+    q = np.empty(rows * cols, np.int8)
+    E.quantize_int8_per_channel(w, q, rows, cols, os_)
+    assert np.array_equal(q.reshape(rows, cols), O.quantize_int8_per_channel(w, rows, cols, os_))
+
+
+def test_per_channel_edges():
+    w = np.array([[0.0, 0.0, 0.0], [np.nan, 1.0, 2.0], [1.0, np.nan, -2.0], [1e-12, 2e-12, 0.0]], np.float32)
+    ps = E.calibrate_per_channel_minmax(w, 4, 3)
+    os_ = O.per_channel_scales(w, 4, 3)
+    g = np.array([p.scale for p in ps], np.float32)
+    assert np.array_equal(np.isnan(g), np.isnan(os_))
+    assert _same_f32(g[~np.isnan(g)], os_[~np.isnan(os_)])
+
+
+def test_dynamic_rowwise():
+    x = _data(512 * 300, 5, outliers=True).reshape(512, 300)
+    x[7, :] = 0.0
+    x[9, 3] = np.nan
+    q = np.empty(x.size, np.int8)
+    sc = np.empty(512, np.float32)
+    E.quantize_dynamic_int8_rowwise(x, q, 512, 300, sc)
+    oq, osc = O.quantize_dynamic_int8_rowwise(x, 512, 300)
+    assert np.array_equal(q.reshape(512, 300), oq)
+    assert _same_f32(sc, osc)
+
+
+def test_fp8_decode_all_bytes():
+    b = np.arange(256, dtype=np.uint8)
+    y = np.empty(256, np.float32)
+    M.dequantize_fp8_e4m3(b, y)
+    o = O.dequantize_fp8_e4m3(b)
+    assert _same_f32(y, o)
+    assert T.native_fp8_e4m3_decode(0x7E) == 448.0
+    assert T.fp8e4m3_from_float(1.0).value == 0x38
+
+
+def test_fp8_encode_reference_quirks_and_random():
+    special = np.array([0.0, -0.0, 0.5, 1.0, -1.0, 2.5, 16.0, 240.0, 247.0, 248.0, 255.9, 256.0, 300.0, 448.0,
+                        1e9, -1e9, 2.0 ** -6, 7.6 * 2.0 ** -9, 2.0 ** -9, 2.0 ** -10, 1.5 * 2.0 ** -10,
+                        2.0 ** -149, -2.0 ** -149, np.nan, np.inf, -np.inf], np.float32)
+    rng = np.random.default_rng(6)
+    bits = rng.integers(0, 2 ** 32, 1 << 18, dtype=np.uint64).astype(np.uint32)
+    rand = bits.view(np.float32)
+    near = (rng.standard_normal(1 << 18) * rng.choice([1e-3, 0.05, 1, 30, 250], 1 << 18)).astype(np.float32)
+    x = np.concatenate([special, rand, near])
+    q = np.empty(x.size, np.uint8)
+    M.quantize_fp8_e4m3(x, q)
+    assert np.array_equal(q, O.quantize_fp8_e4m3(x))
+    # list[i32] form stores byte - 128 (matmul.tkv:65)
+    q32 = np.empty(special.size, np.int32)
+    M.quantize_fp8_e4m3(special, q32)
+    assert np.array_equal(q32, O.quantize_fp8_e4m3(special).astype(np.int32) - 128)
+
+
+def test_fp8_scaled_quantize():
+    x = _data(64 * 1024, 8, outliers=True).reshape(64, 1024)
+    amax_rows = np.abs(x).max(axis=1)
+    sc = (amax_rows / 448.0).astype(np.float32)
+    g = M.quantize_fp8_e4m3_scaled(x, 64, 1024, sc, True)
+    assert np.array_equal(g, O.quantize_fp8_e4m3_scaled(x, sc, True))
+    st = np.array([np.abs(x).max() / 448.0], np.float32)
+    g = M.quantize_fp8_e4m3_scaled(x, 64, 1024, st, False)
+    assert np.array_equal(g, O.quantize_fp8_e4m3_scaled(x, st, False))

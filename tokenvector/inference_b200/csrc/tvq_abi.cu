@@ -1,0 +1,716 @@
+// tvq_abi.cu -- the exported C ABI (include/tvq.h): argument checks with the
+// reference's error behaviour (ValueError -> TVQ_ERR_SIZE), host-buffer
+// staging for the tvq_* entry points, and the asynchronous tvq_dev_* forms.
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "tvq_common.cuh"
+#include "tvq_kernels.h"
+
+namespace tvq {
+
+// ---------------------------------------------------------------- errors
+namespace {
+thread_local std::string g_last_error;
+}
+
+void set_error(int code, const std::string& msg) { g_last_error = "tvq error " + std::to_string(code) + ": " + msg; }
+
+int cuda_fail(cudaError_t e, const char* what) {
+    set_error(TVQ_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    return TVQ_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------- devices
+namespace {
+constexpr int kMaxDev = 64;
+DeviceState g_dev[kMaxDev];
+std::mutex g_dev_mu;
+
+// Grow-only device scratch for the host-buffer entry points, one pool and
+// one stream per device; the pool mutex serialises host-buffer calls.
+struct HostCtx {
+    std::mutex mu;
+    cudaStream_t stream = nullptr;
+    std::vector<std::pair<void*, size_t>> slots;
+};
+HostCtx g_host[kMaxDev];
+}  // namespace
+
+DeviceState* device_state(int* rc) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) { *rc = cuda_fail(e, "cudaGetDevice"); return nullptr; }
+    if (dev < 0 || dev >= kMaxDev) { set_error(TVQ_ERR_UNSUPPORTED, "device ordinal too large"); *rc = TVQ_ERR_UNSUPPORTED; return nullptr; }
+    DeviceState& d = g_dev[dev];
+    if (d.sm_count == 0) {
+        std::lock_guard<std::mutex> lk(g_dev_mu);
+        if (d.sm_count == 0) {
+            int sms = 0, maj = 0, mnr = 0;
+            if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+                (e = cudaDeviceGetAttribute(&maj, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+                (e = cudaDeviceGetAttribute(&mnr, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess) {
+                *rc = cuda_fail(e, "cudaDeviceGetAttribute");
+                return nullptr;
+            }
+            int* err = nullptr;
+            if ((e = cudaMalloc(&err, sizeof(int))) != cudaSuccess || (e = cudaMemset(err, 0, sizeof(int))) != cudaSuccess) {
+                *rc = cuda_fail(e, "device error word");
+                return nullptr;
+            }
+            d.cc_major = maj;
+            d.cc_minor = mnr;
+            d.d_error = err;
+            d.sm_count = sms;  // published last
+        }
+    }
+    *rc = TVQ_OK;
+    return &d;
+}
+
+int check_device_error(cudaStream_t st) {
+    int rc = 0;
+    DeviceState* d = device_state(&rc);
+    if (!d) return rc;
+    TVQ_CUDA(cudaStreamSynchronize(st));
+    int h = 0;
+    TVQ_CUDA(cudaMemcpy(&h, d->d_error, sizeof(int), cudaMemcpyDeviceToHost));
+    if (h != 0) {
+        TVQ_CUDA(cudaMemset(d->d_error, 0, sizeof(int)));
+        set_error(TVQ_ERR_TIMEOUT, "device-side wait timed out (code " + std::to_string(h) + ")");
+        return TVQ_ERR_TIMEOUT;
+    }
+    return TVQ_OK;
+}
+
+namespace {
+
+// RAII context of one host-buffer call.
+struct Host {
+    HostCtx* ctx = nullptr;
+    std::unique_lock<std::mutex> lk;
+    int rc = TVQ_OK;
+    Host() {
+        DeviceState* d = device_state(&rc);
+        if (!d) return;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        ctx = &g_host[dev];
+        lk = std::unique_lock<std::mutex>(ctx->mu);
+        if (!ctx->stream) {
+            cudaError_t e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+            if (e != cudaSuccess) rc = cuda_fail(e, "cudaStreamCreate");
+        }
+    }
+    cudaStream_t st() const { return ctx->stream; }
+    // device buffer of at least `bytes` in slot i (contents not preserved)
+    void* buf(size_t i, size_t bytes) {
+        if (rc) return nullptr;
+        if (ctx->slots.size() <= i) ctx->slots.resize(i + 1, {nullptr, 0});
+        auto& s = ctx->slots[i];
+        if (s.second < bytes || !s.first) {
+            if (s.first) cudaFree(s.first);
+            s.first = nullptr;
+            s.second = 0;
+            size_t want = bytes < 256 ? 256 : bytes;
+            cudaError_t e = cudaMalloc(&s.first, want);
+            if (e != cudaSuccess) { rc = cuda_fail(e, "cudaMalloc (scratch)"); return nullptr; }
+            s.second = want;
+        }
+        return s.first;
+    }
+    int h2d(void* d, const void* h, size_t bytes) {
+        if (rc || bytes == 0) return rc;
+        cudaError_t e = cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, st());
+        if (e != cudaSuccess) rc = cuda_fail(e, "cudaMemcpyAsync H2D");
+        return rc;
+    }
+    int d2h(void* h, const void* d, size_t bytes) {
+        if (rc || bytes == 0) return rc;
+        cudaError_t e = cudaMemcpyAsync(h, d, bytes, cudaMemcpyDeviceToHost, st());
+        if (e != cudaSuccess) rc = cuda_fail(e, "cudaMemcpyAsync D2H");
+        return rc;
+    }
+    int finish() {
+        if (rc) return rc;
+        return check_device_error(st());
+    }
+};
+
+#define TVQ_TRY try {
+#define TVQ_CATCH                                                              \
+    }                                                                          \
+    catch (const std::bad_alloc&) {                                            \
+        ::tvq::set_error(TVQ_ERR_CUDA, "host allocation failed");              \
+        return TVQ_ERR_CUDA;                                                   \
+    }                                                                          \
+    catch (...) {                                                              \
+        ::tvq::set_error(TVQ_ERR_INVALID, "unexpected exception");             \
+        return TVQ_ERR_INVALID;                                                \
+    }
+
+#define HOST_BEGIN          \
+    ::tvq::Host H;          \
+    if (H.rc) return H.rc;
+
+#define STEP(expr)                  \
+    do {                            \
+        int r__ = (expr);           \
+        if (r__) return r__;        \
+    } while (0)
+
+template <typename T>
+T* dev(Host& H, size_t slot, size_t count) {
+    return static_cast<T*>(H.buf(slot, count * sizeof(T)));
+}
+
+// shared tail of the host GEMM entry points
+int host_gemm(int kind, const void* A, const void* W, size_t elem_bytes_ignored, const float* bias, int64_t n_bias,
+              float* Y, int64_t m, int64_t n, int64_t k, float scale_a, const float* scales_w, int64_t n_scales,
+              int per_channel, int act) {
+    (void)elem_bytes_ignored;
+    TVQ_CHECK(m >= 0 && n >= 0 && k >= 0 && n_bias >= 0, TVQ_ERR_INVALID, "negative size");
+    if (m == 0 || n == 0) return TVQ_OK;
+    TVQ_CHECK(Y && (k == 0 || (A && W)), TVQ_ERR_INVALID, "null buffer");
+    TVQ_CHECK(n_bias == 0 || n_bias >= n, TVQ_ERR_SIZE, "bias smaller than N");
+    TVQ_CHECK(n_bias == 0 || bias, TVQ_ERR_INVALID, "null bias");
+    if (per_channel) TVQ_CHECK(scales_w && n_scales >= n, TVQ_ERR_SIZE, "scales_w smaller than N");
+    HOST_BEGIN
+    const int64_t kp = (k + 15) / 16 * 16;  // TMA row pitch: pad K with zeros
+    uint8_t* dA = dev<uint8_t>(H, 0, static_cast<size_t>(m * kp));
+    uint8_t* dW = dev<uint8_t>(H, 1, static_cast<size_t>(n * kp));
+    float* dY = dev<float>(H, 2, static_cast<size_t>(m * n));
+    float* dB = dev<float>(H, 3, static_cast<size_t>(n_bias > 0 ? n : 1));
+    float* dS = dev<float>(H, 4, static_cast<size_t>(n + 1));
+    if (H.rc) return H.rc;
+    if (kp == k) {
+        STEP(H.h2d(dA, A, static_cast<size_t>(m * k)));
+        STEP(H.h2d(dW, W, static_cast<size_t>(n * k)));
+    } else if (k > 0) {
+        TVQ_CUDA(cudaMemsetAsync(dA, 0, static_cast<size_t>(m * kp), H.st()));
+        TVQ_CUDA(cudaMemsetAsync(dW, 0, static_cast<size_t>(n * kp), H.st()));
+        TVQ_CUDA(cudaMemcpy2DAsync(dA, kp, A, k, k, m, cudaMemcpyHostToDevice, H.st()));
+        TVQ_CUDA(cudaMemcpy2DAsync(dW, kp, W, k, k, n, cudaMemcpyHostToDevice, H.st()));
+    }
+    if (n_bias > 0) STEP(H.h2d(dB, bias, static_cast<size_t>(n) * 4));
+    STEP(H.h2d(dS, &scale_a, 4));
+    if (per_channel) STEP(H.h2d(dS + 1, scales_w, static_cast<size_t>(n) * 4));
+    else STEP(H.h2d(dS + 1, scales_w, 4));
+    GemmArgs g;
+    g.kind = kind;
+    g.A = dA;
+    g.W = dW;
+    g.bias = n_bias > 0 ? dB : nullptr;
+    g.Y = dY;
+    g.m = m;
+    g.n = n;
+    g.k = kp;
+    g.scale_a = dS;
+    g.scales_w = dS + 1;
+    g.per_channel = per_channel;
+    g.act = act;
+    STEP(launch_gemm(g, H.st()));
+    STEP(H.d2h(Y, dY, static_cast<size_t>(m * n) * 4));
+    return H.finish();
+}
+
+}  // namespace
+}  // namespace tvq
+
+using namespace tvq;
+
+extern "C" {
+
+int tvq_version(void) { return 10000; }
+
+int tvq_last_error(char* buf, int64_t len) {
+    if (!buf || len <= 0) return TVQ_ERR_INVALID;
+    const std::string& s = g_last_error;
+    const size_t n = std::min<size_t>(s.size(), static_cast<size_t>(len - 1));
+    memcpy(buf, s.data(), n);
+    buf[n] = 0;
+    return TVQ_OK;
+}
+
+int tvq_device_count(int* n) {
+    TVQ_CHECK(n, TVQ_ERR_INVALID, "null out pointer");
+    int c = 0;
+    cudaError_t e = cudaGetDeviceCount(&c);
+    if (e != cudaSuccess) { *n = 0; return cuda_fail(e, "cudaGetDeviceCount"); }
+    *n = c;
+    return TVQ_OK;
+}
+
+int tvq_device_error(void* stream) { return check_device_error(static_cast<cudaStream_t>(stream)); }
+
+// ================================================================ host: engine.tkv
+
+static int calibrate_common(const float* const* batches, const int64_t* sizes, int64_t nb, int symmetric,
+                            float* scale, int64_t* zp, float* mn, float* mx) {
+    TVQ_CHECK(nb >= 0 && batches && sizes, TVQ_ERR_INVALID, "null batch list");
+    int64_t total = 0;
+    for (int64_t b = 0; b < nb; b++) {
+        TVQ_CHECK(sizes[b] >= 0 && (sizes[b] == 0 || batches[b]), TVQ_ERR_INVALID, "bad batch");
+        total += sizes[b];
+    }
+    if (total == 0) {  // _quant_identity, engine.tkv:9-10
+        if (scale) *scale = 1.0f;
+        if (zp) *zp = 0;
+        if (mn) *mn = -3.4028234663852886e38f;
+        if (mx) *mx = 3.4028234663852886e38f;
+        return TVQ_OK;
+    }
+    TVQ_TRY
+    HOST_BEGIN
+    int64_t biggest = 0;
+    for (int64_t b = 0; b < nb; b++) biggest = std::max(biggest, sizes[b]);
+    float* dx = dev<float>(H, 0, static_cast<size_t>(biggest));
+    uint32_t* dmm = dev<uint32_t>(H, 1, 2);
+    float* dfirst = dev<float>(H, 2, 1);
+    float* dp = dev<float>(H, 3, 4);
+    if (H.rc) return H.rc;
+    STEP(launch_minmax_reset(dmm, H.st()));
+    bool first = true;
+    for (int64_t b = 0; b < nb; b++) {
+        if (sizes[b] == 0) continue;
+        STEP(H.h2d(dx, batches[b], static_cast<size_t>(sizes[b]) * 4));
+        STEP(launch_minmax_accumulate(dx, sizes[b], dmm, first ? dfirst : nullptr, H.st()));
+        first = false;
+    }
+    STEP(launch_minmax_finalize(dmm, dfirst, symmetric, dp, H.st()));
+    float hp[4];
+    STEP(H.d2h(hp, dp, sizeof(hp)));
+    STEP(H.finish());
+    if (scale) *scale = hp[0];
+    if (zp) *zp = static_cast<int64_t>(hp[1]);
+    if (mn) *mn = hp[2];
+    if (mx) *mx = hp[3];
+    return TVQ_OK;
+    TVQ_CATCH
+}
+
+int tvq_calibrate_minmax(const float* data, int64_t n, int symmetric, float* scale, int64_t* zero_point,
+                         float* min_val, float* max_val) {
+    TVQ_CHECK(n >= 0 && (n == 0 || data), TVQ_ERR_INVALID, "null data");
+    const float* b[1] = {data};
+    int64_t s[1] = {n};
+    return calibrate_common(b, s, 1, symmetric, scale, zero_point, min_val, max_val);
+}
+
+int tvq_calibrate_minmax_batches(const float* const* batches, const int64_t* sizes, int64_t n_batches, int symmetric,
+                                 float* scale, int64_t* zero_point, float* min_val, float* max_val) {
+    return calibrate_common(batches, sizes, n_batches, symmetric, scale, zero_point, min_val, max_val);
+}
+
+int tvq_calibrate_per_channel_minmax(const float* data, int64_t len, int64_t rows, int64_t cols, float* scales,
+                                     int64_t n_scales) {
+    // engine.tkv:203-206
+    TVQ_CHECK(rows > 0 && cols > 0, TVQ_ERR_INVALID, "rows/cols must be > 0");
+    TVQ_CHECK(len >= rows * cols, TVQ_ERR_SIZE, "data smaller than rows*cols");
+    TVQ_CHECK(data && scales, TVQ_ERR_INVALID, "null buffer");
+    TVQ_CHECK(n_scales >= rows, TVQ_ERR_SIZE, "scales smaller than rows");
+    TVQ_TRY
+    HOST_BEGIN
+    float* dx = dev<float>(H, 0, static_cast<size_t>(rows * cols));
+    int8_t* dq = dev<int8_t>(H, 1, static_cast<size_t>(rows * cols));
+    float* ds = dev<float>(H, 2, static_cast<size_t>(rows));
+    if (H.rc) return H.rc;
+    STEP(H.h2d(dx, data, static_cast<size_t>(rows * cols) * 4));
+    STEP(launch_rowwise(0, dx, dq, ds, rows, cols, H.st()));
+    STEP(H.d2h(scales, ds, static_cast<size_t>(rows) * 4));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_quantize_int8_symmetric(const float* src, int64_t n, int8_t* dst, int64_t dst_len, float scale) {
+    TVQ_CHECK(n >= 0 && dst_len >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(dst_len >= n, TVQ_ERR_SIZE, "dst too small");  // engine.tkv:217-218
+    if (n == 0) return TVQ_OK;
+    TVQ_CHECK(src && dst, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    float* dx = dev<float>(H, 0, static_cast<size_t>(n));
+    int8_t* dq = dev<int8_t>(H, 1, static_cast<size_t>(n));
+    float* ds = dev<float>(H, 2, 1);
+    if (H.rc) return H.rc;
+    STEP(H.h2d(dx, src, static_cast<size_t>(n) * 4));
+    STEP(H.h2d(ds, &scale, 4));
+    STEP(launch_quantize_i8(dx, dq, n, ds, H.st()));
+    STEP(H.d2h(dst, dq, static_cast<size_t>(n)));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_dequantize_int8_symmetric(const int8_t* src, int64_t n, float* dst, int64_t dst_len, float scale) {
+    TVQ_CHECK(n >= 0 && dst_len >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(dst_len >= n, TVQ_ERR_SIZE, "dst too small");  // engine.tkv:230-231
+    if (n == 0) return TVQ_OK;
+    TVQ_CHECK(src && dst, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    int8_t* dq = dev<int8_t>(H, 0, static_cast<size_t>(n));
+    float* dy = dev<float>(H, 1, static_cast<size_t>(n));
+    float* ds = dev<float>(H, 2, 1);
+    if (H.rc) return H.rc;
+    STEP(H.h2d(dq, src, static_cast<size_t>(n)));
+    STEP(H.h2d(ds, &scale, 4));
+    STEP(launch_dequantize_i8(dq, dy, 1, n, ds, 0, H.st()));
+    STEP(H.d2h(dst, dy, static_cast<size_t>(n) * 4));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_quantize_int8_per_channel(const float* src, int64_t src_len, int8_t* dst, int64_t dst_len, int64_t rows,
+                                  int64_t cols, const float* scales, int64_t n_scales) {
+    TVQ_CHECK(rows >= 0 && cols >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(dst_len >= rows * cols && src_len >= rows * cols, TVQ_ERR_SIZE, "span too small");  // :238-239
+    TVQ_CHECK(n_scales >= rows, TVQ_ERR_SIZE, "scales smaller than rows");                       // :240-241
+    if (rows * cols == 0) return TVQ_OK;
+    TVQ_CHECK(src && dst && scales, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    float* dx = dev<float>(H, 0, static_cast<size_t>(rows * cols));
+    int8_t* dq = dev<int8_t>(H, 1, static_cast<size_t>(rows * cols));
+    float* ds = dev<float>(H, 2, static_cast<size_t>(rows));
+    if (H.rc) return H.rc;
+    STEP(H.h2d(dx, src, static_cast<size_t>(rows * cols) * 4));
+    STEP(H.h2d(ds, scales, static_cast<size_t>(rows) * 4));
+    STEP(launch_rowwise(1, dx, dq, ds, rows, cols, H.st()));
+    STEP(H.d2h(dst, dq, static_cast<size_t>(rows * cols)));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_dequantize_int8_per_channel(const int8_t* src, int64_t src_len, float* dst, int64_t dst_len, int64_t rows,
+                                    int64_t cols, const float* scales, int64_t n_scales) {
+    TVQ_CHECK(rows >= 0 && cols >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(dst_len >= rows * cols && src_len >= rows * cols, TVQ_ERR_SIZE, "span too small");
+    TVQ_CHECK(n_scales >= rows, TVQ_ERR_SIZE, "scales smaller than rows");
+    if (rows * cols == 0) return TVQ_OK;
+    TVQ_CHECK(src && dst && scales, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    int8_t* dq = dev<int8_t>(H, 0, static_cast<size_t>(rows * cols));
+    float* dy = dev<float>(H, 1, static_cast<size_t>(rows * cols));
+    float* ds = dev<float>(H, 2, static_cast<size_t>(rows));
+    if (H.rc) return H.rc;
+    STEP(H.h2d(dq, src, static_cast<size_t>(rows * cols)));
+    STEP(H.h2d(ds, scales, static_cast<size_t>(rows) * 4));
+    STEP(launch_dequantize_i8(dq, dy, rows, cols, ds, 1, H.st()));
+    STEP(H.d2h(dst, dy, static_cast<size_t>(rows * cols) * 4));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_quantize_dynamic_int8_rowwise(const float* src, int64_t src_len, int8_t* dst, int64_t dst_len, int64_t rows,
+                                      int64_t cols, float* scales_out, int64_t n_scales) {
+    TVQ_CHECK(rows >= 0 && cols >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(dst_len >= rows * cols && src_len >= rows * cols, TVQ_ERR_SIZE, "span too small");  // :267-268
+    TVQ_CHECK(n_scales >= rows, TVQ_ERR_SIZE, "scales_out smaller than rows");                   // :269-270
+    if (rows == 0) return TVQ_OK;
+    TVQ_CHECK(scales_out && (cols == 0 || (src && dst)), TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    float* dx = dev<float>(H, 0, static_cast<size_t>(std::max<int64_t>(rows * cols, 1)));
+    int8_t* dq = dev<int8_t>(H, 1, static_cast<size_t>(std::max<int64_t>(rows * cols, 1)));
+    float* ds = dev<float>(H, 2, static_cast<size_t>(rows));
+    if (H.rc) return H.rc;
+    if (cols == 0) {
+        // am = 0 -> 1e-8 -> scale fl32(1e-8/127) for every row
+        std::vector<float> s(static_cast<size_t>(rows), static_cast<float>(0.00000001 / 127.0));
+        memcpy(scales_out, s.data(), s.size() * 4);
+        return TVQ_OK;
+    }
+    STEP(H.h2d(dx, src, static_cast<size_t>(rows * cols) * 4));
+    STEP(launch_rowwise(2, dx, dq, ds, rows, cols, H.st()));
+    STEP(H.d2h(dst, dq, static_cast<size_t>(rows * cols)));
+    STEP(H.d2h(scales_out, ds, static_cast<size_t>(rows) * 4));
+    return H.finish();
+    TVQ_CATCH
+}
+
+// ================================================================ host: matmul.tkv
+
+int tvq_matmul_int8_per_channel(const int8_t* A, const int8_t* W, const float* bias, int64_t n_bias, float* Y,
+                                int64_t m, int64_t n, int64_t k, float scale_a, const float* scales_w,
+                                int64_t n_scales, int act) {
+    TVQ_TRY
+    return host_gemm(GEMM_I8, A, W, 1, bias, n_bias, Y, m, n, k, scale_a, scales_w, n_scales, 1, act);
+    TVQ_CATCH
+}
+
+int tvq_matmul_int8_symmetric(const int8_t* A, const int8_t* W, const float* bias, int64_t n_bias, float* Y,
+                              int64_t m, int64_t n, int64_t k, float scale_a, float scale_w, int act) {
+    TVQ_TRY
+    return host_gemm(GEMM_I8, A, W, 1, bias, n_bias, Y, m, n, k, scale_a, &scale_w, 1, 0, act);
+    TVQ_CATCH
+}
+
+int tvq_gemm_i8_acc(const int8_t* A, const int8_t* W, int32_t* acc, int64_t m, int64_t n, int64_t k) {
+    TVQ_CHECK(m >= 0 && n >= 0 && k >= 0, TVQ_ERR_INVALID, "negative size");
+    if (m == 0 || n == 0) return TVQ_OK;
+    TVQ_CHECK(acc && (k == 0 || (A && W)), TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    const int64_t kp = (k + 15) / 16 * 16;
+    uint8_t* dA = dev<uint8_t>(H, 0, static_cast<size_t>(std::max<int64_t>(m * kp, 1)));
+    uint8_t* dW = dev<uint8_t>(H, 1, static_cast<size_t>(std::max<int64_t>(n * kp, 1)));
+    int32_t* dC = dev<int32_t>(H, 2, static_cast<size_t>(m * n));
+    float* dS = dev<float>(H, 3, 2);
+    if (H.rc) return H.rc;
+    if (k > 0) {
+        TVQ_CUDA(cudaMemsetAsync(dA, 0, static_cast<size_t>(m * kp), H.st()));
+        TVQ_CUDA(cudaMemsetAsync(dW, 0, static_cast<size_t>(n * kp), H.st()));
+        TVQ_CUDA(cudaMemcpy2DAsync(dA, kp, A, k, k, m, cudaMemcpyHostToDevice, H.st()));
+        TVQ_CUDA(cudaMemcpy2DAsync(dW, kp, W, k, k, n, cudaMemcpyHostToDevice, H.st()));
+    }
+    const float one[2] = {1.0f, 1.0f};
+    STEP(H.h2d(dS, one, 8));
+    GemmArgs g;
+    g.kind = GEMM_I8;
+    g.A = dA;
+    g.W = dW;
+    g.acc_out = dC;
+    g.m = m;
+    g.n = n;
+    g.k = kp;
+    g.scale_a = dS;
+    g.scales_w = dS + 1;
+    g.per_channel = 0;
+    STEP(launch_gemm(g, H.st()));
+    STEP(H.d2h(acc, dC, static_cast<size_t>(m * n) * 4));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_quantize_fp8_e4m3(const float* src, int64_t n, uint8_t* dst, int64_t dst_len, int mode) {
+    TVQ_CHECK(n >= 0 && dst_len >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(dst_len >= n, TVQ_ERR_SIZE, "dst too small");  // matmul.tkv:61-62
+    TVQ_CHECK(mode == TVQ_FP8_REF || mode == TVQ_FP8_HW, TVQ_ERR_INVALID, "bad FP8 mode");
+    if (n == 0) return TVQ_OK;
+    TVQ_CHECK(src && dst, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    float* dx = dev<float>(H, 0, static_cast<size_t>(n));
+    uint8_t* dq = dev<uint8_t>(H, 1, static_cast<size_t>(n));
+    if (H.rc) return H.rc;
+    STEP(H.h2d(dx, src, static_cast<size_t>(n) * 4));
+    STEP(launch_fp8_encode(dx, dq, 1, n, nullptr, 0, mode, H.st()));
+    STEP(H.d2h(dst, dq, static_cast<size_t>(n)));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_quantize_fp8_e4m3_scaled(const float* src, int64_t rows, int64_t cols, uint8_t* dst, const float* scales,
+                                 int64_t n_scales, int per_row, int mode) {
+    TVQ_CHECK(rows >= 0 && cols >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(mode == TVQ_FP8_REF || mode == TVQ_FP8_HW, TVQ_ERR_INVALID, "bad FP8 mode");
+    TVQ_CHECK(n_scales >= (per_row ? rows : 1), TVQ_ERR_SIZE, "scales smaller than rows");
+    if (rows * cols == 0) return TVQ_OK;
+    TVQ_CHECK(src && dst && scales, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    float* dx = dev<float>(H, 0, static_cast<size_t>(rows * cols));
+    uint8_t* dq = dev<uint8_t>(H, 1, static_cast<size_t>(rows * cols));
+    float* ds = dev<float>(H, 2, static_cast<size_t>(per_row ? rows : 1));
+    if (H.rc) return H.rc;
+    STEP(H.h2d(dx, src, static_cast<size_t>(rows * cols) * 4));
+    STEP(H.h2d(ds, scales, static_cast<size_t>(per_row ? rows : 1) * 4));
+    STEP(launch_fp8_encode(dx, dq, rows, cols, ds, per_row ? 2 : 1, mode, H.st()));
+    STEP(H.d2h(dst, dq, static_cast<size_t>(rows * cols)));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_dequantize_fp8_e4m3(const uint8_t* src, int64_t n, float* dst, int64_t dst_len) {
+    TVQ_CHECK(n >= 0 && dst_len >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(dst_len >= n, TVQ_ERR_SIZE, "dst too small");  // matmul.tkv:69-70
+    if (n == 0) return TVQ_OK;
+    TVQ_CHECK(src && dst, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    uint8_t* dq = dev<uint8_t>(H, 0, static_cast<size_t>(n));
+    float* dy = dev<float>(H, 1, static_cast<size_t>(n));
+    if (H.rc) return H.rc;
+    STEP(H.h2d(dq, src, static_cast<size_t>(n)));
+    STEP(launch_fp8_decode(dq, dy, n, H.st()));
+    STEP(H.d2h(dst, dy, static_cast<size_t>(n) * 4));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_matmul_fp8_e4m3(const uint8_t* A, const uint8_t* W, const float* bias, int64_t n_bias, float* Y, int64_t m,
+                        int64_t n, int64_t k, float scale_a, const float* scales_w, int act) {
+    TVQ_TRY
+    if (scales_w) return host_gemm(GEMM_F8, A, W, 1, bias, n_bias, Y, m, n, k, scale_a, scales_w, n, 1, act);
+    const float one = 1.0f;
+    return host_gemm(GEMM_F8, A, W, 1, bias, n_bias, Y, m, n, k, scale_a, &one, 1, 1, act);
+    TVQ_CATCH
+}
+
+// ---- list[i32] compatibility forms
+int tvq_quantize_int8_symmetric_i32(const float* src, int64_t n, int32_t* dst, int64_t dst_len, float scale) {
+    TVQ_CHECK(n >= 0 && dst_len >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(dst_len >= n, TVQ_ERR_SIZE, "dst too small");
+    if (n == 0) return TVQ_OK;
+    TVQ_CHECK(src && dst, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    float* dx = dev<float>(H, 0, static_cast<size_t>(n));
+    int8_t* dq = dev<int8_t>(H, 1, static_cast<size_t>(n));
+    float* ds = dev<float>(H, 2, 1);
+    int32_t* dw = dev<int32_t>(H, 3, static_cast<size_t>(n));
+    if (H.rc) return H.rc;
+    STEP(H.h2d(dx, src, static_cast<size_t>(n) * 4));
+    STEP(H.h2d(ds, &scale, 4));
+    STEP(launch_quantize_i8(dx, dq, n, ds, H.st()));
+    STEP(launch_widen(dq, dw, n, 0, 0, H.st()));
+    STEP(H.d2h(dst, dw, static_cast<size_t>(n) * 4));
+    return H.finish();
+    TVQ_CATCH
+}
+
+static int narrow_to_host_bytes(const int32_t* src, int64_t n, int32_t off, std::vector<uint8_t>& out) {
+    // The list[i32] values are narrowed on the host: this is boundary
+    // conversion of the caller's storage format, not computation.
+    out.resize(static_cast<size_t>(n));
+    for (int64_t i = 0; i < n; i++) out[static_cast<size_t>(i)] = static_cast<uint8_t>((src[i] + off) & 0xFF);
+    return TVQ_OK;
+}
+
+int tvq_matmul_int8_per_channel_i32(const int32_t* A, const int32_t* W, const float* bias, int64_t n_bias, float* Y,
+                                    int64_t m, int64_t n, int64_t k, float scale_a, const float* scales_w,
+                                    int64_t n_scales) {
+    TVQ_CHECK(m >= 0 && n >= 0 && k >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(n_scales >= n, TVQ_ERR_SIZE, "scales_w smaller than N");  // matmul.tkv:18-19
+    if (m == 0 || n == 0) return TVQ_OK;
+    TVQ_CHECK(k == 0 || (A && W), TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    std::vector<uint8_t> a8, w8;
+    narrow_to_host_bytes(A, m * k, 0, a8);
+    narrow_to_host_bytes(W, n * k, 0, w8);
+    return host_gemm(GEMM_I8, a8.data(), w8.data(), 1, bias, n_bias, Y, m, n, k, scale_a, scales_w, n_scales, 1,
+                     TVQ_ACT_NONE);
+    TVQ_CATCH
+}
+
+int tvq_quantize_fp8_e4m3_i32(const float* src, int64_t n, int32_t* dst, int64_t dst_len) {
+    TVQ_CHECK(n >= 0 && dst_len >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(dst_len >= n, TVQ_ERR_SIZE, "dst too small");
+    if (n == 0) return TVQ_OK;
+    TVQ_CHECK(src && dst, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    float* dx = dev<float>(H, 0, static_cast<size_t>(n));
+    uint8_t* dq = dev<uint8_t>(H, 1, static_cast<size_t>(n));
+    int32_t* dw = dev<int32_t>(H, 2, static_cast<size_t>(n));
+    if (H.rc) return H.rc;
+    STEP(H.h2d(dx, src, static_cast<size_t>(n) * 4));
+    STEP(launch_fp8_encode(dx, dq, 1, n, nullptr, 0, 0, H.st()));
+    STEP(launch_widen(dq, dw, n, 1, -128, H.st()));  // byte - 128, matmul.tkv:65
+    STEP(H.d2h(dst, dw, static_cast<size_t>(n) * 4));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_matmul_fp8_e4m3_i32(const int32_t* A, const int32_t* W, const float* bias, int64_t n_bias, float* Y,
+                            int64_t m, int64_t n, int64_t k) {
+    TVQ_CHECK(m >= 0 && n >= 0 && k >= 0, TVQ_ERR_INVALID, "negative size");
+    if (m == 0 || n == 0) return TVQ_OK;
+    TVQ_CHECK(k == 0 || (A && W), TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    std::vector<uint8_t> a8, w8;
+    narrow_to_host_bytes(A, m * k, 128, a8);  // _fp8_decode(v) reads byte v + 128, matmul.tkv:76
+    narrow_to_host_bytes(W, n * k, 128, w8);
+    const float one = 1.0f;
+    return host_gemm(GEMM_F8, a8.data(), w8.data(), 1, bias, n_bias, Y, m, n, k, 1.0f, &one, 1, 1, TVQ_ACT_NONE);
+    TVQ_CATCH
+}
+
+// ================================================================ device buffers
+
+int tvq_dev_minmax_reset(uint32_t* minmax_dev, void* stream) {
+    TVQ_CHECK(minmax_dev, TVQ_ERR_INVALID, "null buffer");
+    return launch_minmax_reset(minmax_dev, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_minmax_accumulate(const float* x, int64_t n, uint32_t* minmax_dev, float* first_dev, void* stream) {
+    TVQ_CHECK(n >= 0 && minmax_dev && (n == 0 || x), TVQ_ERR_INVALID, "null buffer");
+    return launch_minmax_accumulate(x, n, minmax_dev, first_dev, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_minmax_finalize(const uint32_t* minmax_dev, const float* first_dev, int symmetric, float* params_dev,
+                            void* stream) {
+    TVQ_CHECK(minmax_dev && params_dev, TVQ_ERR_INVALID, "null buffer");
+    return launch_minmax_finalize(minmax_dev, first_dev, symmetric, params_dev, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_quantize_int8(const float* x, int8_t* q, int64_t n, const float* scale_dev, void* stream) {
+    TVQ_CHECK(n >= 0 && (n == 0 || (x && q && scale_dev)), TVQ_ERR_INVALID, "null buffer");
+    return launch_quantize_i8(x, q, n, scale_dev, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_calibrate_quantize_per_channel(const float* w, int8_t* q, float* scales_dev, int64_t rows, int64_t cols,
+                                           void* stream) {
+    TVQ_CHECK(rows >= 0 && cols >= 0 && (rows * cols == 0 || (w && q && scales_dev)), TVQ_ERR_INVALID, "bad args");
+    return launch_rowwise(0, w, q, scales_dev, rows, cols, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_quantize_int8_per_channel(const float* w, int8_t* q, const float* scales_dev, int64_t rows, int64_t cols,
+                                      void* stream) {
+    TVQ_CHECK(rows >= 0 && cols >= 0 && (rows * cols == 0 || (w && q && scales_dev)), TVQ_ERR_INVALID, "bad args");
+    return launch_rowwise(1, w, q, const_cast<float*>(scales_dev), rows, cols, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_quantize_dynamic_rowwise(const float* x, int8_t* q, float* scales_dev, int64_t rows, int64_t cols,
+                                     void* stream) {
+    TVQ_CHECK(rows >= 0 && cols >= 0 && (rows * cols == 0 || (x && q && scales_dev)), TVQ_ERR_INVALID, "bad args");
+    return launch_rowwise(2, x, q, scales_dev, rows, cols, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_quantize_fp8(const float* x, uint8_t* q, int64_t rows, int64_t cols, const float* scales_dev,
+                         int scale_mode, int mode, void* stream) {
+    TVQ_CHECK(rows >= 0 && cols >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(scale_mode >= 0 && scale_mode <= 2 && (scale_mode == 0 || scales_dev), TVQ_ERR_INVALID, "bad scale mode");
+    TVQ_CHECK(mode == TVQ_FP8_REF || mode == TVQ_FP8_HW, TVQ_ERR_INVALID, "bad FP8 mode");
+    return launch_fp8_encode(x, q, rows, cols, scales_dev, scale_mode, mode, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_dequantize_fp8(const uint8_t* q, float* y, int64_t n, void* stream) {
+    TVQ_CHECK(n >= 0 && (n == 0 || (q && y)), TVQ_ERR_INVALID, "null buffer");
+    return launch_fp8_decode(q, y, n, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_gemm(int kind, const void* A, const void* W, const float* bias, const float* residual, float* Y,
+                 int8_t* Yq, int64_t m, int64_t n, int64_t k, const float* scale_a_dev, const float* scales_w_dev,
+                 int per_channel, int act, const float* scale_out_dev, uint32_t* amax_dev, void* stream) {
+    TVQ_CHECK(kind == GEMM_I8 || kind == GEMM_F8, TVQ_ERR_INVALID, "bad GEMM kind");
+    TVQ_CHECK(act == TVQ_ACT_NONE || act == TVQ_ACT_RELU || act == TVQ_ACT_GELU_TANH || act == TVQ_ACT_GELU_ERF,
+              TVQ_ERR_INVALID, "bad activation");
+    TVQ_CHECK(Y || Yq || amax_dev, TVQ_ERR_INVALID, "no output");
+    GemmArgs g;
+    g.kind = kind;
+    g.A = A;
+    g.W = W;
+    g.bias = bias;
+    g.residual = residual;
+    g.Y = Y;
+    g.Yq = Yq;
+    g.m = m;
+    g.n = n;
+    g.k = k;
+    g.scale_a = scale_a_dev;
+    g.scales_w = scales_w_dev;
+    g.per_channel = per_channel;
+    g.act = act;
+    g.scale_out = scale_out_dev;
+    g.amax = amax_dev;
+    TVQ_TRY
+    return launch_gemm(g, static_cast<cudaStream_t>(stream));
+    TVQ_CATCH
+}
+
+}  // extern "C"

@@ -1,0 +1,508 @@
+// tvq_gemm.cu -- quantized GEMM on the 5th-generation tensor cores.
+//
+// Replaces matmul_int8_per_channel / matmul_int8_symmetric / matmul_fp8_e4m3
+// (tv/quantization/matmul.tkv:4-58, inner loop _dot_int8 :116-127) reached
+// from the QuantizedGemm node (tv/runtime/session.tkv:678-697).
+//
+//   Y[m,n] = epilogue( sum_k A[m,k] * W[n,k] )     A [M,K], W [N,K], K-major
+//
+// One persistent CTA per SM (256 threads, 8 warps), warp-specialised:
+//   warp 0      TMA producer: A and W tiles (128 B of K per row, 128-byte
+//               swizzle) into a STAGES-deep shared-memory ring
+//   warp 1      MMA issuer: tcgen05.mma kind::i8 (int32 accumulate) or
+//               kind::f8f6f4 (E4M3, f32 accumulate), 128 x BN x 32 per
+//               instruction, accumulator in tensor memory
+//   warp 2      tensor-memory allocator
+//   warps 4-7   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
+//               lanes 32*(w%4)...), the reference's f64 dequant + bias, an
+//               optional activation, residual add, f32 and/or int8 stores
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the
+// epilogue of tile i overlaps the MMAs of tile i+1.  Every mbarrier wait is
+// bounded (tvq_common.cuh); on a timeout the kernel records an error code,
+// drains its own TMA loads and MMAs, frees TMEM and returns.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "tvq_common.cuh"
+#include "tvq_kernels.h"
+
+namespace tvq {
+
+namespace {
+
+constexpr int BM = 128;        // rows of A per tile (= TMEM lanes)
+constexpr int BK = 128;        // bytes of K per stage (one 128-byte swizzle row)
+constexpr int UMMA_K = 32;     // K per tcgen05.mma for 8-bit operands
+constexpr int THREADS = 256;
+
+struct KParams {
+    int m, n, k;
+    int num_m_blocks, num_n_blocks, num_k_blocks;
+    const float* bias;
+    const float* residual;
+    float* Y;
+    int8_t* Yq;
+    int32_t* acc_out;
+    const float* scale_a;
+    const float* scales_w;
+    int per_channel;
+    int act;
+    const float* scale_out;
+    uint32_t* amax;
+    int* err;
+};
+
+__device__ __forceinline__ float gelu_tanh_f32(float x) {
+    // apply_activation GELU, tv/optimization/kernels.tkv:22-24 + _tanh :32-38
+    const float t = 0.79788456f * (x + 0.044715f * x * x * x);
+    float th;
+    if (t > 10.0f) th = 1.0f;
+    else if (t < -10.0f) th = -1.0f;
+    else { const float e = expf(2.0f * t); th = (e - 1.0f) / (e + 1.0f); }
+    return 0.5f * x * (1.0f + th);
+}
+
+__device__ __forceinline__ float gelu_erf_f32(float v) {
+    // gelu_erf with the Abramowitz-Stegun 7.1.26 erf, tv/training/tensor.tkv:165-190
+    const float x = v * 0.70710678118654752f;
+    const float ax = fabsf(x);
+    const float t = 1.0f / (1.0f + 0.3275911f * ax);
+    float poly = 1.061405429f;
+    poly = poly * t - 1.453152027f;
+    poly = poly * t + 1.421413741f;
+    poly = poly * t - 0.284496736f;
+    poly = poly * t + 0.254829592f;
+    poly = poly * t;
+    float e = 1.0f - expf(-ax * ax) * poly;
+    e = (x < 0.0f) ? -e : e;
+    return 0.5f * v * (1.0f + e);
+}
+
+__device__ __forceinline__ float apply_act(float y, int act) {
+    switch (act) {
+        case TVQ_ACT_RELU: return y > 0.0f ? y : 0.0f;
+        case TVQ_ACT_GELU_TANH: return gelu_tanh_f32(y);
+        case TVQ_ACT_GELU_ERF: return gelu_erf_f32(y);
+        default: return y;
+    }
+}
+
+__device__ __forceinline__ int8_t q8_out(double v) {
+    if (v != v) return 0;
+    double r = rint(v);
+    r = fmin(fmax(r, -127.0), 127.0);
+    return static_cast<int8_t>(static_cast<int>(r));
+}
+
+template <int KIND, int BN>
+__device__ __forceinline__ constexpr uint32_t make_idesc() {
+    // instruction descriptor: [4,6) D format, [7,10) A format, [10,13) B
+    // format, [15]/[16] A/B major (0 = K), [17,23) N>>3, [24,29) M>>4
+    return (KIND == GEMM_I8 ? (2u << 4) | (1u << 7) | (1u << 10)   // S32 <- s8 x s8
+                            : (1u << 4) | (0u << 7) | (0u << 10))  // F32 <- e4m3 x e4m3
+           | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+}
+
+template <int BN>
+struct Cfg {
+    static constexpr uint32_t A_BYTES = BM * BK;
+    static constexpr uint32_t B_BYTES = BN * BK;
+    static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
+    static constexpr uint32_t TMEM_COLS = 2 * BN;  // 128/256/512: powers of two
+    static constexpr uint32_t RING = STAGES * (A_BYTES + B_BYTES);
+    static constexpr uint32_t SMEM = RING + 1024 /*align*/ + 512 /*barriers*/;
+};
+
+template <int KIND, int BN>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, KParams p) {
+    using C = Cfg<BN>;
+    constexpr int STAGES = C::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * C::A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4);
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 2) {
+        tmem_alloc(tmem_holder, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    const int num_tiles = p.num_m_blocks * p.num_n_blocks;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                const int mb = tile % p.num_m_blocks;
+                const int nb = tile / p.num_m_blocks;
+                for (int kb = 0; kb < p.num_k_blocks; kb++, it++) {
+                    const uint32_t s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1u;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, p.err, DEVERR_TIMEOUT_PRODUCER)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES);
+                    tma_load_2d(&tmA, &full[s], sA + s * C::A_BYTES, kb * BK, mb * BM);
+                    tma_load_2d(&tmB, &full[s], sB + s * C::B_BYTES, kb * BK, nb * BN);
+                }
+            }
+            // every issued load lands before the CTA may exit
+            const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0u;
+            for (uint32_t j = first; j < it; j++)
+                mbar_wait(&full[j % STAGES], (j / STAGES) & 1u, p.err, DEVERR_TIMEOUT_DRAIN);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = make_idesc<KIND, BN>();
+            uint32_t it = 0, tcount = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, tcount++) {
+                const uint32_t b = tcount & 1u;
+                const uint32_t aph = (tcount >> 1) & 1u;
+                if (!mbar_wait(&tempty[b], aph ^ 1u, p.err, DEVERR_TIMEOUT_MMA)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + b * BN;
+                for (int kb = 0; kb < p.num_k_blocks; kb++, it++) {
+                    const uint32_t s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1u;
+                    if (!mbar_wait(&full[s], ph, p.err, DEVERR_TIMEOUT_MMA)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + s * C::A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / UMMA_K; kk++) {
+                        const uint64_t ad = smem_desc_k_sw128(a0 + kk * UMMA_K);
+                        const uint64_t bd = smem_desc_k_sw128(b0 + kk * UMMA_K);
+                        const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
+                        if (KIND == GEMM_I8) umma_i8(d_tmem, ad, bd, idesc, accum);
+                        else umma_f8(d_tmem, ad, bd, idesc, accum);
+                    }
+                    umma_commit(&empty[s]);  // stage s is free once these MMAs retire
+                }
+                if (!ok) break;
+                umma_commit(&tfull[b]);      // accumulator b is complete
+            }
+            // all issued MMAs retire before TMEM is released
+            umma_commit(drain);
+            mbar_wait(drain, 0, p.err, DEVERR_TIMEOUT_DRAIN);
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------ epilogue
+        const int eg = warp & 3;  // TMEM lane group this warp may access
+        const bool bias_on = p.bias != nullptr;
+        const double sa = static_cast<double>(__ldg(p.scale_a));
+        const double sw0 = static_cast<double>(__ldg(p.scales_w));
+        const double s_sym = sa * sw0;  // exact: product of two binary32 values
+        double inv_out = 0.0;
+        if (p.Yq) {
+            const double so = static_cast<double>(__ldg(p.scale_out));
+            inv_out = (so > 0.00000001) ? 1.0 / so : 1.0 / 0.00000001;
+        }
+        float amax = 0.0f;
+        uint32_t tcount = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, tcount++) {
+            const uint32_t b = tcount & 1u;
+            const uint32_t aph = (tcount >> 1) & 1u;
+            const bool got = mbar_wait(&tfull[b], aph, p.err, DEVERR_TIMEOUT_EPILOGUE);
+            __syncwarp();
+            if (!__all_sync(0xffffffffu, got)) break;
+            tc_fence_after();
+            const int mb = tile % p.num_m_blocks;
+            const int nb = tile / p.num_m_blocks;
+            const int row = mb * BM + eg * 32 + lane;
+            const bool row_ok = row < p.m;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; c++) {
+                const int n0 = nb * BN + c * 32;
+                if (n0 >= p.n) break;  // warp-uniform
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld32(tmem_base + (static_cast<uint32_t>(eg * 32) << 16) + b * BN + c * 32, r);
+                tmem_ld_wait();
+                if (row_ok) {
+                const bool full_chunk = (n0 + 32 <= p.n);
+                if (p.acc_out) {
+                    int32_t* dst = p.acc_out + static_cast<int64_t>(row) * p.n + n0;
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (n0 + j < p.n) dst[j] = static_cast<int32_t>(r[j]);
+                }
+                float y[32];
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    const int n = n0 + j;
+                    const int nn = (n < p.n) ? n : (p.n - 1);
+                    const double acc = (KIND == GEMM_I8) ? static_cast<double>(static_cast<int32_t>(r[j]))
+                                                         : static_cast<double>(__uint_as_float(r[j]));
+                    const double bb = bias_on ? static_cast<double>(__ldg(p.bias + nn)) : 0.0;
+                    double v;
+                    if (p.per_channel) {
+                        // matmul.tkv:28  acc * scale_a * scales_w[nn] + bias
+                        v = __dadd_rn(__dmul_rn(__dmul_rn(acc, sa), static_cast<double>(__ldg(p.scales_w + nn))), bb);
+                    } else {
+                        // matmul.tkv:5,14  s = scale_a * scale_w ; acc * s + bias
+                        v = __dadd_rn(__dmul_rn(acc, s_sym), bb);
+                    }
+                    y[j] = apply_act(__double2float_rn(v), p.act);
+                }
+                const int64_t base = static_cast<int64_t>(row) * p.n + n0;
+                const bool vec4 = full_chunk && ((p.n & 3) == 0);
+                if (p.residual) {
+                    if (vec4) {
+                        const float4* rs = reinterpret_cast<const float4*>(p.residual + base);
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            const float4 t = __ldg(rs + j);
+                            y[4 * j + 0] = __fadd_rn(y[4 * j + 0], t.x);
+                            y[4 * j + 1] = __fadd_rn(y[4 * j + 1], t.y);
+                            y[4 * j + 2] = __fadd_rn(y[4 * j + 2], t.z);
+                            y[4 * j + 3] = __fadd_rn(y[4 * j + 3], t.w);
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (n0 + j < p.n) y[j] = __fadd_rn(y[j], p.residual[base + j]);
+                    }
+                }
+                if (p.amax) {
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (n0 + j < p.n) amax = fmaxf(amax, fabsf(y[j]));
+                }
+                if (p.Y) {
+                    if (vec4) {
+                        float4* dst = reinterpret_cast<float4*>(p.Y + base);
+#pragma unroll
+                        for (int j = 0; j < 8; j++)
+                            dst[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (n0 + j < p.n) p.Y[base + j] = y[j];
+                    }
+                }
+                if (p.Yq) {
+                    union { int8_t b8[32]; uint4 u[2]; } o;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) o.b8[j] = q8_out(static_cast<double>(y[j]) * inv_out);
+                    if (full_chunk && (p.n & 15) == 0) {
+                        uint4* dst = reinterpret_cast<uint4*>(p.Yq + base);
+                        dst[0] = o.u[0];
+                        dst[1] = o.u[1];
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (n0 + j < p.n) p.Yq[base + j] = o.b8[j];
+                    }
+                }
+                }  // row_ok
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
+        }
+        if (p.amax) {
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 16));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 8));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            if (lane == 0) atomicMax(p.amax, __float_as_uint(amax));
+        }
+    }
+
+    __syncwarp();  // lanes that skipped a single-thread role wait for it here
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+// K == 0: every accumulator is 0, only the epilogue remains (matmul.tkv:14/28
+// with acc = 0).
+__global__ void gemm_k0_kernel(KParams p) {
+    const int64_t total = static_cast<int64_t>(p.m) * p.n;
+    const double sa = static_cast<double>(__ldg(p.scale_a));
+    double inv_out = 0.0;
+    if (p.Yq) {
+        const double so = static_cast<double>(__ldg(p.scale_out));
+        inv_out = (so > 0.00000001) ? 1.0 / so : 1.0 / 0.00000001;
+    }
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int n = static_cast<int>(i % p.n);
+        const double sw = static_cast<double>(__ldg(p.scales_w + (p.per_channel ? n : 0)));
+        const double bb = p.bias ? static_cast<double>(p.bias[n]) : 0.0;
+        const double v = p.per_channel ? __dadd_rn(__dmul_rn(__dmul_rn(0.0, sa), sw), bb) : __dadd_rn(__dmul_rn(0.0, sa * sw), bb);
+        float y = apply_act(__double2float_rn(v), p.act);
+        if (p.residual) y = __fadd_rn(y, p.residual[i]);
+        if (p.acc_out) p.acc_out[i] = 0;
+        if (p.Y) p.Y[i] = y;
+        if (p.Yq) p.Yq[i] = q8_out(static_cast<double>(y) * inv_out);
+        if (p.amax) atomicMax(p.amax, __float_as_uint(fabsf(y)));
+    }
+}
+
+// ---------------------------------------------------------------- host side
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int get_encoder() {
+    std::call_once(g_encode_once, []() {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (!g_encode) {
+        set_error(TVQ_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+        return TVQ_ERR_CUDA;
+    }
+    return TVQ_OK;
+}
+
+// 2-D K-major 8-bit operand [rows, k]: box {128 bytes of K, box_rows}.
+int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box_rows) {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error(TVQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) + ")");
+        return TVQ_ERR_CUDA;
+    }
+    return TVQ_OK;
+}
+
+template <int KIND, int BN>
+int launch_tc(const KParams& p, const void* A, const void* W, int grid, cudaStream_t st) {
+    using C = Cfg<BN>;
+    static int attr_done[64] = {0};  // per device
+    int dev = 0;
+    TVQ_CUDA(cudaGetDevice(&dev));
+    if (dev < 64 && !attr_done[dev]) {
+        TVQ_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<KIND, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(C::SMEM)));
+        attr_done[dev] = 1;
+    }
+    CUtensorMap ma, mb;
+    int rc = make_map(&ma, A, p.m, p.k, BM);
+    if (rc) return rc;
+    rc = make_map(&mb, W, p.n, p.k, BN);
+    if (rc) return rc;
+    gemm_tc_kernel<KIND, BN><<<grid, THREADS, C::SMEM, st>>>(ma, mb, p);
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
+}
+
+}  // namespace
+
+int launch_gemm(const GemmArgs& g, cudaStream_t st) {
+    TVQ_CHECK(g.m >= 0 && g.n >= 0 && g.k >= 0, TVQ_ERR_INVALID, "negative GEMM size");
+    TVQ_CHECK(g.m < (1ll << 31) && g.n < (1ll << 31) && g.k < 133143, TVQ_ERR_UNSUPPORTED,
+              "GEMM size out of range (k must stay below 133143 for exact int32 accumulation)");
+    if (g.m == 0 || g.n == 0) return TVQ_OK;
+    TVQ_CHECK(g.scale_a && g.scales_w, TVQ_ERR_INVALID, "scale pointers are required");
+    TVQ_CHECK(!g.Yq || g.scale_out, TVQ_ERR_INVALID, "int8 output needs scale_out");
+    int rc = 0;
+    DeviceState* ds = device_state(&rc);
+    if (!ds) return rc;
+    TVQ_CHECK(ds->cc_major == 10, TVQ_ERR_UNSUPPORTED, "the tcgen05 GEMM needs an sm_100 device");
+
+    KParams p{};
+    p.m = static_cast<int>(g.m);
+    p.n = static_cast<int>(g.n);
+    p.k = static_cast<int>(g.k);
+    p.bias = g.bias;
+    p.residual = g.residual;
+    p.Y = g.Y;
+    p.Yq = g.Yq;
+    p.acc_out = g.acc_out;
+    p.scale_a = g.scale_a;
+    p.scales_w = g.scales_w;
+    p.per_channel = g.per_channel;
+    p.act = g.act;
+    p.scale_out = g.scale_out;
+    p.amax = g.amax;
+    p.err = ds->d_error;
+    p.num_m_blocks = static_cast<int>((g.m + BM - 1) / BM);
+    p.num_k_blocks = static_cast<int>((g.k + BK - 1) / BK);
+
+    if (g.k == 0) {
+        const int64_t total = g.m * g.n;
+        int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, ds->sm_count * 8));
+        gemm_k0_kernel<<<grid, 256, 0, st>>>(p);
+        TVQ_CUDA(cudaGetLastError());
+        return TVQ_OK;
+    }
+    TVQ_CHECK(g.k % 16 == 0, TVQ_ERR_UNSUPPORTED, "k must be a multiple of 16 (TMA row pitch)");
+    TVQ_CHECK(((reinterpret_cast<uintptr_t>(g.A) | reinterpret_cast<uintptr_t>(g.W)) & 15) == 0, TVQ_ERR_UNSUPPORTED,
+              "A and W must be 16-byte aligned");
+    TVQ_CHECK(!g.Y || (reinterpret_cast<uintptr_t>(g.Y) & 15) == 0, TVQ_ERR_UNSUPPORTED, "Y must be 16-byte aligned");
+    TVQ_CHECK(!g.residual || (reinterpret_cast<uintptr_t>(g.residual) & 15) == 0, TVQ_ERR_UNSUPPORTED,
+              "residual must be 16-byte aligned");
+    TVQ_CHECK(!g.Yq || (reinterpret_cast<uintptr_t>(g.Yq) & 15) == 0, TVQ_ERR_UNSUPPORTED,
+              "Yq must be 16-byte aligned");
+    rc = get_encoder();
+    if (rc) return rc;
+
+    // Tile width: the widest N tile that still gives every SM a tile.
+    int bn = g.force_bn;
+    if (bn == 0) {
+        const int64_t mblk = p.num_m_blocks;
+        if (mblk * ((g.n + 255) / 256) >= ds->sm_count) bn = 256;
+        else if (mblk * ((g.n + 127) / 128) >= ds->sm_count) bn = 128;
+        else bn = 64;
+    }
+    p.num_n_blocks = static_cast<int>((g.n + bn - 1) / bn);
+    const int tiles = p.num_m_blocks * p.num_n_blocks;
+    const int grid = std::min(tiles, ds->sm_count);
+    if (g.kind == GEMM_I8) {
+        if (bn == 256) return launch_tc<GEMM_I8, 256>(p, g.A, g.W, grid, st);
+        if (bn == 128) return launch_tc<GEMM_I8, 128>(p, g.A, g.W, grid, st);
+        return launch_tc<GEMM_I8, 64>(p, g.A, g.W, grid, st);
+    }
+    if (bn == 256) return launch_tc<GEMM_F8, 256>(p, g.A, g.W, grid, st);
+    if (bn == 128) return launch_tc<GEMM_F8, 128>(p, g.A, g.W, grid, st);
+    return launch_tc<GEMM_F8, 64>(p, g.A, g.W, grid, st);
+}
+
+}  // namespace tvq

@@ -1,0 +1,52 @@
+// tvq_kernels.h -- internal launcher declarations of libtvq (not part of the
+// C ABI; the exported surface is include/tvq.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace tvq {
+
+// tvq_quant.cu
+int launch_minmax_reset(uint32_t* mm, cudaStream_t st);
+int launch_minmax_accumulate(const float* x, int64_t n, uint32_t* mm, float* first, cudaStream_t st);
+int launch_minmax_finalize(const uint32_t* mm, const float* first, int symmetric, float* params, cudaStream_t st);
+int launch_quantize_i8(const float* x, int8_t* q, int64_t n, const float* scale_dev, cudaStream_t st);
+int launch_dequantize_i8(const int8_t* q, float* y, int64_t rows, int64_t cols, const float* scales_dev,
+                         int per_row, cudaStream_t st);
+// mode 0: per-channel calibrate+quantize, 1: per-channel quantize with given
+// scales, 2: dynamic row-wise
+int launch_rowwise(int mode, const float* x, int8_t* q, float* scales, int64_t rows, int64_t cols,
+                   cudaStream_t st);
+int launch_fp8_encode(const float* x, uint8_t* q, int64_t rows, int64_t cols, const float* scales, int scale_mode,
+                      int hw, cudaStream_t st);
+int launch_fp8_decode(const uint8_t* q, float* y, int64_t n, cudaStream_t st);
+int launch_widen(const void* src, int32_t* dst, int64_t n, int is_unsigned, int32_t off, cudaStream_t st);
+int launch_narrow(const int32_t* src, void* dst, int64_t n, int32_t off, cudaStream_t st);
+float e4m3_decode_host(uint32_t v);
+uint8_t e4m3_encode_host(float x);
+
+// tvq_gemm.cu
+enum GemmKind { GEMM_I8 = 0, GEMM_F8 = 1 };
+
+struct GemmArgs {
+    int kind = GEMM_I8;
+    const void* A = nullptr;          // [m,k] 8-bit, row-major
+    const void* W = nullptr;          // [n,k] 8-bit, row-major
+    const float* bias = nullptr;      // [n] or null
+    const float* residual = nullptr;  // [m,n] or null
+    float* Y = nullptr;               // [m,n] or null
+    int8_t* Yq = nullptr;             // [m,n] or null
+    int32_t* acc_out = nullptr;       // [m,n] raw accumulators or null (verification)
+    int64_t m = 0, n = 0, k = 0;
+    const float* scale_a = nullptr;   // device [1]
+    const float* scales_w = nullptr;  // device [n] or [1]
+    int per_channel = 1;
+    int act = 0;
+    const float* scale_out = nullptr; // device [1], needed with Yq
+    uint32_t* amax = nullptr;         // device [1] or null
+    int force_bn = 0;                 // 0 = heuristic, else 64/128/256
+};
+int launch_gemm(const GemmArgs& g, cudaStream_t st);
+
+}  // namespace tvq

@@ -1,0 +1,471 @@
+// tvq_quant.cu -- HBM-bound PTQ kernels: min/max calibration, INT8
+// quantize/dequantize, FP8-E4M3 encode/decode.
+//
+// Each kernel restates one function of tv/quantization (paths relative to the
+// TokenVector.Inference repository) with the reference compiler's numeric
+// model: scale arithmetic in binary64, round half to even (Math.Round), int()
+// saturating with NaN -> 0, rounding to binary32 only at typed stores.  The
+// f64 work is a handful of FP64 instructions per element, well under the
+// FP64 rate needed to keep up with HBM.
+//
+// Layout: 16-byte vector loads/stores where the pointers allow it, grid-
+// stride loops over grids sized to a multiple of the SM count, warp-shuffle +
+// shared-memory reductions, one atomic per block.
+#include <cuda_fp8.h>
+
+#include "tvq_common.cuh"
+#include "tvq_kernels.h"
+
+namespace tvq {
+
+// ------------------------------------------------------------ helpers
+
+// Order-preserving map float -> uint32 (for atomicMin/atomicMax of floats).
+__device__ __forceinline__ uint32_t f2ord(float f) {
+    uint32_t b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float ord2f(uint32_t u) {
+    uint32_t b = (u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u;
+    return __uint_as_float(b);
+}
+
+// clamp(int(round(v)), -127, 127) with .NET semantics (NaN -> 0).
+__device__ __forceinline__ int8_t q8(double v) {
+    if (v != v) return 0;
+    double r = rint(v);
+    r = fmin(fmax(r, -127.0), 127.0);
+    return static_cast<int8_t>(static_cast<int>(r));
+}
+
+// inv = 1.0/scale with the 1e-8 floor of engine.tkv:219-222 / 244-246.
+__device__ __forceinline__ double inv_scale(double sc) {
+    return (sc > 0.00000001) ? 1.0 / sc : 1.0 / 0.00000001;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+static int grid_for(int64_t work_items, int threads, int per_sm) {
+    int rc = 0;
+    DeviceState* ds = device_state(&rc);
+    int sms = ds ? ds->sm_count : 148;
+    int64_t want = (work_items + threads - 1) / threads;
+    int64_t cap = static_cast<int64_t>(sms) * per_sm;
+    if (want < 1) want = 1;
+    return static_cast<int>(want < cap ? want : cap);
+}
+
+// ------------------------------------------------------------ K1: min / max
+// calibrate_minmax, tv/quantization/engine.tkv:13-36: the running min and max
+// with `<` / `>` comparisons, so NaN elements never win; NaN in data[0] is
+// handled in the finalize step (it poisons the comparison chain there).
+__global__ void minmax_kernel(const float* __restrict__ x, int64_t n, uint32_t* __restrict__ mm) {
+    float lo = INFINITY, hi = -INFINITY;
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    int64_t n4 = vec ? n / 4 : 0;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    for (int64_t i = tid; i < n4; i += stride) {
+        float4 v = __ldcs(x4 + i);
+        lo = fminf(lo, fminf(fminf(v.x, v.y), fminf(v.z, v.w)));
+        hi = fmaxf(hi, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+    }
+    for (int64_t i = n4 * 4 + tid; i < n; i += stride) {
+        float v = x[i];
+        lo = fminf(lo, v);
+        hi = fmaxf(hi, v);
+    }
+    lo = warp_min(lo);
+    hi = warp_max(hi);
+    __shared__ float slo[32], shi[32];
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) { slo[w] = lo; shi[w] = hi; }
+    __syncthreads();
+    if (w == 0) {
+        const int nw = blockDim.x >> 5;
+        lo = (l < nw) ? slo[l] : INFINITY;
+        hi = (l < nw) ? shi[l] : -INFINITY;
+        lo = warp_min(lo);
+        hi = warp_max(hi);
+        if (l == 0) {
+            if (lo == lo && lo != INFINITY) atomicMin(mm + 0, f2ord(lo));
+            if (hi == hi && hi != -INFINITY) atomicMax(mm + 1, f2ord(hi));
+            // +/-Inf elements are values, not "nothing seen": record them.
+            if (lo == INFINITY && hi == INFINITY) { atomicMin(mm + 0, f2ord(lo)); atomicMax(mm + 1, f2ord(hi)); }
+            if (lo == -INFINITY && hi == -INFINITY) { atomicMin(mm + 0, f2ord(lo)); atomicMax(mm + 1, f2ord(hi)); }
+        }
+    }
+}
+
+__global__ void minmax_reset_kernel(uint32_t* mm) {
+    mm[0] = 0xFFFFFFFFu;  // above every non-NaN ordinal
+    mm[1] = 0u;
+}
+
+__global__ void copy_first_kernel(const float* x, float* first) { *first = x[0]; }
+
+// QuantParams from the accumulated min/max, exactly as engine.tkv:13-36 in
+// f64 with f32 field stores.  params = {scale, zero_point, min, max}.
+__global__ void minmax_finalize_kernel(const uint32_t* mm, const float* first, int symmetric, float* params) {
+    double mn, mx;
+    const bool poisoned = first && (*first != *first);
+    if (poisoned) {
+        mn = mx = __longlong_as_double(0x7FF8000000000000ll);
+    } else if (mm[0] == 0xFFFFFFFFu && mm[1] == 0u) {
+        // nothing but NaNs after data[0]: cannot happen with data[0] finite
+        mn = mx = 0.0;
+    } else {
+        mn = ord2f(mm[0]);
+        mx = ord2f(mm[1]);
+    }
+    if (symmetric) {
+        double am = fabs(mx);
+        if (fabs(mn) > am) am = fabs(mn);
+        if (am < 0.00000001) am = 0.00000001;
+        params[0] = __double2float_rn(am / 127.0);
+        params[1] = 0.0f;
+        params[2] = __double2float_rn(-am);
+        params[3] = __double2float_rn(am);
+        return;
+    }
+    if (fabs(mx - mn) < 0.00000001) mx = mn + 0.00000001;
+    double scale = (mx - mn) / 255.0;
+    double z = -mn / scale;
+    long long zp = (z != z) ? 0 : static_cast<long long>(rint(fmin(fmax(z, -1e18), 1e18)));
+    zp -= 128;
+    zp = zp < -128 ? -128 : (zp > 127 ? 127 : zp);
+    params[0] = __double2float_rn(scale);
+    params[1] = static_cast<float>(zp);
+    params[2] = __double2float_rn(mn);
+    params[3] = __double2float_rn(mx);
+}
+
+int launch_minmax_reset(uint32_t* mm, cudaStream_t st) {
+    minmax_reset_kernel<<<1, 1, 0, st>>>(mm);
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
+}
+
+int launch_minmax_accumulate(const float* x, int64_t n, uint32_t* mm, float* first, cudaStream_t st) {
+    if (n <= 0) return TVQ_OK;
+    if (first) copy_first_kernel<<<1, 1, 0, st>>>(x, first);
+    const int threads = 512;
+    minmax_kernel<<<grid_for((n + 3) / 4, threads, 4), threads, 0, st>>>(x, n, mm);
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
+}
+
+int launch_minmax_finalize(const uint32_t* mm, const float* first, int symmetric, float* params, cudaStream_t st) {
+    minmax_finalize_kernel<<<1, 1, 0, st>>>(mm, first, symmetric, params);
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
+}
+
+// ------------------------------------------------------------ K2: quantize
+// quantize_int8_symmetric, tv/quantization/engine.tkv:216-226:
+// q = clamp(int(round(x * (1.0/scale))), -127, 127).  16 elements per thread
+// step: four 16-byte loads, one 16-byte store.
+__global__ void quantize_i8_kernel(const float* __restrict__ x, int8_t* __restrict__ q, int64_t n,
+                                   const float* __restrict__ scale) {
+    const double inv = inv_scale(static_cast<double>(__ldg(scale)));
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const bool vec = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(q)) & 15) == 0;
+    const int64_t n16 = vec ? n / 16 : 0;
+    for (int64_t i = tid; i < n16; i += stride) {
+        const float4* src = reinterpret_cast<const float4*>(x) + i * 4;
+        float4 v[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) v[j] = __ldcs(src + j);
+        union { int8_t b[16]; uint4 u; } o;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            o.b[4 * j + 0] = q8(static_cast<double>(v[j].x) * inv);
+            o.b[4 * j + 1] = q8(static_cast<double>(v[j].y) * inv);
+            o.b[4 * j + 2] = q8(static_cast<double>(v[j].z) * inv);
+            o.b[4 * j + 3] = q8(static_cast<double>(v[j].w) * inv);
+        }
+        reinterpret_cast<uint4*>(q)[i] = o.u;
+    }
+    for (int64_t i = n16 * 16 + tid; i < n; i += stride) q[i] = q8(static_cast<double>(x[i]) * inv);
+}
+
+int launch_quantize_i8(const float* x, int8_t* q, int64_t n, const float* scale_dev, cudaStream_t st) {
+    if (n <= 0) return TVQ_OK;
+    const int threads = 256;
+    quantize_i8_kernel<<<grid_for((n + 15) / 16, threads, 8), threads, 0, st>>>(x, q, n, scale_dev);
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
+}
+
+// dequantize_int8_symmetric / _per_channel, engine.tkv:229-234, 253-262:
+// fl32(q * scale) is one correctly rounded f32 multiply.
+__global__ void dequantize_i8_kernel(const int8_t* __restrict__ q, float* __restrict__ y, int64_t rows,
+                                     int64_t cols, const float* __restrict__ scales, int per_row) {
+    const int64_t n = rows * cols;
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = tid; i < n; i += stride) {
+        const float s = per_row ? __ldg(scales + i / cols) : __ldg(scales);
+        y[i] = __fmul_rn(static_cast<float>(q[i]), s);
+    }
+}
+
+int launch_dequantize_i8(const int8_t* q, float* y, int64_t rows, int64_t cols, const float* scales_dev,
+                         int per_row, cudaStream_t st) {
+    if (rows * cols <= 0) return TVQ_OK;
+    const int threads = 256;
+    dequantize_i8_kernel<<<grid_for(rows * cols, threads, 8), threads, 0, st>>>(q, y, rows, cols, scales_dev,
+                                                                                per_row);
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
+}
+
+// One warp per row.  mode 0: calibrate_per_channel_minmax (engine.tkv:202-213)
+// fused with quantize_int8_per_channel (engine.tkv:237-250) -- scale[r] =
+// fl32(max(amax,1e-8)/127), then q with inv = 1/max(scale[r],1e-8).
+// mode 1: quantize with given scales.  mode 2: quantize_dynamic_int8_rowwise
+// (engine.tkv:266-285) -- the f64 scale quantizes, its f32 copy is stored.
+template <int MODE>
+__global__ void rowwise_kernel(const float* __restrict__ x, int8_t* __restrict__ q, float* __restrict__ scales,
+                               int64_t rows, int64_t cols) {
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const bool vec = (cols % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(q) & 3) == 0);
+    for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+        const float* xr = x + r * cols;
+        int8_t* qr = q + r * cols;
+        double inv;
+        if (MODE == 1) {
+            inv = inv_scale(static_cast<double>(__ldg(scales + r)));
+        } else {
+            float am = 0.0f;
+            if (vec) {
+                for (int64_t c = lane * 4; c < cols; c += 128) {
+                    float4 v = *reinterpret_cast<const float4*>(xr + c);
+                    am = fmaxf(am, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+                }
+            } else {
+                for (int64_t c = lane; c < cols; c += 32) am = fmaxf(am, fabsf(xr[c]));
+            }
+            am = warp_max(am);
+            double amd = am;
+            bool poisoned = false;
+            if (MODE == 0) poisoned = (xr[0] != xr[0]);   // NaN first element poisons min/max
+            if (amd < 0.00000001) amd = 0.00000001;
+            if (MODE == 0) {
+                float sc = poisoned ? __int_as_float(0x7FC00000) : __double2float_rn(amd / 127.0);
+                if (lane == 0) scales[r] = sc;
+                inv = (sc != sc) ? __longlong_as_double(0x7FF8000000000000ll) : inv_scale(static_cast<double>(sc));
+            } else {
+                double sc = amd / 127.0;
+                if (lane == 0) scales[r] = __double2float_rn(sc);
+                inv = 1.0 / sc;
+            }
+        }
+        if (vec) {
+            for (int64_t c = lane * 4; c < cols; c += 128) {
+                float4 v = *reinterpret_cast<const float4*>(xr + c);
+                char4 o;
+                o.x = q8(static_cast<double>(v.x) * inv);
+                o.y = q8(static_cast<double>(v.y) * inv);
+                o.z = q8(static_cast<double>(v.z) * inv);
+                o.w = q8(static_cast<double>(v.w) * inv);
+                *reinterpret_cast<char4*>(qr + c) = o;
+            }
+        } else {
+            for (int64_t c = lane; c < cols; c += 32) qr[c] = q8(static_cast<double>(xr[c]) * inv);
+        }
+    }
+}
+
+int launch_rowwise(int mode, const float* x, int8_t* q, float* scales, int64_t rows, int64_t cols,
+                   cudaStream_t st) {
+    if (rows <= 0 || cols <= 0) return TVQ_OK;
+    const int threads = 256;
+    const int grid = grid_for(rows * 32, threads, 8);
+    if (mode == 0) rowwise_kernel<0><<<grid, threads, 0, st>>>(x, q, scales, rows, cols);
+    else if (mode == 1) rowwise_kernel<1><<<grid, threads, 0, st>>>(x, q, scales, rows, cols);
+    else rowwise_kernel<2><<<grid, threads, 0, st>>>(x, q, scales, rows, cols);
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
+}
+
+// ------------------------------------------------------------ K3: FP8 E4M3
+
+// Binary32 pattern as tv/runtime/f32_bits.tkv:6-57 produces it for an f32
+// input: the IEEE pattern, except -0.0 -> 0, +/-2^-149 -> +/-0 (its
+// `sh <= 0` test), NaN -> quiet NaN (that loop cannot finish on NaN/Inf).
+__host__ __device__ __forceinline__ uint32_t ref_f32_bits(uint32_t b) {
+    if ((b & 0x7FFFFFFFu) == 0u) return 0u;
+    if ((b & 0x7F800000u) == 0x7F800000u) return (b & 0x007FFFFFu) ? 0x7FC00000u : b;
+    if ((b & 0x7FFFFFFFu) == 1u) return b & 0x80000000u;
+    return b;
+}
+
+// _qt_rne_rshift, tv/quantization/types.tkv:71-93
+__host__ __device__ __forceinline__ int64_t rne_rshift(int64_t v, int64_t s) {
+    if (s > 40) return 0;
+    if (s <= 0) return v;
+    const int64_t half = static_cast<int64_t>(1) << (s - 1);
+    const int64_t q = v >> s;
+    const int64_t rem = v - (q << s);
+    if (rem > half) return q + 1;
+    if (rem < half) return q;
+    return (q & 1) ? q + 1 : q;
+}
+
+// native_fp8_e4m3_encode = _qt_fp8_encode(x, 7, 3, 15, 0, 126),
+// tv/quantization/types.tkv:154-191, 228-230.
+__host__ __device__ __forceinline__ uint8_t e4m3_encode_ref(uint32_t xbits) {
+    const uint32_t b = ref_f32_bits(xbits);
+    const uint32_t sign = b >> 31;
+    const int64_t ex = (b >> 23) & 255;
+    const int64_t man = b & 8388607;
+    if (ex == 255) return static_cast<uint8_t>((sign << 7) | 127u);
+    int64_t e, full;
+    if (ex == 0) { e = -126; full = man; } else { e = ex - 127; full = man | 8388608; }
+    int64_t e8 = e + 7;
+    if (e8 >= 15) return static_cast<uint8_t>((sign << 7) | 126u);
+    if (e8 <= 0) {
+        int64_t m = rne_rshift(full, 24 - 3 - e8);
+        if (m > 7) m = 7;
+        return static_cast<uint8_t>((sign << 7) | static_cast<uint32_t>(m));
+    }
+    int64_t r = rne_rshift(full, 23 - 3);
+    if (r >= 16) {
+        r = 8;
+        e8 = e8 + 1;
+        if (e8 >= 15) return static_cast<uint8_t>((sign << 7) | 126u);
+    }
+    return static_cast<uint8_t>((sign << 7) | static_cast<uint32_t>(e8 << 3) | static_cast<uint32_t>(r - 8));
+}
+
+// native_fp8_e4m3_decode = _qt_fp8_decode(v, 7, 3, 15, 0), types.tkv:193-226,
+// through f32_bits_to_f64 (f32_bits.tkv:60-74): 0x7F/0xFF give +/-Inf (the
+// exponent-255 branch returns 2^129), -0 gives +0 (0.0 - 0.0), subnormal m
+// gives m * 2^-10 (the decoder's exponent is 127 - bias - n).
+__host__ __device__ __forceinline__ float e4m3_decode_ref(uint32_t v) {
+    const uint32_t sign = (v >> 7) & 1;
+    const uint32_t e8 = (v >> 3) & 15;
+    const uint32_t m8 = v & 7;
+    float mag;
+    if (e8 == 15 && m8 == 7) {
+        mag = INFINITY;
+    } else if (e8 == 0) {
+        if (m8 == 0) return 0.0f;
+        mag = static_cast<float>(m8) * 0.0009765625f;  // 2^-10
+    } else {
+        mag = (1.0f + static_cast<float>(m8) * 0.125f) * ldexpf(1.0f, static_cast<int>(e8) - 7);
+    }
+    return sign ? -mag : mag;
+}
+
+__device__ __forceinline__ uint8_t e4m3_encode_hw(float x) {
+    return static_cast<uint8_t>(__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3));
+}
+
+// SCALE: 0 none (quantize_fp8_e4m3, matmul.tkv:60-66), 1 per tensor, 2 per
+// row; the scaled value is fl32(x * (1/scale)) as the encoder's f32 argument.
+template <int SCALE, int HW>
+__global__ void fp8_encode_kernel(const float* __restrict__ x, uint8_t* __restrict__ q, int64_t rows, int64_t cols,
+                                  const float* __restrict__ scales) {
+    const int64_t n = rows * cols;
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    double inv0 = 1.0;
+    if (SCALE == 1) inv0 = inv_scale(static_cast<double>(__ldg(scales)));
+    for (int64_t i = tid; i < n; i += stride) {
+        float v = x[i];
+        if (SCALE == 1) v = __double2float_rn(static_cast<double>(v) * inv0);
+        if (SCALE == 2) v = __double2float_rn(static_cast<double>(v) * inv_scale(static_cast<double>(__ldg(scales + i / cols))));
+        q[i] = HW ? e4m3_encode_hw(v) : e4m3_encode_ref(__float_as_uint(v));
+    }
+}
+
+int launch_fp8_encode(const float* x, uint8_t* q, int64_t rows, int64_t cols, const float* scales, int scale_mode,
+                      int hw, cudaStream_t st) {
+    const int64_t n = rows * cols;
+    if (n <= 0) return TVQ_OK;
+    const int threads = 256;
+    const int grid = grid_for(n, threads, 8);
+#define TVQ_FP8_LAUNCH(S, H) fp8_encode_kernel<S, H><<<grid, threads, 0, st>>>(x, q, rows, cols, scales)
+    if (scale_mode == 0) { if (hw) TVQ_FP8_LAUNCH(0, 1); else TVQ_FP8_LAUNCH(0, 0); }
+    else if (scale_mode == 1) { if (hw) TVQ_FP8_LAUNCH(1, 1); else TVQ_FP8_LAUNCH(1, 0); }
+    else { if (hw) TVQ_FP8_LAUNCH(2, 1); else TVQ_FP8_LAUNCH(2, 0); }
+#undef TVQ_FP8_LAUNCH
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
+}
+
+__global__ void fp8_decode_kernel(const uint8_t* __restrict__ q, float* __restrict__ y, int64_t n) {
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = tid; i < n; i += stride) y[i] = e4m3_decode_ref(q[i]);
+}
+
+int launch_fp8_decode(const uint8_t* q, float* y, int64_t n, cudaStream_t st) {
+    if (n <= 0) return TVQ_OK;
+    const int threads = 256;
+    fp8_decode_kernel<<<grid_for(n, threads, 8), threads, 0, st>>>(q, y, n);
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
+}
+
+// ------------------------------------------------------------ list[i32] forms
+__global__ void i8_to_i32_kernel(const int8_t* __restrict__ a, int32_t* __restrict__ b, int64_t n, int32_t off) {
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = tid; i < n; i += stride) b[i] = static_cast<int32_t>(a[i]) + off;
+}
+__global__ void u8_to_i32_kernel(const uint8_t* __restrict__ a, int32_t* __restrict__ b, int64_t n, int32_t off) {
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = tid; i < n; i += stride) b[i] = static_cast<int32_t>(a[i]) + off;
+}
+// list[i32] -> bytes: int8 values wrap as the reference's int() of an
+// already-clamped value; FP8 values are byte - 128 (matmul.tkv:65, :76).
+__global__ void i32_to_u8_kernel(const int32_t* __restrict__ a, uint8_t* __restrict__ b, int64_t n, int32_t off) {
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = tid; i < n; i += stride) b[i] = static_cast<uint8_t>((a[i] + off) & 0xFF);
+}
+
+int launch_widen(const void* src, int32_t* dst, int64_t n, int is_unsigned, int32_t off, cudaStream_t st) {
+    if (n <= 0) return TVQ_OK;
+    const int threads = 256;
+    const int grid = grid_for(n, threads, 8);
+    if (is_unsigned) u8_to_i32_kernel<<<grid, threads, 0, st>>>(static_cast<const uint8_t*>(src), dst, n, off);
+    else i8_to_i32_kernel<<<grid, threads, 0, st>>>(static_cast<const int8_t*>(src), dst, n, off);
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
+}
+
+int launch_narrow(const int32_t* src, void* dst, int64_t n, int32_t off, cudaStream_t st) {
+    if (n <= 0) return TVQ_OK;
+    const int threads = 256;
+    i32_to_u8_kernel<<<grid_for(n, threads, 8), threads, 0, st>>>(src, static_cast<uint8_t*>(dst), n, off);
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
+}
+
+// Host copy of the reference decoder for the C ABI's scalar helpers.
+float e4m3_decode_host(uint32_t v) { return e4m3_decode_ref(v); }
+uint8_t e4m3_encode_host(float x) {
+    uint32_t b;
+    memcpy(&b, &x, 4);
+    return e4m3_encode_ref(b);
+}
+
+}  // namespace tvq
