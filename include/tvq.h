@@ -179,6 +179,74 @@ TVQ_API int tvq_dev_gemm(int kind, const void* A, const void* W, const float* bi
                  const float* scales_w_dev, int per_channel, int act, const float* scale_out_dev,
                  uint32_t* amax_dev, void* stream);
 
+/* ================================================================ fp32 glue, device buffers
+ * gpt2_layernorm, tv/training/gpt2_ref.tkv:50-78 (f64 statistics): y (f32)
+ * and/or q = int8 with the static scale qscale_dev[0]; amax_dev records
+ * max|y| (calibration). */
+TVQ_API int tvq_dev_layernorm(const float* x, const float* gamma, const float* beta, float* y, int8_t* q,
+                              const float* qscale_dev, uint32_t* amax_dev, int64_t rows, int64_t d, double eps,
+                              void* stream);
+/* Causal multi-head attention of gpt2_attention (gpt2_ref.tkv:360-395, no
+ * projection) over packed sequences seg[0..n_seg] (host offsets): qkv f32
+ * [T, 3d] rows [Q|K|V]; out f32 [T, d] and/or outq int8 (scale qscale_dev).
+ * tiles_dev: device scratch of 4 x int32 per 64-row query tile, 16-byte
+ * aligned, tiles_cap tiles.  fp32 arithmetic: within 1e-5 of the f64 oracle. */
+TVQ_API int tvq_dev_attention(const float* qkv, const int64_t* seg, int64_t n_seg, int64_t d, int64_t n_heads,
+                              int32_t* tiles_dev, int64_t tiles_cap, float* out, int8_t* outq,
+                              const float* qscale_dev, uint32_t* amax_dev, void* stream);
+
+/* ================================================================ sessions
+ * Device-resident GPT-2-shaped INT8 PTQ stack: embeddings, n_layers blocks of
+ * (ln_1, c_attn, attention, c_proj, ln_2, c_fc, GELU-erf, mlp c_proj) with the
+ * four linears as QuantizedGemm (session.tkv:678-697), ln_f and the tied fp32
+ * LM head (gpt2_ref.tkv:575-610).  Replaces InferenceSession construction +
+ * run (session.tkv:3376-3436) for graphs of this shape.  One handle per GPU. */
+TVQ_API int tvq_session_create(int device, int64_t vocab, int64_t d_model, int64_t n_heads, int64_t n_layers,
+                               int64_t d_ffn, int64_t max_pos, double ln_eps, int64_t max_tokens, int64_t* handle);
+TVQ_API int tvq_session_destroy(int64_t handle);
+/* wte f32 [vocab, d] (also the LM head), wpe f32 [max_pos, d], host. */
+TVQ_API int tvq_session_set_embeddings(int64_t handle, const float* wte, const float* wpe);
+/* layer -1 = ln_f; which 0 = ln_1, 1 = ln_2. */
+TVQ_API int tvq_session_set_layernorm(int64_t handle, int64_t layer, int64_t which, const float* gamma,
+                                      const float* beta);
+/* which 0 c_attn [3d x d], 1 attn c_proj [d x d], 2 c_fc [ffn x d], 3 mlp
+ * c_proj [d x ffn]; f32 weights quantized on the GPU per output channel
+ * (calibrate_per_channel_minmax + quantize_int8_per_channel, engine.tkv:202-250).
+ * layout 0 = [k, n] (HF Conv1D, gpt2_ref.tkv:91-117), 1 = [n, k]. */
+TVQ_API int tvq_session_set_linear_f32(int64_t handle, int64_t layer, int64_t which, const float* w,
+                                       const float* bias, int layout);
+/* Pre-quantized weights [n, k] with per-channel scales (the QuantizedGemm
+ * node's initializers_int8 + scales_w, session.tkv:3149, 497-505). */
+TVQ_API int tvq_session_set_linear_i8(int64_t handle, int64_t layer, int64_t which, const int8_t* w_nk,
+                                      const float* scales_w, const float* bias);
+TVQ_API int tvq_session_get_linear_i8(int64_t handle, int64_t layer, int64_t which, int8_t* w_nk, float* scales_w);
+/* Static activation scales, 4 per layer: ln_1 out, attention context, ln_2
+ * out, GELU out (the scale_a of the four QuantizedGemm nodes). */
+TVQ_API int tvq_session_set_act_scales(int64_t handle, const float* scales, int64_t n);
+TVQ_API int tvq_session_get_act_scales(int64_t handle, float* scales, int64_t n);
+/* Batch layout: seg[0..n_seg] packed sequence offsets (seg[0] = 0, total
+ * tokens seg[n_seg] <= max_tokens); logits_mode 0 = logits for every token,
+ * 1 = for the last token of each sequence. */
+TVQ_API int tvq_session_prepare(int64_t handle, const int64_t* seg, int64_t n_seg, int logits_mode);
+/* Calibration forward on ids (host or device): records max|x| at the four
+ * quantization points of every layer (running max unless reset) and sets
+ * the static scales from it. */
+TVQ_API int tvq_session_calibrate(int64_t handle, const int64_t* ids, int ids_on_device, int reset);
+/* One INT8 forward (CUDA graph) on `stream` (NULL: the session's own).
+ * ids NULL = reuse the resident ids.  logits NULL = keep them on the device
+ * (see tvq_session_logits).  Host buffers make the call synchronous. */
+TVQ_API int tvq_session_forward(int64_t handle, const int64_t* ids, int ids_on_device, float* logits,
+                                int64_t logits_len, int logits_on_device, void* stream);
+TVQ_API int tvq_session_logits(int64_t handle, float** logits_dev, int64_t* rows, int64_t* cols);
+TVQ_API int tvq_session_sync(int64_t handle);
+/* Profiling: with enable = 1 the captured forward records a CUDA event after
+ * every stage; tvq_session_stage_times then returns the last forward's time
+ * per stage class in ms: [0] embedding, [1] layernorms, [2] c_attn GEMMs,
+ * [3] attention, [4] attn c_proj GEMMs, [5] c_fc GEMMs, [6] mlp c_proj GEMMs,
+ * [7] LM head. */
+TVQ_API int tvq_session_set_profiling(int64_t handle, int enable);
+TVQ_API int tvq_session_stage_times(int64_t handle, float* ms, int64_t n);
+
 #ifdef __cplusplus
 }
 #endif

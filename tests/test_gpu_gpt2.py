@@ -1,0 +1,176 @@
+"""GPU parity of the GPT-2 INT8 PTQ stack: glue kernels layer by layer, and
+the whole device-resident session against the oracle composition
+(oracle/gpt2_int8.py) on the same seeded inputs.
+
+Tolerances (written here, used below): LayerNorm and LayerNorm->int8 are
+bit-exact; attention (fp32 flash tiling vs the oracle's f64) within
+rtol 1e-4 / atol 2e-6; whole-model logits within atol 2e-3 with mean
+|diff| < 2e-4 (fp32 attention/GELU may move an activation across an int8
+rounding boundary; the quantized weights and the calibrated scales are
+compared separately, weights bit-exact and scales to 1e-5 relative)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle as O
+from oracle import gpt2_int8 as OG
+from tokenvector.inference_b200 import _native as N
+from tokenvector.inference_b200.gpt2 import GPT2Config, GPT2Session, GPT2Weights, gi_noise, segments_from_lengths
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dev="cuda:0"):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _ptr(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def test_product_generator_matches_reference_generator():
+    # gpt2_ref.tkv:1977-1991 restated in the product (numpy) and the oracle (C)
+    for seed in (1, 12, 1234567):
+        assert np.array_equal(gi_noise(10007, seed), O.gi_noise(10007, seed))
+
+
+@pytest.mark.parametrize("rows,d", [(1, 64), (300, 768), (77, 1600)])
+def test_layernorm_and_quantize_bit_exact(rows, d):
+    import torch
+    rng = np.random.default_rng(rows)
+    x = (rng.standard_normal((rows, d)) * 3 + 0.7).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(d)).astype(np.float32)
+    tx, tg, tb = _t(x), _t(g), _t(b)
+    y = torch.empty((rows, d), dtype=torch.float32, device="cuda:0")
+    q = torch.empty((rows, d), dtype=torch.int8, device="cuda:0")
+    am = torch.zeros(1, dtype=torch.int32, device="cuda:0")
+    ref = O.layernorm(x, g, b, 1e-6)
+    s = np.float32(np.abs(ref).max() / 127.0)
+    ts = _t(np.array([s], np.float32))
+    N.call("tvq_dev_layernorm", _ptr(tx), _ptr(tg), _ptr(tb), _ptr(y), _ptr(q), _ptr(ts), _ptr(am), rows, d, 1e-6,
+           None)
+    torch.cuda.synchronize()
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    assert np.array_equal(q.cpu().numpy(), O.quantize_int8_symmetric(ref, s))
+    assert am.cpu().numpy().view(np.float32)[0] == np.abs(ref).max()
+
+
+@pytest.mark.parametrize("lengths,d,heads", [([1], 64, 4), ([8], 64, 4), ([100, 37, 64, 1], 128, 2),
+                                             ([1024], 768, 12), ([200, 300], 1600, 25)])
+def test_attention_causal_packed(lengths, d, heads):
+    import torch
+    seg = segments_from_lengths(lengths)
+    T = int(seg[-1])
+    rng = np.random.default_rng(T + d)
+    qkv = rng.standard_normal((T, 3 * d)).astype(np.float32)
+    tq = _t(qkv)
+    out = torch.empty((T, d), dtype=torch.float32, device="cuda:0")
+    tiles = torch.empty((T + 64) * 4, dtype=torch.int32, device="cuda:0")
+    N.call("tvq_dev_attention", _ptr(tq), seg.ctypes.data_as(C.c_void_p), seg.size - 1, d, heads, _ptr(tiles),
+           T + 64, _ptr(out), None, None, None, None)
+    torch.cuda.synchronize()
+    ref = O.attention_causal(qkv, heads, seg)
+    assert np.allclose(out.cpu().numpy(), ref, rtol=1e-4, atol=2e-6)
+
+
+def _small_cfg():
+    return GPT2Config(vocab=512, d_model=128, n_heads=2, n_layers=2, d_ffn=512, max_pos=256)
+
+
+def _ids(n, vocab, seed):
+    return np.random.default_rng(seed).integers(0, vocab, n).astype(np.int64)
+
+
+def test_session_weights_quantized_like_reference():
+    cfg = _small_cfg()
+    w = GPT2Weights.random(cfg, seed=3)
+    s = GPT2Session(w, max_tokens=256)
+    qw = OG.quantize_weights(w.layers)
+    for li in range(cfg.n_layers):
+        for which in range(4):
+            gw, gs = s.linear_i8(li, which)
+            assert np.array_equal(gw, qw[li][which][0]) and np.array_equal(gs.view(np.uint32),
+                                                                             qw[li][which][1].view(np.uint32))
+    s.close()
+
+
+@pytest.mark.parametrize("lengths", [[201], [37, 64, 100]])
+def test_session_matches_oracle_composition(lengths):
+    cfg = _small_cfg()
+    w = GPT2Weights.random(cfg, seed=5)
+    seg = segments_from_lengths(lengths)
+    T = int(seg[-1])
+    calib_ids, ids = _ids(T, cfg.vocab, 1), _ids(T, cfg.vocab, 2)
+    s = GPT2Session(w, max_tokens=256)
+    s.prepare(seg, logits_mode=0)
+    s.calibrate(calib_ids)
+    g_scales = s.act_scales()
+    qw = OG.quantize_weights(w.layers)
+    cal = OG.Calibrator(cfg.n_layers)
+    OG.forward(w, calib_ids, seg, calibrator=cal, qweights=qw, n_heads=cfg.n_heads)
+    o_scales = cal.scales()
+    assert np.allclose(g_scales, o_scales, rtol=1e-5, atol=0)
+    # same static scales on both sides, then the INT8 forward
+    s.set_act_scales(o_scales)
+    got = s.forward(ids)
+    ref = OG.forward(w, ids, seg, scales=o_scales, qweights=qw, n_heads=cfg.n_heads)
+    diff = np.abs(got - ref)
+    assert diff.max() < 2e-3 and diff.mean() < 2e-4, (diff.max(), diff.mean())
+    # last-token logits are the same rows
+    s.prepare(seg, logits_mode=1)
+    last = s.forward(ids)
+    assert np.array_equal(last, got[seg[1:] - 1])
+    s.close()
+
+
+def test_session_on_reference_fixture_weights():
+    """The reduced GPT-2 of tv/tests/fixtures/g2_* (vocab 256, d 64, 4 heads,
+    2 layers, 8 tokens) through the INT8 session: equal to the oracle INT8
+    composition, and close to the reference's fp32 torch logits."""
+    import os
+    d = np.load(os.path.join(os.path.dirname(__file__), "golden", "g2_reduced.npz"))
+    cfg = GPT2Config(vocab=256, d_model=64, n_heads=4, n_layers=2, d_ffn=256, max_pos=32)
+    w = GPT2Weights(cfg, d["w_wte"].reshape(256, 64), d["w_wpe"].reshape(32, 64), d["w_lnf_g"], d["w_lnf_b"])
+    for i in range(2):
+        w.layers.append(dict(ln1_g=d[f"w_ln1_g{i}"], ln1_b=d[f"w_ln1_b{i}"],
+                             attn_w=d[f"w_attn_w{i}"].reshape(64, 192), attn_b=d[f"w_attn_b{i}"],
+                             proj_w=d[f"w_proj_w{i}"].reshape(64, 64), proj_b=d[f"w_proj_b{i}"],
+                             ln2_g=d[f"w_ln2_g{i}"], ln2_b=d[f"w_ln2_b{i}"],
+                             fc_w=d[f"w_mlp_w1{i}"].reshape(64, 256), fc_b=d[f"w_mlp_b1{i}"],
+                             mp_w=d[f"w_mlp_w2{i}"].reshape(256, 64), mp_b=d[f"w_mlp_b2{i}"]))
+    ids = d["ids"]
+    seg = np.array([0, 8], np.int64)
+    s = GPT2Session(w, max_tokens=8)
+    s.prepare(seg)
+    s.calibrate(ids)
+    cal = OG.Calibrator(2)
+    qw = OG.quantize_weights(w.layers)
+    OG.forward(w, ids, seg, calibrator=cal, qweights=qw, n_heads=4)
+    assert np.allclose(s.act_scales(), cal.scales(), rtol=1e-5, atol=0)
+    s.set_act_scales(cal.scales())
+    got = s.forward(ids)
+    ref = OG.forward(w, ids, seg, scales=cal.scales(), qweights=qw, n_heads=4)
+    assert np.abs(got - ref).max() < 2e-3
+    fp32 = d["logits"].reshape(8, 256)
+    assert np.abs(got - fp32).max() < 0.05  # PTQ error of INT8 weights+activations
+    s.close()
+
+
+def test_session_errors():
+    cfg = _small_cfg()
+    w = GPT2Weights.random(cfg, seed=7)
+    s = GPT2Session(w, max_tokens=64)
+    with pytest.raises(ValueError):
+        s.prepare(np.array([0, 300], np.int64))       # longer than max_tokens
+    s.prepare(np.array([0, 10], np.int64))
+    bad = np.full(10, cfg.vocab + 5, np.int64)
+    with pytest.raises(N.TvqError):
+        s.forward(bad)                                   # token id out of range
+    ok = s.forward(np.zeros(10, np.int64))               # session still usable
+    assert np.isfinite(ok).all()
+    s.close()
+    with pytest.raises(N.TvqError):
+        N.call("tvq_session_sync", s.handle if s.handle else 999999)

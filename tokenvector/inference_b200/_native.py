@@ -64,6 +64,24 @@ SIGNATURES = {
     "tvq_dev_quantize_fp8": (i32, [P, P, i64, i64, P, i32, i32, P]),
     "tvq_dev_dequantize_fp8": (i32, [P, P, i64, P]),
     "tvq_dev_gemm": (i32, [i32, P, P, P, P, P, P, i64, i64, i64, P, P, i32, i32, P, P, P]),
+    "tvq_dev_layernorm": (i32, [P, P, P, P, P, P, P, i64, i64, C.c_double, P]),
+    "tvq_dev_attention": (i32, [P, P, i64, i64, i64, P, i64, P, P, P, P, P]),
+    "tvq_session_create": (i32, [i32, i64, i64, i64, i64, i64, i64, C.c_double, i64, P]),
+    "tvq_session_destroy": (i32, [i64]),
+    "tvq_session_set_embeddings": (i32, [i64, P, P]),
+    "tvq_session_set_layernorm": (i32, [i64, i64, i64, P, P]),
+    "tvq_session_set_linear_f32": (i32, [i64, i64, i64, P, P, i32]),
+    "tvq_session_set_linear_i8": (i32, [i64, i64, i64, P, P, P]),
+    "tvq_session_get_linear_i8": (i32, [i64, i64, i64, P, P]),
+    "tvq_session_set_act_scales": (i32, [i64, P, i64]),
+    "tvq_session_get_act_scales": (i32, [i64, P, i64]),
+    "tvq_session_prepare": (i32, [i64, P, i64, i32]),
+    "tvq_session_calibrate": (i32, [i64, P, i32, i32]),
+    "tvq_session_forward": (i32, [i64, P, i32, P, i64, i32, P]),
+    "tvq_session_logits": (i32, [i64, P, P, P]),
+    "tvq_session_sync": (i32, [i64]),
+    "tvq_session_set_profiling": (i32, [i64, i32]),
+    "tvq_session_stage_times": (i32, [i64, P, i64]),
 }
 
 _lib = None

@@ -546,8 +546,8 @@ int tvq_matmul_fp8_e4m3(const uint8_t* A, const uint8_t* W, const float* bias, i
                         int64_t n, int64_t k, float scale_a, const float* scales_w, int act) {
     TVQ_TRY
     if (scales_w) return host_gemm(GEMM_F8, A, W, 1, bias, n_bias, Y, m, n, k, scale_a, scales_w, n, 1, act);
-    const float one = 1.0f;
-    return host_gemm(GEMM_F8, A, W, 1, bias, n_bias, Y, m, n, k, scale_a, &one, 1, 1, act);
+    const float one = 1.0f;  // unscaled reference form: acc * (scale_a * 1) + bias
+    return host_gemm(GEMM_F8, A, W, 1, bias, n_bias, Y, m, n, k, scale_a, &one, 1, 0, act);
     TVQ_CATCH
 }
 
@@ -626,7 +626,7 @@ int tvq_matmul_fp8_e4m3_i32(const int32_t* A, const int32_t* W, const float* bia
     narrow_to_host_bytes(A, m * k, 128, a8);  // _fp8_decode(v) reads byte v + 128, matmul.tkv:76
     narrow_to_host_bytes(W, n * k, 128, w8);
     const float one = 1.0f;
-    return host_gemm(GEMM_F8, a8.data(), w8.data(), 1, bias, n_bias, Y, m, n, k, 1.0f, &one, 1, 1, TVQ_ACT_NONE);
+    return host_gemm(GEMM_F8, a8.data(), w8.data(), 1, bias, n_bias, Y, m, n, k, 1.0f, &one, 1, 0, TVQ_ACT_NONE);
     TVQ_CATCH
 }
 

@@ -281,10 +281,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const bool vec4 = full_chunk && ((p.n & 3) == 0);
                 if (p.residual) {
                     if (vec4) {
+                        // plain loads: the residual may alias Y (in-place residual stream)
                         const float4* rs = reinterpret_cast<const float4*>(p.residual + base);
 #pragma unroll
                         for (int j = 0; j < 8; j++) {
-                            const float4 t = __ldg(rs + j);
+                            const float4 t = rs[j];
                             y[4 * j + 0] = __fadd_rn(y[4 * j + 0], t.x);
                             y[4 * j + 1] = __fadd_rn(y[4 * j + 1], t.y);
                             y[4 * j + 2] = __fadd_rn(y[4 * j + 2], t.z);

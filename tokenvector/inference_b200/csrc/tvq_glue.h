@@ -1,0 +1,22 @@
+// tvq_glue.h -- launchers of the fp32 GPT-2 glue kernels (tvq_glue.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace tvq {
+
+int launch_embed(const int64_t* ids, const int* tok_seg_start, const float* wte, const float* wpe, float* x, int T,
+                 int d, int vocab, int max_pos, int* err, cudaStream_t st);
+// y (f32) and/or q (int8 with qscale) and/or amax of y
+int launch_layernorm(const float* x, const float* g, const float* b, float* y, int8_t* q, const float* qscale,
+                     uint32_t* amax, int T, int d, double eps, cudaStream_t st);
+// tiles: int4 {q0, seg_start, seg_end, 0} per 64-row query tile
+int launch_attention(const float* qkv, const int4* tiles, int ntiles, int T, int d, int nheads, float* out,
+                     int8_t* outq, const float* qscale, uint32_t* amax, cudaStream_t st);
+int launch_scale_from_amax(const uint32_t* amax, float* scale, int n, cudaStream_t st);
+int launch_transpose(const float* a, float* b, int rows, int cols, cudaStream_t st);
+int launch_token_seg(const int* seg, int nseg, int* tok_start, cudaStream_t st);
+int launch_gather_last(const float* src, const int* seg, int nseg, int64_t n, float* dst, cudaStream_t st);
+
+}  // namespace tvq

@@ -1,0 +1,662 @@
+// tvq_session.cu -- device-resident executor for GPT-2-shaped stacks of
+// QuantizedGemm layers (the tvq_session_* part of include/tvq.h).
+//
+// Replaces, for this path, InferenceSession.run -> ExecutionNode.execute ->
+// the QuantizedGemm branch (tv/runtime/session.tkv:3403-3436, 678-697) and
+// the initialize_weights upload (:3336-3350): weights are uploaded and
+// quantized once, the whole forward (embedding, 4 INT8 linears per block,
+// fp32 LayerNorm / attention / GELU, LM head) runs on one stream with no host
+// round trip and is captured into a CUDA graph per batch layout.
+//
+// Per layer l the four activation quantization points use static per-tensor
+// scales act_scale[4l + i] (i = 0 ln_1 output, 1 attention context, 2 ln_2
+// output, 3 GELU output).  A calibration forward computes them on the GPU as
+// calibrate_minmax would (tv/quantization/engine.tkv:13-36: scale =
+// fl32(max(max|x|, 1e-8) / 127)), with the running max over calibration
+// batches, and quantizes each activation with its own scale as it goes.
+#include <cublas_v2.h>
+
+#include <algorithm>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <vector>
+
+#include "tvq_common.cuh"
+#include "tvq_glue.h"
+#include "tvq_kernels.h"
+
+namespace tvq {
+namespace {
+
+struct Lin {
+    int8_t* W = nullptr;  // [n, k]
+    float* sw = nullptr;  // [n]
+    float* bias = nullptr;
+    int n = 0, k = 0;
+    bool set = false;
+};
+
+struct LayerW {
+    float* ln[4] = {nullptr, nullptr, nullptr, nullptr};  // ln_1 g, b, ln_2 g, b
+    Lin lin[4];                                          // c_attn, attn c_proj, c_fc, mlp c_proj
+};
+
+struct Session {
+    int device = 0;
+    cudaStream_t st = nullptr;
+    cublasHandle_t blas = nullptr;
+    void* blas_ws = nullptr;
+    int vocab = 0, d = 0, heads = 0, layers = 0, ffn = 0, max_pos = 0, max_tokens = 0;
+    double eps = 1e-6;
+    std::vector<void*> allocs;
+    float *wte = nullptr, *wpe = nullptr, *lnf_g = nullptr, *lnf_b = nullptr;
+    std::vector<LayerW> L;
+    float* act_scale = nullptr;
+    uint32_t* act_amax = nullptr;
+    int64_t* ids = nullptr;
+    int* seg = nullptr;
+    int* tok_start = nullptr;
+    int4* tiles = nullptr;
+    float *x = nullptr, *qkv = nullptr, *hf = nullptr, *xf = nullptr, *xf_last = nullptr, *logits = nullptr;
+    size_t logits_cap = 0;
+    int8_t *aq = nullptr, *hq = nullptr;
+    int* err = nullptr;
+    // batch layout
+    std::vector<int> seg_host;
+    int T = 0, nseg = 0, ntiles = 0, logits_mode = 0;
+    bool prepared = false;
+    cudaGraphExec_t gexec = nullptr;
+    // optional stage events recorded inside the captured graph (profiling)
+    bool profile = false;
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> ev_stage;  // stage id of the interval ending at ev[i]
+    bool capturing = false;
+
+    int64_t logits_rows() const { return logits_mode == 0 ? T : nseg; }
+
+    ~Session() {
+        if (gexec) cudaGraphExecDestroy(gexec);
+        for (cudaEvent_t e : ev) cudaEventDestroy(e);
+        if (blas) cublasDestroy(blas);
+        for (void* p : allocs) cudaFree(p);
+        if (st) cudaStreamDestroy(st);
+    }
+    template <typename T_>
+    int alloc(T_** p, size_t count) {
+        void* q = nullptr;
+        cudaError_t e = cudaMalloc(&q, std::max<size_t>(count * sizeof(T_), 256));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (session)");
+        allocs.push_back(q);
+        *p = static_cast<T_*>(q);
+        return TVQ_OK;
+    }
+};
+
+std::mutex g_mu;
+std::map<int64_t, std::unique_ptr<Session>> g_sessions;
+int64_t g_next = 1;
+
+Session* find(int64_t h) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_sessions.find(h);
+    return it == g_sessions.end() ? nullptr : it->second.get();
+}
+
+// Makes the session's device current for the scope of one call.
+struct DeviceGuard {
+    int prev = -1;
+    int rc = TVQ_OK;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        cudaError_t e = cudaSetDevice(dev);
+        if (e != cudaSuccess) rc = cuda_fail(e, "cudaSetDevice");
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+#define SESSION(h)                                                        \
+    Session* S = find(h);                                                 \
+    TVQ_CHECK(S, TVQ_ERR_HANDLE, "unknown or destroyed session handle");  \
+    DeviceGuard dg__(S->device);                                          \
+    if (dg__.rc) return dg__.rc;
+
+#define STEP(expr)              \
+    do {                        \
+        int r__ = (expr);       \
+        if (r__) return r__;    \
+    } while (0)
+
+void lin_shape(const Session& s, int which, int* n, int* k) {
+    switch (which) {
+        case 0: *n = 3 * s.d; *k = s.d; break;
+        case 1: *n = s.d; *k = s.d; break;
+        case 2: *n = s.ffn; *k = s.d; break;
+        default: *n = s.d; *k = s.ffn; break;
+    }
+}
+
+int gemm(Session& s, const int8_t* A, const Lin& l, const float* scale_a, float* Y, const float* residual,
+         int8_t* Yq, const float* scale_out, uint32_t* amax, int act) {
+    GemmArgs g;
+    g.kind = GEMM_I8;
+    g.A = A;
+    g.W = l.W;
+    g.bias = l.bias;
+    g.residual = residual;
+    g.Y = Y;
+    g.Yq = Yq;
+    g.m = s.T;
+    g.n = l.n;
+    g.k = l.k;
+    g.scale_a = scale_a;
+    g.scales_w = l.sw;
+    g.per_channel = 1;
+    g.act = act;
+    g.scale_out = scale_out;
+    g.amax = amax;
+    return launch_gemm(g, s.st);
+}
+
+// Stage ids reported by tvq_session_stage_times.
+enum Stage { ST_EMBED = 0, ST_LN = 1, ST_GEMM_QKV = 2, ST_ATTN = 3, ST_GEMM_PROJ = 4, ST_GEMM_FC = 5, ST_GEMM_MPROJ = 6,
+             ST_LM_HEAD = 7, ST_COUNT = 8 };
+
+// Marks the end of a stage inside the captured graph (profiling only).
+int mark(Session& s, int stage) {
+    if (!s.profile || !s.capturing) return TVQ_OK;
+    cudaEvent_t e = nullptr;
+    TVQ_CUDA(cudaEventCreate(&e));
+    s.ev.push_back(e);
+    s.ev_stage.push_back(stage);
+    TVQ_CUDA(cudaEventRecordWithFlags(e, s.st, cudaEventRecordExternal));
+    return TVQ_OK;
+}
+
+// The forward pass for the prepared layout, enqueued on s.st.
+int enqueue_forward(Session& s, bool calibrating) {
+    const int T = s.T, d = s.d;
+    STEP(mark(s, -1));
+    STEP(launch_embed(s.ids, s.tok_start, s.wte, s.wpe, s.x, T, d, s.vocab, s.max_pos, s.err, s.st));
+    STEP(mark(s, ST_EMBED));
+    for (int l = 0; l < s.layers; l++) {
+        LayerW& w = s.L[l];
+        float* sc = s.act_scale + 4 * l;
+        uint32_t* am = s.act_amax + 4 * l;
+        // ln_1 -> int8 (c_attn input)
+        if (calibrating) {
+            STEP(launch_layernorm(s.x, w.ln[0], w.ln[1], s.hf, nullptr, nullptr, am + 0, T, d, s.eps, s.st));
+            STEP(launch_scale_from_amax(am + 0, sc + 0, 1, s.st));
+            STEP(launch_quantize_i8(s.hf, s.aq, static_cast<int64_t>(T) * d, sc + 0, s.st));
+        } else {
+            STEP(launch_layernorm(s.x, w.ln[0], w.ln[1], nullptr, s.aq, sc + 0, nullptr, T, d, s.eps, s.st));
+        }
+        STEP(mark(s, ST_LN));
+        // c_attn: qkv = dequant(aq Wqkv) + b
+        STEP(gemm(s, s.aq, w.lin[0], sc + 0, s.qkv, nullptr, nullptr, nullptr, nullptr, TVQ_ACT_NONE));
+        STEP(mark(s, ST_GEMM_QKV));
+        // causal attention -> int8 context (attn c_proj input)
+        if (calibrating) {
+            STEP(launch_attention(s.qkv, s.tiles, s.ntiles, T, d, s.heads, s.hf, nullptr, nullptr, am + 1, s.st));
+            STEP(launch_scale_from_amax(am + 1, sc + 1, 1, s.st));
+            STEP(launch_quantize_i8(s.hf, s.aq, static_cast<int64_t>(T) * d, sc + 1, s.st));
+        } else {
+            STEP(launch_attention(s.qkv, s.tiles, s.ntiles, T, d, s.heads, nullptr, s.aq, sc + 1, nullptr, s.st));
+        }
+        STEP(mark(s, ST_ATTN));
+        // attn c_proj + residual, in place on x
+        STEP(gemm(s, s.aq, w.lin[1], sc + 1, s.x, s.x, nullptr, nullptr, nullptr, TVQ_ACT_NONE));
+        STEP(mark(s, ST_GEMM_PROJ));
+        // ln_2 -> int8 (c_fc input)
+        if (calibrating) {
+            STEP(launch_layernorm(s.x, w.ln[2], w.ln[3], s.hf, nullptr, nullptr, am + 2, T, d, s.eps, s.st));
+            STEP(launch_scale_from_amax(am + 2, sc + 2, 1, s.st));
+            STEP(launch_quantize_i8(s.hf, s.aq, static_cast<int64_t>(T) * d, sc + 2, s.st));
+        } else {
+            STEP(launch_layernorm(s.x, w.ln[2], w.ln[3], nullptr, s.aq, sc + 2, nullptr, T, d, s.eps, s.st));
+        }
+        STEP(mark(s, ST_LN));
+        // c_fc + erf GELU -> int8 (mlp c_proj input)
+        if (calibrating) {
+            STEP(gemm(s, s.aq, w.lin[2], sc + 2, s.hf, nullptr, nullptr, nullptr, am + 3, TVQ_ACT_GELU_ERF));
+            STEP(launch_scale_from_amax(am + 3, sc + 3, 1, s.st));
+            STEP(launch_quantize_i8(s.hf, s.hq, static_cast<int64_t>(T) * s.ffn, sc + 3, s.st));
+        } else {
+            STEP(gemm(s, s.aq, w.lin[2], sc + 2, nullptr, nullptr, s.hq, sc + 3, nullptr, TVQ_ACT_GELU_ERF));
+        }
+        STEP(mark(s, ST_GEMM_FC));
+        // mlp c_proj + residual, in place on x
+        STEP(gemm(s, s.hq, w.lin[3], sc + 3, s.x, s.x, nullptr, nullptr, nullptr, TVQ_ACT_NONE));
+        STEP(mark(s, ST_GEMM_MPROJ));
+    }
+    // ln_f and the tied LM head (gpt2_ref.tkv:589-610), fp32
+    STEP(launch_layernorm(s.x, s.lnf_g, s.lnf_b, s.xf, nullptr, nullptr, nullptr, T, d, s.eps, s.st));
+    STEP(mark(s, ST_LN));
+    const float* xin = s.xf;
+    int rows = T;
+    if (s.logits_mode == 1) {
+        STEP(launch_gather_last(s.xf, s.seg, s.nseg, d, s.xf_last, s.st));
+        xin = s.xf_last;
+        rows = s.nseg;
+    }
+    const float one = 1.0f, zero = 0.0f;
+    cublasStatus_t bs = cublasSgemm(s.blas, CUBLAS_OP_T, CUBLAS_OP_N, s.vocab, rows, d, &one, s.wte, d, xin, d, &zero,
+                                    s.logits, s.vocab);
+    if (bs != CUBLAS_STATUS_SUCCESS) {
+        set_error(TVQ_ERR_CUDA, "cublasSgemm failed (status " + std::to_string(static_cast<int>(bs)) + ")");
+        return TVQ_ERR_CUDA;
+    }
+    STEP(mark(s, ST_LM_HEAD));
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
+}
+
+int check_ready(Session& s) {
+    TVQ_CHECK(s.wte && s.wpe && s.lnf_g && s.lnf_b, TVQ_ERR_INVALID, "embeddings / final layernorm not set");
+    for (int l = 0; l < s.layers; l++) {
+        for (int i = 0; i < 4; i++) TVQ_CHECK(s.L[l].ln[i], TVQ_ERR_INVALID, "layernorm not set");
+        for (int i = 0; i < 4; i++) TVQ_CHECK(s.L[l].lin[i].set, TVQ_ERR_INVALID, "linear not set");
+    }
+    TVQ_CHECK(s.prepared, TVQ_ERR_INVALID, "tvq_session_prepare has not been called");
+    return TVQ_OK;
+}
+
+int check_err(Session& s, cudaStream_t st) {
+    TVQ_CUDA(cudaStreamSynchronize(st));
+    int h = 0;
+    TVQ_CUDA(cudaMemcpy(&h, s.err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (h) {
+        TVQ_CUDA(cudaMemset(s.err, 0, sizeof(int)));
+        set_error(TVQ_ERR_INVALID, "token id out of range or sequence longer than max_pos");
+        return TVQ_ERR_INVALID;
+    }
+    return check_device_error(st);
+}
+
+int capture(Session& s) {
+    if (s.gexec) {
+        cudaGraphExecDestroy(s.gexec);
+        s.gexec = nullptr;
+    }
+    for (cudaEvent_t e : s.ev) cudaEventDestroy(e);
+    s.ev.clear();
+    s.ev_stage.clear();
+    cudaGraph_t g = nullptr;
+    TVQ_CUDA(cudaStreamBeginCapture(s.st, cudaStreamCaptureModeRelaxed));
+    s.capturing = true;
+    int rc = enqueue_forward(s, false);
+    s.capturing = false;
+    cudaError_t e = cudaStreamEndCapture(s.st, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+    e = cudaGraphInstantiate(&s.gexec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+    return TVQ_OK;
+}
+
+}  // namespace
+}  // namespace tvq
+
+using namespace tvq;
+
+extern "C" {
+
+int tvq_session_create(int device, int64_t vocab, int64_t d_model, int64_t n_heads, int64_t n_layers, int64_t d_ffn,
+                       int64_t max_pos, double ln_eps, int64_t max_tokens, int64_t* handle) {
+    TVQ_CHECK(handle, TVQ_ERR_INVALID, "null handle pointer");
+    TVQ_CHECK(vocab > 0 && d_model > 0 && n_heads > 0 && n_layers >= 0 && d_ffn > 0 && max_pos > 0 && max_tokens > 0,
+              TVQ_ERR_INVALID, "model sizes must be positive");
+    TVQ_CHECK(d_model % n_heads == 0, TVQ_ERR_INVALID, "d_model must be a multiple of n_heads");
+    TVQ_CHECK(d_model % 16 == 0 && d_ffn % 16 == 0, TVQ_ERR_UNSUPPORTED, "d_model and d_ffn must be multiples of 16");
+    TVQ_CHECK(max_tokens < (1 << 30) && vocab < (1 << 30), TVQ_ERR_UNSUPPORTED, "size too large");
+    int ndev = 0;
+    cudaError_t e = cudaGetDeviceCount(&ndev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    TVQ_CHECK(device >= 0 && device < ndev, TVQ_ERR_INVALID, "bad device ordinal");
+    try {
+        auto s = std::make_unique<Session>();
+        s->device = device;
+        DeviceGuard dg(device);
+        if (dg.rc) return dg.rc;
+        int rc = 0;
+        DeviceState* ds = device_state(&rc);
+        if (!ds) return rc;
+        TVQ_CHECK(ds->cc_major == 10, TVQ_ERR_UNSUPPORTED, "sessions need an sm_100 device");
+        s->vocab = static_cast<int>(vocab);
+        s->d = static_cast<int>(d_model);
+        s->heads = static_cast<int>(n_heads);
+        s->layers = static_cast<int>(n_layers);
+        s->ffn = static_cast<int>(d_ffn);
+        s->max_pos = static_cast<int>(max_pos);
+        s->max_tokens = static_cast<int>(max_tokens);
+        s->eps = ln_eps;
+        s->L.resize(static_cast<size_t>(n_layers));
+        TVQ_CUDA(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+        if (cublasCreate(&s->blas) != CUBLAS_STATUS_SUCCESS) {
+            set_error(TVQ_ERR_CUDA, "cublasCreate failed");
+            return TVQ_ERR_CUDA;
+        }
+        cublasSetStream(s->blas, s->st);
+        cublasSetMathMode(s->blas, CUBLAS_PEDANTIC_MATH);  // true fp32: no TF32 anywhere
+        const size_t MT = static_cast<size_t>(max_tokens), D = static_cast<size_t>(d_model);
+        const size_t F = static_cast<size_t>(d_ffn);
+        STEP(s->alloc(&s->blas_ws, 32u << 20));
+        cublasSetWorkspace(s->blas, s->blas_ws, 32u << 20);
+        STEP(s->alloc(&s->act_scale, static_cast<size_t>(4 * std::max<int64_t>(n_layers, 1))));
+        STEP(s->alloc(&s->act_amax, static_cast<size_t>(4 * std::max<int64_t>(n_layers, 1))));
+        TVQ_CUDA(cudaMemset(s->act_amax, 0, sizeof(uint32_t) * 4 * std::max<int64_t>(n_layers, 1)));
+        TVQ_CUDA(cudaMemset(s->act_scale, 0, sizeof(float) * 4 * std::max<int64_t>(n_layers, 1)));
+        STEP(s->alloc(&s->ids, MT));
+        STEP(s->alloc(&s->seg, MT + 1));
+        STEP(s->alloc(&s->tok_start, MT));
+        STEP(s->alloc(&s->tiles, MT));
+        STEP(s->alloc(&s->x, MT * D));
+        STEP(s->alloc(&s->qkv, MT * 3 * D));
+        STEP(s->alloc(&s->hf, MT * std::max(D, F)));
+        STEP(s->alloc(&s->xf, MT * D));
+        STEP(s->alloc(&s->xf_last, MT * D));
+        STEP(s->alloc(&s->aq, MT * D));
+        STEP(s->alloc(&s->hq, MT * F));
+        STEP(s->alloc(&s->err, 1));
+        TVQ_CUDA(cudaMemset(s->err, 0, sizeof(int)));
+        std::lock_guard<std::mutex> lk(g_mu);
+        *handle = g_next++;
+        g_sessions[*handle] = std::move(s);
+        return TVQ_OK;
+    } catch (const std::bad_alloc&) {
+        set_error(TVQ_ERR_CUDA, "host allocation failed");
+        return TVQ_ERR_CUDA;
+    }
+}
+
+int tvq_session_destroy(int64_t handle) {
+    std::unique_ptr<Session> s;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_sessions.find(handle);
+        TVQ_CHECK(it != g_sessions.end(), TVQ_ERR_HANDLE, "unknown or destroyed session handle");
+        s = std::move(it->second);
+        g_sessions.erase(it);
+    }
+    DeviceGuard dg(s->device);
+    cudaStreamSynchronize(s->st);
+    s.reset();
+    return TVQ_OK;
+}
+
+int tvq_session_set_embeddings(int64_t handle, const float* wte, const float* wpe) {
+    SESSION(handle)
+    TVQ_CHECK(wte && wpe, TVQ_ERR_INVALID, "null buffer");
+    if (!S->wte) STEP(S->alloc(&S->wte, static_cast<size_t>(S->vocab) * S->d));
+    if (!S->wpe) STEP(S->alloc(&S->wpe, static_cast<size_t>(S->max_pos) * S->d));
+    TVQ_CUDA(cudaMemcpy(S->wte, wte, sizeof(float) * S->vocab * S->d, cudaMemcpyHostToDevice));
+    TVQ_CUDA(cudaMemcpy(S->wpe, wpe, sizeof(float) * S->max_pos * S->d, cudaMemcpyHostToDevice));
+    return TVQ_OK;
+}
+
+int tvq_session_set_layernorm(int64_t handle, int64_t layer, int64_t which, const float* gamma, const float* beta) {
+    SESSION(handle)
+    TVQ_CHECK(gamma && beta, TVQ_ERR_INVALID, "null buffer");
+    TVQ_CHECK(layer >= -1 && layer < S->layers, TVQ_ERR_INVALID, "bad layer");
+    float **g, **b;
+    if (layer < 0) {
+        g = &S->lnf_g;
+        b = &S->lnf_b;
+    } else {
+        TVQ_CHECK(which == 0 || which == 1, TVQ_ERR_INVALID, "which must be 0 (ln_1) or 1 (ln_2)");
+        g = &S->L[layer].ln[2 * which];
+        b = &S->L[layer].ln[2 * which + 1];
+    }
+    if (!*g) STEP(S->alloc(g, S->d));
+    if (!*b) STEP(S->alloc(b, S->d));
+    TVQ_CUDA(cudaMemcpy(*g, gamma, sizeof(float) * S->d, cudaMemcpyHostToDevice));
+    TVQ_CUDA(cudaMemcpy(*b, beta, sizeof(float) * S->d, cudaMemcpyHostToDevice));
+    return TVQ_OK;
+}
+
+static int lin_alloc(Session* S, Lin& l, int n, int k) {
+    if (!l.W) {
+        STEP(S->alloc(&l.W, static_cast<size_t>(n) * k));
+        STEP(S->alloc(&l.sw, static_cast<size_t>(n)));
+        STEP(S->alloc(&l.bias, static_cast<size_t>(n)));
+    }
+    l.n = n;
+    l.k = k;
+    return TVQ_OK;
+}
+
+int tvq_session_set_linear_f32(int64_t handle, int64_t layer, int64_t which, const float* w, const float* bias,
+                               int layout) {
+    SESSION(handle)
+    TVQ_CHECK(layer >= 0 && layer < S->layers && which >= 0 && which < 4, TVQ_ERR_INVALID, "bad layer/which");
+    TVQ_CHECK(w && bias && (layout == 0 || layout == 1), TVQ_ERR_INVALID, "bad arguments");
+    int n, k;
+    lin_shape(*S, static_cast<int>(which), &n, &k);
+    Lin& l = S->L[layer].lin[which];
+    STEP(lin_alloc(S, l, n, k));
+    float *tmp = nullptr, *tmp2 = nullptr;
+    const size_t nk = static_cast<size_t>(n) * k;
+    TVQ_CUDA(cudaMalloc(&tmp, nk * sizeof(float) * 2));
+    tmp2 = tmp + nk;
+    int rc = TVQ_OK;
+    cudaError_t e = cudaMemcpyAsync(tmp, w, nk * sizeof(float), cudaMemcpyHostToDevice, S->st);
+    if (e != cudaSuccess) rc = cuda_fail(e, "cudaMemcpy weights");
+    const float* src = tmp;
+    if (!rc && layout == 0) {  // HF Conv1D / gpt2_ref layout w[k * n + o]
+        rc = launch_transpose(tmp, tmp2, k, n, S->st);
+        src = tmp2;
+    }
+    // per-output-channel calibrate + quantize (engine.tkv:202-213, 237-250)
+    if (!rc) rc = launch_rowwise(0, src, l.W, l.sw, n, k, S->st);
+    if (!rc) {
+        e = cudaMemcpyAsync(l.bias, bias, n * sizeof(float), cudaMemcpyHostToDevice, S->st);
+        if (e != cudaSuccess) rc = cuda_fail(e, "cudaMemcpy bias");
+    }
+    cudaStreamSynchronize(S->st);
+    cudaFree(tmp);
+    if (rc) return rc;
+    l.set = true;
+    return check_device_error(S->st);
+}
+
+int tvq_session_set_linear_i8(int64_t handle, int64_t layer, int64_t which, const int8_t* w_nk, const float* scales_w,
+                              const float* bias) {
+    SESSION(handle)
+    TVQ_CHECK(layer >= 0 && layer < S->layers && which >= 0 && which < 4, TVQ_ERR_INVALID, "bad layer/which");
+    TVQ_CHECK(w_nk && scales_w && bias, TVQ_ERR_INVALID, "null buffer");
+    int n, k;
+    lin_shape(*S, static_cast<int>(which), &n, &k);
+    Lin& l = S->L[layer].lin[which];
+    STEP(lin_alloc(S, l, n, k));
+    TVQ_CUDA(cudaMemcpy(l.W, w_nk, static_cast<size_t>(n) * k, cudaMemcpyHostToDevice));
+    TVQ_CUDA(cudaMemcpy(l.sw, scales_w, sizeof(float) * n, cudaMemcpyHostToDevice));
+    TVQ_CUDA(cudaMemcpy(l.bias, bias, sizeof(float) * n, cudaMemcpyHostToDevice));
+    l.set = true;
+    return TVQ_OK;
+}
+
+int tvq_session_get_linear_i8(int64_t handle, int64_t layer, int64_t which, int8_t* w_nk, float* scales_w) {
+    SESSION(handle)
+    TVQ_CHECK(layer >= 0 && layer < S->layers && which >= 0 && which < 4, TVQ_ERR_INVALID, "bad layer/which");
+    Lin& l = S->L[layer].lin[which];
+    TVQ_CHECK(l.set, TVQ_ERR_INVALID, "linear not set");
+    if (w_nk) TVQ_CUDA(cudaMemcpy(w_nk, l.W, static_cast<size_t>(l.n) * l.k, cudaMemcpyDeviceToHost));
+    if (scales_w) TVQ_CUDA(cudaMemcpy(scales_w, l.sw, sizeof(float) * l.n, cudaMemcpyDeviceToHost));
+    return TVQ_OK;
+}
+
+int tvq_session_set_act_scales(int64_t handle, const float* scales, int64_t n) {
+    SESSION(handle)
+    TVQ_CHECK(scales && n == 4LL * S->layers, TVQ_ERR_SIZE, "need 4 scales per layer");
+    if (n) TVQ_CUDA(cudaMemcpy(S->act_scale, scales, sizeof(float) * n, cudaMemcpyHostToDevice));
+    return TVQ_OK;
+}
+
+int tvq_session_get_act_scales(int64_t handle, float* scales, int64_t n) {
+    SESSION(handle)
+    TVQ_CHECK(scales && n >= 4LL * S->layers, TVQ_ERR_SIZE, "need room for 4 scales per layer");
+    TVQ_CUDA(cudaStreamSynchronize(S->st));
+    if (S->layers) TVQ_CUDA(cudaMemcpy(scales, S->act_scale, sizeof(float) * 4 * S->layers, cudaMemcpyDeviceToHost));
+    return TVQ_OK;
+}
+
+int tvq_session_prepare(int64_t handle, const int64_t* seg, int64_t n_seg, int logits_mode) {
+    SESSION(handle)
+    TVQ_CHECK(seg && n_seg >= 1, TVQ_ERR_INVALID, "need at least one sequence");
+    TVQ_CHECK(logits_mode == 0 || logits_mode == 1, TVQ_ERR_INVALID, "logits_mode must be 0 (all) or 1 (last)");
+    TVQ_CHECK(seg[0] == 0, TVQ_ERR_INVALID, "seg[0] must be 0");
+    const int64_t T = seg[n_seg];
+    TVQ_CHECK(T >= 1 && T <= S->max_tokens, TVQ_ERR_SIZE, "token count exceeds the session's max_tokens");
+    std::vector<int> sh(static_cast<size_t>(n_seg) + 1);
+    std::vector<int> tok(static_cast<size_t>(T));
+    std::vector<int4> tiles;
+    for (int64_t s = 0; s < n_seg; s++) {
+        const int64_t a = seg[s], b = seg[s + 1];
+        TVQ_CHECK(b > a, TVQ_ERR_INVALID, "every sequence needs at least one token");
+        TVQ_CHECK(b - a <= S->max_pos, TVQ_ERR_SIZE, "sequence longer than max_pos");
+        for (int64_t t = a; t < b; t++) tok[t] = static_cast<int>(a);
+        for (int64_t q0 = a; q0 < b; q0 += 64)
+            tiles.push_back(make_int4(static_cast<int>(q0), static_cast<int>(a), static_cast<int>(b), 0));
+        sh[s] = static_cast<int>(a);
+    }
+    sh[n_seg] = static_cast<int>(T);
+    // longest causal work first
+    std::stable_sort(tiles.begin(), tiles.end(), [](const int4& u, const int4& v) { return (u.x - u.y) > (v.x - v.y); });
+    TVQ_CHECK(tiles.size() <= static_cast<size_t>(S->max_tokens), TVQ_ERR_SIZE, "too many attention tiles");
+    TVQ_CUDA(cudaStreamSynchronize(S->st));
+    TVQ_CUDA(cudaMemcpy(S->seg, sh.data(), sizeof(int) * sh.size(), cudaMemcpyHostToDevice));
+    TVQ_CUDA(cudaMemcpy(S->tok_start, tok.data(), sizeof(int) * tok.size(), cudaMemcpyHostToDevice));
+    TVQ_CUDA(cudaMemcpy(S->tiles, tiles.data(), sizeof(int4) * tiles.size(), cudaMemcpyHostToDevice));
+    S->T = static_cast<int>(T);
+    S->nseg = static_cast<int>(n_seg);
+    S->ntiles = static_cast<int>(tiles.size());
+    S->logits_mode = logits_mode;
+    S->seg_host = sh;
+    const size_t need = static_cast<size_t>(S->logits_rows()) * S->vocab;
+    if (need > S->logits_cap) {
+        if (S->logits) {
+            cudaFree(S->logits);
+            S->allocs.erase(std::remove(S->allocs.begin(), S->allocs.end(), static_cast<void*>(S->logits)),
+                            S->allocs.end());
+            S->logits = nullptr;
+        }
+        STEP(S->alloc(&S->logits, need));
+        S->logits_cap = need;
+    }
+    S->prepared = true;
+    if (S->gexec) {
+        cudaGraphExecDestroy(S->gexec);
+        S->gexec = nullptr;
+    }
+    return TVQ_OK;
+}
+
+int tvq_session_calibrate(int64_t handle, const int64_t* ids, int ids_on_device, int reset) {
+    SESSION(handle)
+    STEP(check_ready(*S));
+    TVQ_CHECK(ids, TVQ_ERR_INVALID, "null ids");
+    if (reset && S->layers)
+        TVQ_CUDA(cudaMemsetAsync(S->act_amax, 0, sizeof(uint32_t) * 4 * S->layers, S->st));
+    TVQ_CUDA(cudaMemcpyAsync(S->ids, ids, sizeof(int64_t) * S->T,
+                             ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, S->st));
+    STEP(enqueue_forward(*S, true));
+    return check_err(*S, S->st);
+}
+
+int tvq_session_forward(int64_t handle, const int64_t* ids, int ids_on_device, float* logits, int64_t logits_len,
+                        int logits_on_device, void* stream) {
+    SESSION(handle)
+    STEP(check_ready(*S));
+    const size_t out_elems = static_cast<size_t>(S->logits_rows()) * S->vocab;
+    TVQ_CHECK(!logits || logits_len >= static_cast<int64_t>(out_elems), TVQ_ERR_SIZE, "logits buffer too small");
+    if (!S->gexec) STEP(capture(*S));
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : S->st;
+    if (ids)
+        TVQ_CUDA(cudaMemcpyAsync(S->ids, ids, sizeof(int64_t) * S->T,
+                                 ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+    TVQ_CUDA(cudaGraphLaunch(S->gexec, st));
+    if (logits)
+        TVQ_CUDA(cudaMemcpyAsync(logits, S->logits, out_elems * sizeof(float),
+                                 logits_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
+    if ((ids && !ids_on_device) || (logits && !logits_on_device)) return check_err(*S, st);
+    return TVQ_OK;
+}
+
+int tvq_session_logits(int64_t handle, float** logits_dev, int64_t* rows, int64_t* cols) {
+    SESSION(handle)
+    TVQ_CHECK(logits_dev, TVQ_ERR_INVALID, "null out pointer");
+    *logits_dev = S->logits;
+    if (rows) *rows = S->prepared ? S->logits_rows() : 0;
+    if (cols) *cols = S->vocab;
+    return TVQ_OK;
+}
+
+int tvq_session_set_profiling(int64_t handle, int enable) {
+    SESSION(handle)
+    S->profile = enable != 0;
+    if (S->gexec) {  // recapture with or without the stage events
+        cudaGraphExecDestroy(S->gexec);
+        S->gexec = nullptr;
+    }
+    return TVQ_OK;
+}
+
+int tvq_session_stage_times(int64_t handle, float* ms, int64_t n) {
+    SESSION(handle)
+    TVQ_CHECK(ms && n >= ST_COUNT, TVQ_ERR_SIZE, "need room for every stage");
+    TVQ_CHECK(S->profile && S->ev.size() >= 2, TVQ_ERR_INVALID, "profiling is off or no forward has run");
+    for (int i = 0; i < ST_COUNT; i++) ms[i] = 0.0f;
+    TVQ_CUDA(cudaEventSynchronize(S->ev.back()));
+    for (size_t i = 1; i < S->ev.size(); i++) {
+        float t = 0.0f;
+        TVQ_CUDA(cudaEventElapsedTime(&t, S->ev[i - 1], S->ev[i]));
+        if (S->ev_stage[i] >= 0) ms[S->ev_stage[i]] += t;
+    }
+    return TVQ_OK;
+}
+
+int tvq_session_sync(int64_t handle) {
+    SESSION(handle)
+    return check_err(*S, S->st);
+}
+
+// ---------------------------------------------------------------- glue kernels, device buffers
+
+int tvq_dev_layernorm(const float* x, const float* gamma, const float* beta, float* y, int8_t* q,
+                      const float* qscale_dev, uint32_t* amax_dev, int64_t rows, int64_t d, double eps,
+                      void* stream) {
+    TVQ_CHECK(rows >= 0 && d > 0 && x && gamma && beta && (y || q || amax_dev), TVQ_ERR_INVALID, "bad arguments");
+    TVQ_CHECK(!q || qscale_dev, TVQ_ERR_INVALID, "int8 output needs a scale");
+    return launch_layernorm(x, gamma, beta, y, q, qscale_dev, amax_dev, static_cast<int>(rows), static_cast<int>(d),
+                            eps, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_attention(const float* qkv, const int64_t* seg, int64_t n_seg, int64_t d, int64_t n_heads,
+                      int32_t* tiles_dev32, int64_t tiles_cap, float* out, int8_t* outq, const float* qscale_dev,
+                      uint32_t* amax_dev, void* stream) {
+    int4* tiles_dev = reinterpret_cast<int4*>(tiles_dev32);
+    TVQ_CHECK((reinterpret_cast<uintptr_t>(tiles_dev32) & 15) == 0, TVQ_ERR_UNSUPPORTED, "tile buffer must be 16-byte aligned");
+    TVQ_CHECK(qkv && seg && n_seg >= 1 && tiles_dev && (out || outq || amax_dev), TVQ_ERR_INVALID, "bad arguments");
+    TVQ_CHECK(!outq || qscale_dev, TVQ_ERR_INVALID, "int8 output needs a scale");
+    std::vector<int4> tiles;
+    for (int64_t s = 0; s < n_seg; s++) {
+        TVQ_CHECK(seg[s + 1] >= seg[s], TVQ_ERR_INVALID, "segments must be non-decreasing");
+        for (int64_t q0 = seg[s]; q0 < seg[s + 1]; q0 += 64)
+            tiles.push_back(make_int4(static_cast<int>(q0), static_cast<int>(seg[s]), static_cast<int>(seg[s + 1]), 0));
+    }
+    TVQ_CHECK(static_cast<int64_t>(tiles.size()) <= tiles_cap, TVQ_ERR_SIZE, "tile buffer too small");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (!tiles.empty())
+        TVQ_CUDA(cudaMemcpyAsync(tiles_dev, tiles.data(), sizeof(int4) * tiles.size(), cudaMemcpyHostToDevice, st));
+    TVQ_CUDA(cudaStreamSynchronize(st));  // the host vector dies at return
+    return launch_attention(qkv, tiles_dev, static_cast<int>(tiles.size()), static_cast<int>(seg[n_seg]),
+                            static_cast<int>(d), static_cast<int>(n_heads), out, outq, qscale_dev, amax_dev, st);
+}
+
+}  // extern "C"
