@@ -201,11 +201,14 @@ def run_ours(args, rank, world, local):
     ids = np.random.default_rng(2 + rank).integers(0, cfg.vocab, SEQ).astype(np.int64)
     sess.calibrate(calib_ids)
 
-    stream = torch.cuda.current_stream(dev)
+    # a real stream: handle 0 (the legacy stream) would mean "the session's
+    # own stream" at the C ABI, which these events would not order against
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
     sptr = stream.cuda_stream
     ids_dev = torch.from_numpy(ids).to(dev)
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
-    sess.set_profiling(True)
+    sess.set_profiling(False)
 
     def step_device():
         sess.forward_device(ids_dev.data_ptr(), None, sptr)
@@ -220,8 +223,6 @@ def run_ours(args, rank, world, local):
     clocks = ClockSampler(gpu_id)
     clocks.start()
     time.sleep(0.3)
-    stage_names = GPT2Session.STAGES
-    stage_ms = {k: 0.0 for k in stage_names}
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     if world > 1:
@@ -235,12 +236,30 @@ def run_ours(args, rank, world, local):
         ev1.record(stream)
         ev1.synchronize()
         total_ms += ev0.elapsed_time(ev1)
-        for k, v in sess.stage_times().items():
-            stage_ms[k] += v
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
+
+    # ---- per-stage breakdown: the same graph recaptured with a CUDA event
+    # after every stage (event record nodes), run for a few more steps
+    sess.set_profiling(True)
+    stage_names = GPT2Session.STAGES
+    stage_ms = {k: 0.0 for k in stage_names}
+    prof_steps = max(3, args.steps // 2)
+    prof_total = 0.0
+    for i in range(prof_steps + 1):
+        flush.zero_()
+        ev0.record(stream)
+        step_device()
+        ev1.record(stream)
+        ev1.synchronize()
+        if i == 0:
+            continue  # first replay after the recapture
+        prof_total += ev0.elapsed_time(ev1)
+        for k, v in sess.stage_times().items():
+            stage_ms[k] += v
+    sess.set_profiling(False)
 
     # ---- end to end through the host-buffer API
     ids_pin = torch.from_numpy(ids).pin_memory()
@@ -288,7 +307,7 @@ def run_ours(args, rank, world, local):
         hbm, bf16, src = peaks()
         int8_peak = 2.0 * bf16  # dense INT8 = 2x dense BF16 on B200; no measured INT8 figure exists
         work = gemm_work()
-        per_launch_ms = {k: stage_ms[k] / (args.steps * cfg.n_layers) for k in work}
+        per_launch_ms = {k: stage_ms[k] / (prof_steps * cfg.n_layers) for k in work}
         dom = max(work, key=lambda k: per_launch_ms[k])
         ops, byts = work[dom]
         t = per_launch_ms[dom] / 1000.0
@@ -305,7 +324,7 @@ def run_ours(args, rank, world, local):
                                % (src, src, bf16))
         kernels = {}
         for k in stage_names:
-            kernels[k] = {"ms_per_step": stage_ms[k] / args.steps,
+            kernels[k] = {"ms_per_step": stage_ms[k] / prof_steps,
                           "share": stage_ms[k] / max(sum(stage_ms.values()), 1e-9)}
         for k, (o, b) in work.items():
             tt = per_launch_ms[k] / 1000.0
@@ -336,6 +355,7 @@ def run_ours(args, rank, world, local):
             "library_launches": {"cublasSgemm (fp32 LM head)": args.steps},
             "clocks": clk,
             "kernels": kernels,
+            "profiled_ms_per_step": prof_total / prof_steps,
         }
         print(json.dumps(out), flush=True)
     sess.close()

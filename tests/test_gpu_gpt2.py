@@ -122,7 +122,8 @@ def test_session_matches_oracle_composition(lengths):
     # last-token logits are the same rows
     s.prepare(seg, logits_mode=1)
     last = s.forward(ids)
-    assert np.array_equal(last, got[seg[1:] - 1])
+    # same rows; cuBLAS may pick another SGEMM kernel for 3 rows than for T
+    assert np.allclose(last, got[seg[1:] - 1], rtol=1e-5, atol=1e-6)
     s.close()
 
 
