@@ -194,6 +194,19 @@ TVQ_API int tvq_dev_layernorm(const float* x, const float* gamma, const float* b
 TVQ_API int tvq_dev_attention(const float* qkv, const int64_t* seg, int64_t n_seg, int64_t d, int64_t n_heads,
                               int32_t* tiles_dev, int64_t tiles_cap, float* out, int8_t* outq,
                               const float* qscale_dev, uint32_t* amax_dev, void* stream);
+/* tvq_dev_attention for callers that cannot allocate device memory when they
+ * call (a host runtime whose device memory all belongs to its own pool, a
+ * serving loop that must not allocate): no counterpart in the reference.  The
+ * query-tile scratch is a fixed 512 KiB device array inside the library
+ * (every GPU that loads it holds it until exit), so at most 32768 tiles of
+ * 64 tokens per sequence fit in one call; larger calls fail with
+ * TVQ_ERR_SIZE.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress), so make it before any stream capture.  All
+ * calls share the array: calls that overlap on the GPU race on it.  No
+ * cudaMalloc or cudaFree is called. */
+TVQ_API int tvq_dev_attention_noalloc(const float* qkv, const int64_t* seg, int64_t n_seg, int64_t d,
+                                      int64_t n_heads, float* out, int8_t* outq, const float* qscale_dev,
+                                      uint32_t* amax_dev, void* stream);
 
 /* ================================================================ sessions
  * Device-resident GPT-2-shaped INT8 PTQ stack: embeddings, n_layers blocks of

@@ -66,6 +66,7 @@ SIGNATURES = {
     "tvq_dev_gemm": (i32, [i32, P, P, P, P, P, P, i64, i64, i64, P, P, i32, i32, P, P, P]),
     "tvq_dev_layernorm": (i32, [P, P, P, P, P, P, P, i64, i64, C.c_double, P]),
     "tvq_dev_attention": (i32, [P, P, i64, i64, i64, P, i64, P, P, P, P, P]),
+    "tvq_dev_attention_noalloc": (i32, [P, P, i64, i64, i64, P, P, P, P, P]),
     "tvq_session_create": (i32, [i32, i64, i64, i64, i64, i64, i64, C.c_double, i64, P]),
     "tvq_session_destroy": (i32, [i64]),
     "tvq_session_set_embeddings": (i32, [i64, P, P]),
