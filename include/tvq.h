@@ -179,6 +179,18 @@ TVQ_API int tvq_dev_gemm(int kind, const void* A, const void* W, const float* bi
                  const float* scales_w_dev, int per_channel, int act, const float* scale_out_dev,
                  uint32_t* amax_dev, void* stream);
 
+/* fp32 GEMM Y[m,n] = A[m,k] W[n,k]^T on the tcgen05 tensor cores with split
+ * precision: each operand is given as high + low parts (tvq_dev_split_tf32),
+ * and Y accumulates xh*wh + xh*wl + xl*wh in f32 (relative error about 2^-21
+ * per product, the size of an fp32 GEMM's own accumulation error).  Used for
+ * the tied LM head (gpt2_ref.tkv:603-610).  k*4 must be a multiple of 16 and
+ * all pointers 16-byte aligned. */
+TVQ_API int tvq_dev_gemm_f32x3(const float* A_hi, const float* A_lo, const float* W_hi, const float* W_lo, float* Y,
+                               int64_t m, int64_t n, int64_t k, void* stream);
+/* x ~ hi + lo with both parts on the TF32 grid: hi = tf32(x), lo =
+ * tf32(x - hi), |x - hi - lo| <= 2^-22 |x|. */
+TVQ_API int tvq_dev_split_tf32(const float* x, float* hi, float* lo, int64_t n, void* stream);
+
 /* ================================================================ fp32 glue, device buffers
  * gpt2_layernorm, tv/training/gpt2_ref.tkv:50-78 (f64 statistics): y (f32)
  * and/or q = int8 with the static scale qscale_dev[0]; amax_dev records

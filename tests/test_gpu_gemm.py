@@ -215,3 +215,35 @@ def test_device_gemm_fused_epilogue():
     assert np.array_equal(Yq.cpu().numpy(), q_ref)
     am = amax.cpu().numpy().view(np.float32)[0]
     assert am == np.abs(got).max()
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 50257, 768), (37, 1000, 64), (1024, 4096, 768), (130, 300, 1600)])
+def test_split_tf32_gemm_is_fp32_accurate(m, n, k):
+    """The LM head's fp32 GEMM on tensor cores (hi/lo split on the TF32 grid:
+    22-bit operands, 3 products): |error| <= 2^-18 * sum_k |a_k w_k| per
+    output against a float64 reference, and within 4x the max error of
+    torch's true-fp32 (non-TF32) matmul on the same data."""
+    import torch
+    torch.backends.cuda.matmul.allow_tf32 = False
+    rng = np.random.default_rng(m + n)
+    A = rng.standard_normal((m, k)).astype(np.float32)
+    W = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    dev = torch.device("cuda:0")
+    tA, tW = torch.from_numpy(A).to(dev), torch.from_numpy(W).to(dev)
+    parts = [torch.empty_like(t) for t in (tA, tA, tW, tW)]
+    from tokenvector.inference_b200.quantization import _buf as B
+    N.call("tvq_dev_split_tf32", B.ptr(tA), B.ptr(parts[0]), B.ptr(parts[1]), tA.numel(), None)
+    N.call("tvq_dev_split_tf32", B.ptr(tW), B.ptr(parts[2]), B.ptr(parts[3]), tW.numel(), None)
+    Y = torch.empty((m, n), dtype=torch.float32, device=dev)
+    N.call("tvq_dev_gemm_f32x3", *(B.ptr(p) for p in parts), B.ptr(Y), m, n, k, None)
+    torch.cuda.synchronize()
+    # the split represents x to 2^-22 relative
+    d = (parts[0].double() + parts[1].double() - tA.double()).abs()
+    assert bool((d <= tA.double().abs() * 2.0 ** -22).all())
+    ref = A.astype(np.float64) @ W.astype(np.float64).T
+    mag = np.abs(A).astype(np.float64) @ np.abs(W).astype(np.float64).T
+    err = np.abs(Y.cpu().numpy().astype(np.float64) - ref)
+    t32 = (tA @ tW.T).cpu().numpy().astype(np.float64)
+    e32 = np.abs(t32 - ref)
+    assert np.all(err <= mag * 2.0 ** -18 + 1e-30), float((err / (mag + 1e-30)).max())
+    assert err.max() <= 4.0 * e32.max() + 1e-12, (err.max(), e32.max())

@@ -64,6 +64,8 @@ SIGNATURES = {
     "tvq_dev_quantize_fp8": (i32, [P, P, i64, i64, P, i32, i32, P]),
     "tvq_dev_dequantize_fp8": (i32, [P, P, i64, P]),
     "tvq_dev_gemm": (i32, [i32, P, P, P, P, P, P, i64, i64, i64, P, P, i32, i32, P, P, P]),
+    "tvq_dev_gemm_f32x3": (i32, [P, P, P, P, P, i64, i64, i64, P]),
+    "tvq_dev_split_tf32": (i32, [P, P, P, i64, P]),
     "tvq_dev_layernorm": (i32, [P, P, P, P, P, P, P, i64, i64, C.c_double, P]),
     "tvq_dev_attention": (i32, [P, P, i64, i64, i64, P, i64, P, P, P, P, P]),
     "tvq_dev_attention_noalloc": (i32, [P, P, i64, i64, i64, P, P, P, P, P]),
@@ -95,17 +97,6 @@ class TvqError(RuntimeError):
         self.code = code
 
 
-def _preload_deps():
-    # libtvq links cudart statically; libcublas (if a build links it) comes
-    # from the CUDA toolkit or the torch wheel, whichever the loader finds.
-    for cand in ("/usr/local/cuda/lib64/libcublas.so.12",):
-        if os.path.exists(cand):
-            try:
-                C.CDLL(cand, mode=C.RTLD_GLOBAL)
-            except OSError:
-                pass
-
-
 def lib():
     global _lib
     if _lib is not None:
@@ -116,7 +107,6 @@ def lib():
                 raise RuntimeError(
                     "libtvq.so is not built (%s); run tokenvector/inference_b200/build.py -- "
                     "there is no CPU fallback" % LIB_PATH)
-            _preload_deps()
             L = C.CDLL(LIB_PATH)
             for name, (res, args) in SIGNATURES.items():
                 fn = getattr(L, name)

@@ -72,7 +72,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
                     sys.stderr.write("== %s\n%s" % (os.path.basename(futs[f]), log))
     if jobs or force or not os.path.exists(LIB):
         tmp = LIB + ".tmp"
-        cmd = [nvcc] + ARCH + ["-shared", "-o", tmp] + objs + ["-cudart", "static", "-lcublas", "-Xlinker", "-rpath=/usr/local/cuda/lib64"]
+        cmd = [nvcc] + ARCH + ["-shared", "-o", tmp] + objs + ["-cudart", "static"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n%s%s" % (r.stdout, r.stderr))

@@ -713,4 +713,28 @@ int tvq_dev_gemm(int kind, const void* A, const void* W, const float* bias, cons
     TVQ_CATCH
 }
 
+int tvq_dev_split_tf32(const float* x, float* hi, float* lo, int64_t n, void* stream) {
+    TVQ_CHECK(n >= 0 && (n == 0 || (x && hi && lo)), TVQ_ERR_INVALID, "null buffer");
+    return launch_split_tf32(x, hi, lo, n, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_gemm_f32x3(const float* A_hi, const float* A_lo, const float* W_hi, const float* W_lo, float* Y, int64_t m,
+                       int64_t n, int64_t k, void* stream) {
+    TVQ_CHECK(Y && A_hi && A_lo && W_hi && W_lo, TVQ_ERR_INVALID, "null buffer");
+    GemmArgs g;
+    g.kind = GEMM_TF32X3;
+    g.A = A_hi;
+    g.A2 = A_lo;
+    g.W = W_hi;
+    g.W2 = W_lo;
+    g.Y = Y;
+    g.m = m;
+    g.n = n;
+    g.k = k;
+    g.per_channel = 0;  // this kind reads no scales: Y is the accumulator
+    TVQ_TRY
+    return launch_gemm(g, static_cast<cudaStream_t>(stream));
+    TVQ_CATCH
+}
+
 }  // extern "C"

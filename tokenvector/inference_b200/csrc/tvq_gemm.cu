@@ -20,11 +20,13 @@
 //               memory transpose, then residual add and coalesced f32 / int8
 //               stores
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the
-// epilogue of tile i overlaps the MMAs of tile i+1.  Every mbarrier wait is
+// epilogue of tile i overlaps the MMAs of tile i+1 (GEMM_TF32X3: four
+// buffers of short K runs, summed in the epilogue's registers).  Every mbarrier wait is
 // bounded (tvq_common.cuh); on a timeout the kernel records an error code,
 // drains its own TMA loads and MMAs, frees TMEM and returns.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "tvq_common.cuh"
@@ -41,10 +43,18 @@ constexpr int UMMA_K = 32;     // K per tcgen05.mma for 8-bit operands
 constexpr int EPI_WARPS = 8;   // two epilogue warps per TMEM lane group
 constexpr int THREADS = 128 + 32 * EPI_WARPS;  // warps 0-3: TMA, MMA, TMEM alloc, spare; 4-11: epilogue
 constexpr int CH = 16;         // accumulator columns per epilogue chunk (tcgen05.ld .x16)
+// GEMM_TF32X3 sums its products in TMEM over this many k-blocks (32 f32
+// each) only; the epilogue adds the partial sums in registers with IEEE
+// round-to-nearest.  The tensor core's own f32 accumulation is less exact
+// than IEEE addition, and over a long K its error grows to ~2^-18 of
+// sum|a*w|; promoting every few k-blocks keeps the result at fp32 SGEMM
+// accuracy.  TVQ_TF32_PROMOTE_KB overrides it (tuning).
+constexpr int TF32_PROMOTE_KB = 2;  // max error ~3x cuBLAS SGEMM, ~15% slower than no promotion
 
 struct KParams {
     int m, n, k;
     int num_m_blocks, num_n_blocks, num_k_blocks;
+    int promote_kb;  // k-blocks per TMEM accumulation unit (GEMM_TF32X3)
     const float* bias;
     const float* residual;
     float* Y;
@@ -101,40 +111,113 @@ __device__ __forceinline__ int8_t q8_out(double v) {
     return static_cast<int8_t>(static_cast<int>(r));
 }
 
+struct EpiCtx {
+    bool vec_ok;     // n % 4 == 0: 16-byte row segments
+    InvScale qs;     // 1 / scale_out for the int8 output
+};
+
+// Second half of the epilogue for one 32-row x CH-column chunk, y = row
+// `lane`: swizzled shared-memory transpose (float4 slot j of row r sits at
+// slot j ^ ((r >> 1) & 3), conflict-free both ways), then four lanes per
+// 64-byte row segment: residual add, f32 / int8 stores, running amax.
+__device__ __forceinline__ void stage_and_store(const KParams& p, const EpiCtx& e, float* stage, const float (&y)[CH],
+                                                int lane, int row0, int n0, float& amax) {
+#pragma unroll
+    for (int j = 0; j < CH / 4; j++)
+        *reinterpret_cast<float4*>(&stage[lane * CH + 4 * (j ^ ((lane >> 1) & 3))]) =
+            make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < 4; it++) {
+        const int rr = it * 8 + (lane >> 2);
+        const int c4 = lane & 3;
+        const int row = row0 + rr;
+        const int col = n0 + 4 * c4;
+        float4 v = *reinterpret_cast<const float4*>(&stage[rr * CH + 4 * (c4 ^ ((rr >> 1) & 3))]);
+        if (row >= p.m || col >= p.n) continue;
+        const int64_t off = static_cast<int64_t>(row) * p.n + col;
+        if (e.vec_ok && col + 3 < p.n) {
+            if (p.residual) {
+                // plain load: the residual may alias Y (in-place residual stream)
+                const float4 t = *reinterpret_cast<const float4*>(p.residual + off);
+                v.x = __fadd_rn(v.x, t.x);
+                v.y = __fadd_rn(v.y, t.y);
+                v.z = __fadd_rn(v.z, t.z);
+                v.w = __fadd_rn(v.w, t.w);
+            }
+            if (p.amax) amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            if (p.Y) *reinterpret_cast<float4*>(p.Y + off) = v;
+            if (p.Yq) {
+                char4 q;
+                const bool ok = quant_fast(v.x, e.qs, q.x) & quant_fast(v.y, e.qs, q.y) &
+                                quant_fast(v.z, e.qs, q.z) & quant_fast(v.w, e.qs, q.w);
+                if (!ok) {
+                    q.x = quant_exact(v.x, e.qs);
+                    q.y = quant_exact(v.y, e.qs);
+                    q.z = quant_exact(v.z, e.qs);
+                    q.w = quant_exact(v.w, e.qs);
+                }
+                *reinterpret_cast<char4*>(p.Yq + off) = q;
+            }
+        } else {
+            const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                if (col + k >= p.n) break;
+                float x = vv[k];
+                if (p.residual) x = __fadd_rn(x, p.residual[off + k]);
+                if (p.amax) amax = fmaxf(amax, fabsf(x));
+                if (p.Y) p.Y[off + k] = x;
+                if (p.Yq) p.Yq[off + k] = quant_exact(x, e.qs);
+            }
+        }
+    }
+}
+
 template <int KIND, int BN>
 __device__ __forceinline__ constexpr uint32_t make_idesc() {
     // instruction descriptor: [4,6) D format, [7,10) A format, [10,13) B
     // format, [15]/[16] A/B major (0 = K), [17,23) N>>3, [24,29) M>>4
-    return (KIND == GEMM_I8 ? (2u << 4) | (1u << 7) | (1u << 10)   // S32 <- s8 x s8
-                            : (1u << 4) | (0u << 7) | (0u << 10))  // F32 <- e4m3 x e4m3
+    return (KIND == GEMM_I8   ? (2u << 4) | (1u << 7) | (1u << 10)    // S32 <- s8 x s8
+            : KIND == GEMM_F8 ? (1u << 4) | (0u << 7) | (0u << 10)    // F32 <- e4m3 x e4m3
+                              : (1u << 4) | (2u << 7) | (2u << 10))   // F32 <- tf32 x tf32
            | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
 }
 
-template <int BN>
+// NS operand parts per stage: 1, or 2 (high + low) for the TF32 split GEMM.
+template <int KIND, int BN>
 struct Cfg {
-    static constexpr uint32_t A_BYTES = BM * BK;
+    static constexpr int NS = (KIND == GEMM_TF32X3) ? 2 : 1;
+    static constexpr int ELEM = (KIND == GEMM_TF32X3) ? 4 : 1;  // bytes per element
+    static constexpr int BKE = BK / ELEM;                         // K elements per stage
+    static constexpr uint32_t A_BYTES = BM * BK;                  // one part
     static constexpr uint32_t B_BYTES = BN * BK;
-    static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
-    static constexpr uint32_t TMEM_COLS = 2 * BN;  // 128/256/512: powers of two
-    static constexpr uint32_t RING = STAGES * (A_BYTES + B_BYTES);
+    static constexpr int STAGES = (NS * (BM + BN) * BK * 8 <= 196608) ? 8 : 196608 / (NS * (BM + BN) * BK);
+    // TMEM accumulator buffers: 2 (tile i+1's MMAs overlap tile i's
+    // epilogue), 4 for the short promotion units of GEMM_TF32X3
+    static constexpr int NACC = (KIND == GEMM_TF32X3) ? 4 : 2;
+    static constexpr uint32_t TMEM_COLS = NACC * BN;  // 128/256/512: powers of two
+    static constexpr uint32_t RING = STAGES * NS * (A_BYTES + B_BYTES);
     static constexpr uint32_t EPI = EPI_WARPS * 32 * CH * 4;  // per-epilogue-warp 32 x 16 f32 staging tiles
     static constexpr uint32_t SMEM = RING + EPI + 1024 /*align*/ + 512 /*barriers*/;
 };
 
 template <int KIND, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, KParams p) {
-    using C = Cfg<BN>;
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, KParams p) {
+    using C = Cfg<KIND, BN>;
     constexpr int STAGES = C::STAGES;
+    constexpr int NS = C::NS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sA = smem;
-    uint8_t* sB = smem + STAGES * C::A_BYTES;
+    uint8_t* sA = smem;                                // stage s: NS parts of A_BYTES
+    uint8_t* sB = smem + STAGES * NS * C::A_BYTES;     // stage s: NS parts of B_BYTES
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING + C::EPI);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
-    uint64_t* tempty = tfull + 2;
-    uint64_t* drain = tempty + 2;
+    uint64_t* tempty = tfull + C::NACC;
+    uint64_t* drain = tempty + C::NACC;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -145,7 +228,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < C::NACC; b++) {
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], EPI_WARPS);
         }
@@ -155,6 +238,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        if (NS == 2) {
+            tma_prefetch_desc(&tmA2);
+            tma_prefetch_desc(&tmB2);
+        }
     }
     if (warp == 2) {
         tmem_alloc(tmem_holder, C::TMEM_COLS);
@@ -179,9 +266,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint32_t s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1u;
                     if (!mbar_wait(&empty[s], ph ^ 1u, p.err, DEVERR_TIMEOUT_PRODUCER)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES);
-                    tma_load_2d(&tmA, &full[s], sA + s * C::A_BYTES, kb * BK, mb * BM);
-                    tma_load_2d(&tmB, &full[s], sB + s * C::B_BYTES, kb * BK, nb * BN);
+                    mbar_arrive_expect_tx(&full[s], NS * (C::A_BYTES + C::B_BYTES));
+                    tma_load_2d(&tmA, &full[s], sA + s * NS * C::A_BYTES, kb * C::BKE, mb * BM);
+                    tma_load_2d(&tmB, &full[s], sB + s * NS * C::B_BYTES, kb * C::BKE, nb * BN);
+                    if (NS == 2) {
+                        tma_load_2d(&tmA2, &full[s], sA + (s * NS + 1) * C::A_BYTES, kb * C::BKE, mb * BM);
+                        tma_load_2d(&tmB2, &full[s], sB + (s * NS + 1) * C::B_BYTES, kb * C::BKE, nb * BN);
+                    }
                 }
             }
             // every issued load lands before the CTA may exit
@@ -193,33 +284,48 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = make_idesc<KIND, BN>();
-            uint32_t it = 0, tcount = 0;
+            // one accumulation unit = a tile (or, GEMM_TF32X3, a run of
+            // TF32_PROMOTE_KB k-blocks of it) in one of the two TMEM buffers
+            const int pk = (KIND == GEMM_TF32X3) ? p.promote_kb : p.num_k_blocks;
+            uint32_t it = 0, ucount = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, tcount++) {
-                const uint32_t b = tcount & 1u;
-                const uint32_t aph = (tcount >> 1) & 1u;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x)
+            for (int kb0 = 0; kb0 < p.num_k_blocks && ok; kb0 += pk, ucount++) {
+                const uint32_t b = ucount % C::NACC;
+                const uint32_t aph = (ucount / C::NACC) & 1u;
                 if (!mbar_wait(&tempty[b], aph ^ 1u, p.err, DEVERR_TIMEOUT_MMA)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + b * BN;
-                for (int kb = 0; kb < p.num_k_blocks; kb++, it++) {
+                const int kb1 = min(p.num_k_blocks, kb0 + pk);
+                for (int kb = kb0; kb < kb1; kb++, it++) {
                     const uint32_t s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1u;
                     if (!mbar_wait(&full[s], ph, p.err, DEVERR_TIMEOUT_MMA)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(sA + s * C::A_BYTES);
-                    const uint32_t b0 = smem_u32(sB + s * C::B_BYTES);
+                    const uint32_t a0 = smem_u32(sA + s * NS * C::A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + s * NS * C::B_BYTES);
 #pragma unroll
-                    for (int kk = 0; kk < BK / UMMA_K; kk++) {
+                    for (int kk = 0; kk < BK / UMMA_K; kk++) {  // 32 bytes of K per instruction
                         const uint64_t ad = smem_desc_k_sw128(a0 + kk * UMMA_K);
                         const uint64_t bd = smem_desc_k_sw128(b0 + kk * UMMA_K);
-                        const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
-                        if (KIND == GEMM_I8) umma_i8(d_tmem, ad, bd, idesc, accum);
-                        else umma_f8(d_tmem, ad, bd, idesc, accum);
+                        const uint32_t accum = (kb > kb0 || kk > 0) ? 1u : 0u;
+                        if (KIND == GEMM_I8) {
+                            umma_i8(d_tmem, ad, bd, idesc, accum);
+                        } else if (KIND == GEMM_F8) {
+                            umma_f8(d_tmem, ad, bd, idesc, accum);
+                        } else {
+                            // x*w ~ xh*wh + xh*wl + xl*wh, small terms first
+                            const uint64_t adl = smem_desc_k_sw128(a0 + C::A_BYTES + kk * UMMA_K);
+                            const uint64_t bdl = smem_desc_k_sw128(b0 + C::B_BYTES + kk * UMMA_K);
+                            umma_tf32(d_tmem, adl, bd, idesc, accum);
+                            umma_tf32(d_tmem, ad, bdl, idesc, 1u);
+                            umma_tf32(d_tmem, ad, bd, idesc, 1u);
+                        }
                     }
                     umma_commit(&empty[s]);  // stage s is free once these MMAs retire
                 }
                 if (!ok) break;
-                umma_commit(&tfull[b]);      // accumulator b is complete
+                umma_commit(&tfull[b]);      // accumulator b holds the unit's sum
             }
             // all issued MMAs retire before TMEM is released
             umma_commit(drain);
@@ -236,19 +342,66 @@ __global__ void __launch_bounds__(THREADS, 1)
         float* stage = reinterpret_cast<float*>(smem + C::RING) + (warp - 4) * (32 * CH);
         const bool bias_on = p.bias != nullptr;
         const bool per_channel = p.per_channel != 0;
-        const float sa = __ldg(p.scale_a);
-        const float sw0 = __ldg(p.scales_w);
+        const float sa = (KIND == GEMM_TF32X3) ? 1.0f : __ldg(p.scale_a);
+        const float sw0 = (KIND == GEMM_TF32X3) ? 1.0f : __ldg(p.scales_w);
         InvScale qs{0.0, 0.0f, 0.0f};
         if (p.Yq) qs = make_inv_scale(static_cast<double>(__ldg(p.scale_out)));
-        const bool vec_ok = (p.n & 3) == 0;
+        EpiCtx ec{(p.n & 3) == 0, qs};
         // 16-byte vector loads of the per-column scales / bias need aligned bases
-        const bool vec_cols = vec_ok && (!per_channel || (reinterpret_cast<uintptr_t>(p.scales_w) & 15) == 0) &&
+        const bool vec_cols = ec.vec_ok && (!per_channel || (reinterpret_cast<uintptr_t>(p.scales_w) & 15) == 0) &&
                               (!bias_on || (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0);
         float amax = 0.0f;
+        const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(eg * 32) << 16);
+        if constexpr (KIND == GEMM_TF32X3) {
+            // partial sums of TF32_PROMOTE_KB k-blocks each, added in registers
+            constexpr int NCH = BN / CH / 2;  // chunks this warp owns: half, half + 2, ...
+            uint32_t ucount = 0;
+            bool alive = true;
+            for (int tile = blockIdx.x; tile < num_tiles && alive; tile += gridDim.x) {
+                const int mb = tile % p.num_m_blocks;
+                const int nb = tile / p.num_m_blocks;
+                const int row0 = mb * BM + eg * 32;
+                float acc[NCH][CH];
+                for (int kb0 = 0; kb0 < p.num_k_blocks; kb0 += p.promote_kb, ucount++) {
+                    const uint32_t b = ucount % C::NACC;
+                    const uint32_t aph = (ucount / C::NACC) & 1u;
+                    const bool got = mbar_wait(&tfull[b], aph, p.err, DEVERR_TIMEOUT_EPILOGUE);
+                    __syncwarp();
+                    if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
+                    tc_fence_after();
+                    uint32_t r[NCH][CH];
+#pragma unroll
+                    for (int i = 0; i < NCH; i++) tmem_ld16(lane_base + b * BN + (half + 2 * i) * CH, r[i]);
+                    tmem_ld_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[b]);
+                    if (kb0 == 0) {
+#pragma unroll
+                        for (int i = 0; i < NCH; i++)
+#pragma unroll
+                            for (int j = 0; j < CH; j++) acc[i][j] = __uint_as_float(r[i][j]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < NCH; i++)
+#pragma unroll
+                            for (int j = 0; j < CH; j++) acc[i][j] = __fadd_rn(acc[i][j], __uint_as_float(r[i][j]));
+                    }
+                }
+                if (!alive) break;
+#pragma unroll
+                for (int i = 0; i < NCH; i++) {
+                    const int n0 = nb * BN + (half + 2 * i) * CH;
+                    if (n0 >= p.n) break;  // warp-uniform
+                    __syncwarp();           // the previous chunk's staging reads are done
+                    stage_and_store(p, ec, stage, acc[i], lane, row0, n0, amax);
+                }
+            }
+        } else {
         uint32_t tcount = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, tcount++) {
-            const uint32_t b = tcount & 1u;
-            const uint32_t aph = (tcount >> 1) & 1u;
+            const uint32_t b = tcount % C::NACC;
+            const uint32_t aph = (tcount / C::NACC) & 1u;
             const bool got = mbar_wait(&tfull[b], aph, p.err, DEVERR_TIMEOUT_EPILOGUE);
             __syncwarp();
             if (!__all_sync(0xffffffffu, got)) break;
@@ -262,7 +415,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (n0 >= p.n) break;  // warp-uniform
                 uint32_t r[CH];
                 __syncwarp();
-                tmem_ld16(tmem_base + (static_cast<uint32_t>(eg * 32) << 16) + b * BN + c * CH, r);
+                tmem_ld16(lane_base + b * BN + c * CH, r);
                 tmem_ld_wait();
                 if (p.acc_out && row0 + lane < p.m) {
                     int32_t* dst = p.acc_out + static_cast<int64_t>(row0 + lane) * p.n + n0;
@@ -334,62 +487,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < CH; j++) y[j] = y[j] > 0.0f ? y[j] : 0.0f;
                 }
-                // stage row `lane`: float4 slot j stored at slot j ^ ((lane >> 1) & 3)
-                // (conflict-free for both the row writes and the column reads)
-#pragma unroll
-                for (int j = 0; j < CH / 4; j++)
-                    *reinterpret_cast<float4*>(&stage[lane * CH + 4 * (j ^ ((lane >> 1) & 3))]) =
-                        make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
-                __syncwarp();
-#pragma unroll
-                for (int it = 0; it < 4; it++) {
-                    const int rr = it * 8 + (lane >> 2);
-                    const int c4 = lane & 3;
-                    const int row = row0 + rr;
-                    const int col = n0 + 4 * c4;
-                    float4 v = *reinterpret_cast<const float4*>(&stage[rr * CH + 4 * (c4 ^ ((rr >> 1) & 3))]);
-                    if (row >= p.m || col >= p.n) continue;
-                    const int64_t off = static_cast<int64_t>(row) * p.n + col;
-                    if (vec_ok && col + 3 < p.n) {
-                        if (p.residual) {
-                            // plain load: the residual may alias Y (in-place residual stream)
-                            const float4 t = *reinterpret_cast<const float4*>(p.residual + off);
-                            v.x = __fadd_rn(v.x, t.x);
-                            v.y = __fadd_rn(v.y, t.y);
-                            v.z = __fadd_rn(v.z, t.z);
-                            v.w = __fadd_rn(v.w, t.w);
-                        }
-                        if (p.amax) amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-                        if (p.Y) *reinterpret_cast<float4*>(p.Y + off) = v;
-                        if (p.Yq) {
-                            char4 q;
-                            const bool ok = quant_fast(v.x, qs, q.x) & quant_fast(v.y, qs, q.y) &
-                                            quant_fast(v.z, qs, q.z) & quant_fast(v.w, qs, q.w);
-                            if (!ok) {
-                                q.x = quant_exact(v.x, qs);
-                                q.y = quant_exact(v.y, qs);
-                                q.z = quant_exact(v.z, qs);
-                                q.w = quant_exact(v.w, qs);
-                            }
-                            *reinterpret_cast<char4*>(p.Yq + off) = q;
-                        }
-                    } else {
-                        const float vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            if (col + e >= p.n) break;
-                            float x = vv[e];
-                            if (p.residual) x = __fadd_rn(x, p.residual[off + e]);
-                            if (p.amax) amax = fmaxf(amax, fabsf(x));
-                            if (p.Y) p.Y[off + e] = x;
-                            if (p.Yq) p.Yq[off + e] = quant_exact(x, qs);
-                        }
-                    }
-                }
+                stage_and_store(p, ec, stage, y, lane, row0, n0, amax);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[b]);
+        }
         }
         if (p.amax) {
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 16));
@@ -454,15 +557,17 @@ int get_encoder() {
     return TVQ_OK;
 }
 
-// 2-D K-major 8-bit operand [rows, k]: box {128 bytes of K, box_rows}.
-int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box_rows) {
+// 2-D K-major operand [rows, k] of 1-byte or 4-byte elements: box {128 bytes
+// of K, box_rows}, 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box_rows, int elem) {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k)};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * elem};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK / elem), static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = g_encode(map, elem == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                          const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_error(TVQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) + ")");
         return TVQ_ERR_CUDA;
@@ -471,8 +576,8 @@ int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box
 }
 
 template <int KIND, int BN>
-int launch_tc(const KParams& p, const void* A, const void* W, int grid, cudaStream_t st) {
-    using C = Cfg<BN>;
+int launch_tc(const KParams& p, const GemmArgs& g, int grid, cudaStream_t st) {
+    using C = Cfg<KIND, BN>;
     static int attr_done[64] = {0};  // per device
     int dev = 0;
     TVQ_CUDA(cudaGetDevice(&dev));
@@ -481,14 +586,42 @@ int launch_tc(const KParams& p, const void* A, const void* W, int grid, cudaStre
                                       static_cast<int>(C::SMEM)));
         attr_done[dev] = 1;
     }
-    CUtensorMap ma, mb;
-    int rc = make_map(&ma, A, p.m, p.k, BM);
+    CUtensorMap ma, mb, ma2, mb2;
+    int rc = make_map(&ma, g.A, p.m, p.k, BM, C::ELEM);
+    if (!rc) rc = make_map(&mb, g.W, p.n, p.k, BN, C::ELEM);
+    if (!rc && C::NS == 2) rc = make_map(&ma2, g.A2, p.m, p.k, BM, C::ELEM);
+    if (!rc && C::NS == 2) rc = make_map(&mb2, g.W2, p.n, p.k, BN, C::ELEM);
     if (rc) return rc;
-    rc = make_map(&mb, W, p.n, p.k, BN);
-    if (rc) return rc;
-    gemm_tc_kernel<KIND, BN><<<grid, THREADS, C::SMEM, st>>>(ma, mb, p);
+    if (C::NS == 1) {
+        ma2 = ma;
+        mb2 = mb;
+    }
+    gemm_tc_kernel<KIND, BN><<<grid, THREADS, C::SMEM, st>>>(ma, mb, ma2, mb2, p);
     TVQ_CUDA(cudaGetLastError());
     return TVQ_OK;
+}
+
+// Round a float to the TF32 grid (10 explicit mantissa bits), half away
+// from zero, so the tensor core reads it without truncation.
+__device__ __forceinline__ float round_tf32(float v) {
+    const uint32_t u = __float_as_uint(v);
+    if ((u & 0x7F800000u) == 0x7F800000u) return v;
+    float h = __uint_as_float((u + 0x1000u) & 0xFFFFE000u);
+    if ((__float_as_uint(h) & 0x7F800000u) == 0x7F800000u) h = __uint_as_float(u & 0xFFFFE000u);
+    return h;
+}
+
+// x ~ hi + lo with hi and lo both on the TF32 grid: hi = tf32(x), lo =
+// tf32(x - hi); |x - hi - lo| <= 2^-22 |x|.  (hi + lo == x when x itself
+// has at most 22 significant bits.)
+__global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo,
+                                  int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        const float h = round_tf32(v);
+        hi[i] = h;
+        lo[i] = (h == v) ? 0.0f : round_tf32(__fsub_rn(v, h));
+    }
 }
 
 }  // namespace
@@ -498,7 +631,9 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     TVQ_CHECK(g.m < (1ll << 31) && g.n < (1ll << 31) && g.k < 133143, TVQ_ERR_UNSUPPORTED,
               "GEMM size out of range (k must stay below 133143 for exact int32 accumulation)");
     if (g.m == 0 || g.n == 0) return TVQ_OK;
-    TVQ_CHECK(g.scale_a && g.scales_w, TVQ_ERR_INVALID, "scale pointers are required");
+    TVQ_CHECK(g.kind == GEMM_TF32X3 || (g.scale_a && g.scales_w), TVQ_ERR_INVALID, "scale pointers are required");
+    TVQ_CHECK(g.kind != GEMM_TF32X3 || (!g.Yq && !g.bias && !g.residual && g.act == 0 && g.Y), TVQ_ERR_INVALID,
+              "the split fp32 GEMM writes plain f32 Y only");
     TVQ_CHECK(!g.Yq || g.scale_out, TVQ_ERR_INVALID, "int8 output needs scale_out");
     int rc = 0;
     DeviceState* ds = device_state(&rc);
@@ -522,8 +657,15 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.amax = g.amax;
     p.err = ds->d_error;
     p.num_m_blocks = static_cast<int>((g.m + BM - 1) / BM);
-    p.num_k_blocks = static_cast<int>((g.k + BK - 1) / BK);
+    const int elem = (g.kind == GEMM_TF32X3) ? 4 : 1;
+    p.num_k_blocks = static_cast<int>((g.k * elem + BK - 1) / BK);
+    p.promote_kb = TF32_PROMOTE_KB;
+    if (const char* env = getenv("TVQ_TF32_PROMOTE_KB")) p.promote_kb = std::max(1, atoi(env));
 
+    if (g.k == 0 && g.kind == GEMM_TF32X3) {
+        TVQ_CUDA(cudaMemsetAsync(g.Y, 0, sizeof(float) * g.m * g.n, st));
+        return TVQ_OK;
+    }
     if (g.k == 0) {
         const int64_t total = g.m * g.n;
         int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, ds->sm_count * 8));
@@ -531,9 +673,12 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
         TVQ_CUDA(cudaGetLastError());
         return TVQ_OK;
     }
-    TVQ_CHECK(g.k % 16 == 0, TVQ_ERR_UNSUPPORTED, "k must be a multiple of 16 (TMA row pitch)");
+    TVQ_CHECK((g.k * elem) % 16 == 0, TVQ_ERR_UNSUPPORTED, "k must be a multiple of 16 bytes (TMA row pitch)");
     TVQ_CHECK(((reinterpret_cast<uintptr_t>(g.A) | reinterpret_cast<uintptr_t>(g.W)) & 15) == 0, TVQ_ERR_UNSUPPORTED,
               "A and W must be 16-byte aligned");
+    TVQ_CHECK(g.kind != GEMM_TF32X3 ||
+                  (g.A2 && g.W2 && ((reinterpret_cast<uintptr_t>(g.A2) | reinterpret_cast<uintptr_t>(g.W2)) & 15) == 0),
+              TVQ_ERR_UNSUPPORTED, "the split GEMM needs 16-byte aligned low parts");
     TVQ_CHECK(!g.Y || (reinterpret_cast<uintptr_t>(g.Y) & 15) == 0, TVQ_ERR_UNSUPPORTED, "Y must be 16-byte aligned");
     TVQ_CHECK(!g.residual || (reinterpret_cast<uintptr_t>(g.residual) & 15) == 0, TVQ_ERR_UNSUPPORTED,
               "residual must be 16-byte aligned");
@@ -544,9 +689,10 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
 
     // Tile width: the widest N tile that still gives every SM a tile.
     int bn = g.force_bn;
+    if (g.kind == GEMM_TF32X3 && bn > 128) bn = 128;  // its partial sums live in registers
     if (bn == 0) {
         const int64_t mblk = p.num_m_blocks;
-        if (mblk * ((g.n + 255) / 256) >= ds->sm_count) bn = 256;
+        if (g.kind != GEMM_TF32X3 && mblk * ((g.n + 255) / 256) >= ds->sm_count) bn = 256;
         else if (mblk * ((g.n + 127) / 128) >= ds->sm_count) bn = 128;
         else bn = 64;
     }
@@ -554,13 +700,28 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     const int tiles = p.num_m_blocks * p.num_n_blocks;
     const int grid = std::min(tiles, ds->sm_count);
     if (g.kind == GEMM_I8) {
-        if (bn == 256) return launch_tc<GEMM_I8, 256>(p, g.A, g.W, grid, st);
-        if (bn == 128) return launch_tc<GEMM_I8, 128>(p, g.A, g.W, grid, st);
-        return launch_tc<GEMM_I8, 64>(p, g.A, g.W, grid, st);
+        if (bn == 256) return launch_tc<GEMM_I8, 256>(p, g, grid, st);
+        if (bn == 128) return launch_tc<GEMM_I8, 128>(p, g, grid, st);
+        return launch_tc<GEMM_I8, 64>(p, g, grid, st);
     }
-    if (bn == 256) return launch_tc<GEMM_F8, 256>(p, g.A, g.W, grid, st);
-    if (bn == 128) return launch_tc<GEMM_F8, 128>(p, g.A, g.W, grid, st);
-    return launch_tc<GEMM_F8, 64>(p, g.A, g.W, grid, st);
+    if (g.kind == GEMM_F8) {
+        if (bn == 256) return launch_tc<GEMM_F8, 256>(p, g, grid, st);
+        if (bn == 128) return launch_tc<GEMM_F8, 128>(p, g, grid, st);
+        return launch_tc<GEMM_F8, 64>(p, g, grid, st);
+    }
+    if (bn >= 128) return launch_tc<GEMM_TF32X3, 128>(p, g, grid, st);
+    return launch_tc<GEMM_TF32X3, 64>(p, g, grid, st);
+}
+
+int launch_split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStream_t st) {
+    if (n <= 0) return TVQ_OK;
+    int rc = 0;
+    DeviceState* ds = device_state(&rc);
+    if (!ds) return rc;
+    const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, ds->sm_count * 8));
+    split_tf32_kernel<<<grid, 256, 0, st>>>(x, hi, lo, n);
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
 }
 
 }  // namespace tvq

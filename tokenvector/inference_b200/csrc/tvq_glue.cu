@@ -169,6 +169,137 @@ __global__ void layernorm_kernel(const float* __restrict__ x, const float* __res
     }
 }
 
+// Register-resident variant for d % 4 == 0 and d <= 128 * NV: the row is
+// read once into NV float4 per lane; four independent float-pair
+// accumulators per lane shorten the two-sum chains.  Same arithmetic as
+// layernorm_kernel.
+template <int NV>
+__global__ void layernorm_reg_kernel(const float* __restrict__ x, const float* __restrict__ g,
+                                     const float* __restrict__ b, float* __restrict__ y, int8_t* __restrict__ q,
+                                     const float* __restrict__ qscale, uint32_t* __restrict__ amax, int T, int d,
+                                     double eps) {
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const int d4 = d >> 2;
+    InvScale qs{0.0, 0.0f, 0.0f};
+    if (q) qs = make_inv_scale(static_cast<double>(__ldg(qscale)));
+    const float eps_h = __double2float_rn(eps);
+    const float eps_l = __double2float_rn(eps - static_cast<double>(eps_h));
+    const float df = static_cast<float>(d);
+    float am = 0.0f;
+    for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
+        const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(t) * d);
+        float4 v[NV];
+#pragma unroll
+        for (int j = 0; j < NV; j++) {
+            const int i = j * 32 + lane;
+            v[j] = (i < d4) ? __ldcs(xr + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        // sum: four float-pair accumulators (x, y, z, w components)
+        float sh[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int j = 0; j < NV; j++) {
+            const float c[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                float s, e;
+                two_sum(sh[k], c[k], s, e);
+                sh[k] = s;
+                sl[k] = __fadd_rn(sl[k], e);
+            }
+        }
+        df_add(sh[0], sl[0], sh[1], sl[1], sh[0], sl[0]);
+        df_add(sh[2], sl[2], sh[3], sl[3], sh[2], sl[2]);
+        df_add(sh[0], sl[0], sh[2], sl[2], sh[0], sl[0]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float oh = __shfl_xor_sync(0xffffffffu, sh[0], o), ol = __shfl_xor_sync(0xffffffffu, sl[0], o);
+            df_add(sh[0], sl[0], oh, ol, sh[0], sl[0]);
+        }
+        float mh, ml;
+        df_div_int(sh[0], sl[0], df, mh, ml);
+        // variance of the valid elements (padding lanes contribute nothing)
+        float vh[4] = {0.0f, 0.0f, 0.0f, 0.0f}, vl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int j = 0; j < NV; j++) {
+            if (j * 32 + lane >= d4) continue;
+            const float c[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                float dh, de;
+                two_sum(c[k], -mh, dh, de);
+                de = __fsub_rn(de, ml);
+                const float p = __fmul_rn(dh, dh);
+                float pe = fmaf(dh, dh, -p);
+                pe = fmaf(2.0f * dh, de, pe);
+                float s, e;
+                two_sum(vh[k], p, s, e);
+                vh[k] = s;
+                vl[k] = __fadd_rn(vl[k], __fadd_rn(e, pe));
+            }
+        }
+        df_add(vh[0], vl[0], vh[1], vl[1], vh[0], vl[0]);
+        df_add(vh[2], vl[2], vh[3], vl[3], vh[2], vl[2]);
+        df_add(vh[0], vl[0], vh[2], vl[2], vh[0], vl[0]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float oh = __shfl_xor_sync(0xffffffffu, vh[0], o), ol = __shfl_xor_sync(0xffffffffu, vl[0], o);
+            df_add(vh[0], vl[0], oh, ol, vh[0], vl[0]);
+        }
+        float wh, wl, rh, rl;
+        df_div_int(vh[0], vl[0], df, wh, wl);
+        df_add(wh, wl, eps_h, eps_l, wh, wl);
+        df_rsqrt(wh, wl, rh, rl);
+        const float4* g4 = reinterpret_cast<const float4*>(g);
+        const float4* b4 = reinterpret_cast<const float4*>(b);
+#pragma unroll
+        for (int j = 0; j < NV; j++) {
+            const int i = j * 32 + lane;
+            if (i >= d4) continue;
+            const float4 gg = __ldg(g4 + i), bb = __ldg(b4 + i);
+            const float c[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+            const float gv[4] = {gg.x, gg.y, gg.z, gg.w};
+            const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
+            float o4[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                float dh, de;
+                two_sum(c[k], -mh, dh, de);
+                de = __fsub_rn(de, ml);
+                const float tt = __fmul_rn(dh, rh);
+                float te = fmaf(dh, rh, -tt);
+                te = fmaf(dh, rl, te);
+                te = fmaf(de, rh, te);
+                const float u = __fmul_rn(tt, gv[k]);
+                float ue = fmaf(tt, gv[k], -u);
+                ue = fmaf(te, gv[k], ue);
+                float s, e;
+                two_sum(u, bv[k], s, e);
+                o4[k] = __fadd_rn(s, __fadd_rn(e, ue));
+                am = fmaxf(am, fabsf(o4[k]));
+            }
+            const int64_t idx = static_cast<int64_t>(t) * d + 4 * i;
+            if (y) *reinterpret_cast<float4*>(y + idx) = make_float4(o4[0], o4[1], o4[2], o4[3]);
+            if (q) {
+                char4 qq;
+                const bool ok = quant_fast(o4[0], qs, qq.x) & quant_fast(o4[1], qs, qq.y) &
+                                quant_fast(o4[2], qs, qq.z) & quant_fast(o4[3], qs, qq.w);
+                if (!ok) {
+                    qq.x = quant_exact(o4[0], qs);
+                    qq.y = quant_exact(o4[1], qs);
+                    qq.z = quant_exact(o4[2], qs);
+                    qq.w = quant_exact(o4[3], qs);
+                }
+                *reinterpret_cast<char4*>(q + idx) = qq;
+            }
+        }
+    }
+    if (amax) {
+        am = warp_max_f(am);
+        if (lane == 0) atomicMax(amax, __float_as_uint(am));
+    }
+}
+
 int launch_layernorm(const float* x, const float* g, const float* b, float* y, int8_t* q, const float* qscale,
                      uint32_t* amax, int T, int d, double eps, cudaStream_t st) {
     if (T <= 0) return TVQ_OK;
@@ -176,7 +307,23 @@ int launch_layernorm(const float* x, const float* g, const float* b, float* y, i
     const int rows_per_block = threads / 32;
     int grid = (T + rows_per_block - 1) / rows_per_block;
     grid = std::min(grid, sm_count() * 16);
-    layernorm_kernel<<<grid, threads, 0, st>>>(x, g, b, y, q, qscale, amax, T, d, eps);
+    const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(g) |
+                         reinterpret_cast<uintptr_t>(b) | (y ? reinterpret_cast<uintptr_t>(y) : 0) |
+                         (q ? reinterpret_cast<uintptr_t>(q) & 3 : 0);
+    const int nv = (d + 127) / 128;
+    if ((d & 3) == 0 && (al & 15) == 0 && nv <= 16) {
+#define TVQ_LN(NV) layernorm_reg_kernel<NV><<<grid, threads, 0, st>>>(x, g, b, y, q, qscale, amax, T, d, eps)
+        if (nv <= 1) TVQ_LN(1);
+        else if (nv <= 2) TVQ_LN(2);
+        else if (nv <= 4) TVQ_LN(4);
+        else if (nv <= 6) TVQ_LN(6);
+        else if (nv <= 8) TVQ_LN(8);
+        else if (nv <= 13) TVQ_LN(13);
+        else TVQ_LN(16);
+#undef TVQ_LN
+    } else {
+        layernorm_kernel<<<grid, threads, 0, st>>>(x, g, b, y, q, qscale, amax, T, d, eps);
+    }
     TVQ_CUDA(cudaGetLastError());
     return TVQ_OK;
 }
@@ -185,157 +332,209 @@ int launch_layernorm(const float* x, const float* g, const float* b, float* y, i
 // gpt2_attention, tv/training/gpt2_ref.tkv:360-395 (scores -> causal softmax
 // -> context), per head, over packed sequences: token t of the sequence
 // [s0, s1) attends to u in [s0, t].  qkv rows are [Q | K | V], heads
-// contiguous.  fp32 flash-style tiling: a block owns BQ=64 query rows of one
-// head, walks the key tiles up to the diagonal with an online softmax.
-// 256 threads: thread (ty, tx) holds rows 4ty..4ty+3 and columns 4tx..4tx+3
-// of the 64x64 score tile and of the 64 x HD output tile.
+// contiguous.  fp32 flash-style tiling with an online softmax in base 2
+// (log2(e) / sqrt(hd) folded into Q).  A block of 128 threads owns 64 query
+// rows of one head and one chunk of keys; thread (ty, tx) holds rows
+// 4ty..4ty+3, keys tx, tx+8, ..., tx+56 of each 64-key tile (strided, so the
+// K reads are conflict-free) and output columns tx*HD/8...  Row-major Q, K, V
+// and P tiles in shared memory, float4 loads throughout.
+//
+// Work items: tiles[i] = {q0, seq start, seq end, 0}; with split[i] =
+// {key begin, key end, partial slot, 0} a block handles one key chunk and,
+// when the slot is >= 0, writes an unnormalised partial (O, m, l) that
+// attention_combine_kernel merges; without split the chunk is the whole
+// causal range and the output is final.
 namespace {
 constexpr int AQ = 64;   // query rows per block
-constexpr int AK = 64;   // key rows per tile
-constexpr int APAD = 4;
-}
+constexpr int AK = 64;   // keys per tile
+constexpr int APAD = 4;  // row padding (floats) of the shared tiles
+constexpr int ATHREADS = 128;
+}  // namespace
 
 template <int HD>
-__global__ void __launch_bounds__(256)
-    attention_kernel(const float* __restrict__ qkv, const int4* __restrict__ tiles, int ntiles, int T, int d,
-                     int nheads, float sm_scale, float* __restrict__ out, int8_t* __restrict__ outq,
-                     const float* __restrict__ qscale, uint32_t* __restrict__ amax) {
+__global__ void __launch_bounds__(ATHREADS)
+    attention_kernel(const float* __restrict__ qkv, const int4* __restrict__ tiles, const int4* __restrict__ split,
+                     int d, int nheads, float q_scale, float* __restrict__ out, int8_t* __restrict__ outq,
+                     const float* __restrict__ qscale, uint32_t* __restrict__ amax, float* __restrict__ part_o,
+                     float2* __restrict__ part_ml) {
     static_assert(HD % 16 == 0 && HD <= 64, "head dim");
-    constexpr int CPT = HD / 16;  // output columns per thread
+    constexpr int LD = HD + APAD;   // row pitch of Q, K, V tiles
+    constexpr int PLD = AK + APAD;  // row pitch of P
+    constexpr int DPT = HD / 8;     // output columns per thread
     extern __shared__ float sm[];
-    float* Qt = sm;                         // [HD][AQ+APAD]   Q^T
-    float* Kt = Qt + HD * (AQ + APAD);      // [HD][AK+APAD]   K^T
-    float* Vs = Kt + HD * (AK + APAD);      // [AK][HD]
-    float* Pt = Vs + AK * HD;               // [AK][AQ+APAD]   P^T
+    float* Qs = sm;             // [AQ][LD]
+    float* Ks = Qs + AQ * LD;   // [AK][LD]
+    float* Vs = Ks + AK * LD;   // [AK][LD]
+    float* Ps = Vs + AK * LD;   // [AQ][PLD]
 
-    const int tile_id = blockIdx.x / nheads;
+    const int item = blockIdx.x / nheads;
     const int head = blockIdx.x % nheads;
-    if (tile_id >= ntiles) return;
-    const int4 tl = tiles[tile_id];  // {q0, seg start, seg end, unused}
+    const int4 tl = tiles[item];
     const int q0 = tl.x, s0 = tl.y, s1 = tl.z;
+    int kb = s0, ke = min(q0 + AQ, s1), part = -1;
+    if (split) {
+        const int4 sp = split[item];
+        kb = sp.x;
+        ke = sp.y;
+        part = sp.z;
+    }
     const int tid = threadIdx.x;
-    const int ty = tid >> 4, tx = tid & 15;
-    const int64_t row_stride = 3LL * d;
+    const int ty = tid >> 3, tx = tid & 7;
+    const int64_t rs = 3LL * d;
     const int qoff = head * HD, koff = d + head * HD, voff = 2 * d + head * HD;
+    constexpr int V4 = HD / 4;
 
-    // Q tile, transposed into shared memory (rows beyond the sequence are 0)
-    for (int i = tid; i < AQ * HD; i += 256) {
-        const int r = i / HD, c = i % HD;
+    for (int i = tid; i < AQ * V4; i += ATHREADS) {
+        const int r = i / V4, c = (i % V4) * 4;
         const int t = q0 + r;
-        Qt[c * (AQ + APAD) + r] = (t < s1) ? qkv[t * row_stride + qoff + c] : 0.0f;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (t < s1) {
+            v = *reinterpret_cast<const float4*>(qkv + t * rs + qoff + c);
+            v.x *= q_scale; v.y *= q_scale; v.z *= q_scale; v.w *= q_scale;
+        }
+        *reinterpret_cast<float4*>(&Qs[r * LD + c]) = v;
     }
 
-    float o[4][CPT];
+    float o[4][DPT];
     float mrow[4], lrow[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         mrow[i] = -INFINITY;
         lrow[i] = 0.0f;
 #pragma unroll
-        for (int j = 0; j < CPT; j++) o[i][j] = 0.0f;
+        for (int j = 0; j < DPT; j++) o[i][j] = 0.0f;
     }
 
-    const int last_key = min(q0 + AQ, s1) - 1;  // keys needed: [s0, last_key]
-    for (int k0 = s0; k0 <= last_key; k0 += AK) {
-        __syncthreads();  // previous tile's Kt/Vs/Pt fully consumed
-        for (int i = tid; i < AK * HD; i += 256) {
-            const int r = i / HD, c = i % HD;
+    for (int k0 = kb; k0 < ke; k0 += AK) {
+        __syncthreads();  // previous tile's K / V / P consumed
+        for (int i = tid; i < AK * V4; i += ATHREADS) {
+            const int r = i / V4, c = (i % V4) * 4;
             const int u = k0 + r;
-            const bool ok = u < s1;
-            Kt[c * (AK + APAD) + r] = ok ? qkv[u * row_stride + koff + c] : 0.0f;
-            Vs[r * HD + c] = ok ? qkv[u * row_stride + voff + c] : 0.0f;
+            float4 kv = make_float4(0.0f, 0.0f, 0.0f, 0.0f), vv = kv;
+            if (u < ke) {
+                kv = *reinterpret_cast<const float4*>(qkv + u * rs + koff + c);
+                vv = *reinterpret_cast<const float4*>(qkv + u * rs + voff + c);
+            }
+            *reinterpret_cast<float4*>(&Ks[r * LD + c]) = kv;
+            *reinterpret_cast<float4*>(&Vs[r * LD + c]) = vv;
         }
         __syncthreads();
 
-        // S = Q K^T for this thread's 4 x 4 block
-        float s[4][4];
+        float s[4][8];
 #pragma unroll
         for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int j = 0; j < 4; j++) s[i][j] = 0.0f;
-#pragma unroll 8
-        for (int c = 0; c < HD; c++) {
-            const float4 qa = *reinterpret_cast<const float4*>(&Qt[c * (AQ + APAD) + ty * 4]);
-            const float4 kb = *reinterpret_cast<const float4*>(&Kt[c * (AK + APAD) + tx * 4]);
-            const float qv[4] = {qa.x, qa.y, qa.z, qa.w};
-            const float kv[4] = {kb.x, kb.y, kb.z, kb.w};
+            for (int j = 0; j < 8; j++) s[i][j] = 0.0f;
+#pragma unroll 2
+        for (int c = 0; c < HD; c += 4) {
+            float4 qa[4], kf[8];
+#pragma unroll
+            for (int i = 0; i < 4; i++) qa[i] = *reinterpret_cast<const float4*>(&Qs[(4 * ty + i) * LD + c]);
+#pragma unroll
+            for (int j = 0; j < 8; j++) kf[j] = *reinterpret_cast<const float4*>(&Ks[(tx + 8 * j) * LD + c]);
 #pragma unroll
             for (int i = 0; i < 4; i++)
 #pragma unroll
-                for (int j = 0; j < 4; j++) s[i][j] = fmaf(qv[i], kv[j], s[i][j]);
+                for (int j = 0; j < 8; j++) {
+                    s[i][j] = fmaf(qa[i].x, kf[j].x, s[i][j]);
+                    s[i][j] = fmaf(qa[i].y, kf[j].y, s[i][j]);
+                    s[i][j] = fmaf(qa[i].z, kf[j].z, s[i][j]);
+                    s[i][j] = fmaf(qa[i].w, kf[j].w, s[i][j]);
+                }
         }
 
-        // mask, online softmax (rows are shared by the 16 lanes of a half warp)
+        // causal mask + online softmax; a row's 64 keys are spread over the
+        // 8 consecutive lanes tx = 0..7
         float alpha[4];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            const int t = q0 + ty * 4 + i;
+            const int t = q0 + 4 * ty + i;
             float mx = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int u = k0 + tx * 4 + j;
-                const bool valid = (u <= t) && (u < s1);
-                s[i][j] = valid ? s[i][j] * sm_scale : -INFINITY;
+            for (int j = 0; j < 8; j++) {
+                const int u = k0 + tx + 8 * j;
+                s[i][j] = (u <= t && u < ke) ? s[i][j] : -INFINITY;
                 mx = fmaxf(mx, s[i][j]);
             }
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
             const float mnew = fmaxf(mrow[i], mx);
+            const float mref = (mnew == -INFINITY) ? 0.0f : mnew;  // rows with no key yet stay empty
             float sum = 0.0f;
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float p = (s[i][j] == -INFINITY) ? 0.0f : expf(s[i][j] - mnew);
-                s[i][j] = p;
-                sum += p;
+            for (int j = 0; j < 8; j++) {
+                const float pexp = exp2f(s[i][j] - mref);
+                s[i][j] = pexp;
+                sum += pexp;
             }
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-            alpha[i] = (mrow[i] == -INFINITY) ? 0.0f : expf(mrow[i] - mnew);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+            alpha[i] = exp2f(mrow[i] - mref);  // 0 while mrow is -inf
             lrow[i] = lrow[i] * alpha[i] + sum;
             mrow[i] = mnew;
         }
-        // P^T into shared memory
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-            *reinterpret_cast<float4*>(&Pt[(tx * 4 + j) * (AQ + APAD) + ty * 4]) =
-                make_float4(s[0][j], s[1][j], s[2][j], s[3][j]);
-        __syncthreads();
-
-        // O = alpha * O + P V
 #pragma unroll
         for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int j = 0; j < CPT; j++) o[i][j] *= alpha[i];
-        const int kmax = min(AK, last_key - k0 + 1);
-#pragma unroll 4
-        for (int u = 0; u < kmax; u++) {
-            const float4 pa = *reinterpret_cast<const float4*>(&Pt[u * (AQ + APAD) + ty * 4]);
-            const float pv[4] = {pa.x, pa.y, pa.z, pa.w};
-            float vv[CPT];
+            for (int j = 0; j < 8; j++) Ps[(4 * ty + i) * PLD + tx + 8 * j] = s[i][j];
+        __syncthreads();
+
 #pragma unroll
-            for (int j = 0; j < CPT; j++) vv[j] = Vs[u * HD + tx * CPT + j];
+        for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int i = 0; i < 4; i++)
+            for (int j = 0; j < DPT; j++) o[i][j] *= alpha[i];
+        const int kmax = min(AK, ke - k0);
+        for (int u = 0; u < kmax; u += 4) {
+            float4 pa[4];
 #pragma unroll
-                for (int j = 0; j < CPT; j++) o[i][j] = fmaf(pv[i], vv[j], o[i][j]);
+            for (int i = 0; i < 4; i++) pa[i] = *reinterpret_cast<const float4*>(&Ps[(4 * ty + i) * PLD + u]);
+#pragma unroll
+            for (int uu = 0; uu < 4; uu++) {
+                float vv[DPT];
+#pragma unroll
+                for (int j = 0; j < DPT; j += 2) {
+                    const float2 t2 = *reinterpret_cast<const float2*>(&Vs[(u + uu) * LD + tx * DPT + j]);
+                    vv[j] = t2.x;
+                    vv[j + 1] = t2.y;
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float pv = uu == 0 ? pa[i].x : uu == 1 ? pa[i].y : uu == 2 ? pa[i].z : pa[i].w;
+#pragma unroll
+                    for (int j = 0; j < DPT; j++) o[i][j] = fmaf(pv, vv[j], o[i][j]);
+                }
+            }
         }
     }
 
-    // normalise and store
+    if (part >= 0) {  // unnormalised partial for the combine step
+        const int64_t slot = static_cast<int64_t>(part) * nheads + head;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int r = 4 * ty + i;
+            float* dst = part_o + (slot * AQ + r) * HD + tx * DPT;
+#pragma unroll
+            for (int j = 0; j < DPT; j++) dst[j] = o[i][j];
+            if (tx == 0) part_ml[slot * AQ + r] = make_float2(mrow[i], lrow[i]);
+        }
+        return;
+    }
     InvScale qs{0.0, 0.0f, 0.0f};
     if (outq) qs = make_inv_scale(static_cast<double>(__ldg(qscale)));
     float am = 0.0f;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const int t = q0 + ty * 4 + i;
+        const int t = q0 + 4 * ty + i;
         if (t >= s1) continue;
         const float il = 1.0f / lrow[i];
+        const int64_t base = static_cast<int64_t>(t) * d + head * HD + tx * DPT;
 #pragma unroll
-        for (int j = 0; j < CPT; j++) {
+        for (int j = 0; j < DPT; j++) {
             const float v = o[i][j] * il;
-            const int64_t idx = static_cast<int64_t>(t) * d + head * HD + tx * CPT + j;
-            if (out) out[idx] = v;
-            if (outq) outq[idx] = quant_exact(v, qs);
+            if (out) out[base + j] = v;
+            if (outq) outq[base + j] = quant_exact(v, qs);
             am = fmaxf(am, fabsf(v));
         }
     }
@@ -345,10 +544,51 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// Merge the key-chunk partials of one (query tile, head): m = max m_c,
+// l = sum l_c 2^(m_c - m), O = sum O_c 2^(m_c - m) / l.
 template <int HD>
-static int launch_attention_hd(const float* qkv, const int4* tiles, int ntiles, int T, int d, int nheads,
-                               float* out, int8_t* outq, const float* qscale, uint32_t* amax, cudaStream_t st) {
-    const size_t smem = sizeof(float) * (HD * (AQ + APAD) + HD * (AK + APAD) + AK * HD + AK * (AQ + APAD));
+__global__ void __launch_bounds__(ATHREADS)
+    attention_combine_kernel(const int4* __restrict__ comb, int d, int nheads, const float* __restrict__ part_o,
+                             const float2* __restrict__ part_ml, float* __restrict__ out, int8_t* __restrict__ outq,
+                             const float* __restrict__ qscale, uint32_t* __restrict__ amax) {
+    const int e = blockIdx.x / nheads;
+    const int head = blockIdx.x % nheads;
+    const int4 c = comb[e];  // {q0, seq end, first partial slot, number of partials}
+    const int q0 = c.x, s1 = c.y, first = c.z, np = c.w;
+    InvScale qs{0.0, 0.0f, 0.0f};
+    if (outq) qs = make_inv_scale(static_cast<double>(__ldg(qscale)));
+    float am = 0.0f;
+    for (int idx = threadIdx.x; idx < AQ * HD; idx += ATHREADS) {
+        const int r = idx / HD, col = idx % HD;
+        const int t = q0 + r;
+        if (t >= s1) continue;
+        float m = -INFINITY;
+        for (int k = 0; k < np; k++) m = fmaxf(m, part_ml[(static_cast<int64_t>(first + k) * nheads + head) * AQ + r].x);
+        float l = 0.0f, acc = 0.0f;
+        for (int k = 0; k < np; k++) {
+            const int64_t slot = static_cast<int64_t>(first + k) * nheads + head;
+            const float2 ml = part_ml[slot * AQ + r];
+            const float w = (ml.x == -INFINITY) ? 0.0f : exp2f(ml.x - m);
+            l = fmaf(ml.y, w, l);
+            acc = fmaf(part_o[(slot * AQ + r) * HD + col], w, acc);
+        }
+        const float v = acc / l;
+        const int64_t o = static_cast<int64_t>(t) * d + head * HD + col;
+        if (out) out[o] = v;
+        if (outq) outq[o] = quant_exact(v, qs);
+        am = fmaxf(am, fabsf(v));
+    }
+    if (amax) {
+        am = warp_max_f(am);
+        if ((threadIdx.x & 31) == 0) atomicMax(amax, __float_as_uint(am));
+    }
+}
+
+template <int HD>
+static int launch_attention_hd(const float* qkv, const int4* tiles, const int4* split, int nitems, const int4* comb,
+                               int ncomb, int d, int nheads, float* out, int8_t* outq, const float* qscale,
+                               uint32_t* amax, float* part_o, float2* part_ml, cudaStream_t st) {
+    constexpr size_t smem = sizeof(float) * (3 * AQ * (HD + APAD) + AQ * (AK + APAD));
     static bool attr[64] = {false};
     int dev = 0;
     TVQ_CUDA(cudaGetDevice(&dev));
@@ -357,27 +597,41 @@ static int launch_attention_hd(const float* qkv, const int4* tiles, int ntiles, 
                                       static_cast<int>(smem)));
         attr[dev] = true;
     }
-    const float sm_scale = static_cast<float>(1.0 / sqrt(static_cast<double>(HD)));
-    attention_kernel<HD><<<ntiles * nheads, 256, smem, st>>>(qkv, tiles, ntiles, T, d, nheads, sm_scale, out, outq,
-                                                             qscale, amax);
+    // softmax in base 2: scores scaled by log2(e)/sqrt(hd) through Q
+    const float q_scale = static_cast<float>(1.4426950408889634 / sqrt(static_cast<double>(HD)));
+    attention_kernel<HD><<<nitems * nheads, ATHREADS, smem, st>>>(qkv, tiles, split, d, nheads, q_scale, out, outq,
+                                                                  qscale, amax, part_o, part_ml);
     TVQ_CUDA(cudaGetLastError());
+    if (ncomb > 0) {
+        attention_combine_kernel<HD><<<ncomb * nheads, ATHREADS, 0, st>>>(comb, d, nheads, part_o, part_ml, out,
+                                                                         outq, qscale, amax);
+        TVQ_CUDA(cudaGetLastError());
+    }
     return TVQ_OK;
 }
 
-int launch_attention(const float* qkv, const int4* tiles, int ntiles, int T, int d, int nheads, float* out,
-                     int8_t* outq, const float* qscale, uint32_t* amax, cudaStream_t st) {
-    if (ntiles <= 0) return TVQ_OK;
+int launch_attention_split(const float* qkv, const int4* tiles, const int4* split, int nitems, const int4* comb,
+                           int ncomb, int d, int nheads, float* out, int8_t* outq, const float* qscale,
+                           uint32_t* amax, float* part_o, float2* part_ml, cudaStream_t st) {
+    if (nitems <= 0) return TVQ_OK;
     TVQ_CHECK(nheads > 0 && d % nheads == 0, TVQ_ERR_INVALID, "d must be a multiple of the head count");
     const int hd = d / nheads;
     switch (hd) {
-        case 16: return launch_attention_hd<16>(qkv, tiles, ntiles, T, d, nheads, out, outq, qscale, amax, st);
-        case 32: return launch_attention_hd<32>(qkv, tiles, ntiles, T, d, nheads, out, outq, qscale, amax, st);
-        case 48: return launch_attention_hd<48>(qkv, tiles, ntiles, T, d, nheads, out, outq, qscale, amax, st);
-        case 64: return launch_attention_hd<64>(qkv, tiles, ntiles, T, d, nheads, out, outq, qscale, amax, st);
+        case 16: return launch_attention_hd<16>(qkv, tiles, split, nitems, comb, ncomb, d, nheads, out, outq, qscale, amax, part_o, part_ml, st);
+        case 32: return launch_attention_hd<32>(qkv, tiles, split, nitems, comb, ncomb, d, nheads, out, outq, qscale, amax, part_o, part_ml, st);
+        case 48: return launch_attention_hd<48>(qkv, tiles, split, nitems, comb, ncomb, d, nheads, out, outq, qscale, amax, part_o, part_ml, st);
+        case 64: return launch_attention_hd<64>(qkv, tiles, split, nitems, comb, ncomb, d, nheads, out, outq, qscale, amax, part_o, part_ml, st);
         default:
             set_error(TVQ_ERR_UNSUPPORTED, "head dim must be 16, 32, 48 or 64");
             return TVQ_ERR_UNSUPPORTED;
     }
+}
+
+int launch_attention(const float* qkv, const int4* tiles, int ntiles, int T, int d, int nheads, float* out,
+                     int8_t* outq, const float* qscale, uint32_t* amax, cudaStream_t st) {
+    (void)T;
+    return launch_attention_split(qkv, tiles, nullptr, ntiles, nullptr, 0, d, nheads, out, outq, qscale, amax, nullptr,
+                                  nullptr, st);
 }
 
 // ------------------------------------------------------------------ scales

@@ -14,6 +14,12 @@ int launch_layernorm(const float* x, const float* g, const float* b, float* y, i
 // tiles: int4 {q0, seg_start, seg_end, 0} per 64-row query tile
 int launch_attention(const float* qkv, const int4* tiles, int ntiles, int T, int d, int nheads, float* out,
                      int8_t* outq, const float* qscale, uint32_t* amax, cudaStream_t st);
+// split-KV form: split[i] = {key begin, key end, partial slot or -1, 0} per
+// item; comb[e] = {q0, seq end, first partial slot, count} merges partials
+// (part_o: slots x heads x 64 x hd floats, part_ml: slots x heads x 64).
+int launch_attention_split(const float* qkv, const int4* tiles, const int4* split, int nitems, const int4* comb,
+                           int ncomb, int d, int nheads, float* out, int8_t* outq, const float* qscale,
+                           uint32_t* amax, float* part_o, float2* part_ml, cudaStream_t st);
 int launch_scale_from_amax(const uint32_t* amax, float* scale, int n, cudaStream_t st);
 int launch_transpose(const float* a, float* b, int rows, int cols, cudaStream_t st);
 int launch_token_seg(const int* seg, int nseg, int* tok_start, cudaStream_t st);

@@ -27,12 +27,14 @@ float e4m3_decode_host(uint32_t v);
 uint8_t e4m3_encode_host(float x);
 
 // tvq_gemm.cu
-enum GemmKind { GEMM_I8 = 0, GEMM_F8 = 1 };
+enum GemmKind { GEMM_I8 = 0, GEMM_F8 = 1, GEMM_TF32X3 = 2 };
 
 struct GemmArgs {
     int kind = GEMM_I8;
     const void* A = nullptr;          // [m,k] 8-bit, row-major
     const void* W = nullptr;          // [n,k] 8-bit, row-major
+    const void* A2 = nullptr;         // GEMM_TF32X3: low parts of A and W (A, W hold the high parts, f32)
+    const void* W2 = nullptr;
     const float* bias = nullptr;      // [n] or null
     const float* residual = nullptr;  // [m,n] or null
     float* Y = nullptr;               // [m,n] or null
@@ -48,5 +50,7 @@ struct GemmArgs {
     int force_bn = 0;                 // 0 = heuristic, else 64/128/256
 };
 int launch_gemm(const GemmArgs& g, cudaStream_t st);
+// x = hi + lo with hi rounded to TF32 precision (10 explicit mantissa bits)
+int launch_split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStream_t st);
 
 }  // namespace tvq

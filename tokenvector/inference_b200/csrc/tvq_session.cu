@@ -14,9 +14,8 @@
 // calibrate_minmax would (tv/quantization/engine.tkv:13-36: scale =
 // fl32(max(max|x|, 1e-8) / 127)), with the running max over calibration
 // batches, and quantizes each activation with its own scale as it goes.
-#include <cublas_v2.h>
-
 #include <algorithm>
+#include <cstdlib>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -45,19 +44,25 @@ struct LayerW {
 struct Session {
     int device = 0;
     cudaStream_t st = nullptr;
-    cublasHandle_t blas = nullptr;
-    void* blas_ws = nullptr;
     int vocab = 0, d = 0, heads = 0, layers = 0, ffn = 0, max_pos = 0, max_tokens = 0;
     double eps = 1e-6;
     std::vector<void*> allocs;
     float *wte = nullptr, *wpe = nullptr, *lnf_g = nullptr, *lnf_b = nullptr;
+    float *wte_hi = nullptr, *wte_lo = nullptr;  // LM head operand split (high + low parts)
+    float *xf_hi = nullptr, *xf_lo = nullptr;
     std::vector<LayerW> L;
     float* act_scale = nullptr;
     uint32_t* act_amax = nullptr;
     int64_t* ids = nullptr;
     int* seg = nullptr;
     int* tok_start = nullptr;
-    int4* tiles = nullptr;
+    int4* tiles = nullptr;   // attention work items {q0, seq start, seq end, 0}
+    int4* split = nullptr;   // {key begin, key end, partial slot, 0}
+    int4* comb = nullptr;    // partial merges {q0, seq end, first slot, count}
+    float* part_o = nullptr;
+    float2* part_ml = nullptr;
+    size_t tiles_cap = 0, split_cap = 0, comb_cap = 0, part_o_cap = 0, part_ml_cap = 0;
+    int ncomb = 0;
     float *x = nullptr, *qkv = nullptr, *hf = nullptr, *xf = nullptr, *xf_last = nullptr, *logits = nullptr;
     size_t logits_cap = 0;
     int8_t *aq = nullptr, *hq = nullptr;
@@ -78,7 +83,6 @@ struct Session {
     ~Session() {
         if (gexec) cudaGraphExecDestroy(gexec);
         for (cudaEvent_t e : ev) cudaEventDestroy(e);
-        if (blas) cublasDestroy(blas);
         for (void* p : allocs) cudaFree(p);
         if (st) cudaStreamDestroy(st);
     }
@@ -199,11 +203,13 @@ int enqueue_forward(Session& s, bool calibrating) {
         STEP(mark(s, ST_GEMM_QKV));
         // causal attention -> int8 context (attn c_proj input)
         if (calibrating) {
-            STEP(launch_attention(s.qkv, s.tiles, s.ntiles, T, d, s.heads, s.hf, nullptr, nullptr, am + 1, s.st));
+            STEP(launch_attention_split(s.qkv, s.tiles, s.split, s.ntiles, s.comb, s.ncomb, d, s.heads, s.hf, nullptr,
+                                        nullptr, am + 1, s.part_o, s.part_ml, s.st));
             STEP(launch_scale_from_amax(am + 1, sc + 1, 1, s.st));
             STEP(launch_quantize_i8(s.hf, s.aq, static_cast<int64_t>(T) * d, sc + 1, s.st));
         } else {
-            STEP(launch_attention(s.qkv, s.tiles, s.ntiles, T, d, s.heads, nullptr, s.aq, sc + 1, nullptr, s.st));
+            STEP(launch_attention_split(s.qkv, s.tiles, s.split, s.ntiles, s.comb, s.ncomb, d, s.heads, nullptr, s.aq,
+                                        sc + 1, nullptr, s.part_o, s.part_ml, s.st));
         }
         STEP(mark(s, ST_ATTN));
         // attn c_proj + residual, in place on x
@@ -241,12 +247,21 @@ int enqueue_forward(Session& s, bool calibrating) {
         xin = s.xf_last;
         rows = s.nseg;
     }
-    const float one = 1.0f, zero = 0.0f;
-    cublasStatus_t bs = cublasSgemm(s.blas, CUBLAS_OP_T, CUBLAS_OP_N, s.vocab, rows, d, &one, s.wte, d, xin, d, &zero,
-                                    s.logits, s.vocab);
-    if (bs != CUBLAS_STATUS_SUCCESS) {
-        set_error(TVQ_ERR_CUDA, "cublasSgemm failed (status " + std::to_string(static_cast<int>(bs)) + ")");
-        return TVQ_ERR_CUDA;
+    // tied LM head, fp32 on the tensor cores with split precision
+    STEP(launch_split_tf32(xin, s.xf_hi, s.xf_lo, static_cast<int64_t>(rows) * d, s.st));
+    {
+        GemmArgs g;
+        g.kind = GEMM_TF32X3;
+        g.A = s.xf_hi;
+        g.A2 = s.xf_lo;
+        g.W = s.wte_hi;
+        g.W2 = s.wte_lo;
+        g.Y = s.logits;
+        g.m = rows;
+        g.n = s.vocab;
+        g.k = d;
+        g.per_channel = 0;
+        STEP(launch_gemm(g, s.st));
     }
     STEP(mark(s, ST_LM_HEAD));
     TVQ_CUDA(cudaGetLastError());
@@ -338,16 +353,8 @@ int tvq_session_create(int device, int64_t vocab, int64_t d_model, int64_t n_hea
         s->eps = ln_eps;
         s->L.resize(static_cast<size_t>(n_layers));
         TVQ_CUDA(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
-        if (cublasCreate(&s->blas) != CUBLAS_STATUS_SUCCESS) {
-            set_error(TVQ_ERR_CUDA, "cublasCreate failed");
-            return TVQ_ERR_CUDA;
-        }
-        cublasSetStream(s->blas, s->st);
-        cublasSetMathMode(s->blas, CUBLAS_PEDANTIC_MATH);  // true fp32: no TF32 anywhere
         const size_t MT = static_cast<size_t>(max_tokens), D = static_cast<size_t>(d_model);
         const size_t F = static_cast<size_t>(d_ffn);
-        STEP(s->alloc(&s->blas_ws, 32u << 20));
-        cublasSetWorkspace(s->blas, s->blas_ws, 32u << 20);
         STEP(s->alloc(&s->act_scale, static_cast<size_t>(4 * std::max<int64_t>(n_layers, 1))));
         STEP(s->alloc(&s->act_amax, static_cast<size_t>(4 * std::max<int64_t>(n_layers, 1))));
         TVQ_CUDA(cudaMemset(s->act_amax, 0, sizeof(uint32_t) * 4 * std::max<int64_t>(n_layers, 1)));
@@ -355,12 +362,13 @@ int tvq_session_create(int device, int64_t vocab, int64_t d_model, int64_t n_hea
         STEP(s->alloc(&s->ids, MT));
         STEP(s->alloc(&s->seg, MT + 1));
         STEP(s->alloc(&s->tok_start, MT));
-        STEP(s->alloc(&s->tiles, MT));
         STEP(s->alloc(&s->x, MT * D));
         STEP(s->alloc(&s->qkv, MT * 3 * D));
         STEP(s->alloc(&s->hf, MT * std::max(D, F)));
         STEP(s->alloc(&s->xf, MT * D));
         STEP(s->alloc(&s->xf_last, MT * D));
+        STEP(s->alloc(&s->xf_hi, MT * D));
+        STEP(s->alloc(&s->xf_lo, MT * D));
         STEP(s->alloc(&s->aq, MT * D));
         STEP(s->alloc(&s->hq, MT * F));
         STEP(s->alloc(&s->err, 1));
@@ -393,10 +401,15 @@ int tvq_session_destroy(int64_t handle) {
 int tvq_session_set_embeddings(int64_t handle, const float* wte, const float* wpe) {
     SESSION(handle)
     TVQ_CHECK(wte && wpe, TVQ_ERR_INVALID, "null buffer");
-    if (!S->wte) STEP(S->alloc(&S->wte, static_cast<size_t>(S->vocab) * S->d));
+    const size_t vd = static_cast<size_t>(S->vocab) * S->d;
+    if (!S->wte) STEP(S->alloc(&S->wte, vd));
+    if (!S->wte_hi) STEP(S->alloc(&S->wte_hi, vd));
+    if (!S->wte_lo) STEP(S->alloc(&S->wte_lo, vd));
     if (!S->wpe) STEP(S->alloc(&S->wpe, static_cast<size_t>(S->max_pos) * S->d));
-    TVQ_CUDA(cudaMemcpy(S->wte, wte, sizeof(float) * S->vocab * S->d, cudaMemcpyHostToDevice));
+    TVQ_CUDA(cudaMemcpy(S->wte, wte, sizeof(float) * vd, cudaMemcpyHostToDevice));
     TVQ_CUDA(cudaMemcpy(S->wpe, wpe, sizeof(float) * S->max_pos * S->d, cudaMemcpyHostToDevice));
+    STEP(launch_split_tf32(S->wte, S->wte_hi, S->wte_lo, static_cast<int64_t>(vd), S->st));
+    TVQ_CUDA(cudaStreamSynchronize(S->st));
     return TVQ_OK;
 }
 
@@ -515,24 +528,72 @@ int tvq_session_prepare(int64_t handle, const int64_t* seg, int64_t n_seg, int l
     TVQ_CHECK(T >= 1 && T <= S->max_tokens, TVQ_ERR_SIZE, "token count exceeds the session's max_tokens");
     std::vector<int> sh(static_cast<size_t>(n_seg) + 1);
     std::vector<int> tok(static_cast<size_t>(T));
-    std::vector<int4> tiles;
+    // attention work: one item per 64-row query tile, or, when its causal key
+    // range is longer than kKeyChunk, one item per key chunk plus a merge
+    // TVQ_ATTN_KEY_CHUNK overrides the chunk (keys, multiple of 64; 0 = never split)
+    int kKeyChunk = 256;
+    if (const char* env = getenv("TVQ_ATTN_KEY_CHUNK")) {
+        const int v = atoi(env);
+        kKeyChunk = v <= 0 ? (1 << 30) : std::max(64, v / 64 * 64);
+    }
+    struct Item { int4 tile, split; int work; };
+    std::vector<Item> items;
+    std::vector<int4> comb;
+    int nparts = 0;
     for (int64_t s = 0; s < n_seg; s++) {
         const int64_t a = seg[s], b = seg[s + 1];
         TVQ_CHECK(b > a, TVQ_ERR_INVALID, "every sequence needs at least one token");
         TVQ_CHECK(b - a <= S->max_pos, TVQ_ERR_SIZE, "sequence longer than max_pos");
         for (int64_t t = a; t < b; t++) tok[t] = static_cast<int>(a);
-        for (int64_t q0 = a; q0 < b; q0 += 64)
-            tiles.push_back(make_int4(static_cast<int>(q0), static_cast<int>(a), static_cast<int>(b), 0));
+        for (int64_t q0 = a; q0 < b; q0 += 64) {
+            const int kend = static_cast<int>(std::min<int64_t>(q0 + 64, b));
+            const int len = kend - static_cast<int>(a);
+            const int4 tile = make_int4(static_cast<int>(q0), static_cast<int>(a), static_cast<int>(b), 0);
+            if (len <= kKeyChunk) {
+                items.push_back({tile, make_int4(static_cast<int>(a), kend, -1, 0), len});
+            } else {
+                const int first = nparts;
+                int nch = 0;
+                for (int kb = static_cast<int>(a); kb < kend; kb += kKeyChunk, nch++)
+                    items.push_back({tile, make_int4(kb, std::min(kb + kKeyChunk, kend), nparts++, 0),
+                                     std::min(kKeyChunk, kend - kb)});
+                comb.push_back(make_int4(static_cast<int>(q0), static_cast<int>(b), first, nch));
+            }
+        }
         sh[s] = static_cast<int>(a);
     }
     sh[n_seg] = static_cast<int>(T);
     // longest causal work first
-    std::stable_sort(tiles.begin(), tiles.end(), [](const int4& u, const int4& v) { return (u.x - u.y) > (v.x - v.y); });
-    TVQ_CHECK(tiles.size() <= static_cast<size_t>(S->max_tokens), TVQ_ERR_SIZE, "too many attention tiles");
+    std::stable_sort(items.begin(), items.end(), [](const Item& u, const Item& v) { return u.work > v.work; });
+    std::vector<int4> tiles(items.size()), splits(items.size());
+    for (size_t i = 0; i < items.size(); i++) {
+        tiles[i] = items[i].tile;
+        splits[i] = items[i].split;
+    }
     TVQ_CUDA(cudaStreamSynchronize(S->st));
+    auto grow = [&](auto** ptr, size_t& cap, size_t want) -> int {
+        if (want <= cap) return TVQ_OK;
+        if (*ptr) {
+            cudaFree(*ptr);
+            S->allocs.erase(std::remove(S->allocs.begin(), S->allocs.end(), static_cast<void*>(*ptr)), S->allocs.end());
+            *ptr = nullptr;
+        }
+        int r = S->alloc(ptr, want);
+        if (!r) cap = want;
+        return r;
+    };
+    STEP(grow(&S->tiles, S->tiles_cap, items.size()));
+    STEP(grow(&S->split, S->split_cap, items.size()));
+    STEP(grow(&S->comb, S->comb_cap, std::max<size_t>(comb.size(), 1)));
+    const size_t slots = static_cast<size_t>(std::max(nparts, 1)) * S->heads * 64;
+    STEP(grow(&S->part_o, S->part_o_cap, slots * (S->d / S->heads)));
+    STEP(grow(&S->part_ml, S->part_ml_cap, slots));
     TVQ_CUDA(cudaMemcpy(S->seg, sh.data(), sizeof(int) * sh.size(), cudaMemcpyHostToDevice));
     TVQ_CUDA(cudaMemcpy(S->tok_start, tok.data(), sizeof(int) * tok.size(), cudaMemcpyHostToDevice));
     TVQ_CUDA(cudaMemcpy(S->tiles, tiles.data(), sizeof(int4) * tiles.size(), cudaMemcpyHostToDevice));
+    TVQ_CUDA(cudaMemcpy(S->split, splits.data(), sizeof(int4) * splits.size(), cudaMemcpyHostToDevice));
+    if (!comb.empty()) TVQ_CUDA(cudaMemcpy(S->comb, comb.data(), sizeof(int4) * comb.size(), cudaMemcpyHostToDevice));
+    S->ncomb = static_cast<int>(comb.size());
     S->T = static_cast<int>(T);
     S->nseg = static_cast<int>(n_seg);
     S->ntiles = static_cast<int>(tiles.size());
