@@ -201,8 +201,11 @@ TVQ_API int tvq_dev_layernorm(const float* x, const float* gamma, const float* b
 /* Causal multi-head attention of gpt2_attention (gpt2_ref.tkv:360-395, no
  * projection) over packed sequences seg[0..n_seg] (host offsets): qkv f32
  * [T, 3d] rows [Q|K|V]; out f32 [T, d] and/or outq int8 (scale qscale_dev).
- * tiles_dev: device scratch of 4 x int32 per 64-row query tile, 16-byte
- * aligned, tiles_cap tiles.  fp32 arithmetic: within 1e-5 of the f64 oracle. */
+ * tiles_dev: device scratch of tiles_cap entries of 4 x int32, 16-byte
+ * aligned; a call needs one entry per 64-row query tile, or with head dim 64
+ * (tensor-core kernel, 3xTF32 products) two per 128-row tile -- at most
+ * ceil(len / 64) + 1 entries per sequence either way.  fp32-accurate: within
+ * 1e-4 relative / 2e-6 absolute of the f64 oracle. */
 TVQ_API int tvq_dev_attention(const float* qkv, const int64_t* seg, int64_t n_seg, int64_t d, int64_t n_heads,
                               int32_t* tiles_dev, int64_t tiles_cap, float* out, int8_t* outq,
                               const float* qscale_dev, uint32_t* amax_dev, void* stream);

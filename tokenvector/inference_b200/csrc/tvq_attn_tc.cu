@@ -1,0 +1,581 @@
+// tvq_attn_tc.cu -- causal attention over packed sequences on the
+// 5th-generation tensor cores, head dim 64.
+//
+// gpt2_attention, tv/training/gpt2_ref.tkv:360-395 (scores q.k / sqrt(hd),
+// causal softmax, context = P V), per head, token t of the sequence [s0, s1)
+// attending to u in [s0, t].  qkv rows are [Q | K | V] with heads contiguous.
+//
+// fp32 accuracy on TF32 tensor cores: every operand x is split into
+// hi = tf32(x) and lo = tf32(x - hi), and each product is formed as
+// xl*yh + xh*yl + xh*yh (the "3xTF32" scheme).  The scores of one 64-key
+// block and the P*V partial of one 64-key block are each summed in TMEM over
+// K = 64 only; the running output is kept in registers with IEEE adds (the
+// tensor core's own accumulation is less exact than IEEE fp32 over long
+// sums).
+//
+// Operands: split_kv writes K as hi/lo f32 arrays [T, d] and V transposed,
+// V^T hi/lo [d, Tp] (keys contiguous, Tp = T rounded up to 4); the attention
+// kernel brings 64-key blocks of them into two 2-stage shared-memory rings
+// (K, V^T) with TMA, both as K-major B operands (of S = Q K^T and of P V).
+// Q (hi/lo) sits in shared memory as the A operand of S; P (hi/lo) is
+// written to tensor memory, double-buffered, as the A operand of P V, so the
+// softmax of block j never waits for P V of block j-1.
+//
+// One CTA = one (128-query tile, head, key range) work item; 384 threads:
+//   warp 0      TMA producer (K/V blocks)
+//   warp 1      MMA issuer: S_j = Q K_j^T into TMEM S[j&1] (M 128, N 64,
+//               K 64), then PV_{j-1} = P_{j-1} V_{j-1} into TMEM O[(j-1)&1]
+//   warp 2      TMEM allocator (all 512 columns)
+//   warps 4-11  softmax, two warps per TMEM lane group (32 query rows), one
+//               per 32-key half of each block: Q to shared memory once, then
+//               per block the row max exchanged between the pair through
+//               shared memory, online softmax in base 2, P (hi/lo) to TMEM,
+//               and the previous PV partial folded into the register
+//               accumulator (each warp owns 32 of the 64 output columns)
+// Every wait is a bounded mbarrier wait; on a timeout the kernel records an
+// error, drains its MMAs and TMA loads, frees TMEM and returns.
+//
+// Work items are those of the fp32 kernel (tvq_glue.cu) with 128-row query
+// tiles: tiles[i] = {q0, s0, s1, 0}, split[i] = {key begin, key end, partial
+// slot or -1, 0}; a partial (unnormalised O, m, l) is merged by
+// attention_combine_kernel.
+#include <algorithm>
+
+#include "tvq_common.cuh"
+#include "tvq_exact.cuh"
+#include "tvq_glue.h"
+#include "tvq_kernels.h"
+
+namespace tvq {
+
+namespace {
+
+constexpr int TQ = 128;  // query rows per CTA (TMEM lanes, MMA M)
+constexpr int TK = 64;   // keys per block
+constexpr int HD = 64;   // head dim
+constexpr int NTHREADS = 384;
+
+// shared memory (1024-byte aligned regions):
+//   Q hi, Q lo      128 rows x 64 head columns: two 16 KB K-blocks of 128-byte rows
+//   K ring [2]      per stage K hi, K lo: two 8 KB halves (head columns 32h..) of 64 key rows
+//   V^T ring [2]    per stage V^T hi, V^T lo: two 8 KB halves (keys 32h.. of the block) of 64 head rows
+constexpr uint32_t HALF = TK * 128;                  // 8 KB
+constexpr uint32_t QPART = TQ * 128 * 2;             // 32 KB
+constexpr uint32_t OFF_QH = 0, OFF_QL = QPART;
+constexpr uint32_t KSTAGE = 4 * HALF;                // 32 KB: hi halves then lo halves
+constexpr uint32_t OFF_K = 2 * QPART;                // + s * KSTAGE
+constexpr uint32_t OFF_V = OFF_K + 2 * KSTAGE;       // + s * KSTAGE
+constexpr uint32_t OFF_RED = OFF_V + 2 * KSTAGE;     // float [2][2][128] row maxima
+constexpr uint32_t OFF_LSUM = OFF_RED + 2 * 2 * TQ * 4;  // float [2][128] row sums
+constexpr uint32_t OFF_BAR = OFF_LSUM + 2 * TQ * 4;
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 512 + 1024;
+
+// tensor memory columns: S[2], O[2] (64 each), P[2] (hi 64 + lo 64 each)
+constexpr uint32_t COL_S = 0, COL_O = 128, COL_P = 256;
+constexpr uint32_t TMEM_COLS = 512;
+
+// kind::tf32, D f32, A and B tf32 K-major, N = 64, M = 128 (both products)
+constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(64 >> 3) << 17) |
+                           (static_cast<uint32_t>(TQ >> 4) << 24);
+
+// device error codes: the wait that gave up first (tens digit: 3 TMA
+// producer, 4 MMA issuer, 5 softmax)
+enum : int {
+    DEVERR_ATTN_K_EMPTY = 31, DEVERR_ATTN_V_EMPTY = 32, DEVERR_ATTN_TMA_DRAIN = 33,
+    DEVERR_ATTN_Q_FULL = 41, DEVERR_ATTN_K_FULL = 42, DEVERR_ATTN_S_EMPTY = 43, DEVERR_ATTN_P_FULL = 44,
+    DEVERR_ATTN_O_EMPTY = 45, DEVERR_ATTN_V_FULL = 46, DEVERR_ATTN_MMA_DRAIN = 47,
+    DEVERR_ATTN_S_FULL = 51, DEVERR_ATTN_XCH = 52, DEVERR_ATTN_O_FULL = 53, DEVERR_ATTN_LXCH = 55
+};
+
+__device__ __forceinline__ float round_tf32_a(float v) {
+    // nearest TF32 value (10 explicit mantissa bits), ties away from zero
+    const uint32_t u = __float_as_uint(v);
+    if ((u & 0x7F800000u) == 0x7F800000u) return v;
+    float h = __uint_as_float((u + 0x1000u) & 0xFFFFE000u);
+    if ((__float_as_uint(h) & 0x7F800000u) == 0x7F800000u) h = __uint_as_float(u & 0xFFFFE000u);
+    return h;
+}
+
+__device__ __forceinline__ void split1(float v, uint32_t& h, uint32_t& l) {
+    const float hf = round_tf32_a(v);
+    h = __float_as_uint(hf);
+    l = __float_as_uint(round_tf32_a(__fsub_rn(v, hf)));
+}
+
+__device__ __forceinline__ void split4(const float4 v, float4& h, float4& l) {
+    h.x = round_tf32_a(v.x); l.x = round_tf32_a(__fsub_rn(v.x, h.x));
+    h.y = round_tf32_a(v.y); l.y = round_tf32_a(__fsub_rn(v.y, h.y));
+    h.z = round_tf32_a(v.z); l.z = round_tf32_a(__fsub_rn(v.z, h.z));
+    h.w = round_tf32_a(v.w); l.w = round_tf32_a(__fsub_rn(v.w, h.w));
+}
+
+// K part of qkv [T, 3d] -> hi / lo arrays [T, d]
+__global__ void split_k_kernel(const float* __restrict__ qkv, int T, int d, float* __restrict__ kh,
+                               float* __restrict__ kl) {
+    const int d4 = d >> 2;
+    const int64_t n = static_cast<int64_t>(T) * d4;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / d4;
+        const int c4 = static_cast<int>(i - t * d4);
+        float4 h, l;
+        split4(__ldg(reinterpret_cast<const float4*>(qkv + t * 3 * d) + d4 + c4), h, l);
+        reinterpret_cast<float4*>(kh)[i] = h;
+        reinterpret_cast<float4*>(kl)[i] = l;
+    }
+}
+
+// V part of qkv [T, 3d] -> V^T hi / lo [d, Tp]: 32 x 32 tiles through
+// shared memory (coalesced on both sides); keys T..Tp-1 are written as 0.
+__global__ void split_vt_kernel(const float* __restrict__ qkv, int T, int Tp, int d, float* __restrict__ vth,
+                                float* __restrict__ vtl) {
+    __shared__ float tile[32][33];
+    const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int t = t0 + i;
+        tile[i][threadIdx.x] = (t < T) ? __ldg(qkv + static_cast<int64_t>(t) * 3 * d + 2 * d + c0 + threadIdx.x) : 0.0f;
+    }
+    __syncthreads();
+    const int t = t0 + threadIdx.x;
+    if (t >= Tp) return;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        uint32_t h, l;
+        split1(tile[threadIdx.x][i], h, l);
+        const int64_t o = static_cast<int64_t>(c0 + i) * Tp + t;
+        vth[o] = __uint_as_float(h);
+        vtl[o] = __uint_as_float(l);
+    }
+}
+
+struct AttnParams {
+    const float* qkv;
+    const int4* tiles;
+    const int4* split;
+    int d, nheads;
+    float scale2;  // log2(e) / sqrt(hd)
+    float* out;
+    int8_t* outq;
+    const float* qscale;
+    uint32_t* amax;
+    float* part_o;
+    float2* part_ml;
+    int* err;
+};
+
+// Byte offset of the 16-byte chunk (row r, chunk c of its 128-byte row) in
+// a tile of 128-byte rows with the 128-byte swizzle (chunk ^= row % 8).
+__device__ __forceinline__ uint32_t sw128(int r, int c) {
+    return static_cast<uint32_t>(r) * 128u + static_cast<uint32_t>((c ^ (r & 7)) << 4);
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
+                        const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl,
+                        const AttnParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* red = reinterpret_cast<float*>(sm + OFF_RED);    // [parity][half][row]
+    float* lsum = reinterpret_cast<float*>(sm + OFF_LSUM);  // [half][row]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+    uint64_t* k_full = bars;           // [2]
+    uint64_t* k_empty = bars + 2;      // [2]
+    uint64_t* v_full = bars + 4;       // [2]
+    uint64_t* v_empty = bars + 6;      // [2]
+    uint64_t* s_full = bars + 8;       // [2]
+    uint64_t* s_empty = bars + 10;     // [2]
+    uint64_t* p_full = bars + 12;      // [2]
+    uint64_t* o_full = bars + 14;      // [2]
+    uint64_t* o_empty = bars + 16;     // [2]
+    uint64_t* q_full = bars + 18;
+    uint64_t* drain = bars + 19;
+    uint64_t* xch = bars + 20;         // [4 lane groups][2 parities]: row-max exchange
+    uint64_t* lxch = bars + 28;        // [4]: row-sum exchange
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 32);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int item = blockIdx.x / p.nheads;
+    const int head = blockIdx.x % p.nheads;
+    const int4 tl = p.tiles[item];
+    const int q0 = tl.x, s1 = tl.z;
+    const int4 sp = p.split[item];
+    const int kb = sp.x, ke = sp.y, part = sp.z;
+    // blocks start at kb rounded down to 4 keys (16 bytes, the TMA rule for
+    // the V^T key coordinate); keys below kb are masked
+    const int kb_al = kb & ~3;
+    const int nkb = (ke - kb_al + TK - 1) / TK;
+
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&k_full[b], 1);
+            mbar_init(&k_empty[b], 1);
+            mbar_init(&v_full[b], 1);
+            mbar_init(&v_empty[b], 1);
+            mbar_init(&s_full[b], 1);
+            mbar_init(&s_empty[b], 8);
+            mbar_init(&p_full[b], 8);
+            mbar_init(&o_full[b], 1);
+            mbar_init(&o_empty[b], 8);
+        }
+        mbar_init(q_full, 8);
+        mbar_init(drain, 1);
+        for (int i = 0; i < 8; i++) mbar_init(&xch[i], 2);
+        for (int i = 0; i < 4; i++) mbar_init(&lxch[i], 2);
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmKh);
+        tma_prefetch_desc(&tmKl);
+        tma_prefetch_desc(&tmVh);
+        tma_prefetch_desc(&tmVl);
+    }
+    if (warp == 2) {
+        tmem_alloc(tmem_holder, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int kissued = 0, vissued = 0;
+            for (int j = 0; j < nkb; j++) {
+                const int s = j & 1;
+                const uint32_t ph = ((j >> 1) & 1) ^ 1;
+                const int key = kb_al + j * TK;  // a multiple of 4
+                if (!mbar_wait(&k_empty[s], ph, p.err, DEVERR_ATTN_K_EMPTY)) break;
+                mbar_arrive_expect_tx(&k_full[s], KSTAGE);
+                uint8_t* ks = sm + OFF_K + s * KSTAGE;
+                tma_load_2d(&tmKh, &k_full[s], ks, head * HD, key);
+                tma_load_2d(&tmKh, &k_full[s], ks + HALF, head * HD + 32, key);
+                tma_load_2d(&tmKl, &k_full[s], ks + 2 * HALF, head * HD, key);
+                tma_load_2d(&tmKl, &k_full[s], ks + 3 * HALF, head * HD + 32, key);
+                kissued = j + 1;
+                if (!mbar_wait(&v_empty[s], ph, p.err, DEVERR_ATTN_V_EMPTY)) break;
+                mbar_arrive_expect_tx(&v_full[s], KSTAGE);
+                uint8_t* vs = sm + OFF_V + s * KSTAGE;
+                tma_load_2d(&tmVh, &v_full[s], vs, key, head * HD);
+                tma_load_2d(&tmVh, &v_full[s], vs + HALF, key + 32, head * HD);
+                tma_load_2d(&tmVl, &v_full[s], vs + 2 * HALF, key, head * HD);
+                tma_load_2d(&tmVl, &v_full[s], vs + 3 * HALF, key + 32, head * HD);
+                vissued = j + 1;
+            }
+            // every issued load lands before the CTA may exit
+            for (int j = kissued > 2 ? kissued - 2 : 0; j < kissued; j++)
+                mbar_wait(&k_full[j & 1], (j >> 1) & 1, p.err, DEVERR_ATTN_TMA_DRAIN);
+            for (int j = vissued > 2 ? vissued - 2 : 0; j < vissued; j++)
+                mbar_wait(&v_full[j & 1], (j >> 1) & 1, p.err, DEVERR_ATTN_TMA_DRAIN);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t sbase = smem_u32(sm);
+            bool ok = mbar_wait(q_full, 0, p.err, DEVERR_ATTN_Q_FULL);
+            auto issue_pv = [&](int i) -> bool {
+                const int b = i & 1;
+                const uint32_t ph = (i >> 1) & 1;
+                if (!mbar_wait(&p_full[b], ph, p.err, DEVERR_ATTN_P_FULL)) return false;
+                if (!mbar_wait(&o_empty[b], ph ^ 1, p.err, DEVERR_ATTN_O_EMPTY)) return false;
+                if (!mbar_wait(&v_full[b], ph, p.err, DEVERR_ATTN_V_FULL)) return false;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + COL_O + b * 64;
+                const uint32_t vb = sbase + OFF_V + b * KSTAGE;
+                const uint32_t pcol = tmem_base + COL_P + b * 128;
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++) {  // 8 keys (32 bytes of V^T rows) per instruction
+                        const uint64_t vh = smem_desc_k_sw128(vb + h * HALF + kk * 32);
+                        const uint64_t vl = smem_desc_k_sw128(vb + 2 * HALF + h * HALF + kk * 32);
+                        const uint32_t pc = 32 * h + 8 * kk;
+                        umma_tf32_ts(d_tmem, pcol + 64 + pc, vh, IDESC, (h | kk) ? 1u : 0u);
+                        umma_tf32_ts(d_tmem, pcol + pc, vl, IDESC, 1u);
+                        umma_tf32_ts(d_tmem, pcol + pc, vh, IDESC, 1u);
+                    }
+                }
+                umma_commit(&o_full[b]);   // PV_i in O[b]; P[b] free again
+                umma_commit(&v_empty[b]);
+                return true;
+            };
+            for (int j = 0; j < nkb && ok; j++) {
+                const int b = j & 1;
+                const uint32_t ph = (j >> 1) & 1;
+                if (!mbar_wait(&k_full[b], ph, p.err, DEVERR_ATTN_K_FULL)) { ok = false; break; }
+                if (!mbar_wait(&s_empty[b], ph ^ 1, p.err, DEVERR_ATTN_S_EMPTY)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + COL_S + b * 64;
+                const uint32_t kbs = sbase + OFF_K + b * KSTAGE;
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++) {  // 8 head columns (32 bytes) per instruction
+                        const uint64_t qh = smem_desc_k_sw128(sbase + OFF_QH + h * (TQ * 128) + kk * 32);
+                        const uint64_t ql = smem_desc_k_sw128(sbase + OFF_QL + h * (TQ * 128) + kk * 32);
+                        const uint64_t kh = smem_desc_k_sw128(kbs + h * HALF + kk * 32);
+                        const uint64_t kl = smem_desc_k_sw128(kbs + 2 * HALF + h * HALF + kk * 32);
+                        umma_tf32(d_tmem, ql, kh, IDESC, (h | kk) ? 1u : 0u);
+                        umma_tf32(d_tmem, qh, kl, IDESC, 1u);
+                        umma_tf32(d_tmem, qh, kh, IDESC, 1u);
+                    }
+                }
+                umma_commit(&s_full[b]);
+                umma_commit(&k_empty[b]);
+                if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+            }
+            if (ok) issue_pv(nkb - 1);
+            umma_commit(drain);
+            mbar_wait(drain, 0, p.err, DEVERR_ATTN_MMA_DRAIN);
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------ softmax
+        const int g = warp & 3;          // TMEM lane group
+        const int h = (warp - 4) >> 2;   // key half of each block, output half
+        const int r = 32 * g + lane;     // query row of the tile = TMEM lane
+        const int q = q0 + r;
+        const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(32 * g) << 16);
+        bool alive = true;
+        // Q (this row, head columns 32h..32h+31) -> hi / lo, K-major in shared memory
+        {
+            const float4* src = reinterpret_cast<const float4*>(p.qkv + static_cast<int64_t>(q) * 3 * p.d +
+                                                               head * HD + 32 * h);
+#pragma unroll
+            for (int c4 = 0; c4 < 8; c4++) {
+                const float4 v = (q < s1) ? __ldg(src + c4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                float4 vh, vl;
+                split4(v, vh, vl);
+                const uint32_t off = h * (TQ * 128) + sw128(r, c4);
+                *reinterpret_cast<float4*>(sm + OFF_QH + off) = vh;
+                *reinterpret_cast<float4*>(sm + OFF_QL + off) = vl;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(q_full);
+        }
+        float o[32];
+#pragma unroll
+        for (int c = 0; c < 32; c++) o[c] = 0.0f;
+        float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
+        for (int j = 0; j < nkb; j++) {
+            const int b = j & 1;
+            const uint32_t ph = (j >> 1) & 1;
+            bool got = mbar_wait(&s_full[b], ph, p.err, DEVERR_ATTN_S_FULL);
+            if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
+            tc_fence_after();
+            uint32_t sr[32];
+            tmem_ld32(lane_base + COL_S + b * 64 + 32 * h, sr);
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_empty[b]);
+            // causal + key-range mask, scale to base 2: key k0 + c is visible
+            // for lo <= c <= hi
+            const int k0 = kb_al + j * TK + 32 * h;
+            const int lo = kb - k0, hi = min(q, ke - 1) - k0;
+            float x[32];
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 32; c++) {
+                x[c] = (c >= lo && c <= hi) ? __fmul_rn(__uint_as_float(sr[c]), p.scale2) : -INFINITY;
+                mx = fmaxf(mx, x[c]);
+            }
+            // row max over both halves: exchange with the partner warp
+            red[(b * 2 + h) * TQ + r] = mx;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xch[g * 2 + b]);
+            got = mbar_wait(&xch[g * 2 + b], ph, p.err, DEVERR_ATTN_XCH);
+            if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
+            mx = fmaxf(mx, red[(b * 2 + (h ^ 1)) * TQ + r]);
+            const float mnew = fmaxf(m, mx);
+            const float mref = (mnew == -INFINITY) ? 0.0f : mnew;  // a row with no visible key yet stays empty
+            const float alpha = exp2f(m - mref);
+            // P_j = 2^(x - m) in [0, 1] as hi (nearest TF32) + lo (exact
+            // remainder, read by the tensor core to TF32 precision: |error|
+            // <= 2^-21 P) into P[b]; P[b] was last read by PV_{j-2}, whose
+            // completion the previous iteration already waited for
+            uint32_t phi[32], plo[32];
+            float sum = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 32; c++) {
+                const float e = exp2f(x[c] - mref);
+                sum += e;
+                const uint32_t hb = (__float_as_uint(e) + 0x1000u) & 0xFFFFE000u;
+                phi[c] = hb;
+                plo[c] = __float_as_uint(__fsub_rn(e, __uint_as_float(hb)));
+            }
+            tmem_st32(lane_base + COL_P + b * 128 + 32 * h, phi);
+            tmem_st32(lane_base + COL_P + b * 128 + 64 + 32 * h, plo);
+            l = fmaf(l, alpha, sum);
+            m = mnew;
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[b]);
+            // fold PV_{j-1} into the register accumulator
+            if (j >= 1) {
+                const int bp = (j - 1) & 1;
+                got = mbar_wait(&o_full[bp], ((j - 1) >> 1) & 1, p.err, DEVERR_ATTN_O_FULL);
+                if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
+                tc_fence_after();
+                uint32_t pv[32];
+                tmem_ld32(lane_base + COL_O + bp * 64 + 32 * h, pv);
+                tmem_ld_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&o_empty[bp]);
+#pragma unroll
+                for (int c = 0; c < 32; c++) o[c] = fmaf(o[c], alpha_prev, __uint_as_float(pv[c]));
+            }
+            alpha_prev = alpha;
+        }
+        if (alive) {
+            const int bp = (nkb - 1) & 1;
+            const bool got = mbar_wait(&o_full[bp], ((nkb - 1) >> 1) & 1, p.err, DEVERR_ATTN_O_FULL);
+            alive = __all_sync(0xffffffffu, got);
+            if (alive) {
+                tc_fence_after();
+                uint32_t pv[32];
+                tmem_ld32(lane_base + COL_O + bp * 64 + 32 * h, pv);
+                tmem_ld_wait();
+#pragma unroll
+                for (int c = 0; c < 32; c++) o[c] = fmaf(o[c], alpha_prev, __uint_as_float(pv[c]));
+            }
+        }
+        if (alive) {  // row sum over both halves
+            lsum[h * TQ + r] = l;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&lxch[g]);
+            const bool got = mbar_wait(&lxch[g], 0, p.err, DEVERR_ATTN_LXCH);
+            alive = __all_sync(0xffffffffu, got);
+            if (alive) l += lsum[(h ^ 1) * TQ + r];
+        }
+        if (alive) {
+            if (part >= 0) {  // unnormalised partial for the combine step
+                const int64_t slot = static_cast<int64_t>(part) * p.nheads + head;
+                float4* dst = reinterpret_cast<float4*>(p.part_o + (slot * TQ + r) * HD + 32 * h);
+#pragma unroll
+                for (int c4 = 0; c4 < 8; c4++)
+                    dst[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
+                if (h == 0) p.part_ml[slot * TQ + r] = make_float2(m, l);
+            } else {
+                float am = 0.0f;
+                if (q < s1) {
+                    const float il = 1.0f / l;
+                    const int64_t base = static_cast<int64_t>(q) * p.d + head * HD + 32 * h;
+#pragma unroll
+                    for (int c = 0; c < 32; c++) {
+                        o[c] = o[c] * il;
+                        am = fmaxf(am, fabsf(o[c]));
+                    }
+                    if (p.out) {
+                        float4* dst = reinterpret_cast<float4*>(p.out + base);
+#pragma unroll
+                        for (int c4 = 0; c4 < 8; c4++)
+                            dst[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
+                    }
+                    if (p.outq) {
+                        const InvScale qs = make_inv_scale(static_cast<double>(__ldg(p.qscale)));
+                        char4* dst = reinterpret_cast<char4*>(p.outq + base);
+#pragma unroll
+                        for (int c4 = 0; c4 < 8; c4++) {
+                            char4 v;
+                            v.x = quant_exact(o[4 * c4], qs);
+                            v.y = quant_exact(o[4 * c4 + 1], qs);
+                            v.z = quant_exact(o[4 * c4 + 2], qs);
+                            v.w = quant_exact(o[4 * c4 + 3], qs);
+                            dst[c4] = v;
+                        }
+                    }
+                }
+                if (p.amax) {
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+                    if (lane == 0) atomicMax(p.amax, __float_as_uint(am));
+                }
+            }
+        }
+    }
+
+    __syncwarp();  // lanes that skipped a single-thread role wait for it here
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+}  // namespace
+
+int attention_tc_rows() { return TQ; }
+
+int attention_tc_pitch(int T) { return (T + 3) & ~3; }
+
+int launch_split_kv(const float* qkv, int T, int d, float* kh, float* kl, float* vth, float* vtl, cudaStream_t st) {
+    if (T <= 0) return TVQ_OK;
+    TVQ_CHECK(d % 32 == 0, TVQ_ERR_UNSUPPORTED, "d must be a multiple of 32");
+    int rc = 0;
+    DeviceState* ds = device_state(&rc);
+    if (!ds) return rc;
+    const int64_t n = static_cast<int64_t>(T) * (d / 4);
+    const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, ds->sm_count * 8));
+    split_k_kernel<<<grid, 256, 0, st>>>(qkv, T, d, kh, kl);
+    TVQ_CUDA(cudaGetLastError());
+    const int Tp = attention_tc_pitch(T);
+    split_vt_kernel<<<dim3((Tp + 31) / 32, d / 32), dim3(32, 8), 0, st>>>(qkv, T, Tp, d, vth, vtl);
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
+}
+
+int launch_attention_tc(const float* qkv, const float* kh, const float* kl, const float* vth, const float* vtl, int T,
+                        const int4* tiles, const int4* split, int nitems, const int4* comb, int ncomb, int d,
+                        int nheads, float* out, int8_t* outq, const float* qscale, uint32_t* amax, float* part_o,
+                        float2* part_ml, cudaStream_t st) {
+    if (nitems <= 0) return TVQ_OK;
+    TVQ_CHECK(nheads > 0 && d == nheads * HD, TVQ_ERR_UNSUPPORTED, "the tensor-core attention needs head dim 64");
+    TVQ_CHECK(split && kh && kl && vth && vtl, TVQ_ERR_INVALID,
+              "the tensor-core attention needs key ranges and split K / V^T");
+    TVQ_CHECK((reinterpret_cast<uintptr_t>(qkv) & 15) == 0 && (!out || (reinterpret_cast<uintptr_t>(out) & 15) == 0) &&
+                  (!outq || (reinterpret_cast<uintptr_t>(outq) & 3) == 0),
+              TVQ_ERR_UNSUPPORTED, "attention buffers must be 16-byte aligned");
+    int rc = 0;
+    DeviceState* ds = device_state(&rc);
+    if (!ds) return rc;
+    TVQ_CHECK(ds->cc_major == 10, TVQ_ERR_UNSUPPORTED, "the tcgen05 attention needs an sm_100 device");
+    static bool attr[64] = {false};
+    int dev = 0;
+    TVQ_CUDA(cudaGetDevice(&dev));
+    if (dev < 64 && !attr[dev]) {
+        TVQ_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(SMEM_BYTES)));
+        attr[dev] = true;
+    }
+    CUtensorMap mkh, mkl, mvh, mvl;
+    rc = make_tma_f32_sw128(&mkh, kh, T, d, TK);
+    if (!rc) rc = make_tma_f32_sw128(&mkl, kl, T, d, TK);
+    if (!rc) rc = make_tma_f32_sw128(&mvh, vth, d, T, HD, attention_tc_pitch(T));
+    if (!rc) rc = make_tma_f32_sw128(&mvl, vtl, d, T, HD, attention_tc_pitch(T));
+    if (rc) return rc;
+    AttnParams p;
+    p.qkv = qkv;
+    p.tiles = tiles;
+    p.split = split;
+    p.d = d;
+    p.nheads = nheads;
+    p.scale2 = static_cast<float>(1.4426950408889634 / 8.0);  // log2(e) / sqrt(64)
+    p.out = out;
+    p.outq = outq;
+    p.qscale = qscale;
+    p.amax = amax;
+    p.part_o = part_o;
+    p.part_ml = part_ml;
+    p.err = ds->d_error;
+    attention_tc_kernel<<<nitems * nheads, NTHREADS, SMEM_BYTES, st>>>(mkh, mkl, mvh, mvl, p);
+    TVQ_CUDA(cudaGetLastError());
+    if (ncomb > 0) return launch_attention_combine(comb, ncomb, d, nheads, TQ, part_o, part_ml, out, outq, qscale,
+                                                   amax, st);
+    return TVQ_OK;
+}
+
+}  // namespace tvq

@@ -559,9 +559,9 @@ int get_encoder() {
 
 // 2-D K-major operand [rows, k] of 1-byte or 4-byte elements: box {128 bytes
 // of K, box_rows}, 128-byte swizzle.
-int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box_rows, int elem) {
+int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box_rows, int elem, int64_t pitch = 0) {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * elem};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch ? pitch : k) * elem};
     const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK / elem), static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = g_encode(map, elem == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
@@ -625,6 +625,15 @@ __global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict
 }
 
 }  // namespace
+
+int make_tma_f32_sw128(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int box_rows, int64_t pitch) {
+    int rc = get_encoder();
+    if (rc) return rc;
+    if (pitch == 0) pitch = cols;
+    TVQ_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && pitch % 4 == 0 && pitch >= cols, TVQ_ERR_UNSUPPORTED,
+              "TMA operand must be 16-byte aligned with a 16-byte row pitch");
+    return make_map(map, ptr, rows, cols, box_rows, 4, pitch);
+}
 
 int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     TVQ_CHECK(g.m >= 0 && g.n >= 0 && g.k >= 0, TVQ_ERR_INVALID, "negative GEMM size");

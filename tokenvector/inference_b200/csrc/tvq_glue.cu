@@ -544,43 +544,88 @@ __global__ void __launch_bounds__(ATHREADS)
     }
 }
 
-// Merge the key-chunk partials of one (query tile, head): m = max m_c,
-// l = sum l_c 2^(m_c - m), O = sum O_c 2^(m_c - m) / l.
-template <int HD>
-__global__ void __launch_bounds__(ATHREADS)
+// Merge the key-chunk partials of one (query tile of QR rows, head):
+// m = max m_c, l = sum l_c 2^(m_c - m), O = sum O_c 2^(m_c - m) / l.  Two
+// threads per row, each owning HD/2 output columns.
+template <int HD, int QR>
+__global__ void __launch_bounds__(QR * 2)
     attention_combine_kernel(const int4* __restrict__ comb, int d, int nheads, const float* __restrict__ part_o,
                              const float2* __restrict__ part_ml, float* __restrict__ out, int8_t* __restrict__ outq,
                              const float* __restrict__ qscale, uint32_t* __restrict__ amax) {
+    constexpr int HC = HD / 2;
     const int e = blockIdx.x / nheads;
     const int head = blockIdx.x % nheads;
     const int4 c = comb[e];  // {q0, seq end, first partial slot, number of partials}
     const int q0 = c.x, s1 = c.y, first = c.z, np = c.w;
-    InvScale qs{0.0, 0.0f, 0.0f};
-    if (outq) qs = make_inv_scale(static_cast<double>(__ldg(qscale)));
+    const int r = threadIdx.x >> 1, half = threadIdx.x & 1;
+    const int t = q0 + r;
     float am = 0.0f;
-    for (int idx = threadIdx.x; idx < AQ * HD; idx += ATHREADS) {
-        const int r = idx / HD, col = idx % HD;
-        const int t = q0 + r;
-        if (t >= s1) continue;
+    if (t < s1) {
         float m = -INFINITY;
-        for (int k = 0; k < np; k++) m = fmaxf(m, part_ml[(static_cast<int64_t>(first + k) * nheads + head) * AQ + r].x);
-        float l = 0.0f, acc = 0.0f;
+        for (int k = 0; k < np; k++)
+            m = fmaxf(m, part_ml[(static_cast<int64_t>(first + k) * nheads + head) * QR + r].x);
+        float l = 0.0f, acc[HC];
+#pragma unroll
+        for (int j = 0; j < HC; j++) acc[j] = 0.0f;
         for (int k = 0; k < np; k++) {
             const int64_t slot = static_cast<int64_t>(first + k) * nheads + head;
-            const float2 ml = part_ml[slot * AQ + r];
+            const float2 ml = part_ml[slot * QR + r];
             const float w = (ml.x == -INFINITY) ? 0.0f : exp2f(ml.x - m);
             l = fmaf(ml.y, w, l);
-            acc = fmaf(part_o[(slot * AQ + r) * HD + col], w, acc);
+            const float4* src = reinterpret_cast<const float4*>(part_o + (slot * QR + r) * HD + half * HC);
+#pragma unroll
+            for (int j = 0; j < HC / 4; j++) {
+                const float4 v = src[j];
+                acc[4 * j] = fmaf(v.x, w, acc[4 * j]);
+                acc[4 * j + 1] = fmaf(v.y, w, acc[4 * j + 1]);
+                acc[4 * j + 2] = fmaf(v.z, w, acc[4 * j + 2]);
+                acc[4 * j + 3] = fmaf(v.w, w, acc[4 * j + 3]);
+            }
         }
-        const float v = acc / l;
-        const int64_t o = static_cast<int64_t>(t) * d + head * HD + col;
-        if (out) out[o] = v;
-        if (outq) outq[o] = quant_exact(v, qs);
-        am = fmaxf(am, fabsf(v));
+        InvScale qs{0.0, 0.0f, 0.0f};
+        if (outq) qs = make_inv_scale(static_cast<double>(__ldg(qscale)));
+        const int64_t o = static_cast<int64_t>(t) * d + head * HD + half * HC;
+#pragma unroll
+        for (int j = 0; j < HC; j++) {
+            const float v = acc[j] / l;
+            if (out) out[o + j] = v;
+            if (outq) outq[o + j] = quant_exact(v, qs);
+            am = fmaxf(am, fabsf(v));
+        }
     }
     if (amax) {
         am = warp_max_f(am);
         if ((threadIdx.x & 31) == 0) atomicMax(amax, __float_as_uint(am));
+    }
+}
+
+template <int HD>
+static int launch_combine_hd(const int4* comb, int ncomb, int d, int nheads, int rows, const float* part_o,
+                             const float2* part_ml, float* out, int8_t* outq, const float* qscale, uint32_t* amax,
+                             cudaStream_t st) {
+    if (rows == 64)
+        attention_combine_kernel<HD, 64><<<ncomb * nheads, 128, 0, st>>>(comb, d, nheads, part_o, part_ml, out, outq,
+                                                                        qscale, amax);
+    else
+        attention_combine_kernel<HD, 128><<<ncomb * nheads, 256, 0, st>>>(comb, d, nheads, part_o, part_ml, out, outq,
+                                                                         qscale, amax);
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
+}
+
+int launch_attention_combine(const int4* comb, int ncomb, int d, int nheads, int rows, const float* part_o,
+                             const float2* part_ml, float* out, int8_t* outq, const float* qscale, uint32_t* amax,
+                             cudaStream_t st) {
+    if (ncomb <= 0) return TVQ_OK;
+    TVQ_CHECK(rows == 64 || rows == 128, TVQ_ERR_INVALID, "query tiles are 64 or 128 rows");
+    switch (d / nheads) {
+        case 16: return launch_combine_hd<16>(comb, ncomb, d, nheads, rows, part_o, part_ml, out, outq, qscale, amax, st);
+        case 32: return launch_combine_hd<32>(comb, ncomb, d, nheads, rows, part_o, part_ml, out, outq, qscale, amax, st);
+        case 48: return launch_combine_hd<48>(comb, ncomb, d, nheads, rows, part_o, part_ml, out, outq, qscale, amax, st);
+        case 64: return launch_combine_hd<64>(comb, ncomb, d, nheads, rows, part_o, part_ml, out, outq, qscale, amax, st);
+        default:
+            set_error(TVQ_ERR_UNSUPPORTED, "head dim must be 16, 32, 48 or 64");
+            return TVQ_ERR_UNSUPPORTED;
     }
 }
 
@@ -602,11 +647,8 @@ static int launch_attention_hd(const float* qkv, const int4* tiles, const int4* 
     attention_kernel<HD><<<nitems * nheads, ATHREADS, smem, st>>>(qkv, tiles, split, d, nheads, q_scale, out, outq,
                                                                   qscale, amax, part_o, part_ml);
     TVQ_CUDA(cudaGetLastError());
-    if (ncomb > 0) {
-        attention_combine_kernel<HD><<<ncomb * nheads, ATHREADS, 0, st>>>(comb, d, nheads, part_o, part_ml, out,
-                                                                         outq, qscale, amax);
-        TVQ_CUDA(cudaGetLastError());
-    }
+    if (ncomb > 0)
+        return launch_combine_hd<HD>(comb, ncomb, d, nheads, AQ, part_o, part_ml, out, outq, qscale, amax, st);
     return TVQ_OK;
 }
 

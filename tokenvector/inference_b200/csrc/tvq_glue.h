@@ -20,6 +20,21 @@ int launch_attention(const float* qkv, const int4* tiles, int ntiles, int T, int
 int launch_attention_split(const float* qkv, const int4* tiles, const int4* split, int nitems, const int4* comb,
                            int ncomb, int d, int nheads, float* out, int8_t* outq, const float* qscale,
                            uint32_t* amax, float* part_o, float2* part_ml, cudaStream_t st);
+int launch_attention_combine(const int4* comb, int ncomb, int d, int nheads, int rows, const float* part_o,
+                             const float2* part_ml, float* out, int8_t* outq, const float* qscale, uint32_t* amax,
+                             cudaStream_t st);
+// tvq_attn_tc.cu: head dim 64 on the tensor cores.  launch_split_kv writes
+// the K part of qkv as TF32 hi / lo arrays [T, d] (kh + kl = K to 2^-22) and
+// the V part transposed, V^T hi / lo [d, attention_tc_pitch(T)];
+// launch_attention_tc takes them with the same work items as above but
+// attention_tc_rows() (128) query rows per tile; split[] is required.
+int attention_tc_rows();
+int attention_tc_pitch(int T);
+int launch_split_kv(const float* qkv, int T, int d, float* kh, float* kl, float* vth, float* vtl, cudaStream_t st);
+int launch_attention_tc(const float* qkv, const float* kh, const float* kl, const float* vth, const float* vtl, int T,
+                        const int4* tiles, const int4* split, int nitems, const int4* comb, int ncomb, int d,
+                        int nheads, float* out, int8_t* outq, const float* qscale, uint32_t* amax, float* part_o,
+                        float2* part_ml, cudaStream_t st);
 int launch_scale_from_amax(const uint32_t* amax, float* scale, int n, cudaStream_t st);
 int launch_transpose(const float* a, float* b, int rows, int cols, cudaStream_t st);
 int launch_token_seg(const int* seg, int nseg, int* tok_start, cudaStream_t st);

@@ -2,6 +2,7 @@
 // C ABI; the exported surface is include/tvq.h).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -50,6 +51,11 @@ struct GemmArgs {
     int force_bn = 0;                 // 0 = heuristic, else 64/128/256
 };
 int launch_gemm(const GemmArgs& g, cudaStream_t st);
+// Tensor map of a row-major f32 matrix [rows, cols] (row pitch `pitch`
+// elements, 0 = cols): box of 32 columns (128 bytes) x box_rows rows,
+// 128-byte swizzle.
+int make_tma_f32_sw128(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int box_rows,
+                       int64_t pitch = 0);
 // x = hi + lo with hi rounded to TF32 precision (10 explicit mantissa bits)
 int launch_split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStream_t st);
 

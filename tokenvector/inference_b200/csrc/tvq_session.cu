@@ -63,6 +63,9 @@ struct Session {
     float2* part_ml = nullptr;
     size_t tiles_cap = 0, split_cap = 0, comb_cap = 0, part_o_cap = 0, part_ml_cap = 0;
     int ncomb = 0;
+    bool attn_tc = false;  // head dim 64: tensor-core attention, 128-row query tiles
+    int attn_rows = 64;
+    float *kh = nullptr, *kl = nullptr, *vh = nullptr, *vl = nullptr;  // split K and V^T (tensor-core attention)
     float *x = nullptr, *qkv = nullptr, *hf = nullptr, *xf = nullptr, *xf_last = nullptr, *logits = nullptr;
     size_t logits_cap = 0;
     int8_t *aq = nullptr, *hq = nullptr;
@@ -164,6 +167,16 @@ int gemm(Session& s, const int8_t* A, const Lin& l, const float* scale_a, float*
     return launch_gemm(g, s.st);
 }
 
+int attention(Session& s, float* out, int8_t* outq, const float* qscale, uint32_t* amax) {
+    if (s.attn_tc) {
+        STEP(launch_split_kv(s.qkv, s.T, s.d, s.kh, s.kl, s.vh, s.vl, s.st));
+        return launch_attention_tc(s.qkv, s.kh, s.kl, s.vh, s.vl, s.T, s.tiles, s.split, s.ntiles, s.comb, s.ncomb,
+                                   s.d, s.heads, out, outq, qscale, amax, s.part_o, s.part_ml, s.st);
+    }
+    return launch_attention_split(s.qkv, s.tiles, s.split, s.ntiles, s.comb, s.ncomb, s.d, s.heads, out, outq, qscale,
+                                  amax, s.part_o, s.part_ml, s.st);
+}
+
 // Stage ids reported by tvq_session_stage_times.
 enum Stage { ST_EMBED = 0, ST_LN = 1, ST_GEMM_QKV = 2, ST_ATTN = 3, ST_GEMM_PROJ = 4, ST_GEMM_FC = 5, ST_GEMM_MPROJ = 6,
              ST_LM_HEAD = 7, ST_COUNT = 8 };
@@ -203,13 +216,11 @@ int enqueue_forward(Session& s, bool calibrating) {
         STEP(mark(s, ST_GEMM_QKV));
         // causal attention -> int8 context (attn c_proj input)
         if (calibrating) {
-            STEP(launch_attention_split(s.qkv, s.tiles, s.split, s.ntiles, s.comb, s.ncomb, d, s.heads, s.hf, nullptr,
-                                        nullptr, am + 1, s.part_o, s.part_ml, s.st));
+            STEP(attention(s, s.hf, nullptr, nullptr, am + 1));
             STEP(launch_scale_from_amax(am + 1, sc + 1, 1, s.st));
             STEP(launch_quantize_i8(s.hf, s.aq, static_cast<int64_t>(T) * d, sc + 1, s.st));
         } else {
-            STEP(launch_attention_split(s.qkv, s.tiles, s.split, s.ntiles, s.comb, s.ncomb, d, s.heads, nullptr, s.aq,
-                                        sc + 1, nullptr, s.part_o, s.part_ml, s.st));
+            STEP(attention(s, nullptr, s.aq, sc + 1, nullptr));
         }
         STEP(mark(s, ST_ATTN));
         // attn c_proj + residual, in place on x
@@ -528,13 +539,19 @@ int tvq_session_prepare(int64_t handle, const int64_t* seg, int64_t n_seg, int l
     TVQ_CHECK(T >= 1 && T <= S->max_tokens, TVQ_ERR_SIZE, "token count exceeds the session's max_tokens");
     std::vector<int> sh(static_cast<size_t>(n_seg) + 1);
     std::vector<int> tok(static_cast<size_t>(T));
-    // attention work: one item per 64-row query tile, or, when its causal key
-    // range is longer than kKeyChunk, one item per key chunk plus a merge
-    // TVQ_ATTN_KEY_CHUNK overrides the chunk (keys, multiple of 64; 0 = never split)
+    // attention work: one item per query tile (128 rows on the tensor-core
+    // path, else 64), or, when its causal key range is longer than kKeyChunk,
+    // one item per key chunk plus a merge.  Chunks start at multiples of
+    // kKeyChunk (a multiple of the tile height) from the sequence start, so
+    // every row of a tile sees at least one key of every chunk.
+    // TVQ_ATTN_TC=0 selects the fp32 kernel; TVQ_ATTN_KEY_CHUNK overrides the
+    // chunk (keys, rounded to the tile height; 0 = never split).
+    const bool tc = S->heads > 0 && S->d / S->heads == 64 && !(getenv("TVQ_ATTN_TC") && atoi(getenv("TVQ_ATTN_TC")) == 0);
+    const int QT = tc ? attention_tc_rows() : 64;
     int kKeyChunk = 256;
     if (const char* env = getenv("TVQ_ATTN_KEY_CHUNK")) {
         const int v = atoi(env);
-        kKeyChunk = v <= 0 ? (1 << 30) : std::max(64, v / 64 * 64);
+        kKeyChunk = v <= 0 ? (1 << 30) : std::max(QT, v / QT * QT);
     }
     struct Item { int4 tile, split; int work; };
     std::vector<Item> items;
@@ -545,8 +562,8 @@ int tvq_session_prepare(int64_t handle, const int64_t* seg, int64_t n_seg, int l
         TVQ_CHECK(b > a, TVQ_ERR_INVALID, "every sequence needs at least one token");
         TVQ_CHECK(b - a <= S->max_pos, TVQ_ERR_SIZE, "sequence longer than max_pos");
         for (int64_t t = a; t < b; t++) tok[t] = static_cast<int>(a);
-        for (int64_t q0 = a; q0 < b; q0 += 64) {
-            const int kend = static_cast<int>(std::min<int64_t>(q0 + 64, b));
+        for (int64_t q0 = a; q0 < b; q0 += QT) {
+            const int kend = static_cast<int>(std::min<int64_t>(q0 + QT, b));
             const int len = kend - static_cast<int>(a);
             const int4 tile = make_int4(static_cast<int>(q0), static_cast<int>(a), static_cast<int>(b), 0);
             if (len <= kKeyChunk) {
@@ -585,7 +602,7 @@ int tvq_session_prepare(int64_t handle, const int64_t* seg, int64_t n_seg, int l
     STEP(grow(&S->tiles, S->tiles_cap, items.size()));
     STEP(grow(&S->split, S->split_cap, items.size()));
     STEP(grow(&S->comb, S->comb_cap, std::max<size_t>(comb.size(), 1)));
-    const size_t slots = static_cast<size_t>(std::max(nparts, 1)) * S->heads * 64;
+    const size_t slots = static_cast<size_t>(std::max(nparts, 1)) * S->heads * QT;
     STEP(grow(&S->part_o, S->part_o_cap, slots * (S->d / S->heads)));
     STEP(grow(&S->part_ml, S->part_ml_cap, slots));
     TVQ_CUDA(cudaMemcpy(S->seg, sh.data(), sizeof(int) * sh.size(), cudaMemcpyHostToDevice));
@@ -594,6 +611,15 @@ int tvq_session_prepare(int64_t handle, const int64_t* seg, int64_t n_seg, int l
     TVQ_CUDA(cudaMemcpy(S->split, splits.data(), sizeof(int4) * splits.size(), cudaMemcpyHostToDevice));
     if (!comb.empty()) TVQ_CUDA(cudaMemcpy(S->comb, comb.data(), sizeof(int4) * comb.size(), cudaMemcpyHostToDevice));
     S->ncomb = static_cast<int>(comb.size());
+    S->attn_tc = tc;
+    S->attn_rows = QT;
+    if (tc && !S->kh) {
+        const size_t n = static_cast<size_t>(attention_tc_pitch(S->max_tokens)) * S->d;
+        STEP(S->alloc(&S->kh, n));
+        STEP(S->alloc(&S->kl, n));
+        STEP(S->alloc(&S->vh, n));
+        STEP(S->alloc(&S->vl, n));
+    }
     S->T = static_cast<int>(T);
     S->nseg = static_cast<int>(n_seg);
     S->ntiles = static_cast<int>(tiles.size());
@@ -705,19 +731,42 @@ int tvq_dev_attention(const float* qkv, const int64_t* seg, int64_t n_seg, int64
     TVQ_CHECK((reinterpret_cast<uintptr_t>(tiles_dev32) & 15) == 0, TVQ_ERR_UNSUPPORTED, "tile buffer must be 16-byte aligned");
     TVQ_CHECK(qkv && seg && n_seg >= 1 && tiles_dev && (out || outq || amax_dev), TVQ_ERR_INVALID, "bad arguments");
     TVQ_CHECK(!outq || qscale_dev, TVQ_ERR_INVALID, "int8 output needs a scale");
-    std::vector<int4> tiles;
+    TVQ_CHECK(n_heads > 0 && d % n_heads == 0, TVQ_ERR_INVALID, "d must be a multiple of the head count");
+    // head dim 64: the tensor-core kernel, 128-row query tiles with their key
+    // ranges (two entries per tile); otherwise the fp32 kernel, 64-row tiles
+    const bool tc = d / n_heads == 64;
+    const int rows = tc ? attention_tc_rows() : 64;
+    std::vector<int4> tiles, keys;
     for (int64_t s = 0; s < n_seg; s++) {
         TVQ_CHECK(seg[s + 1] >= seg[s], TVQ_ERR_INVALID, "segments must be non-decreasing");
-        for (int64_t q0 = seg[s]; q0 < seg[s + 1]; q0 += 64)
+        for (int64_t q0 = seg[s]; q0 < seg[s + 1]; q0 += rows) {
             tiles.push_back(make_int4(static_cast<int>(q0), static_cast<int>(seg[s]), static_cast<int>(seg[s + 1]), 0));
+            keys.push_back(make_int4(static_cast<int>(seg[s]), static_cast<int>(std::min(q0 + rows, seg[s + 1])), -1, 0));
+        }
     }
-    TVQ_CHECK(static_cast<int64_t>(tiles.size()) <= tiles_cap, TVQ_ERR_SIZE, "tile buffer too small");
+    const int64_t n = static_cast<int64_t>(tiles.size());
+    TVQ_CHECK((tc ? 2 * n : n) <= tiles_cap, TVQ_ERR_SIZE, "tile buffer too small");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (!tiles.empty())
-        TVQ_CUDA(cudaMemcpyAsync(tiles_dev, tiles.data(), sizeof(int4) * tiles.size(), cudaMemcpyHostToDevice, st));
-    TVQ_CUDA(cudaStreamSynchronize(st));  // the host vector dies at return
-    return launch_attention(qkv, tiles_dev, static_cast<int>(tiles.size()), static_cast<int>(seg[n_seg]),
-                            static_cast<int>(d), static_cast<int>(n_heads), out, outq, qscale_dev, amax_dev, st);
+    if (n) TVQ_CUDA(cudaMemcpyAsync(tiles_dev, tiles.data(), sizeof(int4) * n, cudaMemcpyHostToDevice, st));
+    if (n && tc) TVQ_CUDA(cudaMemcpyAsync(tiles_dev + n, keys.data(), sizeof(int4) * n, cudaMemcpyHostToDevice, st));
+    TVQ_CUDA(cudaStreamSynchronize(st));  // the host vectors die at return
+    if (tc) {
+        // split K / V scratch, stream-ordered (freed when the kernel is done)
+        const int T = static_cast<int>(seg[n_seg]);
+        const size_t n4 = static_cast<size_t>(attention_tc_pitch(T)) * d;
+        float* kv = nullptr;
+        TVQ_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&kv), sizeof(float) * 4 * std::max<size_t>(n4, 4), st));
+        int r = launch_split_kv(qkv, T, static_cast<int>(d), kv, kv + n4, kv + 2 * n4, kv + 3 * n4, st);
+        if (!r)
+            r = launch_attention_tc(qkv, kv, kv + n4, kv + 2 * n4, kv + 3 * n4, T, tiles_dev, tiles_dev + n,
+                                    static_cast<int>(n), nullptr, 0, static_cast<int>(d), static_cast<int>(n_heads), out,
+                                    outq, qscale_dev, amax_dev, nullptr, nullptr, st);
+        cudaError_t e = cudaFreeAsync(kv, st);
+        if (!r && e != cudaSuccess) return cuda_fail(e, "cudaFreeAsync");
+        return r;
+    }
+    return launch_attention(qkv, tiles_dev, static_cast<int>(n), static_cast<int>(seg[n_seg]), static_cast<int>(d),
+                            static_cast<int>(n_heads), out, outq, qscale_dev, amax_dev, st);
 }
 
 }  // extern "C"
