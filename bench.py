@@ -65,6 +65,63 @@ def gemm_work(T=SEQ, d=768, ffn=3072):
     }
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one gemm_c_fc launch in
+# the forward, from ncu (profiles/gemm_i8_gpt2_124m.md)
+GEMM_CFC_TRAFFIC = 3256320
+
+
+def attention_roofline(per_stage_ms, bf16, src, n_layers, T=SEQ, hd=64, heads=12):
+    """Causal attention of one 1024-token sequence per layer: useful flops
+    4 T^2 hd heads / 2 (QK^T and PV over the causal half) against the dense
+    TF32 rate (half the measured bf16 rate).  The kernel issues three TF32
+    products per useful product (3xTF32 for fp32 accuracy), so frac <= 1/3
+    by construction; the stage time includes the K/V split and the merge."""
+    flops = 4.0 * T * T * hd * heads / 2
+    t = per_stage_ms / n_layers / 1000.0
+    achieved = flops / t / 1e12
+    peak = bf16 / 2.0
+    return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "traffic": None, "kernel": "attention_tc_kernel (+ split_k, split_vt, combine), per layer",
+            "peak_source": "dense TF32 = %s bf16 / 2" % src, "products_per_useful_product": 3}
+
+
+def gemm_large(torch, dev, stream, flush, n=8192, reps=10):
+    """INT8 GEMM n x n x n with the per-channel f32 epilogue: TOPS and the
+    fraction of the dense INT8 peak (2 x measured bf16).  Kernel time only
+    (CUDA events on the launching stream, L2 flushed before each launch)."""
+    import ctypes as C
+    from tokenvector.inference_b200 import _native as N
+    A = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev)
+    W = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev)
+    Y = torch.empty((n, n), dtype=torch.float32, device=dev)
+    bias = torch.randn(n, device=dev) * 0.02
+    sw = torch.rand(n, device=dev) * 1e-3
+    sa = torch.tensor([0.01], device=dev)
+    p = lambda t: C.c_void_p(t.data_ptr())
+    sp = C.c_void_p(stream.cuda_stream)
+
+    def fn():
+        N.call("tvq_dev_gemm", 0, p(A), p(W), p(bias), None, p(Y), None, n, n, n, p(sa), p(sw), 1, 0, None, None, sp)
+    for _ in range(3):
+        fn()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    tot = 0.0
+    for _ in range(reps):
+        flush.zero_()
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        e1.synchronize()
+        tot += e0.elapsed_time(e1)
+    t = tot / reps / 1000.0
+    _, bf16, src = peaks()
+    tops = 2.0 * n ** 3 / t / 1e12
+    del A, W, Y
+    return {"m": n, "n": n, "k": n, "us": t * 1e6, "tops": tops, "peak_tops": 2.0 * bf16,
+            "frac": tops / (2.0 * bf16), "peak_source": "2 x %s dense bf16" % src}
+
+
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -260,6 +317,12 @@ def run_ours(args, rank, world, local):
         for k, v in sess.stage_times().items():
             stage_ms[k] += v
     sess.set_profiling(False)
+    step_device()  # recapture without the stage events
+    torch.cuda.synchronize(dev)
+    n_launches = sess.launches()
+
+    # ---- the INT8 GEMM at the north-star size (M >= 4096): 8192^3, kernel only
+    big = gemm_large(torch, dev, stream, flush) if world == 1 else None
 
     # ---- end to end through the host-buffer API
     ids_pin = torch.from_numpy(ids).pin_memory()
@@ -318,7 +381,9 @@ def run_ours(args, rank, world, local):
         else:
             roof = {"bound": "tensor", "achieved": ops / t / 1e12, "peak": int8_peak, "unit": "TOPS"}
         roof["frac"] = roof["achieved"] / roof["peak"]
-        roof["traffic"] = None
+        # dram__bytes_read + dram__bytes_write of one c_fc launch inside the
+        # forward (ncu, profiles/gemm_i8_gpt2_124m.md); outputs stay in L2
+        roof["traffic"] = GEMM_CFC_TRAFFIC if dom == "gemm_c_fc" else None
         roof["kernel"] = "gemm_tc_kernel<I8> (%s, M=1024 N,K of the layer)" % dom
         roof["peak_source"] = ("%s HBM copy bandwidth; INT8 peak = 2 x %s dense bf16 (%.1f TFLOP/s)"
                                % (src, src, bf16))
@@ -338,7 +403,7 @@ def run_ours(args, rank, world, local):
                    "sample": "embedding + 1 of 12 blocks on 1024 tokens (%.2f s) + LM head on 32 of 1024 rows "
                              "(%.2f s), extrapolated to the full forward" % (detail["block_s"],
                                                                               detail["lm_head_32rows_s"])}
-        launches_per_step = 7 * cfg.n_layers + 4  # embed, 7 per block, ln_f, split, LM head GEMM
+        launches_per_step = n_launches  # kernel nodes of the captured forward graph
         out = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
@@ -350,6 +415,9 @@ def run_ours(args, rank, world, local):
                     "d2h_bytes_per_step": rows * V * 4 * world, "ms_per_step": e2e_ms / e2e_steps,
                     "wall_ms_per_step": 1000.0 * e2e_wall / e2e_steps, "logits_finite": dev_logits_ok},
             "roofline": roof,
+            "roofline_attention": attention_roofline(per_stage_ms=stage_ms["attention"] / prof_steps, bf16=bf16,
+                                                     src=src, n_layers=cfg.n_layers),
+            "gemm_large": big,
             "cpu_baseline": cpu,
             "gpu_launches": launches_per_step * args.steps,
             

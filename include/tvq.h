@@ -266,6 +266,10 @@ TVQ_API int tvq_session_calibrate(int64_t handle, const int64_t* ids, int ids_on
 TVQ_API int tvq_session_forward(int64_t handle, const int64_t* ids, int ids_on_device, float* logits,
                                 int64_t logits_len, int logits_on_device, void* stream);
 TVQ_API int tvq_session_logits(int64_t handle, float** logits_dev, int64_t* rows, int64_t* cols);
+/* Kernel launches of one forward for the prepared layout (kernel nodes of
+ * its captured CUDA graph; profiling event nodes excluded); needs a forward
+ * to have run since the last prepare / profiling change. */
+TVQ_API int tvq_session_launches(int64_t handle, int64_t* kernels);
 TVQ_API int tvq_session_sync(int64_t handle);
 /* Profiling: with enable = 1 the captured forward records a CUDA event after
  * every stage; tvq_session_stage_times then returns the last forward's time

@@ -192,3 +192,37 @@ def test_session_errors():
     s.close()
     with pytest.raises(N.TvqError):
         N.call("tvq_session_sync", s.handle if s.handle else 999999)
+
+
+def test_session_launch_count_and_both_attention_paths(monkeypatch):
+    """The captured forward's kernel count, and the fp32 SIMT attention path
+    (TVQ_ATTN_TC=0) against the same oracle as the tensor-core path."""
+    cfg = _small_cfg()
+    w = GPT2Weights.random(cfg, seed=5)
+    lengths = [201]
+    seg = segments_from_lengths(lengths)
+    T = int(seg[-1])
+    calib_ids, ids = _ids(T, cfg.vocab, 1), _ids(T, cfg.vocab, 2)
+    qw = OG.quantize_weights(w.layers)
+    cal = OG.Calibrator(cfg.n_layers)
+    OG.forward(w, calib_ids, seg, calibrator=cal, qweights=qw, n_heads=cfg.n_heads)
+    scales = cal.scales()
+    ref = OG.forward(w, ids, seg, scales=scales, qweights=qw, n_heads=cfg.n_heads)
+    s = GPT2Session(w, max_tokens=1024)
+    try:
+        # tensor-core path: embed; per layer LN, c_attn, split K, split V^T,
+        # attention, c_proj, LN, c_fc, mlp c_proj; ln_f, LM-head split, LM head
+        s.prepare(seg)
+        s.set_act_scales(scales)
+        got_tc = s.forward(ids)
+        assert s.launches() == 1 + 9 * cfg.n_layers + 3
+        monkeypatch.setenv("TVQ_ATTN_TC", "0")
+        s.prepare(seg)
+        got_simt = s.forward(ids)
+        assert s.launches() == 1 + 7 * cfg.n_layers + 3
+    finally:
+        s.close()
+    for got in (got_tc, got_simt):
+        diff = np.abs(got - ref)
+        rowmax = diff.max(axis=1)
+        assert diff.mean() < 2e-4 and (rowmax > 2e-3).mean() <= 0.02 and rowmax.max() < 5e-2

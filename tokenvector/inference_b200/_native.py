@@ -82,6 +82,7 @@ SIGNATURES = {
     "tvq_session_calibrate": (i32, [i64, P, i32, i32]),
     "tvq_session_forward": (i32, [i64, P, i32, P, i64, i32, P]),
     "tvq_session_logits": (i32, [i64, P, P, P]),
+    "tvq_session_launches": (i32, [i64, P]),
     "tvq_session_sync": (i32, [i64]),
     "tvq_session_set_profiling": (i32, [i64, i32]),
     "tvq_session_stage_times": (i32, [i64, P, i64]),

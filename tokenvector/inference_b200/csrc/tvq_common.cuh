@@ -268,6 +268,11 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
     return d;
 }
 
+// Bring the cache line holding `p` into L2 (no register result).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // Named barrier over a subset of warps.
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

@@ -120,8 +120,24 @@ struct EpiCtx {
 // `lane`: swizzled shared-memory transpose (float4 slot j of row r sits at
 // slot j ^ ((r >> 1) & 3), conflict-free both ways), then four lanes per
 // 64-byte row segment: residual add, f32 / int8 stores, running amax.
+// The residual segments (row0 + 8 it + lane / 4, n0 + 4 (lane % 4)) that
+// stage_and_store adds, loaded ahead so their latency overlaps the TMEM read
+// and the epilogue arithmetic (the residual may alias Y; each segment is read
+// here, before the same thread stores it).
+__device__ __forceinline__ void load_residual(const KParams& p, const EpiCtx& e, int lane, int row0, int n0,
+                                              float4 (&res)[4]) {
+#pragma unroll
+    for (int it = 0; it < 4; it++) {
+        const int row = row0 + it * 8 + (lane >> 2);
+        const int col = n0 + 4 * (lane & 3);
+        res[it] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (p.residual && e.vec_ok && row < p.m && col + 3 < p.n)
+            res[it] = *reinterpret_cast<const float4*>(p.residual + static_cast<int64_t>(row) * p.n + col);
+    }
+}
+
 __device__ __forceinline__ void stage_and_store(const KParams& p, const EpiCtx& e, float* stage, const float (&y)[CH],
-                                                int lane, int row0, int n0, float& amax) {
+                                                int lane, int row0, int n0, float& amax, const float4 (&res)[4]) {
 #pragma unroll
     for (int j = 0; j < CH / 4; j++)
         *reinterpret_cast<float4*>(&stage[lane * CH + 4 * (j ^ ((lane >> 1) & 3))]) =
@@ -138,8 +154,7 @@ __device__ __forceinline__ void stage_and_store(const KParams& p, const EpiCtx& 
         const int64_t off = static_cast<int64_t>(row) * p.n + col;
         if (e.vec_ok && col + 3 < p.n) {
             if (p.residual) {
-                // plain load: the residual may alias Y (in-place residual stream)
-                const float4 t = *reinterpret_cast<const float4*>(p.residual + off);
+                const float4 t = res[it];
                 v.x = __fadd_rn(v.x, t.x);
                 v.y = __fadd_rn(v.y, t.y);
                 v.z = __fadd_rn(v.z, t.z);
@@ -394,7 +409,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const int n0 = nb * BN + (half + 2 * i) * CH;
                     if (n0 >= p.n) break;  // warp-uniform
                     __syncwarp();           // the previous chunk's staging reads are done
-                    stage_and_store(p, ec, stage, acc[i], lane, row0, n0, amax);
+                    const float4 nores[4] = {};
+                    stage_and_store(p, ec, stage, acc[i], lane, row0, n0, amax, nores);
                 }
             }
         } else {
@@ -402,6 +418,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, tcount++) {
             const uint32_t b = tcount % C::NACC;
             const uint32_t aph = (tcount / C::NACC) & 1u;
+            {
+                // while the tile's MMAs run: pull this warp's residual rows and
+                // the tile's per-column scales / bias toward L2
+                const int mb = tile % p.num_m_blocks;
+                const int nb = tile / p.num_m_blocks;
+                const int row = mb * BM + eg * 32 + lane;
+                for (int c = half; c < BN / CH; c += 2) {
+                    const int n0 = nb * BN + c * CH;
+                    if (n0 >= p.n) break;
+                    if (p.residual && row < p.m) prefetch_l2(p.residual + static_cast<int64_t>(row) * p.n + n0);
+                    if (lane == 0 && per_channel) prefetch_l2(p.scales_w + n0);
+                    if (lane == 1 && bias_on) prefetch_l2(p.bias + n0);
+                }
+            }
             const bool got = mbar_wait(&tfull[b], aph, p.err, DEVERR_TIMEOUT_EPILOGUE);
             __syncwarp();
             if (!__all_sync(0xffffffffu, got)) break;
@@ -413,16 +443,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int c = half; c < BN / CH; c += 2) {
                 const int n0 = nb * BN + c * CH;
                 if (n0 >= p.n) break;  // warp-uniform
-                uint32_t r[CH];
-                __syncwarp();
-                tmem_ld16(lane_base + b * BN + c * CH, r);
-                tmem_ld_wait();
-                if (p.acc_out && row0 + lane < p.m) {
-                    int32_t* dst = p.acc_out + static_cast<int64_t>(row0 + lane) * p.n + n0;
-#pragma unroll
-                    for (int j = 0; j < CH; j++)
-                        if (n0 + j < p.n) dst[j] = static_cast<int32_t>(r[j]);
-                }
+                float4 res[4];
+                load_residual(p, ec, lane, row0, n0, res);
                 // per-column scale and bias (same addresses in every lane)
                 float swv[CH], bv[CH];
                 if (vec_cols && n0 + CH <= p.n) {
@@ -442,6 +464,16 @@ __global__ void __launch_bounds__(THREADS, 1)
                         swv[j] = per_channel ? __ldg(p.scales_w + n) : sw0;
                         bv[j] = bias_on ? __ldg(p.bias + n) : 0.0f;
                     }
+                }
+                uint32_t r[CH];
+                __syncwarp();
+                tmem_ld16(lane_base + b * BN + c * CH, r);
+                tmem_ld_wait();
+                if (p.acc_out && row0 + lane < p.m) {
+                    int32_t* dst = p.acc_out + static_cast<int64_t>(row0 + lane) * p.n + n0;
+#pragma unroll
+                    for (int j = 0; j < CH; j++)
+                        if (n0 + j < p.n) dst[j] = static_cast<int32_t>(r[j]);
                 }
                 // fast path for all columns (straight-line), rare f64 fix-ups after
                 float y[CH];
@@ -487,7 +519,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < CH; j++) y[j] = y[j] > 0.0f ? y[j] : 0.0f;
                 }
-                stage_and_store(p, ec, stage, y, lane, row0, n0, amax);
+                stage_and_store(p, ec, stage, y, lane, row0, n0, amax, res);
             }
             tc_fence_before();
             __syncwarp();
@@ -698,6 +730,14 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
 
     // Tile width: the widest N tile that still gives every SM a tile.
     int bn = g.force_bn;
+    if (bn == 0) {  // TVQ_GEMM_BN=64|128|256 pins the tile width (tuning)
+        static const int env_bn = [] {
+            const char* e = getenv("TVQ_GEMM_BN");
+            const int v = e ? atoi(e) : 0;
+            return (v == 64 || v == 128 || v == 256) ? v : 0;
+        }();
+        bn = env_bn;
+    }
     if (g.kind == GEMM_TF32X3 && bn > 128) bn = 128;  // its partial sums live in registers
     if (bn == 0) {
         const int64_t mblk = p.num_m_blocks;

@@ -169,30 +169,54 @@ __global__ void layernorm_kernel(const float* __restrict__ x, const float* __res
     }
 }
 
-// Register-resident variant for d % 4 == 0 and d <= 128 * NV: the row is
-// read once into NV float4 per lane; four independent float-pair
-// accumulators per lane shorten the two-sum chains.  Same arithmetic as
-// layernorm_kernel.
+// Block-per-row variant for d % 4 == 0 (16-byte aligned rows): LNW warps
+// share a row, each thread holding NV float4 of it in registers; the
+// float-pair partial sums are reduced over the warp by shuffles and over the
+// block through shared memory in a fixed order.  Same arithmetic as
+// layernorm_kernel (only the summation order differs).
+constexpr int LNW = 4;
+
+__device__ __forceinline__ void ln_block_sum(float& h, float& l, float2* red, int lane, int warp) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float oh = __shfl_xor_sync(0xffffffffu, h, o), ol = __shfl_xor_sync(0xffffffffu, l, o);
+        df_add(h, l, oh, ol, h, l);
+    }
+    if (lane == 0) red[warp] = make_float2(h, l);
+    __syncthreads();
+    float2 t = red[0];
+    h = t.x;
+    l = t.y;
+#pragma unroll
+    for (int w = 1; w < LNW; w++) {
+        t = red[w];
+        df_add(h, l, t.x, t.y, h, l);
+    }
+}
+
 template <int NV>
-__global__ void layernorm_reg_kernel(const float* __restrict__ x, const float* __restrict__ g,
-                                     const float* __restrict__ b, float* __restrict__ y, int8_t* __restrict__ q,
-                                     const float* __restrict__ qscale, uint32_t* __restrict__ amax, int T, int d,
-                                     double eps) {
-    const int lane = threadIdx.x & 31;
-    const int warps = blockDim.x >> 5;
+__global__ void __launch_bounds__(32 * LNW)
+    layernorm_block_kernel(const float* __restrict__ x, const float* __restrict__ g, const float* __restrict__ b,
+                           float* __restrict__ y, int8_t* __restrict__ q, const float* __restrict__ qscale,
+                           uint32_t* __restrict__ amax, int T, int d, double eps) {
+    __shared__ float2 red[2][LNW];
+    const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
     const int d4 = d >> 2;
     InvScale qs{0.0, 0.0f, 0.0f};
     if (q) qs = make_inv_scale(static_cast<double>(__ldg(qscale)));
     const float eps_h = __double2float_rn(eps);
     const float eps_l = __double2float_rn(eps - static_cast<double>(eps_h));
     const float df = static_cast<float>(d);
+    const float4* g4 = reinterpret_cast<const float4*>(g);
+    const float4* b4 = reinterpret_cast<const float4*>(b);
     float am = 0.0f;
-    for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
+    for (int t = blockIdx.x; t < T; t += gridDim.x) {
         const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(t) * d);
         float4 v[NV];
 #pragma unroll
         for (int j = 0; j < NV; j++) {
-            const int i = j * 32 + lane;
+            const int i = j * 32 * LNW + tid;
             v[j] = (i < d4) ? __ldcs(xr + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
         // sum: four float-pair accumulators (x, y, z, w components)
@@ -211,29 +235,25 @@ __global__ void layernorm_reg_kernel(const float* __restrict__ x, const float* _
         df_add(sh[0], sl[0], sh[1], sl[1], sh[0], sl[0]);
         df_add(sh[2], sl[2], sh[3], sl[3], sh[2], sl[2]);
         df_add(sh[0], sl[0], sh[2], sl[2], sh[0], sl[0]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float oh = __shfl_xor_sync(0xffffffffu, sh[0], o), ol = __shfl_xor_sync(0xffffffffu, sl[0], o);
-            df_add(sh[0], sl[0], oh, ol, sh[0], sl[0]);
-        }
+        ln_block_sum(sh[0], sl[0], red[0], lane, warp);
         float mh, ml;
         df_div_int(sh[0], sl[0], df, mh, ml);
-        // variance of the valid elements (padding lanes contribute nothing)
+        // variance of the valid elements
         float vh[4] = {0.0f, 0.0f, 0.0f, 0.0f}, vl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
         for (int j = 0; j < NV; j++) {
-            if (j * 32 + lane >= d4) continue;
+            if (j * 32 * LNW + tid >= d4) continue;
             const float c[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
 #pragma unroll
             for (int k = 0; k < 4; k++) {
                 float dh, de;
                 two_sum(c[k], -mh, dh, de);
                 de = __fsub_rn(de, ml);
-                const float p = __fmul_rn(dh, dh);
-                float pe = fmaf(dh, dh, -p);
+                const float pp = __fmul_rn(dh, dh);
+                float pe = fmaf(dh, dh, -pp);
                 pe = fmaf(2.0f * dh, de, pe);
                 float s, e;
-                two_sum(vh[k], p, s, e);
+                two_sum(vh[k], pp, s, e);
                 vh[k] = s;
                 vl[k] = __fadd_rn(vl[k], __fadd_rn(e, pe));
             }
@@ -241,20 +261,14 @@ __global__ void layernorm_reg_kernel(const float* __restrict__ x, const float* _
         df_add(vh[0], vl[0], vh[1], vl[1], vh[0], vl[0]);
         df_add(vh[2], vl[2], vh[3], vl[3], vh[2], vl[2]);
         df_add(vh[0], vl[0], vh[2], vl[2], vh[0], vl[0]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float oh = __shfl_xor_sync(0xffffffffu, vh[0], o), ol = __shfl_xor_sync(0xffffffffu, vl[0], o);
-            df_add(vh[0], vl[0], oh, ol, vh[0], vl[0]);
-        }
+        ln_block_sum(vh[0], vl[0], red[1], lane, warp);
         float wh, wl, rh, rl;
         df_div_int(vh[0], vl[0], df, wh, wl);
         df_add(wh, wl, eps_h, eps_l, wh, wl);
         df_rsqrt(wh, wl, rh, rl);
-        const float4* g4 = reinterpret_cast<const float4*>(g);
-        const float4* b4 = reinterpret_cast<const float4*>(b);
 #pragma unroll
         for (int j = 0; j < NV; j++) {
-            const int i = j * 32 + lane;
+            const int i = j * 32 * LNW + tid;
             if (i >= d4) continue;
             const float4 gg = __ldg(g4 + i), bb = __ldg(b4 + i);
             const float c[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
@@ -293,6 +307,7 @@ __global__ void layernorm_reg_kernel(const float* __restrict__ x, const float* _
                 *reinterpret_cast<char4*>(q + idx) = qq;
             }
         }
+        __syncthreads();  // red is reused by the next row
     }
     if (amax) {
         am = warp_max_f(am);
@@ -310,15 +325,14 @@ int launch_layernorm(const float* x, const float* g, const float* b, float* y, i
     const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(g) |
                          reinterpret_cast<uintptr_t>(b) | (y ? reinterpret_cast<uintptr_t>(y) : 0) |
                          (q ? reinterpret_cast<uintptr_t>(q) & 3 : 0);
-    const int nv = (d + 127) / 128;
+    const int nv = (d / 4 + 32 * LNW - 1) / (32 * LNW);
     if ((d & 3) == 0 && (al & 15) == 0 && nv <= 16) {
-#define TVQ_LN(NV) layernorm_reg_kernel<NV><<<grid, threads, 0, st>>>(x, g, b, y, q, qscale, amax, T, d, eps)
+        const int bgrid = std::min(T, sm_count() * 16);
+#define TVQ_LN(NV) layernorm_block_kernel<NV><<<bgrid, 32 * LNW, 0, st>>>(x, g, b, y, q, qscale, amax, T, d, eps)
         if (nv <= 1) TVQ_LN(1);
         else if (nv <= 2) TVQ_LN(2);
         else if (nv <= 4) TVQ_LN(4);
-        else if (nv <= 6) TVQ_LN(6);
         else if (nv <= 8) TVQ_LN(8);
-        else if (nv <= 13) TVQ_LN(13);
         else TVQ_LN(16);
 #undef TVQ_LN
     } else {

@@ -80,6 +80,7 @@ struct Session {
     std::vector<cudaEvent_t> ev;
     std::vector<int> ev_stage;  // stage id of the interval ending at ev[i]
     bool capturing = false;
+    int64_t graph_kernels = 0;  // kernel nodes of the captured forward
 
     int64_t logits_rows() const { return logits_mode == 0 ? T : nseg; }
 
@@ -320,6 +321,20 @@ int capture(Session& s) {
         return rc;
     }
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+    {  // kernel launches per forward: the graph's kernel nodes
+        size_t n = 0;
+        if (cudaGraphGetNodes(g, nullptr, &n) == cudaSuccess && n) {
+            std::vector<cudaGraphNode_t> nodes(n);
+            if (cudaGraphGetNodes(g, nodes.data(), &n) == cudaSuccess) {
+                int64_t k = 0;
+                for (size_t i = 0; i < n; i++) {
+                    cudaGraphNodeType t;
+                    if (cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) k++;
+                }
+                s.graph_kernels = k;
+            }
+        }
+    }
     e = cudaGraphInstantiate(&s.gexec, g, 0);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
@@ -548,7 +563,7 @@ int tvq_session_prepare(int64_t handle, const int64_t* seg, int64_t n_seg, int l
     // chunk (keys, rounded to the tile height; 0 = never split).
     const bool tc = S->heads > 0 && S->d / S->heads == 64 && !(getenv("TVQ_ATTN_TC") && atoi(getenv("TVQ_ATTN_TC")) == 0);
     const int QT = tc ? attention_tc_rows() : 64;
-    int kKeyChunk = 256;
+    int kKeyChunk = 512;
     if (const char* env = getenv("TVQ_ATTN_KEY_CHUNK")) {
         const int v = atoi(env);
         kKeyChunk = v <= 0 ? (1 << 30) : std::max(QT, v / QT * QT);
@@ -705,6 +720,14 @@ int tvq_session_stage_times(int64_t handle, float* ms, int64_t n) {
         TVQ_CUDA(cudaEventElapsedTime(&t, S->ev[i - 1], S->ev[i]));
         if (S->ev_stage[i] >= 0) ms[S->ev_stage[i]] += t;
     }
+    return TVQ_OK;
+}
+
+int tvq_session_launches(int64_t handle, int64_t* kernels) {
+    SESSION(handle)
+    TVQ_CHECK(kernels, TVQ_ERR_INVALID, "null output pointer");
+    TVQ_CHECK(S->gexec, TVQ_ERR_INVALID, "no forward has been captured for this layout");
+    *kernels = S->graph_kernels;
     return TVQ_OK;
 }
 

@@ -212,6 +212,12 @@ class GPT2Session:
     def sync(self):
         N.call("tvq_session_sync", self.handle)
 
+    def launches(self) -> int:
+        """Kernel launches of one forward (kernel nodes of its CUDA graph)."""
+        n = C.c_int64(0)
+        N.call("tvq_session_launches", self.handle, C.byref(n))
+        return int(n.value)
+
     STAGES = ("embed", "layernorm", "gemm_c_attn", "attention", "gemm_attn_proj", "gemm_c_fc", "gemm_mlp_proj",
               "lm_head")
 
