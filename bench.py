@@ -39,8 +39,12 @@ sys.path.insert(0, ROOT)
 
 SEQ = 1024
 METRIC = "GPT-2 124M INT8 PTQ forward tokens/s"
+METRIC4 = "GPT-2 124M INT8 PTQ batched serving tokens/s"
 UNIT = "tokens/s"
 WORKLOAD = "config 2: GPT-2 124M (12 L, d 768, 12 heads, vocab 50257), all 4 linears/block INT8 PTQ, seq 1024, batch 1 per GPU"
+WORKLOAD4 = ("config 4: GPT-2 124M INT8 PTQ, 256 requests with lengths U[32,1024] packed into 131072 tokens, "
+             "whole requests sharded over the GPUs, last-token logits")
+C4_REQUESTS, C4_TOKENS = 256, 131072
 FLUSH_BYTES = 256 << 20
 
 
@@ -176,6 +180,7 @@ def cpu_sample(weights, ids, scales, reps=1):
     import oracle as O
     from oracle import gpt2_int8 as OG
     cfg = weights.cfg
+    ids = np.asarray(ids, np.int64)[:SEQ]  # one 1024-token sequence
     seg = np.array([0, SEQ], np.int64)
     qw = OG.quantize_weights(weights.layers[:1])
     best = None
@@ -227,10 +232,12 @@ def run_reference(args, rank):
     v = statistics.median(vals)
     sample = ("embedding + 1 of 12 blocks on 1024 tokens + LM head on 32 of 1024 rows, extrapolated to the full "
               "forward; median of %d steps" % args.steps)
-    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+    line = {"metric": METRIC if args.config == 2 else METRIC4, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 * SEQ / v, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "seq_len": SEQ, "global_batch": 1, "parallelism": "cpu"},
+            "config": {"workload": WORKLOAD if args.config == 2 else WORKLOAD4, "seq_len": SEQ, "global_batch": 1,
+                       "parallelism": "cpu", "sample_note": "per-token CPU rate of the same model"},
             "impl": "reference",
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -251,11 +258,26 @@ def run_ours(args, rank, world, local):
 
     cfg = GPT2Config.gpt2_124m()
     w = GPT2Weights.random(cfg, seed=0)
-    sess = GPT2Session(w, device=local, max_tokens=SEQ)
-    seg = np.array([0, SEQ], np.int64)
-    sess.prepare(seg, logits_mode=0)
-    calib_ids = np.random.default_rng(1).integers(0, cfg.vocab, SEQ).astype(np.int64)
-    ids = np.random.default_rng(2 + rank).integers(0, cfg.vocab, SEQ).astype(np.int64)
+    if args.config == 4:
+        # 256 requests, lengths U[32, 1024] summing to 131072 tokens, whole
+        # requests sharded over the ranks (longest first), packed per rank;
+        # serving logits = the last token of every request
+        from tokenvector.inference_b200 import sharding as S
+        lengths = S.ragged_lengths(C4_REQUESTS, C4_TOKENS, 32, 1024, seed=0)
+        pl = S.plan(lengths, world, rank)
+        seg, T, logits_mode = pl.seg, pl.tokens, 1
+        ids = np.concatenate([np.random.default_rng(1000 + i).integers(0, cfg.vocab, lengths[i])
+                              for i in pl.requests]).astype(np.int64)
+        calib_ids = np.concatenate([np.random.default_rng(5000 + i).integers(0, cfg.vocab, lengths[i])
+                                    for i in pl.requests]).astype(np.int64)
+        job_tokens = C4_TOKENS
+    else:
+        seg, T, logits_mode = np.array([0, SEQ], np.int64), SEQ, 0
+        calib_ids = np.random.default_rng(1).integers(0, cfg.vocab, SEQ).astype(np.int64)
+        ids = np.random.default_rng(2 + rank).integers(0, cfg.vocab, SEQ).astype(np.int64)
+        job_tokens = world * SEQ
+    sess = GPT2Session(w, device=local, max_tokens=T)
+    sess.prepare(seg, logits_mode=logits_mode)
     sess.calibrate(calib_ids)
 
     # a real stream: handle 0 (the legacy stream) would mean "the session's
@@ -364,12 +386,12 @@ def run_ours(args, rank, world, local):
 
     out = None
     if rank == 0:
-        tokens = world * SEQ
+        tokens = job_tokens
         value = tokens * args.steps / (total_ms / 1000.0)
         e2e_value = tokens * e2e_steps / (e2e_ms / 1000.0)
         hbm, bf16, src = peaks()
         int8_peak = 2.0 * bf16  # dense INT8 = 2x dense BF16 on B200; no measured INT8 figure exists
-        work = gemm_work()
+        work = gemm_work(T=T)
         per_launch_ms = {k: stage_ms[k] / (prof_steps * cfg.n_layers) for k in work}
         dom = max(work, key=lambda k: per_launch_ms[k])
         ops, byts = work[dom]
@@ -405,14 +427,23 @@ def run_ours(args, rank, world, local):
                                                                               detail["lm_head_32rows_s"])}
         launches_per_step = n_launches  # kernel nodes of the captured forward graph
         out = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": METRIC if args.config == 2 else METRIC4, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "seq_len": SEQ, "global_batch": world,
-                       "parallelism": "replicas%d" % world, "l2": "flushed (256 MiB write) between steps",
-                       "weights": "seeded N(0,0.02) LCG+Box-Muller (gpt2_ref.tkv init), calibrated by 1 forward"},
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": SEQ * 8 * world,
-                    "d2h_bytes_per_step": rows * V * 4 * world, "ms_per_step": e2e_ms / e2e_steps,
+            "scaling": "weak" if args.config == 2 else "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": ({"workload": WORKLOAD, "seq_len": SEQ, "global_batch": world,
+                        "parallelism": "replicas%d" % world, "l2": "flushed (256 MiB write) between steps",
+                        "weights": "seeded N(0,0.02) LCG+Box-Muller (gpt2_ref.tkv init), calibrated by 1 forward"}
+                       if args.config == 2 else
+                       {"workload": WORKLOAD4, "requests": C4_REQUESTS, "tokens": C4_TOKENS,
+                        "parallelism": "requests sharded over %d ranks (longest first), packed" % world,
+                        "rank0_tokens": T, "logits": "last token of every request",
+                        "l2": "inputs larger than L2; flushed (256 MiB write) between steps",
+                        "weights": "seeded N(0,0.02) LCG+Box-Muller (gpt2_ref.tkv init), calibrated by 1 forward"}),
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 8 * job_tokens,
+                    "d2h_bytes_per_step": (rows * V * 4 * world) if args.config == 2 else C4_REQUESTS * V * 4,
+                    "ms_per_step": e2e_ms / e2e_steps,
                     "wall_ms_per_step": 1000.0 * e2e_wall / e2e_steps, "logits_finite": dev_logits_ok},
             "roofline": roof,
             "roofline_attention": attention_roofline(per_stage_ms=stage_ms["attention"] / prof_steps, bf16=bf16,
@@ -439,6 +470,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, choices=[2, 4], default=2,
+                    help="2: GPT-2 124M forward, seq 1024 per GPU (default, the headline); "
+                         "4: batched serving, 131072 packed tokens sharded over the GPUs")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -353,6 +353,10 @@ def embed(ids, pos, wte, wpe) -> np.ndarray:
     wte = _f32(wte)
     wpe = _f32(wpe)
     h = wte.shape[1]
+    if pos.size != ids.size or wpe.shape[1] != h:
+        raise ValueError("embed: one position per token and equal widths are required")
+    if ids.size and (ids.min() < 0 or ids.max() >= wte.shape[0] or pos.min() < 0 or pos.max() >= wpe.shape[0]):
+        raise ValueError("embed: token id or position out of range")
     out = np.empty((ids.size, h), dtype=np.float32)
     lib().tvo_embed(_p(ids), _p(pos), _p(wte), _p(wpe), _p(out), ids.size, h)
     return out

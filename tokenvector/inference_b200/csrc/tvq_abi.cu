@@ -2,6 +2,7 @@
 // reference's error behaviour (ValueError -> TVQ_ERR_SIZE), host-buffer
 // staging for the tvq_* entry points, and the asynchronous tvq_dev_* forms.
 #include <cstring>
+#include <cstdlib>
 #include <mutex>
 #include <new>
 #include <string>
@@ -39,6 +40,14 @@ struct HostCtx {
 };
 HostCtx g_host[kMaxDev];
 }  // namespace
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("TVQ_PDL");
+        return !(e && atoi(e) == 0);
+    }();
+    return on;
+}
 
 DeviceState* device_state(int* rc) {
     int dev = 0;

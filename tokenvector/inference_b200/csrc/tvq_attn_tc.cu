@@ -112,6 +112,7 @@ __device__ __forceinline__ void split4(const float4 v, float4& h, float4& l) {
 // K part of qkv [T, 3d] -> hi / lo arrays [T, d]
 __global__ void split_k_kernel(const float* __restrict__ qkv, int T, int d, float* __restrict__ kh,
                                float* __restrict__ kl) {
+    griddep_wait();
     const int d4 = d >> 2;
     const int64_t n = static_cast<int64_t>(T) * d4;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
@@ -129,6 +130,7 @@ __global__ void split_k_kernel(const float* __restrict__ qkv, int T, int d, floa
 __global__ void split_vt_kernel(const float* __restrict__ qkv, int T, int Tp, int d, float* __restrict__ vth,
                                 float* __restrict__ vtl) {
     __shared__ float tile[32][33];
+    griddep_wait();
     const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
         const int t = t0 + i;
@@ -236,6 +238,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
+    griddep_wait();  // qkv and the split K / V^T come from the previous kernels
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
@@ -520,12 +523,10 @@ int launch_split_kv(const float* qkv, int T, int d, float* kh, float* kl, float*
     if (!ds) return rc;
     const int64_t n = static_cast<int64_t>(T) * (d / 4);
     const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, ds->sm_count * 8));
-    split_k_kernel<<<grid, 256, 0, st>>>(qkv, T, d, kh, kl);
-    TVQ_CUDA(cudaGetLastError());
+    int rc2 = launch_pdl(split_k_kernel, dim3(grid), dim3(256), 0, st, qkv, T, d, kh, kl);
+    if (rc2) return rc2;
     const int Tp = attention_tc_pitch(T);
-    split_vt_kernel<<<dim3((Tp + 31) / 32, d / 32), dim3(32, 8), 0, st>>>(qkv, T, Tp, d, vth, vtl);
-    TVQ_CUDA(cudaGetLastError());
-    return TVQ_OK;
+    return launch_pdl(split_vt_kernel, dim3((Tp + 31) / 32, d / 32), dim3(32, 8), 0, st, qkv, T, Tp, d, vth, vtl);
 }
 
 int launch_attention_tc(const float* qkv, const float* kh, const float* kl, const float* vth, const float* vtl, int T,
@@ -571,8 +572,8 @@ int launch_attention_tc(const float* qkv, const float* kh, const float* kl, cons
     p.part_o = part_o;
     p.part_ml = part_ml;
     p.err = ds->d_error;
-    attention_tc_kernel<<<nitems * nheads, NTHREADS, SMEM_BYTES, st>>>(mkh, mkl, mvh, mvl, p);
-    TVQ_CUDA(cudaGetLastError());
+    rc = launch_pdl(attention_tc_kernel, dim3(nitems * nheads), dim3(NTHREADS), SMEM_BYTES, st, mkh, mkl, mvh, mvl, p);
+    if (rc) return rc;
     if (ncomb > 0) return launch_attention_combine(comb, ncomb, d, nheads, TQ, part_o, part_ml, out, outq, qscale,
                                                    amax, st);
     return TVQ_OK;

@@ -56,6 +56,40 @@ enum : int {
 // ---------------------------------------------------------------- device side
 #if defined(__CUDACC__)
 
+// Programmatic dependent launch.  A kernel started with launch_pdl may begin
+// (set-up: barriers, tensor memory, descriptor prefetch) while the previous
+// kernel of its stream is still running: its CTAs start as the
+// predecessor's CTAs exit.  Every thread calls griddep_wait() before it reads
+// anything the predecessor writes or writes anything the predecessor reads,
+// and before it exits.  griddep_launch() (an earlier explicit trigger) is not
+// used: triggering at kernel start measured slower, since chains of waiting
+// CTAs then hold SMs.  Without the launch attribute both are no-ops.
+__device__ __forceinline__ void griddep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Host: TVQ_PDL=0 launches without the attribute (plain stream order).
+bool pdl_enabled();
+
+template <typename... Params, typename... Args>
+int launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    TVQ_CUDA(cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...));
+    return TVQ_OK;
+}
+
 // Wall-clock bound on one wait (ns).  A healthy wait lasts microseconds.
 #ifndef TVQ_WAIT_LIMIT_NS
 #define TVQ_WAIT_LIMIT_NS 2000000000ull

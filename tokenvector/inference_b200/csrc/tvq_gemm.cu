@@ -266,6 +266,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
+    griddep_wait();  // A and the residual come from the previous kernel
 
     const int num_tiles = p.num_m_blocks * p.num_n_blocks;
 
@@ -548,6 +549,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // K == 0: every accumulator is 0, only the epilogue remains (matmul.tkv:14/28
 // with acc = 0).
 __global__ void gemm_k0_kernel(KParams p) {
+    griddep_wait();
     const int64_t total = static_cast<int64_t>(p.m) * p.n;
     const double sa = static_cast<double>(__ldg(p.scale_a));
     double inv_out = 0.0;
@@ -628,9 +630,7 @@ int launch_tc(const KParams& p, const GemmArgs& g, int grid, cudaStream_t st) {
         ma2 = ma;
         mb2 = mb;
     }
-    gemm_tc_kernel<KIND, BN><<<grid, THREADS, C::SMEM, st>>>(ma, mb, ma2, mb2, p);
-    TVQ_CUDA(cudaGetLastError());
-    return TVQ_OK;
+    return launch_pdl(gemm_tc_kernel<KIND, BN>, dim3(grid), dim3(THREADS), C::SMEM, st, ma, mb, ma2, mb2, p);
 }
 
 // Round a float to the TF32 grid (10 explicit mantissa bits), half away
@@ -648,6 +648,7 @@ __device__ __forceinline__ float round_tf32(float v) {
 // has at most 22 significant bits.)
 __global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo,
                                   int64_t n) {
+    griddep_wait();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const float v = x[i];
         const float h = round_tf32(v);
@@ -710,9 +711,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     if (g.k == 0) {
         const int64_t total = g.m * g.n;
         int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, ds->sm_count * 8));
-        gemm_k0_kernel<<<grid, 256, 0, st>>>(p);
-        TVQ_CUDA(cudaGetLastError());
-        return TVQ_OK;
+        return launch_pdl(gemm_k0_kernel, dim3(grid), dim3(256), 0, st, p);
     }
     TVQ_CHECK((g.k * elem) % 16 == 0, TVQ_ERR_UNSUPPORTED, "k must be a multiple of 16 bytes (TMA row pitch)");
     TVQ_CHECK(((reinterpret_cast<uintptr_t>(g.A) | reinterpret_cast<uintptr_t>(g.W)) & 15) == 0, TVQ_ERR_UNSUPPORTED,
@@ -740,10 +739,20 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     }
     if (g.kind == GEMM_TF32X3 && bn > 128) bn = 128;  // its partial sums live in registers
     if (bn == 0) {
+        // Tile width with the least work on the busiest SM: rounds of tiles
+        // (ceil(tiles / SMs)) x BN columns; ties go to the wider tile (fewer,
+        // longer MMA runs per operand load).
         const int64_t mblk = p.num_m_blocks;
-        if (g.kind != GEMM_TF32X3 && mblk * ((g.n + 255) / 256) >= ds->sm_count) bn = 256;
-        else if (mblk * ((g.n + 127) / 128) >= ds->sm_count) bn = 128;
-        else bn = 64;
+        int64_t best = -1;
+        for (int cand : {256, 128, 64}) {
+            if (g.kind == GEMM_TF32X3 && cand > 128) continue;
+            const int64_t tiles = mblk * ((g.n + cand - 1) / cand);
+            const int64_t cost = (tiles + ds->sm_count - 1) / ds->sm_count * cand;
+            if (best < 0 || cost < best) {
+                best = cost;
+                bn = cand;
+            }
+        }
     }
     p.num_n_blocks = static_cast<int>((g.n + bn - 1) / bn);
     const int tiles = p.num_m_blocks * p.num_n_blocks;
@@ -768,9 +777,7 @@ int launch_split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStrea
     DeviceState* ds = device_state(&rc);
     if (!ds) return rc;
     const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, ds->sm_count * 8));
-    split_tf32_kernel<<<grid, 256, 0, st>>>(x, hi, lo, n);
-    TVQ_CUDA(cudaGetLastError());
-    return TVQ_OK;
+    return launch_pdl(split_tf32_kernel, dim3(grid), dim3(256), 0, st, x, hi, lo, n);
 }
 
 }  // namespace tvq

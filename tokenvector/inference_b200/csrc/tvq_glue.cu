@@ -34,6 +34,7 @@ int sm_count() {
 __global__ void embed_kernel(const int64_t* __restrict__ ids, const int* __restrict__ tok_seg_start,
                              const float* __restrict__ wte, const float* __restrict__ wpe, float* __restrict__ x,
                              int T, int d, int vocab, int max_pos, int* err) {
+    griddep_wait();
     const int t = blockIdx.x;
     if (t >= T) return;
     int64_t id = ids[t];
@@ -52,9 +53,8 @@ __global__ void embed_kernel(const int64_t* __restrict__ ids, const int* __restr
 int launch_embed(const int64_t* ids, const int* tok_seg_start, const float* wte, const float* wpe, float* x, int T,
                  int d, int vocab, int max_pos, int* err, cudaStream_t st) {
     if (T <= 0) return TVQ_OK;
-    embed_kernel<<<T, 128, 0, st>>>(ids, tok_seg_start, wte, wpe, x, T, d, vocab, max_pos, err);
-    TVQ_CUDA(cudaGetLastError());
-    return TVQ_OK;
+    return launch_pdl(embed_kernel, dim3(T), dim3(128), 0, st, ids, tok_seg_start, wte, wpe, x, T, d, vocab, max_pos,
+                      err);
 }
 
 // ------------------------------------------------------------------ layernorm
@@ -92,6 +92,7 @@ __global__ void layernorm_kernel(const float* __restrict__ x, const float* __res
                                  const float* __restrict__ b, float* __restrict__ y, int8_t* __restrict__ q,
                                  const float* __restrict__ qscale, uint32_t* __restrict__ amax, int T, int d,
                                  double eps) {
+    griddep_wait();
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
     InvScale qs{0.0, 0.0f, 0.0f};
@@ -199,6 +200,7 @@ __global__ void __launch_bounds__(32 * LNW)
     layernorm_block_kernel(const float* __restrict__ x, const float* __restrict__ g, const float* __restrict__ b,
                            float* __restrict__ y, int8_t* __restrict__ q, const float* __restrict__ qscale,
                            uint32_t* __restrict__ amax, int T, int d, double eps) {
+    griddep_wait();
     __shared__ float2 red[2][LNW];
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
@@ -328,18 +330,17 @@ int launch_layernorm(const float* x, const float* g, const float* b, float* y, i
     const int nv = (d / 4 + 32 * LNW - 1) / (32 * LNW);
     if ((d & 3) == 0 && (al & 15) == 0 && nv <= 16) {
         const int bgrid = std::min(T, sm_count() * 16);
-#define TVQ_LN(NV) layernorm_block_kernel<NV><<<bgrid, 32 * LNW, 0, st>>>(x, g, b, y, q, qscale, amax, T, d, eps)
-        if (nv <= 1) TVQ_LN(1);
-        else if (nv <= 2) TVQ_LN(2);
-        else if (nv <= 4) TVQ_LN(4);
-        else if (nv <= 8) TVQ_LN(8);
-        else TVQ_LN(16);
+#define TVQ_LN(NV) \
+    launch_pdl(layernorm_block_kernel<NV>, dim3(bgrid), dim3(32 * LNW), 0, st, x, g, b, y, q, qscale, amax, T, d, eps)
+        if (nv <= 1) return TVQ_LN(1);
+        if (nv <= 2) return TVQ_LN(2);
+        if (nv <= 4) return TVQ_LN(4);
+        if (nv <= 8) return TVQ_LN(8);
+        return TVQ_LN(16);
 #undef TVQ_LN
     } else {
-        layernorm_kernel<<<grid, threads, 0, st>>>(x, g, b, y, q, qscale, amax, T, d, eps);
+        return launch_pdl(layernorm_kernel, dim3(grid), dim3(threads), 0, st, x, g, b, y, q, qscale, amax, T, d, eps);
     }
-    TVQ_CUDA(cudaGetLastError());
-    return TVQ_OK;
 }
 
 // ------------------------------------------------------------------ attention
@@ -371,6 +372,7 @@ __global__ void __launch_bounds__(ATHREADS)
                      int d, int nheads, float q_scale, float* __restrict__ out, int8_t* __restrict__ outq,
                      const float* __restrict__ qscale, uint32_t* __restrict__ amax, float* __restrict__ part_o,
                      float2* __restrict__ part_ml) {
+    griddep_wait();
     static_assert(HD % 16 == 0 && HD <= 64, "head dim");
     constexpr int LD = HD + APAD;   // row pitch of Q, K, V tiles
     constexpr int PLD = AK + APAD;  // row pitch of P
@@ -566,6 +568,7 @@ __global__ void __launch_bounds__(QR * 2)
     attention_combine_kernel(const int4* __restrict__ comb, int d, int nheads, const float* __restrict__ part_o,
                              const float2* __restrict__ part_ml, float* __restrict__ out, int8_t* __restrict__ outq,
                              const float* __restrict__ qscale, uint32_t* __restrict__ amax) {
+    griddep_wait();
     constexpr int HC = HD / 2;
     const int e = blockIdx.x / nheads;
     const int head = blockIdx.x % nheads;
@@ -618,13 +621,10 @@ static int launch_combine_hd(const int4* comb, int ncomb, int d, int nheads, int
                              const float2* part_ml, float* out, int8_t* outq, const float* qscale, uint32_t* amax,
                              cudaStream_t st) {
     if (rows == 64)
-        attention_combine_kernel<HD, 64><<<ncomb * nheads, 128, 0, st>>>(comb, d, nheads, part_o, part_ml, out, outq,
-                                                                        qscale, amax);
-    else
-        attention_combine_kernel<HD, 128><<<ncomb * nheads, 256, 0, st>>>(comb, d, nheads, part_o, part_ml, out, outq,
-                                                                         qscale, amax);
-    TVQ_CUDA(cudaGetLastError());
-    return TVQ_OK;
+        return launch_pdl(attention_combine_kernel<HD, 64>, dim3(ncomb * nheads), dim3(128), 0, st, comb, d, nheads,
+                          part_o, part_ml, out, outq, qscale, amax);
+    return launch_pdl(attention_combine_kernel<HD, 128>, dim3(ncomb * nheads), dim3(256), 0, st, comb, d, nheads,
+                      part_o, part_ml, out, outq, qscale, amax);
 }
 
 int launch_attention_combine(const int4* comb, int ncomb, int d, int nheads, int rows, const float* part_o,
@@ -658,9 +658,9 @@ static int launch_attention_hd(const float* qkv, const int4* tiles, const int4* 
     }
     // softmax in base 2: scores scaled by log2(e)/sqrt(hd) through Q
     const float q_scale = static_cast<float>(1.4426950408889634 / sqrt(static_cast<double>(HD)));
-    attention_kernel<HD><<<nitems * nheads, ATHREADS, smem, st>>>(qkv, tiles, split, d, nheads, q_scale, out, outq,
-                                                                  qscale, amax, part_o, part_ml);
-    TVQ_CUDA(cudaGetLastError());
+    const int lrc = launch_pdl(attention_kernel<HD>, dim3(nitems * nheads), dim3(ATHREADS), smem, st, qkv, tiles,
+                               split, d, nheads, q_scale, out, outq, qscale, amax, part_o, part_ml);
+    if (lrc) return lrc;
     if (ncomb > 0)
         return launch_combine_hd<HD>(comb, ncomb, d, nheads, AQ, part_o, part_ml, out, outq, qscale, amax, st);
     return TVQ_OK;
@@ -694,6 +694,7 @@ int launch_attention(const float* qkv, const int4* tiles, int ntiles, int T, int
 // calibrate_minmax symmetric (tv/quantization/engine.tkv:24-30) from a
 // recorded amax: scale = fl32(max(amax, 1e-8) / 127).
 __global__ void scale_from_amax_kernel(const uint32_t* __restrict__ amax, float* __restrict__ scale, int n) {
+    griddep_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     double am = static_cast<double>(__uint_as_float(amax[i]));
@@ -703,9 +704,7 @@ __global__ void scale_from_amax_kernel(const uint32_t* __restrict__ amax, float*
 
 int launch_scale_from_amax(const uint32_t* amax, float* scale, int n, cudaStream_t st) {
     if (n <= 0) return TVQ_OK;
-    scale_from_amax_kernel<<<(n + 127) / 128, 128, 0, st>>>(amax, scale, n);
-    TVQ_CUDA(cudaGetLastError());
-    return TVQ_OK;
+    return launch_pdl(scale_from_amax_kernel, dim3((n + 127) / 128), dim3(128), 0, st, amax, scale, n);
 }
 
 // [k, n] (HF Conv1D layout) -> [n, k]
@@ -750,6 +749,7 @@ int launch_token_seg(const int* seg, int nseg, int* tok_start, cudaStream_t st) 
 // last token of every sequence: rows seg[s+1]-1 of a [T, n] matrix
 __global__ void gather_last_kernel(const float* __restrict__ src, const int* __restrict__ seg, int nseg, int64_t n,
                                    float* __restrict__ dst) {
+    griddep_wait();
     const int s = blockIdx.y;
     if (s >= nseg) return;
     const int64_t row = seg[s + 1] - 1;
@@ -760,9 +760,7 @@ __global__ void gather_last_kernel(const float* __restrict__ src, const int* __r
 int launch_gather_last(const float* src, const int* seg, int nseg, int64_t n, float* dst, cudaStream_t st) {
     if (nseg <= 0) return TVQ_OK;
     dim3 grid(static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 64)), nseg);
-    gather_last_kernel<<<grid, 256, 0, st>>>(src, seg, nseg, n, dst);
-    TVQ_CUDA(cudaGetLastError());
-    return TVQ_OK;
+    return launch_pdl(gather_last_kernel, grid, dim3(256), 0, st, src, seg, nseg, n, dst);
 }
 
 }  // namespace tvq

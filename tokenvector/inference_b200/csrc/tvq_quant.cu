@@ -168,6 +168,7 @@ int launch_minmax_finalize(const uint32_t* mm, const float* first, int symmetric
 // step: four 16-byte loads, one 16-byte store.
 __global__ void quantize_i8_kernel(const float* __restrict__ x, int8_t* __restrict__ q, int64_t n,
                                    const float* __restrict__ scale) {
+    griddep_wait();
     const InvScale qs = make_inv_scale(static_cast<double>(__ldg(scale)));
     const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -194,9 +195,8 @@ __global__ void quantize_i8_kernel(const float* __restrict__ x, int8_t* __restri
 int launch_quantize_i8(const float* x, int8_t* q, int64_t n, const float* scale_dev, cudaStream_t st) {
     if (n <= 0) return TVQ_OK;
     const int threads = 256;
-    quantize_i8_kernel<<<grid_for((n + 15) / 16, threads, 8), threads, 0, st>>>(x, q, n, scale_dev);
-    TVQ_CUDA(cudaGetLastError());
-    return TVQ_OK;
+    return launch_pdl(quantize_i8_kernel, dim3(grid_for((n + 15) / 16, threads, 8)), dim3(threads), 0, st, x, q, n,
+                      scale_dev);
 }
 
 // dequantize_int8_symmetric / _per_channel, engine.tkv:229-234, 253-262:
