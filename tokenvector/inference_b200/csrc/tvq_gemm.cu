@@ -40,9 +40,24 @@ namespace {
 constexpr int BM = 128;        // rows of A per tile (= TMEM lanes)
 constexpr int BK = 128;        // bytes of K per stage (one 128-byte swizzle row)
 constexpr int UMMA_K = 32;     // K per tcgen05.mma for 8-bit operands
-constexpr int EPI_WARPS = 8;   // two epilogue warps per TMEM lane group
-constexpr int THREADS = 128 + 32 * EPI_WARPS;  // warps 0-3: TMA, MMA, TMEM alloc, spare; 4-11: epilogue
-constexpr int CH = 16;         // accumulator columns per epilogue chunk (tcgen05.ld .x16)
+// Epilogue geometry for EW epilogue warps (EPW per TMEM lane group, each
+// taking CH-column chunks): 16 warps / 8 columns for the INT8 and FP8
+// epilogues (their exact dequant is latency-bound: more warps hide it), 8
+// warps / 16 columns for the split-TF32 GEMM (register promotion of short K
+// runs, fewer arrivals per run).
+template <int EW>
+struct Epi {
+    static_assert(EW == 8 || EW == 16, "8 or 16 epilogue warps");
+    static constexpr int EPI_WARPS = EW;
+    static constexpr int EPW = EW / 4;
+    static constexpr int THREADS = 128 + 32 * EW;  // warps 0-3: TMA, MMA, TMEM alloc, spare; then the epilogue
+    static constexpr int CH = 128 / EW;            // accumulator columns per epilogue chunk
+    static constexpr int LPR = CH / 4;             // store phase: lanes per 4*CH-byte row segment
+    static constexpr int RPI = 32 / LPR;           // rows per store iteration
+    static constexpr int SWS = (CH == 16) ? 1 : 2; // staging swizzle: slot j of row r at j ^ ((r >> SWS) & (LPR - 1))
+};
+template <int KIND>
+using EpiOf = Epi<(KIND == GEMM_TF32X3) ? 8 : 16>;
 // GEMM_TF32X3 sums its products in TMEM over this many k-blocks (32 f32
 // each) only; the epilogue adds the partial sums in registers with IEEE
 // round-to-nearest.  The tensor core's own f32 accumulation is less exact
@@ -116,40 +131,51 @@ struct EpiCtx {
     InvScale qs;     // 1 / scale_out for the int8 output
 };
 
-// Second half of the epilogue for one 32-row x CH-column chunk, y = row
-// `lane`: swizzled shared-memory transpose (float4 slot j of row r sits at
-// slot j ^ ((r >> 1) & 3), conflict-free both ways), then four lanes per
-// 64-byte row segment: residual add, f32 / int8 stores, running amax.
-// The residual segments (row0 + 8 it + lane / 4, n0 + 4 (lane % 4)) that
-// stage_and_store adds, loaded ahead so their latency overlaps the TMEM read
-// and the epilogue arithmetic (the residual may alias Y; each segment is read
-// here, before the same thread stores it).
+template <int N>
+__device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, uint32_t (&r)[N]) {
+    if constexpr (N == 16) {
+        tmem_ld16(taddr, r);
+    } else {
+        tmem_ld8(taddr, r);
+    }
+}
+
+// The residual segments (row0 + RPI it + lane / LPR, n0 + 4 (lane % LPR))
+// that stage_and_store adds, loaded ahead so their latency overlaps the TMEM
+// read and the epilogue arithmetic (the residual may alias Y; each segment is
+// read here, before the same thread stores it).
+template <class E>
 __device__ __forceinline__ void load_residual(const KParams& p, const EpiCtx& e, int lane, int row0, int n0,
-                                              float4 (&res)[4]) {
+                                              float4 (&res)[E::LPR]) {
 #pragma unroll
-    for (int it = 0; it < 4; it++) {
-        const int row = row0 + it * 8 + (lane >> 2);
-        const int col = n0 + 4 * (lane & 3);
+    for (int it = 0; it < E::LPR; it++) {
+        const int row = row0 + it * E::RPI + lane / E::LPR;
+        const int col = n0 + 4 * (lane % E::LPR);
         res[it] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         if (p.residual && e.vec_ok && row < p.m && col + 3 < p.n)
             res[it] = *reinterpret_cast<const float4*>(p.residual + static_cast<int64_t>(row) * p.n + col);
     }
 }
 
-__device__ __forceinline__ void stage_and_store(const KParams& p, const EpiCtx& e, float* stage, const float (&y)[CH],
-                                                int lane, int row0, int n0, float& amax, const float4 (&res)[4]) {
+// Second half of the epilogue for one 32-row x CH-column chunk, y = row
+// `lane`: swizzled shared-memory transpose (float4 slot j of row r sits at
+// slot j ^ ((r >> SWS) & (LPR - 1)), conflict-free both ways), then LPR lanes
+// per 4*CH-byte row segment: residual add, f32 / int8 stores, running amax.
+template <class E>
+__device__ __forceinline__ void stage_and_store(const KParams& p, const EpiCtx& e, float* stage, const float (&y)[E::CH],
+                                                int lane, int row0, int n0, float& amax, const float4 (&res)[E::LPR]) {
 #pragma unroll
-    for (int j = 0; j < CH / 4; j++)
-        *reinterpret_cast<float4*>(&stage[lane * CH + 4 * (j ^ ((lane >> 1) & 3))]) =
+    for (int j = 0; j < E::LPR; j++)
+        *reinterpret_cast<float4*>(&stage[lane * E::CH + 4 * (j ^ ((lane >> E::SWS) & (E::LPR - 1)))]) =
             make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
     __syncwarp();
 #pragma unroll
-    for (int it = 0; it < 4; it++) {
-        const int rr = it * 8 + (lane >> 2);
-        const int c4 = lane & 3;
+    for (int it = 0; it < E::LPR; it++) {
+        const int rr = it * E::RPI + lane / E::LPR;
+        const int c4 = lane % E::LPR;
         const int row = row0 + rr;
         const int col = n0 + 4 * c4;
-        float4 v = *reinterpret_cast<const float4*>(&stage[rr * CH + 4 * (c4 ^ ((rr >> 1) & 3))]);
+        float4 v = *reinterpret_cast<const float4*>(&stage[rr * E::CH + 4 * (c4 ^ ((rr >> E::SWS) & (E::LPR - 1)))]);
         if (row >= p.m || col >= p.n) continue;
         const int64_t off = static_cast<int64_t>(row) * p.n + col;
         if (e.vec_ok && col + 3 < p.n) {
@@ -213,15 +239,16 @@ struct Cfg {
     static constexpr int NACC = (KIND == GEMM_TF32X3) ? 4 : 2;
     static constexpr uint32_t TMEM_COLS = NACC * BN;  // 128/256/512: powers of two
     static constexpr uint32_t RING = STAGES * NS * (A_BYTES + B_BYTES);
-    static constexpr uint32_t EPI = EPI_WARPS * 32 * CH * 4;  // per-epilogue-warp 32 x 16 f32 staging tiles
+    static constexpr uint32_t EPI = EpiOf<KIND>::EPI_WARPS * 32 * EpiOf<KIND>::CH * 4;  // per-warp 32 x CH f32 staging
     static constexpr uint32_t SMEM = RING + EPI + 1024 /*align*/ + 512 /*barriers*/;
 };
 
 template <int KIND, int BN>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, KParams p) {
     using C = Cfg<KIND, BN>;
+    using E = EpiOf<KIND>;
     constexpr int STAGES = C::STAGES;
     constexpr int NS = C::NS;
     extern __shared__ uint8_t smem_raw[];
@@ -245,7 +272,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int b = 0; b < C::NACC; b++) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], EPI_WARPS);
+            mbar_init(&tempty[b], E::EPI_WARPS);
         }
         mbar_init(drain, 1);
         fence_barrier_init();
@@ -354,8 +381,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         // phase 2: lanes along columns: residual, f32 / int8 stores (four
         //          lanes write one 64-byte row segment), amax
         const int eg = warp & 3;            // TMEM lane group this warp may access
-        const int half = (warp - 4) >> 2;   // which alternate chunks it takes
-        float* stage = reinterpret_cast<float*>(smem + C::RING) + (warp - 4) * (32 * CH);
+        const int half = (warp - 4) >> 2;   // which of the E::EPW interleaved chunk sequences it takes
+        float* stage = reinterpret_cast<float*>(smem + C::RING) + (warp - 4) * (32 * E::CH);
         const bool bias_on = p.bias != nullptr;
         const bool per_channel = p.per_channel != 0;
         const float sa = (KIND == GEMM_TF32X3) ? 1.0f : __ldg(p.scale_a);
@@ -370,14 +397,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(eg * 32) << 16);
         if constexpr (KIND == GEMM_TF32X3) {
             // partial sums of TF32_PROMOTE_KB k-blocks each, added in registers
-            constexpr int NCH = BN / CH / 2;  // chunks this warp owns: half, half + 2, ...
+            constexpr int NCH = BN / E::CH / E::EPW;  // chunks this warp owns: half, half + E::EPW, ...
             uint32_t ucount = 0;
             bool alive = true;
             for (int tile = blockIdx.x; tile < num_tiles && alive; tile += gridDim.x) {
                 const int mb = tile % p.num_m_blocks;
                 const int nb = tile / p.num_m_blocks;
                 const int row0 = mb * BM + eg * 32;
-                float acc[NCH][CH];
+                float acc[NCH][E::CH];
                 for (int kb0 = 0; kb0 < p.num_k_blocks; kb0 += p.promote_kb, ucount++) {
                     const uint32_t b = ucount % C::NACC;
                     const uint32_t aph = (ucount / C::NACC) & 1u;
@@ -385,9 +412,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                     __syncwarp();
                     if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
                     tc_fence_after();
-                    uint32_t r[NCH][CH];
+                    uint32_t r[NCH][E::CH];
 #pragma unroll
-                    for (int i = 0; i < NCH; i++) tmem_ld16(lane_base + b * BN + (half + 2 * i) * CH, r[i]);
+                    for (int i = 0; i < NCH; i++) tmem_ld_chunk(lane_base + b * BN + (half + E::EPW * i) * E::CH, r[i]);
                     tmem_ld_wait();
                     tc_fence_before();
                     __syncwarp();
@@ -396,22 +423,22 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                         for (int i = 0; i < NCH; i++)
 #pragma unroll
-                            for (int j = 0; j < CH; j++) acc[i][j] = __uint_as_float(r[i][j]);
+                            for (int j = 0; j < E::CH; j++) acc[i][j] = __uint_as_float(r[i][j]);
                     } else {
 #pragma unroll
                         for (int i = 0; i < NCH; i++)
 #pragma unroll
-                            for (int j = 0; j < CH; j++) acc[i][j] = __fadd_rn(acc[i][j], __uint_as_float(r[i][j]));
+                            for (int j = 0; j < E::CH; j++) acc[i][j] = __fadd_rn(acc[i][j], __uint_as_float(r[i][j]));
                     }
                 }
                 if (!alive) break;
 #pragma unroll
                 for (int i = 0; i < NCH; i++) {
-                    const int n0 = nb * BN + (half + 2 * i) * CH;
+                    const int n0 = nb * BN + (half + E::EPW * i) * E::CH;
                     if (n0 >= p.n) break;  // warp-uniform
                     __syncwarp();           // the previous chunk's staging reads are done
-                    const float4 nores[4] = {};
-                    stage_and_store(p, ec, stage, acc[i], lane, row0, n0, amax, nores);
+                    const float4 nores[E::LPR] = {};
+                    stage_and_store<E>(p, ec, stage, acc[i], lane, row0, n0, amax, nores);
                 }
             }
         } else {
@@ -425,8 +452,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int mb = tile % p.num_m_blocks;
                 const int nb = tile / p.num_m_blocks;
                 const int row = mb * BM + eg * 32 + lane;
-                for (int c = half; c < BN / CH; c += 2) {
-                    const int n0 = nb * BN + c * CH;
+                for (int c = half; c < BN / E::CH; c += E::EPW) {
+                    const int n0 = nb * BN + c * E::CH;
                     if (n0 >= p.n) break;
                     if (p.residual && row < p.m) prefetch_l2(p.residual + static_cast<int64_t>(row) * p.n + n0);
                     if (lane == 0 && per_channel) prefetch_l2(p.scales_w + n0);
@@ -441,16 +468,16 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int nb = tile / p.num_m_blocks;
             const int row0 = mb * BM + eg * 32;
 #pragma unroll 1
-            for (int c = half; c < BN / CH; c += 2) {
-                const int n0 = nb * BN + c * CH;
+            for (int c = half; c < BN / E::CH; c += E::EPW) {
+                const int n0 = nb * BN + c * E::CH;
                 if (n0 >= p.n) break;  // warp-uniform
-                float4 res[4];
-                load_residual(p, ec, lane, row0, n0, res);
+                float4 res[E::LPR];
+                load_residual<E>(p, ec, lane, row0, n0, res);
                 // per-column scale and bias (same addresses in every lane)
-                float swv[CH], bv[CH];
-                if (vec_cols && n0 + CH <= p.n) {
+                float swv[E::CH], bv[E::CH];
+                if (vec_cols && n0 + E::CH <= p.n) {
 #pragma unroll
-                    for (int j = 0; j < CH / 4; j++) {
+                    for (int j = 0; j < E::CH / 4; j++) {
                         const float4 t = per_channel ? __ldg(reinterpret_cast<const float4*>(p.scales_w + n0) + j)
                                                      : make_float4(sw0, sw0, sw0, sw0);
                         const float4 u = bias_on ? __ldg(reinterpret_cast<const float4*>(p.bias + n0) + j)
@@ -460,27 +487,27 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                 } else {
 #pragma unroll
-                    for (int j = 0; j < CH; j++) {
+                    for (int j = 0; j < E::CH; j++) {
                         const int n = (n0 + j < p.n) ? n0 + j : p.n - 1;
                         swv[j] = per_channel ? __ldg(p.scales_w + n) : sw0;
                         bv[j] = bias_on ? __ldg(p.bias + n) : 0.0f;
                     }
                 }
-                uint32_t r[CH];
+                uint32_t r[E::CH];
                 __syncwarp();
-                tmem_ld16(lane_base + b * BN + c * CH, r);
+                tmem_ld_chunk(lane_base + b * BN + c * E::CH, r);
                 tmem_ld_wait();
                 if (p.acc_out && row0 + lane < p.m) {
                     int32_t* dst = p.acc_out + static_cast<int64_t>(row0 + lane) * p.n + n0;
 #pragma unroll
-                    for (int j = 0; j < CH; j++)
+                    for (int j = 0; j < E::CH; j++)
                         if (n0 + j < p.n) dst[j] = static_cast<int32_t>(r[j]);
                 }
                 // fast path for all columns (straight-line), rare f64 fix-ups after
-                float y[CH];
+                float y[E::CH];
                 uint32_t bad = 0;
 #pragma unroll
-                for (int j = 0; j < CH; j++) {
+                for (int j = 0; j < E::CH; j++) {
                     float ah, ar;
                     if (KIND == GEMM_I8) {
                         const int a = static_cast<int>(r[j]);
@@ -495,7 +522,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 if (bad) {
 #pragma unroll
-                    for (int j = 0; j < CH; j++) {
+                    for (int j = 0; j < E::CH; j++) {
                         if (bad & (1u << j)) {
                             float ah, ar;
                             if (KIND == GEMM_I8) {
@@ -512,15 +539,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 if (p.act == TVQ_ACT_GELU_ERF) {
 #pragma unroll
-                    for (int j = 0; j < CH; j++) y[j] = gelu_erf_f32(y[j]);
+                    for (int j = 0; j < E::CH; j++) y[j] = gelu_erf_f32(y[j]);
                 } else if (p.act == TVQ_ACT_GELU_TANH) {
 #pragma unroll
-                    for (int j = 0; j < CH; j++) y[j] = gelu_tanh_f32(y[j]);
+                    for (int j = 0; j < E::CH; j++) y[j] = gelu_tanh_f32(y[j]);
                 } else if (p.act == TVQ_ACT_RELU) {
 #pragma unroll
-                    for (int j = 0; j < CH; j++) y[j] = y[j] > 0.0f ? y[j] : 0.0f;
+                    for (int j = 0; j < E::CH; j++) y[j] = y[j] > 0.0f ? y[j] : 0.0f;
                 }
-                stage_and_store(p, ec, stage, y, lane, row0, n0, amax, res);
+                stage_and_store<E>(p, ec, stage, y, lane, row0, n0, amax, res);
             }
             tc_fence_before();
             __syncwarp();
@@ -630,7 +657,7 @@ int launch_tc(const KParams& p, const GemmArgs& g, int grid, cudaStream_t st) {
         ma2 = ma;
         mb2 = mb;
     }
-    return launch_pdl(gemm_tc_kernel<KIND, BN>, dim3(grid), dim3(THREADS), C::SMEM, st, ma, mb, ma2, mb2, p);
+    return launch_pdl(gemm_tc_kernel<KIND, BN>, dim3(grid), dim3(EpiOf<KIND>::THREADS), C::SMEM, st, ma, mb, ma2, mb2, p);
 }
 
 // Round a float to the TF32 grid (10 explicit mantissa bits), half away
@@ -742,10 +769,13 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
         // Tile width with the least work on the busiest SM: rounds of tiles
         // (ceil(tiles / SMs)) x BN columns; ties go to the wider tile (fewer,
         // longer MMA runs per operand load).
+        // The split-TF32 form keeps 128 (its N = 64 MMAs run well below the
+        // TF32 rate) unless that leaves SMs without a tile.
         const int64_t mblk = p.num_m_blocks;
         int64_t best = -1;
         for (int cand : {256, 128, 64}) {
             if (g.kind == GEMM_TF32X3 && cand > 128) continue;
+            if (g.kind == GEMM_TF32X3 && cand == 64 && mblk * ((g.n + 127) / 128) >= ds->sm_count) continue;
             const int64_t tiles = mblk * ((g.n + cand - 1) / cand);
             const int64_t cost = (tiles + ds->sm_count - 1) / ds->sm_count * cand;
             if (best < 0 || cost < best) {
