@@ -223,6 +223,42 @@ TVQ_API int tvq_dev_attention_noalloc(const float* qkv, const int64_t* seg, int6
                                       int64_t n_heads, float* out, int8_t* outq, const float* qscale_dev,
                                       uint32_t* amax_dev, void* stream);
 
+/* ================================================================ ONNX QDQ operators
+ * The quantized-operator family of the reference runtime's fp32 graph
+ * executor (tv/runtime/session.tkv), reached from ExecutionNode.execute
+ * (:642-675).  Quantize / dequantize take the tensor split at its axis into
+ * (outer, dim, inner) (session.tkv:1926-1940, qlinear_axis); n_scales == 1 is
+ * per tensor, n_scales == dim per channel (else TVQ_ERR_SIZE).  B of the two
+ * matmuls is row-major [K, N] as in the reference.  Host-buffer forms first,
+ * then device-buffer forms (stream-ordered). */
+/* _exec_quantize_linear, session.tkv:1896-1953: y = clamp(int(round(x / s))
+ * + zero_point, -128, 127), s = max(scale, 1e-12). */
+TVQ_API int tvq_quantize_linear(const float* x, int8_t* y, int64_t outer, int64_t dim, int64_t inner,
+                                const float* scales, int64_t n_scales, int64_t zero_point);
+/* _exec_dequantize_linear, session.tkv:1955-1990: y = (x - zero_point) * scale. */
+TVQ_API int tvq_dequantize_linear(const int8_t* x, float* y, int64_t outer, int64_t dim, int64_t inner,
+                                  const float* scales, int64_t n_scales, int64_t zero_point);
+/* _exec_matmul_integer, session.tkv:2789-2851: y int32 [m, n] = a [m, k] x b [k, n]. */
+TVQ_API int tvq_matmul_integer(const int8_t* a, const int8_t* b, int32_t* y, int64_t m, int64_t k, int64_t n);
+/* _exec_qlinear_matmul, session.tkv:1992-2071: y = clamp(int(round(sum (a - zp_a)(b - zp_b)
+ * * scale_a * scale_b / scale_y)) + zp_y, -128, 127) (scale_y == 0 -> 1). */
+TVQ_API int tvq_qlinear_matmul(const int8_t* a, float scale_a, int64_t zp_a, const int8_t* b, float scale_b,
+                               int64_t zp_b, float scale_y, int64_t zp_y, int8_t* y, int64_t m, int64_t k, int64_t n);
+/* _exec_dyn_quant, session.tkv:2853-2905: uint8 asymmetric over the tensor, stored as
+ * int8 (q - 128); y_scale = (max(mx,0) - min(mn,0)) / 255, y_zero_point in [0, 255]. */
+TVQ_API int tvq_dynamic_quantize_linear(const float* x, int64_t n, int8_t* y, float* y_scale, float* y_zero_point);
+TVQ_API int tvq_dev_quantize_linear(const float* x, int8_t* y, int64_t outer, int64_t dim, int64_t inner,
+                                    const float* scales_dev, int64_t n_scales, int64_t zero_point, void* stream);
+TVQ_API int tvq_dev_dequantize_linear(const int8_t* x, float* y, int64_t outer, int64_t dim, int64_t inner,
+                                      const float* scales_dev, int64_t n_scales, int64_t zero_point, void* stream);
+TVQ_API int tvq_dev_matmul_integer(const int8_t* a, const int8_t* b, int32_t* y, int64_t m, int64_t k, int64_t n,
+                                   void* stream);
+TVQ_API int tvq_dev_qlinear_matmul(const int8_t* a, float scale_a, int64_t zp_a, const int8_t* b, float scale_b,
+                                   int64_t zp_b, float scale_y, int64_t zp_y, int8_t* y, int64_t m, int64_t k,
+                                   int64_t n, void* stream);
+TVQ_API int tvq_dev_dynamic_quantize_linear(const float* x, int64_t n, int8_t* y, float* y_scale_dev,
+                                            float* y_zp_dev, void* stream);
+
 /* ================================================================ sessions
  * Device-resident GPT-2-shaped INT8 PTQ stack: embeddings, n_layers blocks of
  * (ln_1, c_attn, attention, c_proj, ln_2, c_fc, GELU-erf, mlp c_proj) with the

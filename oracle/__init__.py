@@ -84,6 +84,11 @@ def lib():
             "tvo_add": (None, [P, P, P, i64]),
             "tvo_lm_head": (None, [P, P, P, i64, i64, i64]),
             "tvo_gi_noise": (None, [P, i64, i64, f64]),
+            "tvo_quantize_linear": (i32, [P, P, i64, i64, i64, P, i64, i64]),
+            "tvo_dequantize_linear": (i32, [P, P, i64, i64, i64, P, i64, i64]),
+            "tvo_matmul_integer": (i32, [P, P, P, i64, i64, i64]),
+            "tvo_qlinear_matmul": (i32, [P, f32, i64, P, f32, i64, f32, i64, P, i64, i64, i64]),
+            "tvo_dynamic_quantize_linear": (i32, [P, i64, P, P, P]),
             "tvo_num_threads": (i32, []),
             "tvo_set_num_threads": (None, [i32]),
         }
@@ -403,3 +408,74 @@ def num_threads() -> int:
 
 def set_num_threads(n: int) -> None:
     lib().tvo_set_num_threads(int(n))
+
+
+# ---------------------------------------------------------------- ONNX QDQ operators (session.tkv)
+def _axis_split(shape, axis: int, nsc: int):
+    """(outer, dim, inner) of `shape` at `axis` (negative counts from the end,
+    session.tkv:1926-1940); per tensor when nsc == 1."""
+    shape = list(shape)
+    if nsc == 1:
+        n = int(np.prod(shape)) if shape else 1
+        return 1, n, 1
+    ax = axis if axis >= 0 else axis + len(shape)
+    outer = int(np.prod(shape[:ax])) if ax > 0 else 1
+    inner = int(np.prod(shape[ax + 1:])) if ax + 1 < len(shape) else 1
+    return outer, int(shape[ax]), inner
+
+
+def quantize_linear(x, scales, zero_point: int = 0, axis: int = 1) -> np.ndarray:
+    """_exec_quantize_linear, tv/runtime/session.tkv:1896-1953"""
+    x = _f32(x)
+    sc = _f32(np.atleast_1d(scales))
+    outer, dim, inner = _axis_split(x.shape, axis, sc.size)
+    y = np.empty(x.shape, np.int8)
+    if lib().tvo_quantize_linear(_p(x), _p(y), outer, dim, inner, _p(sc), sc.size, int(zero_point)) != 0:
+        raise ValueError("one scale, or one per channel of the axis")
+    return y
+
+
+def dequantize_linear(x, scales, zero_point: int = 0, axis: int = 1) -> np.ndarray:
+    """_exec_dequantize_linear, tv/runtime/session.tkv:1955-1990"""
+    x = _i8(x)
+    sc = _f32(np.atleast_1d(scales))
+    outer, dim, inner = _axis_split(x.shape, axis, sc.size)
+    y = np.empty(x.shape, np.float32)
+    if lib().tvo_dequantize_linear(_p(x), _p(y), outer, dim, inner, _p(sc), sc.size, int(zero_point)) != 0:
+        raise ValueError("one scale, or one per channel of the axis")
+    return y
+
+
+def matmul_integer(a, b) -> np.ndarray:
+    """_exec_matmul_integer, tv/runtime/session.tkv:2789-2851 (B is [K, N])"""
+    a = _i8(a)
+    b = _i8(b)
+    m, k = a.shape
+    n = b.shape[1]
+    y = np.empty((m, n), np.int32)
+    lib().tvo_matmul_integer(_p(a), _p(b), _p(y), m, k, n)
+    return y
+
+
+def qlinear_matmul(a, sa, zpa, b, sw, zpw, sy, zpy) -> np.ndarray:
+    """_exec_qlinear_matmul, tv/runtime/session.tkv:1992-2071 (B is [K, N])"""
+    a = _i8(a)
+    b = _i8(b)
+    m, k = a.shape
+    n = b.shape[1]
+    y = np.empty((m, n), np.int8)
+    lib().tvo_qlinear_matmul(_p(a), float(sa), int(zpa), _p(b), float(sw), int(zpw), float(sy), int(zpy), _p(y),
+                             m, k, n)
+    return y
+
+
+def dynamic_quantize_linear(x):
+    """_exec_dyn_quant, tv/runtime/session.tkv:2853-2905 -> (int8 y, scale, zero point)"""
+    x = _f32(x).ravel()
+    y = np.empty(x.size, np.int8)
+    s = np.zeros(1, np.float32)
+    z = np.zeros(1, np.float32)
+    if lib().tvo_dynamic_quantize_linear(_p(x), x.size, _p(y), _p(s), _p(z)) != 0:
+        raise ValueError("empty input")
+    return y, float(s[0]), float(z[0])
+

@@ -702,3 +702,107 @@ TVO_API void tvo_set_num_threads(int n) {
     (void)n;
 #endif
 }
+
+/* ---------------------------------------------------------------------- */
+/* tv/runtime/session.tkv: the ONNX QDQ operator family                   */
+/* ---------------------------------------------------------------------- */
+
+/* Channel of flat index i for the (outer, dim, inner) split of a tensor at
+ * its quantization axis (session.tkv:1925-1940); 0 when per-tensor. */
+static inline int64_t qdq_channel(int64_t i, int64_t dim, int64_t inner, int64_t nsc) {
+    return nsc == 1 ? 0 : (i / inner) % dim;
+}
+
+/* _exec_quantize_linear, session.tkv:1896-1953.  s = sc > 1e-12 ? sc : 1e-12
+ * (the floor is the double 1e-12), q = int(round(x / s)) + zp in f64,
+ * clamped to [-128, 127].  nsc == 1: per tensor; else one scale per channel
+ * of the axis split (outer, dim, inner), nsc == dim. */
+TVO_API int tvo_quantize_linear(const float* x, int8_t* y, int64_t outer, int64_t dim, int64_t inner,
+                                const float* sc, int64_t nsc, int64_t zp) {
+    const int64_t n = outer * dim * inner;
+    if (nsc != 1 && nsc != dim) return -1;
+    for (int64_t i = 0; i < n; i++) {
+        const float sf = sc[qdq_channel(i, dim, inner, nsc)];
+        const double s = ((double)sf > 0.000000000001) ? (double)sf : 0.000000000001;
+        int64_t q = net_round_to_i64((double)x[i] / s);
+        q = (q > INT64_MAX - 256 || q < INT64_MIN + 256) ? q : q + zp;
+        y[i] = (int8_t)clamp_i64(q, -128, 127);
+    }
+    return 0;
+}
+
+/* _exec_dequantize_linear, session.tkv:1955-1990: y = float(int(x) - zp) * sc
+ * in f64, stored to f32. */
+TVO_API int tvo_dequantize_linear(const int8_t* x, float* y, int64_t outer, int64_t dim, int64_t inner,
+                                  const float* sc, int64_t nsc, int64_t zp) {
+    const int64_t n = outer * dim * inner;
+    if (nsc != 1 && nsc != dim) return -1;
+    for (int64_t i = 0; i < n; i++) {
+        const double v = (double)((int64_t)x[i] - zp) * (double)sc[qdq_channel(i, dim, inner, nsc)];
+        y[i] = (float)v;
+    }
+    return 0;
+}
+
+/* _exec_matmul_integer, session.tkv:2789-2851: Y int32 [m, n] = A int8
+ * [m, k] x B int8 [k, n] (B row-major [K, N]); zero points are not read. */
+TVO_API int tvo_matmul_integer(const int8_t* a, const int8_t* b, int32_t* y, int64_t m, int64_t k, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < m; i++)
+        for (int64_t j = 0; j < n; j++) {
+            int64_t acc = 0;
+            for (int64_t p = 0; p < k; p++) acc += (int64_t)a[i * k + p] * (int64_t)b[p * n + j];
+            y[i * n + j] = (int32_t)acc;
+        }
+    return 0;
+}
+
+/* _exec_qlinear_matmul, session.tkv:1992-2071: acc = sum (a - zpa)(b - zpw)
+ * over k (B row-major [K, N]), mult = sa * sw / sy in f64 (sy == 0 -> 1),
+ * y = clamp(int(round(acc * mult)) + zpy, -128, 127). */
+TVO_API int tvo_qlinear_matmul(const int8_t* a, float sa, int64_t zpa, const int8_t* b, float sw, int64_t zpw,
+                               float sy, int64_t zpy, int8_t* y, int64_t m, int64_t k, int64_t n) {
+    const double syd = ((double)sy == 0.0) ? 1.0 : (double)sy;
+    const double mult = (double)sa * (double)sw / syd;
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < m; i++)
+        for (int64_t j = 0; j < n; j++) {
+            int64_t acc = 0;
+            for (int64_t p = 0; p < k; p++)
+                acc += ((int64_t)a[i * k + p] - zpa) * ((int64_t)b[p * n + j] - zpw);
+            int64_t v = net_round_to_i64((double)acc * mult);
+            v = (v > INT64_MAX - 256 || v < INT64_MIN + 256) ? v : v + zpy;
+            y[i * n + j] = (int8_t)clamp_i64(v, -128, 127);
+        }
+    return 0;
+}
+
+/* _exec_dyn_quant, session.tkv:2853-2905: uint8 asymmetric quantization over
+ * the whole tensor, stored shifted to int8.  mn / mx start at x[0] and take
+ * strict comparisons (a NaN never replaces them), then include 0; the range
+ * is at least 1e-8; sc = (mx - mn) / 255 in f64 (stored to f32 as the scale
+ * output), zp = clamp(int(round(-mn / sc)), 0, 255), q = clamp(int(round(x /
+ * sc)) + zp, 0, 255) - 128 with the unrounded f64 sc. */
+TVO_API int tvo_dynamic_quantize_linear(const float* x, int64_t n, int8_t* y, float* y_scale, float* y_zp) {
+    if (n < 1) return -1;
+    float mn = x[0], mx = x[0];
+    for (int64_t i = 1; i < n; i++) {
+        if (x[i] < mn) mn = x[i];
+        if (x[i] > mx) mx = x[i];
+    }
+    double mnd = mn, mxd = mx;
+    if (mnd > 0.0) mnd = 0.0;
+    if (mxd < 0.0) mxd = 0.0;
+    if (mxd - mnd < 0.00000001) mxd = mnd + 0.00000001;
+    const double sc = (mxd - mnd) / 255.0;
+    const int64_t zp = clamp_i64(net_round_to_i64(-mnd / sc), 0, 255);
+    *y_scale = (float)sc;
+    *y_zp = (float)zp;
+    for (int64_t i = 0; i < n; i++) {
+        int64_t q = net_round_to_i64((double)x[i] / sc);
+        q = (q > INT64_MAX - 256 || q < INT64_MIN + 256) ? q : q + zp;
+        q = clamp_i64(q, 0, 255) - 128;
+        y[i] = (int8_t)clamp_i64(q, -128, 127);
+    }
+    return 0;
+}

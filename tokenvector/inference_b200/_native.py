@@ -82,6 +82,16 @@ SIGNATURES = {
     "tvq_session_calibrate": (i32, [i64, P, i32, i32]),
     "tvq_session_forward": (i32, [i64, P, i32, P, i64, i32, P]),
     "tvq_session_logits": (i32, [i64, P, P, P]),
+    "tvq_quantize_linear": (i32, [P, P, i64, i64, i64, P, i64, i64]),
+    "tvq_dequantize_linear": (i32, [P, P, i64, i64, i64, P, i64, i64]),
+    "tvq_matmul_integer": (i32, [P, P, P, i64, i64, i64]),
+    "tvq_qlinear_matmul": (i32, [P, f32, i64, P, f32, i64, f32, i64, P, i64, i64, i64]),
+    "tvq_dynamic_quantize_linear": (i32, [P, i64, P, P, P]),
+    "tvq_dev_quantize_linear": (i32, [P, P, i64, i64, i64, P, i64, i64, P]),
+    "tvq_dev_dequantize_linear": (i32, [P, P, i64, i64, i64, P, i64, i64, P]),
+    "tvq_dev_matmul_integer": (i32, [P, P, P, i64, i64, i64, P]),
+    "tvq_dev_qlinear_matmul": (i32, [P, f32, i64, P, f32, i64, f32, i64, P, i64, i64, i64, P]),
+    "tvq_dev_dynamic_quantize_linear": (i32, [P, i64, P, P, P, P]),
     "tvq_session_launches": (i32, [i64, P]),
     "tvq_session_sync": (i32, [i64]),
     "tvq_session_set_profiling": (i32, [i64, i32]),

@@ -747,3 +747,148 @@ int tvq_dev_gemm_f32x3(const float* A_hi, const float* A_lo, const float* W_hi, 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- ONNX QDQ operators
+// (tv/runtime/session.tkv:1896-2071, 2789-2905)
+
+extern "C" {
+
+int tvq_dev_quantize_linear(const float* x, int8_t* y, int64_t outer, int64_t dim, int64_t inner,
+                            const float* scales_dev, int64_t n_scales, int64_t zero_point, void* stream) {
+    TVQ_CHECK(outer >= 0 && dim >= 0 && inner >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(outer * dim * inner == 0 || (x && y && scales_dev), TVQ_ERR_INVALID, "null buffer");
+    return launch_quantize_linear(x, y, outer, dim, inner, scales_dev, n_scales, zero_point,
+                                  static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_dequantize_linear(const int8_t* x, float* y, int64_t outer, int64_t dim, int64_t inner,
+                              const float* scales_dev, int64_t n_scales, int64_t zero_point, void* stream) {
+    TVQ_CHECK(outer >= 0 && dim >= 0 && inner >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(outer * dim * inner == 0 || (x && y && scales_dev), TVQ_ERR_INVALID, "null buffer");
+    return launch_dequantize_linear(x, y, outer, dim, inner, scales_dev, n_scales, zero_point,
+                                    static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_matmul_integer(const int8_t* a, const int8_t* b, int32_t* y, int64_t m, int64_t k, int64_t n,
+                           void* stream) {
+    TVQ_CHECK(m * n == 0 || (y && (k == 0 || (a && b))), TVQ_ERR_INVALID, "null buffer");
+    return launch_matmul_integer(a, b, y, m, k, n, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_qlinear_matmul(const int8_t* a, float scale_a, int64_t zp_a, const int8_t* b, float scale_b,
+                           int64_t zp_b, float scale_y, int64_t zp_y, int8_t* y, int64_t m, int64_t k, int64_t n,
+                           void* stream) {
+    TVQ_CHECK(m * n == 0 || (y && (k == 0 || (a && b))), TVQ_ERR_INVALID, "null buffer");
+    return launch_qlinear_matmul(a, scale_a, zp_a, b, scale_b, zp_b, scale_y, zp_y, y, m, k, n,
+                                 static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_dynamic_quantize_linear(const float* x, int64_t n, int8_t* y, float* y_scale_dev, float* y_zp_dev,
+                                    void* stream) {
+    TVQ_CHECK(n >= 1, TVQ_ERR_SIZE, "DynamicQuantizeLinear needs at least one element");
+    TVQ_CHECK(x && y && y_scale_dev && y_zp_dev, TVQ_ERR_INVALID, "null buffer");
+    return launch_dynamic_quantize_linear(x, n, y, y_scale_dev, y_zp_dev, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_quantize_linear(const float* x, int8_t* y, int64_t outer, int64_t dim, int64_t inner, const float* scales,
+                        int64_t n_scales, int64_t zero_point) {
+    TVQ_CHECK(outer >= 0 && dim >= 0 && inner >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(n_scales == 1 || n_scales == dim, TVQ_ERR_SIZE, "need one scale or one per channel of the axis");
+    const int64_t n = outer * dim * inner;
+    if (n == 0) return TVQ_OK;
+    TVQ_CHECK(x && y && scales, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    float* dx = dev<float>(H, 0, static_cast<size_t>(n));
+    int8_t* dy = dev<int8_t>(H, 1, static_cast<size_t>(n));
+    float* ds = dev<float>(H, 2, static_cast<size_t>(n_scales));
+    if (H.rc) return H.rc;
+    STEP(H.h2d(dx, x, static_cast<size_t>(n) * 4));
+    STEP(H.h2d(ds, scales, static_cast<size_t>(n_scales) * 4));
+    STEP(launch_quantize_linear(dx, dy, outer, dim, inner, ds, n_scales, zero_point, H.st()));
+    STEP(H.d2h(y, dy, static_cast<size_t>(n)));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_dequantize_linear(const int8_t* x, float* y, int64_t outer, int64_t dim, int64_t inner, const float* scales,
+                          int64_t n_scales, int64_t zero_point) {
+    TVQ_CHECK(outer >= 0 && dim >= 0 && inner >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(n_scales == 1 || n_scales == dim, TVQ_ERR_SIZE, "need one scale or one per channel of the axis");
+    const int64_t n = outer * dim * inner;
+    if (n == 0) return TVQ_OK;
+    TVQ_CHECK(x && y && scales, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    int8_t* dx = dev<int8_t>(H, 0, static_cast<size_t>(n));
+    float* dy = dev<float>(H, 1, static_cast<size_t>(n));
+    float* ds = dev<float>(H, 2, static_cast<size_t>(n_scales));
+    if (H.rc) return H.rc;
+    STEP(H.h2d(dx, x, static_cast<size_t>(n)));
+    STEP(H.h2d(ds, scales, static_cast<size_t>(n_scales) * 4));
+    STEP(launch_dequantize_linear(dx, dy, outer, dim, inner, ds, n_scales, zero_point, H.st()));
+    STEP(H.d2h(y, dy, static_cast<size_t>(n) * 4));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_matmul_integer(const int8_t* a, const int8_t* b, int32_t* y, int64_t m, int64_t k, int64_t n) {
+    TVQ_CHECK(m >= 0 && k >= 0 && n >= 0, TVQ_ERR_INVALID, "negative size");
+    if (m == 0 || n == 0) return TVQ_OK;
+    TVQ_CHECK(y && (k == 0 || (a && b)), TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    int8_t* da = dev<int8_t>(H, 0, static_cast<size_t>(std::max<int64_t>(m * k, 1)));
+    int8_t* db = dev<int8_t>(H, 1, static_cast<size_t>(std::max<int64_t>(k * n, 1)));
+    int32_t* dy = dev<int32_t>(H, 2, static_cast<size_t>(m * n));
+    if (H.rc) return H.rc;
+    if (k > 0) {
+        STEP(H.h2d(da, a, static_cast<size_t>(m * k)));
+        STEP(H.h2d(db, b, static_cast<size_t>(k * n)));
+    }
+    STEP(launch_matmul_integer(da, db, dy, m, k, n, H.st()));
+    STEP(H.d2h(y, dy, static_cast<size_t>(m * n) * 4));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_qlinear_matmul(const int8_t* a, float scale_a, int64_t zp_a, const int8_t* b, float scale_b, int64_t zp_b,
+                       float scale_y, int64_t zp_y, int8_t* y, int64_t m, int64_t k, int64_t n) {
+    TVQ_CHECK(m >= 0 && k >= 0 && n >= 0, TVQ_ERR_INVALID, "negative size");
+    if (m == 0 || n == 0) return TVQ_OK;
+    TVQ_CHECK(y && (k == 0 || (a && b)), TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    int8_t* da = dev<int8_t>(H, 0, static_cast<size_t>(std::max<int64_t>(m * k, 1)));
+    int8_t* db = dev<int8_t>(H, 1, static_cast<size_t>(std::max<int64_t>(k * n, 1)));
+    int8_t* dy = dev<int8_t>(H, 2, static_cast<size_t>(m * n));
+    if (H.rc) return H.rc;
+    if (k > 0) {
+        STEP(H.h2d(da, a, static_cast<size_t>(m * k)));
+        STEP(H.h2d(db, b, static_cast<size_t>(k * n)));
+    }
+    STEP(launch_qlinear_matmul(da, scale_a, zp_a, db, scale_b, zp_b, scale_y, zp_y, dy, m, k, n, H.st()));
+    STEP(H.d2h(y, dy, static_cast<size_t>(m * n)));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_dynamic_quantize_linear(const float* x, int64_t n, int8_t* y, float* y_scale, float* y_zero_point) {
+    TVQ_CHECK(n >= 1, TVQ_ERR_SIZE, "DynamicQuantizeLinear needs at least one element");
+    TVQ_CHECK(x && y && y_scale && y_zero_point, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    float* dx = dev<float>(H, 0, static_cast<size_t>(n));
+    int8_t* dy = dev<int8_t>(H, 1, static_cast<size_t>(n));
+    float* dsz = dev<float>(H, 2, 2);
+    if (H.rc) return H.rc;
+    STEP(H.h2d(dx, x, static_cast<size_t>(n) * 4));
+    STEP(launch_dynamic_quantize_linear(dx, n, dy, dsz, dsz + 1, H.st()));
+    STEP(H.d2h(y, dy, static_cast<size_t>(n)));
+    STEP(H.d2h(y_scale, dsz, 4));
+    STEP(H.d2h(y_zero_point, dsz + 1, 4));
+    return H.finish();
+    TVQ_CATCH
+}
+
+}  // extern "C"

@@ -70,6 +70,7 @@ struct KParams {
     int m, n, k;
     int num_m_blocks, num_n_blocks, num_k_blocks;
     int promote_kb;  // k-blocks per TMEM accumulation unit (GEMM_TF32X3)
+    int acc_only;    // only the raw int32 accumulators (acc_out) are written
     const float* bias;
     const float* residual;
     float* Y;
@@ -385,8 +386,8 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
         float* stage = reinterpret_cast<float*>(smem + C::RING) + (warp - 4) * (32 * E::CH);
         const bool bias_on = p.bias != nullptr;
         const bool per_channel = p.per_channel != 0;
-        const float sa = (KIND == GEMM_TF32X3) ? 1.0f : __ldg(p.scale_a);
-        const float sw0 = (KIND == GEMM_TF32X3) ? 1.0f : __ldg(p.scales_w);
+        const float sa = (KIND == GEMM_TF32X3 || p.acc_only) ? 1.0f : __ldg(p.scale_a);
+        const float sw0 = (KIND == GEMM_TF32X3 || p.acc_only) ? 1.0f : __ldg(p.scales_w);
         InvScale qs{0.0, 0.0f, 0.0f};
         if (p.Yq) qs = make_inv_scale(static_cast<double>(__ldg(p.scale_out)));
         EpiCtx ec{(p.n & 3) == 0, qs};
@@ -503,6 +504,7 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                     for (int j = 0; j < E::CH; j++)
                         if (n0 + j < p.n) dst[j] = static_cast<int32_t>(r[j]);
                 }
+                if (p.acc_only) continue;  // MatMulInteger: the accumulators are the result
                 // fast path for all columns (straight-line), rare f64 fix-ups after
                 float y[E::CH];
                 uint32_t bad = 0;
@@ -578,6 +580,11 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
 __global__ void gemm_k0_kernel(KParams p) {
     griddep_wait();
     const int64_t total = static_cast<int64_t>(p.m) * p.n;
+    if (p.acc_only) {
+        for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
+            p.acc_out[i] = 0;
+        return;
+    }
     const double sa = static_cast<double>(__ldg(p.scale_a));
     double inv_out = 0.0;
     if (p.Yq) {
@@ -700,7 +707,9 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     TVQ_CHECK(g.m < (1ll << 31) && g.n < (1ll << 31) && g.k < 133143, TVQ_ERR_UNSUPPORTED,
               "GEMM size out of range (k must stay below 133143 for exact int32 accumulation)");
     if (g.m == 0 || g.n == 0) return TVQ_OK;
-    TVQ_CHECK(g.kind == GEMM_TF32X3 || (g.scale_a && g.scales_w), TVQ_ERR_INVALID, "scale pointers are required");
+    const bool acc_only = g.kind == GEMM_I8 && g.acc_out && !g.Y && !g.Yq && !g.amax;
+    TVQ_CHECK(g.kind == GEMM_TF32X3 || acc_only || (g.scale_a && g.scales_w), TVQ_ERR_INVALID,
+              "scale pointers are required");
     TVQ_CHECK(g.kind != GEMM_TF32X3 || (!g.Yq && !g.bias && !g.residual && g.act == 0 && g.Y), TVQ_ERR_INVALID,
               "the split fp32 GEMM writes plain f32 Y only");
     TVQ_CHECK(!g.Yq || g.scale_out, TVQ_ERR_INVALID, "int8 output needs scale_out");
@@ -720,7 +729,8 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.acc_out = g.acc_out;
     p.scale_a = g.scale_a;
     p.scales_w = g.scales_w;
-    p.per_channel = g.per_channel;
+    p.per_channel = acc_only ? 0 : g.per_channel;
+    p.acc_only = acc_only ? 1 : 0;
     p.act = g.act;
     p.scale_out = g.scale_out;
     p.amax = g.amax;

@@ -59,4 +59,19 @@ int make_tma_f32_sw128(CUtensorMap* map, const float* ptr, int64_t rows, int64_t
 // x = hi + lo with hi rounded to TF32 precision (10 explicit mantissa bits)
 int launch_split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStream_t st);
 
+// tvq_qdq.cu: the ONNX QDQ operator family (session.tkv:1896-2071, 2789-2905).
+// Quantize / dequantize split the tensor at its axis into (outer, dim, inner);
+// nsc == 1 is per tensor, nsc == dim per channel.  B of the two matmuls is
+// [K, N] row-major as in the reference.
+int launch_quantize_linear(const float* x, int8_t* y, int64_t outer, int64_t dim, int64_t inner, const float* scales,
+                           int64_t nsc, int64_t zp, cudaStream_t st);
+int launch_dequantize_linear(const int8_t* x, float* y, int64_t outer, int64_t dim, int64_t inner,
+                             const float* scales, int64_t nsc, int64_t zp, cudaStream_t st);
+int launch_matmul_integer(const int8_t* a, const int8_t* b, int32_t* y, int64_t m, int64_t k, int64_t n,
+                          cudaStream_t st);
+int launch_qlinear_matmul(const int8_t* a, float sa, int64_t zpa, const int8_t* b, float sw, int64_t zpw, float sy,
+                          int64_t zpy, int8_t* y, int64_t m, int64_t k, int64_t n, cudaStream_t st);
+int launch_dynamic_quantize_linear(const float* x, int64_t n, int8_t* y, float* y_scale, float* y_zp,
+                                   cudaStream_t st);
+
 }  // namespace tvq

@@ -9,8 +9,10 @@ QuantizedGemm node runs the tcgen05 GEMM of libtvq with the node's scale_a and
 scales_w (or scale_b) -- per-channel iff len(scales_w) > 0, the activation
 field ignored, exactly as the reference's branch (session.tkv:678-697).
 
-Only the PTQ path is executable here; other operator types belong to the
-reference's fp32 runtime and raise NotImplementedError.
+Also executable: the ONNX QDQ family (QuantizeLinear, DequantizeLinear,
+QLinearMatMul, MatMulInteger, DynamicQuantizeLinear, session.tkv:1896-2071,
+2789-2905) and the QdqFoldPass graph pass (:3774-3804).  Other operator types
+belong to the reference's fp32 runtime and raise NotImplementedError.
 """
 from __future__ import annotations
 
@@ -56,6 +58,11 @@ OperatorType_Identity = 22
 OperatorType_QuantizeLinear = 63
 OperatorType_DequantizeLinear = 64
 OperatorType_QLinearMatMul = 65
+OperatorType_MatMulInteger = 78
+OperatorType_DynamicQuantizeLinear = 79
+
+QDQ_OPS = (OperatorType_QuantizeLinear, OperatorType_DequantizeLinear, OperatorType_QLinearMatMul,
+           OperatorType_MatMulInteger, OperatorType_DynamicQuantizeLinear)
 
 
 def calc_element_count(shape) -> int:
@@ -119,6 +126,7 @@ class ExecutionNode:
         self.zp_b = 0
         self.zp_y = 0
         self.scales_w: list = []
+        self.qlinear_axis = 1  # session.tkv:550
 
     # session.tkv:3029-3051
     def _m(self) -> int:
@@ -176,6 +184,39 @@ class ExecutionGraph:
         return 0
 
 
+class QdqFoldPass:
+    """session.tkv:3774-3804: a QuantizeLinear whose only output feeds the
+    next node, a DequantizeLinear with one output, is removed together with
+    it; readers of the DequantizeLinear output read the QuantizeLinear input
+    instead (graph outputs too)."""
+
+    def __init__(self, verbose: int = 1):
+        self.verbose = verbose
+
+    def name(self) -> str:
+        return "QdqFoldPass"
+
+    def run(self, graph: "ExecutionGraph") -> int:
+        modified = 0
+        i = 0
+        while i < len(graph.nodes):
+            node = graph.nodes[i]
+            if node.op_type == OperatorType_QuantizeLinear and len(node.outputs) == 1 and i + 1 < len(graph.nodes):
+                nxt = graph.nodes[i + 1]
+                if (nxt.op_type == OperatorType_DequantizeLinear and len(nxt.inputs) > 0
+                        and nxt.inputs[0] == node.outputs[0] and len(nxt.outputs) == 1):
+                    orig, dead = node.inputs[0], nxt.outputs[0]
+                    for nd in graph.nodes:
+                        nd.inputs = [orig if x == dead else x for x in nd.inputs]
+                    graph.outputs = [orig if x == dead else x for x in graph.outputs]
+                    graph.nodes.pop(i + 1)
+                    graph.nodes.pop(i)
+                    modified = 1
+                    continue
+            i += 1
+        return modified
+
+
 class NamedTensor:
     """session.tkv:3376-3387"""
 
@@ -220,6 +261,10 @@ class InferenceSession:
         self.graph = graph
         self.device = torch.device("cuda", device)
         self._disposed = 0
+        if apply_optimizations:
+            # session.tkv:3388-3396; constant folding, operator fusion and
+            # dead-code elimination act on the fp32 operators, outside this path
+            QdqFoldPass(1).run(graph)
         # resolve node tensor descriptors (the reference binds them at graph build)
         for node in graph.nodes:
             node.input_descs = [graph.tensors[n] for n in node.inputs]
@@ -247,9 +292,28 @@ class InferenceSession:
                 v = np.asarray(vals).ravel().astype(np.int64).astype(np.int8)
                 self._view(g.tensors[nm]).copy_(torch.as_tensor(v).view(_torch_dtype(g.tensors[nm].dtype)))
 
+    def _scalar(self, desc: TensorDesc) -> float:
+        """_span0 (session.tkv:25-27): element 0 of a float span."""
+        nm = desc.name
+        if nm in self.graph.initializers:
+            return float(np.asarray(self.graph.initializers[nm], np.float32).ravel()[0])
+        return float(self._view(desc)[:1].cpu().numpy()[0])
+
+    def _axis_split(self, desc: TensorDesc, nsc: int, axis: int):
+        """(outer, dim, inner) at the node's qlinear_axis (session.tkv:1926-1940)."""
+        if nsc == 1:
+            return 1, desc.element_count, 1
+        rank = len(desc.shape)
+        ax = axis if axis >= 0 else axis + rank
+        outer = int(np.prod(desc.shape[:ax])) if ax > 0 else 1
+        inner = int(np.prod(desc.shape[ax + 1:])) if ax + 1 < rank else 1
+        return outer, int(desc.shape[ax]), inner
+
     def _prepare(self, node: ExecutionNode):
         import torch
         if node.op_type == OperatorType_Identity:
+            return None
+        if node.op_type in QDQ_OPS:
             return None
         if node.op_type != OperatorType_QuantizedGemm:
             raise NotImplementedError("operator %d is outside the PTQ path this runtime executes" % node.op_type)
@@ -267,10 +331,46 @@ class InferenceSession:
                    torch.zeros((n, kp), dtype=torch.int8, device=self.device))
         return dict(m=m, n=n, k=k, kp=kp, sa=sa, sw=sw, per_channel=per_channel, pad=pad)
 
+    def _exec_qdq(self, node: ExecutionNode, stream):
+        """The QDQ operator family, session.tkv:1896-2071 and 2789-2905."""
+        ptr = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+        ins, outs = node.input_descs, node.output_descs
+        op = node.op_type
+        if op in (OperatorType_QuantizeLinear, OperatorType_DequantizeLinear):
+            x, sc, y = ins[0], ins[1], outs[0]
+            zp = int(self._scalar(ins[2])) if len(ins) > 2 else 0
+            outer, dim, inner = self._axis_split(x, sc.element_count, node.qlinear_axis)
+            fn = "tvq_dev_quantize_linear" if op == OperatorType_QuantizeLinear else "tvq_dev_dequantize_linear"
+            N.call(fn, ptr(self._view(x)), ptr(self._view(y)), outer, dim, inner, ptr(self._view(sc)),
+                   sc.element_count, zp, stream)
+        elif op in (OperatorType_MatMulInteger, OperatorType_QLinearMatMul):
+            ad = ins[0]
+            bd = ins[1] if op == OperatorType_MatMulInteger else ins[3]
+            m = ad.shape[0] if len(ad.shape) > 0 else 1
+            if op == OperatorType_QLinearMatMul and len(ad.shape) <= 1:
+                m = 1
+            k = ad.shape[1] if len(ad.shape) > 1 else ad.element_count
+            n = bd.shape[1] if len(bd.shape) > 1 else bd.element_count
+            a, b, y = self._view(ad), self._view(bd), self._view(outs[0])
+            if op == OperatorType_MatMulInteger:
+                N.call("tvq_dev_matmul_integer", ptr(a), ptr(b), ptr(y), m, k, n, stream)
+            else:
+                sa, zpa = self._scalar(ins[1]), int(self._scalar(ins[2]))
+                sw, zpw = self._scalar(ins[4]), int(self._scalar(ins[5]))
+                sy, zpy = self._scalar(ins[6]), int(self._scalar(ins[7]))
+                N.call("tvq_dev_qlinear_matmul", ptr(a), sa, zpa, ptr(b), sw, zpw, sy, zpy, ptr(y), m, k, n, stream)
+        else:  # DynamicQuantizeLinear
+            x = ins[0]
+            N.call("tvq_dev_dynamic_quantize_linear", ptr(self._view(x)), x.element_count,
+                   ptr(self._view(outs[0])), ptr(self._view(outs[1])), ptr(self._view(outs[2])), stream)
+
     def _exec(self, node: ExecutionNode, prep):
         import torch
         if node.op_type == OperatorType_Identity:
             self._view(node.output_descs[0]).copy_(self._view(node.input_descs[0]))
+            return
+        if node.op_type in QDQ_OPS:
+            self._exec_qdq(node, C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
             return
         a = self._view(node.input_descs[0])
         w = self._view(node.input_descs[1])
