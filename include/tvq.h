@@ -80,6 +80,26 @@ TVQ_API int tvq_calibrate_minmax(const float* data, int64_t n, int symmetric, fl
 TVQ_API int tvq_calibrate_minmax_batches(const float* const* batches, const int64_t* sizes, int64_t n_batches,
                                  int symmetric, float* scale, int64_t* zero_point, float* min_val,
                                  float* max_val);
+/* calibrate_kl, engine.tkv:42-122 (TensorRT-style KL over a num_bins histogram
+ * of |x|, candidate thresholds every 16 bins from target_bins); symmetric
+ * result.  num_bins <= 4096.  max |x| < 1e-8 returns calibrate_minmax(data, 1). */
+TVQ_API int tvq_calibrate_kl(const float* data, int64_t n, int64_t num_bins, int64_t target_bins, float* scale,
+                             int64_t* zero_point, float* min_val, float* max_val);
+/* calibrate_percentile, engine.tkv:125-162: clip at the percentile of |x|
+ * (exact rank int(min(n-1, percentile/100 n)) of |x|; inputs without NaN);
+ * TVQ_ERR_SIZE (ValueError) for percentile outside (0, 100]. */
+TVQ_API int tvq_calibrate_percentile(const float* data, int64_t n, float percentile, int symmetric, float* scale,
+                                     int64_t* zero_point, float* min_val, float* max_val);
+/* calibrate_mse, engine.tkv:165-197: the threshold am*c/num (c = 1..num, num
+ * >= 4) with the least mean squared quantization error; symmetric result. */
+TVQ_API int tvq_calibrate_mse(const float* data, int64_t n, int64_t num_candidates, float* scale,
+                              int64_t* zero_point, float* min_val, float* max_val);
+/* Device form of calibrate_mse that also writes the per-candidate mean squared
+ * errors (curve_dev[num_candidates], f64) and the result to out4_dev
+ * {scale, zero point, min, max}; *fallback = 1 when max |x| < 1e-8 (then
+ * nothing is written: the reference returns calibrate_minmax). */
+TVQ_API int tvq_dev_calibrate_mse_curve(const float* x, int64_t n, int64_t num_candidates, double* curve_dev,
+                                        float* out4_dev, int* fallback, void* stream);
 /* calibrate_per_channel_minmax(data, rows, cols, 1), engine.tkv:202-213: the
  * per-row symmetric scales (fl32(max|W[r,:]|/127), floor 1e-8). */
 TVQ_API int tvq_calibrate_per_channel_minmax(const float* data, int64_t len, int64_t rows, int64_t cols,

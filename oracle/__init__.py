@@ -89,6 +89,10 @@ def lib():
             "tvo_matmul_integer": (i32, [P, P, P, i64, i64, i64]),
             "tvo_qlinear_matmul": (i32, [P, f32, i64, P, f32, i64, f32, i64, P, i64, i64, i64]),
             "tvo_dynamic_quantize_linear": (i32, [P, i64, P, P, P]),
+            "tvo_calibrate_kl": (QParams, [P, i64, i64, i64]),
+            "tvo_calibrate_percentile": (QParams, [P, i64, f32, i32, P]),
+            "tvo_calibrate_mse": (QParams, [P, i64, i64]),
+            "tvo_calibrate_mse_curve": (None, [P, i64, i64, P]),
             "tvo_num_threads": (i32, []),
             "tvo_set_num_threads": (None, [i32]),
         }
@@ -478,4 +482,34 @@ def dynamic_quantize_linear(x):
     if lib().tvo_dynamic_quantize_linear(_p(x), x.size, _p(y), _p(s), _p(z)) != 0:
         raise ValueError("empty input")
     return y, float(s[0]), float(z[0])
+
+
+# ---------------------------------------------------------------- calibration methods (engine.tkv:42-197)
+def calibrate_kl(data, num_bins: int = 2048, target_bins: int = 128) -> QParams:
+    """calibrate_kl, tv/quantization/engine.tkv:42-122"""
+    d = _f32(data).ravel()
+    return lib().tvo_calibrate_kl(_p(d), d.size, int(num_bins), int(target_bins))
+
+
+def calibrate_percentile(data, percentile: float = 99.99, symmetric: int = 1) -> QParams:
+    """calibrate_percentile, tv/quantization/engine.tkv:125-162"""
+    d = _f32(data).ravel()
+    err = C.c_int(0)
+    r = lib().tvo_calibrate_percentile(_p(d), d.size, float(percentile), int(symmetric), C.byref(err))
+    if err.value:
+        raise ValueError("percentile must be in (0, 100]")
+    return r
+
+
+def calibrate_mse(data, num_candidates: int = 50) -> QParams:
+    """calibrate_mse, tv/quantization/engine.tkv:165-197"""
+    d = _f32(data).ravel()
+    return lib().tvo_calibrate_mse(_p(d), d.size, int(num_candidates))
+
+
+def calibrate_mse_curve(data, num_candidates: int = 50) -> np.ndarray:
+    d = _f32(data).ravel()
+    out = np.empty(num_candidates, np.float64)
+    lib().tvo_calibrate_mse_curve(_p(d), d.size, int(num_candidates), _p(out))
+    return out
 

@@ -806,3 +806,208 @@ TVO_API int tvo_dynamic_quantize_linear(const float* x, int64_t n, int8_t* y, fl
     }
     return 0;
 }
+
+/* ---------------------------------------------------------------------- */
+/* tv/quantization/engine.tkv -- calibration methods (KL, percentile, MSE) */
+/* ---------------------------------------------------------------------- */
+
+/* int() of a non-negative f64 (truncation, saturating, NaN -> 0). */
+static inline int64_t net_trunc_to_i64(double v) {
+    if (isnan(v)) return 0;
+    if (v >= 9.2233720368547758e18) return INT64_MAX;
+    if (v <= -9.2233720368547758e18) return INT64_MIN;
+    return (int64_t)v;
+}
+
+/* max |data[i]| with `a > am` from am = 0 (NaN never wins), f64. */
+static double abs_max(const float* data, int64_t n) {
+    double am = 0.0;
+    for (int64_t i = 0; i < n; i++) {
+        double a = fabs((double)data[i]);
+        if (a > am) am = a;
+    }
+    return am;
+}
+
+/* calibrate_kl, tv/quantization/engine.tkv:42-122: histogram of |x| over
+ * [0, am) in num_bins bins (bin = int(|x| / bw), NaN -> bin 0, the top clamps
+ * to the last bin); for th = target_bins, +16, ..., num_bins the tail is
+ * merged into bin th-1, the truncated distribution normalised, quantized to
+ * target_bins equal-width groups and expanded back, KL(P||Q) summed in bin
+ * order over the bins where both exceed 1e-12; the first strict minimum
+ * wins; threshold = best_th * bw.  All sums in f64, in the reference's order. */
+TVO_API tvo_qparams tvo_calibrate_kl(const float* data, int64_t n, int64_t num_bins, int64_t target_bins) {
+    if (n == 0) return quant_identity();
+    const double am = abs_max(data, n);
+    if (am < 0.00000001) return tvo_calibrate_minmax(data, n, 1);
+    int64_t* hist = (int64_t*)calloc((size_t)num_bins, sizeof(int64_t));
+    double* p = (double*)calloc((size_t)num_bins, sizeof(double));
+    double* q = (double*)calloc((size_t)num_bins, sizeof(double));
+    const double bw = am / (double)num_bins;
+    for (int64_t i = 0; i < n; i++) {
+        int64_t b = net_trunc_to_i64(fabs((double)data[i]) / bw);
+        if (b >= num_bins) b = num_bins - 1;
+        hist[b] += 1;
+    }
+    double total = 0.0;
+    for (int64_t i = 0; i < num_bins; i++) total = total + (double)hist[i];
+    if (total == 0) {
+        free(hist); free(p); free(q);
+        return tvo_calibrate_minmax(data, n, 1);
+    }
+    int64_t best_bin = num_bins;
+    double best_kl = 1e45;
+    for (int64_t th = target_bins; th <= num_bins; th += 16) {
+        double s = 0.0;
+        for (int64_t i = 0; i < th; i++) {
+            p[i] = (double)hist[i];
+            s = s + (double)hist[i];
+        }
+        for (int64_t i = th; i < num_bins; i++) {
+            p[th - 1] = p[th - 1] + (double)hist[i];
+            s = s + (double)hist[i];
+        }
+        if (s != 0) {
+            for (int64_t i = 0; i < th; i++) p[i] = p[i] / s;
+            const int64_t per = th / target_bins;
+            if (per >= 1) {
+                for (int64_t i = 0; i < th; i++) q[i] = 0.0;
+                for (int64_t b = 0; b < target_bins; b++) {
+                    const int64_t start = b * per;
+                    const int64_t end = (b == target_bins - 1) ? th : start + per;
+                    double mass = 0.0;
+                    for (int64_t i = start; i < end; i++) mass = mass + p[i];
+                    int64_t span = end - start;
+                    if (span < 1) span = 1;
+                    const double share = mass / (double)span;
+                    for (int64_t i = start; i < end; i++) q[i] = share;
+                }
+                double kl = 0.0;
+                for (int64_t i = 0; i < th; i++)
+                    if (p[i] > 0.000000000001 && q[i] > 0.000000000001) kl = kl + p[i] * log(p[i] / q[i]);
+                if (kl < best_kl) {
+                    best_kl = kl;
+                    best_bin = th;
+                }
+            }
+        }
+    }
+    free(hist); free(p); free(q);
+    const double thr = (double)best_bin * bw;
+    tvo_qparams r = {(float)(thr / 127.0), 0, (float)(-thr), (float)thr};
+    return r;
+}
+
+static int cmp_f32_asc(const void* a, const void* b) {
+    const float x = *(const float*)a, y = *(const float*)b;
+    return (x > y) - (x < y);
+}
+
+/* calibrate_percentile, tv/quantization/engine.tkv:125-162: clip = the
+ * int(min(n-1, percentile/100 * n))-th smallest |x| (ascending; inputs
+ * without NaN -- the reference's heap sort leaves NaN placement undefined),
+ * floored at 1e-8.  Symmetric: scale clip/127.  Asymmetric: mn / mx start at
+ * data[0] unclamped, then take data[1..] clamped to [-clip, clip].
+ * *err = 1 for percentile outside (0, 100] (the reference's ValueError). */
+TVO_API tvo_qparams tvo_calibrate_percentile(const float* data, int64_t n, float percentile, int symmetric,
+                                             int* err) {
+    *err = 0;
+    if (n == 0) return quant_identity();
+    if (percentile <= 0.0f || percentile > 100.0f) {
+        *err = 1;
+        return quant_identity();
+    }
+    float* ab = (float*)malloc((size_t)n * sizeof(float));
+    for (int64_t i = 0; i < n; i++) ab[i] = fabsf(data[i]);
+    qsort(ab, (size_t)n, sizeof(float), cmp_f32_asc);
+    const double nab = (double)(n - 1 < 0 ? 0 : n - 1);
+    const double want = (double)percentile / 100.0 * (double)n;
+    const int64_t idx = net_trunc_to_i64(nab < want ? nab : want);
+    double clip = ab[idx];
+    free(ab);
+    if (clip <= 0.00000001) clip = 0.00000001;
+    tvo_qparams r;
+    if (symmetric) {
+        r.scale = (float)(clip / 127.0);
+        r.zero_point = 0;
+        r.min_val = (float)(-clip);
+        r.max_val = (float)clip;
+        return r;
+    }
+    double mn = data[0], mx = data[0];
+    for (int64_t i = 1; i < n; i++) {
+        double v = data[i];
+        if (v < -clip) v = -clip;
+        if (v > clip) v = clip;
+        if (v < mn) mn = v;
+        if (v > mx) mx = v;
+    }
+    if (fabs(mx - mn) < 0.00000001) mx = mn + 0.00000001;
+    const double scale = (mx - mn) / 255.0;
+    int64_t zp = net_round_to_i64(-mn / scale) - 128;
+    r.scale = (float)scale;
+    r.zero_point = clamp_i64(zp, -128, 127);
+    r.min_val = (float)mn;
+    r.max_val = (float)mx;
+    return r;
+}
+
+/* calibrate_mse, tv/quantization/engine.tkv:165-197: thresholds am*c/num for
+ * c = 1..num (num >= 4); per threshold the mean of (x - dq)^2 with
+ * dq = clamp(int(round(clamp(x, +-thr) * (1/scale))), -127, 127) * scale,
+ * scale = thr/127; the first strict minimum wins.  Each candidate's sum runs
+ * in element order (candidates in parallel). */
+TVO_API tvo_qparams tvo_calibrate_mse(const float* data, int64_t n, int64_t num_candidates) {
+    if (n == 0) return quant_identity();
+    if (num_candidates < 4) num_candidates = 4;
+    const double am = abs_max(data, n);
+    if (am < 0.00000001) return tvo_calibrate_minmax(data, n, 1);
+    double* mses = (double*)malloc((size_t)num_candidates * sizeof(double));
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t c = 1; c <= num_candidates; c++) {
+        const double thr = am * (double)c / (double)num_candidates;
+        const double scale = thr / 127.0;
+        const double inv = 1.0 / scale;
+        double mse = 0.0;
+        for (int64_t i = 0; i < n; i++) {
+            double cl = data[i];
+            if (cl < -thr) cl = -thr;
+            if (cl > thr) cl = thr;
+            const double dq = (double)clamp_i64(net_round_to_i64(cl * inv), -127, 127) * scale;
+            const double d = (double)data[i] - dq;
+            mse = mse + d * d;
+        }
+        mses[c - 1] = mse / (double)n;
+    }
+    double best_thr = am, best_mse = 1e45;
+    for (int64_t c = 1; c <= num_candidates; c++) {
+        if (mses[c - 1] < best_mse) {
+            best_mse = mses[c - 1];
+            best_thr = am * (double)c / (double)num_candidates;
+        }
+    }
+    free(mses);
+    tvo_qparams r = {(float)(best_thr / 127.0), 0, (float)(-best_thr), (float)best_thr};
+    return r;
+}
+
+/* The per-candidate mean squared errors of calibrate_mse (test support). */
+TVO_API void tvo_calibrate_mse_curve(const float* data, int64_t n, int64_t num_candidates, double* out) {
+    const double am = abs_max(data, n);
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t c = 1; c <= num_candidates; c++) {
+        const double thr = am * (double)c / (double)num_candidates;
+        const double scale = thr / 127.0;
+        const double inv = 1.0 / scale;
+        double mse = 0.0;
+        for (int64_t i = 0; i < n; i++) {
+            double cl = data[i];
+            if (cl < -thr) cl = -thr;
+            if (cl > thr) cl = thr;
+            const double dq = (double)clamp_i64(net_round_to_i64(cl * inv), -127, 127) * scale;
+            const double d = (double)data[i] - dq;
+            mse = mse + d * d;
+        }
+        out[c - 1] = mse / (double)n;
+    }
+}

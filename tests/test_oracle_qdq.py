@@ -100,3 +100,56 @@ def test_qdq_fold_pass():
     g.nodes = g.nodes[:2]
     RS.QdqFoldPass(1).run(g)
     assert g.outputs == ["X"] and g.nodes == []
+
+
+# ---- calibration methods (engine.tkv:42-197) on the oracle
+def _outlier_data(n=50000, seed=0):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal(n).astype(np.float32)
+    x[rng.choice(n, n // 1000, replace=False)] *= 20  # 0.1 % outliers x20 (BASELINE config 3's distribution)
+    return x
+
+
+def test_calibrate_kl_properties():
+    x = _outlier_data()
+    p = O.calibrate_kl(x)
+    am = float(np.abs(x).max())
+    thr = p.max_val
+    assert p.zero_point == 0 and p.min_val == -thr
+    # the threshold is a candidate: th * am / 2048 with th = 128 + 16 j
+    th = thr / (am / 2048)
+    assert abs(th - round(th)) < 1e-3 and (round(th) - 128) % 16 == 0 and 128 <= round(th) <= 2048
+    assert thr < am  # outliers are clipped
+    assert np.float32(thr / 127.0) == np.float32(p.scale)
+    # tiny data -> calibrate_minmax(data, 1)
+    t = np.array([1e-9, -2e-9], np.float32)
+    q, r = O.calibrate_kl(t), O.calibrate_minmax(t, 1)
+    assert (q.scale, q.max_val) == (r.scale, r.max_val)
+    assert O.calibrate_kl(np.zeros(0, np.float32)).scale == 1.0
+
+
+def test_calibrate_percentile_semantics():
+    x = _outlier_data()
+    ab = np.sort(np.abs(x))
+    for pct in (99.99, 99.0, 50.0, 100.0, 0.001):
+        idx = int(min(len(x) - 1, float(np.float32(pct)) / 100.0 * len(x)))
+        p = O.calibrate_percentile(x, pct)
+        assert p.max_val == ab[idx] and p.scale == np.float32(float(ab[idx]) / 127.0)
+    with pytest.raises(ValueError):
+        O.calibrate_percentile(x, 0.0)
+    with pytest.raises(ValueError):
+        O.calibrate_percentile(x, 100.5)
+    # asymmetric: data[0] enters unclamped
+    y = np.array([50.0, 1.0, -1.0, 2.0], np.float32)
+    p = O.calibrate_percentile(y, 50.0, 0)  # clip = the 2nd smallest |y| = 1.0
+    assert p.max_val == 50.0 and p.min_val == -1.0
+
+
+def test_calibrate_mse_properties():
+    x = _outlier_data(20000, 3)
+    p = O.calibrate_mse(x)
+    curve = O.calibrate_mse_curve(x)
+    c = int(np.argmin(curve)) + 1
+    am = float(np.abs(x).max())
+    assert p.max_val == np.float32(am * c / 50)
+    assert O.calibrate_mse(x, 2).max_val == O.calibrate_mse(x, 4).max_val  # at least 4 candidates

@@ -92,6 +92,10 @@ SIGNATURES = {
     "tvq_dev_matmul_integer": (i32, [P, P, P, i64, i64, i64, P]),
     "tvq_dev_qlinear_matmul": (i32, [P, f32, i64, P, f32, i64, f32, i64, P, i64, i64, i64, P]),
     "tvq_dev_dynamic_quantize_linear": (i32, [P, i64, P, P, P, P]),
+    "tvq_calibrate_kl": (i32, [P, i64, i64, i64, P, P, P, P]),
+    "tvq_calibrate_percentile": (i32, [P, i64, f32, i32, P, P, P, P]),
+    "tvq_calibrate_mse": (i32, [P, i64, i64, P, P, P, P]),
+    "tvq_dev_calibrate_mse_curve": (i32, [P, i64, i64, P, P, P, P]),
     "tvq_session_launches": (i32, [i64, P]),
     "tvq_session_sync": (i32, [i64]),
     "tvq_session_set_profiling": (i32, [i64, i32]),

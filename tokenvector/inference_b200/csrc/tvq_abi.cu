@@ -892,3 +892,88 @@ int tvq_dynamic_quantize_linear(const float* x, int64_t n, int8_t* y, float* y_s
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- calibration methods
+// calibrate_kl / _percentile / _mse, tv/quantization/engine.tkv:42-197.
+
+namespace {
+
+int calib_identity(float* scale, int64_t* zp, float* mn, float* mx) {
+    // _quant_identity, engine.tkv:9-10
+    *scale = 1.0f;
+    *zp = 0;
+    *mn = -3.4028234663852886e38f;
+    *mx = 3.4028234663852886e38f;
+    return TVQ_OK;
+}
+
+// run one device calibration on a host array; method 0 KL, 1 percentile, 2 MSE
+int host_calibrate(int method, const float* data, int64_t n, int a0, int a1, float pct, float* scale, int64_t* zp,
+                   float* mn, float* mx) {
+    TVQ_CHECK(scale && zp && mn && mx, TVQ_ERR_INVALID, "null output");
+    if (n == 0) return calib_identity(scale, zp, mn, mx);  // the empty check comes first in all three
+    TVQ_CHECK(n > 0 && data, TVQ_ERR_INVALID, "null data");
+    int fallback = 0;
+    {
+        TVQ_TRY
+        HOST_BEGIN
+        float* dx = dev<float>(H, 0, static_cast<size_t>(n));
+        float* d4 = dev<float>(H, 1, 4);
+        if (H.rc) return H.rc;
+        STEP(H.h2d(dx, data, static_cast<size_t>(n) * 4));
+        if (method == 0) STEP(launch_calibrate_kl(dx, n, a0, a1, d4, &fallback, H.st()));
+        else if (method == 1) STEP(launch_calibrate_percentile(dx, n, pct, a0, d4, H.st()));
+        else STEP(launch_calibrate_mse(dx, n, a0, d4, nullptr, &fallback, H.st()));
+        float o[4] = {0, 0, 0, 0};
+        if (!fallback) STEP(H.d2h(o, d4, 16));
+        const int rc = H.finish();
+        if (rc) return rc;
+        if (!fallback) {
+            *scale = o[0];
+            *zp = static_cast<int64_t>(o[1]);
+            *mn = o[2];
+            *mx = o[3];
+        }
+        TVQ_CATCH
+    }
+    if (fallback) return tvq_calibrate_minmax(data, n, 1, scale, zp, mn, mx);  // max |x| < 1e-8
+    return TVQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tvq_calibrate_kl(const float* data, int64_t n, int64_t num_bins, int64_t target_bins, float* scale,
+                     int64_t* zero_point, float* min_val, float* max_val) {
+    TVQ_CHECK(n >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(num_bins >= 1 && num_bins <= 4096 && target_bins >= 1, TVQ_ERR_UNSUPPORTED,
+              "num_bins must be in [1, 4096] and target_bins >= 1");
+    return host_calibrate(0, data, n, static_cast<int>(num_bins), static_cast<int>(target_bins), 0.0f, scale,
+                          zero_point, min_val, max_val);
+}
+
+int tvq_calibrate_percentile(const float* data, int64_t n, float percentile, int symmetric, float* scale,
+                             int64_t* zero_point, float* min_val, float* max_val) {
+    TVQ_CHECK(n >= 0, TVQ_ERR_INVALID, "negative size");
+    if (n > 0) TVQ_CHECK(percentile > 0.0f && percentile <= 100.0f, TVQ_ERR_SIZE, "percentile must be in (0, 100]");
+    return host_calibrate(1, data, n, symmetric, 0, percentile, scale, zero_point, min_val, max_val);
+}
+
+int tvq_calibrate_mse(const float* data, int64_t n, int64_t num_candidates, float* scale, int64_t* zero_point,
+                      float* min_val, float* max_val) {
+    TVQ_CHECK(n >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(num_candidates <= 65535, TVQ_ERR_UNSUPPORTED, "too many candidates");
+    return host_calibrate(2, data, n, static_cast<int>(num_candidates), 0, 0.0f, scale, zero_point, min_val,
+                          max_val);
+}
+
+int tvq_dev_calibrate_mse_curve(const float* x, int64_t n, int64_t num_candidates, double* curve_dev,
+                                float* out4_dev, int* fallback, void* stream) {
+    TVQ_CHECK(n >= 1 && x && curve_dev && out4_dev && fallback, TVQ_ERR_INVALID, "bad arguments");
+    TVQ_CHECK(num_candidates >= 4 && num_candidates <= 65535, TVQ_ERR_UNSUPPORTED, "4..65535 candidates");
+    return launch_calibrate_mse(x, n, static_cast<int>(num_candidates), out4_dev, curve_dev, fallback,
+                                static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -74,4 +74,14 @@ int launch_qlinear_matmul(const int8_t* a, float sa, int64_t zpa, const int8_t* 
 int launch_dynamic_quantize_linear(const float* x, int64_t n, int8_t* y, float* y_scale, float* y_zp,
                                    cudaStream_t st);
 
+// tvq_calib.cu: calibrate_kl / _percentile / _mse (engine.tkv:42-197).
+// out4 (device) = {scale, zero point, min, max}; *fallback = 1 when max |x| <
+// 1e-8, where the reference returns calibrate_minmax(data, 1) instead.
+int launch_calibrate_kl(const float* x, int64_t n, int num_bins, int target_bins, float* out4, int* fallback,
+                        cudaStream_t st);
+int launch_calibrate_percentile(const float* x, int64_t n, float percentile, int symmetric, float* out4,
+                                cudaStream_t st);
+int launch_calibrate_mse(const float* x, int64_t n, int num_candidates, float* out4, double* curve, int* fallback,
+                         cudaStream_t st);
+
 }  // namespace tvq
