@@ -37,8 +37,9 @@
 //
 // Work items are those of the fp32 kernel (tvq_glue.cu) with 128-row query
 // tiles: tiles[i] = {q0, s0, s1, 0}, split[i] = {key begin, key end, partial
-// slot or -1, 0}; a partial (unnormalised O, m, l) is merged by
-// attention_combine_kernel.
+// slot or -1, merge entry}; the partials (unnormalised O, m, l) of one query
+// tile are merged by the CTA that writes the last of them (a counter per
+// entry and head, reset by that CTA).
 #include <algorithm>
 
 #include "tvq_common.cuh"
@@ -160,6 +161,8 @@ struct AttnParams {
     uint32_t* amax;
     float* part_o;
     float2* part_ml;
+    const int4* comb;  // per merge entry {q0, seq end, first slot, count}; split[i].w = entry of item i
+    int* counters;     // per (entry, head): partials counted in (0 between launches)
     int* err;
 };
 
@@ -453,49 +456,105 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             alive = __all_sync(0xffffffffu, got);
             if (alive) l += lsum[(h ^ 1) * TQ + r];
         }
-        if (alive) {
-            if (part >= 0) {  // unnormalised partial for the combine step
+        // Key-chunk items: write the unnormalised partial (O, m, l); the CTA
+        // that completes the set merges them (the last to count in).
+        bool write_out = part < 0;
+        bool merged = false;
+        if (part >= 0) {
+            if (alive) {
                 const int64_t slot = static_cast<int64_t>(part) * p.nheads + head;
                 float4* dst = reinterpret_cast<float4*>(p.part_o + (slot * TQ + r) * HD + 32 * h);
 #pragma unroll
                 for (int c4 = 0; c4 < 8; c4++)
                     dst[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
                 if (h == 0) p.part_ml[slot * TQ + r] = make_float2(m, l);
-            } else {
-                float am = 0.0f;
-                if (q < s1) {
-                    const float il = 1.0f / l;
-                    const int64_t base = static_cast<int64_t>(q) * p.d + head * HD + 32 * h;
+            }
+            __threadfence();
+            named_bar_sync(1, 256);  // all eight softmax warps wrote their part
+            int* last_flag = reinterpret_cast<int*>(lsum);  // lsum is free again (both halves read it)
+            if (threadIdx.x == 128) {
+                int* ctr = p.counters + static_cast<int64_t>(sp.w) * p.nheads + head;
+                const int prev = atomicAdd(ctr, 1);
+                const int last = (prev == p.comb[sp.w].w - 1) ? 1 : 0;
+                if (last) *ctr = 0;  // every other part has counted in: ready for the next launch
+                last_flag[TQ * 2 - 1] = last;
+            }
+            named_bar_sync(1, 256);
+            write_out = merged = last_flag[TQ * 2 - 1] != 0;
+            if (merged) __threadfence();  // the other CTAs' partials are visible from here
+        }
+        if (write_out && alive) {
+            float am = 0.0f;
+            if (merged) {
+                // m = max m_c, l = sum l_c 2^(m_c - m), O = sum O_c 2^(m_c - m) / l, in slot order
+                const int4 ce = p.comb[sp.w];  // {q0, seq end, first slot, count}
+                float mm = -INFINITY;
+                for (int k = 0; k < ce.w; k++) {
+                    const int slot_k = ce.z + k;
+                    const float mk = (slot_k == part)
+                                         ? m
+                                         : p.part_ml[(static_cast<int64_t>(slot_k) * p.nheads + head) * TQ + r].x;
+                    mm = fmaxf(mm, mk);
+                }
+                float lt = 0.0f, acc[32];
 #pragma unroll
-                    for (int c = 0; c < 32; c++) {
-                        o[c] = o[c] * il;
-                        am = fmaxf(am, fabsf(o[c]));
-                    }
-                    if (p.out) {
-                        float4* dst = reinterpret_cast<float4*>(p.out + base);
+                for (int c = 0; c < 32; c++) acc[c] = 0.0f;
+                for (int k = 0; k < ce.w; k++) {
+                    const int slot_k = ce.z + k;
+                    const int64_t sl = static_cast<int64_t>(slot_k) * p.nheads + head;
+                    const float2 ml = (slot_k == part) ? make_float2(m, l) : p.part_ml[sl * TQ + r];
+                    const float wgt = (ml.x == -INFINITY) ? 0.0f : exp2f(ml.x - mm);
+                    lt = fmaf(ml.y, wgt, lt);
+                    if (slot_k == part) {
 #pragma unroll
-                        for (int c4 = 0; c4 < 8; c4++)
-                            dst[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
-                    }
-                    if (p.outq) {
-                        const InvScale qs = make_inv_scale(static_cast<double>(__ldg(p.qscale)));
-                        char4* dst = reinterpret_cast<char4*>(p.outq + base);
+                        for (int c = 0; c < 32; c++) acc[c] = fmaf(o[c], wgt, acc[c]);
+                    } else {
+                        const float4* src = reinterpret_cast<const float4*>(p.part_o + (sl * TQ + r) * HD + 32 * h);
 #pragma unroll
                         for (int c4 = 0; c4 < 8; c4++) {
-                            char4 v;
-                            v.x = quant_exact(o[4 * c4], qs);
-                            v.y = quant_exact(o[4 * c4 + 1], qs);
-                            v.z = quant_exact(o[4 * c4 + 2], qs);
-                            v.w = quant_exact(o[4 * c4 + 3], qs);
-                            dst[c4] = v;
+                            const float4 v = src[c4];
+                            acc[4 * c4] = fmaf(v.x, wgt, acc[4 * c4]);
+                            acc[4 * c4 + 1] = fmaf(v.y, wgt, acc[4 * c4 + 1]);
+                            acc[4 * c4 + 2] = fmaf(v.z, wgt, acc[4 * c4 + 2]);
+                            acc[4 * c4 + 3] = fmaf(v.w, wgt, acc[4 * c4 + 3]);
                         }
                     }
                 }
-                if (p.amax) {
 #pragma unroll
-                    for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
-                    if (lane == 0) atomicMax(p.amax, __float_as_uint(am));
+                for (int c = 0; c < 32; c++) o[c] = acc[c] / lt;
+            } else {
+                const float il = 1.0f / l;
+#pragma unroll
+                for (int c = 0; c < 32; c++) o[c] = o[c] * il;
+            }
+            if (q < s1) {
+                const int64_t base = static_cast<int64_t>(q) * p.d + head * HD + 32 * h;
+#pragma unroll
+                for (int c = 0; c < 32; c++) am = fmaxf(am, fabsf(o[c]));
+                if (p.out) {
+                    float4* dst = reinterpret_cast<float4*>(p.out + base);
+#pragma unroll
+                    for (int c4 = 0; c4 < 8; c4++)
+                        dst[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
                 }
+                if (p.outq) {
+                    const InvScale qs = make_inv_scale(static_cast<double>(__ldg(p.qscale)));
+                    char4* dst = reinterpret_cast<char4*>(p.outq + base);
+#pragma unroll
+                    for (int c4 = 0; c4 < 8; c4++) {
+                        char4 v;
+                        v.x = quant_exact(o[4 * c4], qs);
+                        v.y = quant_exact(o[4 * c4 + 1], qs);
+                        v.z = quant_exact(o[4 * c4 + 2], qs);
+                        v.w = quant_exact(o[4 * c4 + 3], qs);
+                        dst[c4] = v;
+                    }
+                }
+            }
+            if (p.amax) {
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+                if (lane == 0) atomicMax(p.amax, __float_as_uint(am));
             }
         }
     }
@@ -532,7 +591,7 @@ int launch_split_kv(const float* qkv, int T, int d, float* kh, float* kl, float*
 int launch_attention_tc(const float* qkv, const float* kh, const float* kl, const float* vth, const float* vtl, int T,
                         const int4* tiles, const int4* split, int nitems, const int4* comb, int ncomb, int d,
                         int nheads, float* out, int8_t* outq, const float* qscale, uint32_t* amax, float* part_o,
-                        float2* part_ml, cudaStream_t st) {
+                        float2* part_ml, int* counters, cudaStream_t st) {
     if (nitems <= 0) return TVQ_OK;
     TVQ_CHECK(nheads > 0 && d == nheads * HD, TVQ_ERR_UNSUPPORTED, "the tensor-core attention needs head dim 64");
     TVQ_CHECK(split && kh && kl && vth && vtl, TVQ_ERR_INVALID,
@@ -572,11 +631,12 @@ int launch_attention_tc(const float* qkv, const float* kh, const float* kl, cons
     p.part_o = part_o;
     p.part_ml = part_ml;
     p.err = ds->d_error;
-    rc = launch_pdl(attention_tc_kernel, dim3(nitems * nheads), dim3(NTHREADS), SMEM_BYTES, st, mkh, mkl, mvh, mvl, p);
-    if (rc) return rc;
-    if (ncomb > 0) return launch_attention_combine(comb, ncomb, d, nheads, TQ, part_o, part_ml, out, outq, qscale,
-                                                   amax, st);
-    return TVQ_OK;
+    TVQ_CHECK(ncomb == 0 || (comb && counters), TVQ_ERR_INVALID, "key-chunk items need merge entries and counters");
+    p.comb = comb;
+    p.counters = counters;
+    // key-chunk partials are merged inside the kernel by the last CTA of each set
+    return launch_pdl(attention_tc_kernel, dim3(nitems * nheads), dim3(NTHREADS), SMEM_BYTES, st, mkh, mkl, mvh, mvl,
+                      p);
 }
 
 }  // namespace tvq

@@ -83,7 +83,22 @@ struct KParams {
     const float* scale_out;
     uint32_t* amax;
     int* err;
+    // Optional attention operands of a c_attn GEMM (Y = qkv [m, 3 kvd]): the K
+    // columns [kvd, 2 kvd) also as TF32 hi / lo [m, kvd] (kh, kl) and the V
+    // columns [2 kvd, 3 kvd) transposed as hi / lo [kvd, vt_pitch] (vth, vtl).
+    float *kh, *kl, *vth, *vtl;
+    int kvd, vt_pitch;
 };
+
+// nearest TF32 value (10 explicit mantissa bits), ties away from zero: the
+// hi / lo split x = hi + lo of the attention operands (lo again rounded)
+__device__ __forceinline__ float round_tf32_e(float v) {
+    const uint32_t u = __float_as_uint(v);
+    if ((u & 0x7F800000u) == 0x7F800000u) return v;
+    float h = __uint_as_float((u + 0x1000u) & 0xFFFFE000u);
+    if ((__float_as_uint(h) & 0x7F800000u) == 0x7F800000u) h = __uint_as_float(u & 0xFFFFE000u);
+    return h;
+}
 
 __device__ __forceinline__ float gelu_tanh_f32(float x) {
     // apply_activation GELU, tv/optimization/kernels.tkv:22-24 + _tanh :32-38
@@ -179,6 +194,16 @@ __device__ __forceinline__ void stage_and_store(const KParams& p, const EpiCtx& 
         float4 v = *reinterpret_cast<const float4*>(&stage[rr * E::CH + 4 * (c4 ^ ((rr >> E::SWS) & (E::LPR - 1)))]);
         if (row >= p.m || col >= p.n) continue;
         const int64_t off = static_cast<int64_t>(row) * p.n + col;
+        if (p.kh && col >= p.kvd && col < 2 * p.kvd) {  // K part: hi / lo split, row-major [m, kvd]
+            const int64_t ko = static_cast<int64_t>(row) * p.kvd + (col - p.kvd);
+            float4 h, l;
+            h.x = round_tf32_e(v.x); l.x = round_tf32_e(__fsub_rn(v.x, h.x));
+            h.y = round_tf32_e(v.y); l.y = round_tf32_e(__fsub_rn(v.y, h.y));
+            h.z = round_tf32_e(v.z); l.z = round_tf32_e(__fsub_rn(v.z, h.z));
+            h.w = round_tf32_e(v.w); l.w = round_tf32_e(__fsub_rn(v.w, h.w));
+            *reinterpret_cast<float4*>(p.kh + ko) = h;
+            *reinterpret_cast<float4*>(p.kl + ko) = l;
+        }
         if (e.vec_ok && col + 3 < p.n) {
             if (p.residual) {
                 const float4 t = res[it];
@@ -539,6 +564,17 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                         }
                     }
                 }
+                if (p.vth && n0 >= 2 * p.kvd && row0 + lane < p.m) {
+                    // V part, transposed: column n0 + j -> row of V^T; lanes
+                    // (consecutive tokens) write consecutive addresses
+                    const int64_t vo = static_cast<int64_t>(n0 - 2 * p.kvd) * p.vt_pitch + row0 + lane;
+#pragma unroll
+                    for (int j = 0; j < E::CH; j++) {
+                        const float h = round_tf32_e(y[j]);
+                        p.vth[vo + static_cast<int64_t>(j) * p.vt_pitch] = h;
+                        p.vtl[vo + static_cast<int64_t>(j) * p.vt_pitch] = round_tf32_e(__fsub_rn(y[j], h));
+                    }
+                }
                 if (p.act == TVQ_ACT_GELU_ERF) {
 #pragma unroll
                     for (int j = 0; j < E::CH; j++) y[j] = gelu_erf_f32(y[j]);
@@ -730,6 +766,12 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.scale_a = g.scale_a;
     p.scales_w = g.scales_w;
     p.per_channel = acc_only ? 0 : g.per_channel;
+    p.kh = g.kh;
+    p.kl = g.kl;
+    p.vth = g.vth;
+    p.vtl = g.vtl;
+    p.kvd = g.kvd;
+    p.vt_pitch = g.vt_pitch;
     p.acc_only = acc_only ? 1 : 0;
     p.act = g.act;
     p.scale_out = g.scale_out;
@@ -761,6 +803,9 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
               "residual must be 16-byte aligned");
     TVQ_CHECK(!g.Yq || (reinterpret_cast<uintptr_t>(g.Yq) & 15) == 0, TVQ_ERR_UNSUPPORTED,
               "Yq must be 16-byte aligned");
+    TVQ_CHECK(!g.kh || (g.kind == GEMM_I8 && g.kl && g.vth && g.vtl && g.Y && g.n == 3 * g.kvd && g.kvd % 16 == 0 &&
+                        g.vt_pitch >= g.m && g.act == 0 && !g.residual),
+              TVQ_ERR_INVALID, "attention operand split needs an INT8 qkv GEMM with N = 3 kvd");
     rc = get_encoder();
     if (rc) return rc;
 

@@ -34,7 +34,7 @@ int launch_split_kv(const float* qkv, int T, int d, float* kh, float* kl, float*
 int launch_attention_tc(const float* qkv, const float* kh, const float* kl, const float* vth, const float* vtl, int T,
                         const int4* tiles, const int4* split, int nitems, const int4* comb, int ncomb, int d,
                         int nheads, float* out, int8_t* outq, const float* qscale, uint32_t* amax, float* part_o,
-                        float2* part_ml, cudaStream_t st);
+                        float2* part_ml, int* counters, cudaStream_t st);
 int launch_scale_from_amax(const uint32_t* amax, float* scale, int n, cudaStream_t st);
 int launch_transpose(const float* a, float* b, int rows, int cols, cudaStream_t st);
 int launch_token_seg(const int* seg, int nseg, int* tok_start, cudaStream_t st);

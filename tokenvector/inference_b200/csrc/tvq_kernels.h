@@ -49,6 +49,10 @@ struct GemmArgs {
     const float* scale_out = nullptr; // device [1], needed with Yq
     uint32_t* amax = nullptr;         // device [1] or null
     int force_bn = 0;                 // 0 = heuristic, else 64/128/256
+    // c_attn only: also write K [m, kvd] and V^T [kvd, vt_pitch] of qkv as
+    // TF32 hi / lo (the tensor-core attention's operands)
+    float *kh = nullptr, *kl = nullptr, *vth = nullptr, *vtl = nullptr;
+    int kvd = 0, vt_pitch = 0;
 };
 int launch_gemm(const GemmArgs& g, cudaStream_t st);
 // Tensor map of a row-major f32 matrix [rows, cols] (row pitch `pitch`

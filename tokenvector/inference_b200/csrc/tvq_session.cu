@@ -61,7 +61,8 @@ struct Session {
     int4* comb = nullptr;    // partial merges {q0, seq end, first slot, count}
     float* part_o = nullptr;
     float2* part_ml = nullptr;
-    size_t tiles_cap = 0, split_cap = 0, comb_cap = 0, part_o_cap = 0, part_ml_cap = 0;
+    int* counters = nullptr;  // per (merge entry, head): key-chunk partials counted in
+    size_t tiles_cap = 0, split_cap = 0, comb_cap = 0, part_o_cap = 0, part_ml_cap = 0, counters_cap = 0;
     int ncomb = 0;
     bool attn_tc = false;  // head dim 64: tensor-core attention, 128-row query tiles
     int attn_rows = 64;
@@ -147,8 +148,16 @@ void lin_shape(const Session& s, int which, int* n, int* k) {
 }
 
 int gemm(Session& s, const int8_t* A, const Lin& l, const float* scale_a, float* Y, const float* residual,
-         int8_t* Yq, const float* scale_out, uint32_t* amax, int act) {
+         int8_t* Yq, const float* scale_out, uint32_t* amax, int act, bool kv_split = false) {
     GemmArgs g;
+    if (kv_split) {  // c_attn on the tensor-core attention path: K and V^T operands from the epilogue
+        g.kh = s.kh;
+        g.kl = s.kl;
+        g.vth = s.vh;
+        g.vtl = s.vl;
+        g.kvd = s.d;
+        g.vt_pitch = attention_tc_pitch(s.T);
+    }
     g.kind = GEMM_I8;
     g.A = A;
     g.W = l.W;
@@ -169,10 +178,9 @@ int gemm(Session& s, const int8_t* A, const Lin& l, const float* scale_a, float*
 }
 
 int attention(Session& s, float* out, int8_t* outq, const float* qscale, uint32_t* amax) {
-    if (s.attn_tc) {
-        STEP(launch_split_kv(s.qkv, s.T, s.d, s.kh, s.kl, s.vh, s.vl, s.st));
+    if (s.attn_tc) {  // K / V^T hi-lo come from the c_attn epilogue
         return launch_attention_tc(s.qkv, s.kh, s.kl, s.vh, s.vl, s.T, s.tiles, s.split, s.ntiles, s.comb, s.ncomb,
-                                   s.d, s.heads, out, outq, qscale, amax, s.part_o, s.part_ml, s.st);
+                                   s.d, s.heads, out, outq, qscale, amax, s.part_o, s.part_ml, s.counters, s.st);
     }
     return launch_attention_split(s.qkv, s.tiles, s.split, s.ntiles, s.comb, s.ncomb, s.d, s.heads, out, outq, qscale,
                                   amax, s.part_o, s.part_ml, s.st);
@@ -197,6 +205,8 @@ int mark(Session& s, int stage) {
 int enqueue_forward(Session& s, bool calibrating) {
     const int T = s.T, d = s.d;
     STEP(mark(s, -1));
+    if (s.attn_tc && s.ncomb > 0)  // merge counters start at 0 (a run that stopped early may leave them set)
+        TVQ_CUDA(cudaMemsetAsync(s.counters, 0, sizeof(int) * static_cast<size_t>(s.ncomb) * s.heads, s.st));
     STEP(launch_embed(s.ids, s.tok_start, s.wte, s.wpe, s.x, T, d, s.vocab, s.max_pos, s.err, s.st));
     STEP(mark(s, ST_EMBED));
     for (int l = 0; l < s.layers; l++) {
@@ -213,7 +223,7 @@ int enqueue_forward(Session& s, bool calibrating) {
         }
         STEP(mark(s, ST_LN));
         // c_attn: qkv = dequant(aq Wqkv) + b
-        STEP(gemm(s, s.aq, w.lin[0], sc + 0, s.qkv, nullptr, nullptr, nullptr, nullptr, TVQ_ACT_NONE));
+        STEP(gemm(s, s.aq, w.lin[0], sc + 0, s.qkv, nullptr, nullptr, nullptr, nullptr, TVQ_ACT_NONE, s.attn_tc));
         STEP(mark(s, ST_GEMM_QKV));
         // causal attention -> int8 context (attn c_proj input)
         if (calibrating) {
@@ -587,7 +597,8 @@ int tvq_session_prepare(int64_t handle, const int64_t* seg, int64_t n_seg, int l
                 const int first = nparts;
                 int nch = 0;
                 for (int kb = static_cast<int>(a); kb < kend; kb += kKeyChunk, nch++)
-                    items.push_back({tile, make_int4(kb, std::min(kb + kKeyChunk, kend), nparts++, 0),
+                    items.push_back({tile, make_int4(kb, std::min(kb + kKeyChunk, kend), nparts++,
+                                                     static_cast<int>(comb.size())),
                                      std::min(kKeyChunk, kend - kb)});
                 comb.push_back(make_int4(static_cast<int>(q0), static_cast<int>(b), first, nch));
             }
@@ -620,6 +631,8 @@ int tvq_session_prepare(int64_t handle, const int64_t* seg, int64_t n_seg, int l
     const size_t slots = static_cast<size_t>(std::max(nparts, 1)) * S->heads * QT;
     STEP(grow(&S->part_o, S->part_o_cap, slots * (S->d / S->heads)));
     STEP(grow(&S->part_ml, S->part_ml_cap, slots));
+    STEP(grow(&S->counters, S->counters_cap, std::max<size_t>(comb.size(), 1) * S->heads));
+    TVQ_CUDA(cudaMemset(S->counters, 0, sizeof(int) * std::max<size_t>(comb.size(), 1) * S->heads));
     TVQ_CUDA(cudaMemcpy(S->seg, sh.data(), sizeof(int) * sh.size(), cudaMemcpyHostToDevice));
     TVQ_CUDA(cudaMemcpy(S->tok_start, tok.data(), sizeof(int) * tok.size(), cudaMemcpyHostToDevice));
     TVQ_CUDA(cudaMemcpy(S->tiles, tiles.data(), sizeof(int4) * tiles.size(), cudaMemcpyHostToDevice));
@@ -783,7 +796,7 @@ int tvq_dev_attention(const float* qkv, const int64_t* seg, int64_t n_seg, int64
         if (!r)
             r = launch_attention_tc(qkv, kv, kv + n4, kv + 2 * n4, kv + 3 * n4, T, tiles_dev, tiles_dev + n,
                                     static_cast<int>(n), nullptr, 0, static_cast<int>(d), static_cast<int>(n_heads), out,
-                                    outq, qscale_dev, amax_dev, nullptr, nullptr, st);
+                                    outq, qscale_dev, amax_dev, nullptr, nullptr, nullptr, st);
         cudaError_t e = cudaFreeAsync(kv, st);
         if (!r && e != cudaSuccess) return cuda_fail(e, "cudaFreeAsync");
         return r;
