@@ -211,6 +211,25 @@ TVQ_API int tvq_dev_gemm_f32x3(const float* A_hi, const float* A_lo, const float
  * tf32(x - hi), |x - hi - lo| <= 2^-22 |x|. */
 TVQ_API int tvq_dev_split_tf32(const float* x, float* hi, float* lo, int64_t n, void* stream);
 
+/* fp32 GEMM Y[m,n] = A[m,k] W[n,k]^T on the FP16 tensor cores (kind::f16):
+ * each row of A and of W is split by tvq_dev_split_f16_rows into fp16
+ * high + low parts under a power-of-two row scale, Y accumulates xh*wh +
+ * xh*wl + xl*wh in f32 and the epilogue multiplies by A_rscale[m] *
+ * W_rscale[n] (exact).  Twice the K per instruction and half the operand
+ * bytes of tvq_dev_gemm_f32x3 at the same accuracy.  k must be a multiple
+ * of 8 and all pointers 16-byte aligned.  Used for the tied LM head
+ * (gpt2_ref.tkv:603-610). */
+TVQ_API int tvq_dev_gemm_f16x3(const void* A_hi, const void* A_lo, const float* A_rscale, const void* W_hi,
+                               const void* W_lo, const float* W_rscale, float* Y, int64_t m, int64_t n, int64_t k,
+                               void* stream);
+/* Row-scaled fp16 split of x [rows, k] (f32): per row the power of two s
+ * with max|x| * s in [2^14, 2^15), hi = fp16(x*s), lo = fp16(x*s - hi)
+ * (fp16 bit patterns, [rows, k] each), rscale[row] = 1/s (1 for k = 0).
+ * |x*s - hi - lo| <= max(2^-22 |x*s|, 2^-25).  A row with Inf or NaN gets
+ * s = 1. */
+TVQ_API int tvq_dev_split_f16_rows(const float* x, void* hi, void* lo, float* rscale, int64_t rows, int64_t k,
+                                   void* stream);
+
 /* ================================================================ fp32 glue, device buffers
  * gpt2_layernorm, tv/training/gpt2_ref.tkv:50-78 (f64 statistics): y (f32)
  * and/or q = int8 with the static scale qscale_dev[0]; amax_dev records

@@ -247,3 +247,74 @@ def test_split_tf32_gemm_is_fp32_accurate(m, n, k):
     e32 = np.abs(t32 - ref)
     assert np.all(err <= mag * 2.0 ** -18 + 1e-30), float((err / (mag + 1e-30)).max())
     assert err.max() <= 4.0 * e32.max() + 1e-12, (err.max(), e32.max())
+
+
+def _split_f16(t):
+    """Row-scaled fp16 split through the C-ABI: (hi, lo, rscale)."""
+    import torch
+    from tokenvector.inference_b200.quantization import _buf as B
+    rows, k = t.shape
+    hi = torch.empty((rows, k), dtype=torch.float16, device=t.device)
+    lo = torch.empty_like(hi)
+    rs = torch.empty((rows,), dtype=torch.float32, device=t.device)
+    N.call("tvq_dev_split_f16_rows", B.ptr(t), B.ptr(hi), B.ptr(lo), B.ptr(rs), rows, k, None)
+    return hi, lo, rs
+
+
+def test_split_f16_rows_represents_rows_to_2e22():
+    """hi + lo under the row's power-of-two scale: the largest |x*s| sits in
+    [2^14, 2^15), |x*s - hi - lo| <= max(2^-22 |x*s|, 2^-25); zero rows get
+    scale 1; rows of very different magnitude get their own scales."""
+    import torch
+    rng = np.random.default_rng(7)
+    X = rng.standard_normal((64, 200)).astype(np.float32)
+    X[1] *= 1e-20
+    X[2] *= 1e20
+    X[3] = 0.0
+    X[4, 5] = 3.0e38
+    X[5] = np.ldexp(rng.standard_normal(200), rng.integers(-60, 1, 200)).astype(np.float32)
+    t = torch.from_numpy(X).cuda()
+    hi, lo, rs = _split_f16(t)
+    torch.cuda.synchronize()
+    s = 1.0 / rs.double().cpu().numpy()
+    xs = X.astype(np.float64) * s[:, None]
+    h, l = hi.double().cpu().numpy(), lo.double().cpu().numpy()
+    assert np.all(np.abs(xs - h - l) <= np.maximum(np.abs(xs) * 2.0 ** -22, 2.0 ** -25))
+    mx = np.abs(xs).max(axis=1)
+    nz = mx > 0
+    assert np.all((mx[nz] >= 2.0 ** 14) & (mx[nz] < 2.0 ** 15))
+    assert s[3] == 1.0
+    assert np.all(np.log2(s) == np.round(np.log2(s)))
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 50257, 768), (37, 1000, 64), (1024, 4096, 768), (130, 300, 1600),
+                                   (200, 129, 8)])
+def test_f16_split_gemm_is_fp32_accurate(m, n, k):
+    """The LM head's fp32 GEMM on the FP16 tensor cores (row-scaled fp16
+    hi/lo split, 3 products, power-of-two scales undone in the epilogue):
+    |error| <= 2^-18 * sum_k |a_k w_k| per output against a float64
+    reference, and within 4x the max error of torch's true-fp32 (non-TF32)
+    matmul on the same data.  Rows of A span 2^-30..2^30 in magnitude."""
+    import torch
+    torch.backends.cuda.matmul.allow_tf32 = False
+    rng = np.random.default_rng(m + n + k)
+    A = rng.standard_normal((m, k)).astype(np.float32)
+    A *= np.ldexp(1.0, rng.integers(-30, 31, (m, 1))).astype(np.float32)
+    W = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    dev = torch.device("cuda:0")
+    tA, tW = torch.from_numpy(A).to(dev), torch.from_numpy(W).to(dev)
+    ah, al, ar = _split_f16(tA)
+    wh, wl, wr = _split_f16(tW)
+    from tokenvector.inference_b200.quantization import _buf as B
+    Y = torch.empty((m, n), dtype=torch.float32, device=dev)
+    N.call("tvq_dev_gemm_f16x3", B.ptr(ah), B.ptr(al), B.ptr(ar), B.ptr(wh), B.ptr(wl), B.ptr(wr), B.ptr(Y),
+           m, n, k, None)
+    torch.cuda.synchronize()
+    ref = A.astype(np.float64) @ W.astype(np.float64).T
+    mag = np.abs(A).astype(np.float64) @ np.abs(W).astype(np.float64).T
+    err = np.abs(Y.cpu().numpy().astype(np.float64) - ref)
+    t32 = (tA @ tW.T).cpu().numpy().astype(np.float64)
+    e32 = np.abs(t32 - ref) / (mag + 1e-300)
+    rel = err / (mag + 1e-300)
+    assert np.all(rel <= 2.0 ** -18), float(rel.max())
+    assert rel.max() <= 4.0 * e32.max() + 1e-12, (rel.max(), e32.max())

@@ -66,6 +66,8 @@ SIGNATURES = {
     "tvq_dev_gemm": (i32, [i32, P, P, P, P, P, P, i64, i64, i64, P, P, i32, i32, P, P, P]),
     "tvq_dev_gemm_f32x3": (i32, [P, P, P, P, P, i64, i64, i64, P]),
     "tvq_dev_split_tf32": (i32, [P, P, P, i64, P]),
+    "tvq_dev_gemm_f16x3": (i32, [P, P, P, P, P, P, P, i64, i64, i64, P]),
+    "tvq_dev_split_f16_rows": (i32, [P, P, P, P, i64, i64, P]),
     "tvq_dev_layernorm": (i32, [P, P, P, P, P, P, P, i64, i64, C.c_double, P]),
     "tvq_dev_attention": (i32, [P, P, i64, i64, i64, P, i64, P, P, P, P, P]),
     "tvq_dev_attention_noalloc": (i32, [P, P, i64, i64, i64, P, P, P, P, P]),

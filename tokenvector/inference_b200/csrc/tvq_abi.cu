@@ -746,6 +746,35 @@ int tvq_dev_gemm_f32x3(const float* A_hi, const float* A_lo, const float* W_hi, 
     TVQ_CATCH
 }
 
+int tvq_dev_split_f16_rows(const float* x, void* hi, void* lo, float* rscale, int64_t rows, int64_t k, void* stream) {
+    TVQ_CHECK(rows >= 0 && k >= 0, TVQ_ERR_INVALID, "negative size");
+    if (rows == 0) return TVQ_OK;
+    TVQ_CHECK(rscale && (k == 0 || (x && hi && lo)), TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    return launch_split_f16_rows(x, hi, lo, rscale, rows, k, static_cast<cudaStream_t>(stream));
+    TVQ_CATCH
+}
+
+int tvq_dev_gemm_f16x3(const void* A_hi, const void* A_lo, const float* A_rscale, const void* W_hi, const void* W_lo,
+                       const float* W_rscale, float* Y, int64_t m, int64_t n, int64_t k, void* stream) {
+    TVQ_CHECK(Y && A_hi && A_lo && A_rscale && W_hi && W_lo && W_rscale, TVQ_ERR_INVALID, "null buffer");
+    GemmArgs g;
+    g.kind = GEMM_F16X3;
+    g.A = A_hi;
+    g.A2 = A_lo;
+    g.W = W_hi;
+    g.W2 = W_lo;
+    g.scale_a = A_rscale;
+    g.scales_w = W_rscale;
+    g.Y = Y;
+    g.m = m;
+    g.n = n;
+    g.k = k;
+    TVQ_TRY
+    return launch_gemm(g, static_cast<cudaStream_t>(stream));
+    TVQ_CATCH
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------- ONNX QDQ operators

@@ -25,6 +25,7 @@
 // bounded (tvq_common.cuh); on a timeout the kernel records an error code,
 // drains its own TMA loads and MMAs, frees TMEM and returns.
 #include <cudaTypedefs.h>
+#include <cuda_fp16.h>
 
 #include <cstdlib>
 #include <mutex>
@@ -56,8 +57,10 @@ struct Epi {
     static constexpr int RPI = 32 / LPR;           // rows per store iteration
     static constexpr int SWS = (CH == 16) ? 1 : 2; // staging swizzle: slot j of row r at j ^ ((r >> SWS) & (LPR - 1))
 };
+// the split-precision fp32 GEMMs: hi / lo operand parts, three products
+__host__ __device__ constexpr bool split_kind(int kind) { return kind == GEMM_TF32X3 || kind == GEMM_F16X3; }
 template <int KIND>
-using EpiOf = Epi<(KIND == GEMM_TF32X3) ? 8 : 16>;
+using EpiOf = Epi<split_kind(KIND) ? 8 : 16>;
 // GEMM_TF32X3 sums its products in TMEM over this many k-blocks (32 f32
 // each) only; the epilogue adds the partial sums in registers with IEEE
 // round-to-nearest.  The tensor core's own f32 accumulation is less exact
@@ -69,7 +72,7 @@ constexpr int TF32_PROMOTE_KB = 2;  // max error ~3x cuBLAS SGEMM, ~15% slower t
 struct KParams {
     int m, n, k;
     int num_m_blocks, num_n_blocks, num_k_blocks;
-    int promote_kb;  // k-blocks per TMEM accumulation unit (GEMM_TF32X3)
+    int promote_kb;  // k-blocks per TMEM accumulation unit (split kinds)
     int acc_only;    // only the raw int32 accumulators (acc_out) are written
     const float* bias;
     const float* residual;
@@ -247,22 +250,23 @@ __device__ __forceinline__ constexpr uint32_t make_idesc() {
     // format, [15]/[16] A/B major (0 = K), [17,23) N>>3, [24,29) M>>4
     return (KIND == GEMM_I8   ? (2u << 4) | (1u << 7) | (1u << 10)    // S32 <- s8 x s8
             : KIND == GEMM_F8 ? (1u << 4) | (0u << 7) | (0u << 10)    // F32 <- e4m3 x e4m3
+            : KIND == GEMM_F16X3 ? (1u << 4) | (0u << 7) | (0u << 10) // F32 <- f16 x f16 (kind::f16)
                               : (1u << 4) | (2u << 7) | (2u << 10))   // F32 <- tf32 x tf32
            | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
 }
 
-// NS operand parts per stage: 1, or 2 (high + low) for the TF32 split GEMM.
+// NS operand parts per stage: 1, or 2 (high + low) for the split GEMMs.
 template <int KIND, int BN>
 struct Cfg {
-    static constexpr int NS = (KIND == GEMM_TF32X3) ? 2 : 1;
-    static constexpr int ELEM = (KIND == GEMM_TF32X3) ? 4 : 1;  // bytes per element
+    static constexpr int NS = split_kind(KIND) ? 2 : 1;
+    static constexpr int ELEM = (KIND == GEMM_TF32X3) ? 4 : (KIND == GEMM_F16X3) ? 2 : 1;  // bytes per element
     static constexpr int BKE = BK / ELEM;                         // K elements per stage
     static constexpr uint32_t A_BYTES = BM * BK;                  // one part
     static constexpr uint32_t B_BYTES = BN * BK;
     static constexpr int STAGES = (NS * (BM + BN) * BK * 8 <= 196608) ? 8 : 196608 / (NS * (BM + BN) * BK);
     // TMEM accumulator buffers: 2 (tile i+1's MMAs overlap tile i's
-    // epilogue), 4 for the short promotion units of GEMM_TF32X3
-    static constexpr int NACC = (KIND == GEMM_TF32X3) ? 4 : 2;
+    // epilogue), 4 for the short promotion units of the split kinds
+    static constexpr int NACC = split_kind(KIND) ? 4 : 2;
     static constexpr uint32_t TMEM_COLS = NACC * BN;  // 128/256/512: powers of two
     static constexpr uint32_t RING = STAGES * NS * (A_BYTES + B_BYTES);
     static constexpr uint32_t EPI = EpiOf<KIND>::EPI_WARPS * 32 * EpiOf<KIND>::CH * 4;  // per-warp 32 x CH f32 staging
@@ -353,9 +357,9 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = make_idesc<KIND, BN>();
-            // one accumulation unit = a tile (or, GEMM_TF32X3, a run of
-            // TF32_PROMOTE_KB k-blocks of it) in one of the two TMEM buffers
-            const int pk = (KIND == GEMM_TF32X3) ? p.promote_kb : p.num_k_blocks;
+            // one accumulation unit = a tile (or, split kinds, a run of
+            // promote_kb k-blocks of it) in one of the NACC TMEM buffers
+            const int pk = split_kind(KIND) ? p.promote_kb : p.num_k_blocks;
             uint32_t it = 0, ucount = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x)
@@ -382,6 +386,13 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                             umma_i8(d_tmem, ad, bd, idesc, accum);
                         } else if (KIND == GEMM_F8) {
                             umma_f8(d_tmem, ad, bd, idesc, accum);
+                        } else if (KIND == GEMM_F16X3) {
+                            // same three products on fp16 parts (16 K per instruction)
+                            const uint64_t adl = smem_desc_k_sw128(a0 + C::A_BYTES + kk * UMMA_K);
+                            const uint64_t bdl = smem_desc_k_sw128(b0 + C::B_BYTES + kk * UMMA_K);
+                            umma_f16(d_tmem, adl, bd, idesc, accum);
+                            umma_f16(d_tmem, ad, bdl, idesc, 1u);
+                            umma_f16(d_tmem, ad, bd, idesc, 1u);
                         } else {
                             // x*w ~ xh*wh + xh*wl + xl*wh, small terms first
                             const uint64_t adl = smem_desc_k_sw128(a0 + C::A_BYTES + kk * UMMA_K);
@@ -411,8 +422,8 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
         float* stage = reinterpret_cast<float*>(smem + C::RING) + (warp - 4) * (32 * E::CH);
         const bool bias_on = p.bias != nullptr;
         const bool per_channel = p.per_channel != 0;
-        const float sa = (KIND == GEMM_TF32X3 || p.acc_only) ? 1.0f : __ldg(p.scale_a);
-        const float sw0 = (KIND == GEMM_TF32X3 || p.acc_only) ? 1.0f : __ldg(p.scales_w);
+        const float sa = (split_kind(KIND) || p.acc_only) ? 1.0f : __ldg(p.scale_a);
+        const float sw0 = (split_kind(KIND) || p.acc_only) ? 1.0f : __ldg(p.scales_w);
         InvScale qs{0.0, 0.0f, 0.0f};
         if (p.Yq) qs = make_inv_scale(static_cast<double>(__ldg(p.scale_out)));
         EpiCtx ec{(p.n & 3) == 0, qs};
@@ -421,8 +432,8 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                               (!bias_on || (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0);
         float amax = 0.0f;
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(eg * 32) << 16);
-        if constexpr (KIND == GEMM_TF32X3) {
-            // partial sums of TF32_PROMOTE_KB k-blocks each, added in registers
+        if constexpr (split_kind(KIND)) {
+            // partial sums of promote_kb k-blocks each, added in registers
             constexpr int NCH = BN / E::CH / E::EPW;  // chunks this warp owns: half, half + E::EPW, ...
             uint32_t ucount = 0;
             bool alive = true;
@@ -458,6 +469,20 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                     }
                 }
                 if (!alive) break;
+                if constexpr (KIND == GEMM_F16X3) {
+                    // undo the rows' power-of-two scales (exact)
+                    const int row = row0 + lane;
+                    const float ra = (row < p.m) ? __ldg(p.scale_a + row) : 0.0f;
+#pragma unroll
+                    for (int i = 0; i < NCH; i++) {
+                        const int n0 = nb * BN + (half + E::EPW * i) * E::CH;
+#pragma unroll
+                        for (int j = 0; j < E::CH; j++) {
+                            const int n = (n0 + j < p.n) ? n0 + j : p.n - 1;
+                            acc[i][j] = acc[i][j] * ra * __ldg(p.scales_w + n);
+                        }
+                    }
+                }
 #pragma unroll
                 for (int i = 0; i < NCH; i++) {
                     const int n0 = nb * BN + (half + E::EPW * i) * E::CH;
@@ -661,14 +686,17 @@ int get_encoder() {
     return TVQ_OK;
 }
 
-// 2-D K-major operand [rows, k] of 1-byte or 4-byte elements: box {128 bytes
-// of K, box_rows}, 128-byte swizzle.
+// 2-D K-major operand [rows, k] of 1-, 2- or 4-byte elements: box {128
+// bytes of K, box_rows}, 128-byte swizzle.
 int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box_rows, int elem, int64_t pitch = 0) {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch ? pitch : k) * elem};
     const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK / elem), static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = g_encode(map, elem == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+    const CUtensorMapDataType dt = elem == 4   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : elem == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    CUresult r = g_encode(map, dt, 2,
                           const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -727,7 +755,55 @@ __global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict
     }
 }
 
+// Row-scaled fp16 split, one warp per row of x [rows, k].  With s = 2^e
+// chosen so that max|x| * s lies in [2^14, 2^15), x*s is exact and
+// x*s = hi + lo + r with hi = fp16(x*s), lo = fp16(x*s - hi) and |r| <=
+// max(2^-22 |x*s|, 2^-25) (the second term: lo in fp16's subnormal range,
+// at most 2^-39 of the row's largest |x*s|).  rscale[row] = 1/s.  s is capped at 2^126 (rows with
+// max|x| below 2^-111 keep fewer bits); a row holding Inf or NaN gets s = 1
+// and carries it into its products.
+__global__ void split_f16_rows_kernel(const float* __restrict__ x, __half* __restrict__ hi, __half* __restrict__ lo,
+                                      float* __restrict__ rscale, int64_t rows, int64_t k) {
+    griddep_wait();
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+        const float* xr = x + r * k;
+        float m = 0.0f;
+        for (int64_t j = lane; j < k; j += 32) m = fmaxf(m, fabsf(xr[j]));  // fmaxf drops NaN: checked below
+        bool bad = false;
+        for (int64_t j = lane; j < k; j += 32) bad |= !isfinite(xr[j]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        bad = __any_sync(0xffffffffu, bad);
+        int sh = 0;
+        if (!bad && m > 0.0f) {
+            int e;
+            frexpf(m, &e);  // m in [2^(e-1), 2^e)
+            sh = min(15 - e, 126);
+        }
+        if (lane == 0) rscale[r] = ldexpf(1.0f, -sh);
+        for (int64_t j = lane; j < k; j += 32) {
+            const float v = ldexpf(xr[j], sh);
+            const __half h = __float2half_rn(v);
+            hi[r * k + j] = h;
+            lo[r * k + j] = __float2half_rn(v - __half2float(h));
+        }
+    }
+}
+
 }  // namespace
+
+int launch_split_f16_rows(const float* x, void* hi, void* lo, float* rscale, int64_t rows, int64_t k,
+                          cudaStream_t st) {
+    if (rows <= 0) return TVQ_OK;
+    int rc = 0;
+    DeviceState* ds = device_state(&rc);
+    if (!ds) return rc;
+    const int grid = static_cast<int>(std::min<int64_t>((rows + 7) / 8, ds->sm_count * 8));
+    return launch_pdl(split_f16_rows_kernel, dim3(grid), dim3(256), 0, st, x, static_cast<__half*>(hi),
+                      static_cast<__half*>(lo), rscale, rows, k);
+}
 
 int make_tma_f32_sw128(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int box_rows, int64_t pitch) {
     int rc = get_encoder();
@@ -744,9 +820,11 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
               "GEMM size out of range (k must stay below 133143 for exact int32 accumulation)");
     if (g.m == 0 || g.n == 0) return TVQ_OK;
     const bool acc_only = g.kind == GEMM_I8 && g.acc_out && !g.Y && !g.Yq && !g.amax;
+    TVQ_CHECK(g.kind >= GEMM_I8 && g.kind <= GEMM_F16X3, TVQ_ERR_INVALID, "unknown GEMM kind");
+    const bool split = split_kind(g.kind);
     TVQ_CHECK(g.kind == GEMM_TF32X3 || acc_only || (g.scale_a && g.scales_w), TVQ_ERR_INVALID,
               "scale pointers are required");
-    TVQ_CHECK(g.kind != GEMM_TF32X3 || (!g.Yq && !g.bias && !g.residual && g.act == 0 && g.Y), TVQ_ERR_INVALID,
+    TVQ_CHECK(!split || (!g.Yq && !g.bias && !g.residual && g.act == 0 && g.Y && !g.amax), TVQ_ERR_INVALID,
               "the split fp32 GEMM writes plain f32 Y only");
     TVQ_CHECK(!g.Yq || g.scale_out, TVQ_ERR_INVALID, "int8 output needs scale_out");
     int rc = 0;
@@ -765,7 +843,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.acc_out = g.acc_out;
     p.scale_a = g.scale_a;
     p.scales_w = g.scales_w;
-    p.per_channel = acc_only ? 0 : g.per_channel;
+    p.per_channel = (acc_only || split) ? 0 : g.per_channel;
     p.kh = g.kh;
     p.kl = g.kl;
     p.vth = g.vth;
@@ -778,12 +856,12 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.amax = g.amax;
     p.err = ds->d_error;
     p.num_m_blocks = static_cast<int>((g.m + BM - 1) / BM);
-    const int elem = (g.kind == GEMM_TF32X3) ? 4 : 1;
+    const int elem = (g.kind == GEMM_TF32X3) ? 4 : (g.kind == GEMM_F16X3) ? 2 : 1;
     p.num_k_blocks = static_cast<int>((g.k * elem + BK - 1) / BK);
     p.promote_kb = TF32_PROMOTE_KB;
     if (const char* env = getenv("TVQ_TF32_PROMOTE_KB")) p.promote_kb = std::max(1, atoi(env));
 
-    if (g.k == 0 && g.kind == GEMM_TF32X3) {
+    if (g.k == 0 && split) {
         TVQ_CUDA(cudaMemsetAsync(g.Y, 0, sizeof(float) * g.m * g.n, st));
         return TVQ_OK;
     }
@@ -795,7 +873,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     TVQ_CHECK((g.k * elem) % 16 == 0, TVQ_ERR_UNSUPPORTED, "k must be a multiple of 16 bytes (TMA row pitch)");
     TVQ_CHECK(((reinterpret_cast<uintptr_t>(g.A) | reinterpret_cast<uintptr_t>(g.W)) & 15) == 0, TVQ_ERR_UNSUPPORTED,
               "A and W must be 16-byte aligned");
-    TVQ_CHECK(g.kind != GEMM_TF32X3 ||
+    TVQ_CHECK(!split ||
                   (g.A2 && g.W2 && ((reinterpret_cast<uintptr_t>(g.A2) | reinterpret_cast<uintptr_t>(g.W2)) & 15) == 0),
               TVQ_ERR_UNSUPPORTED, "the split GEMM needs 16-byte aligned low parts");
     TVQ_CHECK(!g.Y || (reinterpret_cast<uintptr_t>(g.Y) & 15) == 0, TVQ_ERR_UNSUPPORTED, "Y must be 16-byte aligned");
@@ -819,7 +897,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
         }();
         bn = env_bn;
     }
-    if (g.kind == GEMM_TF32X3 && bn > 128) bn = 128;  // its partial sums live in registers
+    if (split && bn > 128) bn = 128;  // their partial sums live in registers
     if (bn == 0) {
         // Tile width with the least work on the busiest SM: rounds of tiles
         // (ceil(tiles / SMs)) x BN columns; ties go to the wider tile (fewer,
@@ -829,8 +907,8 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
         const int64_t mblk = p.num_m_blocks;
         int64_t best = -1;
         for (int cand : {256, 128, 64}) {
-            if (g.kind == GEMM_TF32X3 && cand > 128) continue;
-            if (g.kind == GEMM_TF32X3 && cand == 64 && mblk * ((g.n + 127) / 128) >= ds->sm_count) continue;
+            if (split && cand > 128) continue;
+            if (split && cand == 64 && mblk * ((g.n + 127) / 128) >= ds->sm_count) continue;
             const int64_t tiles = mblk * ((g.n + cand - 1) / cand);
             const int64_t cost = (tiles + ds->sm_count - 1) / ds->sm_count * cand;
             if (best < 0 || cost < best) {
@@ -851,6 +929,10 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
         if (bn == 256) return launch_tc<GEMM_F8, 256>(p, g, grid, st);
         if (bn == 128) return launch_tc<GEMM_F8, 128>(p, g, grid, st);
         return launch_tc<GEMM_F8, 64>(p, g, grid, st);
+    }
+    if (g.kind == GEMM_F16X3) {
+        if (bn >= 128) return launch_tc<GEMM_F16X3, 128>(p, g, grid, st);
+        return launch_tc<GEMM_F16X3, 64>(p, g, grid, st);
     }
     if (bn >= 128) return launch_tc<GEMM_TF32X3, 128>(p, g, grid, st);
     return launch_tc<GEMM_TF32X3, 64>(p, g, grid, st);

@@ -28,13 +28,16 @@ float e4m3_decode_host(uint32_t v);
 uint8_t e4m3_encode_host(float x);
 
 // tvq_gemm.cu
-enum GemmKind { GEMM_I8 = 0, GEMM_F8 = 1, GEMM_TF32X3 = 2 };
+enum GemmKind { GEMM_I8 = 0, GEMM_F8 = 1, GEMM_TF32X3 = 2, GEMM_F16X3 = 3 };
 
 struct GemmArgs {
     int kind = GEMM_I8;
     const void* A = nullptr;          // [m,k] 8-bit, row-major
     const void* W = nullptr;          // [n,k] 8-bit, row-major
-    const void* A2 = nullptr;         // GEMM_TF32X3: low parts of A and W (A, W hold the high parts, f32)
+    // GEMM_TF32X3 / GEMM_F16X3: low parts of A and W (A, W hold the high
+    // parts: f32 on the TF32 grid / fp16).  GEMM_F16X3 also reads scale_a [m]
+    // and scales_w [n]: the rows' power-of-two scales (launch_split_f16_rows).
+    const void* A2 = nullptr;
     const void* W2 = nullptr;
     const float* bias = nullptr;      // [n] or null
     const float* residual = nullptr;  // [m,n] or null
@@ -62,6 +65,10 @@ int make_tma_f32_sw128(CUtensorMap* map, const float* ptr, int64_t rows, int64_t
                        int64_t pitch = 0);
 // x = hi + lo with hi rounded to TF32 precision (10 explicit mantissa bits)
 int launch_split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStream_t st);
+// Row-scaled fp16 split of x [rows, k]: per row s = 2^e with max|x|*s in
+// [2^14, 2^15); hi = fp16(x*s), lo = fp16(x*s - hi); rscale[row] = 1/s.
+int launch_split_f16_rows(const float* x, void* hi, void* lo, float* rscale, int64_t rows, int64_t k,
+                          cudaStream_t st);
 
 // tvq_qdq.cu: the ONNX QDQ operator family (session.tkv:1896-2071, 2789-2905).
 // Quantize / dequantize split the tensor at its axis into (outer, dim, inner);

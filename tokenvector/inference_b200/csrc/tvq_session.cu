@@ -48,8 +48,10 @@ struct Session {
     double eps = 1e-6;
     std::vector<void*> allocs;
     float *wte = nullptr, *wpe = nullptr, *lnf_g = nullptr, *lnf_b = nullptr;
-    float *wte_hi = nullptr, *wte_lo = nullptr;  // LM head operand split (high + low parts)
-    float *xf_hi = nullptr, *xf_lo = nullptr;
+    // LM head operands split into fp16 high + low parts under power-of-two
+    // row scales (launch_split_f16_rows)
+    uint16_t *wte_hi = nullptr, *wte_lo = nullptr, *xf_hi = nullptr, *xf_lo = nullptr;
+    float *wte_rs = nullptr, *xf_rs = nullptr;
     std::vector<LayerW> L;
     float* act_scale = nullptr;
     uint32_t* act_amax = nullptr;
@@ -269,15 +271,17 @@ int enqueue_forward(Session& s, bool calibrating) {
         xin = s.xf_last;
         rows = s.nseg;
     }
-    // tied LM head, fp32 on the tensor cores with split precision
-    STEP(launch_split_tf32(xin, s.xf_hi, s.xf_lo, static_cast<int64_t>(rows) * d, s.st));
+    // tied LM head, fp32 on the FP16 tensor cores with split precision
+    STEP(launch_split_f16_rows(xin, s.xf_hi, s.xf_lo, s.xf_rs, rows, d, s.st));
     {
         GemmArgs g;
-        g.kind = GEMM_TF32X3;
+        g.kind = GEMM_F16X3;
         g.A = s.xf_hi;
         g.A2 = s.xf_lo;
         g.W = s.wte_hi;
         g.W2 = s.wte_lo;
+        g.scale_a = s.xf_rs;
+        g.scales_w = s.wte_rs;
         g.Y = s.logits;
         g.m = rows;
         g.n = s.vocab;
@@ -405,6 +409,7 @@ int tvq_session_create(int device, int64_t vocab, int64_t d_model, int64_t n_hea
         STEP(s->alloc(&s->xf_last, MT * D));
         STEP(s->alloc(&s->xf_hi, MT * D));
         STEP(s->alloc(&s->xf_lo, MT * D));
+        STEP(s->alloc(&s->xf_rs, MT));
         STEP(s->alloc(&s->aq, MT * D));
         STEP(s->alloc(&s->hq, MT * F));
         STEP(s->alloc(&s->err, 1));
@@ -441,10 +446,11 @@ int tvq_session_set_embeddings(int64_t handle, const float* wte, const float* wp
     if (!S->wte) STEP(S->alloc(&S->wte, vd));
     if (!S->wte_hi) STEP(S->alloc(&S->wte_hi, vd));
     if (!S->wte_lo) STEP(S->alloc(&S->wte_lo, vd));
+    if (!S->wte_rs) STEP(S->alloc(&S->wte_rs, static_cast<size_t>(S->vocab)));
     if (!S->wpe) STEP(S->alloc(&S->wpe, static_cast<size_t>(S->max_pos) * S->d));
     TVQ_CUDA(cudaMemcpy(S->wte, wte, sizeof(float) * vd, cudaMemcpyHostToDevice));
     TVQ_CUDA(cudaMemcpy(S->wpe, wpe, sizeof(float) * S->max_pos * S->d, cudaMemcpyHostToDevice));
-    STEP(launch_split_tf32(S->wte, S->wte_hi, S->wte_lo, static_cast<int64_t>(vd), S->st));
+    STEP(launch_split_f16_rows(S->wte, S->wte_hi, S->wte_lo, S->wte_rs, S->vocab, S->d, S->st));
     TVQ_CUDA(cudaStreamSynchronize(S->st));
     return TVQ_OK;
 }
