@@ -45,6 +45,11 @@ WORKLOAD = "config 2: GPT-2 124M (12 L, d 768, 12 heads, vocab 50257), all 4 lin
 WORKLOAD4 = ("config 4: GPT-2 124M INT8 PTQ, 256 requests with lengths U[32,1024] packed into 131072 tokens, "
              "whole requests sharded over the GPUs, last-token logits")
 C4_REQUESTS, C4_TOKENS = 256, 131072
+METRIC5 = "GPT-2 XL-shaped INT8 PTQ layer stack tokens/s"
+WORKLOAD5 = ("config 5: GPT-2 XL-shaped INT8 PTQ layer stack (48 L, d 1600, ffn 6400, 25 heads), 8192 tokens per "
+             "step as 8 sequences of 1024, seeded N(0,1) hidden states, on-GPU calibrate + quantize of every "
+             "activation per layer per step, sequences sharded over the GPUs")
+C5_SEQS, C5_SEQ = 8, 1024
 FLUSH_BYTES = 256 << 20
 
 
@@ -213,8 +218,63 @@ def cpu_sample(weights, ids, scales, reps=1):
     return SEQ / best, {"block_s": t2 - t1, "lm_head_32rows_s": t3 - t2}
 
 
+def xl_layer(cfg, li, seed=0):
+    """Block li of the XL-shaped stack: N(0, 0.02) linears from numpy's
+    PCG64 (the reference's LCG is too slow for 1.5 G weights), zero biases,
+    LayerNorm gamma 1 / beta 0."""
+    d, f = cfg.d_model, cfg.d_ffn
+    rng = np.random.default_rng(seed * 1000 + li)
+    w = lambda *shape: (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02))  # noqa: E731
+    one, zero = np.ones(d, np.float32), np.zeros(d, np.float32)
+    return dict(ln1_g=one, ln1_b=zero, attn_w=w(d, 3 * d), attn_b=np.zeros(3 * d, np.float32), proj_w=w(d, d),
+                proj_b=zero, ln2_g=one, ln2_b=zero, fc_w=w(d, f), fc_b=np.zeros(f, np.float32), mp_w=w(f, d),
+                mp_b=zero)
+
+
+def xl_hidden(rows_from, rows_to, d=1600):
+    """Rows [rows_from, rows_to) of the seeded N(0,1) hidden states."""
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((C5_SEQS * C5_SEQ, d), dtype=np.float32)
+    return np.ascontiguousarray(x[rows_from:rows_to])
+
+
+def cpu_sample_c5(cfg):
+    """Bounded sample of config 5 on the CPU oracle: one block with dynamic
+    calibration on one 1024-token sequence, extrapolated to 48 blocks x 8
+    sequences.  Returns (tokens/s, seconds of the sample)."""
+    from oracle import gpt2_int8 as OG
+    L = xl_layer(cfg, 0)
+    x = xl_hidden(0, C5_SEQ, cfg.d_model)
+    seg = np.array([0, C5_SEQ], np.int64)
+    qw = OG.quantize_weights([L])
+    t0 = time.perf_counter()
+    OG.blocks([L], x, seg, calibrator=OG.Calibrator(1), qweights=qw, n_heads=cfg.n_heads, eps=cfg.eps)
+    t = time.perf_counter() - t0
+    full = t * cfg.n_layers * C5_SEQS
+    return C5_SEQS * C5_SEQ / full, t
+
+
 def run_reference(args, rank):
     if rank != 0:
+        return 0
+    if args.config == 5:
+        import oracle as O
+        from tokenvector.inference_b200.gpt2 import GPT2Config
+        cfg = GPT2Config.gpt2_xl_shape()
+        for _ in range(min(args.warmup, 1)):
+            cpu_sample_c5(cfg)
+        vals = [cpu_sample_c5(cfg)[0] for _ in range(min(args.steps, 3))]
+        v = statistics.median(vals)
+        sample = ("1 of 48 blocks with per-step calibration on 1 of 8 sequences (1024 tokens), extrapolated to "
+                  "the full step; median of %d" % len(vals))
+        line = {"metric": METRIC5, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": 1000.0 * C5_SEQS * C5_SEQ / v, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+                "config": {"workload": WORKLOAD5, "parallelism": "cpu"}, "impl": "reference",
+                "cpu_baseline": {"value": v, "unit": UNIT, "cores": O.num_threads(), "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return 0
     import oracle as O
     from tokenvector.inference_b200.gpt2 import GPT2Config, GPT2Weights
@@ -464,21 +524,179 @@ def run_ours(args, rank, world, local):
     return 0
 
 
+def run_ours_c5(args, rank, world, local):
+    """Config 5: the XL-shaped layer stack on hidden states, sequences
+    sharded over the ranks (strong scaling), dynamic calibration per step."""
+    import ctypes as C
+    import torch
+    import torch.distributed as dist
+    from tokenvector.inference_b200 import _native as N
+    from tokenvector.inference_b200.gpt2 import GPT2Config, LayerStack, segments_from_lengths
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    assert C5_SEQS % world == 0, "config 5 shards 8 sequences evenly"
+    cfg = GPT2Config.gpt2_xl_shape()
+    nseq = C5_SEQS // world
+    T = nseq * C5_SEQ
+    r0 = rank * T
+    x = xl_hidden(r0, r0 + T, cfg.d_model)
+    t_up = time.perf_counter()
+    st = LayerStack(cfg, (xl_layer(cfg, li) for li in range(cfg.n_layers)), device=local, max_tokens=T)
+    t_up = time.perf_counter() - t_up
+    st.prepare(segments_from_lengths([C5_SEQ] * nseq))
+
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    sptr = stream.cuda_stream
+    x_dev = torch.from_numpy(x).to(dev)
+    torch.cuda.synchronize(dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def step_device():
+        st.run_layers_device(x_dev.data_ptr(), None, dynamic=True, stream_ptr=sptr)
+
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        step_device()
+    torch.cuda.synchronize(dev)
+    gpu_id = str(torch.cuda.get_device_properties(local).uuid)
+    gpu_id = gpu_id if gpu_id.startswith("GPU-") else "GPU-" + gpu_id
+    clocks = ClockSampler(gpu_id)
+    clocks.start()
+    time.sleep(0.3)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    total_ms = 0.0
+    for _ in range(args.steps):
+        flush.zero_()
+        ev0.record(stream)
+        step_device()
+        ev1.record(stream)
+        ev1.synchronize()
+        total_ms += ev0.elapsed_time(ev1)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    n_launches = st.launches()
+
+    # per-stage breakdown (stage events inside a recaptured graph)
+    st.set_profiling(True)
+    stage_ms = {k: 0.0 for k in st.STAGES}
+    prof_steps = max(2, min(args.steps // 2, 5))
+    for i in range(prof_steps + 1):
+        flush.zero_()
+        step_device()
+        torch.cuda.synchronize(dev)
+        if i == 0:
+            continue
+        for k, v in st.stage_times().items():
+            stage_ms[k] += v
+    st.set_profiling(False)
+    step_device()
+    torch.cuda.synchronize(dev)
+
+    # end to end: pinned host hidden states in, host hidden states out
+    x_pin = torch.from_numpy(x).pin_memory()
+    y_pin = torch.empty_like(x_pin).pin_memory()
+
+    def step_e2e():
+        N.call("tvq_session_run_layers", st.handle, C.c_void_p(x_pin.data_ptr()), 0, C.c_void_p(y_pin.data_ptr()), 0,
+               1, C.c_void_p(sptr))
+
+    step_e2e()
+    e2e_steps = max(3, min(args.steps, 10))
+    e2e_ms = 0.0
+    if world > 1:
+        dist.barrier()
+    for _ in range(e2e_steps):
+        flush.zero_()
+        torch.cuda.synchronize(dev)
+        ev0.record(stream)
+        step_e2e()
+        ev1.record(stream)
+        ev1.synchronize()
+        e2e_ms += ev0.elapsed_time(ev1)
+    finite = bool(torch.isfinite(y_pin).all().item())
+
+    vals = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms = vals.tolist()
+    if rank == 0:
+        job = C5_SEQS * C5_SEQ
+        hbm, bf16, src = peaks()
+        int8_peak = 2.0 * bf16
+        work = gemm_work(T=T, d=cfg.d_model, ffn=cfg.d_ffn)
+        per_launch_ms = {k: stage_ms[k] / (prof_steps * cfg.n_layers) for k in work}
+        dom = max(work, key=lambda k: per_launch_ms[k])
+        ops, byts = work[dom]
+        t = per_launch_ms[dom] / 1000.0
+        if ops / byts < int8_peak * 1e12 / (hbm * 1e9):
+            roof = {"bound": "hbm", "achieved": byts / t / 1e9, "peak": hbm, "unit": "GB/s"}
+        else:
+            roof = {"bound": "tensor", "achieved": ops / t / 1e12, "peak": int8_peak, "unit": "TOPS"}
+        roof["frac"] = roof["achieved"] / roof["peak"]
+        roof["traffic"] = None
+        roof["kernel"] = "gemm_tc_kernel<I8> (%s, M=%d, N,K of the XL layer)" % (dom, T)
+        roof["peak_source"] = "%s HBM copy bandwidth; INT8 peak = 2 x %s dense bf16 (%.1f TFLOP/s)" % (src, src, bf16)
+        kernels = {k: {"ms_per_step": v / prof_steps} for k, v in stage_ms.items() if v > 0}
+        for k, (o, b) in work.items():
+            kernels[k].update({"us_per_launch": per_launch_ms[k] * 1000.0,
+                               "tops": o / (per_launch_ms[k] / 1000.0) / 1e12})
+        cpu = None
+        if world == 1:
+            from oracle import num_threads
+            v, secs = cpu_sample_c5(cfg)
+            cpu = {"value": v, "unit": UNIT, "cores": num_threads(), "kind": "port",
+                   "sample": "1 of 48 blocks with per-step calibration on 1 of 8 sequences (%.2f s), extrapolated "
+                             "to the full step" % secs}
+        out = {"metric": METRIC5, "value": job * args.steps / (total_ms / 1000.0), "unit": UNIT, "n_gpus": world,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+               "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+               "data": "synthetic",
+               "config": {"workload": WORKLOAD5, "tokens": job, "rank0_tokens": T,
+                          "parallelism": "sequences sharded over %d ranks" % world,
+                          "l2": "flushed (256 MiB write) between steps; weights (1.5 GB int8) exceed L2",
+                          "weights": "seeded N(0,0.02) (numpy PCG64), quantized per channel on the GPU",
+                          "upload_s": t_up},
+               "e2e": {"value": job * e2e_steps / (e2e_ms / 1000.0), "unit": UNIT,
+                       "h2d_bytes_per_step": 4 * job * cfg.d_model, "d2h_bytes_per_step": 4 * job * cfg.d_model,
+                       "ms_per_step": e2e_ms / e2e_steps, "finite": finite},
+               "roofline": roof, "cpu_baseline": cpu, "gpu_launches": n_launches * args.steps, "clocks": clk,
+               "kernels": kernels}
+        print(json.dumps(out), flush=True)
+    st.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, choices=[2, 4], default=2,
+    ap.add_argument("--config", type=int, choices=[2, 4, 5], default=2,
                     help="2: GPT-2 124M forward, seq 1024 per GPU (default, the headline); "
-                         "4: batched serving, 131072 packed tokens sharded over the GPUs")
+                         "4: batched serving, 131072 packed tokens sharded over the GPUs; "
+                         "5: XL-shaped INT8 layer stack, 8192 tokens sharded over the GPUs")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank)
+    if args.config == 5:
+        return run_ours_c5(args, rank, world, local)
     return run_ours(args, rank, world, local)
 
 

@@ -303,7 +303,9 @@ TVQ_API int tvq_dev_dynamic_quantize_linear(const float* x, int64_t n, int8_t* y
  * (ln_1, c_attn, attention, c_proj, ln_2, c_fc, GELU-erf, mlp c_proj) with the
  * four linears as QuantizedGemm (session.tkv:678-697), ln_f and the tied fp32
  * LM head (gpt2_ref.tkv:575-610).  Replaces InferenceSession construction +
- * run (session.tkv:3376-3436) for graphs of this shape.  One handle per GPU. */
+ * run (session.tkv:3376-3436) for graphs of this shape.  One handle per GPU.
+ * vocab 0 makes a layer stack without embeddings, ln_f or LM head: it runs
+ * through tvq_session_run_layers only. */
 TVQ_API int tvq_session_create(int device, int64_t vocab, int64_t d_model, int64_t n_heads, int64_t n_layers,
                                int64_t d_ffn, int64_t max_pos, double ln_eps, int64_t max_tokens, int64_t* handle);
 TVQ_API int tvq_session_destroy(int64_t handle);
@@ -341,8 +343,21 @@ TVQ_API int tvq_session_calibrate(int64_t handle, const int64_t* ids, int ids_on
 TVQ_API int tvq_session_forward(int64_t handle, const int64_t* ids, int ids_on_device, float* logits,
                                 int64_t logits_len, int logits_on_device, void* stream);
 TVQ_API int tvq_session_logits(int64_t handle, float** logits_dev, int64_t* rows, int64_t* cols);
-/* Kernel launches of one forward for the prepared layout (kernel nodes of
- * its captured CUDA graph; profiling event nodes excluded); needs a forward
+/* The transformer blocks alone (a CUDA graph of their own) on hidden states
+ * x f32 [T, d_model] (T = the prepared layout's tokens; host or device; NULL
+ * = the resident hidden states, tvq_session_hidden), written to y (NULL =
+ * keep them on the device).  dynamic 0 uses the static activation scales;
+ * dynamic 1 calibrates every quantization point on this call's activations
+ * (calibrate_minmax, engine.tkv:13-36, then quantize_int8_symmetric, per
+ * layer on the GPU) and leaves those scales as the static ones.  Host
+ * buffers make the call synchronous. */
+TVQ_API int tvq_session_run_layers(int64_t handle, const float* x, int x_on_device, float* y, int y_on_device,
+                                   int dynamic, void* stream);
+/* Device pointer of the resident hidden states [max_tokens, d_model]. */
+TVQ_API int tvq_session_hidden(int64_t handle, float** x_dev);
+/* Kernel launches of the graph launched last (tvq_session_forward or
+ * tvq_session_run_layers) for the prepared layout (kernel nodes of its
+ * captured CUDA graph; memset and profiling event nodes excluded); needs one
  * to have run since the last prepare / profiling change. */
 TVQ_API int tvq_session_launches(int64_t handle, int64_t* kernels);
 TVQ_API int tvq_session_sync(int64_t handle);
@@ -350,7 +365,8 @@ TVQ_API int tvq_session_sync(int64_t handle);
  * every stage; tvq_session_stage_times then returns the last forward's time
  * per stage class in ms: [0] embedding, [1] layernorms, [2] c_attn GEMMs,
  * [3] attention, [4] attn c_proj GEMMs, [5] c_fc GEMMs, [6] mlp c_proj GEMMs,
- * [7] LM head. */
+ * [7] LM head, [8] calibrate-then-quantize passes (calibrating / dynamic
+ * runs).  n >= 9. */
 TVQ_API int tvq_session_set_profiling(int64_t handle, int enable);
 TVQ_API int tvq_session_stage_times(int64_t handle, float* ms, int64_t n);
 

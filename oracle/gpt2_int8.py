@@ -71,18 +71,17 @@ class Calibrator:
                         np.float32)
 
 
-def forward(weights, ids, seg, scales=None, calibrator: Calibrator | None = None, qweights=None,
-            logits_mode: int = 0, n_heads: int = 12, eps: float = 1e-6, record=None):
-    """INT8 forward.  `weights`: object with wte, wpe, lnf_g, lnf_b, layers
-    (dicts as in tokenvector.inference_b200.gpt2.GPT2Weights).  Exactly one of
-    `scales` ([L,4] static) or `calibrator` must be given.  Returns logits
-    (all rows, or the last row of each sequence for logits_mode 1)."""
+def blocks(layers, x, seg, scales=None, calibrator: Calibrator | None = None, qweights=None, n_heads: int = 12,
+           eps: float = 1e-6, record=None):
+    """The transformer blocks (gpt2_ref.tkv:575-588 per layer) on hidden
+    states x f32 [T, d]; returns the new hidden states.  Exactly one of
+    `scales` ([L,4] static) or `calibrator` must be given."""
     assert (scales is None) != (calibrator is None)
     seg = np.asarray(seg, np.int64)
     if qweights is None:
-        qweights = quantize_weights(weights.layers)
-    x = embed(ids, positions(seg), weights.wte, weights.wpe)
-    for li, L in enumerate(weights.layers):
+        qweights = quantize_weights(layers)
+    x = np.asarray(x, np.float32)
+    for li, L in enumerate(layers):
         (wq0, sw0), (wq1, sw1), (wq2, sw2), (wq3, sw3) = qweights[li]
 
         def sc(point, act):
@@ -105,6 +104,18 @@ def forward(weights, ids, seg, scales=None, calibrator: Calibrator | None = None
         x = add(x, matmul_int8_per_channel(q3, wq3, L["mp_b"], s3, sw3))
         if record is not None:
             record.append(dict(q0=q0, qkv=qkv, ctx=ctx, q1=q1, q2=q2, q3=q3, x=x))
+    return x
+
+
+def forward(weights, ids, seg, scales=None, calibrator: Calibrator | None = None, qweights=None,
+            logits_mode: int = 0, n_heads: int = 12, eps: float = 1e-6, record=None):
+    """INT8 forward.  `weights`: object with wte, wpe, lnf_g, lnf_b, layers
+    (dicts as in tokenvector.inference_b200.gpt2.GPT2Weights).  Exactly one of
+    `scales` ([L,4] static) or `calibrator` must be given.  Returns logits
+    (all rows, or the last row of each sequence for logits_mode 1)."""
+    seg = np.asarray(seg, np.int64)
+    x = embed(ids, positions(seg), weights.wte, weights.wpe)
+    x = blocks(weights.layers, x, seg, scales, calibrator, qweights, n_heads, eps, record)
     xf = layernorm(x, weights.lnf_g, weights.lnf_b, eps)
     if logits_mode == 1:
         xf = np.ascontiguousarray(xf[seg[1:] - 1])

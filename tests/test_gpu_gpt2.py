@@ -10,7 +10,9 @@ rtol 1e-4 / atol 2e-6; whole-model logits within atol 2e-3 on at least 98% of th
 within 5e-2, mean |diff| < 2e-4 (fp32 attention/GELU may move an activation
 across an int8 rounding boundary; the quantized weights and the calibrated
 scales are compared separately, weights bit-exact and scales to 1e-5
-relative)."""
+relative).  The hidden states of the layer stack: the same bounds with at
+most 10% of the rows above 2e-3 over three blocks (a flip cascades through
+the later blocks) and 2% for one block run on the oracle's own input."""
 import ctypes as C
 
 import numpy as np
@@ -19,7 +21,8 @@ import pytest
 import oracle as O
 from oracle import gpt2_int8 as OG
 from tokenvector.inference_b200 import _native as N
-from tokenvector.inference_b200.gpt2 import GPT2Config, GPT2Session, GPT2Weights, gi_noise, segments_from_lengths
+from tokenvector.inference_b200.gpt2 import (GPT2Config, GPT2Session, GPT2Weights, LayerStack, gi_noise,
+                                             random_layers, segments_from_lengths)
 
 pytestmark = pytest.mark.gpu
 
@@ -227,3 +230,96 @@ def test_session_launch_count_and_both_attention_paths(monkeypatch):
         diff = np.abs(got - ref)
         rowmax = diff.max(axis=1)
         assert diff.mean() < 2e-4 and (rowmax > 2e-3).mean() <= 0.02 and rowmax.max() < 5e-2
+
+
+def _assert_flip_bounded(got, ref, rows_frac=0.02):
+    """Hidden states / logits within the flip-aware bounds of the module
+    docstring: mean |diff| < 2e-4, at most rows_frac of the rows above 2e-3,
+    all rows below 5e-2."""
+    diff = np.abs(got - ref)
+    rowmax = diff.max(axis=1)
+    assert diff.mean() < 2e-4, diff.mean()
+    assert (rowmax > 2e-3).mean() <= rows_frac and rowmax.max() < 5e-2, ((rowmax > 2e-3).sum(), rowmax.max())
+
+
+# The XL-shaped INT8 PTQ layer stack: hidden states in and out, every call
+# calibrating its own activation scales on the GPU.  Small widths for the
+# logic (3 blocks, 3 sequences with key-chunk splits), one block at the XL
+# widths (d 1600, 25 heads, ffn 6400).
+@pytest.mark.parametrize("cfg,lengths", [
+    (GPT2Config(vocab=0, d_model=256, n_heads=4, n_layers=3, d_ffn=1024, max_pos=1024), [150, 70, 600]),
+    (GPT2Config(vocab=0, d_model=1600, n_heads=25, n_layers=1, d_ffn=6400, max_pos=1024), [96, 64]),
+])
+def test_layer_stack_dynamic_matches_oracle(cfg, lengths):
+    layers = random_layers(cfg, seed=9)
+    seg = segments_from_lengths(lengths)
+    T = int(seg[-1])
+    x = gi_noise(T * cfg.d_model, 77, 1.0).reshape(T, cfg.d_model)
+    st = LayerStack(cfg, layers, max_tokens=T)
+    st.prepare(seg)
+    qw = OG.quantize_weights(layers)
+    for li in range(cfg.n_layers):  # weights quantized like the reference
+        for which in range(4):
+            gw, gs = st.linear_i8(li, which)
+            assert np.array_equal(gw, qw[li][which][0])
+    for xin in (x, 0.5 * x):  # each call's scales are its own (no running max across calls)
+        got = st.run(xin, dynamic=True)
+        assert st.launches() == 11 * cfg.n_layers
+        cal = OG.Calibrator(cfg.n_layers)
+        rec = []
+        ref = OG.blocks(layers, xin, seg, calibrator=cal, qweights=qw, n_heads=cfg.n_heads, record=rec)
+        assert np.allclose(st.act_scales(), cal.scales(), rtol=1e-5, atol=0)
+        # an int8 flip of an LN output in block l moves its whole row of
+        # c_fc / qkv by one step, which re-rounds many GELU outputs of that
+        # row and so on through the later blocks: 10% of the rows over three
+        # blocks (the mean stays below 2e-4)
+        _assert_flip_bounded(got, ref, rows_frac=0.10)
+    # each block alone on the oracle's own input (no cascade across blocks): 2% of rows
+    for li in range(cfg.n_layers):
+        one = LayerStack(GPT2Config(vocab=0, d_model=cfg.d_model, n_heads=cfg.n_heads, n_layers=1,
+                                    d_ffn=cfg.d_ffn, max_pos=cfg.max_pos), [layers[li]], max_tokens=T)
+        one.prepare(seg)
+        xin = 0.5 * x if li == 0 else rec[li - 1]["x"]
+        got = one.run(xin, dynamic=True)
+        c1 = OG.Calibrator(1)
+        ref = OG.blocks([layers[li]], xin, seg, calibrator=c1, qweights=[qw[li]], n_heads=cfg.n_heads)
+        assert np.allclose(one.act_scales(), c1.scales(), rtol=1e-5, atol=0)
+        _assert_flip_bounded(got, ref, rows_frac=0.02)
+        one.close()
+    # static scales (the oracle's) through the 7-launch-per-block graph
+    scales = cal.scales()
+    st.set_act_scales(scales)
+    got = st.run(x, dynamic=False)
+    assert st.launches() == 7 * cfg.n_layers
+    _assert_flip_bounded(got, OG.blocks(layers, x, seg, scales=scales, qweights=qw, n_heads=cfg.n_heads),
+                         rows_frac=0.10)
+    # device-resident form: in place on the session's hidden states, twice;
+    # bit-identical to the same two passes through the host-buffer call
+    # (the same graph, deterministic kernels)
+    import torch
+    h2 = st.run(got, dynamic=False)
+    tx = _t(x)
+    torch.cuda.synchronize()
+    st.run_layers_device(tx.data_ptr(), None, dynamic=False)
+    ty = torch.empty_like(tx)
+    hp = st.hidden_device_ptr()
+    N.call("tvq_session_run_layers", st.handle, None, 1, _ptr(ty), 1, 0, None)  # second pass on the result
+    st.sync()
+    assert np.array_equal(ty.cpu().numpy(), h2)
+    assert hp != 0
+    st.close()
+
+
+def test_layer_stack_rejects_model_calls():
+    cfg = GPT2Config(vocab=0, d_model=128, n_heads=2, n_layers=1, d_ffn=256, max_pos=64)
+    st = LayerStack(cfg, random_layers(cfg, 1), max_tokens=64)
+    st.prepare(segments_from_lengths([10]))
+    wte = np.zeros((1, 128), np.float32)
+    with pytest.raises(N.TvqError):
+        N.call("tvq_session_set_embeddings", st.handle, wte.ctypes.data_as(C.c_void_p), wte.ctypes.data_as(C.c_void_p))
+    ids = np.zeros(10, np.int64)
+    with pytest.raises(N.TvqError):
+        N.call("tvq_session_forward", st.handle, ids.ctypes.data_as(C.c_void_p), 0, None, 0, 0, None)
+    with pytest.raises(N.TvqError):
+        N.call("tvq_session_run_layers", st.handle, None, 1, None, 1, 2, None)
+    st.close()

@@ -329,6 +329,21 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Named barrier over a subset of warps that also ANDs a predicate over them:
+// every participant gets the same answer.
+__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t nthreads, bool pred) {
+    uint32_t out;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}\n"
+        : "=r"(out)
+        : "r"(pred ? 1u : 0u), "r"(id), "r"(nthreads)
+        : "memory");
+    return out != 0;
+}
+
 #endif  // __CUDACC__
 
 }  // namespace tvq

@@ -24,6 +24,14 @@ __device__ __forceinline__ int8_t q8_f64(double v) {
     return static_cast<int8_t>(static_cast<int>(r));
 }
 
+// calibrate_minmax symmetric (tv/quantization/engine.tkv:24-30) from a
+// recorded max|x| (f32 bit pattern): scale = fl32(max(amax, 1e-8) / 127).
+__device__ __forceinline__ float scale_from_amax_bits(uint32_t amax_bits) {
+    double am = static_cast<double>(__uint_as_float(amax_bits));
+    if (am < 0.00000001) am = 0.00000001;
+    return __double2float_rn(am / 127.0);
+}
+
 // 1/scale of tv/quantization/engine.tkv:219-222 (and :244-246), kept as a
 // binary64 value and as a float pair hi + lo (|hi + lo - inv| <= 2^-48 |inv|).
 struct InvScale {
@@ -154,6 +162,68 @@ __device__ __forceinline__ float epilogue_exact(float ah, float ar, float sa, fl
     float y;
     if (!epilogue_fast(ah, ar, sa, sw, b, y)) y = epilogue_slow(ah, ar, sa, sw, b, per_channel);
     return y;
+}
+
+// ---- pairs of floats in one 64-bit register for the f32x2 arithmetic of
+// sm_100: two independent IEEE binary32 operations per instruction, with
+// the rounding of the scalar forms (.rn unless named).
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+#define TVQ_F2_BINOP(name, instr)                                  \
+    __device__ __forceinline__ uint64_t name(uint64_t a, uint64_t b) { \
+        uint64_t r;                                                \
+        asm(instr " %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));       \
+        return r;                                                  \
+    }
+TVQ_F2_BINOP(f2_add, "add.rn.f32x2")
+TVQ_F2_BINOP(f2_sub, "sub.rn.f32x2")
+TVQ_F2_BINOP(f2_mul, "mul.rn.f32x2")
+TVQ_F2_BINOP(f2_sub_rd, "sub.rm.f32x2")
+TVQ_F2_BINOP(f2_add_ru, "add.rp.f32x2")
+#undef TVQ_F2_BINOP
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_abs(uint64_t a) { return a & 0x7FFFFFFF7FFFFFFFull; }
+__device__ __forceinline__ uint64_t f2_neg(uint64_t a) { return a ^ 0x8000000080000000ull; }
+
+// epilogue_fast for two columns at once, accumulators below 2^24 in
+// magnitude (ar = 0): the same operations as the scalar form, so the same
+// results and the same decisions.  Bit j of the return value is set when
+// column j needs the f64 chain.
+__device__ __forceinline__ uint32_t epilogue_fast_x2(float ah0, float ah1, float sa, float sw0, float sw1, float b0,
+                                                     float b1, float& y0, float& y1) {
+    const uint64_t SA = f2_pack(sa, sa), SW = f2_pack(sw0, sw1), AH = f2_pack(ah0, ah1), B = f2_pack(b0, b1);
+    const uint64_t SH = f2_mul(SA, SW);
+    const uint64_t SL = f2_fma(SA, SW, f2_neg(SH));
+    const uint64_t P1 = f2_mul(AH, SH);
+    const uint64_t E1 = f2_fma(AH, SH, f2_neg(P1));
+    const uint64_t PL = f2_fma(AH, SL, E1);
+    const uint64_t S = f2_add(P1, B);
+    const uint64_t BB = f2_sub(S, P1);
+    const uint64_t E2 = f2_add(f2_sub(P1, f2_sub(S, BB)), f2_sub(B, BB));
+    const uint64_t LO = f2_add(E2, PL);
+    const uint64_t Y = f2_add(S, LO);
+    const uint64_t THR = f2_fma(f2_add(f2_abs(P1), f2_abs(B)), f2_pack(9.094947017729282e-13f, 9.094947017729282e-13f),
+                                f2_pack(1e-37f, 1e-37f));
+    const uint64_t YLO = f2_add(S, f2_sub_rd(LO, THR));
+    const uint64_t YHI = f2_add(S, f2_add_ru(LO, THR));
+    float lo0, lo1, hi0, hi1;
+    f2_unpack(Y, y0, y1);
+    f2_unpack(YLO, lo0, lo1);
+    f2_unpack(YHI, hi0, hi1);
+    const float a0 = fabsf(y0), a1 = fabsf(y1);
+    const bool ok0 = (lo0 == hi0) && (a0 >= 7.888609052210118e-31f) && (a0 < 3.0e38f);
+    const bool ok1 = (lo1 == hi1) && (a1 >= 7.888609052210118e-31f) && (a1 < 3.0e38f);
+    return (ok0 ? 0u : 1u) | (ok1 ? 0u : 2u);
 }
 
 // Error-free sum of two floats.

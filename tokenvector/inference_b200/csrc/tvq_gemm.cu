@@ -115,18 +115,40 @@ __device__ __forceinline__ float gelu_tanh_f32(float x) {
 
 __device__ __forceinline__ float gelu_erf_f32(float v) {
     // gelu_erf with the Abramowitz-Stegun 7.1.26 erf, tv/training/tensor.tkv:165-190
-    const float x = v * 0.70710678118654752f;
+    // (every operation spelled out, so that gelu_erf_x2 matches it bit for bit)
+    const float x = __fmul_rn(v, 0.70710678118654752f);
     const float ax = fabsf(x);
     const float t = __fdividef(1.0f, fmaf(0.3275911f, ax, 1.0f));
-    float poly = 1.061405429f;
-    poly = poly * t - 1.453152027f;
-    poly = poly * t + 1.421413741f;
-    poly = poly * t - 0.284496736f;
-    poly = poly * t + 0.254829592f;
-    poly = poly * t;
-    float e = 1.0f - __expf(-ax * ax) * poly;
-    e = (x < 0.0f) ? -e : e;
-    return 0.5f * v * (1.0f + e);
+    float poly = fmaf(1.061405429f, t, -1.453152027f);
+    poly = fmaf(poly, t, 1.421413741f);
+    poly = fmaf(poly, t, -0.284496736f);
+    poly = fmaf(poly, t, 0.254829592f);
+    poly = __fmul_rn(poly, t);
+    float e = fmaf(-__expf(__fmul_rn(-ax, ax)), poly, 1.0f);
+    e = __uint_as_float(__float_as_uint(e) ^ (__float_as_uint(x) & 0x80000000u));  // erf is odd
+    return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, e));
+}
+
+// gelu_erf_f32 of two values with the f32x2 instructions (the reciprocal and
+// exponential stay scalar): the same operations, the same results.
+__device__ __forceinline__ void gelu_erf_x2(float& v0, float& v1) {
+    const uint64_t V = f2_pack(v0, v1);
+    const uint64_t X = f2_mul(V, f2_pack(0.70710678118654752f, 0.70710678118654752f));
+    const uint64_t AX = f2_abs(X);
+    float d0, d1;
+    f2_unpack(f2_fma(f2_pack(0.3275911f, 0.3275911f), AX, f2_pack(1.0f, 1.0f)), d0, d1);
+    const uint64_t T = f2_pack(__fdividef(1.0f, d0), __fdividef(1.0f, d1));
+    uint64_t P = f2_fma(f2_pack(1.061405429f, 1.061405429f), T, f2_pack(-1.453152027f, -1.453152027f));
+    P = f2_fma(P, T, f2_pack(1.421413741f, 1.421413741f));
+    P = f2_fma(P, T, f2_pack(-0.284496736f, -0.284496736f));
+    P = f2_fma(P, T, f2_pack(0.254829592f, 0.254829592f));
+    P = f2_mul(P, T);
+    float m0, m1;
+    f2_unpack(f2_mul(f2_neg(AX), AX), m0, m1);
+    const uint64_t NEX = f2_pack(-__expf(m0), -__expf(m1));
+    uint64_t E = f2_fma(NEX, P, f2_pack(1.0f, 1.0f));
+    E ^= X & 0x8000000080000000ull;  // erf is odd
+    f2_unpack(f2_mul(f2_mul(f2_pack(0.5f, 0.5f), V), f2_add(f2_pack(1.0f, 1.0f), E)), v0, v1);
 }
 
 __device__ __forceinline__ float apply_act(float y, int act) {
@@ -270,7 +292,8 @@ struct Cfg {
     static constexpr uint32_t TMEM_COLS = NACC * BN;  // 128/256/512: powers of two
     static constexpr uint32_t RING = STAGES * NS * (A_BYTES + B_BYTES);
     static constexpr uint32_t EPI = EpiOf<KIND>::EPI_WARPS * 32 * EpiOf<KIND>::CH * 4;  // per-warp 32 x CH f32 staging
-    static constexpr uint32_t SMEM = RING + EPI + 1024 /*align*/ + 512 /*barriers*/;
+    static constexpr uint32_t COLS = 2 * 2 * BN * 4;  // per-column scale and bias of a tile, double-buffered
+    static constexpr uint32_t SMEM = RING + EPI + COLS + 1024 /*align*/ + 512 /*barriers*/;
 };
 
 template <int KIND, int BN>
@@ -285,7 +308,8 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;                                // stage s: NS parts of A_BYTES
     uint8_t* sB = smem + STAGES * NS * C::A_BYTES;     // stage s: NS parts of B_BYTES
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING + C::EPI);
+    float* colv = reinterpret_cast<float*>(smem + C::RING + C::EPI);  // [2 buffers][scale BN | bias BN]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING + C::EPI + C::COLS);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + C::NACC;
@@ -427,9 +451,6 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
         InvScale qs{0.0, 0.0f, 0.0f};
         if (p.Yq) qs = make_inv_scale(static_cast<double>(__ldg(p.scale_out)));
         EpiCtx ec{(p.n & 3) == 0, qs};
-        // 16-byte vector loads of the per-column scales / bias need aligned bases
-        const bool vec_cols = ec.vec_ok && (!per_channel || (reinterpret_cast<uintptr_t>(p.scales_w) & 15) == 0) &&
-                              (!bias_on || (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0);
         float amax = 0.0f;
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(eg * 32) << 16);
         if constexpr (split_kind(KIND)) {
@@ -494,55 +515,57 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
             }
         } else {
         uint32_t tcount = 0;
+        const int etid = threadIdx.x - 128;  // 0 .. EPI_WARPS * 32 - 1
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, tcount++) {
             const uint32_t b = tcount % C::NACC;
             const uint32_t aph = (tcount / C::NACC) & 1u;
-            {
-                // while the tile's MMAs run: pull this warp's residual rows and
-                // the tile's per-column scales / bias toward L2
-                const int mb = tile % p.num_m_blocks;
-                const int nb = tile / p.num_m_blocks;
-                const int row = mb * BM + eg * 32 + lane;
-                for (int c = half; c < BN / E::CH; c += E::EPW) {
-                    const int n0 = nb * BN + c * E::CH;
-                    if (n0 >= p.n) break;
-                    if (p.residual && row < p.m) prefetch_l2(p.residual + static_cast<int64_t>(row) * p.n + n0);
-                    if (lane == 0 && per_channel) prefetch_l2(p.scales_w + n0);
-                    if (lane == 1 && bias_on) prefetch_l2(p.bias + n0);
-                }
-            }
-            const bool got = mbar_wait(&tfull[b], aph, p.err, DEVERR_TIMEOUT_EPILOGUE);
-            __syncwarp();
-            if (!__all_sync(0xffffffffu, got)) break;
-            tc_fence_after();
             const int mb = tile % p.num_m_blocks;
             const int nb = tile / p.num_m_blocks;
             const int row0 = mb * BM + eg * 32;
+            // while the tile's MMAs run: the tile's per-column scales and
+            // bias into shared memory (buffer tcount & 1; the barrier below
+            // publishes it, and the next tile's barrier keeps it alive until
+            // every epilogue warp is done with this tile) and this warp's
+            // residual rows toward L2
+            float* csc = colv + (tcount & 1u) * 2 * BN;
+            float* cbi = csc + BN;
+            for (int i = etid; i < BN; i += E::EPI_WARPS * 32) {
+                const int n = min(nb * BN + i, p.n - 1);
+                csc[i] = per_channel ? __ldg(p.scales_w + n) : sw0;
+                cbi[i] = bias_on ? __ldg(p.bias + n) : 0.0f;
+            }
+            if (p.residual) {
+                const int row = row0 + lane;
+                for (int c = half; c < BN / E::CH; c += E::EPW) {
+                    const int n0 = nb * BN + c * E::CH;
+                    if (n0 >= p.n) break;
+                    if (row < p.m) prefetch_l2(p.residual + static_cast<int64_t>(row) * p.n + n0);
+                }
+            }
+            const bool got = mbar_wait(&tfull[b], aph, p.err, DEVERR_TIMEOUT_EPILOGUE);
+            // every epilogue warp takes the same decision (and sees the scales)
+            if (!named_bar_and(1, E::EPI_WARPS * 32, got)) break;
+            tc_fence_after();
+            float4 res_next[E::LPR];
+            if (half * E::CH + nb * BN < p.n) load_residual<E>(p, ec, lane, row0, nb * BN + half * E::CH, res_next);
 #pragma unroll 1
             for (int c = half; c < BN / E::CH; c += E::EPW) {
                 const int n0 = nb * BN + c * E::CH;
                 if (n0 >= p.n) break;  // warp-uniform
                 float4 res[E::LPR];
-                load_residual<E>(p, ec, lane, row0, n0, res);
-                // per-column scale and bias (same addresses in every lane)
+#pragma unroll
+                for (int it = 0; it < E::LPR; it++) res[it] = res_next[it];
+                // the next chunk's residual is in flight while this one is evaluated
+                if (c + E::EPW < BN / E::CH && n0 + E::EPW * E::CH < p.n)
+                    load_residual<E>(p, ec, lane, row0, n0 + E::EPW * E::CH, res_next);
+                // per-column scale and bias (shared memory, same address in every lane)
                 float swv[E::CH], bv[E::CH];
-                if (vec_cols && n0 + E::CH <= p.n) {
 #pragma unroll
-                    for (int j = 0; j < E::CH / 4; j++) {
-                        const float4 t = per_channel ? __ldg(reinterpret_cast<const float4*>(p.scales_w + n0) + j)
-                                                     : make_float4(sw0, sw0, sw0, sw0);
-                        const float4 u = bias_on ? __ldg(reinterpret_cast<const float4*>(p.bias + n0) + j)
-                                                 : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                        swv[4 * j] = t.x; swv[4 * j + 1] = t.y; swv[4 * j + 2] = t.z; swv[4 * j + 3] = t.w;
-                        bv[4 * j] = u.x; bv[4 * j + 1] = u.y; bv[4 * j + 2] = u.z; bv[4 * j + 3] = u.w;
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < E::CH; j++) {
-                        const int n = (n0 + j < p.n) ? n0 + j : p.n - 1;
-                        swv[j] = per_channel ? __ldg(p.scales_w + n) : sw0;
-                        bv[j] = bias_on ? __ldg(p.bias + n) : 0.0f;
-                    }
+                for (int j = 0; j < E::CH / 4; j++) {
+                    const float4 t = *reinterpret_cast<const float4*>(csc + c * E::CH + 4 * j);
+                    const float4 u = *reinterpret_cast<const float4*>(cbi + c * E::CH + 4 * j);
+                    swv[4 * j] = t.x; swv[4 * j + 1] = t.y; swv[4 * j + 2] = t.z; swv[4 * j + 3] = t.w;
+                    bv[4 * j] = u.x; bv[4 * j + 1] = u.y; bv[4 * j + 2] = u.z; bv[4 * j + 3] = u.w;
                 }
                 uint32_t r[E::CH];
                 __syncwarp();
@@ -555,22 +578,39 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                         if (n0 + j < p.n) dst[j] = static_cast<int32_t>(r[j]);
                 }
                 if (p.acc_only) continue;  // MatMulInteger: the accumulators are the result
-                // fast path for all columns (straight-line), rare f64 fix-ups after
+                // fast path for all columns (straight-line), rare f64 fix-ups after;
+                // accumulators below 2^24 (exact in f32: nearly always) two
+                // columns per f32x2 instruction
                 float y[E::CH];
                 uint32_t bad = 0;
+                bool small = true;
+                if (KIND == GEMM_I8) {
 #pragma unroll
-                for (int j = 0; j < E::CH; j++) {
-                    float ah, ar;
-                    if (KIND == GEMM_I8) {
-                        const int a = static_cast<int>(r[j]);
-                        ah = __int2float_rn(a);
-                        ar = __int2float_rn(a - __float2int_rn(ah));
-                    } else {
-                        ah = __uint_as_float(r[j]);
-                        ar = 0.0f;
+                    for (int j = 0; j < E::CH; j++) small &= (r[j] + 0x01000000u) < 0x02000000u;  // |acc| < 2^24
+                }
+                if (small) {
+#pragma unroll
+                    for (int j = 0; j < E::CH; j += 2) {
+                        const float a0 = (KIND == GEMM_I8) ? __int2float_rn(static_cast<int>(r[j])) : __uint_as_float(r[j]);
+                        const float a1 =
+                            (KIND == GEMM_I8) ? __int2float_rn(static_cast<int>(r[j + 1])) : __uint_as_float(r[j + 1]);
+                        bad |= epilogue_fast_x2(a0, a1, sa, swv[j], swv[j + 1], bv[j], bv[j + 1], y[j], y[j + 1]) << j;
                     }
-                    const bool ok = epilogue_fast(ah, ar, sa, swv[j], bv[j], y[j]);
-                    bad |= ok ? 0u : (1u << j);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < E::CH; j++) {
+                        float ah, ar;
+                        if (KIND == GEMM_I8) {
+                            const int a = static_cast<int>(r[j]);
+                            ah = __int2float_rn(a);
+                            ar = __int2float_rn(a - __float2int_rn(ah));
+                        } else {
+                            ah = __uint_as_float(r[j]);
+                            ar = 0.0f;
+                        }
+                        const bool ok = epilogue_fast(ah, ar, sa, swv[j], bv[j], y[j]);
+                        bad |= ok ? 0u : (1u << j);
+                    }
                 }
                 if (bad) {
 #pragma unroll
@@ -602,7 +642,7 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                 }
                 if (p.act == TVQ_ACT_GELU_ERF) {
 #pragma unroll
-                    for (int j = 0; j < E::CH; j++) y[j] = gelu_erf_f32(y[j]);
+                    for (int j = 0; j < E::CH; j += 2) gelu_erf_x2(y[j], y[j + 1]);
                 } else if (p.act == TVQ_ACT_GELU_TANH) {
 #pragma unroll
                     for (int j = 0; j < E::CH; j++) y[j] = gelu_tanh_f32(y[j]);
@@ -898,20 +938,27 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
         bn = env_bn;
     }
     if (split && bn > 128) bn = 128;  // their partial sums live in registers
-    if (bn == 0) {
-        // Tile width with the least work on the busiest SM: rounds of tiles
-        // (ceil(tiles / SMs)) x BN columns; ties go to the wider tile (fewer,
-        // longer MMA runs per operand load).
-        // The split-TF32 form keeps 128 (its N = 64 MMAs run well below the
-        // TF32 rate) unless that leaves SMs without a tile.
+    if (bn == 0 && split) {
+        // The split forms keep 128 (their N = 64 MMAs run well below the
+        // tensor rate) unless that leaves SMs without a tile.
+        bn = (static_cast<int64_t>(p.num_m_blocks) * ((g.n + 127) / 128) >= ds->sm_count) ? 128 : 64;
+    } else if (bn == 0) {
+        // Tile width with the least time on the busiest SM: rounds of tiles
+        // (ceil(tiles / SMs)) x the time of one tile, the slower of its K
+        // loop and its epilogue (which overlap across consecutive tiles).
+        // Per 128-byte k-block a 128 x BN tile takes ~0.37 / 0.45 / 0.53 us
+        // at BN 64 / 128 / 256 (operand traffic bounds the narrow tiles, so
+        // wider tiles do more work per byte), and the exact epilogue ~0.55 ns
+        // per output element; ~1 us of fixed cost per tile.  (Measured on
+        // B200 over the GPT-2 124M and XL layer shapes.)
         const int64_t mblk = p.num_m_blocks;
-        int64_t best = -1;
+        double best = -1.0;
         for (int cand : {256, 128, 64}) {
-            if (split && cand > 128) continue;
-            if (split && cand == 64 && mblk * ((g.n + 127) / 128) >= ds->sm_count) continue;
             const int64_t tiles = mblk * ((g.n + cand - 1) / cand);
-            const int64_t cost = (tiles + ds->sm_count - 1) / ds->sm_count * cand;
-            if (best < 0 || cost < best) {
+            const double t_kb = cand == 256 ? 0.53 : cand == 128 ? 0.45 : 0.37;
+            const double t_tile = std::max(p.num_k_blocks * t_kb, 128.0 * cand * 0.55e-3) + 1.0;
+            const double cost = static_cast<double>((tiles + ds->sm_count - 1) / ds->sm_count) * t_tile;
+            if (best < 0.0 || cost < best * 0.999) {  // ties go to the wider tile
                 best = cost;
                 bn = cand;
             }

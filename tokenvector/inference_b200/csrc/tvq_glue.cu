@@ -697,9 +697,7 @@ __global__ void scale_from_amax_kernel(const uint32_t* __restrict__ amax, float*
     griddep_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    double am = static_cast<double>(__uint_as_float(amax[i]));
-    if (am < 0.00000001) am = 0.00000001;
-    scale[i] = __double2float_rn(am / 127.0);
+    scale[i] = scale_from_amax_bits(amax[i]);
 }
 
 int launch_scale_from_amax(const uint32_t* amax, float* scale, int n, cudaStream_t st) {

@@ -13,6 +13,10 @@ int launch_minmax_reset(uint32_t* mm, cudaStream_t st);
 int launch_minmax_accumulate(const float* x, int64_t n, uint32_t* mm, float* first, cudaStream_t st);
 int launch_minmax_finalize(const uint32_t* mm, const float* first, int symmetric, float* params, cudaStream_t st);
 int launch_quantize_i8(const float* x, int8_t* q, int64_t n, const float* scale_dev, cudaStream_t st);
+// Calibrate-then-quantize: scale = fl32(max(*amax, 1e-8) / 127) (stored to
+// *scale_out), then quantize_int8_symmetric with it; one launch.
+int launch_quantize_i8_amax(const float* x, int8_t* q, int64_t n, const uint32_t* amax, float* scale_out,
+                            cudaStream_t st);
 int launch_dequantize_i8(const int8_t* q, float* y, int64_t rows, int64_t cols, const float* scales_dev,
                          int per_row, cudaStream_t st);
 // mode 0: per-channel calibrate+quantize, 1: per-channel quantize with given

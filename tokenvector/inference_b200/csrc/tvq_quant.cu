@@ -14,6 +14,7 @@
 // shared-memory reductions, one atomic per block.
 #include <cuda_fp8.h>
 
+#include <algorithm>
 #include <cstring>
 
 #include "tvq_common.cuh"
@@ -165,11 +166,21 @@ int launch_minmax_finalize(const uint32_t* mm, const float* first, int symmetric
 // ------------------------------------------------------------ K2: quantize
 // quantize_int8_symmetric, tv/quantization/engine.tkv:216-226:
 // q = clamp(int(round(x * (1.0/scale))), -127, 127).  16 elements per thread
-// step: four 16-byte loads, one 16-byte store.
+// step: four 16-byte loads, one 16-byte store.  With amax set, the scale is
+// first calibrated from the recorded max|x| (calibrate_minmax, engine.tkv:
+// 13-36) by every block and block 0 stores it to scale_out.
 __global__ void quantize_i8_kernel(const float* __restrict__ x, int8_t* __restrict__ q, int64_t n,
-                                   const float* __restrict__ scale) {
+                                   const float* __restrict__ scale, const uint32_t* __restrict__ amax,
+                                   float* __restrict__ scale_out) {
     griddep_wait();
-    const InvScale qs = make_inv_scale(static_cast<double>(__ldg(scale)));
+    float sc;
+    if (amax) {
+        sc = scale_from_amax_bits(*amax);
+        if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = sc;
+    } else {
+        sc = __ldg(scale);
+    }
+    const InvScale qs = make_inv_scale(static_cast<double>(sc));
     const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const bool vec = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(q)) & 15) == 0;
@@ -196,7 +207,15 @@ int launch_quantize_i8(const float* x, int8_t* q, int64_t n, const float* scale_
     if (n <= 0) return TVQ_OK;
     const int threads = 256;
     return launch_pdl(quantize_i8_kernel, dim3(grid_for((n + 15) / 16, threads, 8)), dim3(threads), 0, st, x, q, n,
-                      scale_dev);
+                      scale_dev, static_cast<const uint32_t*>(nullptr), static_cast<float*>(nullptr));
+}
+
+int launch_quantize_i8_amax(const float* x, int8_t* q, int64_t n, const uint32_t* amax, float* scale_out,
+                            cudaStream_t st) {
+    const int threads = 256;
+    const int64_t work = std::max<int64_t>((n + 15) / 16, 1);  // n = 0 still stores the scale
+    return launch_pdl(quantize_i8_kernel, dim3(grid_for(work, threads, 8)), dim3(threads), 0, st, x, q, n,
+                      static_cast<const float*>(nullptr), amax, scale_out);
 }
 
 // dequantize_int8_symmetric / _per_channel, engine.tkv:229-234, 253-262:

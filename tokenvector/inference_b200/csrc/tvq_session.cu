@@ -77,18 +77,28 @@ struct Session {
     std::vector<int> seg_host;
     int T = 0, nseg = 0, ntiles = 0, logits_mode = 0;
     bool prepared = false;
-    cudaGraphExec_t gexec = nullptr;
+    // captured graphs per mode (Mode below), rebuilt after prepare
+    cudaGraphExec_t gexec[3] = {nullptr, nullptr, nullptr};
+    int64_t graph_kernels[3] = {0, 0, 0};  // kernel nodes of each captured graph
+    int last_mode = -1;                    // mode of the graph launched last
     // optional stage events recorded inside the captured graph (profiling)
     bool profile = false;
     std::vector<cudaEvent_t> ev;
     std::vector<int> ev_stage;  // stage id of the interval ending at ev[i]
     bool capturing = false;
-    int64_t graph_kernels = 0;  // kernel nodes of the captured forward
 
     int64_t logits_rows() const { return logits_mode == 0 ? T : nseg; }
 
+    void drop_graphs() {
+        for (cudaGraphExec_t& g : gexec)
+            if (g) {
+                cudaGraphExecDestroy(g);
+                g = nullptr;
+            }
+    }
+
     ~Session() {
-        if (gexec) cudaGraphExecDestroy(gexec);
+        drop_graphs();
         for (cudaEvent_t e : ev) cudaEventDestroy(e);
         for (void* p : allocs) cudaFree(p);
         if (st) cudaStreamDestroy(st);
@@ -189,8 +199,10 @@ int attention(Session& s, float* out, int8_t* outq, const float* qscale, uint32_
 }
 
 // Stage ids reported by tvq_session_stage_times.
+// ST_QUANT: the calibrate-then-quantize passes of a calibrating (dynamic)
+// forward.
 enum Stage { ST_EMBED = 0, ST_LN = 1, ST_GEMM_QKV = 2, ST_ATTN = 3, ST_GEMM_PROJ = 4, ST_GEMM_FC = 5, ST_GEMM_MPROJ = 6,
-             ST_LM_HEAD = 7, ST_COUNT = 8 };
+             ST_LM_HEAD = 7, ST_QUANT = 8, ST_COUNT = 9 };
 
 // Marks the end of a stage inside the captured graph (profiling only).
 int mark(Session& s, int stage) {
@@ -203,14 +215,16 @@ int mark(Session& s, int stage) {
     return TVQ_OK;
 }
 
-// The forward pass for the prepared layout, enqueued on s.st.
-int enqueue_forward(Session& s, bool calibrating) {
+// What a captured graph runs: the whole forward (ids -> logits), or the
+// transformer blocks alone on the hidden states in s.x with static
+// activation scales or with per-call (dynamic) calibration.
+enum Mode { M_FORWARD = 0, M_LAYERS = 1, M_LAYERS_DYNAMIC = 2 };
+
+// The transformer blocks on s.x (in place), enqueued on s.st.
+int enqueue_layers(Session& s, bool calibrating) {
     const int T = s.T, d = s.d;
-    STEP(mark(s, -1));
     if (s.attn_tc && s.ncomb > 0)  // merge counters start at 0 (a run that stopped early may leave them set)
         TVQ_CUDA(cudaMemsetAsync(s.counters, 0, sizeof(int) * static_cast<size_t>(s.ncomb) * s.heads, s.st));
-    STEP(launch_embed(s.ids, s.tok_start, s.wte, s.wpe, s.x, T, d, s.vocab, s.max_pos, s.err, s.st));
-    STEP(mark(s, ST_EMBED));
     for (int l = 0; l < s.layers; l++) {
         LayerW& w = s.L[l];
         float* sc = s.act_scale + 4 * l;
@@ -218,49 +232,63 @@ int enqueue_forward(Session& s, bool calibrating) {
         // ln_1 -> int8 (c_attn input)
         if (calibrating) {
             STEP(launch_layernorm(s.x, w.ln[0], w.ln[1], s.hf, nullptr, nullptr, am + 0, T, d, s.eps, s.st));
-            STEP(launch_scale_from_amax(am + 0, sc + 0, 1, s.st));
-            STEP(launch_quantize_i8(s.hf, s.aq, static_cast<int64_t>(T) * d, sc + 0, s.st));
+            STEP(mark(s, ST_LN));
+            STEP(launch_quantize_i8_amax(s.hf, s.aq, static_cast<int64_t>(T) * d, am + 0, sc + 0, s.st));
+            STEP(mark(s, ST_QUANT));
         } else {
             STEP(launch_layernorm(s.x, w.ln[0], w.ln[1], nullptr, s.aq, sc + 0, nullptr, T, d, s.eps, s.st));
+            STEP(mark(s, ST_LN));
         }
-        STEP(mark(s, ST_LN));
         // c_attn: qkv = dequant(aq Wqkv) + b
         STEP(gemm(s, s.aq, w.lin[0], sc + 0, s.qkv, nullptr, nullptr, nullptr, nullptr, TVQ_ACT_NONE, s.attn_tc));
         STEP(mark(s, ST_GEMM_QKV));
         // causal attention -> int8 context (attn c_proj input)
         if (calibrating) {
             STEP(attention(s, s.hf, nullptr, nullptr, am + 1));
-            STEP(launch_scale_from_amax(am + 1, sc + 1, 1, s.st));
-            STEP(launch_quantize_i8(s.hf, s.aq, static_cast<int64_t>(T) * d, sc + 1, s.st));
+            STEP(mark(s, ST_ATTN));
+            STEP(launch_quantize_i8_amax(s.hf, s.aq, static_cast<int64_t>(T) * d, am + 1, sc + 1, s.st));
+            STEP(mark(s, ST_QUANT));
         } else {
             STEP(attention(s, nullptr, s.aq, sc + 1, nullptr));
+            STEP(mark(s, ST_ATTN));
         }
-        STEP(mark(s, ST_ATTN));
         // attn c_proj + residual, in place on x
         STEP(gemm(s, s.aq, w.lin[1], sc + 1, s.x, s.x, nullptr, nullptr, nullptr, TVQ_ACT_NONE));
         STEP(mark(s, ST_GEMM_PROJ));
         // ln_2 -> int8 (c_fc input)
         if (calibrating) {
             STEP(launch_layernorm(s.x, w.ln[2], w.ln[3], s.hf, nullptr, nullptr, am + 2, T, d, s.eps, s.st));
-            STEP(launch_scale_from_amax(am + 2, sc + 2, 1, s.st));
-            STEP(launch_quantize_i8(s.hf, s.aq, static_cast<int64_t>(T) * d, sc + 2, s.st));
+            STEP(mark(s, ST_LN));
+            STEP(launch_quantize_i8_amax(s.hf, s.aq, static_cast<int64_t>(T) * d, am + 2, sc + 2, s.st));
+            STEP(mark(s, ST_QUANT));
         } else {
             STEP(launch_layernorm(s.x, w.ln[2], w.ln[3], nullptr, s.aq, sc + 2, nullptr, T, d, s.eps, s.st));
+            STEP(mark(s, ST_LN));
         }
-        STEP(mark(s, ST_LN));
         // c_fc + erf GELU -> int8 (mlp c_proj input)
         if (calibrating) {
             STEP(gemm(s, s.aq, w.lin[2], sc + 2, s.hf, nullptr, nullptr, nullptr, am + 3, TVQ_ACT_GELU_ERF));
-            STEP(launch_scale_from_amax(am + 3, sc + 3, 1, s.st));
-            STEP(launch_quantize_i8(s.hf, s.hq, static_cast<int64_t>(T) * s.ffn, sc + 3, s.st));
+            STEP(mark(s, ST_GEMM_FC));
+            STEP(launch_quantize_i8_amax(s.hf, s.hq, static_cast<int64_t>(T) * s.ffn, am + 3, sc + 3, s.st));
+            STEP(mark(s, ST_QUANT));
         } else {
             STEP(gemm(s, s.aq, w.lin[2], sc + 2, nullptr, nullptr, s.hq, sc + 3, nullptr, TVQ_ACT_GELU_ERF));
+            STEP(mark(s, ST_GEMM_FC));
         }
-        STEP(mark(s, ST_GEMM_FC));
         // mlp c_proj + residual, in place on x
         STEP(gemm(s, s.hq, w.lin[3], sc + 3, s.x, s.x, nullptr, nullptr, nullptr, TVQ_ACT_NONE));
         STEP(mark(s, ST_GEMM_MPROJ));
     }
+    return TVQ_OK;
+}
+
+// The forward pass for the prepared layout, enqueued on s.st.
+int enqueue_forward(Session& s, bool calibrating) {
+    const int T = s.T, d = s.d;
+    STEP(mark(s, -1));
+    STEP(launch_embed(s.ids, s.tok_start, s.wte, s.wpe, s.x, T, d, s.vocab, s.max_pos, s.err, s.st));
+    STEP(mark(s, ST_EMBED));
+    STEP(enqueue_layers(s, calibrating));
     // ln_f and the tied LM head (gpt2_ref.tkv:589-610), fp32
     STEP(launch_layernorm(s.x, s.lnf_g, s.lnf_b, s.xf, nullptr, nullptr, nullptr, T, d, s.eps, s.st));
     STEP(mark(s, ST_LN));
@@ -294,8 +322,9 @@ int enqueue_forward(Session& s, bool calibrating) {
     return TVQ_OK;
 }
 
-int check_ready(Session& s) {
-    TVQ_CHECK(s.wte && s.wpe && s.lnf_g && s.lnf_b, TVQ_ERR_INVALID, "embeddings / final layernorm not set");
+int check_ready(Session& s, bool layers_only = false) {
+    TVQ_CHECK(layers_only || (s.vocab > 0 && s.wte && s.wpe && s.lnf_g && s.lnf_b), TVQ_ERR_INVALID,
+              "embeddings / final layernorm not set");
     for (int l = 0; l < s.layers; l++) {
         for (int i = 0; i < 4; i++) TVQ_CHECK(s.L[l].ln[i], TVQ_ERR_INVALID, "layernorm not set");
         for (int i = 0; i < 4; i++) TVQ_CHECK(s.L[l].lin[i].set, TVQ_ERR_INVALID, "linear not set");
@@ -316,18 +345,31 @@ int check_err(Session& s, cudaStream_t st) {
     return check_device_error(st);
 }
 
-int capture(Session& s) {
-    if (s.gexec) {
-        cudaGraphExecDestroy(s.gexec);
-        s.gexec = nullptr;
+int capture(Session& s, int mode) {
+    if (s.profile) {
+        // stage events belong to one graph at a time
+        s.drop_graphs();
+        for (cudaEvent_t e : s.ev) cudaEventDestroy(e);
+        s.ev.clear();
+        s.ev_stage.clear();
+    } else if (s.gexec[mode]) {
+        cudaGraphExecDestroy(s.gexec[mode]);
+        s.gexec[mode] = nullptr;
     }
-    for (cudaEvent_t e : s.ev) cudaEventDestroy(e);
-    s.ev.clear();
-    s.ev_stage.clear();
     cudaGraph_t g = nullptr;
     TVQ_CUDA(cudaStreamBeginCapture(s.st, cudaStreamCaptureModeRelaxed));
     s.capturing = true;
-    int rc = enqueue_forward(s, false);
+    int rc = TVQ_OK;
+    if (mode == M_FORWARD) {
+        rc = enqueue_forward(s, false);
+    } else {
+        rc = mark(s, -1);
+        if (!rc && mode == M_LAYERS_DYNAMIC) {  // calibrate_minmax on this call's activations only
+            const cudaError_t me = cudaMemsetAsync(s.act_amax, 0, sizeof(uint32_t) * 4 * s.layers, s.st);
+            if (me != cudaSuccess) rc = cuda_fail(me, "cudaMemsetAsync (amax)");
+        }
+        if (!rc) rc = enqueue_layers(s, mode == M_LAYERS_DYNAMIC);
+    }
     s.capturing = false;
     cudaError_t e = cudaStreamEndCapture(s.st, &g);
     if (rc) {
@@ -345,11 +387,11 @@ int capture(Session& s) {
                     cudaGraphNodeType t;
                     if (cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) k++;
                 }
-                s.graph_kernels = k;
+                s.graph_kernels[mode] = k;
             }
         }
     }
-    e = cudaGraphInstantiate(&s.gexec, g, 0);
+    e = cudaGraphInstantiate(&s.gexec[mode], g, 0);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
     return TVQ_OK;
@@ -365,8 +407,8 @@ extern "C" {
 int tvq_session_create(int device, int64_t vocab, int64_t d_model, int64_t n_heads, int64_t n_layers, int64_t d_ffn,
                        int64_t max_pos, double ln_eps, int64_t max_tokens, int64_t* handle) {
     TVQ_CHECK(handle, TVQ_ERR_INVALID, "null handle pointer");
-    TVQ_CHECK(vocab > 0 && d_model > 0 && n_heads > 0 && n_layers >= 0 && d_ffn > 0 && max_pos > 0 && max_tokens > 0,
-              TVQ_ERR_INVALID, "model sizes must be positive");
+    TVQ_CHECK(vocab >= 0 && d_model > 0 && n_heads > 0 && n_layers >= 0 && d_ffn > 0 && max_pos > 0 && max_tokens > 0,
+              TVQ_ERR_INVALID, "model sizes must be positive (vocab 0: a layer stack without embeddings)");
     TVQ_CHECK(d_model % n_heads == 0, TVQ_ERR_INVALID, "d_model must be a multiple of n_heads");
     TVQ_CHECK(d_model % 16 == 0 && d_ffn % 16 == 0, TVQ_ERR_UNSUPPORTED, "d_model and d_ffn must be multiples of 16");
     TVQ_CHECK(max_tokens < (1 << 30) && vocab < (1 << 30), TVQ_ERR_UNSUPPORTED, "size too large");
@@ -442,6 +484,7 @@ int tvq_session_destroy(int64_t handle) {
 int tvq_session_set_embeddings(int64_t handle, const float* wte, const float* wpe) {
     SESSION(handle)
     TVQ_CHECK(wte && wpe, TVQ_ERR_INVALID, "null buffer");
+    TVQ_CHECK(S->vocab > 0, TVQ_ERR_INVALID, "the session was created without a vocabulary (layer stack)");
     const size_t vd = static_cast<size_t>(S->vocab) * S->d;
     if (!S->wte) STEP(S->alloc(&S->wte, vd));
     if (!S->wte_hi) STEP(S->alloc(&S->wte_hi, vd));
@@ -671,10 +714,7 @@ int tvq_session_prepare(int64_t handle, const int64_t* seg, int64_t n_seg, int l
         S->logits_cap = need;
     }
     S->prepared = true;
-    if (S->gexec) {
-        cudaGraphExecDestroy(S->gexec);
-        S->gexec = nullptr;
-    }
+    S->drop_graphs();
     return TVQ_OK;
 }
 
@@ -696,16 +736,41 @@ int tvq_session_forward(int64_t handle, const int64_t* ids, int ids_on_device, f
     STEP(check_ready(*S));
     const size_t out_elems = static_cast<size_t>(S->logits_rows()) * S->vocab;
     TVQ_CHECK(!logits || logits_len >= static_cast<int64_t>(out_elems), TVQ_ERR_SIZE, "logits buffer too small");
-    if (!S->gexec) STEP(capture(*S));
+    if (!S->gexec[M_FORWARD]) STEP(capture(*S, M_FORWARD));
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : S->st;
     if (ids)
         TVQ_CUDA(cudaMemcpyAsync(S->ids, ids, sizeof(int64_t) * S->T,
                                  ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
-    TVQ_CUDA(cudaGraphLaunch(S->gexec, st));
+    TVQ_CUDA(cudaGraphLaunch(S->gexec[M_FORWARD], st));
+    S->last_mode = M_FORWARD;
     if (logits)
         TVQ_CUDA(cudaMemcpyAsync(logits, S->logits, out_elems * sizeof(float),
                                  logits_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
     if ((ids && !ids_on_device) || (logits && !logits_on_device)) return check_err(*S, st);
+    return TVQ_OK;
+}
+
+int tvq_session_run_layers(int64_t handle, const float* x, int x_on_device, float* y, int y_on_device, int dynamic,
+                           void* stream) {
+    SESSION(handle)
+    STEP(check_ready(*S, true));
+    TVQ_CHECK(dynamic == 0 || dynamic == 1, TVQ_ERR_INVALID, "dynamic must be 0 (static scales) or 1");
+    const int mode = dynamic ? M_LAYERS_DYNAMIC : M_LAYERS;
+    if (!S->gexec[mode]) STEP(capture(*S, mode));
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : S->st;
+    const size_t bytes = sizeof(float) * static_cast<size_t>(S->T) * S->d;
+    if (x) TVQ_CUDA(cudaMemcpyAsync(S->x, x, bytes, x_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+    TVQ_CUDA(cudaGraphLaunch(S->gexec[mode], st));
+    S->last_mode = mode;
+    if (y) TVQ_CUDA(cudaMemcpyAsync(y, S->x, bytes, y_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
+    if ((x && !x_on_device) || (y && !y_on_device)) return check_err(*S, st);
+    return TVQ_OK;
+}
+
+int tvq_session_hidden(int64_t handle, float** x_dev) {
+    SESSION(handle)
+    TVQ_CHECK(x_dev, TVQ_ERR_INVALID, "null out pointer");
+    *x_dev = S->x;
     return TVQ_OK;
 }
 
@@ -721,10 +786,7 @@ int tvq_session_logits(int64_t handle, float** logits_dev, int64_t* rows, int64_
 int tvq_session_set_profiling(int64_t handle, int enable) {
     SESSION(handle)
     S->profile = enable != 0;
-    if (S->gexec) {  // recapture with or without the stage events
-        cudaGraphExecDestroy(S->gexec);
-        S->gexec = nullptr;
-    }
+    S->drop_graphs();  // recapture with or without the stage events
     return TVQ_OK;
 }
 
@@ -745,8 +807,9 @@ int tvq_session_stage_times(int64_t handle, float* ms, int64_t n) {
 int tvq_session_launches(int64_t handle, int64_t* kernels) {
     SESSION(handle)
     TVQ_CHECK(kernels, TVQ_ERR_INVALID, "null output pointer");
-    TVQ_CHECK(S->gexec, TVQ_ERR_INVALID, "no forward has been captured for this layout");
-    *kernels = S->graph_kernels;
+    TVQ_CHECK(S->last_mode >= 0 && S->gexec[S->last_mode], TVQ_ERR_INVALID,
+              "no forward has been captured for this layout");
+    *kernels = S->graph_kernels[S->last_mode];
     return TVQ_OK;
 }
 

@@ -86,21 +86,32 @@ class GPT2Weights:
 
     @staticmethod
     def random(cfg: GPT2Config, seed: int = 0) -> "GPT2Weights":
-        d, f = cfg.d_model, cfg.d_ffn
-        ones = lambda n: np.ones(n, np.float32)  # noqa: E731
-        zeros = lambda n: np.zeros(n, np.float32)  # noqa: E731
+        d = cfg.d_model
         w = GPT2Weights(cfg, gi_noise(cfg.vocab * d, seed + 1).reshape(cfg.vocab, d),
-                        gi_noise(cfg.max_pos * d, seed + 2).reshape(cfg.max_pos, d), ones(d), zeros(d))
-        for li in range(cfg.n_layers):
-            sd = seed + 10 + li * 100
-            w.layers.append(dict(
-                ln1_g=ones(d), ln1_b=zeros(d),
-                attn_w=gi_noise(d * 3 * d, sd + 1).reshape(d, 3 * d), attn_b=zeros(3 * d),
-                proj_w=gi_noise(d * d, sd + 2).reshape(d, d), proj_b=zeros(d),
-                ln2_g=ones(d), ln2_b=zeros(d),
-                fc_w=gi_noise(d * f, sd + 3).reshape(d, f), fc_b=zeros(f),
-                mp_w=gi_noise(f * d, sd + 4).reshape(f, d), mp_b=zeros(d)))
+                        gi_noise(cfg.max_pos * d, seed + 2).reshape(cfg.max_pos, d), np.ones(d, np.float32),
+                        np.zeros(d, np.float32))
+        w.layers = random_layers(cfg, seed)
         return w
+
+
+def random_layers(cfg: GPT2Config, seed: int = 0) -> list:
+    """The blocks of gpt2_init (gpt2_ref.tkv:1997-2026): N(0, 0.02) linears,
+    zero biases, LayerNorm gamma 1 / beta 0; layer l draws from seeds
+    seed + 10 + 100 l + (1..4)."""
+    d, f = cfg.d_model, cfg.d_ffn
+    ones = lambda n: np.ones(n, np.float32)  # noqa: E731
+    zeros = lambda n: np.zeros(n, np.float32)  # noqa: E731
+    out = []
+    for li in range(cfg.n_layers):
+        sd = seed + 10 + li * 100
+        out.append(dict(
+            ln1_g=ones(d), ln1_b=zeros(d),
+            attn_w=gi_noise(d * 3 * d, sd + 1).reshape(d, 3 * d), attn_b=zeros(3 * d),
+            proj_w=gi_noise(d * d, sd + 2).reshape(d, d), proj_b=zeros(d),
+            ln2_g=ones(d), ln2_b=zeros(d),
+            fc_w=gi_noise(d * f, sd + 3).reshape(d, f), fc_b=zeros(f),
+            mp_w=gi_noise(f * d, sd + 4).reshape(f, d), mp_b=zeros(d)))
+    return out
 
 
 LINEARS = (("attn_w", "attn_b"), ("proj_w", "proj_b"), ("fc_w", "fc_b"), ("mp_w", "mp_b"))
@@ -116,26 +127,26 @@ def segments_from_lengths(lengths) -> np.ndarray:
     return seg
 
 
-class GPT2Session:
-    """Device-resident INT8 GPT-2 forward on one GPU (one tvq session)."""
+def _f32(a):
+    return np.ascontiguousarray(a, np.float32)
 
-    def __init__(self, weights: GPT2Weights, device: int = 0, max_tokens: int = 1024):
-        cfg = weights.cfg
+
+class _Session:
+    """One tvq session: the blocks' weights, batch layout and scales."""
+
+    def __init__(self, cfg: GPT2Config, layers: list, vocab: int, device: int, max_tokens: int):
         self.cfg = cfg
         self.device = device
         h = C.c_int64()
-        N.call("tvq_session_create", device, cfg.vocab, cfg.d_model, cfg.n_heads, cfg.n_layers, cfg.d_ffn,
+        N.call("tvq_session_create", device, vocab, cfg.d_model, cfg.n_heads, cfg.n_layers, cfg.d_ffn,
                cfg.max_pos, float(cfg.eps), max_tokens, C.byref(h))
         self.handle = h.value
         self.max_tokens = max_tokens
-        f32 = lambda a: np.ascontiguousarray(a, np.float32)  # noqa: E731
-        N.call("tvq_session_set_embeddings", self.handle, _p(f32(weights.wte)), _p(f32(weights.wpe)))
-        N.call("tvq_session_set_layernorm", self.handle, -1, 0, _p(f32(weights.lnf_g)), _p(f32(weights.lnf_b)))
-        for li, L in enumerate(weights.layers):
-            N.call("tvq_session_set_layernorm", self.handle, li, 0, _p(f32(L["ln1_g"])), _p(f32(L["ln1_b"])))
-            N.call("tvq_session_set_layernorm", self.handle, li, 1, _p(f32(L["ln2_g"])), _p(f32(L["ln2_b"])))
+        for li, L in enumerate(layers):
+            N.call("tvq_session_set_layernorm", self.handle, li, 0, _p(_f32(L["ln1_g"])), _p(_f32(L["ln1_b"])))
+            N.call("tvq_session_set_layernorm", self.handle, li, 1, _p(_f32(L["ln2_g"])), _p(_f32(L["ln2_b"])))
             for which, (wk, bk) in enumerate(LINEARS):
-                N.call("tvq_session_set_linear_f32", self.handle, li, which, _p(f32(L[wk])), _p(f32(L[bk])), 0)
+                N.call("tvq_session_set_linear_f32", self.handle, li, which, _p(_f32(L[wk])), _p(_f32(L[bk])), 0)
         self.seg = None
         self.logits_mode = 0
 
@@ -161,15 +172,6 @@ class GPT2Session:
     def n_tokens(self) -> int:
         return int(self.seg[-1])
 
-    def logits_shape(self):
-        rows = self.n_tokens if self.logits_mode == 0 else self.seg.size - 1
-        return rows, self.cfg.vocab
-
-    def calibrate(self, ids, reset: bool = True):
-        ids = np.ascontiguousarray(ids, np.int64)
-        assert ids.size == self.n_tokens
-        N.call("tvq_session_calibrate", self.handle, _p(ids), 0, 1 if reset else 0)
-
     def act_scales(self) -> np.ndarray:
         out = np.empty(4 * self.cfg.n_layers, np.float32)
         N.call("tvq_session_get_act_scales", self.handle, _p(out), out.size)
@@ -186,6 +188,56 @@ class GPT2Session:
         s = np.empty(n, np.float32)
         N.call("tvq_session_get_linear_i8", self.handle, layer, which, _p(w), _p(s))
         return w, s
+
+    STAGES = ("embed", "layernorm", "gemm_c_attn", "attention", "gemm_attn_proj", "gemm_c_fc", "gemm_mlp_proj",
+              "lm_head", "quantize")
+
+    def set_profiling(self, on: bool):
+        N.call("tvq_session_set_profiling", self.handle, 1 if on else 0)
+
+    def stage_times(self) -> dict:
+        out = np.zeros(len(self.STAGES), np.float32)
+        N.call("tvq_session_stage_times", self.handle, _p(out), out.size)
+        return dict(zip(self.STAGES, out.tolist()))
+
+    def sync(self):
+        N.call("tvq_session_sync", self.handle)
+
+    def launches(self) -> int:
+        """Kernel launches of the graph launched last (its kernel nodes)."""
+        n = C.c_int64(0)
+        N.call("tvq_session_launches", self.handle, C.byref(n))
+        return int(n.value)
+
+    def hidden_device_ptr(self) -> int:
+        p = C.c_void_p()
+        N.call("tvq_session_hidden", self.handle, C.byref(p))
+        return p.value
+
+    def run_layers_device(self, x_dev_ptr=None, y_dev_ptr=None, dynamic: bool = False, stream_ptr=None):
+        """The blocks alone on device hidden states (asynchronous; ints are
+        raw pointers, None = the resident hidden states)."""
+        N.call("tvq_session_run_layers", self.handle, C.c_void_p(x_dev_ptr) if x_dev_ptr else None, 1,
+               C.c_void_p(y_dev_ptr) if y_dev_ptr else None, 1, 1 if dynamic else 0,
+               C.c_void_p(stream_ptr) if stream_ptr else None)
+
+
+class GPT2Session(_Session):
+    """Device-resident INT8 GPT-2 forward on one GPU (one tvq session)."""
+
+    def __init__(self, weights: GPT2Weights, device: int = 0, max_tokens: int = 1024):
+        super().__init__(weights.cfg, weights.layers, weights.cfg.vocab, device, max_tokens)
+        N.call("tvq_session_set_embeddings", self.handle, _p(_f32(weights.wte)), _p(_f32(weights.wpe)))
+        N.call("tvq_session_set_layernorm", self.handle, -1, 0, _p(_f32(weights.lnf_g)), _p(_f32(weights.lnf_b)))
+
+    def logits_shape(self):
+        rows = self.n_tokens if self.logits_mode == 0 else self.seg.size - 1
+        return rows, self.cfg.vocab
+
+    def calibrate(self, ids, reset: bool = True):
+        ids = np.ascontiguousarray(ids, np.int64)
+        assert ids.size == self.n_tokens
+        N.call("tvq_session_calibrate", self.handle, _p(ids), 0, 1 if reset else 0)
 
     # ---- forward
     def forward(self, ids) -> np.ndarray:
@@ -209,22 +261,22 @@ class GPT2Session:
         N.call("tvq_session_logits", self.handle, C.byref(p), None, None)
         return p.value
 
-    def sync(self):
-        N.call("tvq_session_sync", self.handle)
 
-    def launches(self) -> int:
-        """Kernel launches of one forward (kernel nodes of its CUDA graph)."""
-        n = C.c_int64(0)
-        N.call("tvq_session_launches", self.handle, C.byref(n))
-        return int(n.value)
 
-    STAGES = ("embed", "layernorm", "gemm_c_attn", "attention", "gemm_attn_proj", "gemm_c_fc", "gemm_mlp_proj",
-              "lm_head")
+class LayerStack(_Session):
+    """The transformer blocks of a GPT2Config without embeddings or LM head:
+    hidden states [T, d_model] in, hidden states out (the XL-shaped INT8 PTQ
+    layer stack).  With dynamic=True every call calibrates each quantization
+    point on its own activations on the GPU (calibrate_minmax +
+    quantize_int8_symmetric per layer, engine.tkv:13-36, 216-226)."""
 
-    def set_profiling(self, on: bool):
-        N.call("tvq_session_set_profiling", self.handle, 1 if on else 0)
+    def __init__(self, cfg: GPT2Config, layers: list, device: int = 0, max_tokens: int = 8192):
+        super().__init__(cfg, layers, 0, device, max_tokens)
 
-    def stage_times(self) -> dict:
-        out = np.zeros(len(self.STAGES), np.float32)
-        N.call("tvq_session_stage_times", self.handle, _p(out), out.size)
-        return dict(zip(self.STAGES, out.tolist()))
+    def run(self, x, dynamic: bool = True) -> np.ndarray:
+        """Host hidden states in, host hidden states out (synchronous)."""
+        x = _f32(x)
+        assert x.shape == (self.n_tokens, self.cfg.d_model)
+        y = np.empty_like(x)
+        N.call("tvq_session_run_layers", self.handle, _p(x), 0, _p(y), 0, 1 if dynamic else 0, None)
+        return y

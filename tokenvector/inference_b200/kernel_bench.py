@@ -50,7 +50,8 @@ def _p(t):
 
 
 def bench_gemm(m, n, k, epilogue="f32", reps=20, kind=N.GEMM_I8):
-    """epilogue: f32 | f32_residual | gelu_q (GELU-erf then int8 out)"""
+    """epilogue: f32 | f32_residual | gelu_q (GELU-erf then int8 out) |
+    gelu_amax (GELU-erf, f32 out and max|y|: a calibrating c_fc)"""
     torch, dev, st, flush = _env()
     dt = torch.int8 if kind == N.GEMM_I8 else torch.uint8
     A = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=dev).view(dt)
@@ -65,12 +66,13 @@ def bench_gemm(m, n, k, epilogue="f32", reps=20, kind=N.GEMM_I8):
     Y = torch.empty((m, n), device=dev) if epilogue != "gelu_q" else None
     Yq = torch.empty((m, n), dtype=torch.int8, device=dev) if epilogue == "gelu_q" else None
     R = torch.randn((m, n), device=dev) if epilogue == "f32_residual" else None
-    act = N.ACT_GELU_ERF if epilogue == "gelu_q" else N.ACT_NONE
+    act = N.ACT_GELU_ERF if epilogue in ("gelu_q", "gelu_amax") else N.ACT_NONE
+    amax = torch.zeros(1, dtype=torch.int32, device=dev) if epilogue == "gelu_amax" else None
     sp = C.c_void_p(st.cuda_stream)
 
     def fn():
         N.call("tvq_dev_gemm", kind, _p(A), _p(W), _p(bias), _p(R), _p(Y), _p(Yq), m, n, k, _p(sa), _p(sw), 1, act,
-               _p(so) if Yq is not None else None, None, sp)
+               _p(so) if Yq is not None else None, _p(amax), sp)
     us = _time(torch, st, flush, fn, reps)
     ops = 2.0 * m * n * k
     byts = m * k + n * k + (4 * m * n if Y is not None else m * n) + (4 * m * n if R is not None else 0) + 8 * n
@@ -142,7 +144,7 @@ def main():
     ap.add_argument("--n", type=int, default=768)
     ap.add_argument("--k", type=int, default=768)
     ap.add_argument("--heads", type=int, default=12)
-    ap.add_argument("--epilogue", default="f32", choices=["f32", "f32_residual", "gelu_q"])
+    ap.add_argument("--epilogue", default="f32", choices=["f32", "f32_residual", "gelu_q", "gelu_amax"])
     ap.add_argument("--fp8", action="store_true")
     ap.add_argument("--reps", type=int, default=20)
     a = ap.parse_args()
