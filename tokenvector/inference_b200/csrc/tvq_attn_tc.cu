@@ -5,27 +5,32 @@
 // causal softmax, context = P V), per head, token t of the sequence [s0, s1)
 // attending to u in [s0, t].  qkv rows are [Q | K | V] with heads contiguous.
 //
-// fp32 accuracy on TF32 tensor cores: every operand x is split into
-// hi = tf32(x) and lo = tf32(x - hi), and each product is formed as
-// xl*yh + xh*yl + xh*yh (the "3xTF32" scheme).  The scores of one 64-key
-// block and the P*V partial of one 64-key block are each summed in TMEM over
-// K = 64 only; the running output is kept in registers with IEEE adds (the
-// tensor core's own accumulation is less exact than IEEE fp32 over long
-// sums).
+// fp32 accuracy on FP16 tensor cores (kind::f16): every operand x is scaled
+// by a power of two s (so that its largest value sits in [2^14, 2^15)) and
+// split into hi = fp16(x s) and lo = fp16(x s - hi) (|x s - hi - lo| <=
+// max(2^-22 |x s|, 2^-25)), and each product is formed as xl*yh + xh*yl +
+// xh*yh.  The scales: Q per query row (in this kernel), K and V per head
+// (kv_exp, written with the split operands), P = 2^(x - m) in (0, 1] by
+// 2^14.  They are powers of two and are undone exactly: the scores before
+// the softmax, the output at the end.  The scores of one 64-key block and
+// the P*V partial of one block are each summed in TMEM over K = 64 only; the
+// running output is kept in registers with IEEE adds (the tensor core's own
+// accumulation is less exact than IEEE fp32 over long sums).
 //
-// Operands: split_kv writes K as hi/lo f32 arrays [T, d] and V transposed,
-// V^T hi/lo [d, Tp] (keys contiguous, Tp = T rounded up to 4); the attention
-// kernel brings 64-key blocks of them into two 2-stage shared-memory rings
-// (K, V^T) with TMA, both as K-major B operands (of S = Q K^T and of P V).
-// Q (hi/lo) sits in shared memory as the A operand of S; P (hi/lo) is
-// written to tensor memory, double-buffered, as the A operand of P V, so the
-// softmax of block j never waits for P V of block j-1.
+// Operands: K as fp16 hi/lo [T, d] and V transposed, V^T hi/lo [d, Tp]
+// (keys contiguous, Tp = T rounded up to 8), written by the c_attn GEMM's
+// epilogue (or launch_split_kv); the attention kernel brings 64-key blocks
+// of them into two 2-stage shared-memory rings (K, V^T) with TMA, both as
+// K-major B operands (of S = Q K^T and of P V).  Q (hi/lo) sits in shared
+// memory as the A operand of S; P (hi/lo) is written to tensor memory,
+// double-buffered, as the A operand of P V, so the softmax of block j never
+// waits for P V of block j-1.
 //
 // One CTA = one (128-query tile, head, key range) work item; 384 threads:
 //   warp 0      TMA producer (K/V blocks)
 //   warp 1      MMA issuer: S_j = Q K_j^T into TMEM S[j&1] (M 128, N 64,
 //               K 64), then PV_{j-1} = P_{j-1} V_{j-1} into TMEM O[(j-1)&1]
-//   warp 2      TMEM allocator (all 512 columns)
+//   warp 2      TMEM allocator (512 columns)
 //   warps 4-11  softmax, two warps per TMEM lane group (32 query rows), one
 //               per 32-key half of each block: Q to shared memory once, then
 //               per block the row max exchanged between the pair through
@@ -40,6 +45,8 @@
 // slot or -1, merge entry}; the partials (unnormalised O, m, l) of one query
 // tile are merged by the CTA that writes the last of them (a counter per
 // entry and head, reset by that CTA).
+#include <cuda_fp16.h>
+
 #include <algorithm>
 
 #include "tvq_common.cuh"
@@ -56,14 +63,15 @@ constexpr int TK = 64;   // keys per block
 constexpr int HD = 64;   // head dim
 constexpr int NTHREADS = 384;
 
-// shared memory (1024-byte aligned regions):
-//   Q hi, Q lo      128 rows x 64 head columns: two 16 KB K-blocks of 128-byte rows
-//   K ring [2]      per stage K hi, K lo: two 8 KB halves (head columns 32h..) of 64 key rows
-//   V^T ring [2]    per stage V^T hi, V^T lo: two 8 KB halves (keys 32h.. of the block) of 64 head rows
-constexpr uint32_t HALF = TK * 128;                  // 8 KB
-constexpr uint32_t QPART = TQ * 128 * 2;             // 32 KB
+// shared memory (1024-byte aligned regions), every row 128 bytes = 64 fp16
+// with the 128-byte swizzle:
+//   Q hi, Q lo      128 query rows x 64 head columns: 16 KB each
+//   K ring [2]      per stage K hi, K lo: 64 key rows x 64 head columns
+//   V^T ring [2]    per stage V^T hi, V^T lo: 64 head rows x 64 keys
+constexpr uint32_t PART = TK * 128;                  // 8 KB
+constexpr uint32_t QPART = TQ * 128;                 // 16 KB
 constexpr uint32_t OFF_QH = 0, OFF_QL = QPART;
-constexpr uint32_t KSTAGE = 4 * HALF;                // 32 KB: hi halves then lo halves
+constexpr uint32_t KSTAGE = 2 * PART;                // 16 KB: hi then lo
 constexpr uint32_t OFF_K = 2 * QPART;                // + s * KSTAGE
 constexpr uint32_t OFF_V = OFF_K + 2 * KSTAGE;       // + s * KSTAGE
 constexpr uint32_t OFF_RED = OFF_V + 2 * KSTAGE;     // float [2][2][128] row maxima
@@ -71,12 +79,13 @@ constexpr uint32_t OFF_LSUM = OFF_RED + 2 * 2 * TQ * 4;  // float [2][128] row s
 constexpr uint32_t OFF_BAR = OFF_LSUM + 2 * TQ * 4;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 512 + 1024;
 
-// tensor memory columns: S[2], O[2] (64 each), P[2] (hi 64 + lo 64 each)
+// tensor memory columns: S[2], O[2] (64 f32 each), P[2] (hi 32 + lo 32
+// columns each, two fp16 keys per column)
 constexpr uint32_t COL_S = 0, COL_O = 128, COL_P = 256;
 constexpr uint32_t TMEM_COLS = 512;
 
-// kind::tf32, D f32, A and B tf32 K-major, N = 64, M = 128 (both products)
-constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(64 >> 3) << 17) |
+// kind::f16, D f32, A and B fp16 K-major, N = 64, M = 128 (both products)
+constexpr uint32_t IDESC = (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(64 >> 3) << 17) |
                            (static_cast<uint32_t>(TQ >> 4) << 24);
 
 // device error codes: the wait that gave up first (tens digit: 3 TMA
@@ -88,51 +97,74 @@ enum : int {
     DEVERR_ATTN_S_FULL = 51, DEVERR_ATTN_XCH = 52, DEVERR_ATTN_O_FULL = 53, DEVERR_ATTN_LXCH = 55
 };
 
-__device__ __forceinline__ float round_tf32_a(float v) {
-    // nearest TF32 value (10 explicit mantissa bits), ties away from zero
-    const uint32_t u = __float_as_uint(v);
-    if ((u & 0x7F800000u) == 0x7F800000u) return v;
-    float h = __uint_as_float((u + 0x1000u) & 0xFFFFE000u);
-    if ((__float_as_uint(h) & 0x7F800000u) == 0x7F800000u) h = __uint_as_float(u & 0xFFFFE000u);
-    return h;
+// D[tmem] (+)= A[tmem] * B^T for FP16 operands, A read from tensor memory
+// (lane = row of A, two K elements per 32-bit column).
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
 }
 
-__device__ __forceinline__ void split1(float v, uint32_t& h, uint32_t& l) {
-    const float hf = round_tf32_a(v);
-    h = __float_as_uint(hf);
-    l = __float_as_uint(round_tf32_a(__fsub_rn(v, hf)));
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0],"
+        " {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
 }
 
-__device__ __forceinline__ void split4(const float4 v, float4& h, float4& l) {
-    h.x = round_tf32_a(v.x); l.x = round_tf32_a(__fsub_rn(v.x, h.x));
-    h.y = round_tf32_a(v.y); l.y = round_tf32_a(__fsub_rn(v.y, h.y));
-    h.z = round_tf32_a(v.z); l.z = round_tf32_a(__fsub_rn(v.z, h.z));
-    h.w = round_tf32_a(v.w); l.w = round_tf32_a(__fsub_rn(v.w, h.w));
+// 2^x, MUFU approximation (relative error ~2^-22; subnormal results flush
+// to zero, 2^-126 of the row maximum)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
-// K part of qkv [T, 3d] -> hi / lo arrays [T, d]
-__global__ void split_k_kernel(const float* __restrict__ qkv, int T, int d, float* __restrict__ kh,
-                               float* __restrict__ kl) {
+// hi / lo fp16 pair of two scaled values, packed two per 32-bit word
+// (element a in the low half).
+__device__ __forceinline__ void split_h2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(__fsub_rn(a, hf.x), __fsub_rn(b, hf.y));
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// K part of qkv [T, 3d] -> fp16 hi / lo [T, d] under the head scales
+// 2^kv_exp[h] (standalone path; the session's c_attn epilogue writes the same)
+__global__ void split_k16_kernel(const float* __restrict__ qkv, int T, int d, const int* __restrict__ kv_exp,
+                                 uint2* __restrict__ kh, uint2* __restrict__ kl) {
     griddep_wait();
     const int d4 = d >> 2;
     const int64_t n = static_cast<int64_t>(T) * d4;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t t = i / d4;
         const int c4 = static_cast<int>(i - t * d4);
-        float4 h, l;
-        split4(__ldg(reinterpret_cast<const float4*>(qkv + t * 3 * d) + d4 + c4), h, l);
-        reinterpret_cast<float4*>(kh)[i] = h;
-        reinterpret_cast<float4*>(kl)[i] = l;
+        const float f = exp2i(kv_exp[(4 * c4) / HD]);
+        const float4 v = __ldg(reinterpret_cast<const float4*>(qkv + t * 3 * d) + d4 + c4);
+        uint2 h, l;
+        split_h2(v.x * f, v.y * f, h.x, l.x);
+        split_h2(v.z * f, v.w * f, h.y, l.y);
+        kh[i] = h;
+        kl[i] = l;
     }
 }
 
-// V part of qkv [T, 3d] -> V^T hi / lo [d, Tp]: 32 x 32 tiles through
-// shared memory (coalesced on both sides); keys T..Tp-1 are written as 0.
-__global__ void split_vt_kernel(const float* __restrict__ qkv, int T, int Tp, int d, float* __restrict__ vth,
-                                float* __restrict__ vtl) {
+// V part of qkv [T, 3d] -> V^T fp16 hi / lo [d, Tp] under the head scales
+// 2^kv_exp[heads + h]: 32 x 32 tiles through shared memory (coalesced on
+// both sides); keys T..Tp-1 are written as 0.
+__global__ void split_vt16_kernel(const float* __restrict__ qkv, int T, int Tp, int d, const int* __restrict__ kv_exp,
+                                  __half* __restrict__ vth, __half* __restrict__ vtl) {
     __shared__ float tile[32][33];
     griddep_wait();
     const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+    const float f = exp2i(kv_exp[d / HD + c0 / HD]);
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
         const int t = t0 + i;
         tile[i][threadIdx.x] = (t < T) ? __ldg(qkv + static_cast<int64_t>(t) * 3 * d + 2 * d + c0 + threadIdx.x) : 0.0f;
@@ -141,12 +173,34 @@ __global__ void split_vt_kernel(const float* __restrict__ qkv, int T, int Tp, in
     const int t = t0 + threadIdx.x;
     if (t >= Tp) return;
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        uint32_t h, l;
-        split1(tile[threadIdx.x][i], h, l);
+        const float v = tile[threadIdx.x][i] * f;
+        const __half h = __float2half_rn(v);
         const int64_t o = static_cast<int64_t>(c0 + i) * Tp + t;
-        vth[o] = __uint_as_float(h);
-        vtl[o] = __uint_as_float(l);
+        vth[o] = h;
+        vtl[o] = __float2half_rn(__fsub_rn(v, __half2float(h)));
     }
+}
+
+// max |K| and max |V| per head (f32 bit patterns, atomicMax) of qkv [T, 3d]
+__global__ void kv_head_amax_kernel(const float* __restrict__ qkv, int T, int d, uint32_t* __restrict__ amax) {
+    griddep_wait();
+    const int heads = d / HD;
+    const int part = blockIdx.y;  // 0 K, 1 V
+    const int h = blockIdx.z;
+    float m = 0.0f;
+    for (int t = blockIdx.x; t < T; t += gridDim.x) {
+        const float* src = qkv + static_cast<int64_t>(t) * 3 * d + (1 + part) * d + h * HD;
+        for (int c = threadIdx.x; c < HD; c += blockDim.x) m = fmaxf(m, fabsf(src[c]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(amax + part * heads + h, __float_as_uint(m));
+}
+
+__global__ void kv_exp_from_amax_kernel(const uint32_t* __restrict__ amax, int n, int* __restrict__ kv_exp) {
+    griddep_wait();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) kv_exp[i] = pow2_exp_below_2p15(__uint_as_float(amax[i]));
 }
 
 struct AttnParams {
@@ -163,6 +217,7 @@ struct AttnParams {
     float2* part_ml;
     const int4* comb;  // per merge entry {q0, seq end, first slot, count}; split[i].w = entry of item i
     int* counters;     // per (entry, head): partials counted in (0 between launches)
+    const int* kv_exp; // [2 * nheads]: K and V head scales 2^kv_exp of the split operands
     int* err;
 };
 
@@ -204,9 +259,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int q0 = tl.x, s1 = tl.z;
     const int4 sp = p.split[item];
     const int kb = sp.x, ke = sp.y, part = sp.z;
-    // blocks start at kb rounded down to 4 keys (16 bytes, the TMA rule for
-    // the V^T key coordinate); keys below kb are masked
-    const int kb_al = kb & ~3;
+    // blocks start at kb rounded down to 8 keys (16 bytes of fp16, the TMA
+    // rule for the V^T key coordinate); keys below kb are masked
+    const int kb_al = kb & ~7;
     const int nkb = (ke - kb_al + TK - 1) / TK;
 
     if (threadIdx.x == 0) {
@@ -255,17 +310,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 mbar_arrive_expect_tx(&k_full[s], KSTAGE);
                 uint8_t* ks = sm + OFF_K + s * KSTAGE;
                 tma_load_2d(&tmKh, &k_full[s], ks, head * HD, key);
-                tma_load_2d(&tmKh, &k_full[s], ks + HALF, head * HD + 32, key);
-                tma_load_2d(&tmKl, &k_full[s], ks + 2 * HALF, head * HD, key);
-                tma_load_2d(&tmKl, &k_full[s], ks + 3 * HALF, head * HD + 32, key);
+                tma_load_2d(&tmKl, &k_full[s], ks + PART, head * HD, key);
                 kissued = j + 1;
                 if (!mbar_wait(&v_empty[s], ph, p.err, DEVERR_ATTN_V_EMPTY)) break;
                 mbar_arrive_expect_tx(&v_full[s], KSTAGE);
                 uint8_t* vs = sm + OFF_V + s * KSTAGE;
                 tma_load_2d(&tmVh, &v_full[s], vs, key, head * HD);
-                tma_load_2d(&tmVh, &v_full[s], vs + HALF, key + 32, head * HD);
-                tma_load_2d(&tmVl, &v_full[s], vs + 2 * HALF, key, head * HD);
-                tma_load_2d(&tmVl, &v_full[s], vs + 3 * HALF, key + 32, head * HD);
+                tma_load_2d(&tmVl, &v_full[s], vs + PART, key, head * HD);
                 vissued = j + 1;
             }
             // every issued load lands before the CTA may exit
@@ -288,18 +339,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + COL_O + b * 64;
                 const uint32_t vb = sbase + OFF_V + b * KSTAGE;
-                const uint32_t pcol = tmem_base + COL_P + b * 128;
+                const uint32_t pcol = tmem_base + COL_P + b * 64;  // hi: +0..31, lo: +32..63
 #pragma unroll
-                for (int h = 0; h < 2; h++) {
-#pragma unroll
-                    for (int kk = 0; kk < 4; kk++) {  // 8 keys (32 bytes of V^T rows) per instruction
-                        const uint64_t vh = smem_desc_k_sw128(vb + h * HALF + kk * 32);
-                        const uint64_t vl = smem_desc_k_sw128(vb + 2 * HALF + h * HALF + kk * 32);
-                        const uint32_t pc = 32 * h + 8 * kk;
-                        umma_tf32_ts(d_tmem, pcol + 64 + pc, vh, IDESC, (h | kk) ? 1u : 0u);
-                        umma_tf32_ts(d_tmem, pcol + pc, vl, IDESC, 1u);
-                        umma_tf32_ts(d_tmem, pcol + pc, vh, IDESC, 1u);
-                    }
+                for (int kk = 0; kk < 4; kk++) {  // 16 keys (32 bytes of V^T rows, 8 P columns) per instruction
+                    const uint64_t vh = smem_desc_k_sw128(vb + kk * 32);
+                    const uint64_t vl = smem_desc_k_sw128(vb + PART + kk * 32);
+                    const uint32_t pc = 8 * kk;
+                    umma_f16_ts(d_tmem, pcol + 32 + pc, vh, IDESC, kk ? 1u : 0u);
+                    umma_f16_ts(d_tmem, pcol + pc, vl, IDESC, 1u);
+                    umma_f16_ts(d_tmem, pcol + pc, vh, IDESC, 1u);
                 }
                 umma_commit(&o_full[b]);   // PV_i in O[b]; P[b] free again
                 umma_commit(&v_empty[b]);
@@ -314,17 +362,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const uint32_t d_tmem = tmem_base + COL_S + b * 64;
                 const uint32_t kbs = sbase + OFF_K + b * KSTAGE;
 #pragma unroll
-                for (int h = 0; h < 2; h++) {
-#pragma unroll
-                    for (int kk = 0; kk < 4; kk++) {  // 8 head columns (32 bytes) per instruction
-                        const uint64_t qh = smem_desc_k_sw128(sbase + OFF_QH + h * (TQ * 128) + kk * 32);
-                        const uint64_t ql = smem_desc_k_sw128(sbase + OFF_QL + h * (TQ * 128) + kk * 32);
-                        const uint64_t kh = smem_desc_k_sw128(kbs + h * HALF + kk * 32);
-                        const uint64_t kl = smem_desc_k_sw128(kbs + 2 * HALF + h * HALF + kk * 32);
-                        umma_tf32(d_tmem, ql, kh, IDESC, (h | kk) ? 1u : 0u);
-                        umma_tf32(d_tmem, qh, kl, IDESC, 1u);
-                        umma_tf32(d_tmem, qh, kh, IDESC, 1u);
-                    }
+                for (int kk = 0; kk < 4; kk++) {  // 16 head columns (32 bytes) per instruction
+                    const uint64_t qh = smem_desc_k_sw128(sbase + OFF_QH + kk * 32);
+                    const uint64_t ql = smem_desc_k_sw128(sbase + OFF_QL + kk * 32);
+                    const uint64_t kh = smem_desc_k_sw128(kbs + kk * 32);
+                    const uint64_t kl = smem_desc_k_sw128(kbs + PART + kk * 32);
+                    umma_f16(d_tmem, ql, kh, IDESC, kk ? 1u : 0u);
+                    umma_f16(d_tmem, qh, kl, IDESC, 1u);
+                    umma_f16(d_tmem, qh, kh, IDESC, 1u);
                 }
                 umma_commit(&s_full[b]);
                 umma_commit(&k_empty[b]);
@@ -342,23 +387,40 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int q = q0 + r;
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(32 * g) << 16);
         bool alive = true;
-        // Q (this row, head columns 32h..32h+31) -> hi / lo, K-major in shared memory
+        // Q row scale (its largest |value| to [2^14, 2^15)), then head
+        // columns 32h..32h+31 -> fp16 hi / lo, K-major in shared memory
+        int sq = 0;
         {
-            const float4* src = reinterpret_cast<const float4*>(p.qkv + static_cast<int64_t>(q) * 3 * p.d +
-                                                               head * HD + 32 * h);
+            const float4* src = reinterpret_cast<const float4*>(p.qkv + static_cast<int64_t>(q) * 3 * p.d + head * HD);
+            float4 v[16];
+            float mx = 0.0f;
 #pragma unroll
-            for (int c4 = 0; c4 < 8; c4++) {
-                const float4 v = (q < s1) ? __ldg(src + c4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                float4 vh, vl;
-                split4(v, vh, vl);
-                const uint32_t off = h * (TQ * 128) + sw128(r, c4);
-                *reinterpret_cast<float4*>(sm + OFF_QH + off) = vh;
-                *reinterpret_cast<float4*>(sm + OFF_QL + off) = vl;
+            for (int c4 = 0; c4 < 16; c4++) {
+                v[c4] = (q < s1) ? __ldg(src + c4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[c4].x), fabsf(v[c4].y)), fmaxf(fabsf(v[c4].z), fabsf(v[c4].w))));
+            }
+            sq = pow2_exp_below_2p15(mx);
+            const float fq = exp2i(sq);
+#pragma unroll
+            for (int c16 = 0; c16 < 4; c16++) {  // 16-byte chunks of the 128-byte row: 8 fp16 each
+                uint4 hi, lo;
+                const float4 a = h ? v[8 + 2 * c16] : v[2 * c16];  // static indices: registers, not local memory
+                const float4 b = h ? v[9 + 2 * c16] : v[1 + 2 * c16];
+                split_h2(a.x * fq, a.y * fq, hi.x, lo.x);
+                split_h2(a.z * fq, a.w * fq, hi.y, lo.y);
+                split_h2(b.x * fq, b.y * fq, hi.z, lo.z);
+                split_h2(b.z * fq, b.w * fq, hi.w, lo.w);
+                const uint32_t off = sw128(r, 4 * h + c16);
+                *reinterpret_cast<uint4*>(sm + OFF_QH + off) = hi;
+                *reinterpret_cast<uint4*>(sm + OFF_QL + off) = lo;
             }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(q_full);
         }
+        // scores: S = acc 2^-(sq + sk) exactly, times log2(e) / sqrt(hd)
+        const int sk = p.kv_exp[head], sv = p.kv_exp[p.nheads + head];
+        const float xs = p.scale2 * exp2i(-sq) * exp2i(-sk);
         float o[32];
 #pragma unroll
         for (int c = 0; c < 32; c++) o[c] = 0.0f;
@@ -380,12 +442,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int k0 = kb_al + j * TK + 32 * h;
             const int lo = kb - k0, hi = min(q, ke - 1) - k0;
             float x[32];
-            float mx = -INFINITY;
+            float mx = -INFINITY, mx2 = -INFINITY;
+            if (lo <= 0 && hi >= 31) {  // every key of the half visible: most blocks
 #pragma unroll
-            for (int c = 0; c < 32; c++) {
-                x[c] = (c >= lo && c <= hi) ? __fmul_rn(__uint_as_float(sr[c]), p.scale2) : -INFINITY;
-                mx = fmaxf(mx, x[c]);
+                for (int c = 0; c < 32; c += 2) {
+                    x[c] = __fmul_rn(__uint_as_float(sr[c]), xs);
+                    x[c + 1] = __fmul_rn(__uint_as_float(sr[c + 1]), xs);
+                    mx = fmaxf(mx, x[c]);
+                    mx2 = fmaxf(mx2, x[c + 1]);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 32; c++) {
+                    x[c] = (c >= lo && c <= hi) ? __fmul_rn(__uint_as_float(sr[c]), xs) : -INFINITY;
+                    mx = fmaxf(mx, x[c]);
+                }
             }
+            mx = fmaxf(mx, mx2);
             // row max over both halves: exchange with the partner warp
             red[(b * 2 + h) * TQ + r] = mx;
             __syncwarp();
@@ -395,23 +468,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mx = fmaxf(mx, red[(b * 2 + (h ^ 1)) * TQ + r]);
             const float mnew = fmaxf(m, mx);
             const float mref = (mnew == -INFINITY) ? 0.0f : mnew;  // a row with no visible key yet stays empty
-            const float alpha = exp2f(m - mref);
-            // P_j = 2^(x - m) in [0, 1] as hi (nearest TF32) + lo (exact
-            // remainder, read by the tensor core to TF32 precision: |error|
-            // <= 2^-21 P) into P[b]; P[b] was last read by PV_{j-2}, whose
-            // completion the previous iteration already waited for
-            uint32_t phi[32], plo[32];
-            float sum = 0.0f;
+            const float alpha = ex2_approx(m - mref);
+            // P_j = 2^(x - m + 14) in (0, 2^14] (l and O are kept in units of
+            // 2^14) as fp16 hi + lo (|error| <= max(2^-22 P, 2^-25)) into
+            // P[b]; P[b] was last read by PV_{j-2}, whose completion the
+            // previous iteration already waited for
+            const float mref14 = mref - 14.0f;
+            uint32_t phi[16], plo[16];
+            float sa4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-            for (int c = 0; c < 32; c++) {
-                const float e = exp2f(x[c] - mref);
-                sum += e;
-                const uint32_t hb = (__float_as_uint(e) + 0x1000u) & 0xFFFFE000u;
-                phi[c] = hb;
-                plo[c] = __float_as_uint(__fsub_rn(e, __uint_as_float(hb)));
+            for (int c = 0; c < 32; c += 2) {
+                const float e0 = ex2_approx(x[c] - mref14), e1 = ex2_approx(x[c + 1] - mref14);
+                sa4[(c >> 1) & 3] += e0 + e1;
+                split_h2(e0, e1, phi[c / 2], plo[c / 2]);
             }
-            tmem_st32(lane_base + COL_P + b * 128 + 32 * h, phi);
-            tmem_st32(lane_base + COL_P + b * 128 + 64 + 32 * h, plo);
+            const float sum = (sa4[0] + sa4[1]) + (sa4[2] + sa4[3]);
+            tmem_st16(lane_base + COL_P + b * 64 + 16 * h, phi);
+            tmem_st16(lane_base + COL_P + b * 64 + 32 + 16 * h, plo);
             l = fmaf(l, alpha, sum);
             m = mnew;
             tmem_st_wait();
@@ -448,6 +521,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 for (int c = 0; c < 32; c++) o[c] = fmaf(o[c], alpha_prev, __uint_as_float(pv[c]));
             }
         }
+        // O was summed in units of 2^(14 + sv): back to the true scale (exact)
+#pragma unroll
+        for (int c = 0; c < 32; c++) o[c] = o[c] * exp2i(-sv);  // O and l both in units of 2^14 from here
         if (alive) {  // row sum over both halves
             lsum[h * TQ + r] = l;
             __syncwarp();
@@ -520,8 +596,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         }
                     }
                 }
+                const float il = 1.0f / lt;
 #pragma unroll
-                for (int c = 0; c < 32; c++) o[c] = acc[c] / lt;
+                for (int c = 0; c < 32; c++) o[c] = acc[c] * il;
             } else {
                 const float il = 1.0f / l;
 #pragma unroll
@@ -568,34 +645,85 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
+// Per-head bounds of a c_attn layer's K and V outputs for the epilogue's
+// fp16 split (kv_head_exp): block (h, part) over the 64 output columns n of
+// head h in part (0 K, 1 V): A = max sw[n] * 127 * sum_k |W[n,k]|, B = max
+// |bias[n]|, both rounded up.  out [4 heads]: A_K, B_K, A_V, B_V.
+__global__ void kv_head_bound_kernel(const int8_t* __restrict__ W, const float* __restrict__ sw,
+                                     const float* __restrict__ bias, int k, int kvd, float* __restrict__ out) {
+    const int h = blockIdx.x, part = blockIdx.y, heads = gridDim.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ float ra[8], rb[8];
+    float a = 0.0f, bb = 0.0f;
+    for (int i = warp; i < HD; i += blockDim.x >> 5) {
+        const int n = (1 + part) * kvd + h * HD + i;
+        int sum = 0;
+        for (int c = lane; c < k; c += 32) sum += abs(static_cast<int>(W[static_cast<int64_t>(n) * k + c]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        a = fmaxf(a, __fmul_ru(__fmul_ru(fabsf(sw[n]), 127.0f), __int2float_ru(sum)));
+        if (bias) bb = fmaxf(bb, fabsf(bias[n]));
+    }
+    if (lane == 0) {
+        ra[warp] = a;
+        rb[warp] = bb;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); w++) {
+            a = fmaxf(a, ra[w]);
+            bb = fmaxf(bb, rb[w]);
+        }
+        out[(2 * part) * heads + h] = a;
+        out[(2 * part + 1) * heads + h] = bb;
+    }
+}
+
 }  // namespace
 
 int attention_tc_rows() { return TQ; }
 
-int attention_tc_pitch(int T) { return (T + 3) & ~3; }
+int attention_tc_pitch(int T) { return (T + 7) & ~7; }
 
-int launch_split_kv(const float* qkv, int T, int d, float* kh, float* kl, float* vth, float* vtl, cudaStream_t st) {
+int launch_split_kv(const float* qkv, int T, int d, void* kh, void* kl, void* vth, void* vtl, int* kv_exp,
+                    uint32_t* amax, cudaStream_t st) {
     if (T <= 0) return TVQ_OK;
-    TVQ_CHECK(d % 32 == 0, TVQ_ERR_UNSUPPORTED, "d must be a multiple of 32");
+    TVQ_CHECK(d % HD == 0, TVQ_ERR_UNSUPPORTED, "d must be a multiple of 64");
     int rc = 0;
     DeviceState* ds = device_state(&rc);
     if (!ds) return rc;
+    const int heads = d / HD;
+    TVQ_CUDA(cudaMemsetAsync(amax, 0, sizeof(uint32_t) * 2 * heads, st));
+    int r = launch_pdl(kv_head_amax_kernel, dim3(std::min(T, 64), 2, heads), dim3(64), 0, st, qkv, T, d, amax);
+    if (!r) r = launch_pdl(kv_exp_from_amax_kernel, dim3((2 * heads + 127) / 128), dim3(128), 0, st,
+                           static_cast<const uint32_t*>(amax), 2 * heads, kv_exp);
+    if (r) return r;
     const int64_t n = static_cast<int64_t>(T) * (d / 4);
     const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, ds->sm_count * 8));
-    int rc2 = launch_pdl(split_k_kernel, dim3(grid), dim3(256), 0, st, qkv, T, d, kh, kl);
-    if (rc2) return rc2;
+    r = launch_pdl(split_k16_kernel, dim3(grid), dim3(256), 0, st, qkv, T, d, static_cast<const int*>(kv_exp),
+                   static_cast<uint2*>(kh), static_cast<uint2*>(kl));
+    if (r) return r;
     const int Tp = attention_tc_pitch(T);
-    return launch_pdl(split_vt_kernel, dim3((Tp + 31) / 32, d / 32), dim3(32, 8), 0, st, qkv, T, Tp, d, vth, vtl);
+    return launch_pdl(split_vt16_kernel, dim3((Tp + 31) / 32, d / 32), dim3(32, 8), 0, st, qkv, T, Tp, d,
+                      static_cast<const int*>(kv_exp), static_cast<__half*>(vth), static_cast<__half*>(vtl));
 }
 
-int launch_attention_tc(const float* qkv, const float* kh, const float* kl, const float* vth, const float* vtl, int T,
-                        const int4* tiles, const int4* split, int nitems, const int4* comb, int ncomb, int d,
-                        int nheads, float* out, int8_t* outq, const float* qscale, uint32_t* amax, float* part_o,
-                        float2* part_ml, int* counters, cudaStream_t st) {
+int launch_kv_head_bound(const int8_t* W, const float* sw, const float* bias, int k, int kvd, float* out,
+                         cudaStream_t st) {
+    TVQ_CHECK(kvd % HD == 0 && kvd > 0 && k > 0, TVQ_ERR_UNSUPPORTED, "d must be a multiple of 64");
+    kv_head_bound_kernel<<<dim3(kvd / HD, 2), 256, 0, st>>>(W, sw, bias, k, kvd, out);
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
+}
+
+int launch_attention_tc(const float* qkv, const void* kh, const void* kl, const void* vth, const void* vtl,
+                        const int* kv_exp, int T, const int4* tiles, const int4* split, int nitems, const int4* comb,
+                        int ncomb, int d, int nheads, float* out, int8_t* outq, const float* qscale, uint32_t* amax,
+                        float* part_o, float2* part_ml, int* counters, cudaStream_t st) {
     if (nitems <= 0) return TVQ_OK;
     TVQ_CHECK(nheads > 0 && d == nheads * HD, TVQ_ERR_UNSUPPORTED, "the tensor-core attention needs head dim 64");
-    TVQ_CHECK(split && kh && kl && vth && vtl, TVQ_ERR_INVALID,
-              "the tensor-core attention needs key ranges and split K / V^T");
+    TVQ_CHECK(split && kh && kl && vth && vtl && kv_exp, TVQ_ERR_INVALID,
+              "the tensor-core attention needs key ranges, split K / V^T and their head scales");
     TVQ_CHECK((reinterpret_cast<uintptr_t>(qkv) & 15) == 0 && (!out || (reinterpret_cast<uintptr_t>(out) & 15) == 0) &&
                   (!outq || (reinterpret_cast<uintptr_t>(outq) & 3) == 0),
               TVQ_ERR_UNSUPPORTED, "attention buffers must be 16-byte aligned");
@@ -612,10 +740,10 @@ int launch_attention_tc(const float* qkv, const float* kh, const float* kl, cons
         attr[dev] = true;
     }
     CUtensorMap mkh, mkl, mvh, mvl;
-    rc = make_tma_f32_sw128(&mkh, kh, T, d, TK);
-    if (!rc) rc = make_tma_f32_sw128(&mkl, kl, T, d, TK);
-    if (!rc) rc = make_tma_f32_sw128(&mvh, vth, d, T, HD, attention_tc_pitch(T));
-    if (!rc) rc = make_tma_f32_sw128(&mvl, vtl, d, T, HD, attention_tc_pitch(T));
+    rc = make_tma_f16_sw128(&mkh, kh, T, d, TK);
+    if (!rc) rc = make_tma_f16_sw128(&mkl, kl, T, d, TK);
+    if (!rc) rc = make_tma_f16_sw128(&mvh, vth, d, T, HD, attention_tc_pitch(T));
+    if (!rc) rc = make_tma_f16_sw128(&mvl, vtl, d, T, HD, attention_tc_pitch(T));
     if (rc) return rc;
     AttnParams p;
     p.qkv = qkv;
@@ -634,6 +762,7 @@ int launch_attention_tc(const float* qkv, const float* kh, const float* kl, cons
     TVQ_CHECK(ncomb == 0 || (comb && counters), TVQ_ERR_INVALID, "key-chunk items need merge entries and counters");
     p.comb = comb;
     p.counters = counters;
+    p.kv_exp = kv_exp;
     // key-chunk partials are merged inside the kernel by the last CTA of each set
     return launch_pdl(attention_tc_kernel, dim3(nitems * nheads), dim3(NTHREADS), SMEM_BYTES, st, mkh, mkl, mvh, mvl,
                       p);

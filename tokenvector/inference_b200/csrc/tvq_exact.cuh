@@ -32,6 +32,22 @@ __device__ __forceinline__ float scale_from_amax_bits(uint32_t amax_bits) {
     return __double2float_rn(am / 127.0);
 }
 
+// 2^s as a float, exactly, for -126 <= s <= 127 (a multiply by it is the
+// ldexpf of the product: one IEEE rounding, exact unless it under- or
+// overflows).
+__device__ __forceinline__ float exp2i(int s) { return __int_as_float((s + 127) << 23); }
+
+// The exponent s with bound * 2^s in [2^14, 2^15): every |x| <= bound then
+// has |x 2^s| < 2^15, inside the fp16 range with room for the rounding of
+// an fp16 high part.  0 for a zero, infinite or NaN bound; at most 126 in
+// magnitude.
+__device__ __forceinline__ int pow2_exp_below_2p15(float bound) {
+    if (!(bound > 0.0f) || !(bound <= 3.40282347e38f)) return 0;
+    int e;
+    frexpf(bound, &e);  // bound in [2^(e-1), 2^e)
+    return max(-126, min(126, 15 - e));
+}
+
 // 1/scale of tv/quantization/engine.tkv:219-222 (and :244-246), kept as a
 // binary64 value and as a float pair hi + lo (|hi + lo - inv| <= 2^-48 |inv|).
 struct InvScale {

@@ -87,20 +87,24 @@ struct KParams {
     uint32_t* amax;
     int* err;
     // Optional attention operands of a c_attn GEMM (Y = qkv [m, 3 kvd]): the K
-    // columns [kvd, 2 kvd) also as TF32 hi / lo [m, kvd] (kh, kl) and the V
-    // columns [2 kvd, 3 kvd) transposed as hi / lo [kvd, vt_pitch] (vth, vtl).
-    float *kh, *kl, *vth, *vtl;
+    // columns [kvd, 2 kvd) also as fp16 hi / lo [m, kvd] (kh, kl) and the V
+    // columns [2 kvd, 3 kvd) transposed as hi / lo [kvd, vt_pitch] (vth, vtl),
+    // each 64-column head scaled by 2^kv_exp (kv_head_exp, from the bounds
+    // kv_bound) and the exponents stored to kv_exp [2 kvd / 64].
+    __half *kh, *kl, *vth, *vtl;
     int kvd, vt_pitch;
+    int* kv_exp;
+    const float* kv_bound;
 };
 
-// nearest TF32 value (10 explicit mantissa bits), ties away from zero: the
-// hi / lo split x = hi + lo of the attention operands (lo again rounded)
-__device__ __forceinline__ float round_tf32_e(float v) {
-    const uint32_t u = __float_as_uint(v);
-    if ((u & 0x7F800000u) == 0x7F800000u) return v;
-    float h = __uint_as_float((u + 0x1000u) & 0xFFFFE000u);
-    if ((__float_as_uint(h) & 0x7F800000u) == 0x7F800000u) h = __uint_as_float(u & 0xFFFFE000u);
-    return h;
+// hi / lo fp16 pair of two scaled values, packed two per 32-bit word
+// (element a in the low half): hi = fp16(a), lo = fp16(a - hi)
+__device__ __forceinline__ void split_h2_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(__fsub_rn(a, hf.x), __fsub_rn(b, hf.y));
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
 __device__ __forceinline__ float gelu_tanh_f32(float x) {
@@ -170,7 +174,18 @@ __device__ __forceinline__ int8_t q8_out(double v) {
 struct EpiCtx {
     bool vec_ok;     // n % 4 == 0: 16-byte row segments
     InvScale qs;     // 1 / scale_out for the int8 output
+    float sa;        // activation scale (attention operand bounds)
 };
+
+// Exponent of the power-of-two scale of one head (part 0 K, 1 V) of a c_attn
+// output: every |Y| of the head is at most sa * A + B (A = max over its
+// columns of sw[n] * 127 * sum_k |W[n,k]|, B = max |bias[n]|, both rounded
+// up; 127 * sum_k |W[n,k]| bounds the accumulator), widened by 2^-20 for
+// the rounding of Y itself.
+__device__ __forceinline__ int kv_head_exp(const float* bound, int heads, int part, int h, float sa) {
+    const float A = __ldg(bound + (2 * part) * heads + h), B = __ldg(bound + (2 * part + 1) * heads + h);
+    return pow2_exp_below_2p15(__fmul_ru(__fadd_ru(__fmul_ru(sa, A), B), 1.00000095367431640625f));
+}
 
 template <int N>
 __device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, uint32_t (&r)[N]) {
@@ -219,15 +234,14 @@ __device__ __forceinline__ void stage_and_store(const KParams& p, const EpiCtx& 
         float4 v = *reinterpret_cast<const float4*>(&stage[rr * E::CH + 4 * (c4 ^ ((rr >> E::SWS) & (E::LPR - 1)))]);
         if (row >= p.m || col >= p.n) continue;
         const int64_t off = static_cast<int64_t>(row) * p.n + col;
-        if (p.kh && col >= p.kvd && col < 2 * p.kvd) {  // K part: hi / lo split, row-major [m, kvd]
+        if (p.kh && col >= p.kvd && col < 2 * p.kvd) {  // K part: fp16 hi / lo split, row-major [m, kvd]
             const int64_t ko = static_cast<int64_t>(row) * p.kvd + (col - p.kvd);
-            float4 h, l;
-            h.x = round_tf32_e(v.x); l.x = round_tf32_e(__fsub_rn(v.x, h.x));
-            h.y = round_tf32_e(v.y); l.y = round_tf32_e(__fsub_rn(v.y, h.y));
-            h.z = round_tf32_e(v.z); l.z = round_tf32_e(__fsub_rn(v.z, h.z));
-            h.w = round_tf32_e(v.w); l.w = round_tf32_e(__fsub_rn(v.w, h.w));
-            *reinterpret_cast<float4*>(p.kh + ko) = h;
-            *reinterpret_cast<float4*>(p.kl + ko) = l;
+            const float f = exp2i(kv_head_exp(p.kv_bound, p.kvd / 64, 0, (col - p.kvd) / 64, e.sa));
+            uint2 h, l;
+            split_h2_pair(v.x * f, v.y * f, h.x, l.x);
+            split_h2_pair(v.z * f, v.w * f, h.y, l.y);
+            *reinterpret_cast<uint2*>(p.kh + ko) = h;
+            *reinterpret_cast<uint2*>(p.kl + ko) = l;
         }
         if (e.vec_ok && col + 3 < p.n) {
             if (p.residual) {
@@ -450,7 +464,7 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
         const float sw0 = (split_kind(KIND) || p.acc_only) ? 1.0f : __ldg(p.scales_w);
         InvScale qs{0.0, 0.0f, 0.0f};
         if (p.Yq) qs = make_inv_scale(static_cast<double>(__ldg(p.scale_out)));
-        EpiCtx ec{(p.n & 3) == 0, qs};
+        EpiCtx ec{(p.n & 3) == 0, qs, sa};
         float amax = 0.0f;
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(eg * 32) << 16);
         if constexpr (split_kind(KIND)) {
@@ -629,15 +643,23 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                         }
                     }
                 }
-                if (p.vth && n0 >= 2 * p.kvd && row0 + lane < p.m) {
-                    // V part, transposed: column n0 + j -> row of V^T; lanes
-                    // (consecutive tokens) write consecutive addresses
-                    const int64_t vo = static_cast<int64_t>(n0 - 2 * p.kvd) * p.vt_pitch + row0 + lane;
+                if (p.vth && n0 >= p.kvd) {
+                    const int part = n0 >= 2 * p.kvd ? 1 : 0;
+                    const int hh = (n0 - (1 + part) * p.kvd) / 64;
+                    const int sh = kv_head_exp(p.kv_bound, p.kvd / 64, part, hh, sa);
+                    if (row0 == 0 && lane == 0 && (n0 - (1 + part) * p.kvd) % 64 == 0)
+                        p.kv_exp[part * (p.kvd / 64) + hh] = sh;  // one writer per head
+                    if (part == 1 && row0 + lane < p.m) {
+                        // V part, transposed: column n0 + j -> row of V^T; lanes
+                        // (consecutive tokens) write consecutive addresses
+                        const int64_t vo = static_cast<int64_t>(n0 - 2 * p.kvd) * p.vt_pitch + row0 + lane;
 #pragma unroll
-                    for (int j = 0; j < E::CH; j++) {
-                        const float h = round_tf32_e(y[j]);
-                        p.vth[vo + static_cast<int64_t>(j) * p.vt_pitch] = h;
-                        p.vtl[vo + static_cast<int64_t>(j) * p.vt_pitch] = round_tf32_e(__fsub_rn(y[j], h));
+                        for (int j = 0; j < E::CH; j++) {
+                            const float v = y[j] * exp2i(sh);
+                            const __half h = __float2half_rn(v);
+                            p.vth[vo + static_cast<int64_t>(j) * p.vt_pitch] = h;
+                            p.vtl[vo + static_cast<int64_t>(j) * p.vt_pitch] = __float2half_rn(__fsub_rn(v, __half2float(h)));
+                        }
                     }
                 }
                 if (p.act == TVQ_ACT_GELU_ERF) {
@@ -822,9 +844,9 @@ __global__ void split_f16_rows_kernel(const float* __restrict__ x, __half* __res
             frexpf(m, &e);  // m in [2^(e-1), 2^e)
             sh = min(15 - e, 126);
         }
-        if (lane == 0) rscale[r] = ldexpf(1.0f, -sh);
+        if (lane == 0) rscale[r] = exp2i(-sh);
         for (int64_t j = lane; j < k; j += 32) {
-            const float v = ldexpf(xr[j], sh);
+            const float v = xr[j] * exp2i(sh);
             const __half h = __float2half_rn(v);
             hi[r * k + j] = h;
             lo[r * k + j] = __float2half_rn(v - __half2float(h));
@@ -852,6 +874,15 @@ int make_tma_f32_sw128(CUtensorMap* map, const float* ptr, int64_t rows, int64_t
     TVQ_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && pitch % 4 == 0 && pitch >= cols, TVQ_ERR_UNSUPPORTED,
               "TMA operand must be 16-byte aligned with a 16-byte row pitch");
     return make_map(map, ptr, rows, cols, box_rows, 4, pitch);
+}
+
+int make_tma_f16_sw128(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows, int64_t pitch) {
+    int rc = get_encoder();
+    if (rc) return rc;
+    if (pitch == 0) pitch = cols;
+    TVQ_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && pitch % 8 == 0 && pitch >= cols, TVQ_ERR_UNSUPPORTED,
+              "TMA operand must be 16-byte aligned with a 16-byte row pitch");
+    return make_map(map, ptr, rows, cols, box_rows, 2, pitch);
 }
 
 int launch_gemm(const GemmArgs& g, cudaStream_t st) {
@@ -884,12 +915,14 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.scale_a = g.scale_a;
     p.scales_w = g.scales_w;
     p.per_channel = (acc_only || split) ? 0 : g.per_channel;
-    p.kh = g.kh;
-    p.kl = g.kl;
-    p.vth = g.vth;
-    p.vtl = g.vtl;
+    p.kh = static_cast<__half*>(g.kh);
+    p.kl = static_cast<__half*>(g.kl);
+    p.vth = static_cast<__half*>(g.vth);
+    p.vtl = static_cast<__half*>(g.vtl);
     p.kvd = g.kvd;
     p.vt_pitch = g.vt_pitch;
+    p.kv_exp = g.kv_exp;
+    p.kv_bound = g.kv_bound;
     p.acc_only = acc_only ? 1 : 0;
     p.act = g.act;
     p.scale_out = g.scale_out;
@@ -921,8 +954,8 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
               "residual must be 16-byte aligned");
     TVQ_CHECK(!g.Yq || (reinterpret_cast<uintptr_t>(g.Yq) & 15) == 0, TVQ_ERR_UNSUPPORTED,
               "Yq must be 16-byte aligned");
-    TVQ_CHECK(!g.kh || (g.kind == GEMM_I8 && g.kl && g.vth && g.vtl && g.Y && g.n == 3 * g.kvd && g.kvd % 16 == 0 &&
-                        g.vt_pitch >= g.m && g.act == 0 && !g.residual),
+    TVQ_CHECK(!g.kh || (g.kind == GEMM_I8 && g.kl && g.vth && g.vtl && g.kv_exp && g.kv_bound && g.Y &&
+                        g.n == 3 * g.kvd && g.kvd % 64 == 0 && g.vt_pitch >= g.m && g.act == 0 && !g.residual),
               TVQ_ERR_INVALID, "attention operand split needs an INT8 qkv GEMM with N = 3 kvd");
     rc = get_encoder();
     if (rc) return rc;

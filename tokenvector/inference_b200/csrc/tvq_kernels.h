@@ -57,15 +57,22 @@ struct GemmArgs {
     uint32_t* amax = nullptr;         // device [1] or null
     int force_bn = 0;                 // 0 = heuristic, else 64/128/256
     // c_attn only: also write K [m, kvd] and V^T [kvd, vt_pitch] of qkv as
-    // TF32 hi / lo (the tensor-core attention's operands)
-    float *kh = nullptr, *kl = nullptr, *vth = nullptr, *vtl = nullptr;
+    // fp16 hi / lo under per-head power-of-two scales (the tensor-core
+    // attention's operands); kv_bound [4 kvd / 64] holds the per-head bounds
+    // of launch_kv_head_bound, kv_exp [2 kvd / 64] receives the exponents
+    void *kh = nullptr, *kl = nullptr, *vth = nullptr, *vtl = nullptr;
     int kvd = 0, vt_pitch = 0;
+    int* kv_exp = nullptr;
+    const float* kv_bound = nullptr;
 };
 int launch_gemm(const GemmArgs& g, cudaStream_t st);
 // Tensor map of a row-major f32 matrix [rows, cols] (row pitch `pitch`
 // elements, 0 = cols): box of 32 columns (128 bytes) x box_rows rows,
 // 128-byte swizzle.
 int make_tma_f32_sw128(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int box_rows,
+                       int64_t pitch = 0);
+// The same for fp16 [rows, cols]: box of 64 columns x box_rows rows.
+int make_tma_f16_sw128(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows,
                        int64_t pitch = 0);
 // x = hi + lo with hi rounded to TF32 precision (10 explicit mantissa bits)
 int launch_split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStream_t st);

@@ -32,6 +32,7 @@ struct Lin {
     int8_t* W = nullptr;  // [n, k]
     float* sw = nullptr;  // [n]
     float* bias = nullptr;
+    float* kvb = nullptr;  // c_attn, head dim 64: per-head K / V bounds (launch_kv_head_bound)
     int n = 0, k = 0;
     bool set = false;
 };
@@ -68,7 +69,9 @@ struct Session {
     int ncomb = 0;
     bool attn_tc = false;  // head dim 64: tensor-core attention, 128-row query tiles
     int attn_rows = 64;
-    float *kh = nullptr, *kl = nullptr, *vh = nullptr, *vl = nullptr;  // split K and V^T (tensor-core attention)
+    // split K and V^T, fp16 bits (tensor-core attention), and their head scales
+    uint16_t *kh = nullptr, *kl = nullptr, *vh = nullptr, *vl = nullptr;
+    int* kv_exp = nullptr;
     float *x = nullptr, *qkv = nullptr, *hf = nullptr, *xf = nullptr, *xf_last = nullptr, *logits = nullptr;
     size_t logits_cap = 0;
     int8_t *aq = nullptr, *hq = nullptr;
@@ -167,6 +170,8 @@ int gemm(Session& s, const int8_t* A, const Lin& l, const float* scale_a, float*
         g.kl = s.kl;
         g.vth = s.vh;
         g.vtl = s.vl;
+        g.kv_exp = s.kv_exp;
+        g.kv_bound = l.kvb;
         g.kvd = s.d;
         g.vt_pitch = attention_tc_pitch(s.T);
     }
@@ -191,7 +196,7 @@ int gemm(Session& s, const int8_t* A, const Lin& l, const float* scale_a, float*
 
 int attention(Session& s, float* out, int8_t* outq, const float* qscale, uint32_t* amax) {
     if (s.attn_tc) {  // K / V^T hi-lo come from the c_attn epilogue
-        return launch_attention_tc(s.qkv, s.kh, s.kl, s.vh, s.vl, s.T, s.tiles, s.split, s.ntiles, s.comb, s.ncomb,
+        return launch_attention_tc(s.qkv, s.kh, s.kl, s.vh, s.vl, s.kv_exp, s.T, s.tiles, s.split, s.ntiles, s.comb, s.ncomb,
                                    s.d, s.heads, out, outq, qscale, amax, s.part_o, s.part_ml, s.counters, s.st);
     }
     return launch_attention_split(s.qkv, s.tiles, s.split, s.ntiles, s.comb, s.ncomb, s.d, s.heads, out, outq, qscale,
@@ -455,6 +460,7 @@ int tvq_session_create(int device, int64_t vocab, int64_t d_model, int64_t n_hea
         STEP(s->alloc(&s->aq, MT * D));
         STEP(s->alloc(&s->hq, MT * F));
         STEP(s->alloc(&s->err, 1));
+        STEP(s->alloc(&s->kv_exp, static_cast<size_t>(2 * n_heads)));
         TVQ_CUDA(cudaMemset(s->err, 0, sizeof(int)));
         std::lock_guard<std::mutex> lk(g_mu);
         *handle = g_next++;
@@ -518,6 +524,18 @@ int tvq_session_set_layernorm(int64_t handle, int64_t layer, int64_t which, cons
     return TVQ_OK;
 }
 
+// After a linear's int8 weights, scales and bias are in place: the per-head
+// K / V bounds of a c_attn layer with head dim 64 (for the epilogue's split).
+static int lin_finish(Session* S, Lin& l, int64_t which) {
+    if (which == 0 && S->heads > 0 && S->d == 64 * S->heads) {
+        if (!l.kvb) STEP(S->alloc(&l.kvb, static_cast<size_t>(4 * S->heads)));
+        STEP(launch_kv_head_bound(l.W, l.sw, l.bias, l.k, S->d, l.kvb, S->st));
+        TVQ_CUDA(cudaStreamSynchronize(S->st));
+    }
+    l.set = true;
+    return check_device_error(S->st);
+}
+
 static int lin_alloc(Session* S, Lin& l, int n, int k) {
     if (!l.W) {
         STEP(S->alloc(&l.W, static_cast<size_t>(n) * k));
@@ -559,8 +577,7 @@ int tvq_session_set_linear_f32(int64_t handle, int64_t layer, int64_t which, con
     cudaStreamSynchronize(S->st);
     cudaFree(tmp);
     if (rc) return rc;
-    l.set = true;
-    return check_device_error(S->st);
+    return lin_finish(S, l, which);
 }
 
 int tvq_session_set_linear_i8(int64_t handle, int64_t layer, int64_t which, const int8_t* w_nk, const float* scales_w,
@@ -575,8 +592,7 @@ int tvq_session_set_linear_i8(int64_t handle, int64_t layer, int64_t which, cons
     TVQ_CUDA(cudaMemcpy(l.W, w_nk, static_cast<size_t>(n) * k, cudaMemcpyHostToDevice));
     TVQ_CUDA(cudaMemcpy(l.sw, scales_w, sizeof(float) * n, cudaMemcpyHostToDevice));
     TVQ_CUDA(cudaMemcpy(l.bias, bias, sizeof(float) * n, cudaMemcpyHostToDevice));
-    l.set = true;
-    return TVQ_OK;
+    return lin_finish(S, l, which);
 }
 
 int tvq_session_get_linear_i8(int64_t handle, int64_t layer, int64_t which, int8_t* w_nk, float* scales_w) {
@@ -858,12 +874,18 @@ int tvq_dev_attention(const float* qkv, const int64_t* seg, int64_t n_seg, int64
     if (tc) {
         // split K / V scratch, stream-ordered (freed when the kernel is done)
         const int T = static_cast<int>(seg[n_seg]);
-        const size_t n4 = static_cast<size_t>(attention_tc_pitch(T)) * d;
-        float* kv = nullptr;
-        TVQ_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&kv), sizeof(float) * 4 * std::max<size_t>(n4, 4), st));
-        int r = launch_split_kv(qkv, T, static_cast<int>(d), kv, kv + n4, kv + 2 * n4, kv + 3 * n4, st);
+        // fp16 K / V^T hi + lo (n4 halves each), then 2 heads exponents and
+        // 2 heads amax words
+        const size_t n4 = (static_cast<size_t>(attention_tc_pitch(T)) * d + 7) & ~size_t(7);
+        uint16_t* kv = nullptr;
+        TVQ_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&kv),
+                                 sizeof(uint16_t) * 4 * std::max<size_t>(n4, 8) + sizeof(int) * 4 * n_heads, st));
+        int* kv_exp = reinterpret_cast<int*>(kv + 4 * std::max<size_t>(n4, 8));
+        uint32_t* kv_amax = reinterpret_cast<uint32_t*>(kv_exp + 2 * n_heads);
+        int r = launch_split_kv(qkv, T, static_cast<int>(d), kv, kv + n4, kv + 2 * n4, kv + 3 * n4, kv_exp, kv_amax,
+                                st);
         if (!r)
-            r = launch_attention_tc(qkv, kv, kv + n4, kv + 2 * n4, kv + 3 * n4, T, tiles_dev, tiles_dev + n,
+            r = launch_attention_tc(qkv, kv, kv + n4, kv + 2 * n4, kv + 3 * n4, kv_exp, T, tiles_dev, tiles_dev + n,
                                     static_cast<int>(n), nullptr, 0, static_cast<int>(d), static_cast<int>(n_heads), out,
                                     outq, qscale_dev, amax_dev, nullptr, nullptr, nullptr, st);
         cudaError_t e = cudaFreeAsync(kv, st);
