@@ -9,34 +9,36 @@
 // by a power of two s (so that its largest value sits in [2^14, 2^15)) and
 // split into hi = fp16(x s) and lo = fp16(x s - hi) (|x s - hi - lo| <=
 // max(2^-22 |x s|, 2^-25)), and each product is formed as xl*yh + xh*yl +
-// xh*yh.  The scales: Q per query row (in this kernel), K and V per head
-// (kv_exp, written with the split operands), P = 2^(x - m) in (0, 1] by
-// 2^14.  They are powers of two and are undone exactly: the scores before
+// xh*yh.  The scales: Q, K and V per head (kv_exp, written with the split
+// operands), P = 2^(x - m) in (0, 1] by 2^14.  They are powers of two and are undone exactly: the scores before
 // the softmax, the output at the end.  The scores of one 64-key block and
 // the P*V partial of one block are each summed in TMEM over K = 64 only; the
 // running output is kept in registers with IEEE adds (the tensor core's own
 // accumulation is less exact than IEEE fp32 over long sums).
 //
-// Operands: K as fp16 hi/lo [T, d] and V transposed, V^T hi/lo [d, Tp]
-// (keys contiguous, Tp = T rounded up to 8), written by the c_attn GEMM's
-// epilogue (or launch_split_kv); the attention kernel brings 64-key blocks
-// of them into two 2-stage shared-memory rings (K, V^T) with TMA, both as
-// K-major B operands (of S = Q K^T and of P V).  Q (hi/lo) sits in shared
-// memory as the A operand of S; P (hi/lo) is written to tensor memory,
+// Operands: Q and K as fp16 hi/lo [T, d] and V transposed, V^T hi/lo [d,
+// Tp] (keys contiguous, Tp = T rounded up to 8), written by the c_attn GEMM's
+// epilogue (or launch_split_kv); the attention kernel brings the query tile
+// (A operand of S) and 64-key blocks of K and V^T into shared memory with
+// TMA, the blocks through two 2-stage rings, as K-major B operands (of S =
+// Q K^T and of P V).  P (hi/lo) is written to tensor memory,
 // double-buffered, as the A operand of P V, so the softmax of block j never
 // waits for P V of block j-1.
 //
 // One CTA = one (128-query tile, head, key range) work item; 384 threads:
-//   warp 0      TMA producer (K/V blocks)
-//   warp 1      MMA issuer: S_j = Q K_j^T into TMEM S[j&1] (M 128, N 64,
-//               K 64), then PV_{j-1} = P_{j-1} V_{j-1} into TMEM O[(j-1)&1]
+//   warp 0      TMA producer (Q, then K/V blocks)
+//   warp 1      MMA issuer for S_j = Q K_j^T into TMEM S[j&1] (M 128, N 64,
+//               K 64)
 //   warp 2      TMEM allocator (512 columns)
+//   warp 3      MMA issuer for PV_j = P_j V_j into TMEM O[j&1]
+//               (a tcgen05.mma costs its issuing thread ~65 cycles whatever
+//               N, so the two product streams get one issuer each)
 //   warps 4-11  softmax, two warps per TMEM lane group (32 query rows), one
-//               per 32-key half of each block: Q to shared memory once, then
-//               per block the row max exchanged between the pair through
-//               shared memory, online softmax in base 2, P (hi/lo) to TMEM,
-//               and the previous PV partial folded into the register
-//               accumulator (each warp owns 32 of the 64 output columns)
+//               per 32-key half of each block: per block the row max
+//               exchanged between the pair through shared memory, online
+//               softmax in base 2, P (hi/lo) to TMEM, and the previous PV
+//               partial folded into the register accumulator (each warp owns
+//               32 of the 64 output columns)
 // Every wait is a bounded mbarrier wait; on a timeout the kernel records an
 // error, drains its MMAs and TMA loads, frees TMEM and returns.
 //
@@ -65,7 +67,7 @@ constexpr int NTHREADS = 384;
 
 // shared memory (1024-byte aligned regions), every row 128 bytes = 64 fp16
 // with the 128-byte swizzle:
-//   Q hi, Q lo      128 query rows x 64 head columns: 16 KB each
+//   Q hi, Q lo      128 query rows x 64 head columns: 16 KB each (TMA)
 //   K ring [2]      per stage K hi, K lo: 64 key rows x 64 head columns
 //   V^T ring [2]    per stage V^T hi, V^T lo: 64 head rows x 64 keys
 constexpr uint32_t PART = TK * 128;                  // 8 KB
@@ -136,18 +138,19 @@ __device__ __forceinline__ void split_h2(float a, float b, uint32_t& hi, uint32_
     lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
-// K part of qkv [T, 3d] -> fp16 hi / lo [T, d] under the head scales
-// 2^kv_exp[h] (standalone path; the session's c_attn epilogue writes the same)
-__global__ void split_k16_kernel(const float* __restrict__ qkv, int T, int d, const int* __restrict__ kv_exp,
-                                 uint2* __restrict__ kh, uint2* __restrict__ kl) {
+// Q (part 0) or K (part 1) of qkv [T, 3d] -> fp16 hi / lo [T, d] under the
+// head scales 2^kv_exp[part heads + h] (standalone path; the session's
+// c_attn epilogue writes the same)
+__global__ void split_qk16_kernel(const float* __restrict__ qkv, int T, int d, int part,
+                                  const int* __restrict__ kv_exp, uint2* __restrict__ kh, uint2* __restrict__ kl) {
     griddep_wait();
     const int d4 = d >> 2;
     const int64_t n = static_cast<int64_t>(T) * d4;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t t = i / d4;
         const int c4 = static_cast<int>(i - t * d4);
-        const float f = exp2i(kv_exp[(4 * c4) / HD]);
-        const float4 v = __ldg(reinterpret_cast<const float4*>(qkv + t * 3 * d) + d4 + c4);
+        const float f = exp2i(kv_exp[part * (d / HD) + (4 * c4) / HD]);
+        const float4 v = __ldg(reinterpret_cast<const float4*>(qkv + t * 3 * d) + part * d4 + c4);
         uint2 h, l;
         split_h2(v.x * f, v.y * f, h.x, l.x);
         split_h2(v.z * f, v.w * f, h.y, l.y);
@@ -157,14 +160,14 @@ __global__ void split_k16_kernel(const float* __restrict__ qkv, int T, int d, co
 }
 
 // V part of qkv [T, 3d] -> V^T fp16 hi / lo [d, Tp] under the head scales
-// 2^kv_exp[heads + h]: 32 x 32 tiles through shared memory (coalesced on
+// 2^kv_exp[2 heads + h]: 32 x 32 tiles through shared memory (coalesced on
 // both sides); keys T..Tp-1 are written as 0.
 __global__ void split_vt16_kernel(const float* __restrict__ qkv, int T, int Tp, int d, const int* __restrict__ kv_exp,
                                   __half* __restrict__ vth, __half* __restrict__ vtl) {
     __shared__ float tile[32][33];
     griddep_wait();
     const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-    const float f = exp2i(kv_exp[d / HD + c0 / HD]);
+    const float f = exp2i(kv_exp[2 * (d / HD) + c0 / HD]);
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
         const int t = t0 + i;
         tile[i][threadIdx.x] = (t < T) ? __ldg(qkv + static_cast<int64_t>(t) * 3 * d + 2 * d + c0 + threadIdx.x) : 0.0f;
@@ -181,15 +184,16 @@ __global__ void split_vt16_kernel(const float* __restrict__ qkv, int T, int Tp, 
     }
 }
 
-// max |K| and max |V| per head (f32 bit patterns, atomicMax) of qkv [T, 3d]
+// max |Q|, max |K| and max |V| per head (f32 bit patterns, atomicMax) of
+// qkv [T, 3d]
 __global__ void kv_head_amax_kernel(const float* __restrict__ qkv, int T, int d, uint32_t* __restrict__ amax) {
     griddep_wait();
     const int heads = d / HD;
-    const int part = blockIdx.y;  // 0 K, 1 V
+    const int part = blockIdx.y;  // 0 Q, 1 K, 2 V
     const int h = blockIdx.z;
     float m = 0.0f;
     for (int t = blockIdx.x; t < T; t += gridDim.x) {
-        const float* src = qkv + static_cast<int64_t>(t) * 3 * d + (1 + part) * d + h * HD;
+        const float* src = qkv + static_cast<int64_t>(t) * 3 * d + part * d + h * HD;
         for (int c = threadIdx.x; c < HD; c += blockDim.x) m = fmaxf(m, fabsf(src[c]));
     }
 #pragma unroll
@@ -217,7 +221,7 @@ struct AttnParams {
     float2* part_ml;
     const int4* comb;  // per merge entry {q0, seq end, first slot, count}; split[i].w = entry of item i
     int* counters;     // per (entry, head): partials counted in (0 between launches)
-    const int* kv_exp; // [2 * nheads]: K and V head scales 2^kv_exp of the split operands
+    const int* kv_exp; // [3 * nheads]: Q, K and V head scales 2^kv_exp of the split operands
     int* err;
 };
 
@@ -228,7 +232,8 @@ __device__ __forceinline__ uint32_t sw128(int r, int c) {
 }
 
 __global__ void __launch_bounds__(NTHREADS, 1)
-    attention_tc_kernel(const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_constant__ CUtensorMap tmQl,
+                        const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
                         const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl,
                         const AttnParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -246,10 +251,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint64_t* o_full = bars + 14;      // [2]
     uint64_t* o_empty = bars + 16;     // [2]
     uint64_t* q_full = bars + 18;
-    uint64_t* drain = bars + 19;
-    uint64_t* xch = bars + 20;         // [4 lane groups][2 parities]: row-max exchange
-    uint64_t* lxch = bars + 28;        // [4]: row-sum exchange
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 32);
+    uint64_t* drain = bars + 19;       // [2]: S issuer, PV issuer
+    uint64_t* xch = bars + 21;         // [4 lane groups][2 parities]: row-max exchange
+    uint64_t* lxch = bars + 29;        // [4]: row-sum exchange
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 33);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -276,13 +281,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mbar_init(&o_full[b], 1);
             mbar_init(&o_empty[b], 8);
         }
-        mbar_init(q_full, 8);
-        mbar_init(drain, 1);
+        mbar_init(q_full, 1);
+        mbar_init(&drain[0], 1);
+        mbar_init(&drain[1], 1);
         for (int i = 0; i < 8; i++) mbar_init(&xch[i], 2);
         for (int i = 0; i < 4; i++) mbar_init(&lxch[i], 2);
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmQh);
+        tma_prefetch_desc(&tmQl);
         tma_prefetch_desc(&tmKh);
         tma_prefetch_desc(&tmKl);
         tma_prefetch_desc(&tmVh);
@@ -301,6 +309,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
+            // the query tile (rows past the sequence only feed rows that are
+            // never written; rows past T read as 0)
+            mbar_arrive_expect_tx(q_full, 2 * QPART);
+            tma_load_2d(&tmQh, q_full, sm + OFF_QH, head * HD, q0);
+            tma_load_2d(&tmQl, q_full, sm + OFF_QL, head * HD, q0);
             int kissued = 0, vissued = 0;
             for (int j = 0; j < nkb; j++) {
                 const int s = j & 1;
@@ -320,44 +333,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 vissued = j + 1;
             }
             // every issued load lands before the CTA may exit
+            mbar_wait(q_full, 0, p.err, DEVERR_ATTN_TMA_DRAIN);
             for (int j = kissued > 2 ? kissued - 2 : 0; j < kissued; j++)
                 mbar_wait(&k_full[j & 1], (j >> 1) & 1, p.err, DEVERR_ATTN_TMA_DRAIN);
             for (int j = vissued > 2 ? vissued - 2 : 0; j < vissued; j++)
                 mbar_wait(&v_full[j & 1], (j >> 1) & 1, p.err, DEVERR_ATTN_TMA_DRAIN);
         }
     } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer
+        // ------------------------------------------------ S issuer
         if (lane == 0) {
             const uint32_t sbase = smem_u32(sm);
             bool ok = mbar_wait(q_full, 0, p.err, DEVERR_ATTN_Q_FULL);
-            auto issue_pv = [&](int i) -> bool {
-                const int b = i & 1;
-                const uint32_t ph = (i >> 1) & 1;
-                if (!mbar_wait(&p_full[b], ph, p.err, DEVERR_ATTN_P_FULL)) return false;
-                if (!mbar_wait(&o_empty[b], ph ^ 1, p.err, DEVERR_ATTN_O_EMPTY)) return false;
-                if (!mbar_wait(&v_full[b], ph, p.err, DEVERR_ATTN_V_FULL)) return false;
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + COL_O + b * 64;
-                const uint32_t vb = sbase + OFF_V + b * KSTAGE;
-                const uint32_t pcol = tmem_base + COL_P + b * 64;  // hi: +0..31, lo: +32..63
-#pragma unroll
-                for (int kk = 0; kk < 4; kk++) {  // 16 keys (32 bytes of V^T rows, 8 P columns) per instruction
-                    const uint64_t vh = smem_desc_k_sw128(vb + kk * 32);
-                    const uint64_t vl = smem_desc_k_sw128(vb + PART + kk * 32);
-                    const uint32_t pc = 8 * kk;
-                    umma_f16_ts(d_tmem, pcol + 32 + pc, vh, IDESC, kk ? 1u : 0u);
-                    umma_f16_ts(d_tmem, pcol + pc, vl, IDESC, 1u);
-                    umma_f16_ts(d_tmem, pcol + pc, vh, IDESC, 1u);
-                }
-                umma_commit(&o_full[b]);   // PV_i in O[b]; P[b] free again
-                umma_commit(&v_empty[b]);
-                return true;
-            };
             for (int j = 0; j < nkb && ok; j++) {
                 const int b = j & 1;
                 const uint32_t ph = (j >> 1) & 1;
-                if (!mbar_wait(&k_full[b], ph, p.err, DEVERR_ATTN_K_FULL)) { ok = false; break; }
-                if (!mbar_wait(&s_empty[b], ph ^ 1, p.err, DEVERR_ATTN_S_EMPTY)) { ok = false; break; }
+                if (!mbar_wait(&k_full[b], ph, p.err, DEVERR_ATTN_K_FULL)) break;
+                if (!mbar_wait(&s_empty[b], ph ^ 1, p.err, DEVERR_ATTN_S_EMPTY)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + COL_S + b * 64;
                 const uint32_t kbs = sbase + OFF_K + b * KSTAGE;
@@ -373,11 +364,39 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
                 umma_commit(&s_full[b]);
                 umma_commit(&k_empty[b]);
-                if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
             }
-            if (ok) issue_pv(nkb - 1);
-            umma_commit(drain);
-            mbar_wait(drain, 0, p.err, DEVERR_ATTN_MMA_DRAIN);
+            // all issued MMAs retire before TMEM is released
+            umma_commit(&drain[0]);
+            mbar_wait(&drain[0], 0, p.err, DEVERR_ATTN_MMA_DRAIN);
+        }
+    } else if (warp == 3) {
+        // ------------------------------------------------ PV issuer
+        if (lane == 0) {
+            const uint32_t sbase = smem_u32(sm);
+            for (int i = 0; i < nkb; i++) {
+                const int b = i & 1;
+                const uint32_t ph = (i >> 1) & 1;
+                if (!mbar_wait(&p_full[b], ph, p.err, DEVERR_ATTN_P_FULL)) break;
+                if (!mbar_wait(&o_empty[b], ph ^ 1, p.err, DEVERR_ATTN_O_EMPTY)) break;
+                if (!mbar_wait(&v_full[b], ph, p.err, DEVERR_ATTN_V_FULL)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + COL_O + b * 64;
+                const uint32_t vb = sbase + OFF_V + b * KSTAGE;
+                const uint32_t pcol = tmem_base + COL_P + b * 64;  // hi: +0..31, lo: +32..63
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {  // 16 keys (32 bytes of V^T rows, 8 P columns) per instruction
+                    const uint64_t vh = smem_desc_k_sw128(vb + kk * 32);
+                    const uint64_t vl = smem_desc_k_sw128(vb + PART + kk * 32);
+                    const uint32_t pc = 8 * kk;
+                    umma_f16_ts(d_tmem, pcol + 32 + pc, vh, IDESC, kk ? 1u : 0u);
+                    umma_f16_ts(d_tmem, pcol + pc, vl, IDESC, 1u);
+                    umma_f16_ts(d_tmem, pcol + pc, vh, IDESC, 1u);
+                }
+                umma_commit(&o_full[b]);   // PV_i in O[b]; P[b] free again
+                umma_commit(&v_empty[b]);
+            }
+            umma_commit(&drain[1]);
+            mbar_wait(&drain[1], 0, p.err, DEVERR_ATTN_MMA_DRAIN);
         }
     } else if (warp >= 4) {
         // ------------------------------------------------ softmax
@@ -387,39 +406,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int q = q0 + r;
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(32 * g) << 16);
         bool alive = true;
-        // Q row scale (its largest |value| to [2^14, 2^15)), then head
-        // columns 32h..32h+31 -> fp16 hi / lo, K-major in shared memory
-        int sq = 0;
-        {
-            const float4* src = reinterpret_cast<const float4*>(p.qkv + static_cast<int64_t>(q) * 3 * p.d + head * HD);
-            float4 v[16];
-            float mx = 0.0f;
-#pragma unroll
-            for (int c4 = 0; c4 < 16; c4++) {
-                v[c4] = (q < s1) ? __ldg(src + c4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[c4].x), fabsf(v[c4].y)), fmaxf(fabsf(v[c4].z), fabsf(v[c4].w))));
-            }
-            sq = pow2_exp_below_2p15(mx);
-            const float fq = exp2i(sq);
-#pragma unroll
-            for (int c16 = 0; c16 < 4; c16++) {  // 16-byte chunks of the 128-byte row: 8 fp16 each
-                uint4 hi, lo;
-                const float4 a = h ? v[8 + 2 * c16] : v[2 * c16];  // static indices: registers, not local memory
-                const float4 b = h ? v[9 + 2 * c16] : v[1 + 2 * c16];
-                split_h2(a.x * fq, a.y * fq, hi.x, lo.x);
-                split_h2(a.z * fq, a.w * fq, hi.y, lo.y);
-                split_h2(b.x * fq, b.y * fq, hi.z, lo.z);
-                split_h2(b.z * fq, b.w * fq, hi.w, lo.w);
-                const uint32_t off = sw128(r, 4 * h + c16);
-                *reinterpret_cast<uint4*>(sm + OFF_QH + off) = hi;
-                *reinterpret_cast<uint4*>(sm + OFF_QL + off) = lo;
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(q_full);
-        }
         // scores: S = acc 2^-(sq + sk) exactly, times log2(e) / sqrt(hd)
-        const int sk = p.kv_exp[head], sv = p.kv_exp[p.nheads + head];
+        const int sq = p.kv_exp[head], sk = p.kv_exp[p.nheads + head], sv = p.kv_exp[2 * p.nheads + head];
         const float xs = p.scale2 * exp2i(-sq) * exp2i(-sk);
         float o[32];
 #pragma unroll
@@ -645,10 +633,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
-// Per-head bounds of a c_attn layer's K and V outputs for the epilogue's
+// Per-head bounds of a c_attn layer's Q, K and V outputs for the epilogue's
 // fp16 split (kv_head_exp): block (h, part) over the 64 output columns n of
-// head h in part (0 K, 1 V): A = max sw[n] * 127 * sum_k |W[n,k]|, B = max
-// |bias[n]|, both rounded up.  out [4 heads]: A_K, B_K, A_V, B_V.
+// head h in part (0 Q, 1 K, 2 V): A = max sw[n] * 127 * sum_k |W[n,k]|, B =
+// max |bias[n]|, both rounded up.  out [6 heads]: A_Q, B_Q, A_K, B_K, A_V, B_V.
 __global__ void kv_head_bound_kernel(const int8_t* __restrict__ W, const float* __restrict__ sw,
                                      const float* __restrict__ bias, int k, int kvd, float* __restrict__ out) {
     const int h = blockIdx.x, part = blockIdx.y, heads = gridDim.x;
@@ -656,7 +644,7 @@ __global__ void kv_head_bound_kernel(const int8_t* __restrict__ W, const float* 
     __shared__ float ra[8], rb[8];
     float a = 0.0f, bb = 0.0f;
     for (int i = warp; i < HD; i += blockDim.x >> 5) {
-        const int n = (1 + part) * kvd + h * HD + i;
+        const int n = part * kvd + h * HD + i;
         int sum = 0;
         for (int c = lane; c < k; c += 32) sum += abs(static_cast<int>(W[static_cast<int64_t>(n) * k + c]));
 #pragma unroll
@@ -685,23 +673,25 @@ int attention_tc_rows() { return TQ; }
 
 int attention_tc_pitch(int T) { return (T + 7) & ~7; }
 
-int launch_split_kv(const float* qkv, int T, int d, void* kh, void* kl, void* vth, void* vtl, int* kv_exp,
-                    uint32_t* amax, cudaStream_t st) {
+int launch_split_kv(const float* qkv, int T, int d, void* qh, void* ql, void* kh, void* kl, void* vth, void* vtl,
+                    int* kv_exp, uint32_t* amax, cudaStream_t st) {
     if (T <= 0) return TVQ_OK;
     TVQ_CHECK(d % HD == 0, TVQ_ERR_UNSUPPORTED, "d must be a multiple of 64");
     int rc = 0;
     DeviceState* ds = device_state(&rc);
     if (!ds) return rc;
     const int heads = d / HD;
-    TVQ_CUDA(cudaMemsetAsync(amax, 0, sizeof(uint32_t) * 2 * heads, st));
-    int r = launch_pdl(kv_head_amax_kernel, dim3(std::min(T, 64), 2, heads), dim3(64), 0, st, qkv, T, d, amax);
-    if (!r) r = launch_pdl(kv_exp_from_amax_kernel, dim3((2 * heads + 127) / 128), dim3(128), 0, st,
-                           static_cast<const uint32_t*>(amax), 2 * heads, kv_exp);
+    TVQ_CUDA(cudaMemsetAsync(amax, 0, sizeof(uint32_t) * 3 * heads, st));
+    int r = launch_pdl(kv_head_amax_kernel, dim3(std::min(T, 64), 3, heads), dim3(64), 0, st, qkv, T, d, amax);
+    if (!r) r = launch_pdl(kv_exp_from_amax_kernel, dim3((3 * heads + 127) / 128), dim3(128), 0, st,
+                           static_cast<const uint32_t*>(amax), 3 * heads, kv_exp);
     if (r) return r;
     const int64_t n = static_cast<int64_t>(T) * (d / 4);
     const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, ds->sm_count * 8));
-    r = launch_pdl(split_k16_kernel, dim3(grid), dim3(256), 0, st, qkv, T, d, static_cast<const int*>(kv_exp),
-                   static_cast<uint2*>(kh), static_cast<uint2*>(kl));
+    for (int part = 0; part < 2 && !r; part++)
+        r = launch_pdl(split_qk16_kernel, dim3(grid), dim3(256), 0, st, qkv, T, d, part,
+                       static_cast<const int*>(kv_exp), static_cast<uint2*>(part ? kh : qh),
+                       static_cast<uint2*>(part ? kl : ql));
     if (r) return r;
     const int Tp = attention_tc_pitch(T);
     return launch_pdl(split_vt16_kernel, dim3((Tp + 31) / 32, d / 32), dim3(32, 8), 0, st, qkv, T, Tp, d,
@@ -711,18 +701,18 @@ int launch_split_kv(const float* qkv, int T, int d, void* kh, void* kl, void* vt
 int launch_kv_head_bound(const int8_t* W, const float* sw, const float* bias, int k, int kvd, float* out,
                          cudaStream_t st) {
     TVQ_CHECK(kvd % HD == 0 && kvd > 0 && k > 0, TVQ_ERR_UNSUPPORTED, "d must be a multiple of 64");
-    kv_head_bound_kernel<<<dim3(kvd / HD, 2), 256, 0, st>>>(W, sw, bias, k, kvd, out);
+    kv_head_bound_kernel<<<dim3(kvd / HD, 3), 256, 0, st>>>(W, sw, bias, k, kvd, out);
     TVQ_CUDA(cudaGetLastError());
     return TVQ_OK;
 }
 
-int launch_attention_tc(const float* qkv, const void* kh, const void* kl, const void* vth, const void* vtl,
-                        const int* kv_exp, int T, const int4* tiles, const int4* split, int nitems, const int4* comb,
+int launch_attention_tc(const float* qkv, const void* qh, const void* ql, const void* kh, const void* kl,
+                        const void* vth, const void* vtl, const int* kv_exp, int T, const int4* tiles, const int4* split, int nitems, const int4* comb,
                         int ncomb, int d, int nheads, float* out, int8_t* outq, const float* qscale, uint32_t* amax,
                         float* part_o, float2* part_ml, int* counters, cudaStream_t st) {
     if (nitems <= 0) return TVQ_OK;
     TVQ_CHECK(nheads > 0 && d == nheads * HD, TVQ_ERR_UNSUPPORTED, "the tensor-core attention needs head dim 64");
-    TVQ_CHECK(split && kh && kl && vth && vtl && kv_exp, TVQ_ERR_INVALID,
+    TVQ_CHECK(split && qh && ql && kh && kl && vth && vtl && kv_exp, TVQ_ERR_INVALID,
               "the tensor-core attention needs key ranges, split K / V^T and their head scales");
     TVQ_CHECK((reinterpret_cast<uintptr_t>(qkv) & 15) == 0 && (!out || (reinterpret_cast<uintptr_t>(out) & 15) == 0) &&
                   (!outq || (reinterpret_cast<uintptr_t>(outq) & 3) == 0),
@@ -739,8 +729,10 @@ int launch_attention_tc(const float* qkv, const void* kh, const void* kl, const 
                                       static_cast<int>(SMEM_BYTES)));
         attr[dev] = true;
     }
-    CUtensorMap mkh, mkl, mvh, mvl;
-    rc = make_tma_f16_sw128(&mkh, kh, T, d, TK);
+    CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
+    rc = make_tma_f16_sw128(&mqh, qh, T, d, TQ);
+    if (!rc) rc = make_tma_f16_sw128(&mql, ql, T, d, TQ);
+    if (!rc) rc = make_tma_f16_sw128(&mkh, kh, T, d, TK);
     if (!rc) rc = make_tma_f16_sw128(&mkl, kl, T, d, TK);
     if (!rc) rc = make_tma_f16_sw128(&mvh, vth, d, T, HD, attention_tc_pitch(T));
     if (!rc) rc = make_tma_f16_sw128(&mvl, vtl, d, T, HD, attention_tc_pitch(T));
@@ -764,7 +756,8 @@ int launch_attention_tc(const float* qkv, const void* kh, const void* kl, const 
     p.counters = counters;
     p.kv_exp = kv_exp;
     // key-chunk partials are merged inside the kernel by the last CTA of each set
-    return launch_pdl(attention_tc_kernel, dim3(nitems * nheads), dim3(NTHREADS), SMEM_BYTES, st, mkh, mkl, mvh, mvl,
+    return launch_pdl(attention_tc_kernel, dim3(nitems * nheads), dim3(NTHREADS), SMEM_BYTES, st, mqh, mql, mkh, mkl,
+                      mvh, mvl,
                       p);
 }
 

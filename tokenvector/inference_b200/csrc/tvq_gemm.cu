@@ -86,12 +86,12 @@ struct KParams {
     const float* scale_out;
     uint32_t* amax;
     int* err;
-    // Optional attention operands of a c_attn GEMM (Y = qkv [m, 3 kvd]): the K
-    // columns [kvd, 2 kvd) also as fp16 hi / lo [m, kvd] (kh, kl) and the V
-    // columns [2 kvd, 3 kvd) transposed as hi / lo [kvd, vt_pitch] (vth, vtl),
-    // each 64-column head scaled by 2^kv_exp (kv_head_exp, from the bounds
-    // kv_bound) and the exponents stored to kv_exp [2 kvd / 64].
-    __half *kh, *kl, *vth, *vtl;
+    // Optional attention operands of a c_attn GEMM (Y = qkv [m, 3 kvd]): the Q
+    // and K columns [0, 2 kvd) also as fp16 hi / lo [m, kvd] (qh, ql, kh, kl)
+    // and the V columns [2 kvd, 3 kvd) transposed as hi / lo [kvd, vt_pitch]
+    // (vth, vtl), each 64-column head scaled by 2^kv_exp (kv_head_exp, from
+    // the bounds kv_bound) and the exponents stored to kv_exp [3 kvd / 64].
+    __half *qh, *ql, *kh, *kl, *vth, *vtl;
     int kvd, vt_pitch;
     int* kv_exp;
     const float* kv_bound;
@@ -177,8 +177,8 @@ struct EpiCtx {
     float sa;        // activation scale (attention operand bounds)
 };
 
-// Exponent of the power-of-two scale of one head (part 0 K, 1 V) of a c_attn
-// output: every |Y| of the head is at most sa * A + B (A = max over its
+// Exponent of the power-of-two scale of one head (part 0 Q, 1 K, 2 V) of a
+// c_attn output: every |Y| of the head is at most sa * A + B (A = max over its
 // columns of sw[n] * 127 * sum_k |W[n,k]|, B = max |bias[n]|, both rounded
 // up; 127 * sum_k |W[n,k]| bounds the accumulator), widened by 2^-20 for
 // the rounding of Y itself.
@@ -234,14 +234,16 @@ __device__ __forceinline__ void stage_and_store(const KParams& p, const EpiCtx& 
         float4 v = *reinterpret_cast<const float4*>(&stage[rr * E::CH + 4 * (c4 ^ ((rr >> E::SWS) & (E::LPR - 1)))]);
         if (row >= p.m || col >= p.n) continue;
         const int64_t off = static_cast<int64_t>(row) * p.n + col;
-        if (p.kh && col >= p.kvd && col < 2 * p.kvd) {  // K part: fp16 hi / lo split, row-major [m, kvd]
-            const int64_t ko = static_cast<int64_t>(row) * p.kvd + (col - p.kvd);
-            const float f = exp2i(kv_head_exp(p.kv_bound, p.kvd / 64, 0, (col - p.kvd) / 64, e.sa));
+        if (p.kh && col < 2 * p.kvd) {  // Q / K part: fp16 hi / lo split, row-major [m, kvd]
+            const int part = col >= p.kvd ? 1 : 0;
+            const int c = col - part * p.kvd;
+            const int64_t ko = static_cast<int64_t>(row) * p.kvd + c;
+            const float f = exp2i(kv_head_exp(p.kv_bound, p.kvd / 64, part, c / 64, e.sa));
             uint2 h, l;
             split_h2_pair(v.x * f, v.y * f, h.x, l.x);
             split_h2_pair(v.z * f, v.w * f, h.y, l.y);
-            *reinterpret_cast<uint2*>(p.kh + ko) = h;
-            *reinterpret_cast<uint2*>(p.kl + ko) = l;
+            *reinterpret_cast<uint2*>((part ? p.kh : p.qh) + ko) = h;
+            *reinterpret_cast<uint2*>((part ? p.kl : p.ql) + ko) = l;
         }
         if (e.vec_ok && col + 3 < p.n) {
             if (p.residual) {
@@ -643,13 +645,13 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                         }
                     }
                 }
-                if (p.vth && n0 >= p.kvd) {
-                    const int part = n0 >= 2 * p.kvd ? 1 : 0;
-                    const int hh = (n0 - (1 + part) * p.kvd) / 64;
+                if (p.vth) {
+                    const int part = n0 / p.kvd;  // 0 Q, 1 K, 2 V
+                    const int hh = (n0 - part * p.kvd) / 64;
                     const int sh = kv_head_exp(p.kv_bound, p.kvd / 64, part, hh, sa);
-                    if (row0 == 0 && lane == 0 && (n0 - (1 + part) * p.kvd) % 64 == 0)
+                    if (row0 == 0 && lane == 0 && (n0 - part * p.kvd) % 64 == 0)
                         p.kv_exp[part * (p.kvd / 64) + hh] = sh;  // one writer per head
-                    if (part == 1 && row0 + lane < p.m) {
+                    if (part == 2 && row0 + lane < p.m) {
                         // V part, transposed: column n0 + j -> row of V^T; lanes
                         // (consecutive tokens) write consecutive addresses
                         const int64_t vo = static_cast<int64_t>(n0 - 2 * p.kvd) * p.vt_pitch + row0 + lane;
@@ -915,6 +917,8 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.scale_a = g.scale_a;
     p.scales_w = g.scales_w;
     p.per_channel = (acc_only || split) ? 0 : g.per_channel;
+    p.qh = static_cast<__half*>(g.qh);
+    p.ql = static_cast<__half*>(g.ql);
     p.kh = static_cast<__half*>(g.kh);
     p.kl = static_cast<__half*>(g.kl);
     p.vth = static_cast<__half*>(g.vth);
@@ -954,7 +958,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
               "residual must be 16-byte aligned");
     TVQ_CHECK(!g.Yq || (reinterpret_cast<uintptr_t>(g.Yq) & 15) == 0, TVQ_ERR_UNSUPPORTED,
               "Yq must be 16-byte aligned");
-    TVQ_CHECK(!g.kh || (g.kind == GEMM_I8 && g.kl && g.vth && g.vtl && g.kv_exp && g.kv_bound && g.Y &&
+    TVQ_CHECK(!g.kh || (g.kind == GEMM_I8 && g.qh && g.ql && g.kl && g.vth && g.vtl && g.kv_exp && g.kv_bound && g.Y &&
                         g.n == 3 * g.kvd && g.kvd % 64 == 0 && g.vt_pitch >= g.m && g.act == 0 && !g.residual),
               TVQ_ERR_INVALID, "attention operand split needs an INT8 qkv GEMM with N = 3 kvd");
     rc = get_encoder();

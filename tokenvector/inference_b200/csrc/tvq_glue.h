@@ -23,26 +23,27 @@ int launch_attention_split(const float* qkv, const int4* tiles, const int4* spli
 int launch_attention_combine(const int4* comb, int ncomb, int d, int nheads, int rows, const float* part_o,
                              const float2* part_ml, float* out, int8_t* outq, const float* qscale, uint32_t* amax,
                              cudaStream_t st);
-// tvq_attn_tc.cu: head dim 64 on the tensor cores.  The K part of qkv as
-// fp16 hi / lo [T, d] and the V part transposed, V^T hi / lo [d,
-// attention_tc_pitch(T)], each head h scaled by 2^kv_exp[h] (K) and
-// 2^kv_exp[heads + h] (V) so that its values stay below 2^15: written by the
+// tvq_attn_tc.cu: head dim 64 on the tensor cores.  The Q and K parts of
+// qkv as fp16 hi / lo [T, d] and the V part transposed, V^T hi / lo [d,
+// attention_tc_pitch(T)], head h of part p (0 Q, 1 K, 2 V) scaled by
+// 2^kv_exp[p heads + h] so that its values stay below 2^15: written by the
 // c_attn GEMM epilogue in a session, or by launch_split_kv (exact per-head
-// max|K|, max|V| into amax[2 heads], then the split).  launch_attention_tc
-// takes them with the same work items as above but attention_tc_rows() (128)
-// query rows per tile; split[] is required.
+// max |.| into amax[3 heads], then the split).  launch_attention_tc takes
+// them with the same work items as above but attention_tc_rows() (128) query
+// rows per tile; split[] is required.
 int attention_tc_rows();
 int attention_tc_pitch(int T);
-int launch_split_kv(const float* qkv, int T, int d, void* kh, void* kl, void* vth, void* vtl, int* kv_exp,
-                    uint32_t* amax, cudaStream_t st);
-// Per-head bounds [4 d / 64] of a c_attn layer (W int8 [3d, k], per-channel
-// sw, bias or null) for the epilogue's K / V split (GemmArgs::kv_bound).
+int launch_split_kv(const float* qkv, int T, int d, void* qh, void* ql, void* kh, void* kl, void* vth, void* vtl,
+                    int* kv_exp, uint32_t* amax, cudaStream_t st);
+// Per-head bounds [6 d / 64] of a c_attn layer (W int8 [3d, k], per-channel
+// sw, bias or null) for the epilogue's Q / K / V split (GemmArgs::kv_bound).
 int launch_kv_head_bound(const int8_t* W, const float* sw, const float* bias, int k, int kvd, float* out,
                          cudaStream_t st);
-int launch_attention_tc(const float* qkv, const void* kh, const void* kl, const void* vth, const void* vtl,
-                        const int* kv_exp, int T, const int4* tiles, const int4* split, int nitems, const int4* comb,
-                        int ncomb, int d, int nheads, float* out, int8_t* outq, const float* qscale, uint32_t* amax,
-                        float* part_o, float2* part_ml, int* counters, cudaStream_t st);
+int launch_attention_tc(const float* qkv, const void* qh, const void* ql, const void* kh, const void* kl,
+                        const void* vth, const void* vtl, const int* kv_exp, int T, const int4* tiles,
+                        const int4* split, int nitems, const int4* comb, int ncomb, int d, int nheads, float* out,
+                        int8_t* outq, const float* qscale, uint32_t* amax, float* part_o, float2* part_ml,
+                        int* counters, cudaStream_t st);
 int launch_scale_from_amax(const uint32_t* amax, float* scale, int n, cudaStream_t st);
 int launch_transpose(const float* a, float* b, int rows, int cols, cudaStream_t st);
 int launch_token_seg(const int* seg, int nseg, int* tok_start, cudaStream_t st);

@@ -56,11 +56,11 @@ struct GemmArgs {
     const float* scale_out = nullptr; // device [1], needed with Yq
     uint32_t* amax = nullptr;         // device [1] or null
     int force_bn = 0;                 // 0 = heuristic, else 64/128/256
-    // c_attn only: also write K [m, kvd] and V^T [kvd, vt_pitch] of qkv as
+    // c_attn only: also write Q, K [m, kvd] and V^T [kvd, vt_pitch] of qkv as
     // fp16 hi / lo under per-head power-of-two scales (the tensor-core
-    // attention's operands); kv_bound [4 kvd / 64] holds the per-head bounds
-    // of launch_kv_head_bound, kv_exp [2 kvd / 64] receives the exponents
-    void *kh = nullptr, *kl = nullptr, *vth = nullptr, *vtl = nullptr;
+    // attention's operands); kv_bound [6 kvd / 64] holds the per-head bounds
+    // of launch_kv_head_bound, kv_exp [3 kvd / 64] receives the exponents
+    void *qh = nullptr, *ql = nullptr, *kh = nullptr, *kl = nullptr, *vth = nullptr, *vtl = nullptr;
     int kvd = 0, vt_pitch = 0;
     int* kv_exp = nullptr;
     const float* kv_bound = nullptr;

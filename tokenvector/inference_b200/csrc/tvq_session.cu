@@ -69,8 +69,8 @@ struct Session {
     int ncomb = 0;
     bool attn_tc = false;  // head dim 64: tensor-core attention, 128-row query tiles
     int attn_rows = 64;
-    // split K and V^T, fp16 bits (tensor-core attention), and their head scales
-    uint16_t *kh = nullptr, *kl = nullptr, *vh = nullptr, *vl = nullptr;
+    // split Q, K and V^T, fp16 bits (tensor-core attention), and their head scales
+    uint16_t *qh = nullptr, *ql = nullptr, *kh = nullptr, *kl = nullptr, *vh = nullptr, *vl = nullptr;
     int* kv_exp = nullptr;
     float *x = nullptr, *qkv = nullptr, *hf = nullptr, *xf = nullptr, *xf_last = nullptr, *logits = nullptr;
     size_t logits_cap = 0;
@@ -166,6 +166,8 @@ int gemm(Session& s, const int8_t* A, const Lin& l, const float* scale_a, float*
          int8_t* Yq, const float* scale_out, uint32_t* amax, int act, bool kv_split = false) {
     GemmArgs g;
     if (kv_split) {  // c_attn on the tensor-core attention path: K and V^T operands from the epilogue
+        g.qh = s.qh;
+        g.ql = s.ql;
         g.kh = s.kh;
         g.kl = s.kl;
         g.vth = s.vh;
@@ -196,7 +198,7 @@ int gemm(Session& s, const int8_t* A, const Lin& l, const float* scale_a, float*
 
 int attention(Session& s, float* out, int8_t* outq, const float* qscale, uint32_t* amax) {
     if (s.attn_tc) {  // K / V^T hi-lo come from the c_attn epilogue
-        return launch_attention_tc(s.qkv, s.kh, s.kl, s.vh, s.vl, s.kv_exp, s.T, s.tiles, s.split, s.ntiles, s.comb, s.ncomb,
+        return launch_attention_tc(s.qkv, s.qh, s.ql, s.kh, s.kl, s.vh, s.vl, s.kv_exp, s.T, s.tiles, s.split, s.ntiles, s.comb, s.ncomb,
                                    s.d, s.heads, out, outq, qscale, amax, s.part_o, s.part_ml, s.counters, s.st);
     }
     return launch_attention_split(s.qkv, s.tiles, s.split, s.ntiles, s.comb, s.ncomb, s.d, s.heads, out, outq, qscale,
@@ -460,7 +462,7 @@ int tvq_session_create(int device, int64_t vocab, int64_t d_model, int64_t n_hea
         STEP(s->alloc(&s->aq, MT * D));
         STEP(s->alloc(&s->hq, MT * F));
         STEP(s->alloc(&s->err, 1));
-        STEP(s->alloc(&s->kv_exp, static_cast<size_t>(2 * n_heads)));
+        STEP(s->alloc(&s->kv_exp, static_cast<size_t>(3 * n_heads)));
         TVQ_CUDA(cudaMemset(s->err, 0, sizeof(int)));
         std::lock_guard<std::mutex> lk(g_mu);
         *handle = g_next++;
@@ -528,7 +530,7 @@ int tvq_session_set_layernorm(int64_t handle, int64_t layer, int64_t which, cons
 // K / V bounds of a c_attn layer with head dim 64 (for the epilogue's split).
 static int lin_finish(Session* S, Lin& l, int64_t which) {
     if (which == 0 && S->heads > 0 && S->d == 64 * S->heads) {
-        if (!l.kvb) STEP(S->alloc(&l.kvb, static_cast<size_t>(4 * S->heads)));
+        if (!l.kvb) STEP(S->alloc(&l.kvb, static_cast<size_t>(6 * S->heads)));
         STEP(launch_kv_head_bound(l.W, l.sw, l.bias, l.k, S->d, l.kvb, S->st));
         TVQ_CUDA(cudaStreamSynchronize(S->st));
     }
@@ -708,6 +710,8 @@ int tvq_session_prepare(int64_t handle, const int64_t* seg, int64_t n_seg, int l
     S->attn_rows = QT;
     if (tc && !S->kh) {
         const size_t n = static_cast<size_t>(attention_tc_pitch(S->max_tokens)) * S->d;
+        STEP(S->alloc(&S->qh, n));
+        STEP(S->alloc(&S->ql, n));
         STEP(S->alloc(&S->kh, n));
         STEP(S->alloc(&S->kl, n));
         STEP(S->alloc(&S->vh, n));
@@ -874,18 +878,19 @@ int tvq_dev_attention(const float* qkv, const int64_t* seg, int64_t n_seg, int64
     if (tc) {
         // split K / V scratch, stream-ordered (freed when the kernel is done)
         const int T = static_cast<int>(seg[n_seg]);
-        // fp16 K / V^T hi + lo (n4 halves each), then 2 heads exponents and
-        // 2 heads amax words
-        const size_t n4 = (static_cast<size_t>(attention_tc_pitch(T)) * d + 7) & ~size_t(7);
+        // fp16 Q / K / V^T hi + lo (n4 halves each), then 3 heads exponents
+        // and 3 heads amax words
+        const size_t n4 = std::max<size_t>((static_cast<size_t>(attention_tc_pitch(T)) * d + 7) & ~size_t(7), 8);
         uint16_t* kv = nullptr;
-        TVQ_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&kv),
-                                 sizeof(uint16_t) * 4 * std::max<size_t>(n4, 8) + sizeof(int) * 4 * n_heads, st));
-        int* kv_exp = reinterpret_cast<int*>(kv + 4 * std::max<size_t>(n4, 8));
-        uint32_t* kv_amax = reinterpret_cast<uint32_t*>(kv_exp + 2 * n_heads);
-        int r = launch_split_kv(qkv, T, static_cast<int>(d), kv, kv + n4, kv + 2 * n4, kv + 3 * n4, kv_exp, kv_amax,
-                                st);
+        TVQ_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&kv), sizeof(uint16_t) * 6 * n4 + sizeof(int) * 6 * n_heads,
+                                 st));
+        int* kv_exp = reinterpret_cast<int*>(kv + 6 * n4);
+        uint32_t* kv_amax = reinterpret_cast<uint32_t*>(kv_exp + 3 * n_heads);
+        int r = launch_split_kv(qkv, T, static_cast<int>(d), kv, kv + n4, kv + 2 * n4, kv + 3 * n4, kv + 4 * n4,
+                                kv + 5 * n4, kv_exp, kv_amax, st);
         if (!r)
-            r = launch_attention_tc(qkv, kv, kv + n4, kv + 2 * n4, kv + 3 * n4, kv_exp, T, tiles_dev, tiles_dev + n,
+            r = launch_attention_tc(qkv, kv, kv + n4, kv + 2 * n4, kv + 3 * n4, kv + 4 * n4, kv + 5 * n4, kv_exp, T,
+                                    tiles_dev, tiles_dev + n,
                                     static_cast<int>(n), nullptr, 0, static_cast<int>(d), static_cast<int>(n_heads), out,
                                     outq, qscale_dev, amax_dev, nullptr, nullptr, nullptr, st);
         cudaError_t e = cudaFreeAsync(kv, st);
