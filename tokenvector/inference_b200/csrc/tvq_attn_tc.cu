@@ -26,10 +26,10 @@
 // waits for P V of block j-1.
 //
 // One CTA = one (128-query tile, head, key range) work item; 384 threads:
-//   warp 0      TMA producer (Q, then K/V blocks)
+//   warp 0      TMA producer (Q, then K blocks)
 //   warp 1      MMA issuer for S_j = Q K_j^T into TMEM S[j&1] (M 128, N 64,
 //               K 64)
-//   warp 2      TMEM allocator (512 columns)
+//   warp 2      TMEM allocator (512 columns), then TMA producer of V^T blocks
 //   warp 3      MMA issuer for PV_j = P_j V_j into TMEM O[j&1]
 //               (a tcgen05.mma costs its issuing thread ~65 cycles whatever
 //               N, so the two product streams get one issuer each)
@@ -134,6 +134,21 @@ __device__ __forceinline__ void split_h2(float a, float b, uint32_t& hi, uint32_
     const __half2 h = __floats2half2_rn(a, b);
     const float2 hf = __half22float2(h);
     const __half2 l = __floats2half2_rn(__fsub_rn(a, hf.x), __fsub_rn(b, hf.y));
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// The P split of the softmax, for 0 <= a, b <= 2^14: hi = the value rounded
+// to fp16's 11 significant bits with integer operations (exact in fp16 for
+// values >= 2^-14), lo = the exact remainder; one packed conversion each
+// (|a - hi - lo| <= max(2^-22 a, 2^-25), as split_h2).
+__device__ __forceinline__ void split_p2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+    ua = (ua + 0xFFFu + ((ua >> 13) & 1u)) & 0xFFFFE000u;  // nearest, ties to even
+    ub = (ub + 0xFFFu + ((ub >> 13) & 1u)) & 0xFFFFE000u;
+    const float ha = __uint_as_float(ua), hb = __uint_as_float(ub);
+    const __half2 h = __floats2half2_rn(ha, hb);
+    const __half2 l = __floats2half2_rn(__fsub_rn(a, ha), __fsub_rn(b, hb));
     hi = *reinterpret_cast<const uint32_t*>(&h);
     lo = *reinterpret_cast<const uint32_t*>(&l);
 }
@@ -314,17 +329,32 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mbar_arrive_expect_tx(q_full, 2 * QPART);
             tma_load_2d(&tmQh, q_full, sm + OFF_QH, head * HD, q0);
             tma_load_2d(&tmQl, q_full, sm + OFF_QL, head * HD, q0);
-            int kissued = 0, vissued = 0;
+            int kissued = 0;
             for (int j = 0; j < nkb; j++) {
                 const int s = j & 1;
                 const uint32_t ph = ((j >> 1) & 1) ^ 1;
-                const int key = kb_al + j * TK;  // a multiple of 4
+                const int key = kb_al + j * TK;  // a multiple of 8
                 if (!mbar_wait(&k_empty[s], ph, p.err, DEVERR_ATTN_K_EMPTY)) break;
                 mbar_arrive_expect_tx(&k_full[s], KSTAGE);
                 uint8_t* ks = sm + OFF_K + s * KSTAGE;
                 tma_load_2d(&tmKh, &k_full[s], ks, head * HD, key);
                 tma_load_2d(&tmKl, &k_full[s], ks + PART, head * HD, key);
                 kissued = j + 1;
+            }
+            // every issued load lands before the CTA may exit
+            mbar_wait(q_full, 0, p.err, DEVERR_ATTN_TMA_DRAIN);
+            for (int j = kissued > 2 ? kissued - 2 : 0; j < kissued; j++)
+                mbar_wait(&k_full[j & 1], (j >> 1) & 1, p.err, DEVERR_ATTN_TMA_DRAIN);
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------ TMA producer of V^T
+        // (its own thread: K blocks run ahead of the PV products)
+        if (lane == 0) {
+            int vissued = 0;
+            for (int j = 0; j < nkb; j++) {
+                const int s = j & 1;
+                const uint32_t ph = ((j >> 1) & 1) ^ 1;
+                const int key = kb_al + j * TK;
                 if (!mbar_wait(&v_empty[s], ph, p.err, DEVERR_ATTN_V_EMPTY)) break;
                 mbar_arrive_expect_tx(&v_full[s], KSTAGE);
                 uint8_t* vs = sm + OFF_V + s * KSTAGE;
@@ -332,10 +362,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 tma_load_2d(&tmVl, &v_full[s], vs + PART, key, head * HD);
                 vissued = j + 1;
             }
-            // every issued load lands before the CTA may exit
-            mbar_wait(q_full, 0, p.err, DEVERR_ATTN_TMA_DRAIN);
-            for (int j = kissued > 2 ? kissued - 2 : 0; j < kissued; j++)
-                mbar_wait(&k_full[j & 1], (j >> 1) & 1, p.err, DEVERR_ATTN_TMA_DRAIN);
             for (int j = vissued > 2 ? vissued - 2 : 0; j < vissued; j++)
                 mbar_wait(&v_full[j & 1], (j >> 1) & 1, p.err, DEVERR_ATTN_TMA_DRAIN);
         }
@@ -468,7 +494,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int c = 0; c < 32; c += 2) {
                 const float e0 = ex2_approx(x[c] - mref14), e1 = ex2_approx(x[c + 1] - mref14);
                 sa4[(c >> 1) & 3] += e0 + e1;
-                split_h2(e0, e1, phi[c / 2], plo[c / 2]);
+                split_p2(e0, e1, phi[c / 2], plo[c / 2]);
             }
             const float sum = (sa4[0] + sa4[1]) + (sa4[2] + sa4[3]);
             tmem_st16(lane_base + COL_P + b * 64 + 16 * h, phi);
