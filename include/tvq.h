@@ -298,6 +298,46 @@ TVQ_API int tvq_dev_qlinear_matmul(const int8_t* a, float scale_a, int64_t zp_a,
 TVQ_API int tvq_dev_dynamic_quantize_linear(const float* x, int64_t n, int8_t* y, float* y_scale_dev,
                                             float* y_zp_dev, void* stream);
 
+/* ================================================================ group-wise INT4 (int4.tkv)
+ * Weights [rows, cols] -> packed bytes [rows, cols/2] (two nibbles per byte,
+ * low nibble first; the reference's list[i32] holds the same byte values),
+ * scales f32 [rows, cols/group_size], and for the AWQ-style asymmetric form
+ * zero points int64 [rows, cols/group_size] (zps NULL = symmetric).  cols
+ * must be an even multiple of group_size (else TVQ_ERR_SIZE, the reference's
+ * ValueError).  Bit-exact with the reference's f64 arithmetic.
+ *   quantize_int4_grouped        int4.tkv:27-48 (scales :18-29)
+ *   dequantize_int4_grouped      int4.tkv:51-64
+ *   quantize_int4_grouped_asym   int4.tkv:68-150
+ *   dequantize_int4_grouped_asym int4.tkv:153-164
+ *   permute_cols / inv_permute_cols (inverse = 1)  int4.tkv:169-184
+ *   matmul_int4_grouped (perm NULL) / matmul_int4_grouped_ordered (act
+ *     order, A columns gathered by perm)  int4.tkv:187-239: Y[m,n] = sum_k
+ *     A[m, perm[k]] * (nib - 8) * scale[n, k/gs] + bias[n], f32 A [m,k],
+ *     packed W [n, k/2]; on the tensor cores with fp32 accuracy (A split
+ *     into fp16 hi/lo under power-of-two row scales, the weights' integers
+ *     exact in fp16, each group's partial sum times its scale in registers).
+ * Device forms take device pointers and a stream; host forms are synchronous. */
+TVQ_API int tvq_dev_quantize_int4_grouped(const float* src, int64_t rows, int64_t cols, int64_t group_size,
+                                          uint8_t* packed, float* scales, int64_t* zps, void* stream);
+TVQ_API int tvq_dev_dequantize_int4_grouped(const uint8_t* packed, float* dst, int64_t rows, int64_t cols,
+                                            int64_t group_size, const float* scales, const int64_t* zps,
+                                            void* stream);
+TVQ_API int tvq_dev_permute_cols(const float* src, float* dst, int64_t rows, int64_t cols, const int64_t* perm,
+                                 int inverse, void* stream);
+TVQ_API int tvq_dev_matmul_int4_grouped(const float* A, const uint8_t* packed_w, const float* bias, float* Y,
+                                        int64_t m, int64_t n, int64_t k, int64_t group_size, const float* scales_w,
+                                        const int64_t* perm, void* stream);
+TVQ_API int tvq_quantize_int4_grouped(const float* src, int64_t rows, int64_t cols, int64_t group_size,
+                                      uint8_t* packed_out, float* scales_out, int64_t* zps_out);
+TVQ_API int tvq_dequantize_int4_grouped(const uint8_t* packed, float* dst, int64_t rows, int64_t cols,
+                                        int64_t group_size, const float* scales, int64_t n_scales,
+                                        const int64_t* zps);
+TVQ_API int tvq_permute_cols(const float* src, float* dst, int64_t rows, int64_t cols, const int64_t* perm,
+                             int64_t n_perm, int inverse);
+TVQ_API int tvq_matmul_int4_grouped(const float* A, const uint8_t* packed_w, const float* bias, int64_t n_bias,
+                                    float* Y, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                                    const float* scales_w, int64_t n_scales, const int64_t* perm);
+
 /* ================================================================ sessions
  * Device-resident GPT-2-shaped INT8 PTQ stack: embeddings, n_layers blocks of
  * (ln_1, c_attn, attention, c_proj, ln_2, c_fc, GELU-erf, mlp c_proj) with the

@@ -93,6 +93,12 @@ def lib():
             "tvo_calibrate_percentile": (QParams, [P, i64, f32, i32, P]),
             "tvo_calibrate_mse": (QParams, [P, i64, i64]),
             "tvo_calibrate_mse_curve": (None, [P, i64, i64, P]),
+            "tvo_quantize_int4_grouped": (i32, [P, i64, i64, i64, P, P]),
+            "tvo_dequantize_int4_grouped": (i32, [P, P, i64, i64, i64, P]),
+            "tvo_quantize_int4_grouped_asym": (i32, [P, i64, i64, i64, P, P, P]),
+            "tvo_dequantize_int4_grouped_asym": (i32, [P, P, i64, i64, i64, P, P]),
+            "tvo_permute_cols": (i32, [P, P, i64, i64, P, i32]),
+            "tvo_matmul_int4_grouped": (i32, [P, P, P, i64, P, i64, i64, i64, i64, P, P]),
             "tvo_num_threads": (i32, []),
             "tvo_set_num_threads": (None, [i32]),
         }
@@ -513,3 +519,75 @@ def calibrate_mse_curve(data, num_candidates: int = 50) -> np.ndarray:
     lib().tvo_calibrate_mse_curve(_p(d), d.size, int(num_candidates), _p(out))
     return out
 
+
+
+# ---------------------------------------------------------------- tv/quantization/int4.tkv
+def _i4_check(rc):
+    if rc != 0:
+        raise ValueError("cols must be an even multiple of group_size (or a permutation index is out of range)")
+
+
+def quantize_int4_grouped(src, rows: int, cols: int, group_size: int):
+    """int4.tkv:27-48 -> (packed uint8 [rows, cols/2], scales f32 [rows, cols/group_size])."""
+    x = _f32(src).reshape(rows, cols)
+    packed = np.zeros((rows, cols // 2), np.uint8)
+    scales = np.zeros((rows, max(cols // max(group_size, 1), 1)), np.float32)
+    _i4_check(lib().tvo_quantize_int4_grouped(_p(x), rows, cols, group_size, _p(packed), _p(scales)))
+    return packed, scales
+
+
+def dequantize_int4_grouped(packed, rows: int, cols: int, group_size: int, scales) -> np.ndarray:
+    """int4.tkv:51-64."""
+    pk = np.ascontiguousarray(packed, np.uint8)
+    sc = _f32(scales)
+    out = np.empty((rows, cols), np.float32)
+    _i4_check(lib().tvo_dequantize_int4_grouped(_p(pk), _p(out), rows, cols, group_size, _p(sc)))
+    return out
+
+
+def quantize_int4_grouped_asym(src, rows: int, cols: int, group_size: int):
+    """int4.tkv:68-150 -> (packed, scales f32, zero points int64)."""
+    x = _f32(src).reshape(rows, cols)
+    ng = cols // max(group_size, 1)
+    packed = np.zeros((rows, cols // 2), np.uint8)
+    scales = np.zeros((rows, max(ng, 1)), np.float32)
+    zps = np.zeros((rows, max(ng, 1)), np.int64)
+    _i4_check(lib().tvo_quantize_int4_grouped_asym(_p(x), rows, cols, group_size, _p(packed), _p(scales), _p(zps)))
+    return packed, scales, zps
+
+
+def dequantize_int4_grouped_asym(packed, rows: int, cols: int, group_size: int, scales, zps) -> np.ndarray:
+    """int4.tkv:153-164."""
+    pk = np.ascontiguousarray(packed, np.uint8)
+    sc = _f32(scales)
+    zp = np.ascontiguousarray(zps, np.int64)
+    out = np.empty((rows, cols), np.float32)
+    _i4_check(lib().tvo_dequantize_int4_grouped_asym(_p(pk), _p(out), rows, cols, group_size, _p(sc), _p(zp)))
+    return out
+
+
+def permute_cols(src, rows: int, cols: int, perm, inverse: bool = False) -> np.ndarray:
+    """permute_cols / inv_permute_cols, int4.tkv:169-184."""
+    x = _f32(src).reshape(rows, cols)
+    pm = np.ascontiguousarray(perm, np.int64)
+    if pm.size != cols:
+        raise ValueError("perm length must equal cols")
+    out = np.empty_like(x)
+    _i4_check(lib().tvo_permute_cols(_p(x), _p(out), rows, cols, _p(pm), 1 if inverse else 0))
+    return out
+
+
+def matmul_int4_grouped(A, packed, bias, group_size: int, scales, perm=None) -> np.ndarray:
+    """matmul_int4_grouped (int4.tkv:213-239); with perm the act-order form
+    matmul_int4_grouped_ordered (:187-208).  A f32 [m, k], packed [n, k/2]."""
+    a = _f32(A)
+    m, k = a.shape
+    pk = np.ascontiguousarray(packed, np.uint8)
+    n = pk.shape[0]
+    sc = _f32(scales)
+    b = _f32(bias) if bias is not None and len(bias) else np.zeros(0, np.float32)
+    pm = np.ascontiguousarray(perm, np.int64) if perm is not None else None
+    y = np.empty((m, n), np.float32)
+    _i4_check(lib().tvo_matmul_int4_grouped(_p(a), _p(pk), _p(b) if b.size else None, b.size, _p(y), m, n, k,
+                                            group_size, _p(sc), _p(pm) if pm is not None else None))
+    return y

@@ -1011,3 +1011,162 @@ TVO_API void tvo_calibrate_mse_curve(const float* data, int64_t n, int64_t num_c
         out[c - 1] = mse / (double)n;
     }
 }
+
+/* ---------------------------------------------------------------------- */
+/* tv/quantization/int4.tkv: group-wise INT4 (GPTQ / AWQ layout)           */
+/* ---------------------------------------------------------------------- */
+/* Packing: two nibbles per byte, low nibble first; the reference keeps the
+ * bytes in list[i32] (values 0..255), here uint8.  Locals are f64, list
+ * stores round to f32, int(round()) is half-to-even (net_round_to_i64). */
+
+/* quantize_int4_grouped, int4.tkv:27-48 (+ _int4_scales_sym :18-29):
+ * scale[r, g] = fl32(max(max|x|, 1e-8) / 7); q = clamp(round(x * (1/s)),
+ * -8, 7) + 8.  Returns -1 when cols is not a multiple of group_size or odd
+ * (the reference's ValueError). */
+TVO_API int tvo_quantize_int4_grouped(const float* src, int64_t rows, int64_t cols, int64_t group_size,
+                                      uint8_t* packed, float* scales) {
+    if (group_size <= 0 || cols % group_size != 0 || cols % 2 != 0) return -1;
+    const int64_t ng = cols / group_size;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++) {
+        for (int64_t g = 0; g < ng; g++) {
+            double am = 0.0;
+            for (int64_t c = 0; c < group_size; c++) {
+                const double a = fabs((double)src[r * cols + g * group_size + c]);
+                if (a > am) am = a;
+            }
+            if (am < 0.00000001) am = 0.00000001;
+            scales[r * ng + g] = (float)(am / 7.0);
+        }
+        for (int64_t c = 0; c < cols; c += 2) {
+            const double sc = scales[r * ng + c / group_size];
+            const double inv = 1.0 / sc;
+            const int64_t q0 = clamp_i64(net_round_to_i64((double)src[r * cols + c] * inv), -8, 7) + 8;
+            const int64_t q1 = clamp_i64(net_round_to_i64((double)src[r * cols + c + 1] * inv), -8, 7) + 8;
+            packed[r * (cols / 2) + c / 2] = (uint8_t)((q1 << 4) | q0);
+        }
+    }
+    return 0;
+}
+
+/* dequantize_int4_grouped, int4.tkv:51-64: fl32((nib - 8) * s). */
+TVO_API int tvo_dequantize_int4_grouped(const uint8_t* packed, float* dst, int64_t rows, int64_t cols,
+                                        int64_t group_size, const float* scales) {
+    if (group_size <= 0 || cols % group_size != 0 || cols % 2 != 0) return -1;
+    const int64_t ng = cols / group_size;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t c = 0; c < cols; c += 2) {
+            const double sc = scales[r * ng + c / group_size];
+            const int b = packed[r * (cols / 2) + c / 2];
+            dst[r * cols + c] = (float)((double)((b & 0xF) - 8) * sc);
+            dst[r * cols + c + 1] = (float)((double)(((b >> 4) & 0xF) - 8) * sc);
+        }
+    return 0;
+}
+
+/* quantize_int4_grouped_asym, int4.tkv:68-150: per group (scale, zero
+ * point) with the reference's corrections for all-positive groups (zp 0,
+ * scale max/15) and zp clamped to 15 (scale -min/15), floors 1e-8. */
+TVO_API int tvo_quantize_int4_grouped_asym(const float* src, int64_t rows, int64_t cols, int64_t group_size,
+                                           uint8_t* packed, float* scales, int64_t* zps) {
+    if (group_size <= 0 || cols % group_size != 0 || cols % 2 != 0) return -1;
+    const int64_t ng = cols / group_size;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++) {
+        for (int64_t gg = 0; gg < ng; gg++) {
+            double mn = src[r * cols + gg * group_size];
+            double mx = mn;
+            for (int64_t c = 1; c < group_size; c++) {
+                const double v = src[r * cols + gg * group_size + c];
+                if (v < mn) mn = v;
+                if (v > mx) mx = v;
+            }
+            if (mx - mn < 0.00000001) mx = mn + 0.00000001;
+            double sc = (mx - mn) / 15.0;
+            int64_t zp = net_round_to_i64(-mn / sc);
+            if (zp < 0) zp = 0;
+            if (zp > 15) zp = 15;
+            if (zp == 0) {
+                if (mn > 0) {
+                    sc = mx / 15.0;
+                    if (sc < 0.00000001) sc = 0.00000001;
+                    zp = 0;
+                }
+            } else if (zp == 15) {
+                sc = -mn / 15.0;
+            }
+            if (sc < 0.00000001) sc = 0.00000001;
+            scales[r * ng + gg] = (float)sc;
+            zps[r * ng + gg] = zp;
+        }
+        for (int64_t c = 0; c < cols; c += 2) {
+            const int64_t gg = c / group_size;
+            const double sc = scales[r * ng + gg];
+            const int64_t zp = zps[r * ng + gg];
+            const double mn = (double)(-zp) * sc;
+            const int64_t q0 = clamp_i64(net_round_to_i64(((double)src[r * cols + c] - mn) / sc), 0, 15);
+            const int64_t q1 = clamp_i64(net_round_to_i64(((double)src[r * cols + c + 1] - mn) / sc), 0, 15);
+            packed[r * (cols / 2) + c / 2] = (uint8_t)((q1 << 4) | q0);
+        }
+    }
+    return 0;
+}
+
+/* dequantize_int4_grouped_asym, int4.tkv:153-164: fl32((nib - zp) * s). */
+TVO_API int tvo_dequantize_int4_grouped_asym(const uint8_t* packed, float* dst, int64_t rows, int64_t cols,
+                                             int64_t group_size, const float* scales, const int64_t* zps) {
+    if (group_size <= 0 || cols % group_size != 0 || cols % 2 != 0) return -1;
+    const int64_t ng = cols / group_size;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t c = 0; c < cols; c += 2) {
+            const double sc = scales[r * ng + c / group_size];
+            const int64_t zp = zps[r * ng + c / group_size];
+            const int b = packed[r * (cols / 2) + c / 2];
+            dst[r * cols + c] = (float)((double)((b & 0xF) - zp) * sc);
+            dst[r * cols + c + 1] = (float)((double)(((b >> 4) & 0xF) - zp) * sc);
+        }
+    return 0;
+}
+
+/* permute_cols / inv_permute_cols, int4.tkv:169-184: out[r, c] = src[r,
+ * perm[c]] / out[r, perm[c]] = src[r, c].  -1 for an index out of range. */
+TVO_API int tvo_permute_cols(const float* src, float* out, int64_t rows, int64_t cols, const int64_t* perm,
+                             int inverse) {
+    for (int64_t c = 0; c < cols; c++)
+        if (perm[c] < 0 || perm[c] >= cols) return -1;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t c = 0; c < cols; c++) {
+            if (inverse) out[r * cols + perm[c]] = src[r * cols + c];
+            else out[r * cols + c] = src[r * cols + perm[c]];
+        }
+    return 0;
+}
+
+/* matmul_int4_grouped (int4.tkv:213-239) and, with perm, the act-order
+ * matmul_int4_grouped_ordered (:187-208): y[m, n] = fl32(sum_k a[m, perm[k]]
+ * * fl64((nib - 8) * s[n, k / gs]) + bias[n]) with a sequential f64 sum (the
+ * products are exact in f64: 24 + 28 significant bits). */
+TVO_API int tvo_matmul_int4_grouped(const float* A, const uint8_t* packed, const float* bias, int64_t n_bias,
+                                    float* Y, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                                    const float* scales, const int64_t* perm) {
+    if (group_size <= 0 || k % group_size != 0 || k % 2 != 0) return -1;
+    const int64_t ng = k / group_size;
+#pragma omp parallel for schedule(dynamic, 4)
+    for (int64_t i = 0; i < m; i++)
+        for (int64_t j = 0; j < n; j++) {
+            double acc = 0.0;
+            for (int64_t kk = 0; kk < k; kk++) {
+                const int b = packed[j * (k / 2) + kk / 2];
+                const int nib = (kk % 2 == 0) ? (b & 0xF) : ((b >> 4) & 0xF);
+                const double w = (double)(nib - 8) * (double)scales[j * ng + kk / group_size];
+                const double a = A[i * k + (perm ? perm[kk] : kk)];
+                acc = acc + a * w;
+            }
+            const double bb = n_bias > 0 ? (double)bias[j] : 0.0;
+            Y[i * n + j] = (float)(acc + bb);
+        }
+    return 0;
+}

@@ -85,6 +85,14 @@ SIGNATURES = {
     "tvq_session_forward": (i32, [i64, P, i32, P, i64, i32, P]),
     "tvq_session_logits": (i32, [i64, P, P, P]),
     "tvq_session_run_layers": (i32, [i64, P, i32, P, i32, i32, P]),
+    "tvq_dev_quantize_int4_grouped": (i32, [P, i64, i64, i64, P, P, P, P]),
+    "tvq_dev_dequantize_int4_grouped": (i32, [P, P, i64, i64, i64, P, P, P]),
+    "tvq_dev_permute_cols": (i32, [P, P, i64, i64, P, i32, P]),
+    "tvq_dev_matmul_int4_grouped": (i32, [P, P, P, P, i64, i64, i64, i64, P, P, P]),
+    "tvq_quantize_int4_grouped": (i32, [P, i64, i64, i64, P, P, P]),
+    "tvq_dequantize_int4_grouped": (i32, [P, P, i64, i64, i64, P, i64, P]),
+    "tvq_permute_cols": (i32, [P, P, i64, i64, P, i64, i32]),
+    "tvq_matmul_int4_grouped": (i32, [P, P, P, i64, P, i64, i64, i64, i64, P, i64, P]),
     "tvq_session_hidden": (i32, [i64, P]),
     "tvq_quantize_linear": (i32, [P, P, i64, i64, i64, P, i64, i64]),
     "tvq_dequantize_linear": (i32, [P, P, i64, i64, i64, P, i64, i64]),

@@ -97,6 +97,10 @@ int check_device_error(cudaStream_t st) {
     TVQ_CUDA(cudaMemcpy(&h, d->d_error, sizeof(int), cudaMemcpyDeviceToHost));
     if (h != 0) {
         TVQ_CUDA(cudaMemset(d->d_error, 0, sizeof(int)));
+        if (h == DEVERR_BAD_INDEX) {
+            set_error(TVQ_ERR_INVALID, "index out of range (a permutation entry outside [0, cols))");
+            return TVQ_ERR_INVALID;
+        }
         set_error(TVQ_ERR_TIMEOUT, "device-side wait timed out (code " + std::to_string(h) + ")");
         return TVQ_ERR_TIMEOUT;
     }
@@ -1011,6 +1015,185 @@ int tvq_dev_calibrate_mse_curve(const float* x, int64_t n, int64_t num_candidate
     TVQ_CHECK(num_candidates >= 4 && num_candidates <= 65535, TVQ_ERR_UNSUPPORTED, "4..65535 candidates");
     return launch_calibrate_mse(x, n, static_cast<int>(num_candidates), out4_dev, curve_dev, fallback,
                                 static_cast<cudaStream_t>(stream));
+}
+
+
+// ---------------------------------------------------------------- group-wise INT4 (int4.tkv)
+
+int tvq_dev_quantize_int4_grouped(const float* src, int64_t rows, int64_t cols, int64_t group_size, uint8_t* packed,
+                                  float* scales, int64_t* zps, void* stream) {
+    TVQ_CHECK(rows >= 0 && cols >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(rows * cols == 0 || (src && packed && scales), TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    return launch_int4_quantize(src, rows, cols, group_size, packed, scales, zps, static_cast<cudaStream_t>(stream));
+    TVQ_CATCH
+}
+
+int tvq_dev_dequantize_int4_grouped(const uint8_t* packed, float* dst, int64_t rows, int64_t cols, int64_t group_size,
+                                    const float* scales, const int64_t* zps, void* stream) {
+    TVQ_CHECK(rows >= 0 && cols >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(rows * cols == 0 || (packed && dst && scales), TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    return launch_int4_dequantize(packed, dst, rows, cols, group_size, scales, zps, static_cast<cudaStream_t>(stream));
+    TVQ_CATCH
+}
+
+int tvq_dev_permute_cols(const float* src, float* dst, int64_t rows, int64_t cols, const int64_t* perm, int inverse,
+                         void* stream) {
+    TVQ_CHECK(rows >= 0 && cols >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(rows * cols == 0 || (src && dst && perm), TVQ_ERR_INVALID, "null buffer");
+    TVQ_CHECK(src != dst, TVQ_ERR_INVALID, "permute_cols cannot run in place");
+    TVQ_TRY
+    return launch_permute_cols(src, dst, rows, cols, perm, inverse, static_cast<cudaStream_t>(stream));
+    TVQ_CATCH
+}
+
+int tvq_dev_matmul_int4_grouped(const float* A, const uint8_t* packed_w, const float* bias, float* Y, int64_t m,
+                                int64_t n, int64_t k, int64_t group_size, const float* scales_w, const int64_t* perm,
+                                void* stream) {
+    TVQ_CHECK(m >= 0 && n >= 0 && k >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(group_size > 0 && k % group_size == 0 && k % 2 == 0, TVQ_ERR_SIZE,
+              "k must be an even multiple of group_size");
+    if (m == 0 || n == 0) return TVQ_OK;
+    TVQ_CHECK(Y && (k == 0 || (A && packed_w && scales_w)), TVQ_ERR_INVALID, "null buffer");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    TVQ_TRY
+    GemmArgs g;
+    g.kind = GEMM_W4;
+    g.bias = bias;
+    g.Y = Y;
+    g.m = m;
+    g.n = n;
+    g.k = k;
+    g.group_size = group_size;
+    g.scales_w = scales_w;
+    if (k == 0) {
+        g.scale_a = scales_w;  // unread
+        return launch_gemm(g, st);
+    }
+    // scratch (stream-ordered): A hi / lo fp16 [m, k], its row scales, W as fp16 integers [n, k]
+    const size_t ak = (static_cast<size_t>(m) * k * 2 + 15) & ~size_t(15);
+    const size_t wk = (static_cast<size_t>(n) * k * 2 + 15) & ~size_t(15);
+    uint8_t* buf = nullptr;
+    TVQ_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&buf), 2 * ak + wk + sizeof(float) * m, st));
+    float* ra = reinterpret_cast<float*>(buf + 2 * ak + wk);
+    int r = launch_split_f16_rows(A, buf, buf + ak, ra, m, k, st, perm);
+    if (!r) r = launch_int4_unpack_f16(packed_w, buf + 2 * ak, n, k, st);
+    if (!r) {
+        g.A = buf;
+        g.A2 = buf + ak;
+        g.W = buf + 2 * ak;
+        g.scale_a = ra;
+        r = launch_gemm(g, st);
+    }
+    cudaError_t e = cudaFreeAsync(buf, st);
+    if (!r && e != cudaSuccess) return cuda_fail(e, "cudaFreeAsync");
+    return r;
+    TVQ_CATCH
+}
+
+// host-buffer forms (synchronous), the reference's signatures
+int tvq_quantize_int4_grouped(const float* src, int64_t rows, int64_t cols, int64_t group_size, uint8_t* packed_out,
+                              float* scales_out, int64_t* zps_out) {
+    TVQ_CHECK(rows >= 0 && cols >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(group_size > 0 && cols % group_size == 0 && cols % 2 == 0, TVQ_ERR_SIZE,
+              "cols must be a multiple of group_size and even");
+    if (rows * cols == 0) return TVQ_OK;
+    TVQ_CHECK(src && packed_out && scales_out, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    const int64_t ng = cols / group_size;
+    float* ds = dev<float>(H, 0, static_cast<size_t>(rows * cols));
+    uint8_t* dp = dev<uint8_t>(H, 1, static_cast<size_t>(rows * cols / 2));
+    float* dsc = dev<float>(H, 2, static_cast<size_t>(rows * ng));
+    int64_t* dz = zps_out ? dev<int64_t>(H, 3, static_cast<size_t>(rows * ng)) : nullptr;
+    if (H.rc) return H.rc;
+    TVQ_CUDA(cudaMemcpyAsync(ds, src, sizeof(float) * rows * cols, cudaMemcpyHostToDevice, H.st()));
+    STEP(launch_int4_quantize(ds, rows, cols, group_size, dp, dsc, dz, H.st()));
+    TVQ_CUDA(cudaMemcpyAsync(packed_out, dp, static_cast<size_t>(rows * cols / 2), cudaMemcpyDeviceToHost, H.st()));
+    TVQ_CUDA(cudaMemcpyAsync(scales_out, dsc, sizeof(float) * rows * ng, cudaMemcpyDeviceToHost, H.st()));
+    if (dz) TVQ_CUDA(cudaMemcpyAsync(zps_out, dz, sizeof(int64_t) * rows * ng, cudaMemcpyDeviceToHost, H.st()));
+    return check_device_error(H.st());
+    TVQ_CATCH
+}
+
+int tvq_dequantize_int4_grouped(const uint8_t* packed, float* dst, int64_t rows, int64_t cols, int64_t group_size,
+                                const float* scales, int64_t n_scales, const int64_t* zps) {
+    TVQ_CHECK(rows >= 0 && cols >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(group_size > 0 && cols % group_size == 0 && cols % 2 == 0, TVQ_ERR_SIZE,
+              "cols must be a multiple of group_size and even");
+    TVQ_CHECK(n_scales >= rows * (cols / group_size), TVQ_ERR_SIZE, "scales smaller than rows*num_groups");  // :53-54
+    if (rows * cols == 0) return TVQ_OK;
+    TVQ_CHECK(packed && dst && scales, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    const int64_t ng = cols / group_size;
+    uint8_t* dp = dev<uint8_t>(H, 0, static_cast<size_t>(rows * cols / 2));
+    float* dd = dev<float>(H, 1, static_cast<size_t>(rows * cols));
+    float* dsc = dev<float>(H, 2, static_cast<size_t>(rows * ng));
+    int64_t* dz = zps ? dev<int64_t>(H, 3, static_cast<size_t>(rows * ng)) : nullptr;
+    if (H.rc) return H.rc;
+    TVQ_CUDA(cudaMemcpyAsync(dp, packed, static_cast<size_t>(rows * cols / 2), cudaMemcpyHostToDevice, H.st()));
+    TVQ_CUDA(cudaMemcpyAsync(dsc, scales, sizeof(float) * rows * ng, cudaMemcpyHostToDevice, H.st()));
+    if (dz) TVQ_CUDA(cudaMemcpyAsync(dz, zps, sizeof(int64_t) * rows * ng, cudaMemcpyHostToDevice, H.st()));
+    STEP(launch_int4_dequantize(dp, dd, rows, cols, group_size, dsc, dz, H.st()));
+    TVQ_CUDA(cudaMemcpyAsync(dst, dd, sizeof(float) * rows * cols, cudaMemcpyDeviceToHost, H.st()));
+    return check_device_error(H.st());
+    TVQ_CATCH
+}
+
+int tvq_permute_cols(const float* src, float* dst, int64_t rows, int64_t cols, const int64_t* perm, int64_t n_perm,
+                     int inverse) {
+    TVQ_CHECK(rows >= 0 && cols >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(n_perm == cols, TVQ_ERR_SIZE, "perm length must equal cols");  // int4.tkv:170-171
+    if (rows * cols == 0) return TVQ_OK;
+    TVQ_CHECK(src && dst && perm, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    float* ds = dev<float>(H, 0, static_cast<size_t>(rows * cols));
+    float* dd = dev<float>(H, 1, static_cast<size_t>(rows * cols));
+    int64_t* dpm = dev<int64_t>(H, 2, static_cast<size_t>(cols));
+    if (H.rc) return H.rc;
+    TVQ_CUDA(cudaMemcpyAsync(ds, src, sizeof(float) * rows * cols, cudaMemcpyHostToDevice, H.st()));
+    TVQ_CUDA(cudaMemcpyAsync(dpm, perm, sizeof(int64_t) * cols, cudaMemcpyHostToDevice, H.st()));
+    if (inverse) TVQ_CUDA(cudaMemsetAsync(dd, 0, sizeof(float) * rows * cols, H.st()));
+    STEP(launch_permute_cols(ds, dd, rows, cols, dpm, inverse, H.st()));
+    TVQ_CUDA(cudaMemcpyAsync(dst, dd, sizeof(float) * rows * cols, cudaMemcpyDeviceToHost, H.st()));
+    return check_device_error(H.st());
+    TVQ_CATCH
+}
+
+int tvq_matmul_int4_grouped(const float* A, const uint8_t* packed_w, const float* bias, int64_t n_bias, float* Y,
+                            int64_t m, int64_t n, int64_t k, int64_t group_size, const float* scales_w,
+                            int64_t n_scales, const int64_t* perm) {
+    TVQ_CHECK(m >= 0 && n >= 0 && k >= 0 && n_bias >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(group_size > 0 && k % group_size == 0 && k % 2 == 0, TVQ_ERR_SIZE,
+              "k must be an even multiple of group_size");
+    TVQ_CHECK(n_scales >= n * (k / group_size), TVQ_ERR_SIZE, "scales_w smaller than N*num_groups");  // int4.tkv:215-216
+    TVQ_CHECK(n_bias == 0 || n_bias >= n, TVQ_ERR_SIZE, "bias smaller than N");
+    if (m == 0 || n == 0) return TVQ_OK;
+    TVQ_CHECK(Y && (k == 0 || (A && packed_w && scales_w)) && (n_bias == 0 || bias), TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    const int64_t ng = k / group_size;
+    float* dA = dev<float>(H, 0, static_cast<size_t>(std::max<int64_t>(m * k, 1)));
+    uint8_t* dW = dev<uint8_t>(H, 1, static_cast<size_t>(std::max<int64_t>(n * k / 2, 1)));
+    float* dS = dev<float>(H, 2, static_cast<size_t>(std::max<int64_t>(n * ng, 1)));
+    float* dB = n_bias ? dev<float>(H, 3, static_cast<size_t>(n)) : nullptr;
+    float* dY = dev<float>(H, 4, static_cast<size_t>(m * n));
+    int64_t* dP = perm ? dev<int64_t>(H, 5, static_cast<size_t>(std::max<int64_t>(k, 1))) : nullptr;
+    if (H.rc) return H.rc;
+    if (k) {
+        TVQ_CUDA(cudaMemcpyAsync(dA, A, sizeof(float) * m * k, cudaMemcpyHostToDevice, H.st()));
+        TVQ_CUDA(cudaMemcpyAsync(dW, packed_w, static_cast<size_t>(n * k / 2), cudaMemcpyHostToDevice, H.st()));
+        TVQ_CUDA(cudaMemcpyAsync(dS, scales_w, sizeof(float) * n * ng, cudaMemcpyHostToDevice, H.st()));
+        if (dP) TVQ_CUDA(cudaMemcpyAsync(dP, perm, sizeof(int64_t) * k, cudaMemcpyHostToDevice, H.st()));
+    }
+    if (dB) TVQ_CUDA(cudaMemcpyAsync(dB, bias, sizeof(float) * n, cudaMemcpyHostToDevice, H.st()));
+    STEP(tvq_dev_matmul_int4_grouped(dA, dW, dB, dY, m, n, k, group_size, dS, dP, H.st()));
+    TVQ_CUDA(cudaMemcpyAsync(Y, dY, sizeof(float) * m * n, cudaMemcpyDeviceToHost, H.st()));
+    return check_device_error(H.st());
+    TVQ_CATCH
 }
 
 }  // extern "C"

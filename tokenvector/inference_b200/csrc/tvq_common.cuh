@@ -51,6 +51,7 @@ enum : int {
     DEVERR_TIMEOUT_EPILOGUE = 3,
     DEVERR_TIMEOUT_DRAIN = 4,
     DEVERR_TIMEOUT_TEST = 9,
+    DEVERR_BAD_INDEX = 60,  // an index operand out of range (not a timeout)
 };
 
 // ---------------------------------------------------------------- device side

@@ -59,8 +59,10 @@ struct Epi {
 };
 // the split-precision fp32 GEMMs: hi / lo operand parts, three products
 __host__ __device__ constexpr bool split_kind(int kind) { return kind == GEMM_TF32X3 || kind == GEMM_F16X3; }
+// kinds whose partial sums are promoted to registers in short K runs
+__host__ __device__ constexpr bool promoted_kind(int kind) { return split_kind(kind) || kind == GEMM_W4; }
 template <int KIND>
-using EpiOf = Epi<split_kind(KIND) ? 8 : 16>;
+using EpiOf = Epi<promoted_kind(KIND) ? 8 : 16>;
 // GEMM_TF32X3 sums its products in TMEM over this many k-blocks (32 f32
 // each) only; the epilogue adds the partial sums in registers with IEEE
 // round-to-nearest.  The tensor core's own f32 accumulation is less exact
@@ -73,6 +75,8 @@ struct KParams {
     int m, n, k;
     int num_m_blocks, num_n_blocks, num_k_blocks;
     int promote_kb;  // k-blocks per TMEM accumulation unit (split kinds)
+    int group_ks;    // GEMM_W4: k-steps (16 elements) per weight group = per accumulation unit
+    int ngroups;     // GEMM_W4: k / group_size
     int acc_only;    // only the raw int32 accumulators (acc_out) are written
     const float* bias;
     const float* residual;
@@ -288,25 +292,28 @@ __device__ __forceinline__ constexpr uint32_t make_idesc() {
     // format, [15]/[16] A/B major (0 = K), [17,23) N>>3, [24,29) M>>4
     return (KIND == GEMM_I8   ? (2u << 4) | (1u << 7) | (1u << 10)    // S32 <- s8 x s8
             : KIND == GEMM_F8 ? (1u << 4) | (0u << 7) | (0u << 10)    // F32 <- e4m3 x e4m3
-            : KIND == GEMM_F16X3 ? (1u << 4) | (0u << 7) | (0u << 10) // F32 <- f16 x f16 (kind::f16)
+            : (KIND == GEMM_F16X3 || KIND == GEMM_W4) ? (1u << 4) | (0u << 7) | (0u << 10) // F32 <- f16 x f16 (kind::f16)
                               : (1u << 4) | (2u << 7) | (2u << 10))   // F32 <- tf32 x tf32
            | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
 }
 
-// NS operand parts per stage: 1, or 2 (high + low) for the split GEMMs.
+// NSA / NSB operand parts per stage: 1, or 2 (high + low) for the split
+// GEMMs; GEMM_W4 splits A only.
 template <int KIND, int BN>
 struct Cfg {
-    static constexpr int NS = split_kind(KIND) ? 2 : 1;
-    static constexpr int ELEM = (KIND == GEMM_TF32X3) ? 4 : (KIND == GEMM_F16X3) ? 2 : 1;  // bytes per element
+    static constexpr int NSA = (split_kind(KIND) || KIND == GEMM_W4) ? 2 : 1;
+    static constexpr int NSB = split_kind(KIND) ? 2 : 1;
+    static constexpr int ELEM = (KIND == GEMM_TF32X3) ? 4 : (KIND == GEMM_F16X3 || KIND == GEMM_W4) ? 2 : 1;
     static constexpr int BKE = BK / ELEM;                         // K elements per stage
     static constexpr uint32_t A_BYTES = BM * BK;                  // one part
     static constexpr uint32_t B_BYTES = BN * BK;
-    static constexpr int STAGES = (NS * (BM + BN) * BK * 8 <= 196608) ? 8 : 196608 / (NS * (BM + BN) * BK);
+    static constexpr uint32_t STAGE_BYTES = NSA * A_BYTES + NSB * B_BYTES;
+    static constexpr int STAGES = (STAGE_BYTES * 8 <= 196608) ? 8 : 196608 / STAGE_BYTES;
     // TMEM accumulator buffers: 2 (tile i+1's MMAs overlap tile i's
     // epilogue), 4 for the short promotion units of the split kinds
-    static constexpr int NACC = split_kind(KIND) ? 4 : 2;
+    static constexpr int NACC = promoted_kind(KIND) ? 4 : 2;
     static constexpr uint32_t TMEM_COLS = NACC * BN;  // 128/256/512: powers of two
-    static constexpr uint32_t RING = STAGES * NS * (A_BYTES + B_BYTES);
+    static constexpr uint32_t RING = STAGES * STAGE_BYTES;
     static constexpr uint32_t EPI = EpiOf<KIND>::EPI_WARPS * 32 * EpiOf<KIND>::CH * 4;  // per-warp 32 x CH f32 staging
     static constexpr uint32_t COLS = 2 * 2 * BN * 4;  // per-column scale and bias of a tile, double-buffered
     static constexpr uint32_t SMEM = RING + EPI + COLS + 1024 /*align*/ + 512 /*barriers*/;
@@ -319,11 +326,11 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
     using C = Cfg<KIND, BN>;
     using E = EpiOf<KIND>;
     constexpr int STAGES = C::STAGES;
-    constexpr int NS = C::NS;
+    constexpr int NSA = C::NSA, NSB = C::NSB;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sA = smem;                                // stage s: NS parts of A_BYTES
-    uint8_t* sB = smem + STAGES * NS * C::A_BYTES;     // stage s: NS parts of B_BYTES
+    uint8_t* sA = smem;                                // stage s: NSA parts of A_BYTES
+    uint8_t* sB = smem + STAGES * NSA * C::A_BYTES;    // stage s: NSB parts of B_BYTES
     float* colv = reinterpret_cast<float*>(smem + C::RING + C::EPI);  // [2 buffers][scale BN | bias BN]
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING + C::EPI + C::COLS);
     uint64_t* empty = full + STAGES;
@@ -350,10 +357,8 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
-        if (NS == 2) {
-            tma_prefetch_desc(&tmA2);
-            tma_prefetch_desc(&tmB2);
-        }
+        if (NSA == 2) tma_prefetch_desc(&tmA2);
+        if (NSB == 2) tma_prefetch_desc(&tmB2);
     }
     if (warp == 2) {
         tmem_alloc(tmem_holder, C::TMEM_COLS);
@@ -379,13 +384,11 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                     const uint32_t s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1u;
                     if (!mbar_wait(&empty[s], ph ^ 1u, p.err, DEVERR_TIMEOUT_PRODUCER)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&full[s], NS * (C::A_BYTES + C::B_BYTES));
-                    tma_load_2d(&tmA, &full[s], sA + s * NS * C::A_BYTES, kb * C::BKE, mb * BM);
-                    tma_load_2d(&tmB, &full[s], sB + s * NS * C::B_BYTES, kb * C::BKE, nb * BN);
-                    if (NS == 2) {
-                        tma_load_2d(&tmA2, &full[s], sA + (s * NS + 1) * C::A_BYTES, kb * C::BKE, mb * BM);
-                        tma_load_2d(&tmB2, &full[s], sB + (s * NS + 1) * C::B_BYTES, kb * C::BKE, nb * BN);
-                    }
+                    mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+                    tma_load_2d(&tmA, &full[s], sA + s * NSA * C::A_BYTES, kb * C::BKE, mb * BM);
+                    tma_load_2d(&tmB, &full[s], sB + s * NSB * C::B_BYTES, kb * C::BKE, nb * BN);
+                    if (NSA == 2) tma_load_2d(&tmA2, &full[s], sA + (s * NSA + 1) * C::A_BYTES, kb * C::BKE, mb * BM);
+                    if (NSB == 2) tma_load_2d(&tmB2, &full[s], sB + (s * NSB + 1) * C::B_BYTES, kb * C::BKE, nb * BN);
                 }
             }
             // every issued load lands before the CTA may exit
@@ -402,6 +405,48 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
             const int pk = split_kind(KIND) ? p.promote_kb : p.num_k_blocks;
             uint32_t it = 0, ucount = 0;
             bool ok = true;
+            if constexpr (KIND == GEMM_W4) {
+                // one accumulation unit per weight group (group_ks k-steps of
+                // 16, inside one stage or across several): acc = sum a_lo q +
+                // a_hi q; a stage is released after its last k-step
+                constexpr int KS = BK / UMMA_K;  // k-steps per stage (4)
+                const int nks = p.ngroups * p.group_ks;
+                for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                    uint32_t a0 = 0, b0 = 0, s = 0;
+                    for (int g = 0; g < p.ngroups && ok; g++, ucount++) {
+                        const uint32_t b = ucount % C::NACC;
+                        const uint32_t aph = (ucount / C::NACC) & 1u;
+                        if (!mbar_wait(&tempty[b], aph ^ 1u, p.err, DEVERR_TIMEOUT_MMA)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t d_tmem = tmem_base + b * BN;
+                        for (int ks = g * p.group_ks; ks < (g + 1) * p.group_ks; ks++) {
+                            const int kk = ks % KS;
+                            if (kk == 0) {  // a new stage
+                                s = it % STAGES;
+                                const uint32_t ph = (it / STAGES) & 1u;
+                                if (!mbar_wait(&full[s], ph, p.err, DEVERR_TIMEOUT_MMA)) { ok = false; break; }
+                                tc_fence_after();
+                                a0 = smem_u32(sA + s * NSA * C::A_BYTES);
+                                b0 = smem_u32(sB + s * NSB * C::B_BYTES);
+                            }
+                            const uint64_t ad = smem_desc_k_sw128(a0 + kk * UMMA_K);
+                            const uint64_t adl = smem_desc_k_sw128(a0 + C::A_BYTES + kk * UMMA_K);
+                            const uint64_t bd = smem_desc_k_sw128(b0 + kk * UMMA_K);
+                            umma_f16(d_tmem, adl, bd, idesc, ks > g * p.group_ks ? 1u : 0u);
+                            umma_f16(d_tmem, ad, bd, idesc, 1u);
+                            if (kk == KS - 1 || ks == nks - 1) {
+                                umma_commit(&empty[s]);  // stage s is free once these MMAs retire
+                                it++;
+                            }
+                        }
+                        if (!ok) break;
+                        umma_commit(&tfull[b]);  // accumulator b holds the group's sum
+                    }
+                    // stages loaded past the last k-step (a partial last block
+                    // is covered above): none, the producer loads exactly the
+                    // k-blocks that hold the nks k-steps
+                }
+            } else
             for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x)
             for (int kb0 = 0; kb0 < p.num_k_blocks && ok; kb0 += pk, ucount++) {
                 const uint32_t b = ucount % C::NACC;
@@ -415,8 +460,8 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                     const uint32_t ph = (it / STAGES) & 1u;
                     if (!mbar_wait(&full[s], ph, p.err, DEVERR_TIMEOUT_MMA)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(sA + s * NS * C::A_BYTES);
-                    const uint32_t b0 = smem_u32(sB + s * NS * C::B_BYTES);
+                    const uint32_t a0 = smem_u32(sA + s * NSA * C::A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + s * NSB * C::B_BYTES);
 #pragma unroll
                     for (int kk = 0; kk < BK / UMMA_K; kk++) {  // 32 bytes of K per instruction
                         const uint64_t ad = smem_desc_k_sw128(a0 + kk * UMMA_K);
@@ -462,24 +507,26 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
         float* stage = reinterpret_cast<float*>(smem + C::RING) + (warp - 4) * (32 * E::CH);
         const bool bias_on = p.bias != nullptr;
         const bool per_channel = p.per_channel != 0;
-        const float sa = (split_kind(KIND) || p.acc_only) ? 1.0f : __ldg(p.scale_a);
-        const float sw0 = (split_kind(KIND) || p.acc_only) ? 1.0f : __ldg(p.scales_w);
+        const float sa = (promoted_kind(KIND) || p.acc_only) ? 1.0f : __ldg(p.scale_a);
+        const float sw0 = (promoted_kind(KIND) || p.acc_only) ? 1.0f : __ldg(p.scales_w);
         InvScale qs{0.0, 0.0f, 0.0f};
         if (p.Yq) qs = make_inv_scale(static_cast<double>(__ldg(p.scale_out)));
         EpiCtx ec{(p.n & 3) == 0, qs, sa};
         float amax = 0.0f;
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(eg * 32) << 16);
-        if constexpr (split_kind(KIND)) {
-            // partial sums of promote_kb k-blocks each, added in registers
+        if constexpr (promoted_kind(KIND)) {
+            // partial sums of promote_kb k-blocks each (GEMM_W4: of one weight
+            // group each, times the group's scale), added in registers
             constexpr int NCH = BN / E::CH / E::EPW;  // chunks this warp owns: half, half + E::EPW, ...
             uint32_t ucount = 0;
             bool alive = true;
+            const int nunits = (KIND == GEMM_W4) ? p.ngroups : (p.num_k_blocks + p.promote_kb - 1) / p.promote_kb;
             for (int tile = blockIdx.x; tile < num_tiles && alive; tile += gridDim.x) {
                 const int mb = tile % p.num_m_blocks;
                 const int nb = tile / p.num_m_blocks;
                 const int row0 = mb * BM + eg * 32;
                 float acc[NCH][E::CH];
-                for (int kb0 = 0; kb0 < p.num_k_blocks; kb0 += p.promote_kb, ucount++) {
+                for (int u = 0; u < nunits; u++, ucount++) {
                     const uint32_t b = ucount % C::NACC;
                     const uint32_t aph = (ucount / C::NACC) & 1u;
                     const bool got = mbar_wait(&tfull[b], aph, p.err, DEVERR_TIMEOUT_EPILOGUE);
@@ -493,7 +540,20 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[b]);
-                    if (kb0 == 0) {
+                    if constexpr (KIND == GEMM_W4) {
+                        // the group's scales of this warp's columns (same in every lane)
+#pragma unroll
+                        for (int i = 0; i < NCH; i++) {
+                            const int n0 = nb * BN + (half + E::EPW * i) * E::CH;
+#pragma unroll
+                            for (int j = 0; j < E::CH; j++) {
+                                const int n = min(n0 + j, p.n - 1);
+                                const float sc = __ldg(p.scales_w + static_cast<int64_t>(n) * p.ngroups + u);
+                                acc[i][j] = u == 0 ? __fmul_rn(__uint_as_float(r[i][j]), sc)
+                                                   : fmaf(__uint_as_float(r[i][j]), sc, acc[i][j]);
+                            }
+                        }
+                    } else if (u == 0) {
 #pragma unroll
                         for (int i = 0; i < NCH; i++)
 #pragma unroll
@@ -506,6 +566,20 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                     }
                 }
                 if (!alive) break;
+                if constexpr (KIND == GEMM_W4) {
+                    // undo the rows' power-of-two scale of A (exact), then the bias
+                    const int row = row0 + lane;
+                    const float ra = (row < p.m) ? __ldg(p.scale_a + row) : 0.0f;
+#pragma unroll
+                    for (int i = 0; i < NCH; i++) {
+                        const int n0 = nb * BN + (half + E::EPW * i) * E::CH;
+#pragma unroll
+                        for (int j = 0; j < E::CH; j++) {
+                            const int n = min(n0 + j, p.n - 1);
+                            acc[i][j] = __fadd_rn(acc[i][j] * ra, bias_on ? __ldg(p.bias + n) : 0.0f);
+                        }
+                    }
+                }
                 if constexpr (KIND == GEMM_F16X3) {
                     // undo the rows' power-of-two scales (exact)
                     const int row = row0 + lane;
@@ -700,6 +774,14 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
     }
 }
 
+// Y[m, n] = bias[n] (or 0): an INT4 GEMM with k = 0 (int4.tkv:232-238 with
+// acc = 0).
+__global__ void bias_rows_kernel(float* __restrict__ Y, const float* __restrict__ bias, int64_t m, int64_t n) {
+    griddep_wait();
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < m * n; i += (int64_t)gridDim.x * blockDim.x)
+        Y[i] = bias ? bias[i % n] : 0.0f;
+}
+
 // K == 0: every accumulator is 0, only the epilogue remains (matmul.tkv:14/28
 // with acc = 0).
 __global__ void gemm_k0_kernel(KParams p) {
@@ -785,13 +867,11 @@ int launch_tc(const KParams& p, const GemmArgs& g, int grid, cudaStream_t st) {
     CUtensorMap ma, mb, ma2, mb2;
     int rc = make_map(&ma, g.A, p.m, p.k, BM, C::ELEM);
     if (!rc) rc = make_map(&mb, g.W, p.n, p.k, BN, C::ELEM);
-    if (!rc && C::NS == 2) rc = make_map(&ma2, g.A2, p.m, p.k, BM, C::ELEM);
-    if (!rc && C::NS == 2) rc = make_map(&mb2, g.W2, p.n, p.k, BN, C::ELEM);
+    if (!rc && C::NSA == 2) rc = make_map(&ma2, g.A2, p.m, p.k, BM, C::ELEM);
+    if (!rc && C::NSB == 2) rc = make_map(&mb2, g.W2, p.n, p.k, BN, C::ELEM);
     if (rc) return rc;
-    if (C::NS == 1) {
-        ma2 = ma;
-        mb2 = mb;
-    }
+    if (C::NSA == 1) ma2 = ma;
+    if (C::NSB == 1) mb2 = mb;
     return launch_pdl(gemm_tc_kernel<KIND, BN>, dim3(grid), dim3(EpiOf<KIND>::THREADS), C::SMEM, st, ma, mb, ma2, mb2, p);
 }
 
@@ -827,16 +907,27 @@ __global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict
 // max|x| below 2^-111 keep fewer bits); a row holding Inf or NaN gets s = 1
 // and carries it into its products.
 __global__ void split_f16_rows_kernel(const float* __restrict__ x, __half* __restrict__ hi, __half* __restrict__ lo,
-                                      float* __restrict__ rscale, int64_t rows, int64_t k) {
+                                      float* __restrict__ rscale, int64_t rows, int64_t k,
+                                      const int64_t* __restrict__ perm, int* err) {
     griddep_wait();
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
         const float* xr = x + r * k;
         float m = 0.0f;
-        for (int64_t j = lane; j < k; j += 32) m = fmaxf(m, fabsf(xr[j]));  // fmaxf drops NaN: checked below
+        // element j of the row is x[r, perm[j]] with an act-order permutation
+        auto at = [&](int64_t j) -> float {
+            if (!perm) return xr[j];
+            const int64_t pj = __ldg(perm + j);
+            if (pj < 0 || pj >= k) {
+                record_error(err, DEVERR_BAD_INDEX);
+                return 0.0f;
+            }
+            return xr[pj];
+        };
+        for (int64_t j = lane; j < k; j += 32) m = fmaxf(m, fabsf(at(j)));  // fmaxf drops NaN: checked below
         bool bad = false;
-        for (int64_t j = lane; j < k; j += 32) bad |= !isfinite(xr[j]);
+        for (int64_t j = lane; j < k; j += 32) bad |= !isfinite(at(j));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         bad = __any_sync(0xffffffffu, bad);
@@ -848,7 +939,7 @@ __global__ void split_f16_rows_kernel(const float* __restrict__ x, __half* __res
         }
         if (lane == 0) rscale[r] = exp2i(-sh);
         for (int64_t j = lane; j < k; j += 32) {
-            const float v = xr[j] * exp2i(sh);
+            const float v = at(j) * exp2i(sh);
             const __half h = __float2half_rn(v);
             hi[r * k + j] = h;
             lo[r * k + j] = __float2half_rn(v - __half2float(h));
@@ -859,14 +950,14 @@ __global__ void split_f16_rows_kernel(const float* __restrict__ x, __half* __res
 }  // namespace
 
 int launch_split_f16_rows(const float* x, void* hi, void* lo, float* rscale, int64_t rows, int64_t k,
-                          cudaStream_t st) {
+                          cudaStream_t st, const int64_t* perm) {
     if (rows <= 0) return TVQ_OK;
     int rc = 0;
     DeviceState* ds = device_state(&rc);
     if (!ds) return rc;
     const int grid = static_cast<int>(std::min<int64_t>((rows + 7) / 8, ds->sm_count * 8));
     return launch_pdl(split_f16_rows_kernel, dim3(grid), dim3(256), 0, st, x, static_cast<__half*>(hi),
-                      static_cast<__half*>(lo), rscale, rows, k);
+                      static_cast<__half*>(lo), rscale, rows, k, perm, ds->d_error);
 }
 
 int make_tma_f32_sw128(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int box_rows, int64_t pitch) {
@@ -893,10 +984,15 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
               "GEMM size out of range (k must stay below 133143 for exact int32 accumulation)");
     if (g.m == 0 || g.n == 0) return TVQ_OK;
     const bool acc_only = g.kind == GEMM_I8 && g.acc_out && !g.Y && !g.Yq && !g.amax;
-    TVQ_CHECK(g.kind >= GEMM_I8 && g.kind <= GEMM_F16X3, TVQ_ERR_INVALID, "unknown GEMM kind");
+    TVQ_CHECK(g.kind >= GEMM_I8 && g.kind <= GEMM_W4, TVQ_ERR_INVALID, "unknown GEMM kind");
     const bool split = split_kind(g.kind);
+    const bool w4 = g.kind == GEMM_W4;
     TVQ_CHECK(g.kind == GEMM_TF32X3 || acc_only || (g.scale_a && g.scales_w), TVQ_ERR_INVALID,
               "scale pointers are required");
+    TVQ_CHECK(!w4 || (g.group_size > 0 && g.group_size % 16 == 0 && g.k % g.group_size == 0), TVQ_ERR_UNSUPPORTED,
+              "the INT4 GEMM needs k a multiple of group_size, group_size a multiple of 16");
+    TVQ_CHECK(!w4 || (!g.Yq && !g.residual && g.act == 0 && g.Y && !g.amax), TVQ_ERR_INVALID,
+              "the INT4 GEMM writes f32 Y (+ bias) only");
     TVQ_CHECK(!split || (!g.Yq && !g.bias && !g.residual && g.act == 0 && g.Y && !g.amax), TVQ_ERR_INVALID,
               "the split fp32 GEMM writes plain f32 Y only");
     TVQ_CHECK(!g.Yq || g.scale_out, TVQ_ERR_INVALID, "int8 output needs scale_out");
@@ -916,7 +1012,9 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.acc_out = g.acc_out;
     p.scale_a = g.scale_a;
     p.scales_w = g.scales_w;
-    p.per_channel = (acc_only || split) ? 0 : g.per_channel;
+    p.per_channel = (acc_only || split || w4) ? 0 : g.per_channel;
+    p.group_ks = w4 ? static_cast<int>(g.group_size / 16) : 0;
+    p.ngroups = w4 ? static_cast<int>(g.k / g.group_size) : 0;
     p.qh = static_cast<__half*>(g.qh);
     p.ql = static_cast<__half*>(g.ql);
     p.kh = static_cast<__half*>(g.kh);
@@ -933,7 +1031,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.amax = g.amax;
     p.err = ds->d_error;
     p.num_m_blocks = static_cast<int>((g.m + BM - 1) / BM);
-    const int elem = (g.kind == GEMM_TF32X3) ? 4 : (g.kind == GEMM_F16X3) ? 2 : 1;
+    const int elem = (g.kind == GEMM_TF32X3) ? 4 : (g.kind == GEMM_F16X3 || w4) ? 2 : 1;
     p.num_k_blocks = static_cast<int>((g.k * elem + BK - 1) / BK);
     p.promote_kb = TF32_PROMOTE_KB;
     if (const char* env = getenv("TVQ_TF32_PROMOTE_KB")) p.promote_kb = std::max(1, atoi(env));
@@ -941,6 +1039,10 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     if (g.k == 0 && split) {
         TVQ_CUDA(cudaMemsetAsync(g.Y, 0, sizeof(float) * g.m * g.n, st));
         return TVQ_OK;
+    }
+    if (g.k == 0 && w4) {
+        const int grid = static_cast<int>(std::min<int64_t>((g.m * g.n + 255) / 256, ds->sm_count * 8));
+        return launch_pdl(bias_rows_kernel, dim3(grid), dim3(256), 0, st, g.Y, g.bias, g.m, g.n);
     }
     if (g.k == 0) {
         const int64_t total = g.m * g.n;
@@ -953,6 +1055,8 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     TVQ_CHECK(!split ||
                   (g.A2 && g.W2 && ((reinterpret_cast<uintptr_t>(g.A2) | reinterpret_cast<uintptr_t>(g.W2)) & 15) == 0),
               TVQ_ERR_UNSUPPORTED, "the split GEMM needs 16-byte aligned low parts");
+    TVQ_CHECK(!w4 || (g.A2 && (reinterpret_cast<uintptr_t>(g.A2) & 15) == 0), TVQ_ERR_UNSUPPORTED,
+              "the INT4 GEMM needs a 16-byte aligned low part of A");
     TVQ_CHECK(!g.Y || (reinterpret_cast<uintptr_t>(g.Y) & 15) == 0, TVQ_ERR_UNSUPPORTED, "Y must be 16-byte aligned");
     TVQ_CHECK(!g.residual || (reinterpret_cast<uintptr_t>(g.residual) & 15) == 0, TVQ_ERR_UNSUPPORTED,
               "residual must be 16-byte aligned");
@@ -974,8 +1078,8 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
         }();
         bn = env_bn;
     }
-    if (split && bn > 128) bn = 128;  // their partial sums live in registers
-    if (bn == 0 && split) {
+    if ((split || w4) && bn > 128) bn = 128;  // their partial sums live in registers
+    if (bn == 0 && (split || w4)) {
         // The split forms keep 128 (their N = 64 MMAs run well below the
         // tensor rate) unless that leaves SMs without a tile.
         bn = (static_cast<int64_t>(p.num_m_blocks) * ((g.n + 127) / 128) >= ds->sm_count) ? 128 : 64;
@@ -1017,6 +1121,10 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     if (g.kind == GEMM_F16X3) {
         if (bn >= 128) return launch_tc<GEMM_F16X3, 128>(p, g, grid, st);
         return launch_tc<GEMM_F16X3, 64>(p, g, grid, st);
+    }
+    if (w4) {
+        if (bn >= 128) return launch_tc<GEMM_W4, 128>(p, g, grid, st);
+        return launch_tc<GEMM_W4, 64>(p, g, grid, st);
     }
     if (bn >= 128) return launch_tc<GEMM_TF32X3, 128>(p, g, grid, st);
     return launch_tc<GEMM_TF32X3, 64>(p, g, grid, st);

@@ -32,7 +32,11 @@ float e4m3_decode_host(uint32_t v);
 uint8_t e4m3_encode_host(float x);
 
 // tvq_gemm.cu
-enum GemmKind { GEMM_I8 = 0, GEMM_F8 = 1, GEMM_TF32X3 = 2, GEMM_F16X3 = 3 };
+// GEMM_W4: fp32 activations (fp16 hi / lo under row scales, A / A2,
+// scale_a [m]) times group-wise INT4 weights given as their integer values
+// nib - 8 in fp16 (W [n, k]), scales_w [n, k / group_size]; Y = sum over
+// groups of scale * partial, then * scale_a[m] + bias[n].
+enum GemmKind { GEMM_I8 = 0, GEMM_F8 = 1, GEMM_TF32X3 = 2, GEMM_F16X3 = 3, GEMM_W4 = 4 };
 
 struct GemmArgs {
     int kind = GEMM_I8;
@@ -56,6 +60,7 @@ struct GemmArgs {
     const float* scale_out = nullptr; // device [1], needed with Yq
     uint32_t* amax = nullptr;         // device [1] or null
     int force_bn = 0;                 // 0 = heuristic, else 64/128/256
+    int group_size = 0;               // GEMM_W4: k elements per weight scale (a multiple of 16)
     // c_attn only: also write Q, K [m, kvd] and V^T [kvd, vt_pitch] of qkv as
     // fp16 hi / lo under per-head power-of-two scales (the tensor-core
     // attention's operands); kv_bound [6 kvd / 64] holds the per-head bounds
@@ -76,10 +81,24 @@ int make_tma_f16_sw128(CUtensorMap* map, const void* ptr, int64_t rows, int64_t 
                        int64_t pitch = 0);
 // x = hi + lo with hi rounded to TF32 precision (10 explicit mantissa bits)
 int launch_split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStream_t st);
+// tvq_int4.cu: group-wise INT4 (int4.tkv).  zps == nullptr: symmetric
+// (quantize_int4_grouped / dequantize_int4_grouped), else the AWQ-style
+// asymmetric form with per-group zero points.  packed [rows, cols / 2]
+// bytes, scales / zps [rows, cols / gs].
+int launch_int4_quantize(const float* src, int64_t rows, int64_t cols, int64_t gs, uint8_t* packed, float* scales,
+                         int64_t* zps, cudaStream_t st);
+int launch_int4_dequantize(const uint8_t* packed, float* dst, int64_t rows, int64_t cols, int64_t gs,
+                           const float* scales, const int64_t* zps, cudaStream_t st);
+// dst[r, c] = src[r, perm[c]] (inverse: dst[r, perm[c]] = src[r, c])
+int launch_permute_cols(const float* src, float* dst, int64_t rows, int64_t cols, const int64_t* perm, int inverse,
+                        cudaStream_t st);
+// packed [n, k / 2] -> nib - 8 as fp16 [n, k] (GEMM_W4's weights)
+int launch_int4_unpack_f16(const uint8_t* packed, void* q, int64_t n, int64_t k, cudaStream_t st);
+
 // Row-scaled fp16 split of x [rows, k]: per row s = 2^e with max|x|*s in
 // [2^14, 2^15); hi = fp16(x*s), lo = fp16(x*s - hi); rscale[row] = 1/s.
 int launch_split_f16_rows(const float* x, void* hi, void* lo, float* rscale, int64_t rows, int64_t k,
-                          cudaStream_t st);
+                          cudaStream_t st, const int64_t* perm = nullptr);
 
 // tvq_qdq.cu: the ONNX QDQ operator family (session.tkv:1896-2071, 2789-2905).
 // Quantize / dequantize split the tensor at its axis into (outer, dim, inner);
