@@ -76,22 +76,22 @@ def gemm_work(T=SEQ, d=768, ffn=3072):
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one gemm_c_fc launch in
 # the forward, from ncu (profiles/gemm_i8_gpt2_124m.md)
-GEMM_CFC_TRAFFIC = 3256320
+GEMM_CFC_TRAFFIC = 3239936
 
 
 def attention_roofline(per_stage_ms, bf16, src, n_layers, T=SEQ, hd=64, heads=12):
     """Causal attention of one 1024-token sequence per layer: useful flops
     4 T^2 hd heads / 2 (QK^T and PV over the causal half) against the dense
-    TF32 rate (half the measured bf16 rate).  The kernel issues three TF32
-    products per useful product (3xTF32 for fp32 accuracy), so frac <= 1/3
-    by construction; the stage time includes the K/V split and the merge."""
+    FP16 rate (= the measured bf16 rate).  The kernel issues three FP16
+    products per useful product (hi/lo split for fp32 accuracy), so frac <=
+    1/3 by construction; the stage time includes the partial merge."""
     flops = 4.0 * T * T * hd * heads / 2
     t = per_stage_ms / n_layers / 1000.0
     achieved = flops / t / 1e12
-    peak = bf16 / 2.0
+    peak = bf16
     return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-            "traffic": None, "kernel": "attention_tc_kernel (+ split_k, split_vt, combine), per layer",
-            "peak_source": "dense TF32 = %s bf16 / 2" % src, "products_per_useful_product": 3}
+            "traffic": None, "kernel": "attention_tc_kernel (FP16 hi/lo operands, partial merge in-kernel), per layer",
+            "peak_source": "dense FP16 = %s bf16" % src, "products_per_useful_product": 3}
 
 
 def gemm_large(torch, dev, stream, flush, n=8192, reps=10):
