@@ -465,8 +465,8 @@ def run_ours(args, rank, world, local):
         roof["frac"] = roof["achieved"] / roof["peak"]
         # dram__bytes_read + dram__bytes_write of one c_fc launch inside the
         # forward (ncu, profiles/gemm_i8_gpt2_124m.md); outputs stay in L2
-        roof["traffic"] = GEMM_CFC_TRAFFIC if dom == "gemm_c_fc" else None
-        roof["kernel"] = "gemm_tc_kernel<I8> (%s, M=1024 N,K of the layer)" % dom
+        roof["traffic"] = GEMM_CFC_TRAFFIC if (dom == "gemm_c_fc" and args.config == 2) else None
+        roof["kernel"] = "gemm_tc_kernel<I8> (%s, M=%d, N,K of the layer)" % (dom, T)
         roof["peak_source"] = ("%s HBM copy bandwidth; INT8 peak = 2 x %s dense bf16 (%.1f TFLOP/s)"
                                % (src, src, bf16))
         kernels = {}
