@@ -170,11 +170,13 @@ __global__ void layernorm_kernel(const float* __restrict__ x, const float* __res
     }
 }
 
-// Block-per-row variant for d % 4 == 0 (16-byte aligned rows): LNW warps
-// share a row, each thread holding NV float4 of it in registers; the
-// float-pair partial sums are reduced over the warp by shuffles and over the
-// block through shared memory in a fixed order.  Same arithmetic as
-// layernorm_kernel (only the summation order differs).
+// Row-parallel variants for d % 4 == 0 (16-byte aligned rows): WPR warps
+// share a row (WPR = LNW: a block per row, for few rows; WPR = 1: a warp
+// per row, four rows per block, for many rows -- no block barrier between
+// the rows of a warp), each thread holding NV float4 of it in registers; the
+// float-pair partial sums are reduced over the warp by shuffles and, with
+// WPR > 1, over the block through shared memory in a fixed order.  Same
+// arithmetic as layernorm_kernel (only the summation order differs).
 constexpr int LNW = 4;
 
 __device__ __forceinline__ void ln_block_sum(float& h, float& l, float2* red, int lane, int warp) {
@@ -195,15 +197,24 @@ __device__ __forceinline__ void ln_block_sum(float& h, float& l, float2* red, in
     }
 }
 
-template <int NV>
+__device__ __forceinline__ void ln_warp_sum(float& h, float& l) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float oh = __shfl_xor_sync(0xffffffffu, h, o), ol = __shfl_xor_sync(0xffffffffu, l, o);
+        df_add(h, l, oh, ol, h, l);
+    }
+}
+
+template <int NV, int WPR>
 __global__ void __launch_bounds__(32 * LNW)
     layernorm_block_kernel(const float* __restrict__ x, const float* __restrict__ g, const float* __restrict__ b,
                            float* __restrict__ y, int8_t* __restrict__ q, const float* __restrict__ qscale,
                            uint32_t* __restrict__ amax, int T, int d, double eps) {
     griddep_wait();
     __shared__ float2 red[2][LNW];
-    const int tid = threadIdx.x;
-    const int lane = tid & 31, warp = tid >> 5;
+    constexpr int RPB = LNW / WPR;  // rows per block per pass
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int tid = (WPR == 1) ? lane : static_cast<int>(threadIdx.x);  // thread index within its row
     const int d4 = d >> 2;
     InvScale qs{0.0, 0.0f, 0.0f};
     if (q) qs = make_inv_scale(static_cast<double>(__ldg(qscale)));
@@ -213,12 +224,12 @@ __global__ void __launch_bounds__(32 * LNW)
     const float4* g4 = reinterpret_cast<const float4*>(g);
     const float4* b4 = reinterpret_cast<const float4*>(b);
     float am = 0.0f;
-    for (int t = blockIdx.x; t < T; t += gridDim.x) {
+    for (int t = blockIdx.x * RPB + (WPR == 1 ? warp : 0); t < T; t += gridDim.x * RPB) {
         const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(t) * d);
         float4 v[NV];
 #pragma unroll
         for (int j = 0; j < NV; j++) {
-            const int i = j * 32 * LNW + tid;
+            const int i = j * 32 * WPR + tid;
             v[j] = (i < d4) ? __ldcs(xr + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
         // sum: four float-pair accumulators (x, y, z, w components)
@@ -237,14 +248,15 @@ __global__ void __launch_bounds__(32 * LNW)
         df_add(sh[0], sl[0], sh[1], sl[1], sh[0], sl[0]);
         df_add(sh[2], sl[2], sh[3], sl[3], sh[2], sl[2]);
         df_add(sh[0], sl[0], sh[2], sl[2], sh[0], sl[0]);
-        ln_block_sum(sh[0], sl[0], red[0], lane, warp);
+        if constexpr (WPR == 1) ln_warp_sum(sh[0], sl[0]);
+        else ln_block_sum(sh[0], sl[0], red[0], lane, warp);
         float mh, ml;
         df_div_int(sh[0], sl[0], df, mh, ml);
         // variance of the valid elements
         float vh[4] = {0.0f, 0.0f, 0.0f, 0.0f}, vl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
         for (int j = 0; j < NV; j++) {
-            if (j * 32 * LNW + tid >= d4) continue;
+            if (j * 32 * WPR + tid >= d4) continue;
             const float c[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
 #pragma unroll
             for (int k = 0; k < 4; k++) {
@@ -263,14 +275,15 @@ __global__ void __launch_bounds__(32 * LNW)
         df_add(vh[0], vl[0], vh[1], vl[1], vh[0], vl[0]);
         df_add(vh[2], vl[2], vh[3], vl[3], vh[2], vl[2]);
         df_add(vh[0], vl[0], vh[2], vl[2], vh[0], vl[0]);
-        ln_block_sum(vh[0], vl[0], red[1], lane, warp);
+        if constexpr (WPR == 1) ln_warp_sum(vh[0], vl[0]);
+        else ln_block_sum(vh[0], vl[0], red[1], lane, warp);
         float wh, wl, rh, rl;
         df_div_int(vh[0], vl[0], df, wh, wl);
         df_add(wh, wl, eps_h, eps_l, wh, wl);
         df_rsqrt(wh, wl, rh, rl);
 #pragma unroll
         for (int j = 0; j < NV; j++) {
-            const int i = j * 32 * LNW + tid;
+            const int i = j * 32 * WPR + tid;
             if (i >= d4) continue;
             const float4 gg = __ldg(g4 + i), bb = __ldg(b4 + i);
             const float c[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
@@ -309,7 +322,7 @@ __global__ void __launch_bounds__(32 * LNW)
                 *reinterpret_cast<char4*>(q + idx) = qq;
             }
         }
-        __syncthreads();  // red is reused by the next row
+        if constexpr (WPR > 1) __syncthreads();  // red is reused by the next row
     }
     if (amax) {
         am = warp_max_f(am);
@@ -327,15 +340,29 @@ int launch_layernorm(const float* x, const float* g, const float* b, float* y, i
     const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(g) |
                          reinterpret_cast<uintptr_t>(b) | (y ? reinterpret_cast<uintptr_t>(y) : 0) |
                          (q ? reinterpret_cast<uintptr_t>(q) & 3 : 0);
-    const int nv = (d / 4 + 32 * LNW - 1) / (32 * LNW);
+    // a warp per row once there are many more rows than a block-per-row grid
+    // holds at once (TVQ_LN_WARP=0/1 forces the choice: tuning)
+    static const int env_warp = [] {
+        const char* e = getenv("TVQ_LN_WARP");
+        return e ? atoi(e) : -1;
+    }();
+    const int nvw = (d / 4 + 31) / 32;
+    const bool warp_rows = (env_warp >= 0) ? env_warp != 0 : (T >= 4 * sm_count() * 16 && nvw <= 16);
+    const int nv = warp_rows ? nvw : (d / 4 + 32 * LNW - 1) / (32 * LNW);
     if ((d & 3) == 0 && (al & 15) == 0 && nv <= 16) {
-        const int bgrid = std::min(T, sm_count() * 16);
-#define TVQ_LN(NV) \
-    launch_pdl(layernorm_block_kernel<NV>, dim3(bgrid), dim3(32 * LNW), 0, st, x, g, b, y, q, qscale, amax, T, d, eps)
+        const int rpb = warp_rows ? LNW : 1;
+        const int bgrid = std::min((T + rpb - 1) / rpb, sm_count() * 16);
+#define TVQ_LN(NV)                                                                                                  \
+    (warp_rows ? launch_pdl(layernorm_block_kernel<NV, 1>, dim3(bgrid), dim3(32 * LNW), 0, st, x, g, b, y, q, qscale, \
+                            amax, T, d, eps)                                                                         \
+               : launch_pdl(layernorm_block_kernel<NV, LNW>, dim3(bgrid), dim3(32 * LNW), 0, st, x, g, b, y, q,     \
+                            qscale, amax, T, d, eps))
         if (nv <= 1) return TVQ_LN(1);
         if (nv <= 2) return TVQ_LN(2);
         if (nv <= 4) return TVQ_LN(4);
+        if (nv <= 6) return TVQ_LN(6);    // d 768, a warp per row
         if (nv <= 8) return TVQ_LN(8);
+        if (nv <= 13) return TVQ_LN(13);  // d 1600, a warp per row
         return TVQ_LN(16);
 #undef TVQ_LN
     } else {
