@@ -214,16 +214,20 @@ def test_session_launch_count_and_both_attention_paths(monkeypatch):
     s = GPT2Session(w, max_tokens=1024)
     try:
         # tensor-core path: embed; per layer LN, c_attn (which also writes
-        # the K / V^T hi-lo operands), attention, c_proj, LN, c_fc, mlp
-        # c_proj; ln_f, LM-head split, LM head
+        # the Q / K / V^T hi-lo operands), attention, c_proj, LN, c_fc, mlp
+        # c_proj; ln_f writing the LM head's split operand, LM head
         s.prepare(seg)
         s.set_act_scales(scales)
         got_tc = s.forward(ids)
-        assert s.launches() == 1 + 7 * cfg.n_layers + 3
+        assert s.launches() == 1 + 7 * cfg.n_layers + 2
         monkeypatch.setenv("TVQ_ATTN_TC", "0")
         s.prepare(seg)
         got_simt = s.forward(ids)
-        assert s.launches() == 1 + 7 * cfg.n_layers + 3
+        assert s.launches() == 1 + 7 * cfg.n_layers + 2
+        # last-token logits: ln_f, gather of the last rows, split, LM head
+        s.prepare(seg, logits_mode=1)
+        s.forward(ids)
+        assert s.launches() == 1 + 7 * cfg.n_layers + 4
     finally:
         s.close()
     for got in (got_tc, got_simt):

@@ -6,6 +6,8 @@
 //
 // Every producer can also record max|y| of its f32 output into a device word
 // (calibration), so calibrating a whole stack needs no host round trip.
+#include <cuda_fp16.h>
+
 #include "tvq_common.cuh"
 #include "tvq_exact.cuh"
 #include "tvq_glue.h"
@@ -205,11 +207,14 @@ __device__ __forceinline__ void ln_warp_sum(float& h, float& l) {
     }
 }
 
-template <int NV, int WPR>
+// SPLIT: the output goes out as the LM head's operand instead, the row-scaled
+// fp16 split of launch_split_f16_rows (hi, lo [T, d], rscale [T]).
+template <int NV, int WPR, bool SPLIT = false>
 __global__ void __launch_bounds__(32 * LNW)
     layernorm_block_kernel(const float* __restrict__ x, const float* __restrict__ g, const float* __restrict__ b,
                            float* __restrict__ y, int8_t* __restrict__ q, const float* __restrict__ qscale,
-                           uint32_t* __restrict__ amax, int T, int d, double eps) {
+                           uint32_t* __restrict__ amax, int T, int d, double eps, __half* __restrict__ shi = nullptr,
+                           __half* __restrict__ slo = nullptr, float* __restrict__ srs = nullptr) {
     griddep_wait();
     __shared__ float2 red[2][LNW];
     constexpr int RPB = LNW / WPR;  // rows per block per pass
@@ -278,6 +283,9 @@ __global__ void __launch_bounds__(32 * LNW)
         if constexpr (WPR == 1) ln_warp_sum(vh[0], vl[0]);
         else ln_block_sum(vh[0], vl[0], red[1], lane, warp);
         float wh, wl, rh, rl;
+        float4 ov[SPLIT ? NV : 1];
+        float rmax = 0.0f;
+        bool bad = false;
         df_div_int(vh[0], vl[0], df, wh, wl);
         df_add(wh, wl, eps_h, eps_l, wh, wl);
         df_rsqrt(wh, wl, rh, rl);
@@ -307,6 +315,15 @@ __global__ void __launch_bounds__(32 * LNW)
                 o4[k] = __fadd_rn(s, __fadd_rn(e, ue));
                 am = fmaxf(am, fabsf(o4[k]));
             }
+            if constexpr (SPLIT) {
+                ov[j] = make_float4(o4[0], o4[1], o4[2], o4[3]);
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    rmax = fmaxf(rmax, fabsf(o4[k]));
+                    bad |= !isfinite(o4[k]);
+                }
+                continue;
+            }
             const int64_t idx = static_cast<int64_t>(t) * d + 4 * i;
             if (y) *reinterpret_cast<float4*>(y + idx) = make_float4(o4[0], o4[1], o4[2], o4[3]);
             if (q) {
@@ -322,12 +339,73 @@ __global__ void __launch_bounds__(32 * LNW)
                 *reinterpret_cast<char4*>(q + idx) = qq;
             }
         }
+        if constexpr (SPLIT) {
+            // the row's largest |y| (red[0] is free: every thread has read the mean)
+            rmax = warp_max_f(rmax);
+            bad = __any_sync(0xffffffffu, bad);
+            if constexpr (WPR > 1) {
+                if (lane == 0) red[0][warp] = make_float2(rmax, bad ? 1.0f : 0.0f);
+                __syncthreads();
+#pragma unroll
+                for (int w = 0; w < LNW; w++) {
+                    rmax = fmaxf(rmax, red[0][w].x);
+                    bad |= red[0][w].y != 0.0f;
+                }
+            }
+            // as split_f16_rows_kernel: s with max|y| 2^s in [2^14, 2^15), 1 for a non-finite row
+            int sh = 0;
+            if (!bad && rmax > 0.0f) {
+                int e;
+                frexpf(rmax, &e);
+                sh = min(15 - e, 126);
+            }
+            if (tid == 0) srs[t] = exp2i(-sh);
+            const float f = exp2i(sh);
+#pragma unroll
+            for (int j = 0; j < NV; j++) {
+                const int i = j * 32 * WPR + tid;
+                if (i >= d4) continue;
+                const float vv[4] = {ov[j].x * f, ov[j].y * f, ov[j].z * f, ov[j].w * f};
+                __half h[4], l[4];
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    h[k] = __float2half_rn(vv[k]);
+                    l[k] = __float2half_rn(__fsub_rn(vv[k], __half2float(h[k])));
+                }
+                const int64_t idx = static_cast<int64_t>(t) * d + 4 * i;
+                *reinterpret_cast<uint2*>(shi + idx) = make_uint2(
+                    static_cast<uint32_t>(__half_as_ushort(h[0])) | (static_cast<uint32_t>(__half_as_ushort(h[1])) << 16),
+                    static_cast<uint32_t>(__half_as_ushort(h[2])) | (static_cast<uint32_t>(__half_as_ushort(h[3])) << 16));
+                *reinterpret_cast<uint2*>(slo + idx) = make_uint2(
+                    static_cast<uint32_t>(__half_as_ushort(l[0])) | (static_cast<uint32_t>(__half_as_ushort(l[1])) << 16),
+                    static_cast<uint32_t>(__half_as_ushort(l[2])) | (static_cast<uint32_t>(__half_as_ushort(l[3])) << 16));
+            }
+        }
         if constexpr (WPR > 1) __syncthreads();  // red is reused by the next row
     }
     if (amax) {
         am = warp_max_f(am);
         if (lane == 0) atomicMax(amax, __float_as_uint(am));
     }
+}
+
+int launch_layernorm_split(const float* x, const float* g, const float* b, void* hi, void* lo, float* rscale, int T,
+                           int d, double eps, cudaStream_t st) {
+    if (T <= 0) return TVQ_OK;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(b) |
+                         reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo);
+    const int nv = (d / 4 + 32 * LNW - 1) / (32 * LNW);
+    TVQ_CHECK((d & 3) == 0 && (al & 15) == 0 && nv <= 4, TVQ_ERR_UNSUPPORTED,
+              "the fused LayerNorm + split needs d % 4 == 0, d <= 2048 and 16-byte aligned buffers");
+    const int bgrid = std::min(T, sm_count() * 16);
+#define TVQ_LNS(NV)                                                                                                   \
+    launch_pdl(layernorm_block_kernel<NV, LNW, true>, dim3(bgrid), dim3(32 * LNW), 0, st, x, g, b,                    \
+               static_cast<float*>(nullptr), static_cast<int8_t*>(nullptr), static_cast<const float*>(nullptr),        \
+               static_cast<uint32_t*>(nullptr), T, d, eps, static_cast<__half*>(hi), static_cast<__half*>(lo), rscale)
+    if (nv <= 1) return TVQ_LNS(1);
+    if (nv <= 2) return TVQ_LNS(2);
+    return TVQ_LNS(4);
+#undef TVQ_LNS
 }
 
 int launch_layernorm(const float* x, const float* g, const float* b, float* y, int8_t* q, const float* qscale,
@@ -350,13 +428,15 @@ int launch_layernorm(const float* x, const float* g, const float* b, float* y, i
     const bool warp_rows = (env_warp >= 0) ? env_warp != 0 : (T >= 4 * sm_count() * 16 && nvw <= 16);
     const int nv = warp_rows ? nvw : (d / 4 + 32 * LNW - 1) / (32 * LNW);
     if ((d & 3) == 0 && (al & 15) == 0 && nv <= 16) {
+        __half* nh = nullptr;  // no split output
+        float* nf = nullptr;
         const int rpb = warp_rows ? LNW : 1;
         const int bgrid = std::min((T + rpb - 1) / rpb, sm_count() * 16);
 #define TVQ_LN(NV)                                                                                                  \
     (warp_rows ? launch_pdl(layernorm_block_kernel<NV, 1>, dim3(bgrid), dim3(32 * LNW), 0, st, x, g, b, y, q, qscale, \
-                            amax, T, d, eps)                                                                         \
+                            amax, T, d, eps, nh, nh, nf)                                                             \
                : launch_pdl(layernorm_block_kernel<NV, LNW>, dim3(bgrid), dim3(32 * LNW), 0, st, x, g, b, y, q,     \
-                            qscale, amax, T, d, eps))
+                            qscale, amax, T, d, eps, nh, nh, nf))
         if (nv <= 1) return TVQ_LN(1);
         if (nv <= 2) return TVQ_LN(2);
         if (nv <= 4) return TVQ_LN(4);

@@ -9,6 +9,10 @@ namespace tvq {
 int launch_embed(const int64_t* ids, const int* tok_seg_start, const float* wte, const float* wpe, float* x, int T,
                  int d, int vocab, int max_pos, int* err, cudaStream_t st);
 // y (f32) and/or q (int8 with qscale) and/or amax of y
+// LayerNorm with its output as the row-scaled fp16 split of the LM head
+// (launch_split_f16_rows's hi / lo [T, d] and rscale [T]); block per row.
+int launch_layernorm_split(const float* x, const float* g, const float* b, void* hi, void* lo, float* rscale, int T,
+                           int d, double eps, cudaStream_t st);
 int launch_layernorm(const float* x, const float* g, const float* b, float* y, int8_t* q, const float* qscale,
                      uint32_t* amax, int T, int d, double eps, cudaStream_t st);
 // tiles: int4 {q0, seg_start, seg_end, 0} per 64-row query tile

@@ -296,18 +296,20 @@ int enqueue_forward(Session& s, bool calibrating) {
     STEP(launch_embed(s.ids, s.tok_start, s.wte, s.wpe, s.x, T, d, s.vocab, s.max_pos, s.err, s.st));
     STEP(mark(s, ST_EMBED));
     STEP(enqueue_layers(s, calibrating));
-    // ln_f and the tied LM head (gpt2_ref.tkv:589-610), fp32
-    STEP(launch_layernorm(s.x, s.lnf_g, s.lnf_b, s.xf, nullptr, nullptr, nullptr, T, d, s.eps, s.st));
-    STEP(mark(s, ST_LN));
-    const float* xin = s.xf;
+    // ln_f and the tied LM head (gpt2_ref.tkv:589-610), fp32; the LM head's
+    // operand (row-scaled fp16 hi / lo) comes straight from ln_f for all rows
     int rows = T;
     if (s.logits_mode == 1) {
+        STEP(launch_layernorm(s.x, s.lnf_g, s.lnf_b, s.xf, nullptr, nullptr, nullptr, T, d, s.eps, s.st));
         STEP(launch_gather_last(s.xf, s.seg, s.nseg, d, s.xf_last, s.st));
-        xin = s.xf_last;
         rows = s.nseg;
+        STEP(mark(s, ST_LN));
+        STEP(launch_split_f16_rows(s.xf_last, s.xf_hi, s.xf_lo, s.xf_rs, rows, d, s.st));
+    } else {
+        STEP(launch_layernorm_split(s.x, s.lnf_g, s.lnf_b, s.xf_hi, s.xf_lo, s.xf_rs, T, d, s.eps, s.st));
+        STEP(mark(s, ST_LN));
     }
     // tied LM head, fp32 on the FP16 tensor cores with split precision
-    STEP(launch_split_f16_rows(xin, s.xf_hi, s.xf_lo, s.xf_rs, rows, d, s.st));
     {
         GemmArgs g;
         g.kind = GEMM_F16X3;
