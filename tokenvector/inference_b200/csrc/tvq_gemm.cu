@@ -533,37 +533,41 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                     __syncwarp();
                     if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
                     tc_fence_after();
-                    uint32_t r[NCH][E::CH];
+                    // G chunks per TMEM read (all of them when they fit the registers)
+                    constexpr int G = (NCH > 4) ? 2 : NCH;
 #pragma unroll
-                    for (int i = 0; i < NCH; i++) tmem_ld_chunk(lane_base + b * BN + (half + E::EPW * i) * E::CH, r[i]);
-                    tmem_ld_wait();
+                    for (int i0 = 0; i0 < NCH; i0 += G) {
+                        uint32_t r[G][E::CH];
+#pragma unroll
+                        for (int ii = 0; ii < G; ii++)
+                            tmem_ld_chunk(lane_base + b * BN + (half + E::EPW * (i0 + ii)) * E::CH, r[ii]);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int ii = 0; ii < G; ii++) {
+                            const int i = i0 + ii;
+                            if constexpr (KIND == GEMM_W4) {
+                                // the group's scale of each column (same in every lane)
+                                const int n0 = nb * BN + (half + E::EPW * i) * E::CH;
+#pragma unroll
+                                for (int j = 0; j < E::CH; j++) {
+                                    const int n = min(n0 + j, p.n - 1);
+                                    const float sc = __ldg(p.scales_w + static_cast<int64_t>(n) * p.ngroups + u);
+                                    acc[i][j] = u == 0 ? __fmul_rn(__uint_as_float(r[ii][j]), sc)
+                                                       : fmaf(__uint_as_float(r[ii][j]), sc, acc[i][j]);
+                                }
+                            } else if (u == 0) {
+#pragma unroll
+                                for (int j = 0; j < E::CH; j++) acc[i][j] = __uint_as_float(r[ii][j]);
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < E::CH; j++)
+                                    acc[i][j] = __fadd_rn(acc[i][j], __uint_as_float(r[ii][j]));
+                            }
+                        }
+                    }
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[b]);
-                    if constexpr (KIND == GEMM_W4) {
-                        // the group's scales of this warp's columns (same in every lane)
-#pragma unroll
-                        for (int i = 0; i < NCH; i++) {
-                            const int n0 = nb * BN + (half + E::EPW * i) * E::CH;
-#pragma unroll
-                            for (int j = 0; j < E::CH; j++) {
-                                const int n = min(n0 + j, p.n - 1);
-                                const float sc = __ldg(p.scales_w + static_cast<int64_t>(n) * p.ngroups + u);
-                                acc[i][j] = u == 0 ? __fmul_rn(__uint_as_float(r[i][j]), sc)
-                                                   : fmaf(__uint_as_float(r[i][j]), sc, acc[i][j]);
-                            }
-                        }
-                    } else if (u == 0) {
-#pragma unroll
-                        for (int i = 0; i < NCH; i++)
-#pragma unroll
-                            for (int j = 0; j < E::CH; j++) acc[i][j] = __uint_as_float(r[i][j]);
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < NCH; i++)
-#pragma unroll
-                            for (int j = 0; j < E::CH; j++) acc[i][j] = __fadd_rn(acc[i][j], __uint_as_float(r[i][j]));
-                    }
                 }
                 if (!alive) break;
                 if constexpr (KIND == GEMM_W4) {
@@ -1078,10 +1082,12 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
         }();
         bn = env_bn;
     }
-    if ((split || w4) && bn > 128) bn = 128;  // their partial sums live in registers
+    // their partial sums live in registers (BN 256 with a 16-warp epilogue
+    // measured slower for the LM head: 381 vs 356 us, two 96 KB stages)
+    if ((split || w4) && bn > 128) bn = 128;
     if (bn == 0 && (split || w4)) {
-        // The split forms keep 128 (their N = 64 MMAs run well below the
-        // tensor rate) unless that leaves SMs without a tile.
+        // The split forms keep 128 (their N = 64 MMAs are issue-bound and
+        // re-read A per N tile) unless that leaves SMs without a tile.
         bn = (static_cast<int64_t>(p.num_m_blocks) * ((g.n + 127) / 128) >= ds->sm_count) ? 128 : 64;
     } else if (bn == 0) {
         // Tile width with the least time on the busiest SM: rounds of tiles
