@@ -254,9 +254,18 @@ def cpu_sample_c5(cfg):
     return C5_SEQS * C5_SEQ / full, t
 
 
+def _all_host_threads():
+    """The CPU baseline uses every host core: torchrun sets OMP_NUM_THREADS=1
+    per worker, which would otherwise leave the oracle single-threaded."""
+    import oracle as O
+    O.set_num_threads(os.cpu_count() or 1)
+    return O.num_threads()
+
+
 def run_reference(args, rank):
     if rank != 0:
         return 0
+    _all_host_threads()
     if args.config == 5:
         import oracle as O
         from tokenvector.inference_b200.gpt2 import GPT2Config
@@ -480,6 +489,7 @@ def run_ours(args, rank, world, local):
         cpu = None
         if world == 1:
             from oracle import num_threads
+            _all_host_threads()
             cpu_v, detail = cpu_sample(w, ids, sess.act_scales())
             cpu = {"value": cpu_v, "unit": UNIT, "cores": num_threads(), "kind": "port",
                    "sample": "embedding + 1 of 12 blocks on 1024 tokens (%.2f s) + LM head on 32 of 1024 rows "
@@ -653,6 +663,7 @@ def run_ours_c5(args, rank, world, local):
         cpu = None
         if world == 1:
             from oracle import num_threads
+            _all_host_threads()
             v, secs = cpu_sample_c5(cfg)
             cpu = {"value": v, "unit": UNIT, "cores": num_threads(), "kind": "port",
                    "sample": "1 of 48 blocks with per-step calibration on 1 of 8 sequences (%.2f s), extrapolated "
