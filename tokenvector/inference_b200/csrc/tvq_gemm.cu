@@ -1066,7 +1066,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
               "residual must be 16-byte aligned");
     TVQ_CHECK(!g.Yq || (reinterpret_cast<uintptr_t>(g.Yq) & 15) == 0, TVQ_ERR_UNSUPPORTED,
               "Yq must be 16-byte aligned");
-    TVQ_CHECK(!g.kh || (g.kind == GEMM_I8 && g.qh && g.ql && g.kl && g.vth && g.vtl && g.kv_exp && g.kv_bound && g.Y &&
+    TVQ_CHECK(!g.kh || (g.kind == GEMM_I8 && g.qh && g.ql && g.kl && g.vth && g.vtl && g.kv_exp && g.kv_bound &&
                         g.n == 3 * g.kvd && g.kvd % 64 == 0 && g.vt_pitch >= g.m && g.act == 0 && !g.residual),
               TVQ_ERR_INVALID, "attention operand split needs an INT8 qkv GEMM with N = 3 kvd");
     rc = get_encoder();

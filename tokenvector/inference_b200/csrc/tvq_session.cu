@@ -165,7 +165,7 @@ void lin_shape(const Session& s, int which, int* n, int* k) {
 int gemm(Session& s, const int8_t* A, const Lin& l, const float* scale_a, float* Y, const float* residual,
          int8_t* Yq, const float* scale_out, uint32_t* amax, int act, bool kv_split = false) {
     GemmArgs g;
-    if (kv_split) {  // c_attn on the tensor-core attention path: K and V^T operands from the epilogue
+    if (kv_split) {  // c_attn on the tensor-core attention path: Q, K and V^T operands from the epilogue
         g.qh = s.qh;
         g.ql = s.ql;
         g.kh = s.kh;
@@ -174,6 +174,7 @@ int gemm(Session& s, const int8_t* A, const Lin& l, const float* scale_a, float*
         g.vtl = s.vl;
         g.kv_exp = s.kv_exp;
         g.kv_bound = l.kvb;
+        Y = nullptr;  // the attention reads only the fp16 operands: no f32 qkv
         g.kvd = s.d;
         g.vt_pitch = attention_tc_pitch(s.T);
     }
