@@ -153,6 +153,20 @@ __device__ __forceinline__ void split_p2(float a, float b, uint32_t& hi, uint32_
     lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
+// split_p2 with the pair already packed (the remainder as one f32x2 subtract)
+__device__ __forceinline__ void split_p2x(uint64_t E, float a, float b, uint32_t& hi, uint32_t& lo) {
+    uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+    ua = (ua + 0xFFFu + ((ua >> 13) & 1u)) & 0xFFFFE000u;  // nearest, ties to even
+    ub = (ub + 0xFFFu + ((ub >> 13) & 1u)) & 0xFFFFE000u;
+    const float ha = __uint_as_float(ua), hb = __uint_as_float(ub);
+    const __half2 h = __floats2half2_rn(ha, hb);
+    float la, lb;
+    f2_unpack(f2_sub(E, f2_pack(ha, hb)), la, lb);
+    const __half2 l = __floats2half2_rn(la, lb);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
 // Q (part 0) or K (part 1) of qkv [T, 3d] -> fp16 hi / lo [T, d] under the
 // head scales 2^kv_exp[part heads + h] (standalone path; the session's
 // c_attn epilogue writes the same)
@@ -455,21 +469,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             // for lo <= c <= hi
             const int k0 = kb_al + j * TK + 32 * h;
             const int lo = kb - k0, hi = min(q, ke - 1) - k0;
-            float x[32];
+            uint64_t x2[16];  // the scaled scores, two keys per register pair (f32x2)
             float mx = -INFINITY, mx2 = -INFINITY;
             if (lo <= 0 && hi >= 31) {  // every key of the half visible: most blocks
+                const uint64_t XS = f2_pack(xs, xs);
 #pragma unroll
                 for (int c = 0; c < 32; c += 2) {
-                    x[c] = __fmul_rn(__uint_as_float(sr[c]), xs);
-                    x[c + 1] = __fmul_rn(__uint_as_float(sr[c + 1]), xs);
-                    mx = fmaxf(mx, x[c]);
-                    mx2 = fmaxf(mx2, x[c + 1]);
+                    x2[c / 2] = f2_mul(f2_pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), XS);
+                    float a, bq;
+                    f2_unpack(x2[c / 2], a, bq);
+                    mx = fmaxf(mx, a);
+                    mx2 = fmaxf(mx2, bq);
                 }
             } else {
 #pragma unroll
-                for (int c = 0; c < 32; c++) {
-                    x[c] = (c >= lo && c <= hi) ? __fmul_rn(__uint_as_float(sr[c]), xs) : -INFINITY;
-                    mx = fmaxf(mx, x[c]);
+                for (int c = 0; c < 32; c += 2) {
+                    const float a = (c >= lo && c <= hi) ? __fmul_rn(__uint_as_float(sr[c]), xs) : -INFINITY;
+                    const float bq = (c + 1 >= lo && c + 1 <= hi) ? __fmul_rn(__uint_as_float(sr[c + 1]), xs) : -INFINITY;
+                    x2[c / 2] = f2_pack(a, bq);
+                    mx = fmaxf(mx, a);
+                    mx2 = fmaxf(mx2, bq);
                 }
             }
             mx = fmaxf(mx, mx2);
@@ -487,16 +506,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             // 2^14) as fp16 hi + lo (|error| <= max(2^-22 P, 2^-25)) into
             // P[b]; P[b] was last read by PV_{j-2}, whose completion the
             // previous iteration already waited for
-            const float mref14 = mref - 14.0f;
+            const uint64_t M14 = f2_pack(mref - 14.0f, mref - 14.0f);
             uint32_t phi[16], plo[16];
-            float sa4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            uint64_t acc2[2] = {0ull, 0ull};  // (+0, +0) pairs
 #pragma unroll
             for (int c = 0; c < 32; c += 2) {
-                const float e0 = ex2_approx(x[c] - mref14), e1 = ex2_approx(x[c + 1] - mref14);
-                sa4[(c >> 1) & 3] += e0 + e1;
-                split_p2(e0, e1, phi[c / 2], plo[c / 2]);
+                float d0, d1;
+                f2_unpack(f2_sub(x2[c / 2], M14), d0, d1);
+                const float e0 = ex2_approx(d0), e1 = ex2_approx(d1);
+                const uint64_t E = f2_pack(e0, e1);
+                acc2[(c >> 1) & 1] = f2_add(acc2[(c >> 1) & 1], E);
+                split_p2x(E, e0, e1, phi[c / 2], plo[c / 2]);
             }
-            const float sum = (sa4[0] + sa4[1]) + (sa4[2] + sa4[3]);
+            float s0, s1, s2, s3;
+            f2_unpack(acc2[0], s0, s1);
+            f2_unpack(acc2[1], s2, s3);
+            const float sum = (s0 + s1) + (s2 + s3);
             tmem_st16(lane_base + COL_P + b * 64 + 16 * h, phi);
             tmem_st16(lane_base + COL_P + b * 64 + 32 + 16 * h, plo);
             l = fmaf(l, alpha, sum);

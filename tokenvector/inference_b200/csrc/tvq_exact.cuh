@@ -211,6 +211,13 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
 __device__ __forceinline__ uint64_t f2_abs(uint64_t a) { return a & 0x7FFFFFFF7FFFFFFFull; }
 __device__ __forceinline__ uint64_t f2_neg(uint64_t a) { return a ^ 0x8000000080000000ull; }
 
+// two_sum on two pairs at once: S = A + B rounded, E its exact error.
+__device__ __forceinline__ void two_sum2(uint64_t A, uint64_t B, uint64_t& S, uint64_t& E) {
+    S = f2_add(A, B);
+    const uint64_t BB = f2_sub(S, A);
+    E = f2_add(f2_sub(A, f2_sub(S, BB)), f2_sub(B, BB));
+}
+
 // epilogue_fast for two columns at once, accumulators below 2^24 in
 // magnitude (ar = 0): the same operations as the scalar form, so the same
 // results and the same decisions.  Bit j of the return value is set when

@@ -237,18 +237,26 @@ __global__ void __launch_bounds__(32 * LNW)
             const int i = j * 32 * WPR + tid;
             v[j] = (i < d4) ? __ldcs(xr + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
-        // sum: four float-pair accumulators (x, y, z, w components)
-        float sh[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        // sum: four float-pair accumulators (x, y, z, w components), two
+        // components per f32x2 instruction
+        float sh[4], sl[4];
+        {
+            uint64_t SH[2] = {0ull, 0ull}, SL[2] = {0ull, 0ull};
 #pragma unroll
-        for (int j = 0; j < NV; j++) {
-            const float c[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+            for (int j = 0; j < NV; j++) {
+                const uint64_t C[2] = {f2_pack(v[j].x, v[j].y), f2_pack(v[j].z, v[j].w)};
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                float s, e;
-                two_sum(sh[k], c[k], s, e);
-                sh[k] = s;
-                sl[k] = __fadd_rn(sl[k], e);
+                for (int k = 0; k < 2; k++) {
+                    uint64_t S, E;
+                    two_sum2(SH[k], C[k], S, E);
+                    SH[k] = S;
+                    SL[k] = f2_add(SL[k], E);
+                }
             }
+            f2_unpack(SH[0], sh[0], sh[1]);
+            f2_unpack(SH[1], sh[2], sh[3]);
+            f2_unpack(SL[0], sl[0], sl[1]);
+            f2_unpack(SL[1], sl[2], sl[3]);
         }
         df_add(sh[0], sl[0], sh[1], sl[1], sh[0], sl[0]);
         df_add(sh[2], sl[2], sh[3], sl[3], sh[2], sl[2]);
@@ -258,24 +266,33 @@ __global__ void __launch_bounds__(32 * LNW)
         float mh, ml;
         df_div_int(sh[0], sl[0], df, mh, ml);
         // variance of the valid elements
-        float vh[4] = {0.0f, 0.0f, 0.0f, 0.0f}, vl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        float vh[4], vl[4];
+        const uint64_t NMH = f2_pack(-mh, -mh), ML = f2_pack(ml, ml);
+        {
+            uint64_t VH[2] = {0ull, 0ull}, VL[2] = {0ull, 0ull};
+            const uint64_t TWO = f2_pack(2.0f, 2.0f);
 #pragma unroll
-        for (int j = 0; j < NV; j++) {
-            if (j * 32 * WPR + tid >= d4) continue;
-            const float c[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+            for (int j = 0; j < NV; j++) {
+                if (j * 32 * WPR + tid >= d4) continue;
+                const uint64_t C[2] = {f2_pack(v[j].x, v[j].y), f2_pack(v[j].z, v[j].w)};
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                float dh, de;
-                two_sum(c[k], -mh, dh, de);
-                de = __fsub_rn(de, ml);
-                const float pp = __fmul_rn(dh, dh);
-                float pe = fmaf(dh, dh, -pp);
-                pe = fmaf(2.0f * dh, de, pe);
-                float s, e;
-                two_sum(vh[k], pp, s, e);
-                vh[k] = s;
-                vl[k] = __fadd_rn(vl[k], __fadd_rn(e, pe));
+                for (int k = 0; k < 2; k++) {
+                    uint64_t DH, DE;
+                    two_sum2(C[k], NMH, DH, DE);
+                    DE = f2_sub(DE, ML);
+                    const uint64_t PP = f2_mul(DH, DH);
+                    uint64_t PE = f2_fma(DH, DH, f2_neg(PP));
+                    PE = f2_fma(f2_mul(TWO, DH), DE, PE);
+                    uint64_t S, E;
+                    two_sum2(VH[k], PP, S, E);
+                    VH[k] = S;
+                    VL[k] = f2_add(VL[k], f2_add(E, PE));
+                }
             }
+            f2_unpack(VH[0], vh[0], vh[1]);
+            f2_unpack(VH[1], vh[2], vh[3]);
+            f2_unpack(VL[0], vl[0], vl[1]);
+            f2_unpack(VL[1], vl[2], vl[3]);
         }
         df_add(vh[0], vl[0], vh[1], vl[1], vh[0], vl[0]);
         df_add(vh[2], vl[2], vh[3], vl[3], vh[2], vl[2]);
@@ -294,27 +311,29 @@ __global__ void __launch_bounds__(32 * LNW)
             const int i = j * 32 * WPR + tid;
             if (i >= d4) continue;
             const float4 gg = __ldg(g4 + i), bb = __ldg(b4 + i);
-            const float c[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-            const float gv[4] = {gg.x, gg.y, gg.z, gg.w};
-            const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
+            const uint64_t C[2] = {f2_pack(v[j].x, v[j].y), f2_pack(v[j].z, v[j].w)};
+            const uint64_t G2[2] = {f2_pack(gg.x, gg.y), f2_pack(gg.z, gg.w)};
+            const uint64_t B2[2] = {f2_pack(bb.x, bb.y), f2_pack(bb.z, bb.w)};
+            const uint64_t RH = f2_pack(rh, rh), RL = f2_pack(rl, rl);
             float o4[4];
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                float dh, de;
-                two_sum(c[k], -mh, dh, de);
-                de = __fsub_rn(de, ml);
-                const float tt = __fmul_rn(dh, rh);
-                float te = fmaf(dh, rh, -tt);
-                te = fmaf(dh, rl, te);
-                te = fmaf(de, rh, te);
-                const float u = __fmul_rn(tt, gv[k]);
-                float ue = fmaf(tt, gv[k], -u);
-                ue = fmaf(te, gv[k], ue);
-                float s, e;
-                two_sum(u, bv[k], s, e);
-                o4[k] = __fadd_rn(s, __fadd_rn(e, ue));
-                am = fmaxf(am, fabsf(o4[k]));
+            for (int k = 0; k < 2; k++) {
+                uint64_t DH, DE;
+                two_sum2(C[k], NMH, DH, DE);
+                DE = f2_sub(DE, ML);
+                const uint64_t TT = f2_mul(DH, RH);
+                uint64_t TE = f2_fma(DH, RH, f2_neg(TT));
+                TE = f2_fma(DH, RL, TE);
+                TE = f2_fma(DE, RH, TE);
+                const uint64_t U = f2_mul(TT, G2[k]);
+                uint64_t UE = f2_fma(TT, G2[k], f2_neg(U));
+                UE = f2_fma(TE, G2[k], UE);
+                uint64_t S, E;
+                two_sum2(U, B2[k], S, E);
+                f2_unpack(f2_add(S, f2_add(E, UE)), o4[2 * k], o4[2 * k + 1]);
             }
+#pragma unroll
+            for (int k = 0; k < 4; k++) am = fmaxf(am, fabsf(o4[k]));
             if constexpr (SPLIT) {
                 ov[j] = make_float4(o4[0], o4[1], o4[2], o4[3]);
 #pragma unroll
