@@ -446,6 +446,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int q = q0 + r;
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(32 * g) << 16);
         bool alive = true;
+        // 1 / scale of the int8 output, early (its load and f64 quotient stay
+        // off the tail of the CTA)
+        InvScale qs{0.0, 0.0f, 0.0f};
+        if (p.outq) qs = make_inv_scale(static_cast<double>(__ldg(p.qscale)));
         // scores: S = acc 2^-(sq + sk) exactly, times log2(e) / sqrt(hd)
         const int sq = p.kv_exp[head], sk = p.kv_exp[p.nheads + head], sv = p.kv_exp[2 * p.nheads + head];
         const float xs = p.scale2 * exp2i(-sq) * exp2i(-sk);
@@ -654,16 +658,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         dst[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
                 }
                 if (p.outq) {
-                    const InvScale qs = make_inv_scale(static_cast<double>(__ldg(p.qscale)));
-                    char4* dst = reinterpret_cast<char4*>(p.outq + base);
+                    // branch-free fast quantize of all 32, rare f64 fix-ups after
+                    union { int8_t b[32]; uint4 u[2]; } v;
+                    uint32_t bad = 0;
 #pragma unroll
-                    for (int c4 = 0; c4 < 8; c4++) {
-                        char4 v;
-                        v.x = quant_exact(o[4 * c4], qs);
-                        v.y = quant_exact(o[4 * c4 + 1], qs);
-                        v.z = quant_exact(o[4 * c4 + 2], qs);
-                        v.w = quant_exact(o[4 * c4 + 3], qs);
-                        dst[c4] = v;
+                    for (int c = 0; c < 32; c++) bad |= quant_fast(o[c], qs, v.b[c]) ? 0u : (1u << c);
+                    if (bad) {
+#pragma unroll
+                        for (int c = 0; c < 32; c++)
+                            if (bad & (1u << c)) v.b[c] = quant_exact(o[c], qs);
+                    }
+                    if ((reinterpret_cast<uintptr_t>(p.outq + base) & 15) == 0) {
+                        uint4* dst = reinterpret_cast<uint4*>(p.outq + base);
+                        dst[0] = v.u[0];
+                        dst[1] = v.u[1];
+                    } else {
+                        uint32_t* dst = reinterpret_cast<uint32_t*>(p.outq + base);
+#pragma unroll
+                        for (int c4 = 0; c4 < 8; c4++)
+                            dst[c4] = (c4 & 3) == 0 ? v.u[c4 >> 2].x : (c4 & 3) == 1 ? v.u[c4 >> 2].y
+                                                   : (c4 & 3) == 2 ? v.u[c4 >> 2].z : v.u[c4 >> 2].w;
                     }
                 }
             }
