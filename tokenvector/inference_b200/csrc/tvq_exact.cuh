@@ -104,6 +104,31 @@ __device__ __forceinline__ int8_t quant_exact(float x, const InvScale& s) {
     return q;
 }
 
+// q = clamp(int(rint(fl64(x * inv))), -127, 127) from hi = fl32(inv) alone,
+// as the low byte of a float.  t = fl32(x*hi + 1.5*2^23) is 1.5*2^23 plus
+// the integer r nearest the exact product x*hi (|x*hi| < 2^22; ties to even,
+// as 1.5*2^23 is even), r = t - 1.5*2^23 exactly, and d = fl32(x*hi - r)
+// (|d| <= 1/2, error <= 2^-25).  x*inv differs from x*hi by at most
+// 2^-24 |x*hi| plus one f64 ulp, under 2^-15.9 for |x*hi| < 256, so r is
+// also the integer nearest fl64(x*inv) unless ||d| - 1/2| < 2^-15; from 256
+// up both saturate.  t clamped to 1.5*2^23 +- 127 holds 2^22 + q in its
+// mantissa, so its low byte is q as an int8.  Returns false for NaN,
+// infinities and near-ties (quant_slow decides).
+__device__ __forceinline__ bool quant_fast_t(float x, float hi, float& t) {
+    constexpr float M = 12582912.0f;  // 1.5 * 2^23
+    const float tt = fmaf(x, hi, M);
+    const float d = fmaf(x, hi, -__fsub_rn(tt, M));
+    t = fminf(fmaxf(tt, M - 127.0f), M + 127.0f);
+    return fabsf(__fsub_rn(fabsf(d), 0.5f)) >= 3.0517578125e-05f;  // 2^-15; false for NaN
+}
+
+// Four quant_fast_t results as four int8 bytes, the first in the low byte.
+__device__ __forceinline__ uint32_t pack_q4(float t0, float t1, float t2, float t3) {
+    const uint32_t lo = __byte_perm(__float_as_uint(t0), __float_as_uint(t1), 0x0040);
+    const uint32_t hi = __byte_perm(__float_as_uint(t2), __float_as_uint(t3), 0x0040);
+    return __byte_perm(lo, hi, 0x5410);
+}
+
 // ulp of a normal float y (|y| >= 2^-100)
 __device__ __forceinline__ float ulp_of(float y) {
     return __int_as_float((__float_as_int(fabsf(y)) & 0x7F800000) - (23 << 23));

@@ -70,6 +70,12 @@ using EpiOf = Epi<promoted_kind(KIND) ? 8 : 16>;
 // sum|a*w|; promoting every few k-blocks keeps the result at fp32 SGEMM
 // accuracy.  TVQ_TF32_PROMOTE_KB overrides it (tuning).
 constexpr int TF32_PROMOTE_KB = 2;  // max error ~3x cuBLAS SGEMM, ~15% slower than no promotion
+// GEMM_F16X3 (64 fp16 per k-block): every 3 k-blocks (K 192).  Measured at
+// the GPT-2 LM head (M 1024, N 50257, K 768) against a float64 reference,
+// max |error| / sum|a*w| per promotion interval 1 / 2 / 3 / 4 / 6 / 12:
+// 0.30 / 0.47 / 0.66 / 0.93 / 1.41 / 3.28 x that of torch's true-fp32
+// matmul, at 423 / 352 / 304 / 296 / 290 / 278 us.
+constexpr int F16_PROMOTE_KB = 3;
 
 struct KParams {
     int m, n, k;
@@ -86,6 +92,7 @@ struct KParams {
     const float* scale_a;
     const float* scales_w;
     int per_channel;
+    int acc24;  // INT8 with k < 1024: every accumulator is below 2^24 in magnitude
     int act;
     const float* scale_out;
     uint32_t* amax;
@@ -221,7 +228,9 @@ __device__ __forceinline__ void load_residual(const KParams& p, const EpiCtx& e,
 // `lane`: swizzled shared-memory transpose (float4 slot j of row r sits at
 // slot j ^ ((r >> SWS) & (LPR - 1)), conflict-free both ways), then LPR lanes
 // per 4*CH-byte row segment: residual add, f32 / int8 stores, running amax.
-template <class E>
+// QOUT compiles the int8 output in (the promoted fp32 forms never write int8;
+// leaving it out keeps their kernels small).
+template <class E, bool QOUT>
 __device__ __forceinline__ void stage_and_store(const KParams& p, const EpiCtx& e, float* stage, const float (&y)[E::CH],
                                                 int lane, int row0, int n0, float& amax, const float4 (&res)[E::LPR]) {
 #pragma unroll
@@ -259,17 +268,20 @@ __device__ __forceinline__ void stage_and_store(const KParams& p, const EpiCtx& 
             }
             if (p.amax) amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
             if (p.Y) *reinterpret_cast<float4*>(p.Y + off) = v;
-            if (p.Yq) {
-                char4 q;
-                const bool ok = quant_fast(v.x, e.qs, q.x) & quant_fast(v.y, e.qs, q.y) &
-                                quant_fast(v.z, e.qs, q.z) & quant_fast(v.w, e.qs, q.w);
-                if (!ok) {
+            if (QOUT && p.Yq) {
+                float t0, t1, t2, t3;
+                const bool ok = quant_fast_t(v.x, e.qs.hi, t0) & quant_fast_t(v.y, e.qs.hi, t1) &
+                                quant_fast_t(v.z, e.qs.hi, t2) & quant_fast_t(v.w, e.qs.hi, t3);
+                if (ok) {
+                    *reinterpret_cast<uint32_t*>(p.Yq + off) = pack_q4(t0, t1, t2, t3);
+                } else {
+                    char4 q;
                     q.x = quant_exact(v.x, e.qs);
                     q.y = quant_exact(v.y, e.qs);
                     q.z = quant_exact(v.z, e.qs);
                     q.w = quant_exact(v.w, e.qs);
+                    *reinterpret_cast<char4*>(p.Yq + off) = q;
                 }
-                *reinterpret_cast<char4*>(p.Yq + off) = q;
             }
         } else {
             const float vv[4] = {v.x, v.y, v.z, v.w};
@@ -280,7 +292,7 @@ __device__ __forceinline__ void stage_and_store(const KParams& p, const EpiCtx& 
                 if (p.residual) x = __fadd_rn(x, p.residual[off + k]);
                 if (p.amax) amax = fmaxf(amax, fabsf(x));
                 if (p.Y) p.Y[off + k] = x;
-                if (p.Yq) p.Yq[off + k] = quant_exact(x, e.qs);
+                if (QOUT && p.Yq) p.Yq[off + k] = quant_exact(x, e.qs);
             }
         }
     }
@@ -604,7 +616,7 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                     if (n0 >= p.n) break;  // warp-uniform
                     __syncwarp();           // the previous chunk's staging reads are done
                     const float4 nores[E::LPR] = {};
-                    stage_and_store<E>(p, ec, stage, acc[i], lane, row0, n0, amax, nores);
+                    stage_and_store<E, false>(p, ec, stage, acc[i], lane, row0, n0, amax, nores);
                 }
             }
         } else {
@@ -678,7 +690,7 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                 float y[E::CH];
                 uint32_t bad = 0;
                 bool small = true;
-                if (KIND == GEMM_I8) {
+                if (KIND == GEMM_I8 && !p.acc24) {
 #pragma unroll
                     for (int j = 0; j < E::CH; j++) small &= (r[j] + 0x01000000u) < 0x02000000u;  // |acc| < 2^24
                 }
@@ -752,7 +764,7 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < E::CH; j++) y[j] = y[j] > 0.0f ? y[j] : 0.0f;
                 }
-                stage_and_store<E>(p, ec, stage, y, lane, row0, n0, amax, res);
+                stage_and_store<E, true>(p, ec, stage, y, lane, row0, n0, amax, res);
             }
             tc_fence_before();
             __syncwarp();
@@ -1017,6 +1029,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.scale_a = g.scale_a;
     p.scales_w = g.scales_w;
     p.per_channel = (acc_only || split || w4) ? 0 : g.per_channel;
+    p.acc24 = (g.kind == GEMM_I8 && g.k < 1024) ? 1 : 0;
     p.group_ks = w4 ? static_cast<int>(g.group_size / 16) : 0;
     p.ngroups = w4 ? static_cast<int>(g.k / g.group_size) : 0;
     p.qh = static_cast<__half*>(g.qh);
@@ -1037,7 +1050,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.num_m_blocks = static_cast<int>((g.m + BM - 1) / BM);
     const int elem = (g.kind == GEMM_TF32X3) ? 4 : (g.kind == GEMM_F16X3 || w4) ? 2 : 1;
     p.num_k_blocks = static_cast<int>((g.k * elem + BK - 1) / BK);
-    p.promote_kb = TF32_PROMOTE_KB;
+    p.promote_kb = g.kind == GEMM_F16X3 ? F16_PROMOTE_KB : TF32_PROMOTE_KB;
     if (const char* env = getenv("TVQ_TF32_PROMOTE_KB")) p.promote_kb = std::max(1, atoi(env));
 
     if (g.k == 0 && split) {

@@ -346,16 +346,19 @@ __global__ void __launch_bounds__(32 * LNW)
             const int64_t idx = static_cast<int64_t>(t) * d + 4 * i;
             if (y) *reinterpret_cast<float4*>(y + idx) = make_float4(o4[0], o4[1], o4[2], o4[3]);
             if (q) {
-                char4 qq;
-                const bool ok = quant_fast(o4[0], qs, qq.x) & quant_fast(o4[1], qs, qq.y) &
-                                quant_fast(o4[2], qs, qq.z) & quant_fast(o4[3], qs, qq.w);
-                if (!ok) {
+                float t0, t1, t2, t3;
+                const bool ok = quant_fast_t(o4[0], qs.hi, t0) & quant_fast_t(o4[1], qs.hi, t1) &
+                                quant_fast_t(o4[2], qs.hi, t2) & quant_fast_t(o4[3], qs.hi, t3);
+                if (ok) {
+                    *reinterpret_cast<uint32_t*>(q + idx) = pack_q4(t0, t1, t2, t3);
+                } else {
+                    char4 qq;
                     qq.x = quant_exact(o4[0], qs);
                     qq.y = quant_exact(o4[1], qs);
                     qq.z = quant_exact(o4[2], qs);
                     qq.w = quant_exact(o4[3], qs);
+                    *reinterpret_cast<char4*>(q + idx) = qq;
                 }
-                *reinterpret_cast<char4*>(q + idx) = qq;
             }
         }
         if constexpr (SPLIT) {

@@ -190,15 +190,27 @@ __global__ void quantize_i8_kernel(const float* __restrict__ x, int8_t* __restri
         float4 v[4];
 #pragma unroll
         for (int j = 0; j < 4; j++) v[j] = __ldcs(src + j);
-        union { int8_t b[16]; uint4 u; } o;
+        uint32_t w[4];
+        bool ok = true;
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            o.b[4 * j + 0] = quant_exact(v[j].x, qs);
-            o.b[4 * j + 1] = quant_exact(v[j].y, qs);
-            o.b[4 * j + 2] = quant_exact(v[j].z, qs);
-            o.b[4 * j + 3] = quant_exact(v[j].w, qs);
+            float t0, t1, t2, t3;
+            ok &= quant_fast_t(v[j].x, qs.hi, t0) & quant_fast_t(v[j].y, qs.hi, t1) &
+                  quant_fast_t(v[j].z, qs.hi, t2) & quant_fast_t(v[j].w, qs.hi, t3);
+            w[j] = pack_q4(t0, t1, t2, t3);
         }
-        reinterpret_cast<uint4*>(q)[i] = o.u;
+        if (!ok) {  // rare: the binary64 expression decides
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                char4 c;
+                c.x = quant_exact(v[j].x, qs);
+                c.y = quant_exact(v[j].y, qs);
+                c.z = quant_exact(v[j].z, qs);
+                c.w = quant_exact(v[j].w, qs);
+                w[j] = *reinterpret_cast<const uint32_t*>(&c);
+            }
+        }
+        reinterpret_cast<uint4*>(q)[i] = make_uint4(w[0], w[1], w[2], w[3]);
     }
     for (int64_t i = n16 * 16 + tid; i < n; i += stride) q[i] = quant_exact(x[i], qs);
 }

@@ -81,9 +81,14 @@ struct Session {
     int T = 0, nseg = 0, ntiles = 0, logits_mode = 0;
     bool prepared = false;
     // captured graphs per mode (Mode below), rebuilt after prepare
-    cudaGraphExec_t gexec[3] = {nullptr, nullptr, nullptr};
-    int64_t graph_kernels[3] = {0, 0, 0};  // kernel nodes of each captured graph
-    int last_mode = -1;                    // mode of the graph launched last
+    cudaGraphExec_t gexec[4] = {nullptr, nullptr, nullptr, nullptr};
+    int64_t graph_kernels[4] = {0, 0, 0, 0};  // kernel nodes of each captured graph
+    int last_mode = -1;                       // mode of the graph launched last
+    int64_t extra_launches = 0;               // kernels launched beside that graph (LM head chunks)
+    // host-bound logits: the copy stream and its events (created on first use)
+    cudaStream_t cp = nullptr;
+    std::vector<cudaEvent_t> chunk_ev;
+    cudaEvent_t copies_done = nullptr;
     // optional stage events recorded inside the captured graph (profiling)
     bool profile = false;
     std::vector<cudaEvent_t> ev;
@@ -103,6 +108,9 @@ struct Session {
     ~Session() {
         drop_graphs();
         for (cudaEvent_t e : ev) cudaEventDestroy(e);
+        for (cudaEvent_t e : chunk_ev) cudaEventDestroy(e);
+        if (copies_done) cudaEventDestroy(copies_done);
+        if (cp) cudaStreamDestroy(cp);
         for (void* p : allocs) cudaFree(p);
         if (st) cudaStreamDestroy(st);
     }
@@ -223,10 +231,25 @@ int mark(Session& s, int stage) {
     return TVQ_OK;
 }
 
-// What a captured graph runs: the whole forward (ids -> logits), or the
+// What a captured graph runs: the whole forward (ids -> logits), the
 // transformer blocks alone on the hidden states in s.x with static
-// activation scales or with per-call (dynamic) calibration.
-enum Mode { M_FORWARD = 0, M_LAYERS = 1, M_LAYERS_DYNAMIC = 2 };
+// activation scales or with per-call (dynamic) calibration, or the forward up
+// to the LM head's operand (M_BODY: the LM head then runs in row chunks
+// whose logits are copied to the host while the next chunk computes).
+enum Mode { M_FORWARD = 0, M_LAYERS = 1, M_LAYERS_DYNAMIC = 2, M_BODY = 3 };
+
+// Rows of one LM-head chunk on the host-logits path (two 128-row tiles);
+// TVQ_LOGIT_CHUNK_ROWS overrides it (a multiple of 128; 0 = one launch and
+// one copy after it).
+int logit_chunk_rows() {
+    static const int rows = [] {
+        const char* e = getenv("TVQ_LOGIT_CHUNK_ROWS");
+        if (!e) return 256;
+        const int v = atoi(e);
+        return (v >= 0 && v % 128 == 0) ? v : 256;
+    }();
+    return rows;
+}
 
 // The transformer blocks on s.x (in place), enqueued on s.st.
 int enqueue_layers(Session& s, bool calibrating) {
@@ -290,8 +313,30 @@ int enqueue_layers(Session& s, bool calibrating) {
     return TVQ_OK;
 }
 
-// The forward pass for the prepared layout, enqueued on s.st.
-int enqueue_forward(Session& s, bool calibrating) {
+// Tied LM head on rows [r0, r0 + rows) of the split ln_f output, fp32 on the
+// FP16 tensor cores with split precision (gpt2_ref.tkv:589-610): logits[r0:]
+// of the same rows.  Rows are independent, so a chunk's logits are the
+// same bits as those of a launch over all rows.
+int launch_lm_head(Session& s, int r0, int rows, cudaStream_t st) {
+    GemmArgs g;
+    g.kind = GEMM_F16X3;
+    g.A = s.xf_hi + static_cast<size_t>(r0) * s.d;
+    g.A2 = s.xf_lo + static_cast<size_t>(r0) * s.d;
+    g.W = s.wte_hi;
+    g.W2 = s.wte_lo;
+    g.scale_a = s.xf_rs + r0;
+    g.scales_w = s.wte_rs;
+    g.Y = s.logits + static_cast<size_t>(r0) * s.vocab;
+    g.m = rows;
+    g.n = s.vocab;
+    g.k = s.d;
+    g.per_channel = 0;
+    return launch_gemm(g, st);
+}
+
+// The forward pass for the prepared layout, enqueued on s.st (without the LM
+// head for M_BODY).
+int enqueue_forward(Session& s, bool calibrating, bool lm_head = true) {
     const int T = s.T, d = s.d;
     STEP(mark(s, -1));
     STEP(launch_embed(s.ids, s.tok_start, s.wte, s.wpe, s.x, T, d, s.vocab, s.max_pos, s.err, s.st));
@@ -310,24 +355,10 @@ int enqueue_forward(Session& s, bool calibrating) {
         STEP(launch_layernorm_split(s.x, s.lnf_g, s.lnf_b, s.xf_hi, s.xf_lo, s.xf_rs, T, d, s.eps, s.st));
         STEP(mark(s, ST_LN));
     }
-    // tied LM head, fp32 on the FP16 tensor cores with split precision
-    {
-        GemmArgs g;
-        g.kind = GEMM_F16X3;
-        g.A = s.xf_hi;
-        g.A2 = s.xf_lo;
-        g.W = s.wte_hi;
-        g.W2 = s.wte_lo;
-        g.scale_a = s.xf_rs;
-        g.scales_w = s.wte_rs;
-        g.Y = s.logits;
-        g.m = rows;
-        g.n = s.vocab;
-        g.k = d;
-        g.per_channel = 0;
-        STEP(launch_gemm(g, s.st));
+    if (lm_head) {
+        STEP(launch_lm_head(s, 0, rows, s.st));
+        STEP(mark(s, ST_LM_HEAD));
     }
-    STEP(mark(s, ST_LM_HEAD));
     TVQ_CUDA(cudaGetLastError());
     return TVQ_OK;
 }
@@ -370,8 +401,8 @@ int capture(Session& s, int mode) {
     TVQ_CUDA(cudaStreamBeginCapture(s.st, cudaStreamCaptureModeRelaxed));
     s.capturing = true;
     int rc = TVQ_OK;
-    if (mode == M_FORWARD) {
-        rc = enqueue_forward(s, false);
+    if (mode == M_FORWARD || mode == M_BODY) {
+        rc = enqueue_forward(s, false, mode == M_FORWARD);
     } else {
         rc = mark(s, -1);
         if (!rc && mode == M_LAYERS_DYNAMIC) {  // calibrate_minmax on this call's activations only
@@ -759,13 +790,49 @@ int tvq_session_forward(int64_t handle, const int64_t* ids, int ids_on_device, f
     STEP(check_ready(*S));
     const size_t out_elems = static_cast<size_t>(S->logits_rows()) * S->vocab;
     TVQ_CHECK(!logits || logits_len >= static_cast<int64_t>(out_elems), TVQ_ERR_SIZE, "logits buffer too small");
-    if (!S->gexec[M_FORWARD]) STEP(capture(*S, M_FORWARD));
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : S->st;
+    const int chunk_rows = logit_chunk_rows();
+    if (logits && !logits_on_device && S->logits_mode == 0 && chunk_rows > 0 && S->T >= 2 * chunk_rows &&
+        !S->profile) {
+        // all logits to the host: the LM head runs in row chunks after the
+        // captured body, and each chunk's rows are copied out on a second
+        // stream while the next chunk computes (the copy, not the GEMM,
+        // bounds this call)
+        if (!S->gexec[M_BODY]) STEP(capture(*S, M_BODY));
+        const int nch = (S->T + chunk_rows - 1) / chunk_rows;
+        if (!S->cp) TVQ_CUDA(cudaStreamCreateWithFlags(&S->cp, cudaStreamNonBlocking));
+        if (!S->copies_done) TVQ_CUDA(cudaEventCreateWithFlags(&S->copies_done, cudaEventDisableTiming));
+        while (static_cast<int>(S->chunk_ev.size()) < nch) {
+            cudaEvent_t e = nullptr;
+            TVQ_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+            S->chunk_ev.push_back(e);
+        }
+        if (ids)
+            TVQ_CUDA(cudaMemcpyAsync(S->ids, ids, sizeof(int64_t) * S->T,
+                                     ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+        TVQ_CUDA(cudaGraphLaunch(S->gexec[M_BODY], st));
+        for (int c = 0; c < nch; c++) {
+            const int r0 = c * chunk_rows, rows = std::min(S->T - r0, chunk_rows);
+            STEP(launch_lm_head(*S, r0, rows, st));
+            TVQ_CUDA(cudaEventRecord(S->chunk_ev[c], st));
+            TVQ_CUDA(cudaStreamWaitEvent(S->cp, S->chunk_ev[c], 0));
+            const size_t off = static_cast<size_t>(r0) * S->vocab;
+            TVQ_CUDA(cudaMemcpyAsync(logits + off, S->logits + off, static_cast<size_t>(rows) * S->vocab * sizeof(float),
+                                     cudaMemcpyDeviceToHost, S->cp));
+        }
+        TVQ_CUDA(cudaEventRecord(S->copies_done, S->cp));
+        TVQ_CUDA(cudaStreamWaitEvent(st, S->copies_done, 0));
+        S->last_mode = M_BODY;
+        S->extra_launches = nch;
+        return check_err(*S, st);
+    }
+    if (!S->gexec[M_FORWARD]) STEP(capture(*S, M_FORWARD));
     if (ids)
         TVQ_CUDA(cudaMemcpyAsync(S->ids, ids, sizeof(int64_t) * S->T,
                                  ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
     TVQ_CUDA(cudaGraphLaunch(S->gexec[M_FORWARD], st));
     S->last_mode = M_FORWARD;
+    S->extra_launches = 0;
     if (logits)
         TVQ_CUDA(cudaMemcpyAsync(logits, S->logits, out_elems * sizeof(float),
                                  logits_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
@@ -785,6 +852,7 @@ int tvq_session_run_layers(int64_t handle, const float* x, int x_on_device, floa
     if (x) TVQ_CUDA(cudaMemcpyAsync(S->x, x, bytes, x_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
     TVQ_CUDA(cudaGraphLaunch(S->gexec[mode], st));
     S->last_mode = mode;
+    S->extra_launches = 0;
     if (y) TVQ_CUDA(cudaMemcpyAsync(y, S->x, bytes, y_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
     if ((x && !x_on_device) || (y && !y_on_device)) return check_err(*S, st);
     return TVQ_OK;
@@ -832,7 +900,7 @@ int tvq_session_launches(int64_t handle, int64_t* kernels) {
     TVQ_CHECK(kernels, TVQ_ERR_INVALID, "null output pointer");
     TVQ_CHECK(S->last_mode >= 0 && S->gexec[S->last_mode], TVQ_ERR_INVALID,
               "no forward has been captured for this layout");
-    *kernels = S->graph_kernels[S->last_mode];
+    *kernels = S->graph_kernels[S->last_mode] + S->extra_launches;
     return TVQ_OK;
 }
 
