@@ -76,7 +76,7 @@ def gemm_work(T=SEQ, d=768, ffn=3072):
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one gemm_c_fc launch in
 # the forward, from ncu (profiles/gemm_i8_gpt2_124m.md)
-GEMM_CFC_TRAFFIC = 3239936
+GEMM_CFC_TRAFFIC = 3241216
 
 
 def attention_roofline(per_stage_ms, bf16, src, n_layers, T=SEQ, hd=64, heads=12):
