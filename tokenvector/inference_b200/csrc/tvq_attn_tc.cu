@@ -25,7 +25,11 @@
 // double-buffered, as the A operand of P V, so the softmax of block j never
 // waits for P V of block j-1.
 //
-// One CTA = one (128-query tile, head, key range) work item; 384 threads:
+// Persistent: one CTA per SM works through (128-query tile, head, key range)
+// units, units sorted longest first and dealt to the CTAs in snake order;
+// the rings and TMEM buffers run on per-CTA block counts across units, and
+// the Q tile is reloaded once the previous unit's S products have read it.
+// 384 threads:
 //   warp 0      TMA producer (Q, then K blocks)
 //   warp 1      MMA issuer for S_j = Q K_j^T into TMEM S[j&1] (M 128, N 64,
 //               K 64)
@@ -96,7 +100,8 @@ enum : int {
     DEVERR_ATTN_K_EMPTY = 31, DEVERR_ATTN_V_EMPTY = 32, DEVERR_ATTN_TMA_DRAIN = 33,
     DEVERR_ATTN_Q_FULL = 41, DEVERR_ATTN_K_FULL = 42, DEVERR_ATTN_S_EMPTY = 43, DEVERR_ATTN_P_FULL = 44,
     DEVERR_ATTN_O_EMPTY = 45, DEVERR_ATTN_V_FULL = 46, DEVERR_ATTN_MMA_DRAIN = 47,
-    DEVERR_ATTN_S_FULL = 51, DEVERR_ATTN_XCH = 52, DEVERR_ATTN_O_FULL = 53, DEVERR_ATTN_LXCH = 55
+    DEVERR_ATTN_S_FULL = 51, DEVERR_ATTN_XCH = 52, DEVERR_ATTN_O_FULL = 53, DEVERR_ATTN_LXCH = 55,
+    DEVERR_ATTN_Q_EMPTY = 34
 };
 
 // D[tmem] (+)= A[tmem] * B^T for FP16 operands, A read from tensor memory
@@ -252,7 +257,41 @@ struct AttnParams {
     int* counters;     // per (entry, head): partials counted in (0 between launches)
     const int* kv_exp; // [3 * nheads]: Q, K and V head scales 2^kv_exp of the split operands
     int* err;
+    int nunits;        // work units: (item, head) = (u / nheads, u % nheads), items longest first
 };
+
+// Unit k of this CTA: rounds of gridDim.x units in snake order (CTA c takes
+// c in even rounds, gridDim.x - 1 - c in odd ones), so that with units
+// sorted longest first every CTA's total stays within about one unit of the
+// others.
+__device__ __forceinline__ int unit_of(int k) {
+    const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
+    return k * G + ((k & 1) ? (G - 1 - c) : c);
+}
+
+// One work unit: query tile [q0, q0 + 128) of the sequence ending at s1, keys
+// [kb, ke) (blocks from kb rounded down to 8 keys, 16 bytes of fp16: the TMA
+// rule for the V^T key coordinate; keys below kb are masked), partial slot
+// (or -1) and merge entry, head.
+struct Unit {
+    int q0, s1, kb, ke, part, entry, kb_al, nkb, head;
+};
+
+__device__ __forceinline__ Unit load_unit(const AttnParams& p, int u) {
+    Unit w;
+    const int item = u / p.nheads;
+    w.head = u - item * p.nheads;
+    const int4 tl = __ldg(p.tiles + item), sp = __ldg(p.split + item);
+    w.q0 = tl.x;
+    w.s1 = tl.z;
+    w.kb = sp.x;
+    w.ke = sp.y;
+    w.part = sp.z;
+    w.entry = sp.w;
+    w.kb_al = w.kb & ~7;
+    w.nkb = (w.ke - w.kb_al + TK - 1) / TK;
+    return w;
+}
 
 // Byte offset of the 16-byte chunk (row r, chunk c of its 128-byte row) in
 // a tile of 128-byte rows with the 128-byte swizzle (chunk ^= row % 8).
@@ -284,19 +323,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint64_t* xch = bars + 21;         // [4 lane groups][2 parities]: row-max exchange
     uint64_t* lxch = bars + 29;        // [4]: row-sum exchange
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 33);
+    uint64_t* q_empty = bars + 34;     // the S products of a unit have read its Q tile
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int item = blockIdx.x / p.nheads;
-    const int head = blockIdx.x % p.nheads;
-    const int4 tl = p.tiles[item];
-    const int q0 = tl.x, s1 = tl.z;
-    const int4 sp = p.split[item];
-    const int kb = sp.x, ke = sp.y, part = sp.z;
-    // blocks start at kb rounded down to 8 keys (16 bytes of fp16, the TMA
-    // rule for the V^T key coordinate); keys below kb are masked
-    const int kb_al = kb & ~7;
-    const int nkb = (ke - kb_al + TK - 1) / TK;
 
     if (threadIdx.x == 0) {
         for (int b = 0; b < 2; b++) {
@@ -311,6 +341,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mbar_init(&o_empty[b], 8);
         }
         mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
         mbar_init(&drain[0], 1);
         mbar_init(&drain[1], 1);
         for (int i = 0; i < 8; i++) mbar_init(&xch[i], 2);
@@ -338,72 +369,96 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
-            // the query tile (rows past the sequence only feed rows that are
-            // never written; rows past T read as 0)
-            mbar_arrive_expect_tx(q_full, 2 * QPART);
-            tma_load_2d(&tmQh, q_full, sm + OFF_QH, head * HD, q0);
-            tma_load_2d(&tmQl, q_full, sm + OFF_QL, head * HD, q0);
-            int kissued = 0;
-            for (int j = 0; j < nkb; j++) {
-                const int s = j & 1;
-                const uint32_t ph = ((j >> 1) & 1) ^ 1;
-                const int key = kb_al + j * TK;  // a multiple of 8
-                if (!mbar_wait(&k_empty[s], ph, p.err, DEVERR_ATTN_K_EMPTY)) break;
-                mbar_arrive_expect_tx(&k_full[s], KSTAGE);
-                uint8_t* ks = sm + OFF_K + s * KSTAGE;
-                tma_load_2d(&tmKh, &k_full[s], ks, head * HD, key);
-                tma_load_2d(&tmKl, &k_full[s], ks + PART, head * HD, key);
-                kissued = j + 1;
+            int gk = 0, nq = 0;  // K blocks and Q tiles issued so far (all units)
+            bool ok = true;
+            for (int k = 0; ok; k++) {
+                const int u = unit_of(k);
+                if (u >= p.nunits) break;
+                const Unit w = load_unit(p, u);
+                // the query tile (rows past the sequence only feed rows that
+                // are never written; rows past T read as 0), once the previous
+                // unit's S products are done with the buffer
+                if (k > 0 && !mbar_wait(q_empty, (k - 1) & 1, p.err, DEVERR_ATTN_Q_EMPTY)) break;
+                mbar_arrive_expect_tx(q_full, 2 * QPART);
+                tma_load_2d(&tmQh, q_full, sm + OFF_QH, w.head * HD, w.q0);
+                tma_load_2d(&tmQl, q_full, sm + OFF_QL, w.head * HD, w.q0);
+                nq++;
+                for (int j = 0; j < w.nkb; j++, gk++) {
+                    const int s = gk & 1;
+                    const uint32_t ph = ((gk >> 1) & 1) ^ 1;
+                    const int key = w.kb_al + j * TK;  // a multiple of 8
+                    if (!mbar_wait(&k_empty[s], ph, p.err, DEVERR_ATTN_K_EMPTY)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&k_full[s], KSTAGE);
+                    uint8_t* ks = sm + OFF_K + s * KSTAGE;
+                    tma_load_2d(&tmKh, &k_full[s], ks, w.head * HD, key);
+                    tma_load_2d(&tmKl, &k_full[s], ks + PART, w.head * HD, key);
+                }
             }
             // every issued load lands before the CTA may exit
-            mbar_wait(q_full, 0, p.err, DEVERR_ATTN_TMA_DRAIN);
-            for (int j = kissued > 2 ? kissued - 2 : 0; j < kissued; j++)
-                mbar_wait(&k_full[j & 1], (j >> 1) & 1, p.err, DEVERR_ATTN_TMA_DRAIN);
+            if (nq > 0) mbar_wait(q_full, (nq - 1) & 1, p.err, DEVERR_ATTN_TMA_DRAIN);
+            for (int g2 = gk > 2 ? gk - 2 : 0; g2 < gk; g2++)
+                mbar_wait(&k_full[g2 & 1], (g2 >> 1) & 1, p.err, DEVERR_ATTN_TMA_DRAIN);
         }
     } else if (warp == 2) {
         // ------------------------------------------------ TMA producer of V^T
         // (its own thread: K blocks run ahead of the PV products)
         if (lane == 0) {
-            int vissued = 0;
-            for (int j = 0; j < nkb; j++) {
-                const int s = j & 1;
-                const uint32_t ph = ((j >> 1) & 1) ^ 1;
-                const int key = kb_al + j * TK;
-                if (!mbar_wait(&v_empty[s], ph, p.err, DEVERR_ATTN_V_EMPTY)) break;
-                mbar_arrive_expect_tx(&v_full[s], KSTAGE);
-                uint8_t* vs = sm + OFF_V + s * KSTAGE;
-                tma_load_2d(&tmVh, &v_full[s], vs, key, head * HD);
-                tma_load_2d(&tmVl, &v_full[s], vs + PART, key, head * HD);
-                vissued = j + 1;
+            int gv = 0;  // V blocks issued so far (all units)
+            bool ok = true;
+            for (int k = 0; ok; k++) {
+                const int u = unit_of(k);
+                if (u >= p.nunits) break;
+                const Unit w = load_unit(p, u);
+                for (int j = 0; j < w.nkb; j++, gv++) {
+                    const int s = gv & 1;
+                    const uint32_t ph = ((gv >> 1) & 1) ^ 1;
+                    const int key = w.kb_al + j * TK;
+                    if (!mbar_wait(&v_empty[s], ph, p.err, DEVERR_ATTN_V_EMPTY)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&v_full[s], KSTAGE);
+                    uint8_t* vs = sm + OFF_V + s * KSTAGE;
+                    tma_load_2d(&tmVh, &v_full[s], vs, key, w.head * HD);
+                    tma_load_2d(&tmVl, &v_full[s], vs + PART, key, w.head * HD);
+                }
             }
-            for (int j = vissued > 2 ? vissued - 2 : 0; j < vissued; j++)
-                mbar_wait(&v_full[j & 1], (j >> 1) & 1, p.err, DEVERR_ATTN_TMA_DRAIN);
+            for (int g2 = gv > 2 ? gv - 2 : 0; g2 < gv; g2++)
+                mbar_wait(&v_full[g2 & 1], (g2 >> 1) & 1, p.err, DEVERR_ATTN_TMA_DRAIN);
         }
     } else if (warp == 1) {
         // ------------------------------------------------ S issuer
         if (lane == 0) {
             const uint32_t sbase = smem_u32(sm);
-            bool ok = mbar_wait(q_full, 0, p.err, DEVERR_ATTN_Q_FULL);
-            for (int j = 0; j < nkb && ok; j++) {
-                const int b = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
-                if (!mbar_wait(&k_full[b], ph, p.err, DEVERR_ATTN_K_FULL)) break;
-                if (!mbar_wait(&s_empty[b], ph ^ 1, p.err, DEVERR_ATTN_S_EMPTY)) break;
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + COL_S + b * 64;
-                const uint32_t kbs = sbase + OFF_K + b * KSTAGE;
+            int gs = 0;  // S blocks issued so far (all units)
+            bool ok = true;
+            for (int k = 0; ok; k++) {
+                const int u = unit_of(k);
+                if (u >= p.nunits) break;
+                const int nkb = load_unit(p, u).nkb;
+                if (!mbar_wait(q_full, k & 1, p.err, DEVERR_ATTN_Q_FULL)) break;
+                for (int j = 0; j < nkb; j++, gs++) {
+                    const int b = gs & 1;
+                    const uint32_t ph = (gs >> 1) & 1;
+                    if (!mbar_wait(&k_full[b], ph, p.err, DEVERR_ATTN_K_FULL) ||
+                        !mbar_wait(&s_empty[b], ph ^ 1, p.err, DEVERR_ATTN_S_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + COL_S + b * 64;
+                    const uint32_t kbs = sbase + OFF_K + b * KSTAGE;
 #pragma unroll
-                for (int kk = 0; kk < 4; kk++) {  // 16 head columns (32 bytes) per instruction
-                    const uint64_t qh = smem_desc_k_sw128(sbase + OFF_QH + kk * 32);
-                    const uint64_t ql = smem_desc_k_sw128(sbase + OFF_QL + kk * 32);
-                    const uint64_t kh = smem_desc_k_sw128(kbs + kk * 32);
-                    const uint64_t kl = smem_desc_k_sw128(kbs + PART + kk * 32);
-                    umma_f16(d_tmem, ql, kh, IDESC, kk ? 1u : 0u);
-                    umma_f16(d_tmem, qh, kl, IDESC, 1u);
-                    umma_f16(d_tmem, qh, kh, IDESC, 1u);
+                    for (int kk = 0; kk < 4; kk++) {  // 16 head columns (32 bytes) per instruction
+                        const uint64_t qh = smem_desc_k_sw128(sbase + OFF_QH + kk * 32);
+                        const uint64_t ql = smem_desc_k_sw128(sbase + OFF_QL + kk * 32);
+                        const uint64_t kh = smem_desc_k_sw128(kbs + kk * 32);
+                        const uint64_t kl = smem_desc_k_sw128(kbs + PART + kk * 32);
+                        umma_f16(d_tmem, ql, kh, IDESC, kk ? 1u : 0u);
+                        umma_f16(d_tmem, qh, kl, IDESC, 1u);
+                        umma_f16(d_tmem, qh, kh, IDESC, 1u);
+                    }
+                    umma_commit(&s_full[b]);
+                    umma_commit(&k_empty[b]);
                 }
-                umma_commit(&s_full[b]);
-                umma_commit(&k_empty[b]);
+                if (ok) umma_commit(q_empty);  // the Q tile is free once these products complete
             }
             // all issued MMAs retire before TMEM is released
             umma_commit(&drain[0]);
@@ -413,27 +468,37 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // ------------------------------------------------ PV issuer
         if (lane == 0) {
             const uint32_t sbase = smem_u32(sm);
-            for (int i = 0; i < nkb; i++) {
-                const int b = i & 1;
-                const uint32_t ph = (i >> 1) & 1;
-                if (!mbar_wait(&p_full[b], ph, p.err, DEVERR_ATTN_P_FULL)) break;
-                if (!mbar_wait(&o_empty[b], ph ^ 1, p.err, DEVERR_ATTN_O_EMPTY)) break;
-                if (!mbar_wait(&v_full[b], ph, p.err, DEVERR_ATTN_V_FULL)) break;
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + COL_O + b * 64;
-                const uint32_t vb = sbase + OFF_V + b * KSTAGE;
-                const uint32_t pcol = tmem_base + COL_P + b * 64;  // hi: +0..31, lo: +32..63
+            int gp = 0;  // PV blocks issued so far (all units)
+            bool ok = true;
+            for (int k = 0; ok; k++) {
+                const int u = unit_of(k);
+                if (u >= p.nunits) break;
+                const int nkb = load_unit(p, u).nkb;
+                for (int i = 0; i < nkb; i++, gp++) {
+                    const int b = gp & 1;
+                    const uint32_t ph = (gp >> 1) & 1;
+                    if (!mbar_wait(&p_full[b], ph, p.err, DEVERR_ATTN_P_FULL) ||
+                        !mbar_wait(&o_empty[b], ph ^ 1, p.err, DEVERR_ATTN_O_EMPTY) ||
+                        !mbar_wait(&v_full[b], ph, p.err, DEVERR_ATTN_V_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + COL_O + b * 64;
+                    const uint32_t vb = sbase + OFF_V + b * KSTAGE;
+                    const uint32_t pcol = tmem_base + COL_P + b * 64;  // hi: +0..31, lo: +32..63
 #pragma unroll
-                for (int kk = 0; kk < 4; kk++) {  // 16 keys (32 bytes of V^T rows, 8 P columns) per instruction
-                    const uint64_t vh = smem_desc_k_sw128(vb + kk * 32);
-                    const uint64_t vl = smem_desc_k_sw128(vb + PART + kk * 32);
-                    const uint32_t pc = 8 * kk;
-                    umma_f16_ts(d_tmem, pcol + 32 + pc, vh, IDESC, kk ? 1u : 0u);
-                    umma_f16_ts(d_tmem, pcol + pc, vl, IDESC, 1u);
-                    umma_f16_ts(d_tmem, pcol + pc, vh, IDESC, 1u);
+                    for (int kk = 0; kk < 4; kk++) {  // 16 keys (32 bytes of V^T rows, 8 P columns) per instruction
+                        const uint64_t vh = smem_desc_k_sw128(vb + kk * 32);
+                        const uint64_t vl = smem_desc_k_sw128(vb + PART + kk * 32);
+                        const uint32_t pc = 8 * kk;
+                        umma_f16_ts(d_tmem, pcol + 32 + pc, vh, IDESC, kk ? 1u : 0u);
+                        umma_f16_ts(d_tmem, pcol + pc, vl, IDESC, 1u);
+                        umma_f16_ts(d_tmem, pcol + pc, vh, IDESC, 1u);
+                    }
+                    umma_commit(&o_full[b]);   // PV_i in O[b]; P[b] free again
+                    umma_commit(&v_empty[b]);
                 }
-                umma_commit(&o_full[b]);   // PV_i in O[b]; P[b] free again
-                umma_commit(&v_empty[b]);
             }
             umma_commit(&drain[1]);
             mbar_wait(&drain[1], 0, p.err, DEVERR_ATTN_MMA_DRAIN);
@@ -443,249 +508,266 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int g = warp & 3;          // TMEM lane group
         const int h = (warp - 4) >> 2;   // key half of each block, output half
         const int r = 32 * g + lane;     // query row of the tile = TMEM lane
-        const int q = q0 + r;
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(32 * g) << 16);
         bool alive = true;
-        // 1 / scale of the int8 output, early (its load and f64 quotient stay
-        // off the tail of the CTA)
+        // 1 / scale of the int8 output, once per CTA
         InvScale qs{0.0, 0.0f, 0.0f};
         if (p.outq) qs = make_inv_scale(static_cast<double>(__ldg(p.qscale)));
-        // scores: S = acc 2^-(sq + sk) exactly, times log2(e) / sqrt(hd)
-        const int sq = p.kv_exp[head], sk = p.kv_exp[p.nheads + head], sv = p.kv_exp[2 * p.nheads + head];
-        const float xs = p.scale2 * exp2i(-sq) * exp2i(-sk);
-        float o[32];
+        int gj = 0;  // blocks processed so far (all units)
+        for (int k = 0; alive; k++) {
+            const int u = unit_of(k);
+            if (u >= p.nunits) break;
+            const Unit w = load_unit(p, u);
+            const int head = w.head, q0 = w.q0, s1 = w.s1, kb = w.kb, ke = w.ke, part = w.part;
+            const int kb_al = w.kb_al, nkb = w.nkb;
+            const int q = q0 + r;
+            // scores: S = acc 2^-(sq + sk) exactly, times log2(e) / sqrt(hd)
+            const int sq = __ldg(p.kv_exp + head), sk = __ldg(p.kv_exp + p.nheads + head),
+                      sv = __ldg(p.kv_exp + 2 * p.nheads + head);
+            const float xs = p.scale2 * exp2i(-sq) * exp2i(-sk);
+            float o[32];
 #pragma unroll
-        for (int c = 0; c < 32; c++) o[c] = 0.0f;
-        float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
-        for (int j = 0; j < nkb; j++) {
-            const int b = j & 1;
-            const uint32_t ph = (j >> 1) & 1;
-            bool got = mbar_wait(&s_full[b], ph, p.err, DEVERR_ATTN_S_FULL);
-            if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
-            tc_fence_after();
-            uint32_t sr[32];
-            tmem_ld32(lane_base + COL_S + b * 64 + 32 * h, sr);
-            tmem_ld_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_empty[b]);
-            // causal + key-range mask, scale to base 2: key k0 + c is visible
-            // for lo <= c <= hi
-            const int k0 = kb_al + j * TK + 32 * h;
-            const int lo = kb - k0, hi = min(q, ke - 1) - k0;
-            uint64_t x2[16];  // the scaled scores, two keys per register pair (f32x2)
-            float mx = -INFINITY, mx2 = -INFINITY;
-            if (lo <= 0 && hi >= 31) {  // every key of the half visible: most blocks
-                const uint64_t XS = f2_pack(xs, xs);
-#pragma unroll
-                for (int c = 0; c < 32; c += 2) {
-                    x2[c / 2] = f2_mul(f2_pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), XS);
-                    float a, bq;
-                    f2_unpack(x2[c / 2], a, bq);
-                    mx = fmaxf(mx, a);
-                    mx2 = fmaxf(mx2, bq);
-                }
-            } else {
-#pragma unroll
-                for (int c = 0; c < 32; c += 2) {
-                    const float a = (c >= lo && c <= hi) ? __fmul_rn(__uint_as_float(sr[c]), xs) : -INFINITY;
-                    const float bq = (c + 1 >= lo && c + 1 <= hi) ? __fmul_rn(__uint_as_float(sr[c + 1]), xs) : -INFINITY;
-                    x2[c / 2] = f2_pack(a, bq);
-                    mx = fmaxf(mx, a);
-                    mx2 = fmaxf(mx2, bq);
-                }
-            }
-            mx = fmaxf(mx, mx2);
-            // row max over both halves: exchange with the partner warp
-            red[(b * 2 + h) * TQ + r] = mx;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&xch[g * 2 + b]);
-            got = mbar_wait(&xch[g * 2 + b], ph, p.err, DEVERR_ATTN_XCH);
-            if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
-            mx = fmaxf(mx, red[(b * 2 + (h ^ 1)) * TQ + r]);
-            const float mnew = fmaxf(m, mx);
-            const float mref = (mnew == -INFINITY) ? 0.0f : mnew;  // a row with no visible key yet stays empty
-            const float alpha = ex2_approx(m - mref);
-            // P_j = 2^(x - m + 14) in (0, 2^14] (l and O are kept in units of
-            // 2^14) as fp16 hi + lo (|error| <= max(2^-22 P, 2^-25)) into
-            // P[b]; P[b] was last read by PV_{j-2}, whose completion the
-            // previous iteration already waited for
-            const uint64_t M14 = f2_pack(mref - 14.0f, mref - 14.0f);
-            uint32_t phi[16], plo[16];
-            uint64_t acc2[2] = {0ull, 0ull};  // (+0, +0) pairs
-#pragma unroll
-            for (int c = 0; c < 32; c += 2) {
-                float d0, d1;
-                f2_unpack(f2_sub(x2[c / 2], M14), d0, d1);
-                const float e0 = ex2_approx(d0), e1 = ex2_approx(d1);
-                const uint64_t E = f2_pack(e0, e1);
-                acc2[(c >> 1) & 1] = f2_add(acc2[(c >> 1) & 1], E);
-                split_p2x(E, e0, e1, phi[c / 2], plo[c / 2]);
-            }
-            float s0, s1, s2, s3;
-            f2_unpack(acc2[0], s0, s1);
-            f2_unpack(acc2[1], s2, s3);
-            const float sum = (s0 + s1) + (s2 + s3);
-            tmem_st16(lane_base + COL_P + b * 64 + 16 * h, phi);
-            tmem_st16(lane_base + COL_P + b * 64 + 32 + 16 * h, plo);
-            l = fmaf(l, alpha, sum);
-            m = mnew;
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[b]);
-            // fold PV_{j-1} into the register accumulator
-            if (j >= 1) {
-                const int bp = (j - 1) & 1;
-                got = mbar_wait(&o_full[bp], ((j - 1) >> 1) & 1, p.err, DEVERR_ATTN_O_FULL);
+            for (int c = 0; c < 32; c++) o[c] = 0.0f;
+            float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
+            for (int j = 0; j < nkb; j++) {
+                const int gb = gj + j;  // this CTA's block count: the ring and TMEM buffer phases
+                const int b = gb & 1;
+                const uint32_t ph = (gb >> 1) & 1;
+                bool got = mbar_wait(&s_full[b], ph, p.err, DEVERR_ATTN_S_FULL);
                 if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
                 tc_fence_after();
-                uint32_t pv[32];
-                tmem_ld32(lane_base + COL_O + bp * 64 + 32 * h, pv);
+                uint32_t sr[32];
+                tmem_ld32(lane_base + COL_S + b * 64 + 32 * h, sr);
                 tmem_ld_wait();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&o_empty[bp]);
+                if (lane == 0) mbar_arrive(&s_empty[b]);
+                // causal + key-range mask, scale to base 2: key k0 + c is visible
+                // for lo <= c <= hi
+                const int k0 = kb_al + j * TK + 32 * h;
+                const int lo = kb - k0, hi = min(q, ke - 1) - k0;
+                uint64_t x2[16];  // the scaled scores, two keys per register pair (f32x2)
+                float mx = -INFINITY, mx2 = -INFINITY;
+                if (lo <= 0 && hi >= 31) {  // every key of the half visible: most blocks
+                    const uint64_t XS = f2_pack(xs, xs);
 #pragma unroll
-                for (int c = 0; c < 32; c++) o[c] = fmaf(o[c], alpha_prev, __uint_as_float(pv[c]));
-            }
-            alpha_prev = alpha;
-        }
-        if (alive) {
-            const int bp = (nkb - 1) & 1;
-            const bool got = mbar_wait(&o_full[bp], ((nkb - 1) >> 1) & 1, p.err, DEVERR_ATTN_O_FULL);
-            alive = __all_sync(0xffffffffu, got);
-            if (alive) {
-                tc_fence_after();
-                uint32_t pv[32];
-                tmem_ld32(lane_base + COL_O + bp * 64 + 32 * h, pv);
-                tmem_ld_wait();
+                    for (int c = 0; c < 32; c += 2) {
+                        x2[c / 2] = f2_mul(f2_pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), XS);
+                        float a, bq;
+                        f2_unpack(x2[c / 2], a, bq);
+                        mx = fmaxf(mx, a);
+                        mx2 = fmaxf(mx2, bq);
+                    }
+                } else {
 #pragma unroll
-                for (int c = 0; c < 32; c++) o[c] = fmaf(o[c], alpha_prev, __uint_as_float(pv[c]));
-            }
-        }
-        // O was summed in units of 2^(14 + sv): back to the true scale (exact)
-#pragma unroll
-        for (int c = 0; c < 32; c++) o[c] = o[c] * exp2i(-sv);  // O and l both in units of 2^14 from here
-        if (alive) {  // row sum over both halves
-            lsum[h * TQ + r] = l;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&lxch[g]);
-            const bool got = mbar_wait(&lxch[g], 0, p.err, DEVERR_ATTN_LXCH);
-            alive = __all_sync(0xffffffffu, got);
-            if (alive) l += lsum[(h ^ 1) * TQ + r];
-        }
-        // Key-chunk items: write the unnormalised partial (O, m, l); the CTA
-        // that completes the set merges them (the last to count in).
-        bool write_out = part < 0;
-        bool merged = false;
-        if (part >= 0) {
-            if (alive) {
-                const int64_t slot = static_cast<int64_t>(part) * p.nheads + head;
-                float4* dst = reinterpret_cast<float4*>(p.part_o + (slot * TQ + r) * HD + 32 * h);
-#pragma unroll
-                for (int c4 = 0; c4 < 8; c4++)
-                    dst[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
-                if (h == 0) p.part_ml[slot * TQ + r] = make_float2(m, l);
-            }
-            __threadfence();
-            named_bar_sync(1, 256);  // all eight softmax warps wrote their part
-            int* last_flag = reinterpret_cast<int*>(lsum);  // lsum is free again (both halves read it)
-            if (threadIdx.x == 128) {
-                int* ctr = p.counters + static_cast<int64_t>(sp.w) * p.nheads + head;
-                const int prev = atomicAdd(ctr, 1);
-                const int last = (prev == p.comb[sp.w].w - 1) ? 1 : 0;
-                if (last) *ctr = 0;  // every other part has counted in: ready for the next launch
-                last_flag[TQ * 2 - 1] = last;
-            }
-            named_bar_sync(1, 256);
-            write_out = merged = last_flag[TQ * 2 - 1] != 0;
-            if (merged) __threadfence();  // the other CTAs' partials are visible from here
-        }
-        if (write_out && alive) {
-            float am = 0.0f;
-            if (merged) {
-                // m = max m_c, l = sum l_c 2^(m_c - m), O = sum O_c 2^(m_c - m) / l, in slot order
-                const int4 ce = p.comb[sp.w];  // {q0, seq end, first slot, count}
-                float mm = -INFINITY;
-                for (int k = 0; k < ce.w; k++) {
-                    const int slot_k = ce.z + k;
-                    const float mk = (slot_k == part)
-                                         ? m
-                                         : p.part_ml[(static_cast<int64_t>(slot_k) * p.nheads + head) * TQ + r].x;
-                    mm = fmaxf(mm, mk);
-                }
-                float lt = 0.0f, acc[32];
-#pragma unroll
-                for (int c = 0; c < 32; c++) acc[c] = 0.0f;
-                for (int k = 0; k < ce.w; k++) {
-                    const int slot_k = ce.z + k;
-                    const int64_t sl = static_cast<int64_t>(slot_k) * p.nheads + head;
-                    const float2 ml = (slot_k == part) ? make_float2(m, l) : p.part_ml[sl * TQ + r];
-                    const float wgt = (ml.x == -INFINITY) ? 0.0f : exp2f(ml.x - mm);
-                    lt = fmaf(ml.y, wgt, lt);
-                    if (slot_k == part) {
-#pragma unroll
-                        for (int c = 0; c < 32; c++) acc[c] = fmaf(o[c], wgt, acc[c]);
-                    } else {
-                        const float4* src = reinterpret_cast<const float4*>(p.part_o + (sl * TQ + r) * HD + 32 * h);
-#pragma unroll
-                        for (int c4 = 0; c4 < 8; c4++) {
-                            const float4 v = src[c4];
-                            acc[4 * c4] = fmaf(v.x, wgt, acc[4 * c4]);
-                            acc[4 * c4 + 1] = fmaf(v.y, wgt, acc[4 * c4 + 1]);
-                            acc[4 * c4 + 2] = fmaf(v.z, wgt, acc[4 * c4 + 2]);
-                            acc[4 * c4 + 3] = fmaf(v.w, wgt, acc[4 * c4 + 3]);
-                        }
+                    for (int c = 0; c < 32; c += 2) {
+                        const float a = (c >= lo && c <= hi) ? __fmul_rn(__uint_as_float(sr[c]), xs) : -INFINITY;
+                        const float bq = (c + 1 >= lo && c + 1 <= hi) ? __fmul_rn(__uint_as_float(sr[c + 1]), xs) : -INFINITY;
+                        x2[c / 2] = f2_pack(a, bq);
+                        mx = fmaxf(mx, a);
+                        mx2 = fmaxf(mx2, bq);
                     }
                 }
-                const float il = 1.0f / lt;
+                mx = fmaxf(mx, mx2);
+                // row max over both halves: exchange with the partner warp
+                red[(b * 2 + h) * TQ + r] = mx;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&xch[g * 2 + b]);
+                got = mbar_wait(&xch[g * 2 + b], ph, p.err, DEVERR_ATTN_XCH);
+                if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
+                mx = fmaxf(mx, red[(b * 2 + (h ^ 1)) * TQ + r]);
+                const float mnew = fmaxf(m, mx);
+                const float mref = (mnew == -INFINITY) ? 0.0f : mnew;  // a row with no visible key yet stays empty
+                const float alpha = ex2_approx(m - mref);
+                // P_j = 2^(x - m + 14) in (0, 2^14] (l and O are kept in units of
+                // 2^14) as fp16 hi + lo (|error| <= max(2^-22 P, 2^-25)) into
+                // P[b]; P[b] was last read by PV_{j-2}, whose completion the
+                // previous iteration already waited for
+                const uint64_t M14 = f2_pack(mref - 14.0f, mref - 14.0f);
+                uint32_t phi[16], plo[16];
+                uint64_t acc2[2] = {0ull, 0ull};  // (+0, +0) pairs
 #pragma unroll
-                for (int c = 0; c < 32; c++) o[c] = acc[c] * il;
-            } else {
-                const float il = 1.0f / l;
+                for (int c = 0; c < 32; c += 2) {
+                    float d0, d1;
+                    f2_unpack(f2_sub(x2[c / 2], M14), d0, d1);
+                    const float e0 = ex2_approx(d0), e1 = ex2_approx(d1);
+                    const uint64_t E = f2_pack(e0, e1);
+                    acc2[(c >> 1) & 1] = f2_add(acc2[(c >> 1) & 1], E);
+                    split_p2x(E, e0, e1, phi[c / 2], plo[c / 2]);
+                }
+                float s0, s1, s2, s3;
+                f2_unpack(acc2[0], s0, s1);
+                f2_unpack(acc2[1], s2, s3);
+                const float sum = (s0 + s1) + (s2 + s3);
+                tmem_st16(lane_base + COL_P + b * 64 + 16 * h, phi);
+                tmem_st16(lane_base + COL_P + b * 64 + 32 + 16 * h, plo);
+                l = fmaf(l, alpha, sum);
+                m = mnew;
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[b]);
+                // fold PV_{j-1} into the register accumulator
+                if (j >= 1) {
+                    const int bp = (gb - 1) & 1;
+                    got = mbar_wait(&o_full[bp], ((gb - 1) >> 1) & 1, p.err, DEVERR_ATTN_O_FULL);
+                    if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
+                    tc_fence_after();
+                    uint32_t pv[32];
+                    tmem_ld32(lane_base + COL_O + bp * 64 + 32 * h, pv);
+                    tmem_ld_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&o_empty[bp]);
 #pragma unroll
-                for (int c = 0; c < 32; c++) o[c] = o[c] * il;
+                    for (int c = 0; c < 32; c++) o[c] = fmaf(o[c], alpha_prev, __uint_as_float(pv[c]));
+                }
+                alpha_prev = alpha;
             }
-            if (q < s1) {
-                const int64_t base = static_cast<int64_t>(q) * p.d + head * HD + 32 * h;
+            if (alive) {
+                const int gl = gj + nkb - 1;
+                const int bp = gl & 1;
+                const bool got = mbar_wait(&o_full[bp], (gl >> 1) & 1, p.err, DEVERR_ATTN_O_FULL);
+                alive = __all_sync(0xffffffffu, got);
+                if (alive) {
+                    tc_fence_after();
+                    uint32_t pv[32];
+                    tmem_ld32(lane_base + COL_O + bp * 64 + 32 * h, pv);
+                    tmem_ld_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&o_empty[bp]);  // the next unit's PV may reuse O[bp]
 #pragma unroll
-                for (int c = 0; c < 32; c++) am = fmaxf(am, fabsf(o[c]));
-                if (p.out) {
-                    float4* dst = reinterpret_cast<float4*>(p.out + base);
+                    for (int c = 0; c < 32; c++) o[c] = fmaf(o[c], alpha_prev, __uint_as_float(pv[c]));
+                }
+            }
+            gj += nkb;
+            // O was summed in units of 2^(14 + sv): back to the true scale (exact)
+#pragma unroll
+            for (int c = 0; c < 32; c++) o[c] = o[c] * exp2i(-sv);  // O and l both in units of 2^14 from here
+            if (alive) {  // row sum over both halves
+                lsum[h * TQ + r] = l;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&lxch[g]);
+                const bool got = mbar_wait(&lxch[g], k & 1, p.err, DEVERR_ATTN_LXCH);
+                alive = __all_sync(0xffffffffu, got);
+                if (alive) l += lsum[(h ^ 1) * TQ + r];
+            }
+            // Key-chunk items: write the unnormalised partial (O, m, l); the CTA
+            // that completes the set merges them (the last to count in).
+            bool write_out = part < 0;
+            bool merged = false;
+            if (part >= 0) {
+                if (alive) {
+                    const int64_t slot = static_cast<int64_t>(part) * p.nheads + head;
+                    float4* dst = reinterpret_cast<float4*>(p.part_o + (slot * TQ + r) * HD + 32 * h);
 #pragma unroll
                     for (int c4 = 0; c4 < 8; c4++)
                         dst[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
+                    if (h == 0) p.part_ml[slot * TQ + r] = make_float2(m, l);
                 }
-                if (p.outq) {
-                    // branch-free fast quantize of all 32, rare f64 fix-ups after
-                    union { int8_t b[32]; uint4 u[2]; } v;
-                    uint32_t bad = 0;
-#pragma unroll
-                    for (int c = 0; c < 32; c++) bad |= quant_fast(o[c], qs, v.b[c]) ? 0u : (1u << c);
-                    if (bad) {
-#pragma unroll
-                        for (int c = 0; c < 32; c++)
-                            if (bad & (1u << c)) v.b[c] = quant_exact(o[c], qs);
+                __threadfence();
+                named_bar_sync(1, 256);  // all eight softmax warps wrote their part
+                int* last_flag = reinterpret_cast<int*>(lsum);  // lsum is free again (both halves read it)
+                if (threadIdx.x == 128) {
+                    int* ctr = p.counters + static_cast<int64_t>(w.entry) * p.nheads + head;
+                    const int prev = atomicAdd(ctr, 1);
+                    const int last = (prev == p.comb[w.entry].w - 1) ? 1 : 0;
+                    if (last) *ctr = 0;  // every other part has counted in: ready for the next launch
+                    last_flag[TQ * 2 - 1] = last;
+                }
+                named_bar_sync(1, 256);
+                write_out = merged = last_flag[TQ * 2 - 1] != 0;
+                if (merged) __threadfence();  // the other CTAs' partials are visible from here
+            }
+            if (write_out && alive) {
+                float am = 0.0f;
+                if (merged) {
+                    // m = max m_c, l = sum l_c 2^(m_c - m), O = sum O_c 2^(m_c - m) / l, in slot order
+                    const int4 ce = p.comb[w.entry];  // {q0, seq end, first slot, count}
+                    float mm = -INFINITY;
+                    for (int t = 0; t < ce.w; t++) {
+                        const int slot_k = ce.z + t;
+                        const float mk = (slot_k == part)
+                                             ? m
+                                             : p.part_ml[(static_cast<int64_t>(slot_k) * p.nheads + head) * TQ + r].x;
+                        mm = fmaxf(mm, mk);
                     }
-                    if ((reinterpret_cast<uintptr_t>(p.outq + base) & 15) == 0) {
-                        uint4* dst = reinterpret_cast<uint4*>(p.outq + base);
-                        dst[0] = v.u[0];
-                        dst[1] = v.u[1];
-                    } else {
-                        uint32_t* dst = reinterpret_cast<uint32_t*>(p.outq + base);
+                    float lt = 0.0f, acc[32];
+#pragma unroll
+                    for (int c = 0; c < 32; c++) acc[c] = 0.0f;
+                    for (int t = 0; t < ce.w; t++) {
+                        const int slot_k = ce.z + t;
+                        const int64_t sl = static_cast<int64_t>(slot_k) * p.nheads + head;
+                        const float2 ml = (slot_k == part) ? make_float2(m, l) : p.part_ml[sl * TQ + r];
+                        const float wgt = (ml.x == -INFINITY) ? 0.0f : exp2f(ml.x - mm);
+                        lt = fmaf(ml.y, wgt, lt);
+                        if (slot_k == part) {
+#pragma unroll
+                            for (int c = 0; c < 32; c++) acc[c] = fmaf(o[c], wgt, acc[c]);
+                        } else {
+                            const float4* src = reinterpret_cast<const float4*>(p.part_o + (sl * TQ + r) * HD + 32 * h);
+#pragma unroll
+                            for (int c4 = 0; c4 < 8; c4++) {
+                                const float4 v = src[c4];
+                                acc[4 * c4] = fmaf(v.x, wgt, acc[4 * c4]);
+                                acc[4 * c4 + 1] = fmaf(v.y, wgt, acc[4 * c4 + 1]);
+                                acc[4 * c4 + 2] = fmaf(v.z, wgt, acc[4 * c4 + 2]);
+                                acc[4 * c4 + 3] = fmaf(v.w, wgt, acc[4 * c4 + 3]);
+                            }
+                        }
+                    }
+                    const float il = 1.0f / lt;
+#pragma unroll
+                    for (int c = 0; c < 32; c++) o[c] = acc[c] * il;
+                } else {
+                    const float il = 1.0f / l;
+#pragma unroll
+                    for (int c = 0; c < 32; c++) o[c] = o[c] * il;
+                }
+                if (q < s1) {
+                    const int64_t base = static_cast<int64_t>(q) * p.d + head * HD + 32 * h;
+#pragma unroll
+                    for (int c = 0; c < 32; c++) am = fmaxf(am, fabsf(o[c]));
+                    if (p.out) {
+                        float4* dst = reinterpret_cast<float4*>(p.out + base);
 #pragma unroll
                         for (int c4 = 0; c4 < 8; c4++)
-                            dst[c4] = (c4 & 3) == 0 ? v.u[c4 >> 2].x : (c4 & 3) == 1 ? v.u[c4 >> 2].y
-                                                   : (c4 & 3) == 2 ? v.u[c4 >> 2].z : v.u[c4 >> 2].w;
+                            dst[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
+                    }
+                    if (p.outq) {
+                        // branch-free fast quantize of all 32, rare f64 fix-ups after
+                        union { int8_t b[32]; uint4 u[2]; } v;
+                        uint32_t bad = 0;
+#pragma unroll
+                        for (int c = 0; c < 32; c++) bad |= quant_fast(o[c], qs, v.b[c]) ? 0u : (1u << c);
+                        if (bad) {
+#pragma unroll
+                            for (int c = 0; c < 32; c++)
+                                if (bad & (1u << c)) v.b[c] = quant_exact(o[c], qs);
+                        }
+                        if ((reinterpret_cast<uintptr_t>(p.outq + base) & 15) == 0) {
+                            uint4* dst = reinterpret_cast<uint4*>(p.outq + base);
+                            dst[0] = v.u[0];
+                            dst[1] = v.u[1];
+                        } else {
+                            uint32_t* dst = reinterpret_cast<uint32_t*>(p.outq + base);
+#pragma unroll
+                            for (int c4 = 0; c4 < 8; c4++)
+                                dst[c4] = (c4 & 3) == 0 ? v.u[c4 >> 2].x : (c4 & 3) == 1 ? v.u[c4 >> 2].y
+                                                       : (c4 & 3) == 2 ? v.u[c4 >> 2].z : v.u[c4 >> 2].w;
+                        }
                     }
                 }
-            }
-            if (p.amax) {
+                if (p.amax) {
 #pragma unroll
-                for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
-                if (lane == 0) atomicMax(p.amax, __float_as_uint(am));
+                    for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+                    if (lane == 0) atomicMax(p.amax, __float_as_uint(am));
+                }
             }
+            // the eight softmax warps leave the unit loop together (each unit
+            // then runs the same named barriers in every warp)
+            alive = named_bar_and(2, 256, alive);
         }
     }
 
@@ -820,9 +902,11 @@ int launch_attention_tc(const float* qkv, const void* qh, const void* ql, const 
     p.comb = comb;
     p.counters = counters;
     p.kv_exp = kv_exp;
+    p.nunits = nitems * nheads;
+    // persistent: one CTA per SM (all of TMEM) working through the units;
     // key-chunk partials are merged inside the kernel by the last CTA of each set
-    return launch_pdl(attention_tc_kernel, dim3(nitems * nheads), dim3(NTHREADS), SMEM_BYTES, st, mqh, mql, mkh, mkl,
-                      mvh, mvl,
+    const int grid = std::min(p.nunits, ds->sm_count);
+    return launch_pdl(attention_tc_kernel, dim3(grid), dim3(NTHREADS), SMEM_BYTES, st, mqh, mql, mkh, mkl, mvh, mvl,
                       p);
 }
 
