@@ -135,8 +135,11 @@ __device__ __forceinline__ float ulp_of(float y) {
 }
 
 // fl32(fl64(x * inv)) exactly: the scaled value that the FP8 quantizer hands
-// to the encoder's f32 parameter.  Same proof as epilogue_fast with
-// M = |x * inv|.
+// to the encoder's f32 parameter.  x * (hi + lo) is formed as ph + pl within
+// 2^-44 |x * inv| of the exact product; the f64 product differs from it by
+// at most one f64 ulp, so y = fl32(ph + pl) is fl32(fl64(x * inv)) unless
+// ph + pl lies within 2^-40 |ph| of a float midpoint (then, and for zero,
+// tiny, huge and non-finite values, the f64 product decides).
 static __device__ __noinline__ float mul_round_slow(float x, double inv) {
     return __double2float_rn(static_cast<double>(x) * inv);
 }
@@ -154,55 +157,6 @@ __device__ __forceinline__ float mul_round_exact(float x, const InvScale& s) {
     const bool ok = (ay >= 7.888609052210118e-31f) && (ay < 3.0e38f) &&
                     (__fsub_rn(half, fabsf(r)) > fmaf(fabsf(ph), 9.094947017729282e-13f, 1e-37f));
     return ok ? y : mul_round_slow(x, s.d);  // zero, tiny, huge, or near a midpoint
-}
-
-// The INT8 / FP8 GEMM epilogue of tv/quantization/matmul.tkv, exactly:
-//   per channel (:28)  y = fl32(fl64(fl64(acc*sa) * sw) + b)
-//   symmetric (:5,14)  y = fl32(fl64(acc * fl64(sa*sw)) + b)
-// acc = ah + ar exactly (ar = 0 unless |acc| > 2^24).  The exact value
-// E = acc*sa*sw + b is formed as s + lo with |s + lo - E| <= 2^-44 M, M =
-// |acc*sa*sw| + |b|; the f64 chain differs from E by at most 3*2^-53 M.  y =
-// fl32(s + lo) is the reference's result whenever s + lo is farther than
-// 2^-40 M from the nearest float midpoint.  Branch-free: returns false when
-// the f64 chain must decide (epilogue_slow).
-__device__ __forceinline__ bool epilogue_fast(float ah, float ar, float sa, float sw, float b, float& out) {
-    const float sh = __fmul_rn(sa, sw);
-    const float sl = fmaf(sa, sw, -sh);  // sa*sw = sh + sl exactly
-    const float p1 = __fmul_rn(ah, sh);
-    const float e1 = fmaf(ah, sh, -p1);  // ah*sh = p1 + e1 exactly
-    float pl = fmaf(ah, sl, e1);
-    pl = fmaf(ar, sh, pl);
-    pl = fmaf(ar, sl, pl);
-    const float s = __fadd_rn(p1, b);    // two-sum(p1, b)
-    const float bb = __fsub_rn(s, p1);
-    const float e2 = __fadd_rn(__fsub_rn(p1, __fsub_rn(s, bb)), __fsub_rn(b, bb));
-    const float lo = __fadd_rn(e2, pl);
-    const float y = __fadd_rn(s, lo);
-    // every real within 2^-40 M of s + lo rounds to y iff both ends of a
-    // directed-rounding widening of that interval do (rounding is monotone);
-    // E and the f64 chain both lie inside it
-    const float thr = fmaf(fabsf(p1) + fabsf(b), 9.094947017729282e-13f, 1e-37f);
-    const float ylo = __fadd_rn(s, __fsub_rd(lo, thr));
-    const float yhi = __fadd_rn(s, __fadd_ru(lo, thr));
-    out = y;
-    const float ay = fabsf(y);
-    // zeros (signed-zero rules), tiny, huge and non-finite values go to the f64 chain
-    return (ylo == yhi) && (ay >= 7.888609052210118e-31f) && (ay < 3.0e38f);
-}
-
-static __device__ __noinline__ float epilogue_slow(float ah, float ar, float sa, float sw, float b, bool per_channel) {
-    const double acc_d = static_cast<double>(ah) + static_cast<double>(ar);  // exact
-    const double sad = static_cast<double>(sa), swd = static_cast<double>(sw), bd = static_cast<double>(b);
-    double v;
-    if (per_channel) v = __dadd_rn(__dmul_rn(__dmul_rn(acc_d, sad), swd), bd);
-    else v = __dadd_rn(__dmul_rn(acc_d, sad * swd), bd);
-    return __double2float_rn(v);
-}
-
-__device__ __forceinline__ float epilogue_exact(float ah, float ar, float sa, float sw, float b, bool per_channel) {
-    float y;
-    if (!epilogue_fast(ah, ar, sa, sw, b, y)) y = epilogue_slow(ah, ar, sa, sw, b, per_channel);
-    return y;
 }
 
 // ---- pairs of floats in one 64-bit register for the f32x2 arithmetic of
@@ -241,37 +195,6 @@ __device__ __forceinline__ void two_sum2(uint64_t A, uint64_t B, uint64_t& S, ui
     S = f2_add(A, B);
     const uint64_t BB = f2_sub(S, A);
     E = f2_add(f2_sub(A, f2_sub(S, BB)), f2_sub(B, BB));
-}
-
-// epilogue_fast for two columns at once, accumulators below 2^24 in
-// magnitude (ar = 0): the same operations as the scalar form, so the same
-// results and the same decisions.  Bit j of the return value is set when
-// column j needs the f64 chain.
-__device__ __forceinline__ uint32_t epilogue_fast_x2(float ah0, float ah1, float sa, float sw0, float sw1, float b0,
-                                                     float b1, float& y0, float& y1) {
-    const uint64_t SA = f2_pack(sa, sa), SW = f2_pack(sw0, sw1), AH = f2_pack(ah0, ah1), B = f2_pack(b0, b1);
-    const uint64_t SH = f2_mul(SA, SW);
-    const uint64_t SL = f2_fma(SA, SW, f2_neg(SH));
-    const uint64_t P1 = f2_mul(AH, SH);
-    const uint64_t E1 = f2_fma(AH, SH, f2_neg(P1));
-    const uint64_t PL = f2_fma(AH, SL, E1);
-    const uint64_t S = f2_add(P1, B);
-    const uint64_t BB = f2_sub(S, P1);
-    const uint64_t E2 = f2_add(f2_sub(P1, f2_sub(S, BB)), f2_sub(B, BB));
-    const uint64_t LO = f2_add(E2, PL);
-    const uint64_t Y = f2_add(S, LO);
-    const uint64_t THR = f2_fma(f2_add(f2_abs(P1), f2_abs(B)), f2_pack(9.094947017729282e-13f, 9.094947017729282e-13f),
-                                f2_pack(1e-37f, 1e-37f));
-    const uint64_t YLO = f2_add(S, f2_sub_rd(LO, THR));
-    const uint64_t YHI = f2_add(S, f2_add_ru(LO, THR));
-    float lo0, lo1, hi0, hi1;
-    f2_unpack(Y, y0, y1);
-    f2_unpack(YLO, lo0, lo1);
-    f2_unpack(YHI, hi0, hi1);
-    const float a0 = fabsf(y0), a1 = fabsf(y1);
-    const bool ok0 = (lo0 == hi0) && (a0 >= 7.888609052210118e-31f) && (a0 < 3.0e38f);
-    const bool ok1 = (lo1 == hi1) && (a1 >= 7.888609052210118e-31f) && (a1 < 3.0e38f);
-    return (ok0 ? 0u : 1u) | (ok1 ? 0u : 2u);
 }
 
 // Error-free sum of two floats.

@@ -92,7 +92,6 @@ struct KParams {
     const float* scale_a;
     const float* scales_w;
     int per_channel;
-    int acc24;  // INT8 with k < 1024: every accumulator is below 2^24 in magnitude
     int act;
     const float* scale_out;
     uint32_t* amax;
@@ -327,7 +326,7 @@ struct Cfg {
     static constexpr uint32_t TMEM_COLS = NACC * BN;  // 128/256/512: powers of two
     static constexpr uint32_t RING = STAGES * STAGE_BYTES;
     static constexpr uint32_t EPI = EpiOf<KIND>::EPI_WARPS * 32 * EpiOf<KIND>::CH * 4;  // per-warp 32 x CH f32 staging
-    static constexpr uint32_t COLS = 2 * 2 * BN * 4;  // per-column scale and bias of a tile, double-buffered
+    static constexpr uint32_t COLS = 2 * 2 * BN * 8;  // per-column scale and bias of a tile (f64), double-buffered
     static constexpr uint32_t SMEM = RING + EPI + COLS + 1024 /*align*/ + 512 /*barriers*/;
 };
 
@@ -510,8 +509,12 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
         }
     } else if (warp >= 4) {
         // ------------------------------------------------ epilogue
-        // phase 1: lane = row, 16 consecutive columns from TMEM -> the exact
-        //          reference epilogue (tvq_exact.cuh) -> activation -> stage
+        // phase 1: lane = row, CH consecutive columns from TMEM -> the
+        //          reference epilogue in binary64, its own operations
+        //          (matmul.tkv:5,14,28: fl32(fl64(acc * fl64(sa*sw)) + b) or
+        //          fl32(fl64(fl64(acc*sa) * sw) + b), FP64 at half the FP32
+        //          rate on B200, two conversions per element) -> activation
+        //          -> stage
         // phase 2: lanes along columns: residual, f32 / int8 stores (four
         //          lanes write one 64-byte row segment), amax
         const int eg = warp & 3;            // TMEM lane group this warp may access
@@ -633,12 +636,13 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
             // publishes it, and the next tile's barrier keeps it alive until
             // every epilogue warp is done with this tile) and this warp's
             // residual rows toward L2
-            float* csc = colv + (tcount & 1u) * 2 * BN;
-            float* cbi = csc + BN;
+            double* csc = reinterpret_cast<double*>(colv) + (tcount & 1u) * 2 * BN;
+            double* cbi = csc + BN;
             for (int i = etid; i < BN; i += E::EPI_WARPS * 32) {
                 const int n = min(nb * BN + i, p.n - 1);
-                csc[i] = per_channel ? __ldg(p.scales_w + n) : sw0;
-                cbi[i] = bias_on ? __ldg(p.bias + n) : 0.0f;
+                const double sw = static_cast<double>(per_channel ? __ldg(p.scales_w + n) : sw0);
+                csc[i] = per_channel ? sw : static_cast<double>(sa) * sw;  // exact in f64
+                cbi[i] = static_cast<double>(bias_on ? __ldg(p.bias + n) : 0.0f);
             }
             if (p.residual) {
                 const int row = row0 + lane;
@@ -665,13 +669,13 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                 if (c + E::EPW < BN / E::CH && n0 + E::EPW * E::CH < p.n)
                     load_residual<E>(p, ec, lane, row0, n0 + E::EPW * E::CH, res_next);
                 // per-column scale and bias (shared memory, same address in every lane)
-                float swv[E::CH], bv[E::CH];
+                double wv[E::CH], bdv[E::CH];
 #pragma unroll
-                for (int j = 0; j < E::CH / 4; j++) {
-                    const float4 t = *reinterpret_cast<const float4*>(csc + c * E::CH + 4 * j);
-                    const float4 u = *reinterpret_cast<const float4*>(cbi + c * E::CH + 4 * j);
-                    swv[4 * j] = t.x; swv[4 * j + 1] = t.y; swv[4 * j + 2] = t.z; swv[4 * j + 3] = t.w;
-                    bv[4 * j] = u.x; bv[4 * j + 1] = u.y; bv[4 * j + 2] = u.z; bv[4 * j + 3] = u.w;
+                for (int j = 0; j < E::CH / 2; j++) {
+                    const double2 t = *reinterpret_cast<const double2*>(csc + c * E::CH + 2 * j);
+                    const double2 u = *reinterpret_cast<const double2*>(cbi + c * E::CH + 2 * j);
+                    wv[2 * j] = t.x; wv[2 * j + 1] = t.y;
+                    bdv[2 * j] = u.x; bdv[2 * j + 1] = u.y;
                 }
                 uint32_t r[E::CH];
                 __syncwarp();
@@ -684,56 +688,13 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                         if (n0 + j < p.n) dst[j] = static_cast<int32_t>(r[j]);
                 }
                 if (p.acc_only) continue;  // MatMulInteger: the accumulators are the result
-                // fast path for all columns (straight-line), rare f64 fix-ups after;
-                // accumulators below 2^24 (exact in f32: nearly always) two
-                // columns per f32x2 instruction
                 float y[E::CH];
-                uint32_t bad = 0;
-                bool small = true;
-                if (KIND == GEMM_I8 && !p.acc24) {
 #pragma unroll
-                    for (int j = 0; j < E::CH; j++) small &= (r[j] + 0x01000000u) < 0x02000000u;  // |acc| < 2^24
-                }
-                if (small) {
-#pragma unroll
-                    for (int j = 0; j < E::CH; j += 2) {
-                        const float a0 = (KIND == GEMM_I8) ? __int2float_rn(static_cast<int>(r[j])) : __uint_as_float(r[j]);
-                        const float a1 =
-                            (KIND == GEMM_I8) ? __int2float_rn(static_cast<int>(r[j + 1])) : __uint_as_float(r[j + 1]);
-                        bad |= epilogue_fast_x2(a0, a1, sa, swv[j], swv[j + 1], bv[j], bv[j + 1], y[j], y[j + 1]) << j;
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < E::CH; j++) {
-                        float ah, ar;
-                        if (KIND == GEMM_I8) {
-                            const int a = static_cast<int>(r[j]);
-                            ah = __int2float_rn(a);
-                            ar = __int2float_rn(a - __float2int_rn(ah));
-                        } else {
-                            ah = __uint_as_float(r[j]);
-                            ar = 0.0f;
-                        }
-                        const bool ok = epilogue_fast(ah, ar, sa, swv[j], bv[j], y[j]);
-                        bad |= ok ? 0u : (1u << j);
-                    }
-                }
-                if (bad) {
-#pragma unroll
-                    for (int j = 0; j < E::CH; j++) {
-                        if (bad & (1u << j)) {
-                            float ah, ar;
-                            if (KIND == GEMM_I8) {
-                                const int a = static_cast<int>(r[j]);
-                                ah = __int2float_rn(a);
-                                ar = __int2float_rn(a - __float2int_rn(ah));
-                            } else {
-                                ah = __uint_as_float(r[j]);
-                                ar = 0.0f;
-                            }
-                            y[j] = epilogue_slow(ah, ar, sa, swv[j], bv[j], per_channel);
-                        }
-                    }
+                for (int j = 0; j < E::CH; j++) {
+                    const double a = (KIND == GEMM_I8) ? static_cast<double>(static_cast<int>(r[j]))
+                                                       : static_cast<double>(__uint_as_float(r[j]));
+                    const double v = per_channel ? __dmul_rn(__dmul_rn(a, static_cast<double>(sa)), wv[j]) : __dmul_rn(a, wv[j]);
+                    y[j] = __double2float_rn(__dadd_rn(v, bdv[j]));
                 }
                 if (p.vth) {
                     const int part = n0 / p.kvd;  // 0 Q, 1 K, 2 V
@@ -1029,7 +990,6 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.scale_a = g.scale_a;
     p.scales_w = g.scales_w;
     p.per_channel = (acc_only || split || w4) ? 0 : g.per_channel;
-    p.acc24 = (g.kind == GEMM_I8 && g.k < 1024) ? 1 : 0;
     p.group_ks = w4 ? static_cast<int>(g.group_size / 16) : 0;
     p.ngroups = w4 ? static_cast<int>(g.k / g.group_size) : 0;
     p.qh = static_cast<__half*>(g.qh);
