@@ -42,8 +42,11 @@ def test_product_generator_matches_reference_generator():
         assert np.array_equal(gi_noise(10007, seed), O.gi_noise(10007, seed))
 
 
-@pytest.mark.parametrize("rows,d", [(1, 64), (300, 768), (77, 1600)])
+@pytest.mark.parametrize("rows,d", [(1, 64), (300, 768), (77, 1600), (10000, 768), (9500, 1600)])
 def test_layernorm_and_quantize(rows, d):
+    """Block-per-row (few rows) and warp-per-row (>= 4 x SMs x 16 rows, the
+    latter with x converted to binary64 on the fly at d 1600) LayerNorm +
+    int8 quantize against the f64 oracle."""
     import torch
     rng = np.random.default_rng(rows)
     x = (rng.standard_normal((rows, d)) * 3 + 0.7).astype(np.float32)

@@ -207,6 +207,24 @@ __device__ __forceinline__ void ln_warp_sum(float& h, float& l) {
     }
 }
 
+__device__ __forceinline__ double ln_warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Sum over the LNW warps of a block (red: LNW slots, reused after the
+// barrier that ends the row).
+__device__ __forceinline__ double ln_block_sum_d(double v, double* red, int lane, int warp) {
+    v = ln_warp_sum_d(v);
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    double t = red[0];
+#pragma unroll
+    for (int w = 1; w < LNW; w++) t = __dadd_rn(t, red[w]);
+    return t;
+}
+
 // SPLIT: the output goes out as the LM head's operand instead, the row-scaled
 // fp16 split of launch_split_f16_rows (hi, lo [T, d], rscale [T]).
 template <int NV, int WPR, bool SPLIT = false>
@@ -217,15 +235,13 @@ __global__ void __launch_bounds__(32 * LNW)
                            __half* __restrict__ slo = nullptr, float* __restrict__ srs = nullptr) {
     griddep_wait();
     __shared__ float2 red[2][LNW];
+    __shared__ double redd[2][LNW];
     constexpr int RPB = LNW / WPR;  // rows per block per pass
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int tid = (WPR == 1) ? lane : static_cast<int>(threadIdx.x);  // thread index within its row
     const int d4 = d >> 2;
     InvScale qs{0.0, 0.0f, 0.0f};
     if (q) qs = make_inv_scale(static_cast<double>(__ldg(qscale)));
-    const float eps_h = __double2float_rn(eps);
-    const float eps_l = __double2float_rn(eps - static_cast<double>(eps_h));
-    const float df = static_cast<float>(d);
     const float4* g4 = reinterpret_cast<const float4*>(g);
     const float4* b4 = reinterpret_cast<const float4*>(b);
     float am = 0.0f;
@@ -237,100 +253,63 @@ __global__ void __launch_bounds__(32 * LNW)
             const int i = j * 32 * WPR + tid;
             v[j] = (i < d4) ? __ldcs(xr + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
-        // sum: four float-pair accumulators (x, y, z, w components), two
-        // components per f32x2 instruction
-        float sh[4], sl[4];
-        {
-            uint64_t SH[2] = {0ull, 0ull}, SL[2] = {0ull, 0ull};
+        // statistics in binary64 as the reference (gpt2_ref.tkv:61-78):
+        // mu = sum x / d, var = sum (x - mu)^2 / d, rstd = 1 / sqrt(var + eps),
+        // y = fl32(((x - mu) * rstd) * g + b) (B200 runs FP64 at half the FP32
+        // rate); the sums run as a tree instead of the reference's sequence.
+        // Slots past the row hold 0 and add nothing to the sum.
+        constexpr bool KEEP = 4 * NV <= 24;  // x in binary64 registers, else converted again
+        double xd[KEEP ? 4 * NV : 1];
+        double sum = 0.0;
 #pragma unroll
-            for (int j = 0; j < NV; j++) {
-                const uint64_t C[2] = {f2_pack(v[j].x, v[j].y), f2_pack(v[j].z, v[j].w)};
-#pragma unroll
-                for (int k = 0; k < 2; k++) {
-                    uint64_t S, E;
-                    two_sum2(SH[k], C[k], S, E);
-                    SH[k] = S;
-                    SL[k] = f2_add(SL[k], E);
-                }
+        for (int j = 0; j < NV; j++) {
+            const double a0 = v[j].x, a1 = v[j].y, a2 = v[j].z, a3 = v[j].w;
+            if constexpr (KEEP) {
+                xd[4 * j] = a0;
+                xd[4 * j + 1] = a1;
+                xd[4 * j + 2] = a2;
+                xd[4 * j + 3] = a3;
             }
-            f2_unpack(SH[0], sh[0], sh[1]);
-            f2_unpack(SH[1], sh[2], sh[3]);
-            f2_unpack(SL[0], sl[0], sl[1]);
-            f2_unpack(SL[1], sl[2], sl[3]);
+            sum = __dadd_rn(sum, __dadd_rn(__dadd_rn(a0, a1), __dadd_rn(a2, a3)));
         }
-        df_add(sh[0], sl[0], sh[1], sl[1], sh[0], sl[0]);
-        df_add(sh[2], sl[2], sh[3], sl[3], sh[2], sl[2]);
-        df_add(sh[0], sl[0], sh[2], sl[2], sh[0], sl[0]);
-        if constexpr (WPR == 1) ln_warp_sum(sh[0], sl[0]);
-        else ln_block_sum(sh[0], sl[0], red[0], lane, warp);
-        float mh, ml;
-        df_div_int(sh[0], sl[0], df, mh, ml);
-        // variance of the valid elements
-        float vh[4], vl[4];
-        const uint64_t NMH = f2_pack(-mh, -mh), ML = f2_pack(ml, ml);
-        {
-            uint64_t VH[2] = {0ull, 0ull}, VL[2] = {0ull, 0ull};
-            const uint64_t TWO = f2_pack(2.0f, 2.0f);
-#pragma unroll
-            for (int j = 0; j < NV; j++) {
-                if (j * 32 * WPR + tid >= d4) continue;
-                const uint64_t C[2] = {f2_pack(v[j].x, v[j].y), f2_pack(v[j].z, v[j].w)};
-#pragma unroll
-                for (int k = 0; k < 2; k++) {
-                    uint64_t DH, DE;
-                    two_sum2(C[k], NMH, DH, DE);
-                    DE = f2_sub(DE, ML);
-                    const uint64_t PP = f2_mul(DH, DH);
-                    uint64_t PE = f2_fma(DH, DH, f2_neg(PP));
-                    PE = f2_fma(f2_mul(TWO, DH), DE, PE);
-                    uint64_t S, E;
-                    two_sum2(VH[k], PP, S, E);
-                    VH[k] = S;
-                    VL[k] = f2_add(VL[k], f2_add(E, PE));
-                }
+        if constexpr (WPR == 1) sum = ln_warp_sum_d(sum);
+        else sum = ln_block_sum_d(sum, redd[0], lane, warp);
+        // element k of float4 j in binary64 (kept, or converted again)
+        auto x_at = [&](int j, int k) -> double {
+            if constexpr (KEEP) {
+                return xd[4 * j + k];
+            } else {
+                return static_cast<double>(k == 0 ? v[j].x : k == 1 ? v[j].y : k == 2 ? v[j].z : v[j].w);
             }
-            f2_unpack(VH[0], vh[0], vh[1]);
-            f2_unpack(VH[1], vh[2], vh[3]);
-            f2_unpack(VL[0], vl[0], vl[1]);
-            f2_unpack(VL[1], vl[2], vl[3]);
+        };
+        const double mu = sum / static_cast<double>(d);
+        double ss = 0.0;
+#pragma unroll
+        for (int j = 0; j < NV; j++) {
+            if (j * 32 * WPR + tid >= d4) continue;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const double dd = __dsub_rn(x_at(j, k), mu);
+                ss = __fma_rn(dd, dd, ss);
+            }
         }
-        df_add(vh[0], vl[0], vh[1], vl[1], vh[0], vl[0]);
-        df_add(vh[2], vl[2], vh[3], vl[3], vh[2], vl[2]);
-        df_add(vh[0], vl[0], vh[2], vl[2], vh[0], vl[0]);
-        if constexpr (WPR == 1) ln_warp_sum(vh[0], vl[0]);
-        else ln_block_sum(vh[0], vl[0], red[1], lane, warp);
-        float wh, wl, rh, rl;
+        if constexpr (WPR == 1) ss = ln_warp_sum_d(ss);
+        else ss = ln_block_sum_d(ss, redd[1], lane, warp);
+        const double rstd = 1.0 / sqrt(__dadd_rn(ss / static_cast<double>(d), eps));
         float4 ov[SPLIT ? NV : 1];
         float rmax = 0.0f;
         bool bad = false;
-        df_div_int(vh[0], vl[0], df, wh, wl);
-        df_add(wh, wl, eps_h, eps_l, wh, wl);
-        df_rsqrt(wh, wl, rh, rl);
 #pragma unroll
         for (int j = 0; j < NV; j++) {
             const int i = j * 32 * WPR + tid;
             if (i >= d4) continue;
             const float4 gg = __ldg(g4 + i), bb = __ldg(b4 + i);
-            const uint64_t C[2] = {f2_pack(v[j].x, v[j].y), f2_pack(v[j].z, v[j].w)};
-            const uint64_t G2[2] = {f2_pack(gg.x, gg.y), f2_pack(gg.z, gg.w)};
-            const uint64_t B2[2] = {f2_pack(bb.x, bb.y), f2_pack(bb.z, bb.w)};
-            const uint64_t RH = f2_pack(rh, rh), RL = f2_pack(rl, rl);
+            const float gk[4] = {gg.x, gg.y, gg.z, gg.w}, bk[4] = {bb.x, bb.y, bb.z, bb.w};
             float o4[4];
 #pragma unroll
-            for (int k = 0; k < 2; k++) {
-                uint64_t DH, DE;
-                two_sum2(C[k], NMH, DH, DE);
-                DE = f2_sub(DE, ML);
-                const uint64_t TT = f2_mul(DH, RH);
-                uint64_t TE = f2_fma(DH, RH, f2_neg(TT));
-                TE = f2_fma(DH, RL, TE);
-                TE = f2_fma(DE, RH, TE);
-                const uint64_t U = f2_mul(TT, G2[k]);
-                uint64_t UE = f2_fma(TT, G2[k], f2_neg(U));
-                UE = f2_fma(TE, G2[k], UE);
-                uint64_t S, E;
-                two_sum2(U, B2[k], S, E);
-                f2_unpack(f2_add(S, f2_add(E, UE)), o4[2 * k], o4[2 * k + 1]);
+            for (int k = 0; k < 4; k++) {
+                const double t = __dmul_rn(__dmul_rn(__dsub_rn(x_at(j, k), mu), rstd), static_cast<double>(gk[k]));
+                o4[k] = __double2float_rn(__dadd_rn(t, static_cast<double>(bk[k])));
             }
 #pragma unroll
             for (int k = 0; k < 4; k++) am = fmaxf(am, fabsf(o4[k]));
