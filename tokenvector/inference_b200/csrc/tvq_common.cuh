@@ -95,6 +95,11 @@ int launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cu
 #ifndef TVQ_WAIT_LIMIT_NS
 #define TVQ_WAIT_LIMIT_NS 2000000000ull
 #endif
+// Suspend-time hint of one try of a bounded wait (the thread wakes when the
+// phase completes, or after this long to check the time limit).
+#ifndef TVQ_WAIT_SLEEP_NS
+#define TVQ_WAIT_SLEEP_NS 10000u
+#endif
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -143,6 +148,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or about `ns` nanoseconds pass, instead of spinning (a spinning
+// producer or MMA warp takes issue slots from the warps it waits for).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for the phase of `bar` with the given parity to complete.
 // Returns false (and records `code`) when TVQ_WAIT_LIMIT_NS elapses first.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
@@ -150,7 +170,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     const uint64_t t0 = globaltimer_ns();
     uint32_t spins = 0;
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, TVQ_WAIT_SLEEP_NS)) return true;
         if ((++spins & 63u) == 0u) {
             if (globaltimer_ns() - t0 > TVQ_WAIT_LIMIT_NS) {
                 record_error(err, code);

@@ -231,7 +231,8 @@ __device__ __forceinline__ void load_residual(const KParams& p, const EpiCtx& e,
 // leaving it out keeps their kernels small).
 template <class E, bool QOUT>
 __device__ __forceinline__ void stage_and_store(const KParams& p, const EpiCtx& e, float* stage, const float (&y)[E::CH],
-                                                int lane, int row0, int n0, float& amax, const float4 (&res)[E::LPR]) {
+                                                int lane, int row0, int n0, float& amax, const float4 (&res)[E::LPR],
+                                                float kvf = 1.0f) {
 #pragma unroll
     for (int j = 0; j < E::LPR; j++)
         *reinterpret_cast<float4*>(&stage[lane * E::CH + 4 * (j ^ ((lane >> E::SWS) & (E::LPR - 1)))]) =
@@ -250,10 +251,9 @@ __device__ __forceinline__ void stage_and_store(const KParams& p, const EpiCtx& 
             const int part = col >= p.kvd ? 1 : 0;
             const int c = col - part * p.kvd;
             const int64_t ko = static_cast<int64_t>(row) * p.kvd + c;
-            const float f = exp2i(kv_head_exp(p.kv_bound, p.kvd / 64, part, c / 64, e.sa));
-            uint2 h, l;
-            split_h2_pair(v.x * f, v.y * f, h.x, l.x);
-            split_h2_pair(v.z * f, v.w * f, h.y, l.y);
+            uint2 h, l;  // kvf: 2^kv_exp of the chunk's head (a chunk lies inside one head)
+            split_h2_pair(v.x * kvf, v.y * kvf, h.x, l.x);
+            split_h2_pair(v.z * kvf, v.w * kvf, h.y, l.y);
             *reinterpret_cast<uint2*>((part ? p.kh : p.qh) + ko) = h;
             *reinterpret_cast<uint2*>((part ? p.kl : p.ql) + ko) = l;
         }
@@ -696,10 +696,12 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                     const double v = per_channel ? __dmul_rn(__dmul_rn(a, static_cast<double>(sa)), wv[j]) : __dmul_rn(a, wv[j]);
                     y[j] = __double2float_rn(__dadd_rn(v, bdv[j]));
                 }
+                float kvf = 1.0f;
                 if (p.vth) {
                     const int part = n0 / p.kvd;  // 0 Q, 1 K, 2 V
                     const int hh = (n0 - part * p.kvd) / 64;
                     const int sh = kv_head_exp(p.kv_bound, p.kvd / 64, part, hh, sa);
+                    kvf = exp2i(sh);
                     if (row0 == 0 && lane == 0 && (n0 - part * p.kvd) % 64 == 0)
                         p.kv_exp[part * (p.kvd / 64) + hh] = sh;  // one writer per head
                     if (part == 2 && row0 + lane < p.m) {
@@ -708,7 +710,7 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                         const int64_t vo = static_cast<int64_t>(n0 - 2 * p.kvd) * p.vt_pitch + row0 + lane;
 #pragma unroll
                         for (int j = 0; j < E::CH; j++) {
-                            const float v = y[j] * exp2i(sh);
+                            const float v = y[j] * kvf;
                             const __half h = __float2half_rn(v);
                             p.vth[vo + static_cast<int64_t>(j) * p.vt_pitch] = h;
                             p.vtl[vo + static_cast<int64_t>(j) * p.vt_pitch] = __float2half_rn(__fsub_rn(v, __half2float(h)));
@@ -725,7 +727,7 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < E::CH; j++) y[j] = y[j] > 0.0f ? y[j] : 0.0f;
                 }
-                stage_and_store<E, true>(p, ec, stage, y, lane, row0, n0, amax, res);
+                stage_and_store<E, true>(p, ec, stage, y, lane, row0, n0, amax, res, kvf);
             }
             tc_fence_before();
             __syncwarp();
