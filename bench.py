@@ -131,6 +131,76 @@ def gemm_large(torch, dev, stream, flush, n=8192, reps=10):
             "frac": tops / (2.0 * bf16), "peak_source": "2 x %s dense bf16" % src}
 
 
+def nsplit_c_fc(torch, dist, dev, stream, world, flush, T=8192, K=1600, N=6400, reps=10):
+    """The optional N-split of the XL c_fc (1600 -> 6400, split by output
+    column) measured against the token sharding the layer stack uses.  Every
+    rank computes GELU-erf -> int8 for all T tokens on its N / world columns,
+    NCCL all-gathers the int8 slices over NVLink, and re-lays them out into
+    the [T, N] operand of mlp c_proj; the alternative is the same GEMM on
+    T / world tokens and all N columns, with no exchange.  Kernel times by
+    CUDA events on the launching stream, L2 flushed before each repetition,
+    max over ranks.  Called on every rank in the same order."""
+    import ctypes as C
+    from tokenvector.inference_b200 import _native as NT
+    ns = N // world
+    g = torch.Generator(device="cpu").manual_seed(5)
+    A = torch.randint(-127, 128, (T, K), dtype=torch.int8, generator=g).to(dev)
+    W = torch.randint(-127, 128, (N, K), dtype=torch.int8, generator=g).to(dev)
+    Ws = W[dist.get_rank() * ns:(dist.get_rank() + 1) * ns].contiguous()
+    bias = (torch.randn(N, generator=g) * 0.02).to(dev)
+    bs = bias[dist.get_rank() * ns:(dist.get_rank() + 1) * ns].contiguous()
+    sw = (torch.rand(N, generator=g) * 1e-4).to(dev)
+    sws = sw[dist.get_rank() * ns:(dist.get_rank() + 1) * ns].contiguous()
+    sa = torch.tensor([0.02], device=dev)
+    so = torch.tensor([0.05], device=dev)
+    yq_s = torch.empty((T, ns), dtype=torch.int8, device=dev)
+    gath = torch.empty((world, T, ns), dtype=torch.int8, device=dev)
+    full = torch.empty((T, N), dtype=torch.int8, device=dev)
+    tl = T // world
+    yq_t = torch.empty((tl, N), dtype=torch.int8, device=dev)
+    p = lambda t: C.c_void_p(t.data_ptr())
+    sp = C.c_void_p(stream.cuda_stream)
+
+    def gemm(a, w, b, s, y, m, n):
+        NT.call("tvq_dev_gemm", NT.GEMM_I8, p(a), p(w), p(b), None, None, p(y), m, n, K, p(sa), p(s), 1,
+                NT.ACT_GELU_ERF, p(so), None, sp)
+
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    tot = [0.0] * 4
+    for r in range(reps + 3):
+        flush.zero_()
+        ev[0].record(stream)
+        gemm(A, Ws, bs, sws, yq_s, T, ns)
+        ev[1].record(stream)
+        dist.all_gather_into_tensor(gath, yq_s)
+        ev[2].record(stream)
+        full.view(T, world, ns).copy_(gath.permute(1, 0, 2))
+        ev[3].record(stream)
+        flush.zero_()
+        ev[4].record(stream)
+        gemm(A[dist.get_rank() * tl:], W, bias, sw, yq_t, tl, N)
+        ev[5].record(stream)
+        ev[5].synchronize()
+        if r >= 3:
+            tot[0] += ev[0].elapsed_time(ev[1])
+            tot[1] += ev[1].elapsed_time(ev[2])
+            tot[2] += ev[2].elapsed_time(ev[3])
+            tot[3] += ev[4].elapsed_time(ev[5])
+    # the gathered operand equals the token-sharded GEMM's rows of this rank
+    # (the exchange and the re-layout are checked, not assumed)
+    ok = torch.equal(full[dist.get_rank() * tl:(dist.get_rank() + 1) * tl], yq_t)
+    v = torch.tensor([t / reps * 1000.0 for t in tot] + [0.0 if ok else 1.0], dtype=torch.float64, device=dev)
+    dist.all_reduce(v, op=dist.ReduceOp.MAX)
+    gemm_us, ag_us, relay_us, tok_us, bad = v.tolist()
+    return {"layer": "XL c_fc: K %d, N %d, GELU-erf -> int8, %d tokens" % (K, N, T),
+            "nsplit_gemm_us": gemm_us, "allgather_us": ag_us, "relayout_us": relay_us,
+            "nsplit_total_us": gemm_us + ag_us + relay_us,
+            "allgather_bytes_per_rank": (world - 1) * T * ns,
+            "allgather_gbs": (world - 1) * T * ns / (ag_us * 1e-6) / 1e9,
+            "token_sharded_us": tok_us, "nsplit_over_token_sharded": (gemm_us + ag_us + relay_us) / tok_us,
+            "gathered_equals_token_sharded": bad == 0.0}
+
+
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -634,6 +704,9 @@ def run_ours_c5(args, rank, world, local):
         ev1.synchronize()
         e2e_ms += ev0.elapsed_time(ev1)
     finite = bool(torch.isfinite(y_pin).all().item())
+    # the optional N-split of the 6400-wide c_fc with an NCCL all-gather,
+    # measured beside the token sharding (N > 1 only; not on the data path)
+    nsplit = nsplit_c_fc(torch, dist, dev, stream, world, flush) if world > 1 else None
 
     vals = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -681,7 +754,7 @@ def run_ours_c5(args, rank, world, local):
                        "h2d_bytes_per_step": 4 * job * cfg.d_model, "d2h_bytes_per_step": 4 * job * cfg.d_model,
                        "ms_per_step": e2e_ms / e2e_steps, "finite": finite},
                "roofline": roof, "cpu_baseline": cpu, "gpu_launches": n_launches * args.steps, "clocks": clk,
-               "kernels": kernels}
+               "kernels": kernels, "nsplit_c_fc": nsplit}
         print(json.dumps(out), flush=True)
     st.close()
     if world > 1:

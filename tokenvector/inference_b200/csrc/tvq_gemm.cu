@@ -238,6 +238,27 @@ __device__ __forceinline__ void stage_and_store(const KParams& p, const EpiCtx& 
         *reinterpret_cast<float4*>(&stage[lane * E::CH + 4 * (j ^ ((lane >> E::SWS) & (E::LPR - 1)))]) =
             make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
     __syncwarp();
+    if (!e.vec_ok) {
+        // rows not 16-byte aligned (n % 4 != 0, e.g. the 50257-wide LM
+        // head): CH consecutive lanes write CH consecutive columns of one
+        // row, 32 / CH rows per store instruction (staging reads stay
+        // conflict-free: the 32 / CH rows cover the 32 banks once)
+#pragma unroll
+        for (int it = 0; it < E::CH; it++) {
+            const int rr = it * (32 / E::CH) + lane / E::CH;
+            const int c = lane % E::CH;
+            const int row = row0 + rr;
+            const int col = n0 + c;
+            float x = stage[rr * E::CH + 4 * ((c >> 2) ^ ((rr >> E::SWS) & (E::LPR - 1))) + (c & 3)];
+            if (row >= p.m || col >= p.n) continue;
+            const int64_t off = static_cast<int64_t>(row) * p.n + col;
+            if (p.residual) x = __fadd_rn(x, p.residual[off]);
+            if (p.amax) amax = fmaxf(amax, fabsf(x));
+            if (p.Y) p.Y[off] = x;
+            if (QOUT && p.Yq) p.Yq[off] = quant_exact(x, e.qs);
+        }
+        return;
+    }
 #pragma unroll
     for (int it = 0; it < E::LPR; it++) {
         const int rr = it * E::RPI + lane / E::LPR;

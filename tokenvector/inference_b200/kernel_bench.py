@@ -2,6 +2,7 @@
 repetitions), for tuning and for small profiler captures.
 
   python -m tokenvector.inference_b200.kernel_bench gemm --m 1024 --n 3072 --k 768 --epilogue gelu_q
+  python -m tokenvector.inference_b200.kernel_bench lmhead --m 1024 --n 50257 --k 768
   python -m tokenvector.inference_b200.kernel_bench layernorm --m 1024 --n 768
   python -m tokenvector.inference_b200.kernel_bench attention --m 1024 --n 768 --heads 12
   python -m tokenvector.inference_b200.kernel_bench quantize --m 1024 --n 768
@@ -116,6 +117,30 @@ def bench_attention(T, d, heads, reps=20):
     return {"kernel": "attention", "T": T, "d": d, "heads": heads, "us": us, "tflops_causal": fl / us / 1e6}
 
 
+def bench_lmhead(m, n, k, reps=20):
+    """The fp32 tied LM head as the FP16 hi/lo split GEMM (GEMM_F16X3): the
+    two row splits once, then Y = A W^T timed alone."""
+    torch, dev, st, flush = _env()
+    A = torch.randn((m, k), device=dev)
+    W = torch.randn((n, k), device=dev) * 0.02
+    ah = torch.empty((m, k), dtype=torch.float16, device=dev)
+    al = torch.empty_like(ah)
+    wh = torch.empty((n, k), dtype=torch.float16, device=dev)
+    wl = torch.empty_like(wh)
+    ar = torch.empty(m, device=dev)
+    wr = torch.empty(n, device=dev)
+    Y = torch.empty((m, n), device=dev)
+    sp = C.c_void_p(st.cuda_stream)
+    N.call("tvq_dev_split_f16_rows", _p(A), _p(ah), _p(al), _p(ar), m, k, sp)
+    N.call("tvq_dev_split_f16_rows", _p(W), _p(wh), _p(wl), _p(wr), n, k, sp)
+    us = _time(torch, st, flush, lambda: N.call("tvq_dev_gemm_f16x3", _p(ah), _p(al), _p(ar), _p(wh), _p(wl), _p(wr),
+                                                  _p(Y), m, n, k, sp), reps)
+    ref = (A.double() @ W.double().T)
+    err = float(((Y.double() - ref).abs() / (A.double().abs() @ W.double().abs().T)).max())
+    return {"kernel": "gemm_f16x3", "m": m, "n": n, "k": k, "us": us,
+            "tflops_useful": 2.0 * m * n * k / us / 1e6, "max_err_over_sum_abs": err}
+
+
 def bench_gpt2(reps=20):
     import torch
     from .gpt2 import GPT2Config, GPT2Session, GPT2Weights
@@ -139,7 +164,7 @@ def bench_gpt2(reps=20):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "layernorm", "quantize", "attention", "gpt2", "all"])
+    ap.add_argument("what", choices=["gemm", "lmhead", "layernorm", "quantize", "attention", "gpt2", "all"])
     ap.add_argument("--m", type=int, default=1024)
     ap.add_argument("--n", type=int, default=768)
     ap.add_argument("--k", type=int, default=768)
@@ -153,6 +178,8 @@ def main():
     res = []
     if a.what == "gemm":
         res.append(bench_gemm(a.m, a.n, a.k, a.epilogue, a.reps, kind))
+    elif a.what == "lmhead":
+        res.append(bench_lmhead(a.m, a.n, a.k, a.reps))
     elif a.what == "layernorm":
         res.append(bench_layernorm(a.m, a.n, a.reps))
     elif a.what == "quantize":
