@@ -87,7 +87,10 @@ def test_dequantize_bit_exact():
     assert _same_f32(y2, O.dequantize_int8_per_channel(q, 50, 100, sc))
 
 
-@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 7), (64, 768), (3072, 768), (100, 1001)])
+# cols 1025..8192 (multiple of 4) take the block-per-row kernel (row held in
+# registers), the others the warp-per-row kernel
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 7), (64, 768), (3072, 768), (100, 1001), (64, 1600), (5, 4100),
+                                       (7, 6400), (3, 8192), (2, 8196), (9, 1030)])
 def test_per_channel_calibrate_and_quantize(rows, cols):
     w = (O.gi_noise(rows * cols, rows + cols) if rows * cols > 1 else np.array([0.5], np.float32)).reshape(rows, cols)
     ps = E.calibrate_per_channel_minmax(w, rows, cols)
@@ -107,15 +110,16 @@ def test_per_channel_edges():
     assert _same_f32(g[~np.isnan(g)], os_[~np.isnan(os_)])
 
 
-def test_dynamic_rowwise():
-    x = _data(512 * 300, 5, outliers=True).reshape(512, 300)
+@pytest.mark.parametrize("rows,cols", [(512, 300), (40, 6400)])
+def test_dynamic_rowwise(rows, cols):
+    x = _data(rows * cols, 5, outliers=True).reshape(rows, cols)
     x[7, :] = 0.0
     x[9, 3] = np.nan
     q = np.empty(x.size, np.int8)
-    sc = np.empty(512, np.float32)
-    E.quantize_dynamic_int8_rowwise(x, q, 512, 300, sc)
-    oq, osc = O.quantize_dynamic_int8_rowwise(x, 512, 300)
-    assert np.array_equal(q.reshape(512, 300), oq)
+    sc = np.empty(rows, np.float32)
+    E.quantize_dynamic_int8_rowwise(x, q, rows, cols, sc)
+    oq, osc = O.quantize_dynamic_int8_rowwise(x, rows, cols)
+    assert np.array_equal(q.reshape(rows, cols), oq)
     assert _same_f32(sc, osc)
 
 
@@ -138,21 +142,23 @@ def test_fp8_encode_reference_quirks_and_random():
     rand = bits.view(np.float32)
     near = (rng.standard_normal(1 << 18) * rng.choice([1e-3, 0.05, 1, 30, 250], 1 << 18)).astype(np.float32)
     x = np.concatenate([special, rand, near])
-    q = np.empty(x.size, np.uint8)
-    M.quantize_fp8_e4m3(x, q)
-    assert np.array_equal(q, O.quantize_fp8_e4m3(x))
+    for xs in (x, x[: x.size - x.size % 4]):  # scalar and 4-wide vector kernels
+        q = np.empty(xs.size, np.uint8)
+        M.quantize_fp8_e4m3(xs, q)
+        assert np.array_equal(q, O.quantize_fp8_e4m3(xs))
     # list[i32] form stores byte - 128 (matmul.tkv:65)
     q32 = np.empty(special.size, np.int32)
     M.quantize_fp8_e4m3(special, q32)
     assert np.array_equal(q32, O.quantize_fp8_e4m3(special).astype(np.int32) - 128)
 
 
-def test_fp8_scaled_quantize():
-    x = _data(64 * 1024, 8, outliers=True).reshape(64, 1024)
+@pytest.mark.parametrize("cols", [1024, 1001])
+def test_fp8_scaled_quantize(cols):
+    x = _data(64 * cols, 8, outliers=True).reshape(64, cols)
     amax_rows = np.abs(x).max(axis=1)
     sc = (amax_rows / 448.0).astype(np.float32)
-    g = M.quantize_fp8_e4m3_scaled(x, 64, 1024, sc, True)
+    g = M.quantize_fp8_e4m3_scaled(x, 64, cols, sc, True)
     assert np.array_equal(g, O.quantize_fp8_e4m3_scaled(x, sc, True))
     st = np.array([np.abs(x).max() / 448.0], np.float32)
-    g = M.quantize_fp8_e4m3_scaled(x, 64, 1024, st, False)
+    g = M.quantize_fp8_e4m3_scaled(x, 64, cols, st, False)
     assert np.array_equal(g, O.quantize_fp8_e4m3_scaled(x, st, False))

@@ -624,13 +624,25 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                     // undo the rows' power-of-two scales (exact)
                     const int row = row0 + lane;
                     const float ra = (row < p.m) ? __ldg(p.scale_a + row) : 0.0f;
+                    const bool sw_vec = (reinterpret_cast<uintptr_t>(p.scales_w) & 15) == 0;
 #pragma unroll
                     for (int i = 0; i < NCH; i++) {
                         const int n0 = nb * BN + (half + E::EPW * i) * E::CH;
+                        // the chunk's column scales: CH / 4 16-byte loads (one
+                        // address per warp) where the chunk lies inside [0, n)
+                        if (sw_vec && n0 + E::CH <= p.n) {
 #pragma unroll
-                        for (int j = 0; j < E::CH; j++) {
-                            const int n = (n0 + j < p.n) ? n0 + j : p.n - 1;
-                            acc[i][j] = acc[i][j] * ra * __ldg(p.scales_w + n);
+                            for (int q4 = 0; q4 < E::CH / 4; q4++) {
+                                const float4 t = __ldg(reinterpret_cast<const float4*>(p.scales_w + n0) + q4);
+                                acc[i][4 * q4] = acc[i][4 * q4] * ra * t.x;
+                                acc[i][4 * q4 + 1] = acc[i][4 * q4 + 1] * ra * t.y;
+                                acc[i][4 * q4 + 2] = acc[i][4 * q4 + 2] * ra * t.z;
+                                acc[i][4 * q4 + 3] = acc[i][4 * q4 + 3] * ra * t.w;
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < E::CH; j++)
+                                acc[i][j] = acc[i][j] * ra * __ldg(p.scales_w + min(n0 + j, p.n - 1));
                         }
                     }
                 }

@@ -18,6 +18,7 @@
 #include <cstring>
 
 #include "tvq_common.cuh"
+#include "tvq_e4m3.h"
 #include "tvq_exact.cuh"
 #include "tvq_kernels.h"
 
@@ -312,10 +313,81 @@ __global__ void rowwise_kernel(const float* __restrict__ x, int8_t* __restrict__
     }
 }
 
+// Modes 0 and 2 for rows of 1025 .. 8192 floats: one 256-thread block per
+// row with the row held in registers (NV float4 per thread), so the row is
+// read from HBM once.  (The warp-per-row form reads it twice: with ~10k rows
+// in flight its second pass misses L2 once rows exceed a few KB -- 358 MB
+// read for a 210 MB [8192, 6400] tensor.)  Same scale and quantize
+// arithmetic as rowwise_kernel; needs 16-byte aligned rows.
+template <int MODE, int NV>
+__global__ void __launch_bounds__(256) rowwise_block_kernel(const float* __restrict__ x, int8_t* __restrict__ q,
+                                                            float* __restrict__ scales, int64_t rows, int64_t cols) {
+    __shared__ float red[8];
+    const int tid = threadIdx.x;
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const float* xr = x + r * cols;
+        int8_t* qr = q + r * cols;
+        float4 v[NV];
+        float am = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            const int64_t c = (static_cast<int64_t>(i) * 256 + tid) * 4;
+            v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (c < cols) v[i] = __ldcs(reinterpret_cast<const float4*>(xr + c));
+            am = fmaxf(am, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+        }
+        am = warp_max(am);
+        if ((tid & 31) == 0) red[tid >> 5] = am;
+        __syncthreads();
+#pragma unroll
+        for (int w = 0; w < 8; w++) am = fmaxf(am, red[w]);
+        double amd = am;
+        InvScale qs;
+        if (amd < 0.00000001) amd = 0.00000001;
+        if (MODE == 0) {
+            const bool poisoned = (__ldg(xr) != __ldg(xr));  // NaN first element poisons min/max
+            const float sc = poisoned ? __int_as_float(0x7FC00000) : __double2float_rn(amd / 127.0);
+            if (tid == 0) scales[r] = sc;
+            qs = make_inv_scale(static_cast<double>(sc));
+        } else {
+            const double sc = amd / 127.0;
+            if (tid == 0) scales[r] = __double2float_rn(sc);
+            qs = make_inv_from_inv(1.0 / sc);
+        }
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            const int64_t c = (static_cast<int64_t>(i) * 256 + tid) * 4;
+            if (c < cols) {
+                char4 o;
+                o.x = quant_exact(v[i].x, qs);
+                o.y = quant_exact(v[i].y, qs);
+                o.z = quant_exact(v[i].z, qs);
+                o.w = quant_exact(v[i].w, qs);
+                *reinterpret_cast<char4*>(qr + c) = o;
+            }
+        }
+        __syncthreads();  // red[] is rewritten for the next row
+    }
+}
+
 int launch_rowwise(int mode, const float* x, int8_t* q, float* scales, int64_t rows, int64_t cols,
                    cudaStream_t st) {
     if (rows <= 0 || cols <= 0) return TVQ_OK;
     const int threads = 256;
+    const bool vec = (cols % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(q) & 3) == 0);
+    if (mode != 1 && vec && cols > 1024 && cols <= 8192) {
+        const int g = grid_for(rows * threads, threads, 8);
+#define TVQ_ROWB(M, NV) rowwise_block_kernel<M, NV><<<g, threads, 0, st>>>(x, q, scales, rows, cols)
+        if (mode == 0) {
+            if (cols <= 2048) TVQ_ROWB(0, 2); else if (cols <= 4096) TVQ_ROWB(0, 4); else TVQ_ROWB(0, 8);
+        } else {
+            if (cols <= 2048) TVQ_ROWB(2, 2); else if (cols <= 4096) TVQ_ROWB(2, 4); else TVQ_ROWB(2, 8);
+        }
+#undef TVQ_ROWB
+        TVQ_CUDA(cudaGetLastError());
+        return TVQ_OK;
+    }
     const int grid = grid_for(rows * 32, threads, 8);
     if (mode == 0) rowwise_kernel<0><<<grid, threads, 0, st>>>(x, q, scales, rows, cols);
     else if (mode == 1) rowwise_kernel<1><<<grid, threads, 0, st>>>(x, q, scales, rows, cols);
@@ -326,53 +398,8 @@ int launch_rowwise(int mode, const float* x, int8_t* q, float* scales, int64_t r
 
 // ------------------------------------------------------------ K3: FP8 E4M3
 
-// Binary32 pattern as tv/runtime/f32_bits.tkv:6-57 produces it for an f32
-// input: the IEEE pattern, except -0.0 -> 0, +/-2^-149 -> +/-0 (its
-// `sh <= 0` test), NaN -> quiet NaN (that loop cannot finish on NaN/Inf).
-__host__ __device__ __forceinline__ uint32_t ref_f32_bits(uint32_t b) {
-    if ((b & 0x7FFFFFFFu) == 0u) return 0u;
-    if ((b & 0x7F800000u) == 0x7F800000u) return (b & 0x007FFFFFu) ? 0x7FC00000u : b;
-    if ((b & 0x7FFFFFFFu) == 1u) return b & 0x80000000u;
-    return b;
-}
-
-// _qt_rne_rshift, tv/quantization/types.tkv:71-93
-__host__ __device__ __forceinline__ int64_t rne_rshift(int64_t v, int64_t s) {
-    if (s > 40) return 0;
-    if (s <= 0) return v;
-    const int64_t half = static_cast<int64_t>(1) << (s - 1);
-    const int64_t q = v >> s;
-    const int64_t rem = v - (q << s);
-    if (rem > half) return q + 1;
-    if (rem < half) return q;
-    return (q & 1) ? q + 1 : q;
-}
-
-// native_fp8_e4m3_encode = _qt_fp8_encode(x, 7, 3, 15, 0, 126),
-// tv/quantization/types.tkv:154-191, 228-230.
-__host__ __device__ __forceinline__ uint8_t e4m3_encode_ref(uint32_t xbits) {
-    const uint32_t b = ref_f32_bits(xbits);
-    const uint32_t sign = b >> 31;
-    const int64_t ex = (b >> 23) & 255;
-    const int64_t man = b & 8388607;
-    if (ex == 255) return static_cast<uint8_t>((sign << 7) | 127u);
-    int64_t e, full;
-    if (ex == 0) { e = -126; full = man; } else { e = ex - 127; full = man | 8388608; }
-    int64_t e8 = e + 7;
-    if (e8 >= 15) return static_cast<uint8_t>((sign << 7) | 126u);
-    if (e8 <= 0) {
-        int64_t m = rne_rshift(full, 24 - 3 - e8);
-        if (m > 7) m = 7;
-        return static_cast<uint8_t>((sign << 7) | static_cast<uint32_t>(m));
-    }
-    int64_t r = rne_rshift(full, 23 - 3);
-    if (r >= 16) {
-        r = 8;
-        e8 = e8 + 1;
-        if (e8 >= 15) return static_cast<uint8_t>((sign << 7) | 126u);
-    }
-    return static_cast<uint8_t>((sign << 7) | static_cast<uint32_t>(e8 << 3) | static_cast<uint32_t>(r - 8));
-}
+// The reference's E4M3 encoder: tvq_e4m3.h (e4m3_encode_fast in the kernels,
+// e4m3_encode_ref beside it, equal on every binary32 input).
 
 // native_fp8_e4m3_decode = _qt_fp8_decode(v, 7, 3, 15, 0), types.tkv:193-226,
 // through f32_bits_to_f64 (f32_bits.tkv:60-74): 0x7F/0xFF give +/-Inf (the
@@ -398,9 +425,15 @@ __device__ __forceinline__ uint8_t e4m3_encode_hw(float x) {
     return static_cast<uint8_t>(__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3));
 }
 
+__device__ __forceinline__ uint32_t e4m3_byte(float v, bool hw) {
+    return hw ? e4m3_encode_hw(v) : e4m3_encode_fast(__float_as_uint(v));
+}
+
 // SCALE: 0 none (quantize_fp8_e4m3, matmul.tkv:60-66), 1 per tensor, 2 per
 // row; the scaled value is fl32(x * (1/scale)) as the encoder's f32 argument.
-template <int SCALE, int HW>
+// VEC: 16-byte loads and 4-byte stores (x 16-byte and q 4-byte aligned, n % 4
+// == 0 for the flat form, cols % 4 == 0 for the per-row form).
+template <int SCALE, int HW, int VEC>
 __global__ void fp8_encode_kernel(const float* __restrict__ x, uint8_t* __restrict__ q, int64_t rows, int64_t cols,
                                   const float* __restrict__ scales) {
     const int64_t n = rows * cols;
@@ -408,24 +441,49 @@ __global__ void fp8_encode_kernel(const float* __restrict__ x, uint8_t* __restri
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     InvScale s0{1.0, 1.0f, 0.0f};
     if (SCALE == 1) s0 = make_inv_scale(static_cast<double>(__ldg(scales)));
+    if (VEC) {
+        for (int64_t i = tid; i < n / 4; i += stride) {
+            float4 v = __ldcs(reinterpret_cast<const float4*>(x) + i);
+            if (SCALE == 1) {
+                v.x = mul_round_exact(v.x, s0);
+                v.y = mul_round_exact(v.y, s0);
+                v.z = mul_round_exact(v.z, s0);
+                v.w = mul_round_exact(v.w, s0);
+            }
+            reinterpret_cast<uint32_t*>(q)[i] = e4m3_byte(v.x, HW) | (e4m3_byte(v.y, HW) << 8) |
+                                                (e4m3_byte(v.z, HW) << 16) | (e4m3_byte(v.w, HW) << 24);
+        }
+        return;
+    }
     for (int64_t i = tid; i < n; i += stride) {
         float v = x[i];
         if (SCALE == 1) v = mul_round_exact(v, s0);
-        q[i] = HW ? e4m3_encode_hw(v) : e4m3_encode_ref(__float_as_uint(v));
+        q[i] = static_cast<uint8_t>(e4m3_byte(v, HW));
     }
 }
 
 // Per-row scales: one warp per row, the row's 1/scale formed once.
-template <int HW>
+template <int HW, int VEC>
 __global__ void fp8_encode_rows_kernel(const float* __restrict__ x, uint8_t* __restrict__ q, int64_t rows,
                                        int64_t cols, const float* __restrict__ scales) {
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const int lane = threadIdx.x & 31;
     for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
         const InvScale s = make_inv_scale(static_cast<double>(__ldg(scales + r)));
+        if (VEC) {
+            const float4* xr = reinterpret_cast<const float4*>(x + r * cols);
+            uint32_t* qr = reinterpret_cast<uint32_t*>(q + r * cols);
+            for (int64_t c = lane; c < cols / 4; c += 32) {
+                const float4 v = __ldcs(xr + c);
+                qr[c] = e4m3_byte(mul_round_exact(v.x, s), HW) | (e4m3_byte(mul_round_exact(v.y, s), HW) << 8) |
+                        (e4m3_byte(mul_round_exact(v.z, s), HW) << 16) |
+                        (e4m3_byte(mul_round_exact(v.w, s), HW) << 24);
+            }
+            continue;
+        }
         for (int64_t c = lane; c < cols; c += 32) {
             const float v = mul_round_exact(x[r * cols + c], s);
-            q[r * cols + c] = HW ? e4m3_encode_hw(v) : e4m3_encode_ref(__float_as_uint(v));
+            q[r * cols + c] = static_cast<uint8_t>(e4m3_byte(v, HW));
         }
     }
 }
@@ -435,16 +493,24 @@ int launch_fp8_encode(const float* x, uint8_t* q, int64_t rows, int64_t cols, co
     const int64_t n = rows * cols;
     if (n <= 0) return TVQ_OK;
     const int threads = 256;
-    const int grid = grid_for(n, threads, 8);
-#define TVQ_FP8_LAUNCH(S, H) fp8_encode_kernel<S, H><<<grid, threads, 0, st>>>(x, q, rows, cols, scales)
-    if (scale_mode == 0) { if (hw) TVQ_FP8_LAUNCH(0, 1); else TVQ_FP8_LAUNCH(0, 0); }
-    else if (scale_mode == 1) { if (hw) TVQ_FP8_LAUNCH(1, 1); else TVQ_FP8_LAUNCH(1, 0); }
-    else {
+    const bool aligned = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && ((reinterpret_cast<uintptr_t>(q) & 3) == 0);
+    if (scale_mode == 2) {
         const int g = grid_for(rows * 32, threads, 8);
-        if (hw) fp8_encode_rows_kernel<1><<<g, threads, 0, st>>>(x, q, rows, cols, scales);
-        else fp8_encode_rows_kernel<0><<<g, threads, 0, st>>>(x, q, rows, cols, scales);
-    }
+        const bool vec = aligned && cols % 4 == 0;
+#define TVQ_FP8_ROWS(H, V) fp8_encode_rows_kernel<H, V><<<g, threads, 0, st>>>(x, q, rows, cols, scales)
+        if (hw) { if (vec) TVQ_FP8_ROWS(1, 1); else TVQ_FP8_ROWS(1, 0); }
+        else { if (vec) TVQ_FP8_ROWS(0, 1); else TVQ_FP8_ROWS(0, 0); }
+#undef TVQ_FP8_ROWS
+    } else {
+        const bool vec = aligned && n % 4 == 0;
+        const int grid = grid_for(vec ? n / 4 : n, threads, 8);
+#define TVQ_FP8_LAUNCH(S, H, V) fp8_encode_kernel<S, H, V><<<grid, threads, 0, st>>>(x, q, rows, cols, scales)
+#define TVQ_FP8_LAUNCH_V(S, H) do { if (vec) TVQ_FP8_LAUNCH(S, H, 1); else TVQ_FP8_LAUNCH(S, H, 0); } while (0)
+        if (scale_mode == 0) { if (hw) TVQ_FP8_LAUNCH_V(0, 1); else TVQ_FP8_LAUNCH_V(0, 0); }
+        else { if (hw) TVQ_FP8_LAUNCH_V(1, 1); else TVQ_FP8_LAUNCH_V(1, 0); }
+#undef TVQ_FP8_LAUNCH_V
 #undef TVQ_FP8_LAUNCH
+    }
     TVQ_CUDA(cudaGetLastError());
     return TVQ_OK;
 }
@@ -505,7 +571,7 @@ float e4m3_decode_host(uint32_t v) { return e4m3_decode_ref(v); }
 uint8_t e4m3_encode_host(float x) {
     uint32_t b;
     memcpy(&b, &x, 4);
-    return e4m3_encode_ref(b);
+    return e4m3_encode_fast(b);
 }
 
 }  // namespace tvq

@@ -3,6 +3,8 @@ repetitions), for tuning and for small profiler captures.
 
   python -m tokenvector.inference_b200.kernel_bench gemm --m 1024 --n 3072 --k 768 --epilogue gelu_q
   python -m tokenvector.inference_b200.kernel_bench lmhead --m 1024 --n 50257 --k 768
+  python -m tokenvector.inference_b200.kernel_bench hbm --m 8192 --n 6400    # calibrate / quantize GB/s
+  python -m tokenvector.inference_b200.kernel_bench sweep                     # configs 1 and 3 GEMM shapes
   python -m tokenvector.inference_b200.kernel_bench layernorm --m 1024 --n 768
   python -m tokenvector.inference_b200.kernel_bench attention --m 1024 --n 768 --heads 12
   python -m tokenvector.inference_b200.kernel_bench quantize --m 1024 --n 768
@@ -104,6 +106,71 @@ def bench_quantize(m, d, reps=20):
     return {"kernel": "quantize_i8", "n": m * d, "us": us, "gbs": m * d * 5 / us / 1e3}
 
 
+def _peaks():
+    import json
+    import os
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                     "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            m = json.load(f)
+        return m["hbm_gbs"], m["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def bench_hbm(m, d, reps=20):
+    """The memory-bound calibration / quantize kernels on an [m, d] f32
+    tensor larger than L2: GB/s of algorithmic bytes (4 B per element read
+    for max-abs, 5 B read + write for the quantizers, + 4 B per row of
+    scales) against the measured HBM copy bandwidth."""
+    torch, dev, st, flush = _env()
+    hbm, _, src = _peaks()
+    n = m * d
+    x = torch.randn((m, d), device=dev)
+    q = torch.empty((m, d), dtype=torch.int8, device=dev)
+    mm = torch.empty(2, dtype=torch.int32, device=dev)
+    first = torch.empty(1, device=dev)
+    s = torch.tensor([0.03], device=dev)
+    rs = torch.empty(m, device=dev)
+    sp = C.c_void_p(st.cuda_stream)
+    cases = [
+        ("minmax (calibrate_minmax)", 4 * n,
+         lambda: (N.call("tvq_dev_minmax_reset", _p(mm), sp),
+                  N.call("tvq_dev_minmax_accumulate", _p(x), n, _p(mm), _p(first), sp))),
+        ("quantize_i8 per tensor", 5 * n, lambda: N.call("tvq_dev_quantize_int8", _p(x), _p(q), n, _p(s), sp)),
+        ("calibrate + quantize per channel (rows)", 5 * n + 4 * m,
+         lambda: N.call("tvq_dev_calibrate_quantize_per_channel", _p(x), _p(q), _p(rs), m, d, sp)),
+        ("quantize_fp8 e4m3, per-row scale", 5 * n + 4 * m,
+         lambda: N.call("tvq_dev_quantize_fp8", _p(x), _p(q), m, d, _p(rs), 2, 0, sp)),
+    ]
+    out = []
+    N.call("tvq_dev_calibrate_quantize_per_channel", _p(x), _p(q), _p(rs), m, d, sp)
+    for name, byts, fn in cases:
+        us = _time(torch, st, flush, fn, reps)
+        out.append({"kernel": name, "m": m, "d": d, "us": us, "gbs": byts / us / 1e3,
+                    "frac_hbm": byts / us / 1e3 / hbm, "peak_source": "%s HBM copy %.0f GB/s" % (src, hbm)})
+    return out
+
+
+def bench_sweep(reps=20):
+    """The quantized GEMM on the BASELINE shapes: config 1 (INT8, M 1024, N
+    3072, K 768, per-channel f32 epilogue + bias) and the config-3 FP8 E4M3
+    grid ((K, N) in {(1024, 3072), (1024, 4096), (4096, 1024)}, M in {1, 16,
+    128, 1024, 8192}); TOPS against 2 x the measured dense bf16 rate."""
+    _, bf16, src = _peaks()
+    out = []
+    r = bench_gemm(1024, 3072, 768, "f32", reps, N.GEMM_I8)
+    r.update({"config": 1, "kind": "int8", "frac_peak": r["tops"] / (2 * bf16)})
+    out.append(r)
+    for (k, n) in [(1024, 3072), (1024, 4096), (4096, 1024)]:
+        for m in (1, 16, 128, 1024, 8192):
+            r = bench_gemm(m, n, k, "f32", reps, N.GEMM_F8)
+            r.update({"config": 3, "kind": "fp8_e4m3", "frac_peak": r["tops"] / (2 * bf16),
+                      "peak_source": "2 x %s dense bf16" % src})
+            out.append(r)
+    return out
+
+
 def bench_attention(T, d, heads, reps=20):
     torch, dev, st, flush = _env()
     qkv = torch.randn((T, 3 * d), device=dev)
@@ -164,7 +231,8 @@ def bench_gpt2(reps=20):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "lmhead", "layernorm", "quantize", "attention", "gpt2", "all"])
+    ap.add_argument("what", choices=["gemm", "lmhead", "hbm", "sweep", "layernorm", "quantize", "attention", "gpt2",
+                                     "all"])
     ap.add_argument("--m", type=int, default=1024)
     ap.add_argument("--n", type=int, default=768)
     ap.add_argument("--k", type=int, default=768)
@@ -178,6 +246,10 @@ def main():
     res = []
     if a.what == "gemm":
         res.append(bench_gemm(a.m, a.n, a.k, a.epilogue, a.reps, kind))
+    elif a.what == "hbm":
+        res.extend(bench_hbm(a.m, a.n, a.reps))
+    elif a.what == "sweep":
+        res.extend(bench_sweep(a.reps))
     elif a.what == "lmhead":
         res.append(bench_lmhead(a.m, a.n, a.k, a.reps))
     elif a.what == "layernorm":
