@@ -68,6 +68,12 @@ TVQ_API int tvq_device_count(int* n);
 /* Reads and clears the device error word of the current device (bounded
  * waits record there); returns TVQ_OK or TVQ_ERR_TIMEOUT. */
 TVQ_API int tvq_device_error(void* stream);
+/* Failure-detection self test (no reference counterpart: the reference has no
+ * device code).  Launches one kernel whose bounded mbarrier wait -- the wait
+ * every tensor-core kernel uses -- runs out after limit_us (1 .. 10^6) because
+ * nothing arrives, then reads the device error word like any call: returns
+ * TVQ_ERR_TIMEOUT with the word cleared and the context still usable. */
+TVQ_API int tvq_selftest_wait_timeout(int64_t limit_us, void* stream);
 
 /* ================================================================ host buffers
  * tv/quantization/engine.tkv */
@@ -104,6 +110,13 @@ TVQ_API int tvq_dev_calibrate_mse_curve(const float* x, int64_t n, int64_t num_c
  * per-row symmetric scales (fl32(max|W[r,:]|/127), floor 1e-8). */
 TVQ_API int tvq_calibrate_per_channel_minmax(const float* data, int64_t len, int64_t rows, int64_t cols,
                                      float* scales, int64_t n_scales);
+/* calibrate_per_channel_minmax(data, rows, cols, symmetric), engine.tkv:
+ * 202-213, with every QuantParams field per row (one launch): scale, zero
+ * point, and the row's own min / max as calibrate_minmax stores them
+ * (engine.tkv:13-36; symmetric: -am / am). */
+TVQ_API int tvq_calibrate_per_channel_params(const float* data, int64_t len, int64_t rows, int64_t cols,
+                                             int symmetric, float* scales, int64_t* zero_points, float* min_vals,
+                                             float* max_vals, int64_t n);
 /* quantize_int8_symmetric, engine.tkv:216-226 */
 TVQ_API int tvq_quantize_int8_symmetric(const float* src, int64_t n, int8_t* dst, int64_t dst_len, float scale);
 /* dequantize_int8_symmetric, engine.tkv:229-234 */
@@ -257,7 +270,12 @@ TVQ_API int tvq_dev_attention(const float* qkv, const int64_t* seg, int64_t n_se
  * TVQ_ERR_SIZE.  The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress), so make it before any stream capture.  All
  * calls share the array: calls that overlap on the GPU race on it.  No
- * cudaMalloc or cudaFree is called. */
+ * cudaMalloc or cudaFree is called.  The tile list is copied into the array
+ * from host memory, so the call blocks the calling thread until the work
+ * already queued on `stream` has finished.  It always runs the fp32 SIMT
+ * kernel (head dims 16, 32, 48, 64): bit-identical to tvq_dev_attention at
+ * head dims 16-48, within the same 1e-4 / 2e-6 tolerance of it at head dim
+ * 64, where tvq_dev_attention takes the tensor-core kernel. */
 TVQ_API int tvq_dev_attention_noalloc(const float* qkv, const int64_t* seg, int64_t n_seg, int64_t d,
                                       int64_t n_heads, float* out, int8_t* outq, const float* qscale_dev,
                                       uint32_t* amax_dev, void* stream);

@@ -83,6 +83,8 @@ def lib():
             "tvo_attention_causal": (None, [P, P, i64, i64, i64, P, i64]),
             "tvo_add": (None, [P, P, P, i64]),
             "tvo_lm_head": (None, [P, P, P, i64, i64, i64]),
+            "tvo_lm_head_plain": (None, [P, P, P, i64, i64, i64]),
+            "tvo_matmul_int8_per_channel_scalar": (i32, [P, P, P, i64, P, i64, i64, i64, f32, P, i64]),
             "tvo_gi_noise": (None, [P, i64, i64, f64]),
             "tvo_quantize_linear": (i32, [P, P, i64, i64, i64, P, i64, i64]),
             "tvo_dequantize_linear": (i32, [P, P, i64, i64, i64, P, i64, i64]),
@@ -279,6 +281,23 @@ def gemm_i8_acc(A, W) -> np.ndarray:
     return out
 
 
+def matmul_int8_per_channel_scalar(A, W, bias, scale_a: float, scales_w) -> np.ndarray:
+    """The faithful single-thread scalar form of matmul_int8_per_channel
+    (matmul.tkv:17-29, _dot_int8 :116-127): the one-core CPU baseline."""
+    A = _i8(A)
+    W = _i8(W)
+    m, k = A.shape
+    n = W.shape[0]
+    b = _f32(bias) if bias is not None else np.zeros(0, np.float32)
+    sw = _f32(scales_w)
+    Y = np.empty((m, n), dtype=np.float32)
+    rc = lib().tvo_matmul_int8_per_channel_scalar(_p(A), _p(W), _p(b) if b.size else None, b.size, _p(Y), m, n, k,
+                                                  float(scale_a), _p(sw), sw.size)
+    if rc != 0:
+        raise ValueError("scales_w smaller than N")
+    return Y
+
+
 def matmul_int8_per_channel(A, W, bias, scale_a: float, scales_w) -> np.ndarray:
     """matmul_int8_per_channel, tv/quantization/matmul.tkv:17-29"""
     A = _i8(A)
@@ -395,13 +414,15 @@ def add(a, b) -> np.ndarray:
     return out
 
 
-def lm_head(x, wte) -> np.ndarray:
+def lm_head(x, wte, plain: bool = False) -> np.ndarray:
+    """Tied LM head, gpt2_ref.tkv:603-610 (f64 sums in k order); plain=True
+    runs the one-output-at-a-time loop (same bits, slower)."""
     x = _f32(x)
     wte = _f32(wte)
     n, h = x.shape
     vocab = wte.shape[0]
     out = np.empty((n, vocab), dtype=np.float32)
-    lib().tvo_lm_head(_p(x), _p(wte), _p(out), n, vocab, h)
+    (lib().tvo_lm_head_plain if plain else lib().tvo_lm_head)(_p(x), _p(wte), _p(out), n, vocab, h)
     return out
 
 

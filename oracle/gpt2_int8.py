@@ -75,7 +75,9 @@ def blocks(layers, x, seg, scales=None, calibrator: Calibrator | None = None, qw
            eps: float = 1e-6, record=None):
     """The transformer blocks (gpt2_ref.tkv:575-588 per layer) on hidden
     states x f32 [T, d]; returns the new hidden states.  Exactly one of
-    `scales` ([L,4] static) or `calibrator` must be given."""
+    `scales` ([L,4] static) or `calibrator` must be given.  `record`: a list
+    that receives one dict of every intermediate per layer, or a callable
+    record(layer, dict) (then nothing is kept)."""
     assert (scales is None) != (calibrator is None)
     seg = np.asarray(seg, np.int64)
     if qweights is None:
@@ -87,6 +89,7 @@ def blocks(layers, x, seg, scales=None, calibrator: Calibrator | None = None, qw
         def sc(point, act):
             return calibrator.scale(li, point, act) if calibrator is not None else np.float32(scales[li][point])
 
+        x_in = x
         a = layernorm(x, L["ln1_g"], L["ln1_b"], eps)
         s0 = sc(0, a)
         q0 = quantize_int8_symmetric(a, s0)
@@ -94,16 +97,25 @@ def blocks(layers, x, seg, scales=None, calibrator: Calibrator | None = None, qw
         ctx = attention_causal(qkv, n_heads, seg)
         s1 = sc(1, ctx)
         q1 = quantize_int8_symmetric(ctx, s1)
-        x = add(x, matmul_int8_per_channel(q1, wq1, L["proj_b"], s1, sw1))
+        proj = matmul_int8_per_channel(q1, wq1, L["proj_b"], s1, sw1)
+        x = add(x, proj)
+        x_mid = x
         m = layernorm(x, L["ln2_g"], L["ln2_b"], eps)
         s2 = sc(2, m)
         q2 = quantize_int8_symmetric(m, s2)
-        g = gelu_erf_array(matmul_int8_per_channel(q2, wq2, L["fc_b"], s2, sw2))
+        fc = matmul_int8_per_channel(q2, wq2, L["fc_b"], s2, sw2)
+        g = gelu_erf_array(fc)
         s3 = sc(3, g)
         q3 = quantize_int8_symmetric(g, s3)
-        x = add(x, matmul_int8_per_channel(q3, wq3, L["mp_b"], s3, sw3))
+        mp = matmul_int8_per_channel(q3, wq3, L["mp_b"], s3, sw3)
+        x = add(x, mp)
         if record is not None:
-            record.append(dict(q0=q0, qkv=qkv, ctx=ctx, q1=q1, q2=q2, q3=q3, x=x))
+            rec = dict(x_in=x_in, a=a, s0=s0, q0=q0, qkv=qkv, ctx=ctx, s1=s1, q1=q1, proj=proj, x_mid=x_mid, m=m,
+                       s2=s2, q2=q2, fc=fc, g=g, s3=s3, q3=q3, mp=mp, x=x)
+            if callable(record):
+                record(li, rec)
+            else:
+                record.append(rec)
     return x
 
 

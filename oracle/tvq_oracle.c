@@ -32,6 +32,7 @@
 #include <stdlib.h>
 #include <string.h>
 #include <float.h>
+#include <immintrin.h>
 #ifdef _OPENMP
 #include <omp.h>
 #endif
@@ -445,6 +446,35 @@ TVO_API int tvo_matmul_int8_per_channel(const int8_t* A, const int8_t* W, const 
     return 0;
 }
 
+/* The faithful scalar form of matmul_int8_per_channel (matmul.tkv:17-29 with
+ * _dot_int8, :116-127): one thread, the reference's loop order, the 32-way
+ * unrolled i64 accumulation without vectorisation.  It is the single-core CPU
+ * baseline of the INT8 GEMM (same results as the OpenMP form above: integer
+ * sums are exact in any order). */
+__attribute__((optimize("no-tree-vectorize"))) static int64_t dot_int8_scalar(const int8_t* a, const int8_t* b,
+                                                                              int64_t k) {
+    int64_t acc = 0, kk = 0, limit = k - 31;
+    while (kk < limit) {
+        for (int l = 0; l < 32; l++) acc += (int64_t)a[kk + l] * (int64_t)b[kk + l];
+        kk += 32;
+    }
+    while (kk < k) { acc += (int64_t)a[kk] * (int64_t)b[kk]; kk++; }
+    return acc;
+}
+
+__attribute__((optimize("no-tree-vectorize"))) TVO_API int tvo_matmul_int8_per_channel_scalar(
+    const int8_t* A, const int8_t* W, const float* bias, int64_t n_bias, float* Y, int64_t m, int64_t n, int64_t k,
+    float scale_a, const float* scales_w, int64_t n_scales) {
+    if (n_scales < n) return -1;
+    for (int64_t mm = 0; mm < m; mm++)
+        for (int64_t nn = 0; nn < n; nn++) {
+            int64_t acc = dot_int8_scalar(A + mm * k, W + nn * k, k);
+            double b = (n_bias > 0) ? (double)bias[nn] : 0.0;
+            Y[mm * n + nn] = (float)((double)acc * (double)scale_a * (double)scales_w[nn] + b);
+        }
+    return 0;
+}
+
 /* matmul_int8_symmetric, tv/quantization/matmul.tkv:4-15: s = scale_a*scale_w
  * is an untyped local (f64, exact product of two f32). */
 TVO_API int tvo_matmul_int8_symmetric(const int8_t* A, const int8_t* W, const float* bias, int64_t n_bias,
@@ -631,7 +661,8 @@ TVO_API void tvo_attention_causal(const float* qkv, float* ctx, int64_t n, int64
         int64_t lo = seg[s], hi = seg[s + 1];
 #pragma omp parallel for schedule(dynamic, 4)
         for (int64_t t = lo; t < hi; t++) {
-            double* sc = (double*)malloc(sizeof(double) * (size_t)(hi - lo));
+            double* sc = (double*)malloc(sizeof(double) * (size_t)(hi - lo + hd));
+            double* pv = sc + (hi - lo);
             for (int64_t head = 0; head < nheads; head++) {
                 int64_t ho = head * hd;
                 const float* q = qkv + t * 3 * h + ho;
@@ -646,11 +677,15 @@ TVO_API void tvo_attention_causal(const float* qkv, float* ctx, int64_t n, int64
                 double tot = 0.0;
                 for (int64_t u = 0; u <= t - lo; u++) { double e = exp(sc[u] - mx); sc[u] = e; tot = tot + e; }
                 double inv_tot = 1.0 / tot;
-                for (int64_t d = 0; d < hd; d++) {
-                    double acc = 0.0;
-                    for (int64_t u = lo; u <= t; u++) acc = acc + sc[u - lo] * (double)qkv[u * 3 * h + 2 * h + ho + d];
-                    ctx[t * h + ho + d] = (float)(acc * inv_tot);
+                /* every output d sums over u in order; the d outputs advance
+                 * together so that each V row is read once, contiguously */
+                for (int64_t d = 0; d < hd; d++) pv[d] = 0.0;
+                for (int64_t u = lo; u <= t; u++) {
+                    const double p = sc[u - lo];
+                    const float* vr = qkv + u * 3 * h + 2 * h + ho;
+                    for (int64_t d = 0; d < hd; d++) pv[d] = pv[d] + p * (double)vr[d];
                 }
+                for (int64_t d = 0; d < hd; d++) ctx[t * h + ho + d] = (float)(pv[d] * inv_tot);
             }
             free(sc);
         }
@@ -664,8 +699,83 @@ TVO_API void tvo_add(const float* a, const float* b, float* out, int64_t n) {
 }
 
 /* LM head with the tied embedding, tv/training/gpt2_ref.tkv:603-610:
- * logits[i,o] = sum_k x[i,k] * wte[o,k], f64 accumulator. */
+ * logits[i,o] = sum_k x[i,k] * wte[o,k], f64 accumulator, k in order.
+ * Tiled for the cache (64 wte rows x 64 rows of x per tile, both held as
+ * f64, x transposed in groups of eight rows) and for the adder (four wte
+ * rows x eight x rows side by side): every output still keeps its own
+ * sequential k-order sum, so the bits equal the plain loop
+ * (tvo_lm_head_plain); only the order in which outputs are formed changes. */
+#define TVO_LMX 8   /* x rows per vector group */
+#define TVO_LMO 64  /* wte rows per tile */
+#define TVO_LMT 64  /* x rows per tile */
 TVO_API void tvo_lm_head(const float* x, const float* wte, float* logits, int64_t n, int64_t vocab, int64_t h) {
+    const int64_t nb = (n + TVO_LMX - 1) / TVO_LMX;
+    double* xt = (double*)malloc(sizeof(double) * (size_t)(nb * h * TVO_LMX));
+    if (!xt) return;
+    for (int64_t b = 0; b < nb; b++)
+        for (int64_t k = 0; k < h; k++)
+            for (int j = 0; j < TVO_LMX; j++) {
+                const int64_t i = b * TVO_LMX + j;
+                xt[(b * h + k) * TVO_LMX + j] = i < n ? (double)x[i * h + k] : 0.0;
+            }
+    const int64_t ntiles = (vocab + TVO_LMO - 1) / TVO_LMO;
+#pragma omp parallel
+    {
+        double* wd = (double*)malloc(sizeof(double) * (size_t)(TVO_LMO * h));
+#pragma omp for schedule(dynamic, 4)
+        for (int64_t t = 0; t < ntiles; t++) {
+            const int64_t o0 = t * TVO_LMO;
+            const int64_t no = (vocab - o0 < TVO_LMO) ? vocab - o0 : TVO_LMO;
+            if (!wd) continue;
+            for (int64_t r = 0; r < TVO_LMO; r++)
+                for (int64_t k = 0; k < h; k++) wd[r * h + k] = r < no ? (double)wte[(o0 + r) * h + k] : 0.0;
+            for (int64_t b0 = 0; b0 < nb; b0 += TVO_LMT / TVO_LMX)
+                for (int64_t r = 0; r < no; r += 4)
+                    for (int64_t b = b0; b < nb && b < b0 + TVO_LMT / TVO_LMX; b++) {
+                        const double* xb = xt + b * h * TVO_LMX;
+                        const double *w0 = wd + r * h, *w1 = w0 + h, *w2 = w1 + h, *w3 = w2 + h;
+                        /* eight lanes per wte row as two 4-wide vectors: a separate
+                         * multiply and add per lane, exactly the scalar sum */
+                        __m256d a0l = _mm256_setzero_pd(), a0h = a0l, a1l = a0l, a1h = a0l;
+                        __m256d a2l = a0l, a2h = a0l, a3l = a0l, a3h = a0l;
+                        for (int64_t k = 0; k < h; k++) {
+                            const __m256d xl = _mm256_loadu_pd(xb + k * TVO_LMX);
+                            const __m256d xh = _mm256_loadu_pd(xb + k * TVO_LMX + 4);
+                            const __m256d c0 = _mm256_broadcast_sd(w0 + k), c1 = _mm256_broadcast_sd(w1 + k);
+                            const __m256d c2 = _mm256_broadcast_sd(w2 + k), c3 = _mm256_broadcast_sd(w3 + k);
+                            a0l = _mm256_add_pd(a0l, _mm256_mul_pd(xl, c0));
+                            a0h = _mm256_add_pd(a0h, _mm256_mul_pd(xh, c0));
+                            a1l = _mm256_add_pd(a1l, _mm256_mul_pd(xl, c1));
+                            a1h = _mm256_add_pd(a1h, _mm256_mul_pd(xh, c1));
+                            a2l = _mm256_add_pd(a2l, _mm256_mul_pd(xl, c2));
+                            a2h = _mm256_add_pd(a2h, _mm256_mul_pd(xh, c2));
+                            a3l = _mm256_add_pd(a3l, _mm256_mul_pd(xl, c3));
+                            a3h = _mm256_add_pd(a3h, _mm256_mul_pd(xh, c3));
+                        }
+                        double a0[TVO_LMX], a1[TVO_LMX], a2[TVO_LMX], a3[TVO_LMX];
+                        _mm256_storeu_pd(a0, a0l); _mm256_storeu_pd(a0 + 4, a0h);
+                        _mm256_storeu_pd(a1, a1l); _mm256_storeu_pd(a1 + 4, a1h);
+                        _mm256_storeu_pd(a2, a2l); _mm256_storeu_pd(a2 + 4, a2h);
+                        _mm256_storeu_pd(a3, a3l); _mm256_storeu_pd(a3 + 4, a3h);
+                        for (int j = 0; j < TVO_LMX; j++) {
+                            const int64_t i = b * TVO_LMX + j;
+                            if (i >= n) break;
+                            float* row = logits + i * vocab + o0 + r;
+                            row[0] = (float)a0[j];
+                            if (r + 1 < no) row[1] = (float)a1[j];
+                            if (r + 2 < no) row[2] = (float)a2[j];
+                            if (r + 3 < no) row[3] = (float)a3[j];
+                        }
+                    }
+        }
+        free(wd);
+    }
+    free(xt);
+}
+
+/* The same LM head as the plain loop of the reference (one output at a time);
+ * kept to check that the interleaved form above gives the same bits. */
+TVO_API void tvo_lm_head_plain(const float* x, const float* wte, float* logits, int64_t n, int64_t vocab, int64_t h) {
 #pragma omp parallel for schedule(static)
     for (int64_t o = 0; o < vocab; o++)
         for (int64_t i = 0; i < n; i++) {

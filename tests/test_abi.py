@@ -62,3 +62,33 @@ def test_argument_errors_need_no_gpu():
         E.calibrate_per_channel_minmax(np.zeros(4, np.float32), 0, 4)
     with pytest.raises(ValueError):
         E.quantize_int8_per_channel(np.zeros(8, np.float32), np.zeros(8, np.int8), 2, 4, np.ones(1, np.float32))
+
+
+def test_attention_entry_points_refuse_bad_layouts_before_any_device_work():
+    """Negative segment offsets, head counts that do not divide d and head
+    dims without a kernel are refused on the host, before any copy or launch
+    (so no GPU is needed to see it).  The pointers are never dereferenced."""
+    import numpy as np
+    fake = ctypes.c_void_p(256)  # a non-null address that must not be touched
+    neg = np.array([-64, 100], np.int64)
+    ok = np.array([0, 100], np.int64)
+    sp = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    L = N.lib()
+    # tvq_dev_attention_noalloc (fixed device scratch)
+    assert L.tvq_dev_attention_noalloc(fake, sp(neg), 1, 768, 12, fake, None, None, None, None) == N.TVQ_ERR_INVALID
+    assert L.tvq_dev_attention_noalloc(fake, sp(ok), 1, 768, 7, fake, None, None, None, None) == N.TVQ_ERR_INVALID
+    assert L.tvq_dev_attention_noalloc(fake, sp(ok), 1, 768, 0, fake, None, None, None, None) == N.TVQ_ERR_INVALID
+    assert L.tvq_dev_attention_noalloc(fake, sp(ok), 1, 8, 16, fake, None, None, None, None) == N.TVQ_ERR_INVALID
+    assert L.tvq_dev_attention_noalloc(fake, sp(ok), 1, 1024, 8, fake, None, None, None,
+                                       None) == N.TVQ_ERR_UNSUPPORTED  # head dim 128
+    assert L.tvq_dev_attention_noalloc(fake, sp(ok), 1, (1 << 32) + 12, 12, fake, None, None, None,
+                                       None) == N.TVQ_ERR_INVALID  # no narrowing to int
+    # tvq_dev_attention (caller-provided scratch)
+    assert L.tvq_dev_attention(fake, sp(neg), 1, 768, 12, fake, 64, fake, None, None, None,
+                               None) == N.TVQ_ERR_INVALID
+    assert L.tvq_dev_attention(fake, sp(ok), 1, 768, 7, fake, 64, fake, None, None, None, None) == N.TVQ_ERR_INVALID
+
+
+def test_wait_selftest_rejects_out_of_range_limits_without_a_gpu():
+    for bad in (0, -5, 2_000_000):
+        assert N.lib().tvq_selftest_wait_timeout(bad, None) == N.TVQ_ERR_INVALID

@@ -110,6 +110,51 @@ def test_per_channel_edges():
     assert _same_f32(g[~np.isnan(g)], os_[~np.isnan(os_)])
 
 
+def _qp_fields(ps):
+    return (np.array([p.scale for p in ps], np.float32), np.array([p.zero_point for p in ps], np.int64),
+            np.array([p.min_val for p in ps], np.float32), np.array([p.max_val for p in ps], np.float32))
+
+
+def _same_bits_nan(a, b):
+    a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+    na, nb = np.isnan(a), np.isnan(b)
+    return np.array_equal(na, nb) and np.array_equal(a[~na].view(np.uint32), b[~nb].view(np.uint32))
+
+
+@pytest.mark.parametrize("symmetric", [1, 0])
+def test_per_channel_quant_params_are_the_references(symmetric):
+    """Every QuantParams field of calibrate_per_channel_minmax (engine.tkv:
+    202-213 -> calibrate_minmax per row, :13-36), one launch on the GPU,
+    against the oracle: scale, zero point and the row's own min / max, with
+    the reference's first-occurrence rule for zero extremes of either sign
+    and a NaN first element poisoning the row."""
+    rng = np.random.default_rng(11 + symmetric)
+    w = (rng.standard_normal((300, 77)) * 0.02).astype(np.float32)
+    w[1] = 0.0
+    w[2, :3] = [1.0, 0.0, -0.0]           # min 0: the +0 comes first
+    w[2, 3:] = 0.5
+    w[3, :3] = [1.0, -0.0, 0.0]           # min 0: the -0 comes first
+    w[3, 3:] = 0.5
+    w[4, :3] = [-1.0, -0.0, 0.0]          # max 0: the -0 comes first
+    w[4, 3:] = -0.5
+    w[5, 0] = np.nan                      # poisoned row
+    w[6, 10] = np.nan                     # a NaN that never wins
+    w[7] = 3.25                           # constant row (asymmetric: mx = mn + 1e-8)
+    w[8] = 1e-12                          # below the 1e-8 floor
+    w[9, 40] = np.inf
+    ps = E.calibrate_per_channel_minmax(w, 300, 77, symmetric)
+    ref = O.calibrate_per_channel_minmax(w, 300, 77, symmetric)
+    gs, gz, gmn, gmx = _qp_fields(ps)
+    rs = np.array([q.scale for q in ref], np.float32)
+    rz = np.array([q.zero_point for q in ref], np.int64)
+    rmn = np.array([q.min_val for q in ref], np.float32)
+    rmx = np.array([q.max_val for q in ref], np.float32)
+    assert _same_bits_nan(gs, rs) and np.array_equal(gz, rz)
+    assert _same_bits_nan(gmn, rmn) and _same_bits_nan(gmx, rmx)
+    if symmetric:  # the true row max, not fl32(scale) * 127
+        assert gmx[0] == np.float32(np.abs(w[0]).max())
+
+
 @pytest.mark.parametrize("rows,cols", [(512, 300), (40, 6400)])
 def test_dynamic_rowwise(rows, cols):
     x = _data(rows * cols, 5, outliers=True).reshape(rows, cols)

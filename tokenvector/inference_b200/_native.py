@@ -35,9 +35,11 @@ SIGNATURES = {
     "tvq_last_error": (i32, [C.c_char_p, i64]),
     "tvq_device_count": (i32, [P]),
     "tvq_device_error": (i32, [P]),
+    "tvq_selftest_wait_timeout": (i32, [i64, P]),
     "tvq_calibrate_minmax": (i32, [P, i64, i32, P, P, P, P]),
     "tvq_calibrate_minmax_batches": (i32, [P, P, i64, i32, P, P, P, P]),
     "tvq_calibrate_per_channel_minmax": (i32, [P, i64, i64, i64, P, i64]),
+    "tvq_calibrate_per_channel_params": (i32, [P, i64, i64, i64, i32, P, P, P, P, i64]),
     "tvq_quantize_int8_symmetric": (i32, [P, i64, P, i64, f32]),
     "tvq_dequantize_int8_symmetric": (i32, [P, i64, P, i64, f32]),
     "tvq_quantize_int8_per_channel": (i32, [P, i64, P, i64, i64, i64, P, i64]),

@@ -238,6 +238,21 @@ int host_gemm(int kind, const void* A, const void* W, size_t elem_bytes_ignored,
     return H.finish();
 }
 
+// A bounded wait on an mbarrier that nothing ever arrives at: the
+// failure-detection path of every tensor-core kernel (record a code in the
+// device error word, return), made to run out on purpose with a short
+// limit.  The CTA exits normally, so the context stays usable.
+__global__ void wait_selftest_kernel(int* err, uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    if (threadIdx.x == 0) mbar_wait_for(&bar, 0, err, DEVERR_TIMEOUT_TEST, limit_ns);
+    __syncwarp();
+}
+
 }  // namespace
 }  // namespace tvq
 
@@ -266,6 +281,17 @@ int tvq_device_count(int* n) {
 }
 
 int tvq_device_error(void* stream) { return check_device_error(static_cast<cudaStream_t>(stream)); }
+
+int tvq_selftest_wait_timeout(int64_t limit_us, void* stream) {
+    TVQ_CHECK(limit_us >= 1 && limit_us <= 1000000, TVQ_ERR_INVALID, "limit must be 1 us .. 1 s");
+    int rc = 0;
+    DeviceState* d = device_state(&rc);
+    if (!d) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    wait_selftest_kernel<<<1, 32, 0, st>>>(d->d_error, static_cast<uint64_t>(limit_us) * 1000u);
+    TVQ_CUDA(cudaGetLastError());
+    return check_device_error(st);
+}
 
 // ================================================================ host: engine.tkv
 
@@ -342,6 +368,30 @@ int tvq_calibrate_per_channel_minmax(const float* data, int64_t len, int64_t row
     STEP(H.h2d(dx, data, static_cast<size_t>(rows * cols) * 4));
     STEP(launch_rowwise(0, dx, dq, ds, rows, cols, H.st()));
     STEP(H.d2h(scales, ds, static_cast<size_t>(rows) * 4));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_calibrate_per_channel_params(const float* data, int64_t len, int64_t rows, int64_t cols, int symmetric,
+                                     float* scales, int64_t* zero_points, float* min_vals, float* max_vals,
+                                     int64_t n) {
+    // engine.tkv:203-206
+    TVQ_CHECK(rows > 0 && cols > 0, TVQ_ERR_INVALID, "rows/cols must be > 0");
+    TVQ_CHECK(len >= rows * cols, TVQ_ERR_SIZE, "data smaller than rows*cols");
+    TVQ_CHECK(data && scales && zero_points && min_vals && max_vals, TVQ_ERR_INVALID, "null buffer");
+    TVQ_CHECK(n >= rows, TVQ_ERR_SIZE, "output lists smaller than rows");
+    TVQ_TRY
+    HOST_BEGIN
+    float* dx = dev<float>(H, 0, static_cast<size_t>(rows * cols));
+    float* dp = dev<float>(H, 1, static_cast<size_t>(rows) * 5 + 2);  // scale, min, max, then i64 zero points
+    if (H.rc) return H.rc;
+    int64_t* dz = reinterpret_cast<int64_t*>(dp + 3 * rows + (rows & 1));
+    STEP(H.h2d(dx, data, static_cast<size_t>(rows * cols) * 4));
+    STEP(launch_rowwise_params(dx, rows, cols, symmetric ? 1 : 0, dp, dz, dp + rows, dp + 2 * rows, H.st()));
+    STEP(H.d2h(scales, dp, static_cast<size_t>(rows) * 4));
+    STEP(H.d2h(min_vals, dp + rows, static_cast<size_t>(rows) * 4));
+    STEP(H.d2h(max_vals, dp + 2 * rows, static_cast<size_t>(rows) * 4));
+    STEP(H.d2h(zero_points, dz, static_cast<size_t>(rows) * 8));
     return H.finish();
     TVQ_CATCH
 }

@@ -164,15 +164,15 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 
 // Bounded wait for the phase of `bar` with the given parity to complete.
-// Returns false (and records `code`) when TVQ_WAIT_LIMIT_NS elapses first.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+// Returns false (and records `code`) when limit_ns elapses first.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err, int code, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     uint32_t spins = 0;
     while (true) {
         if (mbar_try_wait_sleep(bar, parity, TVQ_WAIT_SLEEP_NS)) return true;
         if ((++spins & 63u) == 0u) {
-            if (globaltimer_ns() - t0 > TVQ_WAIT_LIMIT_NS) {
+            if (globaltimer_ns() - t0 > limit_ns) {
                 record_error(err, code);
                 return false;
             }
@@ -180,6 +180,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
             if (err && *(volatile int*)err != 0) return false;
         }
     }
+}
+
+// The same with the library's limit, TVQ_WAIT_LIMIT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+    return mbar_wait_for(bar, parity, err, code, TVQ_WAIT_LIMIT_NS);
 }
 
 // 2-D TMA tile load global -> shared, completing bytes on `bar`.

@@ -19,6 +19,10 @@ int launch_quantize_i8_amax(const float* x, int8_t* q, int64_t n, const uint32_t
                             cudaStream_t st);
 int launch_dequantize_i8(const int8_t* q, float* y, int64_t rows, int64_t cols, const float* scales_dev,
                          int per_row, cudaStream_t st);
+// calibrate_per_channel_minmax with all four QuantParams fields per row
+// (scale, zero point, min, max), symmetric or asymmetric.
+int launch_rowwise_params(const float* x, int64_t rows, int64_t cols, int symmetric, float* scale, int64_t* zp,
+                          float* mn, float* mx, cudaStream_t st);
 // mode 0: per-channel calibrate+quantize, 1: per-channel quantize with given
 // scales, 2: dynamic row-wise
 int launch_rowwise(int mode, const float* x, int8_t* q, float* scales, int64_t rows, int64_t cols,

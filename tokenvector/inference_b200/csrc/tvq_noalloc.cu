@@ -14,6 +14,15 @@
 // array and overwrites the part it uses before reading it, so nothing needs
 // clearing; calls that overlap on the GPU (other streams, other threads)
 // race on it and must be serialised by the caller.
+//
+// The tile list is built on the host and copied into the array with
+// pageable cudaMemcpyAsync calls from a stack buffer, so a call blocks the
+// calling thread until the work already queued on its stream has finished
+// and the last copy has been staged.  It always runs the fp32 SIMT
+// attention kernel (head dims 16, 32, 48 and 64): the tensor-core kernel
+// that tvq_dev_attention uses at head dim 64 needs fp16 operand copies of
+// the whole qkv tensor as scratch, far beyond a modest fixed array.
+#include <atomic>
 #include <mutex>
 
 #include "tvq_common.cuh"
@@ -28,7 +37,7 @@ constexpr int64_t kNoallocMaxTiles = 32768;
 __device__ __align__(256) int4 g_noalloc_tiles[kNoallocMaxTiles];
 
 constexpr int kMaxDevices = 64;
-int4* g_tiles_dev[kMaxDevices] = {};
+std::atomic<int4*> g_tiles_dev[kMaxDevices] = {};
 std::mutex g_setup_mu;
 
 // Device address of g_noalloc_tiles on the current device (set-up on first use).
@@ -36,16 +45,19 @@ int tiles_address(int4** out) {
     int dev = 0;
     TVQ_CUDA(cudaGetDevice(&dev));
     TVQ_CHECK(dev >= 0 && dev < kMaxDevices, TVQ_ERR_UNSUPPORTED, "device ordinal too large");
-    if (!g_tiles_dev[dev]) {
+    int4* ptr = g_tiles_dev[dev].load(std::memory_order_acquire);
+    if (!ptr) {
         std::lock_guard<std::mutex> lk(g_setup_mu);
-        if (!g_tiles_dev[dev]) {
+        ptr = g_tiles_dev[dev].load(std::memory_order_relaxed);
+        if (!ptr) {
             void* p = nullptr;
             cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_tiles);
             if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress (no-allocation attention scratch)");
-            g_tiles_dev[dev] = static_cast<int4*>(p);
+            ptr = static_cast<int4*>(p);
+            g_tiles_dev[dev].store(ptr, std::memory_order_release);
         }
     }
-    *out = g_tiles_dev[dev];
+    *out = ptr;
     return TVQ_OK;
 }
 
@@ -59,6 +71,12 @@ extern "C" int tvq_dev_attention_noalloc(const float* qkv, const int64_t* seg, i
                                          uint32_t* amax_dev, void* stream) {
     TVQ_CHECK(qkv && seg && n_seg >= 1 && (out || outq || amax_dev), TVQ_ERR_INVALID, "bad arguments");
     TVQ_CHECK(!outq || qscale_dev, TVQ_ERR_INVALID, "int8 output needs a scale");
+    // every size check comes before any copy or launch
+    TVQ_CHECK(n_heads > 0 && d > 0 && n_heads <= d && d % n_heads == 0 && d < (1LL << 29), TVQ_ERR_INVALID,
+              "d must be a positive multiple of the head count");
+    const int64_t hd = d / n_heads;
+    TVQ_CHECK(hd == 16 || hd == 32 || hd == 48 || hd == 64, TVQ_ERR_UNSUPPORTED, "head dim must be 16, 32, 48 or 64");
+    TVQ_CHECK(seg[0] >= 0, TVQ_ERR_INVALID, "segment offsets must be non-negative");
     int64_t ntiles = 0;
     for (int64_t s = 0; s < n_seg; s++) {
         TVQ_CHECK(seg[s + 1] >= seg[s], TVQ_ERR_INVALID, "segments must be non-decreasing");

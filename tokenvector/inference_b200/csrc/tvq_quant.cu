@@ -107,20 +107,9 @@ __global__ void minmax_reset_kernel(uint32_t* mm) {
 
 __global__ void copy_first_kernel(const float* x, float* first) { *first = x[0]; }
 
-// QuantParams from the accumulated min/max, exactly as engine.tkv:13-36 in
-// f64 with f32 field stores.  params = {scale, zero_point, min, max}.
-__global__ void minmax_finalize_kernel(const uint32_t* mm, const float* first, int symmetric, float* params) {
-    double mn, mx;
-    const bool poisoned = first && (*first != *first);
-    if (poisoned) {
-        mn = mx = __longlong_as_double(0x7FF8000000000000ll);
-    } else if (mm[0] == 0xFFFFFFFFu && mm[1] == 0u) {
-        // nothing but NaNs after data[0]: cannot happen with data[0] finite
-        mn = mx = 0.0;
-    } else {
-        mn = ord2f(mm[0]);
-        mx = ord2f(mm[1]);
-    }
+// QuantParams from a min and max, exactly as engine.tkv:24-36 in f64 with f32
+// field stores.  params = {scale, zero_point, min, max}.
+__device__ __forceinline__ void params_from_minmax(double mn, double mx, int symmetric, float* params) {
     if (symmetric) {
         double am = fabs(mx);
         if (fabs(mn) > am) am = fabs(mn);
@@ -141,6 +130,96 @@ __global__ void minmax_finalize_kernel(const uint32_t* mm, const float* first, i
     params[1] = static_cast<float>(zp);
     params[2] = __double2float_rn(mn);
     params[3] = __double2float_rn(mx);
+}
+
+// QuantParams from the accumulated min/max (engine.tkv:13-36).
+__global__ void minmax_finalize_kernel(const uint32_t* mm, const float* first, int symmetric, float* params) {
+    double mn, mx;
+    const bool poisoned = first && (*first != *first);
+    if (poisoned) {
+        mn = mx = __longlong_as_double(0x7FF8000000000000ll);
+    } else if (mm[0] == 0xFFFFFFFFu && mm[1] == 0u) {
+        // nothing but NaNs after data[0]: cannot happen with data[0] finite
+        mn = mx = 0.0;
+    } else {
+        mn = ord2f(mm[0]);
+        mx = ord2f(mm[1]);
+    }
+    params_from_minmax(mn, mx, symmetric, params);
+}
+
+// The reference's running extreme of one row: `v < mn` / `v > mx` from
+// data[0] on keeps the FIRST element (in index order) of the extreme value
+// (which decides the sign of a zero extreme), never takes a NaN, and stays
+// NaN when data[0] is NaN.  A candidate is (value, index); idx < 0 = none.
+struct Extreme {
+    float v;
+    int64_t i;
+};
+template <bool MIN>
+__device__ __forceinline__ Extreme better(Extreme a, Extreme b) {
+    if (b.i < 0) return a;
+    if (a.i < 0) return b;
+    const bool take = MIN ? (b.v < a.v || (b.v == a.v && b.i < a.i)) : (b.v > a.v || (b.v == a.v && b.i < a.i));
+    return take ? b : a;
+}
+template <bool MIN>
+__device__ __forceinline__ Extreme warp_extreme(Extreme e) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        Extreme t;
+        t.v = __shfl_xor_sync(0xffffffffu, e.v, o);
+        t.i = __shfl_xor_sync(0xffffffffu, e.i, o);
+        e = better<MIN>(e, t);
+    }
+    return e;
+}
+
+// calibrate_per_channel_minmax(data, rows, cols, symmetric), engine.tkv:
+// 202-213: calibrate_minmax of every row, one warp per row, all four
+// QuantParams fields (the true row extremes, not rebuilt from the scale).
+__global__ void rowwise_params_kernel(const float* __restrict__ x, int64_t rows, int64_t cols, int symmetric,
+                                      float* __restrict__ scale, int64_t* __restrict__ zp, float* __restrict__ mnv,
+                                      float* __restrict__ mxv) {
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int lane = threadIdx.x & 31;
+    for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+        const float* xr = x + r * cols;
+        Extreme lo{0.0f, -1}, hi{0.0f, -1};
+        for (int64_t c = lane; c < cols; c += 32) {
+            const float v = xr[c];
+            if (v != v) continue;  // a NaN never wins a comparison
+            if (lo.i < 0 || v < lo.v) lo = Extreme{v, c};
+            if (hi.i < 0 || v > hi.v) hi = Extreme{v, c};
+        }
+        lo = warp_extreme<true>(lo);
+        hi = warp_extreme<false>(hi);
+        if (lane == 0) {
+            double mn, mx;
+            if (xr[0] != xr[0]) {
+                mn = mx = __longlong_as_double(0x7FF8000000000000ll);
+            } else {
+                mn = lo.v;
+                mx = hi.v;
+            }
+            float p[4];
+            params_from_minmax(mn, mx, symmetric, p);
+            scale[r] = p[0];
+            zp[r] = static_cast<int64_t>(p[1]);
+            mnv[r] = p[2];
+            mxv[r] = p[3];
+        }
+    }
+}
+
+int launch_rowwise_params(const float* x, int64_t rows, int64_t cols, int symmetric, float* scale, int64_t* zp,
+                          float* mn, float* mx, cudaStream_t st) {
+    if (rows <= 0 || cols <= 0) return TVQ_OK;
+    const int threads = 256;
+    rowwise_params_kernel<<<grid_for(rows * 32, threads, 8), threads, 0, st>>>(x, rows, cols, symmetric, scale, zp, mn,
+                                                                              mx);
+    TVQ_CUDA(cudaGetLastError());
+    return TVQ_OK;
 }
 
 int launch_minmax_reset(uint32_t* mm, cudaStream_t st) {

@@ -927,7 +927,10 @@ int tvq_dev_attention(const float* qkv, const int64_t* seg, int64_t n_seg, int64
     TVQ_CHECK((reinterpret_cast<uintptr_t>(tiles_dev32) & 15) == 0, TVQ_ERR_UNSUPPORTED, "tile buffer must be 16-byte aligned");
     TVQ_CHECK(qkv && seg && n_seg >= 1 && tiles_dev && (out || outq || amax_dev), TVQ_ERR_INVALID, "bad arguments");
     TVQ_CHECK(!outq || qscale_dev, TVQ_ERR_INVALID, "int8 output needs a scale");
-    TVQ_CHECK(n_heads > 0 && d % n_heads == 0, TVQ_ERR_INVALID, "d must be a multiple of the head count");
+    TVQ_CHECK(n_heads > 0 && d > 0 && n_heads <= d && d % n_heads == 0 && d < (1LL << 29), TVQ_ERR_INVALID,
+              "d must be a positive multiple of the head count");
+    TVQ_CHECK(seg[0] >= 0 && seg[n_seg] < (1LL << 31), TVQ_ERR_INVALID,
+              "segment offsets must lie in [0, 2^31)");
     // head dim 64: the tensor-core kernel, 128-row query tiles with their key
     // ranges (two entries per tile); otherwise the fp32 kernel, 64-row tiles
     const bool tc = d / n_heads == 64;

@@ -50,16 +50,13 @@ def calibrate_per_channel_minmax(data, rows: int, cols: int, symmetric: int = 1)
     d = B.host_f32(data).ravel()
     if d.size < rows * cols:
         raise ValueError("data smaller than rows*cols")
-    if not symmetric:
-        return [calibrate_minmax(d[r * cols:(r + 1) * cols], 0) for r in range(rows)]
-    scales = np.empty(rows, np.float32)
-    N.call("tvq_calibrate_per_channel_minmax", B.ptr(d), d.size, rows, cols, B.ptr(scales), rows)
-    out = []
-    for s in scales:
-        s = float(s)
-        am = s * 127.0  # min/max fields are only informative here
-        out.append(QuantParams(s, 0, -am, am))
-    return out
+    sc = np.empty(rows, np.float32)
+    zp = np.empty(rows, np.int64)
+    mn = np.empty(rows, np.float32)
+    mx = np.empty(rows, np.float32)
+    N.call("tvq_calibrate_per_channel_params", B.ptr(d), d.size, rows, cols, int(bool(symmetric)), B.ptr(sc),
+           B.ptr(zp), B.ptr(mn), B.ptr(mx), rows)
+    return [QuantParams(float(sc[r]), int(zp[r]), float(mn[r]), float(mx[r])) for r in range(rows)]
 
 
 def _i8_dst(dst):
