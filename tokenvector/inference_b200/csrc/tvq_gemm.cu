@@ -105,6 +105,7 @@ struct KParams {
     int kvd, vt_pitch;
     int* kv_exp;
     const float* kv_bound;
+    uint32_t* kv_vmax;  // per head max |V| (float bits) or null
 };
 
 // hi / lo fp16 pair of two scaled values, packed two per 32-bit word
@@ -163,6 +164,50 @@ __device__ __forceinline__ void gelu_erf_x2(float& v0, float& v1) {
     uint64_t E = f2_fma(NEX, P, f2_pack(1.0f, 1.0f));
     E ^= X & 0x8000000080000000ull;  // erf is odd
     f2_unpack(f2_mul(f2_mul(f2_pack(0.5f, 0.5f), V), f2_add(f2_pack(1.0f, 1.0f), E)), v0, v1);
+}
+
+// The reference's gelu_erf (tv/training/tensor.tkv:165-190) as the reference
+// evaluates it: binary64 arithmetic, binary32 stores of erf's argument, of
+// erf's result and of the GELU (the oracle's tvo_gelu_erf, operation for
+// operation; exp is the CUDA binary64 exp, within 1 ulp).
+__device__ __noinline__ float gelu_erf_ref(float v) {
+    const float arg = __double2float_rn(__ddiv_rn(static_cast<double>(v), 1.4142135623730951));
+    const double sg = arg < 0.0f ? -1.0 : 1.0;
+    const double ax = fabs(static_cast<double>(arg));
+    const double t = __ddiv_rn(1.0, __dadd_rn(1.0, __dmul_rn(0.3275911, ax)));
+    double poly = 1.061405429;
+    poly = __dadd_rn(__dmul_rn(poly, t), -1.453152027);
+    poly = __dadd_rn(__dmul_rn(poly, t), 1.421413741);
+    poly = __dadd_rn(__dmul_rn(poly, t), -0.284496736);
+    poly = __dadd_rn(__dmul_rn(poly, t), 0.254829592);
+    poly = __dmul_rn(poly, t);
+    const double e = exp(__dmul_rn(-ax, ax));
+    const float erf = __double2float_rn(__dmul_rn(sg, __dadd_rn(1.0, -__dmul_rn(e, poly))));
+    return __double2float_rn(__dmul_rn(__dmul_rn(0.5, static_cast<double>(v)), __dadd_rn(1.0, static_cast<double>(erf))));
+}
+
+// GELU outputs g (from gelu_erf_x2) that an int8 quantize with hi = fl32(1 /
+// scale) could round differently from the reference's own GELU value are
+// re-evaluated with gelu_erf_ref.  The fast GELU lies within 2^-19 (1 + |g|)
+// of the reference's (measured on B200 over 4M inputs in [-12, 12] and N(0,
+// 9): at most 2^-21 + 2^-21.8 |g|), so the int8 value can differ only when
+// g * hi lies within 2^-19 (1 + |g|) hi (+ 2^-16 for the product's own
+// rounding) of a half-integer; about 1e-4 of the elements at GPT-2 scales.
+template <int N>
+__device__ __forceinline__ void gelu_fix_near_boundary(float (&g)[N], const float (&v)[N], float hi) {
+    uint32_t near = 0;
+#pragma unroll
+    for (int j = 0; j < N; j++) {
+        const float t = __fmul_rn(g[j], hi);
+        const float r = __fsub_rn(__fadd_rn(t, 12582912.0f), 12582912.0f);  // rint for |t| < 2^22
+        const float m = fmaf(fabsf(g[j]) + 1.0f, hi * 1.9073486328125e-06f, 1.52587890625e-05f);
+        near |= (fabsf(fabsf(__fsub_rn(t, r)) - 0.5f) < m) ? (1u << j) : 0u;
+    }
+    if (near) {
+#pragma unroll
+        for (int j = 0; j < N; j++)
+            if (near & (1u << j)) g[j] = gelu_erf_ref(v[j]);
+    }
 }
 
 __device__ __forceinline__ float apply_act(float y, int act) {
@@ -749,10 +794,25 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                             p.vtl[vo + static_cast<int64_t>(j) * p.vt_pitch] = __float2half_rn(__fsub_rn(v, __half2float(h)));
                         }
                     }
+                    if (part == 2 && p.kv_vmax) {  // the head's max |V| (warp-uniform branch)
+                        float vm = 0.0f;
+                        if (row0 + lane < p.m) {
+#pragma unroll
+                            for (int j = 0; j < E::CH; j++) vm = fmaxf(vm, fabsf(y[j]));
+                        }
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, o));
+                        if (lane == 0) atomicMax(p.kv_vmax + hh, __float_as_uint(vm));
+                    }
                 }
                 if (p.act == TVQ_ACT_GELU_ERF) {
+                    float pre[E::CH];
+#pragma unroll
+                    for (int j = 0; j < E::CH; j++) pre[j] = y[j];
 #pragma unroll
                     for (int j = 0; j < E::CH; j += 2) gelu_erf_x2(y[j], y[j + 1]);
+                    // the int8 output is the reference's: exact GELU where it matters
+                    if (p.Yq) gelu_fix_near_boundary<E::CH>(y, pre, ec.qs.hi);
                 } else if (p.act == TVQ_ACT_GELU_TANH) {
 #pragma unroll
                     for (int j = 0; j < E::CH; j++) y[j] = gelu_tanh_f32(y[j]);
@@ -1037,6 +1097,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.vt_pitch = g.vt_pitch;
     p.kv_exp = g.kv_exp;
     p.kv_bound = g.kv_bound;
+    p.kv_vmax = g.kv_vmax;
     p.acc_only = acc_only ? 1 : 0;
     p.act = g.act;
     p.scale_out = g.scale_out;

@@ -43,11 +43,22 @@ int launch_split_kv(const float* qkv, int T, int d, void* qh, void* ql, void* kh
 // sw, bias or null) for the epilogue's Q / K / V split (GemmArgs::kv_bound).
 int launch_kv_head_bound(const int8_t* W, const float* sw, const float* bias, int k, int kvd, float* out,
                          cudaStream_t st);
+// Exact int8 context (optional, with outq): vmax [nheads] = max |V| per head
+// (float bits), list [cap] of rows to recompute, n / done: two device ints,
+// zero before the first launch (the fix-up kernel leaves them zero).  The
+// fix-up reads the f32 qkv, so qkv must hold the values when it is given.
+struct AttnFix {
+    const uint32_t* vmax = nullptr;
+    int4* list = nullptr;
+    int* n = nullptr;
+    int* done = nullptr;
+    int cap = 0;
+};
 int launch_attention_tc(const float* qkv, const void* qh, const void* ql, const void* kh, const void* kl,
                         const void* vth, const void* vtl, const int* kv_exp, int T, const int4* tiles,
                         const int4* split, int nitems, const int4* comb, int ncomb, int d, int nheads, float* out,
                         int8_t* outq, const float* qscale, uint32_t* amax, float* part_o, float2* part_ml,
-                        int* counters, cudaStream_t st);
+                        int* counters, cudaStream_t st, const AttnFix* fix = nullptr);
 int launch_scale_from_amax(const uint32_t* amax, float* scale, int n, cudaStream_t st);
 int launch_transpose(const float* a, float* b, int rows, int cols, cudaStream_t st);
 int launch_token_seg(const int* seg, int nseg, int* tok_start, cudaStream_t st);

@@ -73,6 +73,9 @@ struct GemmArgs {
     int kvd = 0, vt_pitch = 0;
     int* kv_exp = nullptr;
     const float* kv_bound = nullptr;
+    // with the operand split: max |V| of each head (float bits, atomicMax;
+    // zeroed by the caller), the attention's exact-int8 error bound
+    uint32_t* kv_vmax = nullptr;
 };
 int launch_gemm(const GemmArgs& g, cudaStream_t st);
 // Tensor map of a row-major f32 matrix [rows, cols] (row pitch `pitch`

@@ -72,6 +72,12 @@ struct Session {
     // split Q, K and V^T, fp16 bits (tensor-core attention), and their head scales
     uint16_t *qh = nullptr, *ql = nullptr, *kh = nullptr, *kl = nullptr, *vh = nullptr, *vl = nullptr;
     int* kv_exp = nullptr;
+    // exact int8 context: per layer and head max |V| (written by c_attn), the
+    // attention's fix-up list and its two counters (zero between launches)
+    uint32_t* vmax = nullptr;
+    int* fix_n = nullptr;
+    int4* fix_list = nullptr;
+    int fix_cap = 0;
     float *x = nullptr, *qkv = nullptr, *hf = nullptr, *xf = nullptr, *xf_last = nullptr, *logits = nullptr;
     size_t logits_cap = 0;
     int8_t *aq = nullptr, *hq = nullptr;
@@ -171,7 +177,8 @@ void lin_shape(const Session& s, int which, int* n, int* k) {
 }
 
 int gemm(Session& s, const int8_t* A, const Lin& l, const float* scale_a, float* Y, const float* residual,
-         int8_t* Yq, const float* scale_out, uint32_t* amax, int act, bool kv_split = false) {
+         int8_t* Yq, const float* scale_out, uint32_t* amax, int act, bool kv_split = false,
+         uint32_t* kv_vmax = nullptr) {
     GemmArgs g;
     if (kv_split) {  // c_attn on the tensor-core attention path: Q, K and V^T operands from the epilogue
         g.qh = s.qh;
@@ -182,7 +189,9 @@ int gemm(Session& s, const int8_t* A, const Lin& l, const float* scale_a, float*
         g.vtl = s.vl;
         g.kv_exp = s.kv_exp;
         g.kv_bound = l.kvb;
-        Y = nullptr;  // the attention reads only the fp16 operands: no f32 qkv
+        // the f32 qkv is still written: the attention's exact fix-up of its
+        // undecided int8 rows reads it, with the head maxima of V
+        g.kv_vmax = kv_vmax;
         g.kvd = s.d;
         g.vt_pitch = attention_tc_pitch(s.T);
     }
@@ -205,10 +214,16 @@ int gemm(Session& s, const int8_t* A, const Lin& l, const float* scale_a, float*
     return launch_gemm(g, s.st);
 }
 
-int attention(Session& s, float* out, int8_t* outq, const float* qscale, uint32_t* amax) {
+int attention(Session& s, int layer, float* out, int8_t* outq, const float* qscale, uint32_t* amax) {
     if (s.attn_tc) {  // K / V^T hi-lo come from the c_attn epilogue
+        AttnFix fx;
+        fx.vmax = s.vmax + static_cast<size_t>(layer) * s.heads;
+        fx.list = s.fix_list;
+        fx.n = s.fix_n;
+        fx.done = s.fix_n + 1;
+        fx.cap = s.fix_cap;
         return launch_attention_tc(s.qkv, s.qh, s.ql, s.kh, s.kl, s.vh, s.vl, s.kv_exp, s.T, s.tiles, s.split, s.ntiles, s.comb, s.ncomb,
-                                   s.d, s.heads, out, outq, qscale, amax, s.part_o, s.part_ml, s.counters, s.st);
+                                   s.d, s.heads, out, outq, qscale, amax, s.part_o, s.part_ml, s.counters, s.st, &fx);
     }
     return launch_attention_split(s.qkv, s.tiles, s.split, s.ntiles, s.comb, s.ncomb, s.d, s.heads, out, outq, qscale,
                                   amax, s.part_o, s.part_ml, s.st);
@@ -256,6 +271,8 @@ int enqueue_layers(Session& s, bool calibrating) {
     const int T = s.T, d = s.d;
     if (s.attn_tc && s.ncomb > 0)  // merge counters start at 0 (a run that stopped early may leave them set)
         TVQ_CUDA(cudaMemsetAsync(s.counters, 0, sizeof(int) * static_cast<size_t>(s.ncomb) * s.heads, s.st));
+    if (s.attn_tc)  // head maxima of V (atomicMax from c_attn) and the fix-up counters start at 0
+        TVQ_CUDA(cudaMemsetAsync(s.vmax, 0, sizeof(uint32_t) * (static_cast<size_t>(s.layers) * s.heads + 2), s.st));
     for (int l = 0; l < s.layers; l++) {
         LayerW& w = s.L[l];
         float* sc = s.act_scale + 4 * l;
@@ -271,16 +288,17 @@ int enqueue_layers(Session& s, bool calibrating) {
             STEP(mark(s, ST_LN));
         }
         // c_attn: qkv = dequant(aq Wqkv) + b
-        STEP(gemm(s, s.aq, w.lin[0], sc + 0, s.qkv, nullptr, nullptr, nullptr, nullptr, TVQ_ACT_NONE, s.attn_tc));
+        STEP(gemm(s, s.aq, w.lin[0], sc + 0, s.qkv, nullptr, nullptr, nullptr, nullptr, TVQ_ACT_NONE, s.attn_tc,
+                  s.vmax + static_cast<size_t>(l) * s.heads));
         STEP(mark(s, ST_GEMM_QKV));
         // causal attention -> int8 context (attn c_proj input)
         if (calibrating) {
-            STEP(attention(s, s.hf, nullptr, nullptr, am + 1));
+            STEP(attention(s, l, s.hf, nullptr, nullptr, am + 1));
             STEP(mark(s, ST_ATTN));
             STEP(launch_quantize_i8_amax(s.hf, s.aq, static_cast<int64_t>(T) * d, am + 1, sc + 1, s.st));
             STEP(mark(s, ST_QUANT));
         } else {
-            STEP(attention(s, nullptr, s.aq, sc + 1, nullptr));
+            STEP(attention(s, l, nullptr, s.aq, sc + 1, nullptr));
             STEP(mark(s, ST_ATTN));
         }
         // attn c_proj + residual, in place on x
@@ -497,6 +515,13 @@ int tvq_session_create(int device, int64_t vocab, int64_t d_model, int64_t n_hea
         STEP(s->alloc(&s->hq, MT * F));
         STEP(s->alloc(&s->err, 1));
         STEP(s->alloc(&s->kv_exp, static_cast<size_t>(3 * n_heads)));
+        // head maxima of V per layer, then the fix-up list's two counters
+        STEP(s->alloc(&s->vmax, static_cast<size_t>(std::max<int64_t>(n_layers, 1) * n_heads + 2)));
+        s->fix_n = reinterpret_cast<int*>(s->vmax + std::max<int64_t>(n_layers, 1) * n_heads);
+        TVQ_CUDA(cudaMemset(s->vmax, 0, sizeof(uint32_t) * (std::max<int64_t>(n_layers, 1) * n_heads + 2)));
+        // at most one entry per (token, head, half of the head's columns)
+        s->fix_cap = static_cast<int>(std::min<int64_t>(2 * max_tokens * n_heads, INT32_MAX));
+        STEP(s->alloc(&s->fix_list, static_cast<size_t>(s->fix_cap)));
         TVQ_CUDA(cudaMemset(s->err, 0, sizeof(int)));
         std::lock_guard<std::mutex> lk(g_mu);
         *handle = g_next++;
@@ -955,18 +980,29 @@ int tvq_dev_attention(const float* qkv, const int64_t* seg, int64_t n_seg, int64
         // fp16 Q / K / V^T hi + lo (n4 halves each), then 3 heads exponents
         // and 3 heads amax words
         const size_t n4 = std::max<size_t>((static_cast<size_t>(attention_tc_pitch(T)) * d + 7) & ~size_t(7), 8);
+        // + the exact-int8 fix-up list (16-byte entries, one per token, head
+        // and half) and its two counters
+        const int64_t fcap = outq ? 2 * static_cast<int64_t>(T) * n_heads : 0;
+        TVQ_CHECK(fcap <= INT32_MAX, TVQ_ERR_UNSUPPORTED, "too many tokens x heads for the int8 fix-up list");
         uint16_t* kv = nullptr;
-        TVQ_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&kv), sizeof(uint16_t) * 6 * n4 + sizeof(int) * 6 * n_heads,
-                                 st));
+        const size_t kv_bytes = (sizeof(uint16_t) * 6 * n4 + sizeof(int) * 6 * n_heads + 2 * sizeof(int) + 15) & ~size_t(15);
+        TVQ_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&kv), kv_bytes + sizeof(int4) * static_cast<size_t>(fcap), st));
         int* kv_exp = reinterpret_cast<int*>(kv + 6 * n4);
         uint32_t* kv_amax = reinterpret_cast<uint32_t*>(kv_exp + 3 * n_heads);
+        AttnFix fx;
+        fx.vmax = kv_amax + 2 * n_heads;  // the V part's exact head maxima (launch_split_kv)
+        fx.n = reinterpret_cast<int*>(kv_amax + 3 * n_heads);
+        fx.done = fx.n + 1;
+        fx.list = reinterpret_cast<int4*>(reinterpret_cast<char*>(kv) + kv_bytes);
+        fx.cap = static_cast<int>(fcap);
+        if (fcap) TVQ_CUDA(cudaMemsetAsync(fx.n, 0, 2 * sizeof(int), st));
         int r = launch_split_kv(qkv, T, static_cast<int>(d), kv, kv + n4, kv + 2 * n4, kv + 3 * n4, kv + 4 * n4,
                                 kv + 5 * n4, kv_exp, kv_amax, st);
         if (!r)
             r = launch_attention_tc(qkv, kv, kv + n4, kv + 2 * n4, kv + 3 * n4, kv + 4 * n4, kv + 5 * n4, kv_exp, T,
                                     tiles_dev, tiles_dev + n,
                                     static_cast<int>(n), nullptr, 0, static_cast<int>(d), static_cast<int>(n_heads), out,
-                                    outq, qscale_dev, amax_dev, nullptr, nullptr, nullptr, st);
+                                    outq, qscale_dev, amax_dev, nullptr, nullptr, nullptr, st, fcap ? &fx : nullptr);
         cudaError_t e = cudaFreeAsync(kv, st);
         if (!r && e != cudaSuccess) return cuda_fail(e, "cudaFreeAsync");
         return r;
