@@ -1,15 +1,15 @@
 """Per-kernel timings of libtvq on one GPU (CUDA events, L2 flushed between
 repetitions), for tuning and for small profiler captures.
 
-  python -m tokenvector.inference_b200.kernel_bench gemm --m 1024 --n 3072 --k 768 --epilogue gelu_q
-  python -m tokenvector.inference_b200.kernel_bench lmhead --m 1024 --n 50257 --k 768
-  python -m tokenvector.inference_b200.kernel_bench hbm --m 8192 --n 6400    # calibrate / quantize GB/s
-  python -m tokenvector.inference_b200.kernel_bench sweep                     # configs 1 and 3 GEMM shapes
-  python -m tokenvector.inference_b200.kernel_bench layernorm --m 1024 --n 768
-  python -m tokenvector.inference_b200.kernel_bench attention --m 1024 --n 768 --heads 12
-  python -m tokenvector.inference_b200.kernel_bench quantize --m 1024 --n 768
-  python -m tokenvector.inference_b200.kernel_bench gpt2       # stage times of the 124M forward
-  python -m tokenvector.inference_b200.kernel_bench all        # the GPT-2 124M shapes
+  python kernel_bench.py gemm --m 1024 --n 3072 --k 768 --epilogue gelu_q
+  python kernel_bench.py lmhead --m 1024 --n 50257 --k 768
+  python kernel_bench.py hbm --m 8192 --n 6400    # calibrate / quantize GB/s
+  python kernel_bench.py sweep                     # configs 1 and 3 GEMM shapes
+  python kernel_bench.py layernorm --m 1024 --n 768
+  python kernel_bench.py attention --m 1024 --n 768 --heads 12
+  python kernel_bench.py quantize --m 1024 --n 768
+  python kernel_bench.py gpt2       # stage times of the 124M forward
+  python kernel_bench.py all        # the GPT-2 124M shapes
 """
 from __future__ import annotations
 
@@ -19,7 +19,12 @@ import json
 
 import numpy as np
 
-from . import _native as N
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+from tokenvector.inference_b200 import _native as N  # noqa: E402
 
 
 def _env():
@@ -210,7 +215,7 @@ def bench_lmhead(m, n, k, reps=20):
 
 def bench_gpt2(reps=20):
     import torch
-    from .gpt2 import GPT2Config, GPT2Session, GPT2Weights
+    from tokenvector.inference_b200.gpt2 import GPT2Config, GPT2Session, GPT2Weights
     cfg = GPT2Config.gpt2_124m()
     w = GPT2Weights.random(cfg, seed=0)
     s = GPT2Session(w, max_tokens=1024)

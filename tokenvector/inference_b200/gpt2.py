@@ -134,7 +134,10 @@ def _f32(a):
 class _Session:
     """One tvq session: the blocks' weights, batch layout and scales."""
 
-    def __init__(self, cfg: GPT2Config, layers: list, vocab: int, device: int, max_tokens: int):
+    # names of the four linears of a block in PTQ artefacts (HF GPT-2 naming)
+    LINEAR_NAMES = ("attn.c_attn", "attn.c_proj", "mlp.c_fc", "mlp.c_proj")
+
+    def __init__(self, cfg: GPT2Config, layers: list, vocab: int, device: int, max_tokens: int, ptq_path=None):
         self.cfg = cfg
         self.device = device
         h = C.c_int64()
@@ -142,13 +145,60 @@ class _Session:
                cfg.max_pos, float(cfg.eps), max_tokens, C.byref(h))
         self.handle = h.value
         self.max_tokens = max_tokens
+        self._bias = []
         for li, L in enumerate(layers):
             N.call("tvq_session_set_layernorm", self.handle, li, 0, _p(_f32(L["ln1_g"])), _p(_f32(L["ln1_b"])))
             N.call("tvq_session_set_layernorm", self.handle, li, 1, _p(_f32(L["ln2_g"])), _p(_f32(L["ln2_b"])))
-            for which, (wk, bk) in enumerate(LINEARS):
-                N.call("tvq_session_set_linear_f32", self.handle, li, which, _p(_f32(L[wk])), _p(_f32(L[bk])), 0)
+            self._bias.append([_f32(L[bk]) for _, bk in LINEARS])
+            if ptq_path is None:
+                for which, (wk, bk) in enumerate(LINEARS):
+                    N.call("tvq_session_set_linear_f32", self.handle, li, which, _p(_f32(L[wk])), _p(_f32(L[bk])), 0)
         self.seg = None
         self.logits_mode = 0
+        if ptq_path is not None:
+            self.load_ptq(ptq_path)
+
+    # ---- PTQ artefacts (ptq.py): the calibrated INT8 linears, reloaded bit-exact
+    def export_ptq(self, path: str, meta: dict | None = None) -> None:
+        """Write every block's INT8 linears (weights [n, k], per-channel
+        scales, bias) with their calibrated activation scales."""
+        from . import ptq
+        sc = self.act_scales()
+        lins = []
+        for li in range(self.cfg.n_layers):
+            for which, nm in enumerate(self.LINEAR_NAMES):
+                w, sw = self.linear_i8(li, which)
+                lins.append(ptq.QuantLinear("h.%d.%s" % (li, nm), w, scales_w=sw, bias=self._bias[li][which],
+                                            scale_a=float(sc[li, which]), act=N.ACT_GELU_ERF if which == 2 else 0))
+        c = self.cfg
+        m = {"model": "gpt2-blocks", "d_model": c.d_model, "n_heads": c.n_heads, "n_layers": c.n_layers,
+             "d_ffn": c.d_ffn}
+        m.update(meta or {})
+        ptq.save(path, lins, m)
+
+    def load_ptq(self, path: str) -> None:
+        """Upload the INT8 linears and activation scales of a PTQ artefact
+        (no recalibration); the artefact must match this session's shape."""
+        from . import ptq
+        lins, meta = ptq.load(path)
+        by_name = {L.name: L for L in lins}
+        c = self.cfg
+        if meta.get("n_layers") != c.n_layers or meta.get("d_model") != c.d_model or meta.get("d_ffn") != c.d_ffn:
+            raise ValueError("PTQ artefact shape does not match the session")
+        scales = np.empty((c.n_layers, 4), np.float32)
+        self._bias = []
+        for li in range(c.n_layers):
+            row = []
+            for which, nm in enumerate(self.LINEAR_NAMES):
+                L = by_name.get("h.%d.%s" % (li, nm))
+                if L is None or L.scales_w is None:
+                    raise ValueError("PTQ artefact lacks per-channel linear h.%d.%s" % (li, nm))
+                bias = L.bias if L.bias is not None else np.zeros(L.n, np.float32)
+                N.call("tvq_session_set_linear_i8", self.handle, li, which, _p(L.w), _p(L.scales_w), _p(bias))
+                scales[li, which] = L.scale_a
+                row.append(bias)
+            self._bias.append(row)
+        self.set_act_scales(scales)
 
     def close(self):
         if getattr(self, "handle", None):
@@ -225,8 +275,10 @@ class _Session:
 class GPT2Session(_Session):
     """Device-resident INT8 GPT-2 forward on one GPU (one tvq session)."""
 
-    def __init__(self, weights: GPT2Weights, device: int = 0, max_tokens: int = 1024):
-        super().__init__(weights.cfg, weights.layers, weights.cfg.vocab, device, max_tokens)
+    def __init__(self, weights: GPT2Weights, device: int = 0, max_tokens: int = 1024, ptq_path=None):
+        """ptq_path: take the blocks' INT8 linears and activation scales from a
+        PTQ artefact (export_ptq) instead of quantizing weights' f32 linears."""
+        super().__init__(weights.cfg, weights.layers, weights.cfg.vocab, device, max_tokens, ptq_path)
         N.call("tvq_session_set_embeddings", self.handle, _p(_f32(weights.wte)), _p(_f32(weights.wpe)))
         N.call("tvq_session_set_layernorm", self.handle, -1, 0, _p(_f32(weights.lnf_g)), _p(_f32(weights.lnf_b)))
 
@@ -270,8 +322,8 @@ class LayerStack(_Session):
     point on its own activations on the GPU (calibrate_minmax +
     quantize_int8_symmetric per layer, engine.tkv:13-36, 216-226)."""
 
-    def __init__(self, cfg: GPT2Config, layers: list, device: int = 0, max_tokens: int = 8192):
-        super().__init__(cfg, layers, 0, device, max_tokens)
+    def __init__(self, cfg: GPT2Config, layers: list, device: int = 0, max_tokens: int = 8192, ptq_path=None):
+        super().__init__(cfg, layers, 0, device, max_tokens, ptq_path)
 
     def run(self, x, dynamic: bool = True) -> np.ndarray:
         """Host hidden states in, host hidden states out (synchronous)."""
