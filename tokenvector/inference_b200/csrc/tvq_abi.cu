@@ -97,6 +97,10 @@ int check_device_error(cudaStream_t st) {
     TVQ_CUDA(cudaMemcpy(&h, d->d_error, sizeof(int), cudaMemcpyDeviceToHost));
     if (h != 0) {
         TVQ_CUDA(cudaMemset(d->d_error, 0, sizeof(int)));
+        if (h == DEVERR_FIX_FULL) {
+            set_error(TVQ_ERR_SIZE, "more undecided int8 attention rows than the exact fix-up lists hold");
+            return TVQ_ERR_SIZE;
+        }
         if (h == DEVERR_BAD_INDEX) {
             set_error(TVQ_ERR_INVALID, "index out of range (a permutation entry outside [0, cols))");
             return TVQ_ERR_INVALID;

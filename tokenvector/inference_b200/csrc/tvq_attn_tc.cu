@@ -82,7 +82,9 @@ constexpr uint32_t OFF_K = 2 * QPART;                // + s * KSTAGE
 constexpr uint32_t OFF_V = OFF_K + 2 * KSTAGE;       // + s * KSTAGE
 constexpr uint32_t OFF_RED = OFF_V + 2 * KSTAGE;     // float [2][2][128] row maxima
 constexpr uint32_t OFF_LSUM = OFF_RED + 2 * 2 * TQ * 4;  // float [2][128] row sums
-constexpr uint32_t OFF_BAR = OFF_LSUM + 2 * TQ * 4;
+// exact-int8 collection: int flag[128], int2 row[128], 4 ints, float row max[128]
+constexpr uint32_t OFF_FIX = OFF_LSUM + 2 * TQ * 4;
+constexpr uint32_t OFF_BAR = OFF_FIX + TQ * 4 + TQ * 8 + 16 + TQ * 4;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 512 + 1024;
 
 // tensor memory columns: S[2], O[2] (64 f32 each), P[2] (hi 32 + lo 32
@@ -259,13 +261,15 @@ struct AttnParams {
     int* err;
     int nunits;        // work units: (item, head) = (u / nheads, u % nheads), items longest first
     // exact int8 output: rows whose int8 context the kernel's error bound
-    // (2^-19 max |V| of the head) could round differently from the
-    // reference's f64 context go to fix[] ({q, sequence start, head, 0},
-    // *fix_n of them), recomputed by attention_fix_kernel
+    // (2^-20 max |V| of the head) could round differently from the
+    // reference's f64 context are recomputed by attention_fix_kernel, grouped
+    // by work unit (one head, one sequence)
     const uint32_t* vmax;  // [nheads] max |V| per head (float bits) or null
-    int4* fix;
-    int* fix_n;
+    int4* fix;             // rows {q, row max (float bits), head, 0}
+    int* fix_n;            // [0] rows, [1] units, [2] finished fix-up CTAs
     int fix_cap;
+    int4* fix_units;       // {first row, rows | head << 8, sequence start, largest q}
+    int fix_ucap;
 };
 
 // Unit k of this CTA: rounds of gridDim.x units in snake order (CTA c takes
@@ -317,6 +321,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* red = reinterpret_cast<float*>(sm + OFF_RED);    // [parity][half][row]
     float* lsum = reinterpret_cast<float*>(sm + OFF_LSUM);  // [half][row]
+    int* fx_flag = reinterpret_cast<int*>(sm + OFF_FIX);      // [row] undecided
+    int2* fx_row = reinterpret_cast<int2*>(sm + OFF_FIX + TQ * 4);  // collected {q, row max}
+    int* fx_ctl = reinterpret_cast<int*>(sm + OFF_FIX + TQ * 12);  // count, first row, largest q, rows
+    float* fx_m = reinterpret_cast<float*>(sm + OFF_FIX + TQ * 12 + 16);  // [row] row max of a flagged row
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
     uint64_t* k_full = bars;           // [2]
     uint64_t* k_empty = bars + 2;      // [2]
@@ -357,6 +365,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int i = 0; i < 4; i++) mbar_init(&lxch[i], 2);
         fence_barrier_init();
     }
+    if (threadIdx.x >= 128 && threadIdx.x < 128 + TQ) fx_flag[threadIdx.x - 128] = 0;
+    if (threadIdx.x < 4) fx_ctl[threadIdx.x] = 0;
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmQh);
         tma_prefetch_desc(&tmQl);
@@ -691,6 +701,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             if (write_out && alive) {
                 float am = 0.0f;
+                float mfin = m;  // the row's max of the base-2 scores (after the merge: over all parts)
                 if (merged) {
                     // m = max m_c, l = sum l_c 2^(m_c - m), O = sum O_c 2^(m_c - m) / l, in slot order
                     const int4 ce = p.comb[w.entry];  // {q0, seq end, first slot, count}
@@ -702,6 +713,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                              : p.part_ml[(static_cast<int64_t>(slot_k) * p.nheads + head) * TQ + r].x;
                         mm = fmaxf(mm, mk);
                     }
+                    mfin = mm;
                     float lt = 0.0f, acc[32];
 #pragma unroll
                     for (int c = 0; c < 32; c++) acc[c] = 0.0f;
@@ -756,10 +768,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                 if (bad & (1u << c)) v.b[c] = quant_exact(o[c], qs);
                         }
                         if (p.fix) {
-                            // |o - reference| <= 2^-19 max|V| (measured: <= 2^-20.9 max|V|
-                            // on B200): a row with a value that close to an int8 rounding
+                            // |o - reference| <= 2^-20 max|V| (measured on B200: at most
+                            // 2^-20.9 of the column's running max |V|, which the head's max
+                            // bounds): a row with a value that close to an int8 rounding
                             // boundary is recomputed exactly by attention_fix_kernel
-                            const float mrg = fmaf(__uint_as_float(__ldg(p.vmax + head)), qs.hi * 1.9073486328125e-06f,
+                            const float mrg = fmaf(__uint_as_float(__ldg(p.vmax + head)), qs.hi * 9.5367431640625e-07f,
                                                    1.52587890625e-05f);
                             bool near = false;
 #pragma unroll
@@ -768,9 +781,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                 const float rr = __fsub_rn(__fadd_rn(t, 12582912.0f), 12582912.0f);
                                 near |= fabsf(fabsf(__fsub_rn(t, rr)) - 0.5f) < mrg;
                             }
-                            if (near) {
-                                const int idx = atomicAdd(p.fix_n, 1);
-                                if (idx < p.fix_cap) p.fix[idx] = make_int4(q, w.s0, head, 0);
+                            if (near) {  // either half (both hold the same row max)
+                                fx_flag[r] = 1;
+                                fx_m[r] = mfin;
                             }
                         }
                         if ((reinterpret_cast<uintptr_t>(p.outq + base) & 15) == 0) {
@@ -791,6 +804,43 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
                     if (lane == 0) atomicMax(p.amax, __float_as_uint(am));
                 }
+            }
+            if (p.fix && p.outq && write_out) {  // write_out is uniform over the 256 softmax threads; alive may not be
+                // the unit's undecided rows, once each, as one group: a unit
+                // entry and its rows (all of one head and one sequence)
+                named_bar_sync(3, 256);  // every flag is set
+                if (h == 0 && fx_flag[r]) {
+                    const int slot = atomicAdd(&fx_ctl[0], 1);
+                    fx_row[slot] = make_int2(q, __float_as_int(fx_m[r]));
+                    atomicMax(&fx_ctl[2], q);
+                    fx_flag[r] = 0;
+                }
+                named_bar_sync(3, 256);
+                if (threadIdx.x == 128) {
+                    const int cnt = fx_ctl[0];
+                    int b = -1;
+                    if (cnt > 0) {
+                        b = atomicAdd(p.fix_n, cnt);
+                        const int ui = atomicAdd(p.fix_n + 1, 1);
+                        if (b + cnt <= p.fix_cap && ui < p.fix_ucap) {
+                            p.fix_units[ui] = make_int4(b, cnt | (head << 8), w.s0, fx_ctl[2]);
+                        } else {
+                            // lists full: record it; a reserved unit slot gets an
+                            // empty entry (no rows, no keys) so the fix-up skips it
+                            record_error(p.err, DEVERR_FIX_FULL);
+                            if (ui < p.fix_ucap) p.fix_units[ui] = make_int4(0, head << 8, w.s0, w.s0 - 1);
+                            b = -1;
+                        }
+                    }
+                    fx_ctl[1] = b;
+                    fx_ctl[3] = cnt;
+                    fx_ctl[0] = 0;
+                    fx_ctl[2] = 0;
+                }
+                named_bar_sync(3, 256);
+                const int cnt = fx_ctl[3], b = fx_ctl[1];
+                const int i = threadIdx.x - 128;
+                if (b >= 0 && i < cnt) p.fix[b + i] = make_int4(fx_row[i].x, fx_row[i].y, head, 0);
             }
             // the eight softmax warps leave the unit loop together (each unit
             // then runs the same named barriers in every warp)
@@ -814,97 +864,185 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 // Rows of the context whose int8 value the tensor-core kernel could not
 // decide (AttnParams::fix), recomputed as the reference computes them
 // (gpt2_ref.tkv:360-395, the oracle's tvo_attention_causal): scores q.k /
-// sqrt(hd) in binary64, softmax with exp in binary64, the P V sum in binary64
-// and one rounding to binary32, then the exact int8 quantize.  The sums run in
-// another order than the reference's sequential loops; that moves the binary64
-// result by about 1e-16 of its size, which changes its binary32 rounding with a
-// probability of about 2^-28 per value.  One CTA per entry (256 threads: keys
-// spread over the threads for the scores, 64 output columns x 4 key groups
-// for P V), keys in chunks of FIX_KEYS with an online (rescaled) softmax.  The
-// last CTA to finish resets the list for the next launch.
-constexpr int FIX_KEYS = 1024;
-__global__ void __launch_bounds__(256) attention_fix_kernel(const float* __restrict__ qkv, const int4* __restrict__ fix,
-                                                            int* fix_n, int* fix_done, int cap, int d, int nheads,
-                                                            float* __restrict__ out, int8_t* __restrict__ outq,
-                                                            const float* __restrict__ qscale) {
+// sqrt(hd) in binary64, softmax weights with exp in binary64, the P V sum in
+// binary64 and one rounding to binary32, then the exact int8 quantize.
+//
+// The weights are exp(s_u - c) with c the tensor-core kernel's row max (base-2
+// units, times ln 2) instead of the exact max: the context sum(e_u v_u) /
+// sum(e_u) does not depend on c, so the keys split into independent 64-key
+// chunks whose partial sums are added (binary64 reductions) into the row's
+// accumulator; attention_fix_finish_kernel then finishes every row.
+// The sums run in another order than the reference's sequential loops; that
+// moves the binary64 result by about 1e-16 of its size, which changes its
+// binary32 rounding with a probability of about 2^-28 per value.
+//
+// Work item i = (unit entry i / max_chunks, chunk i % max_chunks): the chunk's
+// K and V rows are converted to binary64 in shared memory once (the f32 -> f64
+// conversions bound a row-by-row recomputation), and every undecided row of
+// the unit (one head, one sequence) whose causal range reaches the chunk takes
+// it: a warp task per (row, 32-key half of the chunk), a key per lane for the
+// scores, lane = output column (two of them) for P V.
+constexpr int FIX_THREADS = 256;
+constexpr int FIX_KEYS = 64;
+constexpr uint32_t FIX_SMEM = (FIX_KEYS * (HD + 1) + FIX_KEYS * HD + (FIX_THREADS / 32) * HD) * 8;
+__global__ void __launch_bounds__(FIX_THREADS) attention_fix_kernel(
+    const float* __restrict__ qkv, const int4* __restrict__ rows, const int4* __restrict__ units, const int* fix_n,
+    int ucap, double* __restrict__ facc, int max_chunks, int d) {
     griddep_wait();
-    __shared__ double sc[FIX_KEYS];
-    __shared__ double qd[HD];
-    __shared__ double red[8];
-    __shared__ double accs[4][HD];
+    extern __shared__ double fsm[];
+    double* ks = fsm;                        // [FIX_KEYS][HD + 1]
+    double* vs = ks + FIX_KEYS * (HD + 1);   // [FIX_KEYS][HD]
+    double* qsh = vs + FIX_KEYS * HD;        // [warp][HD]
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int hd = d / nheads;
     const int64_t rs = 3LL * d;
+    const int nunits = min(*reinterpret_cast<const volatile int*>(fix_n + 1), ucap);
+    const int64_t nitems = static_cast<int64_t>(nunits) * max_chunks;
+    constexpr int LPT = FIX_KEYS * (HD / 4) / FIX_THREADS;  // 16-byte K (and V) loads per thread and item
+    // the K / V loads of an item, issued together (and for the next item while
+    // this one's tasks run); keys past the item's last needed one read as 0
+    auto load_item = [&](int64_t item, float4 (&kr)[LPT], float4 (&vr)[LPT]) {
+        const int4 un = units[item / max_chunks];
+        const int k0 = un.z + static_cast<int>(item % max_chunks) * FIX_KEYS;
+        const int kn = min(FIX_KEYS, un.w + 1 - k0);
+        const float* base = qkv + (un.y >> 8) * HD;
+#pragma unroll
+        for (int t = 0; t < LPT; t++) {
+            const int idx = tid + t * FIX_THREADS, kk = idx / (HD / 4), c4 = idx % (HD / 4);
+            kr[t] = vr[t] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (kk < kn) {
+                const float* rowp = base + static_cast<int64_t>(k0 + kk) * rs + 4 * c4;
+                kr[t] = __ldg(reinterpret_cast<const float4*>(rowp + d));
+                vr[t] = __ldg(reinterpret_cast<const float4*>(rowp + 2 * d));
+            }
+        }
+    };
+    // next item of this CTA that has keys to do
+    auto next_item = [&](int64_t from) -> int64_t {
+        for (int64_t x = from; x < nitems; x += gridDim.x) {
+            const int4 un = units[x / max_chunks];
+            if (un.z + static_cast<int>(x % max_chunks) * FIX_KEYS <= un.w) return x;
+        }
+        return nitems;
+    };
+    float4 kreg[LPT], vreg[LPT];
+    int64_t it = next_item(blockIdx.x);
+    if (it < nitems) load_item(it, kreg, vreg);
+    while (it < nitems) {
+        const int4 un = units[it / max_chunks];
+        const int c = static_cast<int>(it % max_chunks);
+        const int rb = un.x, rn = un.y & 0xFF, head = un.y >> 8, s0 = un.z, qmax = un.w;
+        const int k0 = s0 + c * FIX_KEYS;
+        const int kn = min(FIX_KEYS, qmax + 1 - k0);
+        const float* base = qkv + head * HD;
+        // the chunk's K and V rows as binary64
+#pragma unroll
+        for (int t = 0; t < LPT; t++) {
+            const int idx = tid + t * FIX_THREADS, kk = idx / (HD / 4), c4 = idx % (HD / 4);
+            double* kd = ks + kk * (HD + 1) + 4 * c4;
+            kd[0] = kreg[t].x;
+            kd[1] = kreg[t].y;
+            kd[2] = kreg[t].z;
+            kd[3] = kreg[t].w;
+            double* vd = vs + kk * HD + 4 * c4;
+            vd[0] = vreg[t].x;
+            vd[1] = vreg[t].y;
+            vd[2] = vreg[t].z;
+            vd[3] = vreg[t].w;
+        }
+        const int64_t nx = next_item(it + gridDim.x);
+        if (nx < nitems) load_item(nx, kreg, vreg);  // in flight during this item's tasks
+        __syncthreads();
+        double* qw = qsh + wid * HD;
+        int qrow = -1;  // the row whose q this warp holds in qw
+        // tasks: (row, 32-key half of the chunk), warps round robin
+        for (int tk = wid; tk < 2 * rn; tk += FIX_THREADS / 32) {  // warp-uniform
+            const int ri = tk >> 1, hlf = tk & 1;
+            const int4 rw = rows[rb + ri];
+            const int q = rw.x;
+            if (q < k0) continue;  // this row's causal range ends before the chunk
+            const double off = static_cast<double>(__int_as_float(rw.y)) * 0.69314718055994531;  // base 2 -> natural
+            if (qrow != q) {
+                const float* qr = base + static_cast<int64_t>(q) * rs;
+                __syncwarp();
+                qw[lane] = qr[lane];
+                qw[lane + 32] = qr[lane + 32];
+                __syncwarp();
+                qrow = q;
+            }
+            const int kk = lane + 32 * hlf;
+            const double* kd = ks + kk * (HD + 1);
+            double p0 = 0.0, p1 = 0.0, p2 = 0.0, p3 = 0.0;
+#pragma unroll
+            for (int dd = 0; dd < HD; dd += 4) {
+                p0 = fma(qw[dd], kd[dd], p0);
+                p1 = fma(qw[dd + 1], kd[dd + 1], p1);
+                p2 = fma(qw[dd + 2], kd[dd + 2], p2);
+                p3 = fma(qw[dd + 3], kd[dd + 3], p3);
+            }
+            const double e = (kk < kn && k0 + kk <= q) ? exp(((p0 + p1) + (p2 + p3)) * 0.125 - off) : 0.0;  // 1/sqrt(64)
+            double l = e;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+            double a0 = 0.0, a1 = 0.0, b0 = 0.0, b1 = 0.0;
+            const double* vh = vs + 32 * hlf * HD;
+#pragma unroll
+            for (int t = 0; t < 32; t += 2) {
+                const double pw = __shfl_sync(0xffffffffu, e, t);
+                const double pv = __shfl_sync(0xffffffffu, e, t + 1);
+                a0 = fma(pw, vh[t * HD + lane], a0);
+                a1 = fma(pw, vh[t * HD + lane + 32], a1);
+                b0 = fma(pv, vh[(t + 1) * HD + lane], b0);
+                b1 = fma(pv, vh[(t + 1) * HD + lane + 32], b1);
+            }
+            a0 += b0;
+            a1 += b1;
+            double* ea = facc + static_cast<int64_t>(rb + ri) * kAttnFixAccWords;  // [0, 64) sums, 64 weights
+            atomicAdd(ea + lane, a0);  // no result used: reductions, ordered by the kernel's end
+            atomicAdd(ea + lane + 32, a1);
+            if (lane == 0) atomicAdd(ea + HD, l);
+        }
+        __syncthreads();  // ks / vs are rewritten by the next item
+        it = nx;
+    }
+}
+
+// The undecided rows' contexts from their accumulators (every chunk added by
+// attention_fix_kernel, which ended before this kernel starts): one warp per
+// row, two columns per lane, then the exact int8 quantize; the accumulators
+// go back to zero, and the last CTA resets the lists for the next launch.
+__global__ void __launch_bounds__(256) attention_fix_finish_kernel(const int4* __restrict__ rows, int* fix_n, int cap,
+                                                                   double* __restrict__ facc, int d,
+                                                                   float* __restrict__ out, int8_t* __restrict__ outq,
+                                                                   const float* __restrict__ qscale) {
+    griddep_wait();
+    const int lane = threadIdx.x & 31;
     const int n = min(*reinterpret_cast<volatile int*>(fix_n), cap);
     const InvScale qs = make_inv_scale(static_cast<double>(__ldg(qscale)));
-    const double inv_sqrt = 1.0 / sqrt(static_cast<double>(hd));
-    const int dd = tid & (HD - 1), g = tid / HD;
-    for (int e = blockIdx.x; e < n; e += gridDim.x) {
-        const int4 f = fix[e];
-        const int q = f.x, s0 = f.y, head = f.z;
-        if (tid < hd) qd[tid] = static_cast<double>(qkv[static_cast<int64_t>(q) * rs + head * hd + tid]);
-        __syncthreads();
-        double m = -INFINITY, tot = 0.0, acc = 0.0;
-        for (int u0 = s0; u0 <= q; u0 += FIX_KEYS) {
-            const int u1 = min(q + 1, u0 + FIX_KEYS);
-            double lm = -INFINITY;
-            for (int u = u0 + tid; u < u1; u += 256) {
-                const float* kr = qkv + static_cast<int64_t>(u) * rs + d + head * hd;
-                double sdot = 0.0;
-                for (int i = 0; i < hd; i++) sdot = fma(qd[i], static_cast<double>(__ldg(kr + i)), sdot);
-                sdot *= inv_sqrt;
-                sc[u - u0] = sdot;
-                lm = fmax(lm, sdot);
-            }
+    const int warps = static_cast<int>(gridDim.x) * (blockDim.x >> 5);
+    for (int ri = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); ri < n; ri += warps) {
+        const int4 rw = rows[ri];
+        double* ea = facc + static_cast<int64_t>(ri) * kAttnFixAccWords;
+        const double inv = 1.0 / ea[HD];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) lm = fmax(lm, __shfl_xor_sync(0xffffffffu, lm, o));
-            if (lane == 0) red[wid] = lm;
-            __syncthreads();
-            lm = red[0];
-#pragma unroll
-            for (int w = 1; w < 8; w++) lm = fmax(lm, red[w]);
-            __syncthreads();
-            const double mn = fmax(m, lm);
-            const double alpha = (m == -INFINITY) ? 0.0 : exp(m - mn);
-            tot *= alpha;
-            acc *= alpha;
-            m = mn;
-            double lt = 0.0;
-            for (int u = u0 + tid; u < u1; u += 256) {
-                const double ex = exp(sc[u - u0] - m);
-                sc[u - u0] = ex;
-                lt += ex;
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o);
-            if (lane == 0) red[wid] = lt;
-            __syncthreads();  // sc holds the weights, red the partial sums
-            lt = 0.0;
-#pragma unroll
-            for (int w = 0; w < 8; w++) lt += red[w];
-            tot += lt;
-            if (dd < hd)
-                for (int u = u0 + g; u < u1; u += 4)
-                    acc = fma(sc[u - u0], static_cast<double>(__ldg(qkv + static_cast<int64_t>(u) * rs + 2 * d + head * hd + dd)),
-                              acc);
-            __syncthreads();  // sc and red are rewritten by the next chunk
+        for (int h2 = 0; h2 < 2; h2++) {
+            const int col = lane + 32 * h2;
+            const float cx = __double2float_rn(ea[col] * inv);
+            const int64_t o = static_cast<int64_t>(rw.x) * d + rw.z * HD + col;
+            if (out) out[o] = cx;
+            if (outq) outq[o] = quant_exact(cx, qs);
         }
-        accs[g][dd] = acc;
-        __syncthreads();
-        if (tid < hd) {
-            const double a = (accs[0][tid] + accs[1][tid]) + (accs[2][tid] + accs[3][tid]);
-            const float c = __double2float_rn(a * (1.0 / tot));
-            const int64_t o = static_cast<int64_t>(q) * d + head * hd + tid;
-            if (out) out[o] = c;
-            if (outq) outq[o] = quant_exact(c, qs);
-        }
-        __syncthreads();
+        __syncwarp();
+        ea[lane] = 0.0;
+        ea[lane + 32] = 0.0;
+        if (lane == 0) ea[HD] = 0.0;
     }
-    if (tid == 0) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
         __threadfence();
-        if (atomicAdd(fix_done, 1) == static_cast<int>(gridDim.x) - 1) {
-            *fix_n = 0;
-            *fix_done = 0;
+        if (atomicAdd(fix_n + 2, 1) == static_cast<int>(gridDim.x) - 1) {
+            fix_n[0] = 0;
+            fix_n[1] = 0;
+            fix_n[2] = 0;
         }
     }
 }
@@ -1029,19 +1167,33 @@ int launch_attention_tc(const float* qkv, const void* qh, const void* ql, const 
     p.kv_exp = kv_exp;
     p.nunits = nitems * nheads;
     const bool fixing = fix && outq;
-    TVQ_CHECK(!fixing || (fix->vmax && fix->list && fix->n && fix->done && fix->cap > 0), TVQ_ERR_INVALID,
-              "the exact int8 context needs the head maxima and a fix-up list");
+    TVQ_CHECK(!fixing || (fix->vmax && fix->list && fix->units && fix->n && fix->cap > 0 && fix->ucap > 0 &&
+                          fix->acc && fix->max_keys > 0),
+              TVQ_ERR_INVALID, "the exact int8 context needs the head maxima, the fix-up lists and accumulators");
     p.vmax = fixing ? fix->vmax : nullptr;
     p.fix = fixing ? fix->list : nullptr;
     p.fix_n = fixing ? fix->n : nullptr;
     p.fix_cap = fixing ? fix->cap : 0;
+    p.fix_units = fixing ? fix->units : nullptr;
+    p.fix_ucap = fixing ? fix->ucap : 0;
     // persistent: one CTA per SM (all of TMEM) working through the units;
     // key-chunk partials are merged inside the kernel by the last CTA of each set
     const int grid = std::min(p.nunits, ds->sm_count);
     rc = launch_pdl(attention_tc_kernel, dim3(grid), dim3(NTHREADS), SMEM_BYTES, st, mqh, mql, mkh, mkl, mvh, mvl, p);
     if (rc || !fixing) return rc;
-    return launch_pdl(attention_fix_kernel, dim3(2 * ds->sm_count), dim3(256), 0, st, qkv,
-                      static_cast<const int4*>(fix->list), fix->n, fix->done, fix->cap, d, nheads, out, outq, qscale);
+    static bool fattr[64] = {false};
+    if (dev < 64 && !fattr[dev]) {
+        TVQ_CUDA(cudaFuncSetAttribute(attention_fix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(FIX_SMEM)));
+        fattr[dev] = true;
+    }
+    const int max_chunks = (fix->max_keys + FIX_KEYS - 1) / FIX_KEYS;
+    rc = launch_pdl(attention_fix_kernel, dim3(3 * ds->sm_count), dim3(FIX_THREADS), FIX_SMEM, st, qkv,
+                    static_cast<const int4*>(fix->list), static_cast<const int4*>(fix->units),
+                    static_cast<const int*>(fix->n), fix->ucap, fix->acc, max_chunks, d);
+    if (rc) return rc;
+    return launch_pdl(attention_fix_finish_kernel, dim3(2 * ds->sm_count), dim3(256), 0, st,
+                      static_cast<const int4*>(fix->list), fix->n, fix->cap, fix->acc, d, out, outq, qscale);
 }
 
 }  // namespace tvq

@@ -52,6 +52,7 @@ enum : int {
     DEVERR_TIMEOUT_DRAIN = 4,
     DEVERR_TIMEOUT_TEST = 9,
     DEVERR_BAD_INDEX = 60,  // an index operand out of range (not a timeout)
+    DEVERR_FIX_FULL = 61,   // more undecided int8 attention rows than the fix-up lists hold
 };
 
 // ---------------------------------------------------------------- device side

@@ -44,16 +44,25 @@ int launch_split_kv(const float* qkv, int T, int d, void* qh, void* ql, void* kh
 int launch_kv_head_bound(const int8_t* W, const float* sw, const float* bias, int k, int kvd, float* out,
                          cudaStream_t st);
 // Exact int8 context (optional, with outq): vmax [nheads] = max |V| per head
-// (float bits), list [cap] of rows to recompute, n / done: two device ints,
-// zero before the first launch (the fix-up kernel leaves them zero).  The
-// fix-up reads the f32 qkv, so qkv must hold the values when it is given.
+// (float bits); list [cap] rows to recompute (one per undecided row), units
+// [ucap] one per attention unit with such rows; n: three device ints (rows,
+// units, finished fix-up CTAs); acc [cap][kAttnFixAccWords] binary64 row
+// accumulators (context sums, weight sum, a count); n and acc zero before the
+// first launch (the fix-up kernel leaves them zero); max_keys = the longest
+// sequence.  The fix-up reads the f32 qkv, so qkv must hold the values.  A
+// launch with more undecided rows than cap records a device error.
 struct AttnFix {
     const uint32_t* vmax = nullptr;
     int4* list = nullptr;
+    int4* units = nullptr;
     int* n = nullptr;
-    int* done = nullptr;
+    double* acc = nullptr;
     int cap = 0;
+    int ucap = 0;
+    int max_keys = 0;
 };
+// binary64 words per accumulator row of AttnFix::acc
+constexpr int kAttnFixAccWords = 66;
 int launch_attention_tc(const float* qkv, const void* qh, const void* ql, const void* kh, const void* kl,
                         const void* vth, const void* vtl, const int* kv_exp, int T, const int4* tiles,
                         const int4* split, int nitems, const int4* comb, int ncomb, int d, int nheads, float* out,
