@@ -164,6 +164,28 @@ TVQ_API int tvq_dequantize_fp8_e4m3(const uint8_t* src, int64_t n, float* dst, i
 TVQ_API int tvq_matmul_fp8_e4m3(const uint8_t* A, const uint8_t* W, const float* bias, int64_t n_bias, float* Y,
                         int64_t m, int64_t n, int64_t k, float scale_a, const float* scales_w, int act);
 
+/* matmul_int8_asymmetric, matmul.tkv:31-44: acc = sum_k (a - zp_a)(w - zp_w)
+ * exact, y = fl32(fl64(acc * fl64(scale_a*scale_w)) + bias[n]).  On the
+ * tensor cores: the int32 dot product, then in the epilogue acc = dot -
+ * zp_w sum_k a - zp_a sum_k w + k zp_a zp_w in binary64 (every term an exact
+ * integer).  |zp_a|, |zp_w| <= 2^17 (TVQ_ERR_UNSUPPORTED beyond). */
+TVQ_API int tvq_matmul_int8_asymmetric(const int8_t* A, const int8_t* W, const float* bias, int64_t n_bias, float* Y,
+                               int64_t m, int64_t n, int64_t k, float scale_a, int64_t zp_a, float scale_w,
+                               int64_t zp_w);
+
+/* matmul_fp16, matmul.tkv:79-96: A [m,k] and W [n,k] fp16 bit patterns,
+ * y = fl32(sum_k a w + bias[n]).  kind::f16 tensor cores with fp32
+ * accumulation, partial sums of 192 k promoted to registers: within
+ * (k/16 + 2) 2^-23 sum_k |a w| of the reference's binary64 sum.  An fp16 NaN
+ * operand stays NaN here; the reference's decoder reads it as +-Inf
+ * (f32_bits_to_f64 maps exponent 255 to 2^129). */
+TVQ_API int tvq_matmul_fp16(const uint16_t* A, const uint16_t* W, const float* bias, int64_t n_bias, float* Y,
+                    int64_t m, int64_t n, int64_t k);
+/* quantize_fp16, matmul.tkv:106-114: the reference's encoder
+ * (native_f16_encode, types.tkv:95-127; its departures from IEEE rounding
+ * are kept: see tvq_f16.h) of n floats, dst_len >= n. */
+TVQ_API int tvq_quantize_fp16(const float* src, int64_t n, uint16_t* dst, int64_t dst_len);
+
 /* ---- list[i32] compatibility forms: the reference stores int8 values in
  * list[i32] (engine.tkv:216, session.tkv:158-170) and FP8 bytes as
  * byte - 128 (matmul.tkv:65, :76).  These convert at the boundary. */
@@ -174,6 +196,15 @@ TVQ_API int tvq_matmul_int8_per_channel_i32(const int32_t* A, const int32_t* W, 
 TVQ_API int tvq_quantize_fp8_e4m3_i32(const float* src, int64_t n, int32_t* dst, int64_t dst_len);
 TVQ_API int tvq_matmul_fp8_e4m3_i32(const int32_t* A, const int32_t* W, const float* bias, int64_t n_bias, float* Y,
                             int64_t m, int64_t n, int64_t k);
+TVQ_API int tvq_matmul_int8_asymmetric_i32(const int32_t* A, const int32_t* W, const float* bias, int64_t n_bias,
+                                   float* Y, int64_t m, int64_t n, int64_t k, float scale_a, int64_t zp_a,
+                                   float scale_w, int64_t zp_w);
+/* FP16 as the reference stores it: two list entries per element, low byte
+ * first (A [2 m k], W [2 n k]; each entry & 255, matmul.tkv:84-87) */
+TVQ_API int tvq_matmul_fp16_i32(const int32_t* A, const int32_t* W, const float* bias, int64_t n_bias, float* Y,
+                        int64_t m, int64_t n, int64_t k);
+/* dst [2 n]: the two bytes of each fp16 as signed values (_to_sbyte, matmul.tkv:98-114) */
+TVQ_API int tvq_quantize_fp16_i32(const float* src, int64_t n, int32_t* dst, int64_t dst_len);
 
 /* ================================================================ device buffers
  * Asynchronous on `stream`.  minmax_dev is float[2] = {min, max} in an
@@ -186,6 +217,18 @@ TVQ_API int tvq_dev_minmax_finalize(const uint32_t* minmax_dev, const float* fir
                             void* stream);
 /* Per-tensor quantize with a device scale (scale_dev[0]). */
 TVQ_API int tvq_dev_quantize_int8(const float* x, int8_t* q, int64_t n, const float* scale_dev, void* stream);
+/* quantize_fp16 on device buffers (fp16 bit patterns out). */
+TVQ_API int tvq_dev_quantize_fp16(const float* x, uint16_t* q, int64_t n, void* stream);
+/* matmul_fp16 on device buffers: k a multiple of 8, A and W 16-byte aligned;
+ * bias [n] or NULL. */
+TVQ_API int tvq_dev_matmul_fp16(const uint16_t* A, const uint16_t* W, const float* bias, float* Y, int64_t m, int64_t n,
+                        int64_t k, void* stream);
+/* matmul_int8_asymmetric on device buffers: k a multiple of 16, A and W
+ * 16-byte aligned; scale_a_dev / scale_w_dev device float[1].  Allocates its
+ * (m + n)-int row-sum scratch stream-ordered (cudaMallocAsync). */
+TVQ_API int tvq_dev_matmul_int8_asymmetric(const int8_t* A, const int8_t* W, const float* bias, float* Y, int64_t m,
+                                   int64_t n, int64_t k, const float* scale_a_dev, int64_t zp_a,
+                                   const float* scale_w_dev, int64_t zp_w, void* stream);
 /* Per-channel weight calibrate + quantize, fused: scales_dev[r] and q[r,:]. */
 TVQ_API int tvq_dev_calibrate_quantize_per_channel(const float* w, int8_t* q, float* scales_dev, int64_t rows,
                                            int64_t cols, void* stream);

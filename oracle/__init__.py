@@ -70,6 +70,8 @@ def lib():
             "tvo_matmul_int8_per_channel": (i32, [P, P, P, i64, P, i64, i64, i64, f32, P, i64]),
             "tvo_matmul_int8_symmetric": (i32, [P, P, P, i64, P, i64, i64, i64, f32, f32]),
             "tvo_matmul_int8_asymmetric": (i32, [P, P, P, i64, P, i64, i64, i64, f32, i64, f32, i64]),
+            "tvo_quantize_fp16": (i32, [P, i64, P]),
+            "tvo_matmul_fp16": (i32, [P, P, P, i64, P, i64, i64, i64]),
             "tvo_quantize_fp8_e4m3": (i32, [P, i64, P]),
             "tvo_quantize_fp8_e4m3_scaled": (i32, [P, i64, i64, P, P, i32]),
             "tvo_dequantize_fp8_e4m3": (i32, [P, i64, P]),
@@ -337,6 +339,26 @@ def matmul_int8_asymmetric(A, W, bias, scale_a, zp_a, scale_w, zp_w) -> np.ndarr
     Y = np.empty((m, n), dtype=np.float32)
     lib().tvo_matmul_int8_asymmetric(_p(A), _p(W), _p(b) if b.size else None, b.size, _p(Y), m, n, k,
                                      float(scale_a), int(zp_a), float(scale_w), int(zp_w))
+    return Y
+
+
+def quantize_fp16(src) -> np.ndarray:
+    """quantize_fp16, tv/quantization/matmul.tkv:106-114 (uint16 patterns)."""
+    s = _f32(src)
+    out = np.empty(s.shape, dtype=np.uint16)
+    lib().tvo_quantize_fp16(_p(s), s.size, _p(out))
+    return out
+
+
+def matmul_fp16(A, W, bias) -> np.ndarray:
+    """matmul_fp16, tv/quantization/matmul.tkv:79-96 (uint16 fp16 operands)."""
+    A = np.ascontiguousarray(A, dtype=np.uint16)
+    W = np.ascontiguousarray(W, dtype=np.uint16)
+    m, k = A.shape
+    n = W.shape[0]
+    b = _f32(bias) if bias is not None else np.zeros(0, np.float32)
+    Y = np.empty((m, n), dtype=np.float32)
+    lib().tvo_matmul_fp16(_p(A), _p(W), _p(b) if b.size else None, b.size, _p(Y), m, n, k)
     return Y
 
 

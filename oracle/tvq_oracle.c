@@ -507,6 +507,36 @@ TVO_API int tvo_matmul_int8_asymmetric(const int8_t* A, const int8_t* W, const f
     return 0;
 }
 
+/* quantize_fp16, tv/quantization/matmul.tkv:106-114 (the fp16 pattern of
+ * each element; the reference splits it into two signed bytes) */
+TVO_API int tvo_quantize_fp16(const float* src, int64_t n, uint16_t* dst) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; i++) dst[i] = (uint16_t)tvo_f16_encode(src[i]);
+    return 0;
+}
+
+/* matmul_fp16, tv/quantization/matmul.tkv:79-96: A [m,k], W [n,k] fp16
+ * patterns decoded by FP16.to_float (native_f16_decode), acc an untyped
+ * (binary64) sum in k order, y = fl32(acc + bias). */
+TVO_API int tvo_matmul_fp16(const uint16_t* A, const uint16_t* W, const float* bias, int64_t n_bias, float* Y,
+                            int64_t m, int64_t n, int64_t k) {
+    static double tab[65536];
+    static int ready = 0;
+    if (!ready) {
+        for (int v = 0; v < 65536; v++) tab[v] = (double)tvo_f16_decode(v);
+        ready = 1;
+    }
+#pragma omp parallel for schedule(static)
+    for (int64_t mm = 0; mm < m; mm++)
+        for (int64_t nn = 0; nn < n; nn++) {
+            double acc = 0.0;
+            for (int64_t kk = 0; kk < k; kk++) acc = acc + tab[A[mm * k + kk]] * tab[W[nn * k + kk]];
+            double b = (n_bias > 0) ? (double)bias[nn] : 0.0;
+            Y[mm * n + nn] = (float)(acc + b);
+        }
+    return 0;
+}
+
 /* Decode table for E4M3 bytes through the restated decoder. */
 static void e4m3_table(double* t) {
     for (int v = 0; v < 256; v++) t[v] = (double)tvo_e4m3_decode(v);

@@ -56,6 +56,15 @@ SIGNATURES = {
     "tvq_matmul_int8_per_channel_i32": (i32, [P, P, P, i64, P, i64, i64, i64, f32, P, i64]),
     "tvq_quantize_fp8_e4m3_i32": (i32, [P, i64, P, i64]),
     "tvq_matmul_fp8_e4m3_i32": (i32, [P, P, P, i64, P, i64, i64, i64]),
+    "tvq_matmul_int8_asymmetric": (i32, [P, P, P, i64, P, i64, i64, i64, f32, i64, f32, i64]),
+    "tvq_matmul_int8_asymmetric_i32": (i32, [P, P, P, i64, P, i64, i64, i64, f32, i64, f32, i64]),
+    "tvq_matmul_fp16": (i32, [P, P, P, i64, P, i64, i64, i64]),
+    "tvq_matmul_fp16_i32": (i32, [P, P, P, i64, P, i64, i64, i64]),
+    "tvq_quantize_fp16": (i32, [P, i64, P, i64]),
+    "tvq_quantize_fp16_i32": (i32, [P, i64, P, i64]),
+    "tvq_dev_quantize_fp16": (i32, [P, P, i64, P]),
+    "tvq_dev_matmul_fp16": (i32, [P, P, P, P, i64, i64, i64, P]),
+    "tvq_dev_matmul_int8_asymmetric": (i32, [P, P, P, P, i64, i64, i64, P, i64, P, i64, P]),
     "tvq_dev_minmax_reset": (i32, [P, P]),
     "tvq_dev_minmax_accumulate": (i32, [P, i64, P, P, P]),
     "tvq_dev_minmax_finalize": (i32, [P, P, i32, P, P]),

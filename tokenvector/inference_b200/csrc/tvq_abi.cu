@@ -242,6 +242,100 @@ int host_gemm(int kind, const void* A, const void* W, size_t elem_bytes_ignored,
     return H.finish();
 }
 
+// matmul_int8_asymmetric on host buffers: the INT8 GEMM with its zero-point
+// epilogue, the row sums of A and W computed on the device first
+int host_gemm_asym(const int8_t* A, const int8_t* W, const float* bias, int64_t n_bias, float* Y, int64_t m, int64_t n,
+                   int64_t k, float scale_a, int64_t zp_a, float scale_w, int64_t zp_w) {
+    TVQ_CHECK(m >= 0 && n >= 0 && k >= 0 && n_bias >= 0, TVQ_ERR_INVALID, "negative size");
+    if (m == 0 || n == 0) return TVQ_OK;
+    TVQ_CHECK(Y && (k == 0 || (A && W)), TVQ_ERR_INVALID, "null buffer");
+    TVQ_CHECK(n_bias == 0 || n_bias >= n, TVQ_ERR_SIZE, "bias smaller than N");
+    TVQ_CHECK(n_bias == 0 || bias, TVQ_ERR_INVALID, "null bias");
+    HOST_BEGIN
+    const int64_t kp = (k + 15) / 16 * 16;
+    uint8_t* dA = dev<uint8_t>(H, 0, static_cast<size_t>(std::max<int64_t>(m * kp, 1)));
+    uint8_t* dW = dev<uint8_t>(H, 1, static_cast<size_t>(std::max<int64_t>(n * kp, 1)));
+    float* dY = dev<float>(H, 2, static_cast<size_t>(m * n));
+    float* dB = dev<float>(H, 3, static_cast<size_t>(n_bias > 0 ? n : 1));
+    float* dS = dev<float>(H, 4, 8);
+    int* dR = dev<int>(H, 5, static_cast<size_t>(m + n));
+    if (H.rc) return H.rc;
+    if (kp == k) {
+        STEP(H.h2d(dA, A, static_cast<size_t>(m * k)));
+        STEP(H.h2d(dW, W, static_cast<size_t>(n * k)));
+    } else if (k > 0) {
+        TVQ_CUDA(cudaMemsetAsync(dA, 0, static_cast<size_t>(m * kp), H.st()));
+        TVQ_CUDA(cudaMemsetAsync(dW, 0, static_cast<size_t>(n * kp), H.st()));
+        TVQ_CUDA(cudaMemcpy2DAsync(dA, kp, A, k, k, m, cudaMemcpyHostToDevice, H.st()));
+        TVQ_CUDA(cudaMemcpy2DAsync(dW, kp, W, k, k, n, cudaMemcpyHostToDevice, H.st()));
+    }
+    if (n_bias > 0) STEP(H.h2d(dB, bias, static_cast<size_t>(n) * 4));
+    const float sc[8] = {scale_a, 0.0f, 0.0f, 0.0f, scale_w, 0.0f, 0.0f, 0.0f};
+    STEP(H.h2d(dS, sc, sizeof(sc)));
+    STEP(launch_row_sums_i8(reinterpret_cast<const int8_t*>(dA), m, kp, dR, H.st()));
+    STEP(launch_row_sums_i8(reinterpret_cast<const int8_t*>(dW), n, kp, dR + m, H.st()));
+    GemmArgs g;
+    g.kind = GEMM_I8;
+    g.A = dA;
+    g.W = dW;
+    g.bias = n_bias > 0 ? dB : nullptr;
+    g.Y = dY;
+    g.m = m;
+    g.n = n;
+    g.k = kp;
+    g.scale_a = dS;
+    g.scales_w = dS + 4;
+    g.per_channel = 0;
+    g.zp_rows = dR;
+    g.zp_cols = dR + m;
+    g.zp_a = zp_a;
+    g.zp_w = zp_w;
+    g.zp_k = k;
+    STEP(launch_gemm(g, H.st()));
+    STEP(H.d2h(Y, dY, static_cast<size_t>(m * n) * 4));
+    return H.finish();
+}
+
+// matmul_fp16 on host buffers: fp16 A [m, k] and W [n, k] (bit patterns), k
+// padded with zeros to a multiple of 8 (the TMA row pitch)
+int host_gemm_f16(const uint16_t* A, const uint16_t* W, const float* bias, int64_t n_bias, float* Y, int64_t m,
+                  int64_t n, int64_t k) {
+    TVQ_CHECK(m >= 0 && n >= 0 && k >= 0 && n_bias >= 0, TVQ_ERR_INVALID, "negative size");
+    if (m == 0 || n == 0) return TVQ_OK;
+    TVQ_CHECK(Y && (k == 0 || (A && W)), TVQ_ERR_INVALID, "null buffer");
+    TVQ_CHECK(n_bias == 0 || n_bias >= n, TVQ_ERR_SIZE, "bias smaller than N");
+    TVQ_CHECK(n_bias == 0 || bias, TVQ_ERR_INVALID, "null bias");
+    HOST_BEGIN
+    const int64_t kp = (k + 7) / 8 * 8;
+    uint16_t* dA = dev<uint16_t>(H, 0, static_cast<size_t>(std::max<int64_t>(m * kp, 1)));
+    uint16_t* dW = dev<uint16_t>(H, 1, static_cast<size_t>(std::max<int64_t>(n * kp, 1)));
+    float* dY = dev<float>(H, 2, static_cast<size_t>(m * n));
+    float* dB = dev<float>(H, 3, static_cast<size_t>(n_bias > 0 ? n : 1));
+    if (H.rc) return H.rc;
+    if (kp == k) {
+        STEP(H.h2d(dA, A, static_cast<size_t>(m * k) * 2));
+        STEP(H.h2d(dW, W, static_cast<size_t>(n * k) * 2));
+    } else if (k > 0) {
+        TVQ_CUDA(cudaMemsetAsync(dA, 0, static_cast<size_t>(m * kp) * 2, H.st()));
+        TVQ_CUDA(cudaMemsetAsync(dW, 0, static_cast<size_t>(n * kp) * 2, H.st()));
+        TVQ_CUDA(cudaMemcpy2DAsync(dA, kp * 2, A, k * 2, k * 2, m, cudaMemcpyHostToDevice, H.st()));
+        TVQ_CUDA(cudaMemcpy2DAsync(dW, kp * 2, W, k * 2, k * 2, n, cudaMemcpyHostToDevice, H.st()));
+    }
+    if (n_bias > 0) STEP(H.h2d(dB, bias, static_cast<size_t>(n) * 4));
+    GemmArgs g;
+    g.kind = GEMM_F16X3;  // without low parts: the plain fp16 product
+    g.A = dA;
+    g.W = dW;
+    g.bias = n_bias > 0 ? dB : nullptr;
+    g.Y = dY;
+    g.m = m;
+    g.n = n;
+    g.k = kp;
+    STEP(launch_gemm(g, H.st()));
+    STEP(H.d2h(Y, dY, static_cast<size_t>(m * n) * 4));
+    return H.finish();
+}
+
 // A bounded wait on an mbarrier that nothing ever arrives at: the
 // failure-detection path of every tensor-core kernel (record a code in the
 // device error word, return), made to run out on purpose with a short
@@ -705,6 +799,88 @@ int tvq_matmul_fp8_e4m3_i32(const int32_t* A, const int32_t* W, const float* bia
     TVQ_CATCH
 }
 
+int tvq_matmul_int8_asymmetric(const int8_t* A, const int8_t* W, const float* bias, int64_t n_bias, float* Y,
+                               int64_t m, int64_t n, int64_t k, float scale_a, int64_t zp_a, float scale_w,
+                               int64_t zp_w) {
+    TVQ_TRY
+    return host_gemm_asym(A, W, bias, n_bias, Y, m, n, k, scale_a, zp_a, scale_w, zp_w);
+    TVQ_CATCH
+}
+
+int tvq_matmul_int8_asymmetric_i32(const int32_t* A, const int32_t* W, const float* bias, int64_t n_bias, float* Y,
+                                   int64_t m, int64_t n, int64_t k, float scale_a, int64_t zp_a, float scale_w,
+                                   int64_t zp_w) {
+    TVQ_CHECK(m >= 0 && n >= 0 && k >= 0, TVQ_ERR_INVALID, "negative size");
+    if (m == 0 || n == 0) return TVQ_OK;
+    TVQ_CHECK(k == 0 || (A && W), TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    std::vector<uint8_t> a8, w8;
+    narrow_to_host_bytes(A, m * k, 0, a8);
+    narrow_to_host_bytes(W, n * k, 0, w8);
+    return host_gemm_asym(reinterpret_cast<const int8_t*>(a8.data()), reinterpret_cast<const int8_t*>(w8.data()), bias,
+                          n_bias, Y, m, n, k, scale_a, zp_a, scale_w, zp_w);
+    TVQ_CATCH
+}
+
+int tvq_matmul_fp16(const uint16_t* A, const uint16_t* W, const float* bias, int64_t n_bias, float* Y, int64_t m,
+                    int64_t n, int64_t k) {
+    TVQ_TRY
+    return host_gemm_f16(A, W, bias, n_bias, Y, m, n, k);
+    TVQ_CATCH
+}
+
+int tvq_matmul_fp16_i32(const int32_t* A, const int32_t* W, const float* bias, int64_t n_bias, float* Y, int64_t m,
+                        int64_t n, int64_t k) {
+    TVQ_CHECK(m >= 0 && n >= 0 && k >= 0, TVQ_ERR_INVALID, "negative size");
+    if (m == 0 || n == 0) return TVQ_OK;
+    TVQ_CHECK(k == 0 || (A && W), TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    // two list entries per element, low byte first (& 255 each, matmul.tkv:84-87)
+    std::vector<uint8_t> a8, w8;
+    narrow_to_host_bytes(A, 2 * m * k, 0, a8);
+    narrow_to_host_bytes(W, 2 * n * k, 0, w8);
+    return host_gemm_f16(reinterpret_cast<const uint16_t*>(a8.data()), reinterpret_cast<const uint16_t*>(w8.data()),
+                         bias, n_bias, Y, m, n, k);
+    TVQ_CATCH
+}
+
+int tvq_quantize_fp16(const float* src, int64_t n, uint16_t* dst, int64_t dst_len) {
+    TVQ_CHECK(n >= 0 && dst_len >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(dst_len >= n, TVQ_ERR_SIZE, "dst too small");
+    if (n == 0) return TVQ_OK;
+    TVQ_CHECK(src && dst, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    float* dx = dev<float>(H, 0, static_cast<size_t>(n));
+    uint16_t* dq = dev<uint16_t>(H, 1, static_cast<size_t>(n));
+    if (H.rc) return H.rc;
+    STEP(H.h2d(dx, src, static_cast<size_t>(n) * 4));
+    STEP(launch_f16_encode(dx, dq, n, H.st()));
+    STEP(H.d2h(dst, dq, static_cast<size_t>(n) * 2));
+    return H.finish();
+    TVQ_CATCH
+}
+
+int tvq_quantize_fp16_i32(const float* src, int64_t n, int32_t* dst, int64_t dst_len) {
+    TVQ_CHECK(n >= 0 && dst_len >= 0, TVQ_ERR_INVALID, "negative size");
+    TVQ_CHECK(dst_len >= 2 * n, TVQ_ERR_SIZE, "dst too small (need 2 bytes/elem)");  // matmul.tkv:107-108
+    if (n == 0) return TVQ_OK;
+    TVQ_CHECK(src && dst, TVQ_ERR_INVALID, "null buffer");
+    TVQ_TRY
+    HOST_BEGIN
+    float* dx = dev<float>(H, 0, static_cast<size_t>(n));
+    uint16_t* dq = dev<uint16_t>(H, 1, static_cast<size_t>(n));
+    int32_t* dw = dev<int32_t>(H, 2, static_cast<size_t>(2 * n));
+    if (H.rc) return H.rc;
+    STEP(H.h2d(dx, src, static_cast<size_t>(n) * 4));
+    STEP(launch_f16_encode(dx, dq, n, H.st()));
+    // each byte as a signed value (_to_sbyte, matmul.tkv:98-103), low byte first
+    STEP(launch_widen(dq, dw, 2 * n, 0, 0, H.st()));
+    STEP(H.d2h(dst, dw, static_cast<size_t>(2 * n) * 4));
+    return H.finish();
+    TVQ_CATCH
+}
+
 // ================================================================ device buffers
 
 int tvq_dev_minmax_reset(uint32_t* minmax_dev, void* stream) {
@@ -726,6 +902,65 @@ int tvq_dev_minmax_finalize(const uint32_t* minmax_dev, const float* first_dev, 
 int tvq_dev_quantize_int8(const float* x, int8_t* q, int64_t n, const float* scale_dev, void* stream) {
     TVQ_CHECK(n >= 0 && (n == 0 || (x && q && scale_dev)), TVQ_ERR_INVALID, "null buffer");
     return launch_quantize_i8(x, q, n, scale_dev, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_quantize_fp16(const float* x, uint16_t* q, int64_t n, void* stream) {
+    TVQ_CHECK(n >= 0 && (n == 0 || (x && q)), TVQ_ERR_INVALID, "null buffer");
+    return launch_f16_encode(x, q, n, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_matmul_fp16(const uint16_t* A, const uint16_t* W, const float* bias, float* Y, int64_t m, int64_t n,
+                        int64_t k, void* stream) {
+    TVQ_CHECK(m >= 0 && n >= 0 && k >= 0, TVQ_ERR_INVALID, "negative size");
+    if (m == 0 || n == 0) return TVQ_OK;
+    TVQ_CHECK(Y && (k == 0 || (A && W)), TVQ_ERR_INVALID, "null buffer");
+    GemmArgs g;
+    g.kind = GEMM_F16X3;  // without low parts: the plain fp16 product
+    g.A = A;
+    g.W = W;
+    g.bias = bias;
+    g.Y = Y;
+    g.m = m;
+    g.n = n;
+    g.k = k;
+    return launch_gemm(g, static_cast<cudaStream_t>(stream));
+}
+
+int tvq_dev_matmul_int8_asymmetric(const int8_t* A, const int8_t* W, const float* bias, float* Y, int64_t m, int64_t n,
+                                   int64_t k, const float* scale_a_dev, int64_t zp_a, const float* scale_w_dev,
+                                   int64_t zp_w, void* stream) {
+    TVQ_CHECK(m >= 0 && n >= 0 && k >= 0, TVQ_ERR_INVALID, "negative size");
+    if (m == 0 || n == 0) return TVQ_OK;
+    TVQ_CHECK(Y && scale_a_dev && scale_w_dev && (k == 0 || (A && W)), TVQ_ERR_INVALID, "null buffer");
+    TVQ_CHECK(m < (1ll << 31) && n < (1ll << 31), TVQ_ERR_UNSUPPORTED, "size out of range");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int* sums = nullptr;  // stream-ordered scratch: [m] + [n] row sums
+    TVQ_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&sums), sizeof(int) * static_cast<size_t>(m + n), st));
+    int rc = launch_row_sums_i8(A, m, k, sums, st);
+    if (!rc) rc = launch_row_sums_i8(W, n, k, sums + m, st);
+    if (!rc) {
+        GemmArgs g;
+        g.kind = GEMM_I8;
+        g.A = A;
+        g.W = W;
+        g.bias = bias;
+        g.Y = Y;
+        g.m = m;
+        g.n = n;
+        g.k = k;
+        g.scale_a = scale_a_dev;
+        g.scales_w = scale_w_dev;
+        g.per_channel = 0;
+        g.zp_rows = sums;
+        g.zp_cols = sums + m;
+        g.zp_a = zp_a;
+        g.zp_w = zp_w;
+        g.zp_k = k;
+        rc = launch_gemm(g, st);
+    }
+    cudaError_t e = cudaFreeAsync(sums, st);
+    if (!rc && e != cudaSuccess) return cuda_fail(e, "cudaFreeAsync");
+    return rc;
 }
 
 int tvq_dev_calibrate_quantize_per_channel(const float* w, int8_t* q, float* scales_dev, int64_t rows, int64_t cols,

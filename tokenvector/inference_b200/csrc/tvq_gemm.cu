@@ -80,6 +80,13 @@ constexpr int F16_PROMOTE_KB = 3;
 struct KParams {
     int m, n, k;
     int num_m_blocks, num_n_blocks, num_k_blocks;
+    int group_m;     // tile order: groups of group_m m-blocks, m fastest inside a group
+    int single;      // GEMM_F16X3 without low parts: y = A W^T + bias on fp16 operands (matmul_fp16)
+    // INT8, per-tensor scales, zero points (matmul_int8_asymmetric):
+    // acc' = acc - zpw zrow[m] - zpa zcol[n] + zconst, exact in binary64
+    const int* zrow;
+    const int* zcol;
+    double zpa, zpw, zconst;
     int promote_kb;  // k-blocks per TMEM accumulation unit (split kinds)
     int group_ks;    // GEMM_W4: k-steps (16 elements) per weight group = per accumulation unit
     int ngroups;     // GEMM_W4: k / group_size
@@ -363,6 +370,24 @@ __device__ __forceinline__ void stage_and_store(const KParams& p, const EpiCtx& 
     }
 }
 
+// Tile -> (m-block, n-block).  Tiles run in groups of group_m m-blocks with
+// the m-block fastest inside a group, so the CTAs working at the same time
+// share a few A row panels and W column panels in L2 (M-fastest order over
+// all m-blocks streams the whole of A once per round of tiles).
+__device__ __forceinline__ void tile_coords(const KParams& p, int tile, int& mb, int& nb) {
+    if (p.group_m >= p.num_m_blocks) {  // one group: plain m-fastest order
+        mb = tile % p.num_m_blocks;
+        nb = tile / p.num_m_blocks;
+        return;
+    }
+    const int per_group = p.group_m * p.num_n_blocks;
+    const int g = tile / per_group, r = tile - g * per_group;
+    const int first = g * p.group_m;
+    const int gm = min(p.group_m, p.num_m_blocks - first);
+    mb = first + r % gm;
+    nb = r / gm;
+}
+
 template <int KIND, int BN>
 __device__ __forceinline__ constexpr uint32_t make_idesc() {
     // instruction descriptor: [4,6) D format, [7,10) A format, [10,13) B
@@ -455,17 +480,19 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
             uint32_t it = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                const int mb = tile % p.num_m_blocks;
-                const int nb = tile / p.num_m_blocks;
+                int mb, nb;
+                tile_coords(p, tile, mb, nb);
                 for (int kb = 0; kb < p.num_k_blocks; kb++, it++) {
                     const uint32_t s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1u;
                     if (!mbar_wait(&empty[s], ph ^ 1u, p.err, DEVERR_TIMEOUT_PRODUCER)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+                    mbar_arrive_expect_tx(&full[s], p.single ? C::A_BYTES + C::B_BYTES : C::STAGE_BYTES);
                     tma_load_2d(&tmA, &full[s], sA + s * NSA * C::A_BYTES, kb * C::BKE, mb * BM);
                     tma_load_2d(&tmB, &full[s], sB + s * NSB * C::B_BYTES, kb * C::BKE, nb * BN);
-                    if (NSA == 2) tma_load_2d(&tmA2, &full[s], sA + (s * NSA + 1) * C::A_BYTES, kb * C::BKE, mb * BM);
-                    if (NSB == 2) tma_load_2d(&tmB2, &full[s], sB + (s * NSB + 1) * C::B_BYTES, kb * C::BKE, nb * BN);
+                    if (NSA == 2 && !p.single)
+                        tma_load_2d(&tmA2, &full[s], sA + (s * NSA + 1) * C::A_BYTES, kb * C::BKE, mb * BM);
+                    if (NSB == 2 && !p.single)
+                        tma_load_2d(&tmB2, &full[s], sB + (s * NSB + 1) * C::B_BYTES, kb * C::BKE, nb * BN);
                 }
             }
             // every issued load lands before the CTA may exit
@@ -549,6 +576,10 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                         } else if (KIND == GEMM_F8) {
                             umma_f8(d_tmem, ad, bd, idesc, accum);
                         } else if (KIND == GEMM_F16X3) {
+                            if (p.single) {  // plain fp16 operands: one product
+                                umma_f16(d_tmem, ad, bd, idesc, accum);
+                                continue;
+                            }
                             // same three products on fp16 parts (16 K per instruction)
                             const uint64_t adl = smem_desc_k_sw128(a0 + C::A_BYTES + kk * UMMA_K);
                             const uint64_t bdl = smem_desc_k_sw128(b0 + C::B_BYTES + kk * UMMA_K);
@@ -588,8 +619,15 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
         float* stage = reinterpret_cast<float*>(smem + C::RING) + (warp - 4) * (32 * E::CH);
         const bool bias_on = p.bias != nullptr;
         const bool per_channel = p.per_channel != 0;
+        // per channel: fl64(fl64(acc*sa)*sw) = fl64(acc*(sa*sw)) whenever acc*sa
+        // is exact in f64 (sa*sw always is: two 24-bit significands): an f32
+        // accumulator always, an int32 one while |acc| <= 127^2 K < 2^29
+        const bool fold = per_channel && (KIND != GEMM_I8 || p.k < 33283);
+        // zero points (per-tensor INT8 only): s = fl64(sa sw) stays in a register
+        const bool asym = KIND == GEMM_I8 && p.zcol != nullptr;
         const float sa = (promoted_kind(KIND) || p.acc_only) ? 1.0f : __ldg(p.scale_a);
         const float sw0 = (promoted_kind(KIND) || p.acc_only) ? 1.0f : __ldg(p.scales_w);
+        const double s_asym = static_cast<double>(sa) * static_cast<double>(sw0);
         InvScale qs{0.0, 0.0f, 0.0f};
         if (p.Yq) qs = make_inv_scale(static_cast<double>(__ldg(p.scale_out)));
         EpiCtx ec{(p.n & 3) == 0, qs, sa};
@@ -603,8 +641,8 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
             bool alive = true;
             const int nunits = (KIND == GEMM_W4) ? p.ngroups : (p.num_k_blocks + p.promote_kb - 1) / p.promote_kb;
             for (int tile = blockIdx.x; tile < num_tiles && alive; tile += gridDim.x) {
-                const int mb = tile % p.num_m_blocks;
-                const int nb = tile / p.num_m_blocks;
+                int mb, nb;
+                tile_coords(p, tile, mb, nb);
                 const int row0 = mb * BM + eg * 32;
                 float acc[NCH][E::CH];
                 for (int u = 0; u < nunits; u++, ucount++) {
@@ -666,6 +704,18 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                     }
                 }
                 if constexpr (KIND == GEMM_F16X3) {
+                  if (p.single) {
+                    // matmul_fp16: y = acc + bias
+                    if (bias_on) {
+#pragma unroll
+                        for (int i = 0; i < NCH; i++) {
+                            const int n0 = nb * BN + (half + E::EPW * i) * E::CH;
+#pragma unroll
+                            for (int j = 0; j < E::CH; j++)
+                                acc[i][j] = __fadd_rn(acc[i][j], __ldg(p.bias + min(n0 + j, p.n - 1)));
+                        }
+                    }
+                  } else {
                     // undo the rows' power-of-two scales (exact)
                     const int row = row0 + lane;
                     const float ra = (row < p.m) ? __ldg(p.scale_a + row) : 0.0f;
@@ -690,6 +740,7 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                                 acc[i][j] = acc[i][j] * ra * __ldg(p.scales_w + min(n0 + j, p.n - 1));
                         }
                     }
+                  }
                 }
 #pragma unroll
                 for (int i = 0; i < NCH; i++) {
@@ -706,8 +757,8 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, tcount++) {
             const uint32_t b = tcount % C::NACC;
             const uint32_t aph = (tcount / C::NACC) & 1u;
-            const int mb = tile % p.num_m_blocks;
-            const int nb = tile / p.num_m_blocks;
+            int mb, nb;
+            tile_coords(p, tile, mb, nb);
             const int row0 = mb * BM + eg * 32;
             // while the tile's MMAs run: the tile's per-column scales and
             // bias into shared memory (buffer tcount & 1; the barrier below
@@ -719,9 +770,15 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
             for (int i = etid; i < BN; i += E::EPI_WARPS * 32) {
                 const int n = min(nb * BN + i, p.n - 1);
                 const double sw = static_cast<double>(per_channel ? __ldg(p.scales_w + n) : sw0);
-                csc[i] = per_channel ? sw : static_cast<double>(sa) * sw;  // exact in f64
+                // (zero points: the column's term -zpa sum_k W[n, k] instead, exact)
+                csc[i] = asym ? -p.zpa * static_cast<double>(__ldg(p.zcol + n))
+                              : (per_channel && !fold) ? sw : static_cast<double>(sa) * sw;  // exact in f64
                 cbi[i] = static_cast<double>(bias_on ? __ldg(p.bias + n) : 0.0f);
             }
+            // this lane's row: zconst - zpw sum_k A[row, k] (exact)
+            const double zrow_term = (asym && row0 + lane < p.m)
+                                         ? p.zconst - p.zpw * static_cast<double>(__ldg(p.zrow + row0 + lane))
+                                         : 0.0;
             if (p.residual) {
                 const int row = row0 + lane;
                 for (int c = half; c < BN / E::CH; c += E::EPW) {
@@ -771,7 +828,9 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                 for (int j = 0; j < E::CH; j++) {
                     const double a = (KIND == GEMM_I8) ? static_cast<double>(static_cast<int>(r[j]))
                                                        : static_cast<double>(__uint_as_float(r[j]));
-                    const double v = per_channel ? __dmul_rn(__dmul_rn(a, static_cast<double>(sa)), wv[j]) : __dmul_rn(a, wv[j]);
+                    const double v = (per_channel && !fold) ? __dmul_rn(__dmul_rn(a, static_cast<double>(sa)), wv[j])
+                                     : asym ? __dmul_rn(__dadd_rn(__dadd_rn(a, zrow_term), wv[j]), s_asym)
+                                            : __dmul_rn(a, wv[j]);
                     y[j] = __double2float_rn(__dadd_rn(v, bdv[j]));
                 }
                 float kvf = 1.0f;
@@ -939,8 +998,8 @@ int launch_tc(const KParams& p, const GemmArgs& g, int grid, cudaStream_t st) {
     CUtensorMap ma, mb, ma2, mb2;
     int rc = make_map(&ma, g.A, p.m, p.k, BM, C::ELEM);
     if (!rc) rc = make_map(&mb, g.W, p.n, p.k, BN, C::ELEM);
-    if (!rc && C::NSA == 2) rc = make_map(&ma2, g.A2, p.m, p.k, BM, C::ELEM);
-    if (!rc && C::NSB == 2) rc = make_map(&mb2, g.W2, p.n, p.k, BN, C::ELEM);
+    if (!rc && C::NSA == 2) rc = make_map(&ma2, g.A2 ? g.A2 : g.A, p.m, p.k, BM, C::ELEM);  // single: unused
+    if (!rc && C::NSB == 2) rc = make_map(&mb2, g.W2 ? g.W2 : g.W, p.n, p.k, BN, C::ELEM);
     if (rc) return rc;
     if (C::NSA == 1) ma2 = ma;
     if (C::NSB == 1) mb2 = mb;
@@ -1059,14 +1118,21 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     TVQ_CHECK(g.kind >= GEMM_I8 && g.kind <= GEMM_W4, TVQ_ERR_INVALID, "unknown GEMM kind");
     const bool split = split_kind(g.kind);
     const bool w4 = g.kind == GEMM_W4;
-    TVQ_CHECK(g.kind == GEMM_TF32X3 || acc_only || (g.scale_a && g.scales_w), TVQ_ERR_INVALID,
+    const bool single = g.kind == GEMM_F16X3 && !g.A2 && !g.W2;
+    const bool asym = g.zp_rows || g.zp_cols;
+    TVQ_CHECK(g.kind == GEMM_TF32X3 || single || acc_only || (g.scale_a && g.scales_w), TVQ_ERR_INVALID,
               "scale pointers are required");
+    TVQ_CHECK(!asym || (g.kind == GEMM_I8 && g.zp_rows && g.zp_cols && !g.per_channel && !acc_only && !g.kh &&
+                        g.zp_k >= 0 && g.zp_k <= g.k),
+              TVQ_ERR_INVALID, "zero points need an INT8 GEMM with per-tensor scales and both sum vectors");
+    TVQ_CHECK(!asym || (std::llabs(g.zp_a) <= (1ll << 17) && std::llabs(g.zp_w) <= (1ll << 17)), TVQ_ERR_UNSUPPORTED,
+              "zero points beyond +-2^17 (the corrected accumulator must stay exact in binary64)");
     TVQ_CHECK(!w4 || (g.group_size > 0 && g.group_size % 16 == 0 && g.k % g.group_size == 0), TVQ_ERR_UNSUPPORTED,
               "the INT4 GEMM needs k a multiple of group_size, group_size a multiple of 16");
     TVQ_CHECK(!w4 || (!g.Yq && !g.residual && g.act == 0 && g.Y && !g.amax), TVQ_ERR_INVALID,
               "the INT4 GEMM writes f32 Y (+ bias) only");
-    TVQ_CHECK(!split || (!g.Yq && !g.bias && !g.residual && g.act == 0 && g.Y && !g.amax), TVQ_ERR_INVALID,
-              "the split fp32 GEMM writes plain f32 Y only");
+    TVQ_CHECK(!split || (!g.Yq && (single || !g.bias) && !g.residual && g.act == 0 && g.Y && !g.amax),
+              TVQ_ERR_INVALID, "the split fp32 GEMM writes plain f32 Y only");
     TVQ_CHECK(!g.Yq || g.scale_out, TVQ_ERR_INVALID, "int8 output needs scale_out");
     int rc = 0;
     DeviceState* ds = device_state(&rc);
@@ -1098,6 +1164,14 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.kv_exp = g.kv_exp;
     p.kv_bound = g.kv_bound;
     p.kv_vmax = g.kv_vmax;
+    p.single = single ? 1 : 0;
+    if (asym) {
+        p.zrow = g.zp_rows;
+        p.zcol = g.zp_cols;
+        p.zpa = static_cast<double>(g.zp_a);
+        p.zpw = static_cast<double>(g.zp_w);
+        p.zconst = static_cast<double>(g.zp_k * g.zp_a * g.zp_w);  // |.| < 2^52: exact
+    }
     p.acc_only = acc_only ? 1 : 0;
     p.act = g.act;
     p.scale_out = g.scale_out;
@@ -1109,11 +1183,11 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.promote_kb = g.kind == GEMM_F16X3 ? F16_PROMOTE_KB : TF32_PROMOTE_KB;
     if (const char* env = getenv("TVQ_TF32_PROMOTE_KB")) p.promote_kb = std::max(1, atoi(env));
 
-    if (g.k == 0 && split) {
+    if (g.k == 0 && split && !single) {
         TVQ_CUDA(cudaMemsetAsync(g.Y, 0, sizeof(float) * g.m * g.n, st));
         return TVQ_OK;
     }
-    if (g.k == 0 && w4) {
+    if (g.k == 0 && (w4 || single)) {
         const int grid = static_cast<int>(std::min<int64_t>((g.m * g.n + 255) / 256, ds->sm_count * 8));
         return launch_pdl(bias_rows_kernel, dim3(grid), dim3(256), 0, st, g.Y, g.bias, g.m, g.n);
     }
@@ -1125,7 +1199,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     TVQ_CHECK((g.k * elem) % 16 == 0, TVQ_ERR_UNSUPPORTED, "k must be a multiple of 16 bytes (TMA row pitch)");
     TVQ_CHECK(((reinterpret_cast<uintptr_t>(g.A) | reinterpret_cast<uintptr_t>(g.W)) & 15) == 0, TVQ_ERR_UNSUPPORTED,
               "A and W must be 16-byte aligned");
-    TVQ_CHECK(!split ||
+    TVQ_CHECK(!split || single ||
                   (g.A2 && g.W2 && ((reinterpret_cast<uintptr_t>(g.A2) | reinterpret_cast<uintptr_t>(g.W2)) & 15) == 0),
               TVQ_ERR_UNSUPPORTED, "the split GEMM needs 16-byte aligned low parts");
     TVQ_CHECK(!w4 || (g.A2 && (reinterpret_cast<uintptr_t>(g.A2) & 15) == 0), TVQ_ERR_UNSUPPORTED,
@@ -1181,6 +1255,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
         }
     }
     p.num_n_blocks = static_cast<int>((g.n + bn - 1) / bn);
+    p.group_m = 16;
     const int tiles = p.num_m_blocks * p.num_n_blocks;
     const int grid = std::min(tiles, ds->sm_count);
     if (g.kind == GEMM_I8) {

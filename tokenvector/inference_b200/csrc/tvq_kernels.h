@@ -76,8 +76,20 @@ struct GemmArgs {
     // with the operand split: max |V| of each head (float bits, atomicMax;
     // zeroed by the caller), the attention's exact-int8 error bound
     uint32_t* kv_vmax = nullptr;
+    // GEMM_I8, per-tensor scales: zero points (matmul_int8_asymmetric).
+    // zp_rows [m] = sum_k A[m, k], zp_cols [n] = sum_k W[n, k] (int32, any k
+    // padding included: zeros), zp_k the unpadded k; |zp_a|, |zp_w| <= 2^17
+    const int* zp_rows = nullptr;
+    const int* zp_cols = nullptr;
+    int64_t zp_a = 0, zp_w = 0, zp_k = 0;
 };
+// GEMM_F16X3 with A2 = W2 = null: the plain fp16 product y = A W^T + bias
+// (fp16 operands given directly, scale_a / scales_w unused; matmul_fp16).
 int launch_gemm(const GemmArgs& g, cudaStream_t st);
+// quantize_fp16: the reference's FP16 encoder (tvq_f16.h) of n floats
+int launch_f16_encode(const float* x, uint16_t* q, int64_t n, cudaStream_t st);
+// sum over k of each row of a [rows, k] int8 matrix (row pitch k)
+int launch_row_sums_i8(const int8_t* a, int64_t rows, int64_t k, int* out, cudaStream_t st);
 // Tensor map of a row-major f32 matrix [rows, cols] (row pitch `pitch`
 // elements, 0 = cols): box of 32 columns (128 bytes) x box_rows rows,
 // 128-byte swizzle.

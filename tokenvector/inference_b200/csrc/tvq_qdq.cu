@@ -248,6 +248,17 @@ int grid_1d(int64_t n, int threads) {
 
 }  // namespace
 
+int launch_row_sums_i8(const int8_t* a, int64_t rows, int64_t k, int* out, cudaStream_t st) {
+    TVQ_CHECK(rows >= 0 && k >= 0 && k < (1ll << 31), TVQ_ERR_INVALID, "bad row-sum size");
+    if (rows == 0) return TVQ_OK;
+    if (k == 0) {
+        TVQ_CUDA(cudaMemsetAsync(out, 0, sizeof(int) * rows, st));
+        return TVQ_OK;
+    }
+    return launch_pdl(row_sums_i8_kernel, dim3(static_cast<unsigned>((rows * 32 + 255) / 256)), dim3(256), 0, st, a,
+                      rows, static_cast<int>(k), out);
+}
+
 int launch_quantize_linear(const float* x, int8_t* y, int64_t outer, int64_t dim, int64_t inner, const float* scales,
                            int64_t nsc, int64_t zp, cudaStream_t st) {
     const int64_t n = outer * dim * inner;

@@ -19,6 +19,7 @@
 
 #include "tvq_common.cuh"
 #include "tvq_e4m3.h"
+#include "tvq_f16.h"
 #include "tvq_exact.cuh"
 #include "tvq_kernels.h"
 
@@ -614,6 +615,34 @@ int launch_fp8_decode(const uint8_t* q, float* y, int64_t n, cudaStream_t st) {
     fp8_decode_kernel<<<grid_for(n, threads, 8), threads, 0, st>>>(q, y, n);
     TVQ_CUDA(cudaGetLastError());
     return TVQ_OK;
+}
+
+// quantize_fp16 (matmul.tkv:106-114): the reference's FP16 encoder
+// (tvq_f16.h) per element.  VEC: 16-byte loads, 8-byte stores.
+template <int VEC>
+__global__ void f16_encode_kernel(const float* __restrict__ x, uint16_t* __restrict__ q, int64_t n) {
+    griddep_wait();
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    if (VEC) {
+        for (int64_t i = tid; i < n / 4; i += stride) {
+            const float4 v = __ldcs(reinterpret_cast<const float4*>(x) + i);
+            const uint32_t lo = f16_encode_fast(__float_as_uint(v.x)) | (f16_encode_fast(__float_as_uint(v.y)) << 16);
+            const uint32_t hi = f16_encode_fast(__float_as_uint(v.z)) | (f16_encode_fast(__float_as_uint(v.w)) << 16);
+            __stcs(reinterpret_cast<uint2*>(q) + i, make_uint2(lo, hi));
+        }
+        return;
+    }
+    for (int64_t i = tid; i < n; i += stride) q[i] = f16_encode_fast(__float_as_uint(x[i]));
+}
+
+int launch_f16_encode(const float* x, uint16_t* q, int64_t n, cudaStream_t st) {
+    if (n <= 0) return TVQ_OK;
+    const int threads = 256;
+    const bool vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && ((reinterpret_cast<uintptr_t>(q) & 7) == 0) &&
+                     n % 4 == 0;
+    if (vec) return launch_pdl(f16_encode_kernel<1>, dim3(grid_for(n / 4, threads, 8)), dim3(threads), 0, st, x, q, n);
+    return launch_pdl(f16_encode_kernel<0>, dim3(grid_for(n, threads, 8)), dim3(threads), 0, st, x, q, n);
 }
 
 // ------------------------------------------------------------ list[i32] forms

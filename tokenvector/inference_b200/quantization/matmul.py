@@ -13,8 +13,9 @@ import numpy as np
 from .. import _native as N
 from . import _buf as B
 
-__all__ = ["matmul_int8_symmetric", "matmul_int8_per_channel", "matmul_fp8_e4m3", "quantize_fp8_e4m3",
-           "quantize_fp8_e4m3_scaled", "dequantize_fp8_e4m3", "gemm_i8_accumulators"]
+__all__ = ["matmul_int8_symmetric", "matmul_int8_per_channel", "matmul_int8_asymmetric", "matmul_fp8_e4m3",
+           "matmul_fp16", "quantize_fp16", "quantize_fp8_e4m3", "quantize_fp8_e4m3_scaled", "dequantize_fp8_e4m3",
+           "gemm_i8_accumulators"]
 
 
 def _as_i8(x) -> np.ndarray:
@@ -144,4 +145,72 @@ def dequantize_fp8_e4m3(src, dst) -> int:
     out = np.empty(q.size, np.float32)
     N.call("tvq_dequantize_fp8_e4m3", B.ptr(q), q.size, B.ptr(out), out.size)
     np.asarray(dst).reshape(-1)[:q.size] = out
+    return 0
+
+
+def matmul_int8_asymmetric(pa, pw, pbias, py, m: int, n: int, k: int, scale_a: float, zp_a: int, scale_w: float,
+                           zp_w: int) -> int:
+    """matmul_int8_asymmetric, matmul.tkv:31-44: sum (a - zp_a)(w - zp_w),
+    exact, times fl64(scale_a scale_w), plus the bias.  Zero points beyond
+    +-2^17 raise TvqError (TVQ_ERR_UNSUPPORTED)."""
+    bias, nb = _bias(pbias)
+    if B.is_dev(pa):
+        sa = _dev_scalar(scale_a, pa)
+        sw = _dev_scalar(scale_w, pa)
+        N.call("tvq_dev_matmul_int8_asymmetric", B.ptr(pa), B.ptr(pw), B.ptr(bias), B.ptr(py), m, n, k, B.ptr(sa),
+               int(zp_a), B.ptr(sw), int(zp_w), B.stream_of(pa))
+        return 0
+    A, W = _as_i8(pa), _as_i8(pw)
+    bh = B.host_f32(bias) if bias is not None else None
+    Y = np.empty(m * n, np.float32)
+    N.call("tvq_matmul_int8_asymmetric", B.ptr(A), B.ptr(W), B.ptr(bh), nb, B.ptr(Y), m, n, k, float(scale_a),
+           int(zp_a), float(scale_w), int(zp_w))
+    np.asarray(py).reshape(-1)[:m * n] = Y
+    return 0
+
+
+def _f16_bits(x, count: int) -> np.ndarray:
+    a = np.asarray(x)
+    if a.dtype in (np.uint16, np.float16):
+        return np.ascontiguousarray(a.view(np.uint16)).reshape(-1)[:count]
+    # the reference's list[i32]: two entries per element, low byte first (matmul.tkv:84-87)
+    b = (a.astype(np.int64).reshape(-1)[:2 * count] & 255).astype(np.uint16)
+    return np.ascontiguousarray(b[0::2] | (b[1::2] << 8))
+
+
+def matmul_fp16(pa, pw, pbias, py, m: int, n: int, k: int) -> int:
+    """matmul_fp16, matmul.tkv:79-96: pa / pw fp16 bit patterns (uint16 or
+    float16 arrays, device uint16 / float16 tensors, or the reference's byte
+    lists), y = sum a w + bias on the FP16 tensor cores (tolerance in
+    include/tvq.h)."""
+    bias, _nb = _bias(pbias)
+    if B.is_dev(pa):
+        N.call("tvq_dev_matmul_fp16", B.ptr(pa), B.ptr(pw), B.ptr(bias), B.ptr(py), m, n, k, B.stream_of(pa))
+        return 0
+    A, W = _f16_bits(pa, m * k), _f16_bits(pw, n * k)
+    bh = B.host_f32(bias) if bias is not None else None
+    Y = np.empty(m * n, np.float32)
+    N.call("tvq_matmul_fp16", B.ptr(A), B.ptr(W), B.ptr(bh), _nb, B.ptr(Y), m, n, k)
+    np.asarray(py).reshape(-1)[:m * n] = Y
+    return 0
+
+
+def quantize_fp16(src, dst) -> int:
+    """quantize_fp16, matmul.tkv:106-114.  A uint16 / float16 dst receives
+    the fp16 patterns; an int32 dst (the reference's list) two signed bytes
+    per element and must hold 2 len(src) (ValueError otherwise)."""
+    s = B.host_f32(src).ravel()
+    d = np.asarray(dst)
+    if d.dtype in (np.uint16, np.float16):
+        if d.size < s.size:
+            raise ValueError("dst too small")
+        out = np.empty(s.size, np.uint16)
+        N.call("tvq_quantize_fp16", B.ptr(s), s.size, B.ptr(out), out.size)
+        d.reshape(-1).view(np.uint16)[:s.size] = out
+        return 0
+    if d.size < 2 * s.size:
+        raise ValueError("dst too small (need 2 bytes/elem)")
+    out = np.empty(2 * s.size, np.int32)
+    N.call("tvq_quantize_fp16_i32", B.ptr(s), s.size, B.ptr(out), out.size)
+    d.reshape(-1)[:2 * s.size] = out
     return 0
