@@ -225,8 +225,8 @@ def test_session_launch_count_and_both_attention_paths(monkeypatch):
         s.prepare(seg)
         s.set_act_scales(scales)
         got_tc = s.forward(ids)
-        # + the exact-int8 fix-up of the attention context per layer (two kernels)
-        assert s.launches() == 1 + 9 * cfg.n_layers + 2
+        # + the exact-int8 fix-up of the attention context per layer (one kernel)
+        assert s.launches() == 1 + 8 * cfg.n_layers + 2
         monkeypatch.setenv("TVQ_ATTN_TC", "0")
         s.prepare(seg)
         got_simt = s.forward(ids)
@@ -260,14 +260,14 @@ def test_host_logits_chunked_lm_head_matches_device_forward(lengths):
         s.prepare(seg)
         s.calibrate(_ids(T, cfg.vocab, 3))
         got = s.forward(ids)
-        assert s.launches() == 1 + 9 * cfg.n_layers + 1 + (T + 255) // 256
+        assert s.launches() == 1 + 8 * cfg.n_layers + 1 + (T + 255) // 256
         got2 = s.forward(ids)  # the events and the copy stream are reused
         ids_dev = torch.from_numpy(ids).to("cuda:0")
         out_dev = torch.empty((T, cfg.vocab), dtype=torch.float32, device="cuda:0")
         torch.cuda.synchronize()
         s.forward_device(ids_dev.data_ptr(), out_dev.data_ptr())
         torch.cuda.synchronize()
-        assert s.launches() == 1 + 9 * cfg.n_layers + 2
+        assert s.launches() == 1 + 8 * cfg.n_layers + 2
         dev = out_dev.cpu().numpy()
     finally:
         s.close()
@@ -333,7 +333,7 @@ def test_layer_stack_dynamic_matches_oracle(cfg, lengths):
     scales = cal.scales()
     st.set_act_scales(scales)
     got = st.run(x, dynamic=False)
-    assert st.launches() == 9 * cfg.n_layers
+    assert st.launches() == 8 * cfg.n_layers
     _assert_flip_bounded(got, OG.blocks(layers, x, seg, scales=scales, qweights=qw, n_heads=cfg.n_heads),
                          rows_frac=0.10)
     # device-resident form: in place on the session's hidden states, twice;

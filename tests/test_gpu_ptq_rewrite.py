@@ -84,9 +84,10 @@ def test_rewritten_linear_relu_fused_bit_exact():
 
 
 def test_rewritten_linear_gelu_fused():
-    """GELU (tanh form) runs in the GEMM epilogue with CUDA's expf; the
-    oracle's apply_activation uses the host libm's.  Tolerance: 4 ulp of the
-    f32 result plus 1e-7 absolute near zero."""
+    """GELU (tanh form) runs in the GEMM epilogue in the reference's binary64
+    model with CUDA's exp; the oracle uses the host libm's exp.  Tolerance: 1
+    ulp of the f32 result (a binary64 quotient within an ulp of an f32
+    rounding boundary), and at most 1 % of the elements off at all."""
     m, k, n = 128, 256, 256
     rng = np.random.default_rng(6)
     x = rng.standard_normal((m, k)).astype(np.float32)
@@ -99,8 +100,9 @@ def test_rewritten_linear_gelu_fused():
     pre = _oracle(x, [x], w_nk, bias)[0]
     ref = np.array([O.gelu_tanh(float(v)) for v in pre.ravel()], np.float32).reshape(m, n)
     err = np.abs(y.astype(np.float64) - ref)
-    tol = 4 * np.spacing(np.abs(ref)).astype(np.float64) + 1e-7
+    tol = np.spacing(np.abs(ref)).astype(np.float64)
     assert (err <= tol).all(), float((err / tol).max())
+    assert (err > 0).mean() < 0.01
 
 
 def test_artefact_reload_reproduces_session(tmp_path):

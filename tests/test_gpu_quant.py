@@ -4,6 +4,7 @@ import numpy as np
 import pytest
 
 import oracle as O
+from tokenvector.inference_b200 import _native as N
 from tokenvector.inference_b200.quantization import engine as E
 from tokenvector.inference_b200.quantization import matmul as M
 from tokenvector.inference_b200.quantization import types as T
@@ -207,3 +208,25 @@ def test_fp8_scaled_quantize(cols):
     st = np.array([np.abs(x).max() / 448.0], np.float32)
     g = M.quantize_fp8_e4m3_scaled(x, 64, cols, st, False)
     assert np.array_equal(g, O.quantize_fp8_e4m3_scaled(x, st, False))
+
+
+def test_fp8_encode_all_binary32_inputs():
+    """The device encoder (hardware RN-satfinite conversion where it agrees
+    with the reference, the integer form elsewhere) against the oracle's
+    restatement of native_fp8_e4m3_encode (types.tkv:154-191) on every one
+    of the 2^32 binary32 bit patterns, in chunks of 2^26 through the device
+    entry point (flat, unscaled: 16-byte loads, the vector kernel)."""
+    import torch
+    dev = torch.device("cuda", 0)
+    st = torch.cuda.current_stream()
+    chunk = 1 << 26
+    xd = torch.empty(chunk, dtype=torch.float32, device=dev)
+    qd = torch.empty(chunk, dtype=torch.uint8, device=dev)
+    bad = 0
+    for c in range(1 << 6):
+        bits = np.arange(c * chunk, (c + 1) * chunk, dtype=np.uint64).astype(np.uint32)
+        x = bits.view(np.float32)
+        xd.copy_(torch.from_numpy(x))
+        N.call("tvq_dev_quantize_fp8", xd.data_ptr(), qd.data_ptr(), 1, chunk, None, 0, N.FP8_REF, st.cuda_stream)
+        bad += int((qd.cpu().numpy() != O.quantize_fp8_e4m3(x)).sum())
+    assert bad == 0

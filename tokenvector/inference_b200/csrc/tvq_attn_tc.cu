@@ -84,7 +84,9 @@ constexpr uint32_t OFF_RED = OFF_V + 2 * KSTAGE;     // float [2][2][128] row ma
 constexpr uint32_t OFF_LSUM = OFF_RED + 2 * 2 * TQ * 4;  // float [2][128] row sums
 // exact-int8 collection: int flag[128], int2 row[128], 4 ints, float row max[128]
 constexpr uint32_t OFF_FIX = OFF_LSUM + 2 * TQ * 4;
-constexpr uint32_t OFF_BAR = OFF_FIX + TQ * 4 + TQ * 8 + 16 + TQ * 4;
+// exact-int8 bookkeeping: undecided-column masks [row][half], the unit's
+// collected rows {q, row max} and their masks, 4 control words, row maxima
+constexpr uint32_t OFF_BAR = OFF_FIX + TQ * 8 + TQ * 8 + TQ * 8 + 16 + TQ * 4;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 512 + 1024;
 
 // tensor memory columns: S[2], O[2] (64 f32 each), P[2] (hi 32 + lo 32
@@ -237,6 +239,16 @@ __global__ void kv_head_amax_kernel(const float* __restrict__ qkv, int T, int d,
     if ((threadIdx.x & 31) == 0) atomicMax(amax + part * heads + h, __float_as_uint(m));
 }
 
+// max |V| of each V column of qkv [T, 3d] (f32 bit patterns, atomicMax):
+// block x = 64 columns (one head), block y strides over the rows
+__global__ void v_col_amax_kernel(const float* __restrict__ qkv, int T, int d, uint32_t* __restrict__ vcol) {
+    griddep_wait();
+    const int c = blockIdx.x * HD + threadIdx.x;
+    float m = 0.0f;
+    for (int t = blockIdx.y; t < T; t += gridDim.y) m = fmaxf(m, fabsf(qkv[static_cast<int64_t>(t) * 3 * d + 2 * d + c]));
+    atomicMax(vcol + c, __float_as_uint(m));
+}
+
 __global__ void kv_exp_from_amax_kernel(const uint32_t* __restrict__ amax, int n, int* __restrict__ kv_exp) {
     griddep_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -261,15 +273,14 @@ struct AttnParams {
     int* err;
     int nunits;        // work units: (item, head) = (u / nheads, u % nheads), items longest first
     // exact int8 output: rows whose int8 context the kernel's error bound
-    // (2^-20 max |V| of the head) could round differently from the
-    // reference's f64 context are recomputed by attention_fix_kernel, grouped
-    // by work unit (one head, one sequence)
-    const uint32_t* vmax;  // [nheads] max |V| per head (float bits) or null
-    int4* fix;             // rows {q, row max (float bits), head, 0}
-    int* fix_n;            // [0] rows, [1] units, [2] finished fix-up CTAs
+    // (2^-20 max |V| of the column) could round differently from the
+    // reference's f64 context are recomputed by attention_fix_kernel, only
+    // the columns it could not decide
+    const uint32_t* vmax;  // [d] max |V| per V column (float bits) or null
+    int4* fix;             // rows {q, row max (float bits), head, sequence start}
+    uint2* fix_mask;       // their undecided columns (bit c of .x / .y: column c / 32 + c)
+    int* fix_n;            // [0] rows, [1] rows taken by the fix-up, [2] finished fix-up CTAs
     int fix_cap;
-    int4* fix_units;       // {first row, rows | head << 8, sequence start, largest q}
-    int fix_ucap;
 };
 
 // Unit k of this CTA: rounds of gridDim.x units in snake order (CTA c takes
@@ -321,10 +332,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* red = reinterpret_cast<float*>(sm + OFF_RED);    // [parity][half][row]
     float* lsum = reinterpret_cast<float*>(sm + OFF_LSUM);  // [half][row]
-    int* fx_flag = reinterpret_cast<int*>(sm + OFF_FIX);      // [row] undecided
-    int2* fx_row = reinterpret_cast<int2*>(sm + OFF_FIX + TQ * 4);  // collected {q, row max}
-    int* fx_ctl = reinterpret_cast<int*>(sm + OFF_FIX + TQ * 12);  // count, first row, largest q, rows
-    float* fx_m = reinterpret_cast<float*>(sm + OFF_FIX + TQ * 12 + 16);  // [row] row max of a flagged row
+    uint32_t* fx_mask = reinterpret_cast<uint32_t*>(sm + OFF_FIX);      // [row][half] undecided columns
+    int2* fx_row = reinterpret_cast<int2*>(sm + OFF_FIX + TQ * 8);        // collected {q, row max}
+    uint2* fx_rmask = reinterpret_cast<uint2*>(sm + OFF_FIX + TQ * 16);   // their column masks
+    int* fx_ctl = reinterpret_cast<int*>(sm + OFF_FIX + TQ * 24);         // count, first list slot, -, rows
+    float* fx_m = reinterpret_cast<float*>(sm + OFF_FIX + TQ * 24 + 16);  // [row] row max of a flagged row
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
     uint64_t* k_full = bars;           // [2]
     uint64_t* k_empty = bars + 2;      // [2]
@@ -365,7 +377,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int i = 0; i < 4; i++) mbar_init(&lxch[i], 2);
         fence_barrier_init();
     }
-    if (threadIdx.x >= 128 && threadIdx.x < 128 + TQ) fx_flag[threadIdx.x - 128] = 0;
+    if (threadIdx.x >= 128 && threadIdx.x < 128 + 2 * TQ) fx_mask[threadIdx.x - 128] = 0u;
     if (threadIdx.x < 4) fx_ctl[threadIdx.x] = 0;
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmQh);
@@ -768,21 +780,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                 if (bad & (1u << c)) v.b[c] = quant_exact(o[c], qs);
                         }
                         if (p.fix) {
-                            // |o - reference| <= 2^-20 max|V| (measured on B200: at most
-                            // 2^-20.9 of the column's running max |V|, which the head's max
-                            // bounds): a row with a value that close to an int8 rounding
-                            // boundary is recomputed exactly by attention_fix_kernel
-                            const float mrg = fmaf(__uint_as_float(__ldg(p.vmax + head)), qs.hi * 9.5367431640625e-07f,
-                                                   1.52587890625e-05f);
-                            bool near = false;
+                            // |o - reference| <= 2^-20 max|V| of the column (measured on
+                            // B200: at most 2^-20.9 of the column's running max |V|): a
+                            // value that close to an int8 rounding boundary is recomputed
+                            // exactly by attention_fix_kernel
+                            const float k20 = qs.hi * 9.5367431640625e-07f;
+                            const uint32_t* vcol = p.vmax + head * HD + 32 * h;
+                            uint32_t near = 0u;  // this half's undecided columns
 #pragma unroll
                             for (int c = 0; c < 32; c++) {
+                                const float mrg = fmaf(__uint_as_float(__ldg(vcol + c)), k20, 1.52587890625e-05f);
                                 const float t = __fmul_rn(o[c], qs.hi);
                                 const float rr = __fsub_rn(__fadd_rn(t, 12582912.0f), 12582912.0f);
-                                near |= fabsf(fabsf(__fsub_rn(t, rr)) - 0.5f) < mrg;
+                                near |= (fabsf(fabsf(__fsub_rn(t, rr)) - 0.5f) < mrg) ? (1u << c) : 0u;
                             }
                             if (near) {  // either half (both hold the same row max)
-                                fx_flag[r] = 1;
+                                fx_mask[2 * r + h] = near;
                                 fx_m[r] = mfin;
                             }
                         }
@@ -808,12 +821,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (p.fix && p.outq && write_out) {  // write_out is uniform over the 256 softmax threads; alive may not be
                 // the unit's undecided rows, once each, as one group: a unit
                 // entry and its rows (all of one head and one sequence)
-                named_bar_sync(3, 256);  // every flag is set
-                if (h == 0 && fx_flag[r]) {
+                named_bar_sync(3, 256);  // every mask is set
+                if (h == 0 && (fx_mask[2 * r] | fx_mask[2 * r + 1])) {
                     const int slot = atomicAdd(&fx_ctl[0], 1);
                     fx_row[slot] = make_int2(q, __float_as_int(fx_m[r]));
-                    atomicMax(&fx_ctl[2], q);
-                    fx_flag[r] = 0;
+                    fx_rmask[slot] = make_uint2(fx_mask[2 * r], fx_mask[2 * r + 1]);
+                    fx_mask[2 * r] = 0u;
+                    fx_mask[2 * r + 1] = 0u;
                 }
                 named_bar_sync(3, 256);
                 if (threadIdx.x == 128) {
@@ -821,26 +835,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     int b = -1;
                     if (cnt > 0) {
                         b = atomicAdd(p.fix_n, cnt);
-                        const int ui = atomicAdd(p.fix_n + 1, 1);
-                        if (b + cnt <= p.fix_cap && ui < p.fix_ucap) {
-                            p.fix_units[ui] = make_int4(b, cnt | (head << 8), w.s0, fx_ctl[2]);
-                        } else {
-                            // lists full: record it; a reserved unit slot gets an
-                            // empty entry (no rows, no keys) so the fix-up skips it
+                        if (b + cnt > p.fix_cap) {  // list full: recorded, these rows stay as computed
                             record_error(p.err, DEVERR_FIX_FULL);
-                            if (ui < p.fix_ucap) p.fix_units[ui] = make_int4(0, head << 8, w.s0, w.s0 - 1);
                             b = -1;
                         }
                     }
                     fx_ctl[1] = b;
                     fx_ctl[3] = cnt;
                     fx_ctl[0] = 0;
-                    fx_ctl[2] = 0;
                 }
                 named_bar_sync(3, 256);
                 const int cnt = fx_ctl[3], b = fx_ctl[1];
                 const int i = threadIdx.x - 128;
-                if (b >= 0 && i < cnt) p.fix[b + i] = make_int4(fx_row[i].x, fx_row[i].y, head, 0);
+                if (b >= 0 && i < cnt) {
+                    p.fix[b + i] = make_int4(fx_row[i].x, fx_row[i].y, head, w.s0);
+                    p.fix_mask[b + i] = fx_rmask[i];
+                }
             }
             // the eight softmax warps leave the unit loop together (each unit
             // then runs the same named barriers in every warp)
@@ -857,187 +867,187 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
-// Per-head bounds of a c_attn layer's Q, K and V outputs for the epilogue's
-// fp16 split (kv_head_exp): block (h, part) over the 64 output columns n of
-// head h in part (0 Q, 1 K, 2 V): A = max sw[n] * 127 * sum_k |W[n,k]|, B =
-// max |bias[n]|, both rounded up.  out [6 heads]: A_Q, B_Q, A_K, B_K, A_V, B_V.
-// Rows of the context whose int8 value the tensor-core kernel could not
-// decide (AttnParams::fix), recomputed as the reference computes them
+// The undecided columns of the context rows the tensor-core kernel listed
+// (AttnParams::fix), recomputed as the reference computes them
 // (gpt2_ref.tkv:360-395, the oracle's tvo_attention_causal): scores q.k /
-// sqrt(hd) in binary64, softmax weights with exp in binary64, the P V sum in
-// binary64 and one rounding to binary32, then the exact int8 quantize.
+// sqrt(hd) in binary64, softmax weights with exp in binary64, the P V sum
+// in binary64 and one rounding to binary32, then the exact int8 quantize.
+// The row's other columns are already the reference's (their int8 values
+// were decided by the kernel's error bound) and stay as written.
 //
-// The weights are exp(s_u - c) with c the tensor-core kernel's row max (base-2
+// One 16-warp CTA per listed row (persistent, one CTA per SM, rows taken
+// from a counter).  Four lanes share a key: each holds 16 of q's dimensions
+// in registers (binary64) and reads the matching 64 bytes of the key's K
+// row, so a warp scores eight keys per step (one binary64 exp stream for
+// the eight) with coalesced 16-byte loads, the next step's loads in flight
+// while one step is scored, and two shuffle steps finish each dot product.  The V value of every undecided
+// column (up to FIX_MAXC per pass) is loaded with the key; the weight sum
+// and the column sums stay in registers until one block reduction per row.
+// The weights are exp(s - c) with c the tensor-core kernel's row max (base-2
 // units, times ln 2) instead of the exact max: the context sum(e_u v_u) /
-// sum(e_u) does not depend on c, so the keys split into independent 64-key
-// chunks whose partial sums are added (binary64 reductions) into the row's
-// accumulator; attention_fix_finish_kernel then finishes every row.
-// The sums run in another order than the reference's sequential loops; that
-// moves the binary64 result by about 1e-16 of its size, which changes its
-// binary32 rounding with a probability of about 2^-28 per value.
-//
-// Work item i = (unit entry i / max_chunks, chunk i % max_chunks): the chunk's
-// K and V rows are converted to binary64 in shared memory once (the f32 -> f64
-// conversions bound a row-by-row recomputation), and every undecided row of
-// the unit (one head, one sequence) whose causal range reaches the chunk takes
-// it: a warp task per (row, 32-key half of the chunk), a key per lane for the
-// scores, lane = output column (two of them) for P V.
-constexpr int FIX_THREADS = 256;
-constexpr int FIX_KEYS = 64;
-constexpr uint32_t FIX_SMEM = (FIX_KEYS * (HD + 1) + FIX_KEYS * HD + (FIX_THREADS / 32) * HD) * 8;
-__global__ void __launch_bounds__(FIX_THREADS) attention_fix_kernel(
-    const float* __restrict__ qkv, const int4* __restrict__ rows, const int4* __restrict__ units, const int* fix_n,
-    int ucap, double* __restrict__ facc, int max_chunks, int d) {
+// sum(e_u) does not depend on it.  The sums run in another order than the
+// reference's sequential loops; that moves the binary64 result by about
+// 1e-16 of its size, which changes its binary32 rounding with a probability
+// of about 2^-28 per value.
+constexpr int FIX_THREADS = 512;
+constexpr int FIX_LPK = 4;                 // lanes per key
+constexpr int FIX_KPS = 32 / FIX_LPK;      // keys per warp step
+constexpr int FIX_UNROLL = 1;              // steps per load group (two groups in flight)
+constexpr int FIX_MAXC = 4;                // undecided columns per pass
+__global__ void __launch_bounds__(FIX_THREADS, 1) attention_fix_kernel(const float* __restrict__ qkv,
+                                                                       const int4* __restrict__ rows,
+                                                                       const uint2* __restrict__ masks, int* fix_n,
+                                                                       int cap, int d, float* __restrict__ out,
+                                                                       int8_t* __restrict__ outq,
+                                                                       const float* __restrict__ qscale) {
     griddep_wait();
-    extern __shared__ double fsm[];
-    double* ks = fsm;                        // [FIX_KEYS][HD + 1]
-    double* vs = ks + FIX_KEYS * (HD + 1);   // [FIX_KEYS][HD]
-    double* qsh = vs + FIX_KEYS * HD;        // [warp][HD]
+    constexpr int NW = FIX_THREADS / 32;
+    constexpr int GK = NW * FIX_KPS * FIX_UNROLL;  // keys per load group of the whole block
+    __shared__ double red[NW][1 + FIX_MAXC];
+    __shared__ int next_row;
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    constexpr int DPL = HD / FIX_LPK;  // dimensions per lane
+    const int sub = lane & (FIX_LPK - 1), kq = lane / FIX_LPK;  // dimensions [DPL sub, DPL sub + DPL) of key slot kq
+    const int n = min(*reinterpret_cast<const volatile int*>(fix_n), cap);
     const int64_t rs = 3LL * d;
-    const int nunits = min(*reinterpret_cast<const volatile int*>(fix_n + 1), ucap);
-    const int64_t nitems = static_cast<int64_t>(nunits) * max_chunks;
-    constexpr int LPT = FIX_KEYS * (HD / 4) / FIX_THREADS;  // 16-byte K (and V) loads per thread and item
-    // the K / V loads of an item, issued together (and for the next item while
-    // this one's tasks run); keys past the item's last needed one read as 0
-    auto load_item = [&](int64_t item, float4 (&kr)[LPT], float4 (&vr)[LPT]) {
-        const int4 un = units[item / max_chunks];
-        const int k0 = un.z + static_cast<int>(item % max_chunks) * FIX_KEYS;
-        const int kn = min(FIX_KEYS, un.w + 1 - k0);
-        const float* base = qkv + (un.y >> 8) * HD;
-#pragma unroll
-        for (int t = 0; t < LPT; t++) {
-            const int idx = tid + t * FIX_THREADS, kk = idx / (HD / 4), c4 = idx % (HD / 4);
-            kr[t] = vr[t] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (kk < kn) {
-                const float* rowp = base + static_cast<int64_t>(k0 + kk) * rs + 4 * c4;
-                kr[t] = __ldg(reinterpret_cast<const float4*>(rowp + d));
-                vr[t] = __ldg(reinterpret_cast<const float4*>(rowp + 2 * d));
-            }
-        }
-    };
-    // next item of this CTA that has keys to do
-    auto next_item = [&](int64_t from) -> int64_t {
-        for (int64_t x = from; x < nitems; x += gridDim.x) {
-            const int4 un = units[x / max_chunks];
-            if (un.z + static_cast<int>(x % max_chunks) * FIX_KEYS <= un.w) return x;
-        }
-        return nitems;
-    };
-    float4 kreg[LPT], vreg[LPT];
-    int64_t it = next_item(blockIdx.x);
-    if (it < nitems) load_item(it, kreg, vreg);
-    while (it < nitems) {
-        const int4 un = units[it / max_chunks];
-        const int c = static_cast<int>(it % max_chunks);
-        const int rb = un.x, rn = un.y & 0xFF, head = un.y >> 8, s0 = un.z, qmax = un.w;
-        const int k0 = s0 + c * FIX_KEYS;
-        const int kn = min(FIX_KEYS, qmax + 1 - k0);
-        const float* base = qkv + head * HD;
-        // the chunk's K and V rows as binary64
-#pragma unroll
-        for (int t = 0; t < LPT; t++) {
-            const int idx = tid + t * FIX_THREADS, kk = idx / (HD / 4), c4 = idx % (HD / 4);
-            double* kd = ks + kk * (HD + 1) + 4 * c4;
-            kd[0] = kreg[t].x;
-            kd[1] = kreg[t].y;
-            kd[2] = kreg[t].z;
-            kd[3] = kreg[t].w;
-            double* vd = vs + kk * HD + 4 * c4;
-            vd[0] = vreg[t].x;
-            vd[1] = vreg[t].y;
-            vd[2] = vreg[t].z;
-            vd[3] = vreg[t].w;
-        }
-        const int64_t nx = next_item(it + gridDim.x);
-        if (nx < nitems) load_item(nx, kreg, vreg);  // in flight during this item's tasks
-        __syncthreads();
-        double* qw = qsh + wid * HD;
-        int qrow = -1;  // the row whose q this warp holds in qw
-        // tasks: (row, 32-key half of the chunk), warps round robin
-        for (int tk = wid; tk < 2 * rn; tk += FIX_THREADS / 32) {  // warp-uniform
-            const int ri = tk >> 1, hlf = tk & 1;
-            const int4 rw = rows[rb + ri];
-            const int q = rw.x;
-            if (q < k0) continue;  // this row's causal range ends before the chunk
-            const double off = static_cast<double>(__int_as_float(rw.y)) * 0.69314718055994531;  // base 2 -> natural
-            if (qrow != q) {
-                const float* qr = base + static_cast<int64_t>(q) * rs;
-                __syncwarp();
-                qw[lane] = qr[lane];
-                qw[lane + 32] = qr[lane + 32];
-                __syncwarp();
-                qrow = q;
-            }
-            const int kk = lane + 32 * hlf;
-            const double* kd = ks + kk * (HD + 1);
-            double p0 = 0.0, p1 = 0.0, p2 = 0.0, p3 = 0.0;
-#pragma unroll
-            for (int dd = 0; dd < HD; dd += 4) {
-                p0 = fma(qw[dd], kd[dd], p0);
-                p1 = fma(qw[dd + 1], kd[dd + 1], p1);
-                p2 = fma(qw[dd + 2], kd[dd + 2], p2);
-                p3 = fma(qw[dd + 3], kd[dd + 3], p3);
-            }
-            const double e = (kk < kn && k0 + kk <= q) ? exp(((p0 + p1) + (p2 + p3)) * 0.125 - off) : 0.0;  // 1/sqrt(64)
-            double l = e;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-            double a0 = 0.0, a1 = 0.0, b0 = 0.0, b1 = 0.0;
-            const double* vh = vs + 32 * hlf * HD;
-#pragma unroll
-            for (int t = 0; t < 32; t += 2) {
-                const double pw = __shfl_sync(0xffffffffu, e, t);
-                const double pv = __shfl_sync(0xffffffffu, e, t + 1);
-                a0 = fma(pw, vh[t * HD + lane], a0);
-                a1 = fma(pw, vh[t * HD + lane + 32], a1);
-                b0 = fma(pv, vh[(t + 1) * HD + lane], b0);
-                b1 = fma(pv, vh[(t + 1) * HD + lane + 32], b1);
-            }
-            a0 += b0;
-            a1 += b1;
-            double* ea = facc + static_cast<int64_t>(rb + ri) * kAttnFixAccWords;  // [0, 64) sums, 64 weights
-            atomicAdd(ea + lane, a0);  // no result used: reductions, ordered by the kernel's end
-            atomicAdd(ea + lane + 32, a1);
-            if (lane == 0) atomicAdd(ea + HD, l);
-        }
-        __syncthreads();  // ks / vs are rewritten by the next item
-        it = nx;
-    }
-}
-
-// The undecided rows' contexts from their accumulators (every chunk added by
-// attention_fix_kernel, which ended before this kernel starts): one warp per
-// row, two columns per lane, then the exact int8 quantize; the accumulators
-// go back to zero, and the last CTA resets the lists for the next launch.
-__global__ void __launch_bounds__(256) attention_fix_finish_kernel(const int4* __restrict__ rows, int* fix_n, int cap,
-                                                                   double* __restrict__ facc, int d,
-                                                                   float* __restrict__ out, int8_t* __restrict__ outq,
-                                                                   const float* __restrict__ qscale) {
-    griddep_wait();
-    const int lane = threadIdx.x & 31;
-    const int n = min(*reinterpret_cast<volatile int*>(fix_n), cap);
     const InvScale qs = make_inv_scale(static_cast<double>(__ldg(qscale)));
-    const int warps = static_cast<int>(gridDim.x) * (blockDim.x >> 5);
-    for (int ri = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); ri < n; ri += warps) {
+    // rows are taken from a counter (fix_n[1]) as CTAs become free: their key
+    // counts range from 1 to the sequence length
+    while (true) {
+        __syncthreads();  // next_row and red[] are free
+        if (tid == 0) next_row = atomicAdd(fix_n + 1, 1);
+        __syncthreads();
+        const int ri = next_row;
+        if (ri >= n) break;
         const int4 rw = rows[ri];
-        double* ea = facc + static_cast<int64_t>(ri) * kAttnFixAccWords;
-        const double inv = 1.0 / ea[HD];
+        const uint2 mk = masks[ri];
+        const int q = rw.x, head = rw.z, s0 = rw.w;
+        const double off = static_cast<double>(__int_as_float(rw.y)) * 0.69314718055994531;  // base 2 -> natural
+        const float* base = qkv + head * HD;
+        double qv[DPL];
+        {
+            const float4* qr = reinterpret_cast<const float4*>(base + static_cast<int64_t>(q) * rs + DPL * sub);
 #pragma unroll
-        for (int h2 = 0; h2 < 2; h2++) {
-            const int col = lane + 32 * h2;
-            const float cx = __double2float_rn(ea[col] * inv);
-            const int64_t o = static_cast<int64_t>(rw.x) * d + rw.z * HD + col;
-            if (out) out[o] = cx;
-            if (outq) outq[o] = quant_exact(cx, qs);
+            for (int t = 0; t < DPL / 4; t++) {
+                const float4 a = __ldg(qr + t);
+                qv[4 * t] = a.x;
+                qv[4 * t + 1] = a.y;
+                qv[4 * t + 2] = a.z;
+                qv[4 * t + 3] = a.w;
+            }
         }
-        __syncwarp();
-        ea[lane] = 0.0;
-        ea[lane + 32] = 0.0;
-        if (lane == 0) ea[HD] = 0.0;
+        uint32_t m0 = mk.x, m1 = mk.y;
+        while (m0 | m1) {  // block-uniform: passes of up to FIX_MAXC undecided columns
+            int col[FIX_MAXC], nc = 0;
+#pragma unroll
+            for (int t = 0; t < FIX_MAXC; t++) {
+                col[t] = 0;
+                if (m0) {
+                    col[t] = __ffs(m0) - 1;
+                    m0 &= m0 - 1u;
+                    nc = t + 1;
+                } else if (m1) {
+                    col[t] = 32 + __ffs(m1) - 1;
+                    m1 &= m1 - 1u;
+                    nc = t + 1;
+                }
+            }
+            double l = 0.0, acc[FIX_MAXC];
+#pragma unroll
+            for (int t = 0; t < FIX_MAXC; t++) acc[t] = 0.0;
+            // group g, step u of this warp: keys s0 + g GK + (u NW + wid) FIX_KPS + kq
+            struct Group {
+                float4 k[FIX_UNROLL][DPL / 4];
+                float v[FIX_UNROLL][FIX_MAXC];
+            };
+            auto key_of = [&](int g, int u) { return s0 + g * GK + (u * NW + wid) * FIX_KPS + kq; };
+            auto load = [&](int g, Group& G) {
+#pragma unroll
+                for (int u = 0; u < FIX_UNROLL; u++) {
+                    const int j = key_of(g, u);
+#pragma unroll
+                    for (int t = 0; t < DPL / 4; t++) G.k[u][t] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+                    for (int t = 0; t < FIX_MAXC; t++) G.v[u][t] = 0.0f;
+                    if (j <= q) {
+                        const float* kj = base + static_cast<int64_t>(j) * rs;
+                        const float4* kp = reinterpret_cast<const float4*>(kj + d + DPL * sub);
+#pragma unroll
+                        for (int t = 0; t < DPL / 4; t++) G.k[u][t] = __ldg(kp + t);
+                        if (sub == 0) {
+#pragma unroll
+                            for (int t = 0; t < FIX_MAXC; t++)
+                                if (t < nc) G.v[u][t] = __ldg(kj + 2 * d + col[t]);
+                        }
+                    }
+                }
+            };
+            auto score = [&](int g, const Group& G) {
+#pragma unroll
+                for (int u = 0; u < FIX_UNROLL; u++) {
+                    double p0 = 0.0, p1 = 0.0;
+#pragma unroll
+                    for (int t = 0; t < DPL / 4; t++) {
+                        p0 = fma(qv[4 * t], static_cast<double>(G.k[u][t].x), p0);
+                        p1 = fma(qv[4 * t + 1], static_cast<double>(G.k[u][t].y), p1);
+                        p0 = fma(qv[4 * t + 2], static_cast<double>(G.k[u][t].z), p0);
+                        p1 = fma(qv[4 * t + 3], static_cast<double>(G.k[u][t].w), p1);
+                    }
+                    double sdot = p0 + p1;
+#pragma unroll
+                    for (int o = 1; o < FIX_LPK; o <<= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, o);
+                    if (key_of(g, u) <= q && sub == 0) {
+                        const double e = exp(sdot * 0.125 - off);  // 1/sqrt(64)
+                        l += e;
+#pragma unroll
+                        for (int t = 0; t < FIX_MAXC; t++) acc[t] = fma(e, static_cast<double>(G.v[u][t]), acc[t]);
+                    }
+                }
+            };
+            // two groups in flight: the next group's loads are issued before
+            // this group is scored (the loop is unrolled twice so that both
+            // register buffers stay statically indexed)
+            const int ng = (q - s0) / GK + 1;  // groups holding keys [s0, q]
+            Group G0, G1;
+            load(0, G0);
+            for (int g = 0; g < ng; g += 2) {
+                if (g + 1 < ng) load(g + 1, G1);
+                score(g, G0);
+                if (g + 1 >= ng) break;
+                if (g + 2 < ng) load(g + 2, G0);
+                score(g + 1, G1);
+            }
+            // the block's sums (lanes other than sub == 0 hold zeros)
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                l += __shfl_xor_sync(0xffffffffu, l, o);
+#pragma unroll
+                for (int t = 0; t < FIX_MAXC; t++) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+            }
+            __syncthreads();  // red[] is free
+            if (lane == 0) {
+                red[wid][0] = l;
+#pragma unroll
+                for (int t = 0; t < FIX_MAXC; t++) red[wid][1 + t] = acc[t];
+            }
+            __syncthreads();
+            if (tid < nc) {
+                double lt = 0.0, at = 0.0;
+#pragma unroll
+                for (int w = 0; w < NW; w++) {
+                    lt += red[w][0];
+                    at += red[w][1 + tid];
+                }
+                const float cx = __double2float_rn(at * (1.0 / lt));
+                const int64_t o = static_cast<int64_t>(q) * d + head * HD + col[tid];
+                if (out) out[o] = cx;
+                outq[o] = quant_exact(cx, qs);
+            }
+        }
     }
+    // the last CTA to finish resets the list for the next launch
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
         __threadfence();
         if (atomicAdd(fix_n + 2, 1) == static_cast<int>(gridDim.x) - 1) {
             fix_n[0] = 0;
@@ -1047,6 +1057,10 @@ __global__ void __launch_bounds__(256) attention_fix_finish_kernel(const int4* _
     }
 }
 
+// Per-head bounds of a c_attn layer's Q, K and V outputs for the epilogue's
+// fp16 split (kv_head_exp): block (h, part) over the 64 output columns n of
+// head h in part (0 Q, 1 K, 2 V): A = max sw[n] * 127 * sum_k |W[n,k]|, B =
+// max |bias[n]|, both rounded up.  out [6 heads]: A_Q, B_Q, A_K, B_K, A_V, B_V.
 __global__ void kv_head_bound_kernel(const int8_t* __restrict__ W, const float* __restrict__ sw,
                                      const float* __restrict__ bias, int k, int kvd, float* __restrict__ out) {
     const int h = blockIdx.x, part = blockIdx.y, heads = gridDim.x;
@@ -1084,7 +1098,7 @@ int attention_tc_rows() { return TQ; }
 int attention_tc_pitch(int T) { return (T + 7) & ~7; }
 
 int launch_split_kv(const float* qkv, int T, int d, void* qh, void* ql, void* kh, void* kl, void* vth, void* vtl,
-                    int* kv_exp, uint32_t* amax, cudaStream_t st) {
+                    int* kv_exp, uint32_t* amax, cudaStream_t st, uint32_t* vcol) {
     if (T <= 0) return TVQ_OK;
     TVQ_CHECK(d % HD == 0, TVQ_ERR_UNSUPPORTED, "d must be a multiple of 64");
     int rc = 0;
@@ -1093,6 +1107,10 @@ int launch_split_kv(const float* qkv, int T, int d, void* qh, void* ql, void* kh
     const int heads = d / HD;
     TVQ_CUDA(cudaMemsetAsync(amax, 0, sizeof(uint32_t) * 3 * heads, st));
     int r = launch_pdl(kv_head_amax_kernel, dim3(std::min(T, 64), 3, heads), dim3(64), 0, st, qkv, T, d, amax);
+    if (!r && vcol) {
+        TVQ_CUDA(cudaMemsetAsync(vcol, 0, sizeof(uint32_t) * d, st));
+        r = launch_pdl(v_col_amax_kernel, dim3(heads, std::min(T, 64)), dim3(HD), 0, st, qkv, T, d, vcol);
+    }
     if (!r) r = launch_pdl(kv_exp_from_amax_kernel, dim3((3 * heads + 127) / 128), dim3(128), 0, st,
                            static_cast<const uint32_t*>(amax), 3 * heads, kv_exp);
     if (r) return r;
@@ -1167,33 +1185,23 @@ int launch_attention_tc(const float* qkv, const void* qh, const void* ql, const 
     p.kv_exp = kv_exp;
     p.nunits = nitems * nheads;
     const bool fixing = fix && outq;
-    TVQ_CHECK(!fixing || (fix->vmax && fix->list && fix->units && fix->n && fix->cap > 0 && fix->ucap > 0 &&
-                          fix->acc && fix->max_keys > 0),
-              TVQ_ERR_INVALID, "the exact int8 context needs the head maxima, the fix-up lists and accumulators");
+    TVQ_CHECK(!fixing || (fix->vmax && fix->list && fix->mask && fix->n && fix->cap > 0),
+              TVQ_ERR_INVALID, "the exact int8 context needs the head maxima and the fix-up lists");
     p.vmax = fixing ? fix->vmax : nullptr;
     p.fix = fixing ? fix->list : nullptr;
+    p.fix_mask = fixing ? fix->mask : nullptr;
     p.fix_n = fixing ? fix->n : nullptr;
     p.fix_cap = fixing ? fix->cap : 0;
-    p.fix_units = fixing ? fix->units : nullptr;
-    p.fix_ucap = fixing ? fix->ucap : 0;
     // persistent: one CTA per SM (all of TMEM) working through the units;
     // key-chunk partials are merged inside the kernel by the last CTA of each set
     const int grid = std::min(p.nunits, ds->sm_count);
     rc = launch_pdl(attention_tc_kernel, dim3(grid), dim3(NTHREADS), SMEM_BYTES, st, mqh, mql, mkh, mkl, mvh, mvl, p);
     if (rc || !fixing) return rc;
-    static bool fattr[64] = {false};
-    if (dev < 64 && !fattr[dev]) {
-        TVQ_CUDA(cudaFuncSetAttribute(attention_fix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(FIX_SMEM)));
-        fattr[dev] = true;
-    }
-    const int max_chunks = (fix->max_keys + FIX_KEYS - 1) / FIX_KEYS;
-    rc = launch_pdl(attention_fix_kernel, dim3(3 * ds->sm_count), dim3(FIX_THREADS), FIX_SMEM, st, qkv,
-                    static_cast<const int4*>(fix->list), static_cast<const int4*>(fix->units),
-                    static_cast<const int*>(fix->n), fix->ucap, fix->acc, max_chunks, d);
-    if (rc) return rc;
-    return launch_pdl(attention_fix_finish_kernel, dim3(2 * ds->sm_count), dim3(256), 0, st,
-                      static_cast<const int4*>(fix->list), fix->n, fix->cap, fix->acc, d, out, outq, qscale);
+    // the listed rows' undecided columns (the list length is known on the
+    // device only: a persistent grid of a few CTAs per SM)
+    return launch_pdl(attention_fix_kernel, dim3(ds->sm_count), dim3(FIX_THREADS), 0, st, qkv,
+                      static_cast<const int4*>(fix->list), static_cast<const uint2*>(fix->mask), fix->n, fix->cap, d,
+                      out, outq, qscale);
 }
 
 }  // namespace tvq

@@ -50,6 +50,7 @@ enum : int {
     DEVERR_TIMEOUT_MMA = 2,
     DEVERR_TIMEOUT_EPILOGUE = 3,
     DEVERR_TIMEOUT_DRAIN = 4,
+    DEVERR_TIMEOUT_ROWS = 5,  // a row copy of the per-channel quantizer
     DEVERR_TIMEOUT_TEST = 9,
     DEVERR_BAD_INDEX = 60,  // an index operand out of range (not a timeout)
     DEVERR_FIX_FULL = 61,   // more undecided int8 attention rows than the fix-up lists hold
@@ -186,6 +187,15 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, in
 // The same with the library's limit, TVQ_WAIT_LIMIT_NS.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
     return mbar_wait_for(bar, parity, err, code, TVQ_WAIT_LIMIT_NS);
+}
+
+// 1-D bulk copy global -> shared (dst, src 16-byte aligned, bytes a
+// multiple of 16), completing bytes on `bar`.  No cluster multicast.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
 }
 
 // 2-D TMA tile load global -> shared, completing bytes on `bar`.

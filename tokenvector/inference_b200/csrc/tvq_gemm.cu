@@ -112,7 +112,7 @@ struct KParams {
     int kvd, vt_pitch;
     int* kv_exp;
     const float* kv_bound;
-    uint32_t* kv_vmax;  // per head max |V| (float bits) or null
+    uint32_t* kv_vmax;  // per V column max |V| (float bits) or null
 };
 
 // hi / lo fp16 pair of two scaled values, packed two per 32-bit word
@@ -126,13 +126,26 @@ __device__ __forceinline__ void split_h2_pair(float a, float b, uint32_t& hi, ui
 }
 
 __device__ __forceinline__ float gelu_tanh_f32(float x) {
-    // apply_activation GELU, tv/optimization/kernels.tkv:22-24 + _tanh :32-38
-    const float t = 0.79788456f * (x + 0.044715f * x * x * x);
+    // apply_activation GELU, tv/optimization/kernels.tkv:22-24 + _tanh
+    // :32-38, in the reference's numeric model: untyped locals and literals
+    // in binary64, binary32 only where a value passes an f32 parameter or
+    // return (_tanh's argument and result, apply_activation's result).  The
+    // exponential is CUDA's binary64 exp: the f32 results agree with a host
+    // libm's except where the binary64 quotient lies within an ulp of an f32
+    // rounding boundary.
+    const double xd = x;
+    const double x3 = xd * xd * xd;
+    const float targ = __double2float_rn(0.79788456 * (xd + 0.044715 * x3));
     float th;
-    if (t > 10.0f) th = 1.0f;
-    else if (t < -10.0f) th = -1.0f;
-    else { const float e = expf(2.0f * t); th = (e - 1.0f) / (e + 1.0f); }
-    return 0.5f * x * (1.0f + th);
+    if (static_cast<double>(targ) > 10.0) {
+        th = 1.0f;
+    } else if (static_cast<double>(targ) < -10.0) {
+        th = -1.0f;
+    } else {
+        const double e = exp(2.0 * static_cast<double>(targ));
+        th = __double2float_rn((e - 1.0) / (e + 1.0));
+    }
+    return __double2float_rn(0.5 * xd * (1.0 + static_cast<double>(th)));
 }
 
 __device__ __forceinline__ float gelu_erf_f32(float v) {
@@ -853,15 +866,30 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
                             p.vtl[vo + static_cast<int64_t>(j) * p.vt_pitch] = __float2half_rn(__fsub_rn(v, __half2float(h)));
                         }
                     }
-                    if (part == 2 && p.kv_vmax) {  // the head's max |V| (warp-uniform branch)
-                        float vm = 0.0f;
-                        if (row0 + lane < p.m) {
+                    if (part == 2 && p.kv_vmax) {  // each V column's max |V| (warp-uniform branch)
+                        static_assert(E::CH == 8, "the column exchange below assumes 8-column chunks");
+                        // max over the warp's 32 rows of each of the 8 columns: three
+                        // rounds that each keep half the columns (lane bits 16, 8, 4
+                        // pick them), then the last two lane bits
+                        float v[8];
 #pragma unroll
-                            for (int j = 0; j < E::CH; j++) vm = fmaxf(vm, fabsf(y[j]));
+                        for (int j = 0; j < 8; j++) v[j] = (row0 + lane < p.m) ? fabsf(y[j]) : 0.0f;
+#pragma unroll
+                        for (int rd = 0, half_n = 4; rd < 3; rd++, half_n >>= 1) {
+                            const bool hi_half = (lane >> (4 - rd)) & 1;
+#pragma unroll
+                            for (int i = 0; i < 4; i++) {
+                                if (i < half_n) {
+                                    const float keep = hi_half ? v[i + half_n] : v[i];
+                                    const float send = hi_half ? v[i] : v[i + half_n];
+                                    v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 16 >> rd));
+                                }
+                            }
                         }
-#pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, o));
-                        if (lane == 0) atomicMax(p.kv_vmax + hh, __float_as_uint(vm));
+                        float vm = fmaxf(v[0], __shfl_xor_sync(0xffffffffu, v[0], 2));
+                        vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, 1));
+                        const int cj = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+                        if ((lane & 3) == 0) atomicMax(p.kv_vmax + (n0 - 2 * p.kvd) + cj, __float_as_uint(vm));
                     }
                 }
                 if (p.act == TVQ_ACT_GELU_ERF) {
@@ -965,7 +993,7 @@ int get_encoder() {
 
 // 2-D K-major operand [rows, k] of 1-, 2- or 4-byte elements: box {128
 // bytes of K, box_rows}, 128-byte swizzle.
-int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box_rows, int elem, int64_t pitch = 0) {
+int encode_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box_rows, int elem, int64_t pitch) {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch ? pitch : k) * elem};
     const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK / elem), static_cast<cuuint32_t>(box_rows)};
@@ -981,6 +1009,53 @@ int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box
         set_error(TVQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) + ")");
         return TVQ_ERR_CUDA;
     }
+    return TVQ_OK;
+}
+
+// Tensor maps by value: a map holds only the address, shape, pitch and box
+// it was encoded from, so a cached one stays valid for any later buffer at
+// the same address with the same shape (nothing to invalidate when memory
+// is freed).  Repeated calls on the same operands -- weights every call,
+// activations of a fixed-shape step -- skip cuTensorMapEncodeTiled.  A
+// small direct-mapped table, guarded by a mutex (host threads may launch
+// concurrently).
+struct MapKey {
+    const void* ptr;
+    int64_t rows, k, pitch;
+    int box_rows, elem;
+    bool operator==(const MapKey& o) const {
+        return ptr == o.ptr && rows == o.rows && k == o.k && pitch == o.pitch && box_rows == o.box_rows &&
+               elem == o.elem;
+    }
+};
+constexpr int kMapCacheSlots = 512;
+struct MapCache {
+    std::mutex mu;
+    MapKey key[kMapCacheSlots];
+    CUtensorMap map[kMapCacheSlots];
+    bool used[kMapCacheSlots] = {};
+};
+
+int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box_rows, int elem, int64_t pitch = 0) {
+    static MapCache cache;
+    const MapKey key{ptr, rows, k, pitch, box_rows, elem};
+    uint64_t h = reinterpret_cast<uintptr_t>(ptr) * 0x9E3779B97F4A7C15ull;
+    h ^= static_cast<uint64_t>(rows) * 0xC2B2AE3D27D4EB4Full + static_cast<uint64_t>(k) * 0x165667B19E3779F9ull;
+    h ^= static_cast<uint64_t>(pitch * 131 + box_rows * 7 + elem);
+    const int slot = static_cast<int>((h >> 32) % kMapCacheSlots);
+    {
+        std::lock_guard<std::mutex> lk(cache.mu);
+        if (cache.used[slot] && cache.key[slot] == key) {
+            *map = cache.map[slot];
+            return TVQ_OK;
+        }
+    }
+    const int rc = encode_map(map, ptr, rows, k, box_rows, elem, pitch);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(cache.mu);
+    cache.key[slot] = key;
+    cache.map[slot] = *map;
+    cache.used[slot] = true;
     return TVQ_OK;
 }
 

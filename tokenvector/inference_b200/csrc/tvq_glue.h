@@ -32,37 +32,32 @@ int launch_attention_combine(const int4* comb, int ncomb, int d, int nheads, int
 // attention_tc_pitch(T)], head h of part p (0 Q, 1 K, 2 V) scaled by
 // 2^kv_exp[p heads + h] so that its values stay below 2^15: written by the
 // c_attn GEMM epilogue in a session, or by launch_split_kv (exact per-head
-// max |.| into amax[3 heads], then the split).  launch_attention_tc takes
+// max |.| into amax[3 heads], optionally each V column's max |V| into
+// vcol[d], then the split).  launch_attention_tc takes
 // them with the same work items as above but attention_tc_rows() (128) query
 // rows per tile; split[] is required.
 int attention_tc_rows();
 int attention_tc_pitch(int T);
 int launch_split_kv(const float* qkv, int T, int d, void* qh, void* ql, void* kh, void* kl, void* vth, void* vtl,
-                    int* kv_exp, uint32_t* amax, cudaStream_t st);
+                    int* kv_exp, uint32_t* amax, cudaStream_t st, uint32_t* vcol = nullptr);
 // Per-head bounds [6 d / 64] of a c_attn layer (W int8 [3d, k], per-channel
 // sw, bias or null) for the epilogue's Q / K / V split (GemmArgs::kv_bound).
 int launch_kv_head_bound(const int8_t* W, const float* sw, const float* bias, int k, int kvd, float* out,
                          cudaStream_t st);
-// Exact int8 context (optional, with outq): vmax [nheads] = max |V| per head
-// (float bits); list [cap] rows to recompute (one per undecided row), units
-// [ucap] one per attention unit with such rows; n: three device ints (rows,
-// units, finished fix-up CTAs); acc [cap][kAttnFixAccWords] binary64 row
-// accumulators (context sums, weight sum, a count); n and acc zero before the
-// first launch (the fix-up kernel leaves them zero); max_keys = the longest
-// sequence.  The fix-up reads the f32 qkv, so qkv must hold the values.  A
-// launch with more undecided rows than cap records a device error.
+// Exact int8 context (optional, with outq): vmax [d] = max |V| per V column
+// (float bits); list [cap] rows whose int8 context has undecided columns
+// {q, row max, head, sequence start}, mask [cap] those columns; n: three
+// device ints (rows, rows taken, finished fix-up CTAs), zero before the first
+// launch (the fix-up kernel leaves them zero).  The fix-up reads the f32
+// qkv, so qkv must hold the values.  A launch with more undecided rows than
+// cap records a device error (DEVERR_FIX_FULL).
 struct AttnFix {
     const uint32_t* vmax = nullptr;
     int4* list = nullptr;
-    int4* units = nullptr;
+    uint2* mask = nullptr;
     int* n = nullptr;
-    double* acc = nullptr;
     int cap = 0;
-    int ucap = 0;
-    int max_keys = 0;
 };
-// binary64 words per accumulator row of AttnFix::acc
-constexpr int kAttnFixAccWords = 66;
 int launch_attention_tc(const float* qkv, const void* qh, const void* ql, const void* kh, const void* kl,
                         const void* vth, const void* vtl, const int* kv_exp, int T, const int4* tiles,
                         const int4* split, int nitems, const int4* comb, int ncomb, int d, int nheads, float* out,

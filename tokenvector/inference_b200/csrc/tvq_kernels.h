@@ -73,8 +73,8 @@ struct GemmArgs {
     int kvd = 0, vt_pitch = 0;
     int* kv_exp = nullptr;
     const float* kv_bound = nullptr;
-    // with the operand split: max |V| of each head (float bits, atomicMax;
-    // zeroed by the caller), the attention's exact-int8 error bound
+    // with the operand split: max |V| of each V column [kvd] (float bits,
+    // atomicMax; zeroed by the caller), the attention's exact-int8 error bound
     uint32_t* kv_vmax = nullptr;
     // GEMM_I8, per-tensor scales: zero points (matmul_int8_asymmetric).
     // zp_rows [m] = sum_k A[m, k], zp_cols [n] = sum_k W[n, k] (int32, any k

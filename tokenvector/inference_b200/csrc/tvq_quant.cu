@@ -393,60 +393,122 @@ __global__ void rowwise_kernel(const float* __restrict__ x, int8_t* __restrict__
     }
 }
 
-// Modes 0 and 2 for rows of 1025 .. 8192 floats: one 256-thread block per
-// row with the row held in registers (NV float4 per thread), so the row is
-// read from HBM once.  (The warp-per-row form reads it twice: with ~10k rows
-// in flight its second pass misses L2 once rows exceed a few KB -- 358 MB
-// read for a 210 MB [8192, 6400] tensor.)  Same scale and quantize
-// arithmetic as rowwise_kernel; needs 16-byte aligned rows.
-template <int MODE, int NV>
-__global__ void __launch_bounds__(256) rowwise_block_kernel(const float* __restrict__ x, int8_t* __restrict__ q,
-                                                            float* __restrict__ scales, int64_t rows, int64_t cols) {
-    __shared__ float red[8];
+// Modes 0 and 2 for rows of 1025 .. 8192 floats (cols % 4 == 0, 16-byte
+// aligned rows): a 512-thread block takes its rows one at a time, and the
+// rows stream into a ring of `ns` (3 or 4) shared-memory slots by 1-D bulk
+// copies (the TMA engine; warp 0 issues up to 8 KB per lane, completion on
+// the slot's mbarrier), so HBM never waits for the arithmetic and each
+// element is read once.  The steps of consecutive rows overlap: while all
+// warps quantize row i with its scale, the block has already reduced row
+// i + 1's max |x| and warp 0 forms row i + 1's scale (two binary64
+// divisions) -- no warp waits for that serial step.  Same scale and
+// quantize arithmetic as rowwise_kernel.  Every wait is bounded
+// (DEVERR_TIMEOUT_ROWS).
+constexpr int ROW_THREADS = 512;      // two blocks per SM: 32 warps
+constexpr uint32_t ROW_CHUNK = 8192;  // bytes per bulk copy
+constexpr int ROW_MAX_SLOTS = 4;
+
+template <int MODE>
+__global__ void __launch_bounds__(ROW_THREADS, 2) rowwise_pipe_kernel(const float* __restrict__ x, int8_t* __restrict__ q,
+                                                                      float* __restrict__ scales, int64_t rows,
+                                                                      int64_t cols, int ns, int* err) {
+    extern __shared__ __align__(128) float4 rbuf[];  // [ns][cols / 4]
+    __shared__ float red[ROW_THREADS / 32];
+    __shared__ InvScale row_qs[2];  // by row parity
+    __shared__ __align__(8) uint64_t full[ROW_MAX_SLOTS];
     const int tid = threadIdx.x;
-    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
-        const float* xr = x + r * cols;
-        int8_t* qr = q + r * cols;
-        float4 v[NV];
+    const int n4 = static_cast<int>(cols / 4);
+    const uint32_t row_bytes = static_cast<uint32_t>(cols) * 4u;
+    const int64_t step = gridDim.x;
+    if (tid == 0) {
+        for (int s = 0; s < ns; s++) mbar_init(&full[s], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    // row r into ring slot `slot` (every thread is done reading the slot's
+    // previous row: a block barrier separates those reads from this call)
+    auto issue = [&](int64_t r, int slot) {
+        if (r >= rows || tid >= 32) return;
+        if (tid == 0) {
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(&full[slot], row_bytes);
+        }
+        __syncwarp();
+        const uint32_t off = static_cast<uint32_t>(tid) * ROW_CHUNK;
+        if (off < row_bytes)
+            bulk_load(reinterpret_cast<char*>(rbuf + static_cast<int64_t>(slot) * n4) + off,
+                      reinterpret_cast<const char*>(x + r * cols) + off, min(ROW_CHUNK, row_bytes - off), &full[slot]);
+    };
+    // this thread's part of row j's max |x|, then the warp's, into red[]
+    auto amax_part = [&](int j) {
+        const float4* row = rbuf + static_cast<int64_t>(j % ns) * n4;
         float am = 0.0f;
-#pragma unroll
-        for (int i = 0; i < NV; i++) {
-            const int64_t c = (static_cast<int64_t>(i) * 256 + tid) * 4;
-            v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (c < cols) v[i] = __ldcs(reinterpret_cast<const float4*>(xr + c));
-            am = fmaxf(am, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+        for (int c = tid; c < n4; c += ROW_THREADS) {
+            const float4 v = row[c];
+            am = fmaxf(am, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
         }
         am = warp_max(am);
         if ((tid & 31) == 0) red[tid >> 5] = am;
-        __syncthreads();
-#pragma unroll
-        for (int w = 0; w < 8; w++) am = fmaxf(am, red[w]);
+    };
+    // warp 0, after the block barrier that follows amax_part(j): row j's
+    // scale (stored) and 1/scale (for the quantize of row j)
+    auto row_scale = [&](int j, int64_t rj) {
+        const float am = warp_max(tid < ROW_THREADS / 32 ? red[tid] : 0.0f);
+        if (tid != 0) return;
         double amd = am;
-        InvScale qs;
         if (amd < 0.00000001) amd = 0.00000001;
         if (MODE == 0) {
-            const bool poisoned = (__ldg(xr) != __ldg(xr));  // NaN first element poisons min/max
+            const float x0 = reinterpret_cast<const float*>(rbuf + static_cast<int64_t>(j % ns) * n4)[0];
+            const bool poisoned = (x0 != x0);  // NaN first element poisons min/max
             const float sc = poisoned ? __int_as_float(0x7FC00000) : __double2float_rn(amd / 127.0);
-            if (tid == 0) scales[r] = sc;
-            qs = make_inv_scale(static_cast<double>(sc));
+            scales[rj] = sc;
+            row_qs[j & 1] = make_inv_scale(static_cast<double>(sc));
         } else {
             const double sc = amd / 127.0;
-            if (tid == 0) scales[r] = __double2float_rn(sc);
-            qs = make_inv_from_inv(1.0 / sc);
+            scales[rj] = __double2float_rn(sc);
+            row_qs[j & 1] = make_inv_from_inv(1.0 / sc);
         }
-#pragma unroll
-        for (int i = 0; i < NV; i++) {
-            const int64_t c = (static_cast<int64_t>(i) * 256 + tid) * 4;
-            if (c < cols) {
+    };
+    int64_t r = blockIdx.x;
+    if (r >= rows) return;
+    for (int s = 0; s < ns - 1; s++) issue(r + s * step, s);
+    {  // row 0 of this block: its scale before the loop
+        const bool ok = mbar_wait(&full[0], 0u, err, DEVERR_TIMEOUT_ROWS);
+        if (!__syncthreads_and(ok)) return;  // the error word holds the cause
+        amax_part(0);
+        __syncthreads();
+        if (tid < 32) row_scale(0, r);
+    }
+    for (int i = 0; r < rows; i++, r += step) {
+        const int64_t rn = r + step;  // row i + 1 (block-uniform)
+        bool ok = true;
+        if (rn < rows) ok = mbar_wait(&full[(i + 1) % ns], static_cast<uint32_t>((i + 1) / ns) & 1u, err,
+                                      DEVERR_TIMEOUT_ROWS);
+        // every thread is past row i - 1 (its slot is free) and row i's scale is published
+        if (!__syncthreads_and(ok)) return;
+        issue(r + (ns - 1) * step, (i + ns - 1) % ns);
+        if (rn < rows) amax_part(i + 1);
+        __syncthreads();
+        if (rn < rows && tid < 32) row_scale(i + 1, rn);
+        const InvScale qs = row_qs[i & 1];
+        const float4* row = rbuf + static_cast<int64_t>(i % ns) * n4;
+        uint32_t* qr = reinterpret_cast<uint32_t*>(q + r * cols);
+        for (int c = tid; c < n4; c += ROW_THREADS) {
+            const float4 v = row[c];
+            float t0, t1, t2, t3;
+            const bool fast = quant_fast_t(v.x, qs.hi, t0) & quant_fast_t(v.y, qs.hi, t1) &
+                              quant_fast_t(v.z, qs.hi, t2) & quant_fast_t(v.w, qs.hi, t3);
+            uint32_t w = pack_q4(t0, t1, t2, t3);
+            if (!fast) {  // rare: the binary64 expression decides
                 char4 o;
-                o.x = quant_exact(v[i].x, qs);
-                o.y = quant_exact(v[i].y, qs);
-                o.z = quant_exact(v[i].z, qs);
-                o.w = quant_exact(v[i].w, qs);
-                *reinterpret_cast<char4*>(qr + c) = o;
+                o.x = quant_exact(v.x, qs);
+                o.y = quant_exact(v.y, qs);
+                o.z = quant_exact(v.z, qs);
+                o.w = quant_exact(v.w, qs);
+                w = *reinterpret_cast<const uint32_t*>(&o);
             }
+            qr[c] = w;
         }
-        __syncthreads();  // red[] is rewritten for the next row
     }
 }
 
@@ -457,14 +519,26 @@ int launch_rowwise(int mode, const float* x, int8_t* q, float* scales, int64_t r
     const bool vec = (cols % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(q) & 3) == 0);
     if (mode != 1 && vec && cols > 1024 && cols <= 8192) {
-        const int g = grid_for(rows * threads, threads, 8);
-#define TVQ_ROWB(M, NV) rowwise_block_kernel<M, NV><<<g, threads, 0, st>>>(x, q, scales, rows, cols)
-        if (mode == 0) {
-            if (cols <= 2048) TVQ_ROWB(0, 2); else if (cols <= 4096) TVQ_ROWB(0, 4); else TVQ_ROWB(0, 8);
-        } else {
-            if (cols <= 2048) TVQ_ROWB(2, 2); else if (cols <= 4096) TVQ_ROWB(2, 4); else TVQ_ROWB(2, 8);
+        // four ring slots while two blocks still fit an SM (227 KB), else three
+        const size_t row_b = static_cast<size_t>(cols) * 4;
+        const int ns = (2 * (4 * row_b + 2048) <= 227 * 1024) ? 4 : 3;
+        const size_t smem = static_cast<size_t>(ns) * row_b;
+        // the ring: at most 4 slots of 7136 floats (114 KB) or 3 of 8192 (96 KB)
+        constexpr int kRingMax = 114 * 1024 + 1024;
+        static int attr_done[64] = {0};  // per device
+        int dev = 0;
+        TVQ_CUDA(cudaGetDevice(&dev));
+        if (dev < 64 && !attr_done[dev]) {
+            TVQ_CUDA(cudaFuncSetAttribute(rowwise_pipe_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRingMax));
+            TVQ_CUDA(cudaFuncSetAttribute(rowwise_pipe_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRingMax));
+            attr_done[dev] = 1;
         }
-#undef TVQ_ROWB
+        int rc = 0;
+        DeviceState* ds = device_state(&rc);
+        if (!ds) return rc;
+        const int g = grid_for(rows * ROW_THREADS, ROW_THREADS, 2);
+        if (mode == 0) rowwise_pipe_kernel<0><<<g, ROW_THREADS, smem, st>>>(x, q, scales, rows, cols, ns, ds->d_error);
+        else rowwise_pipe_kernel<2><<<g, ROW_THREADS, smem, st>>>(x, q, scales, rows, cols, ns, ds->d_error);
         TVQ_CUDA(cudaGetLastError());
         return TVQ_OK;
     }
@@ -513,8 +587,28 @@ __device__ __forceinline__ float mul_round_f64(float x, const InvScale& s) {
     return __double2float_rn(__dmul_rn(static_cast<double>(x), s.d));
 }
 
+// The reference's E4M3 byte.  Away from its departures from OCP E4M3 the
+// reference encoder rounds the exact value to nearest-even on the same grid
+// as the hardware RN-satfinite conversion (one instruction), so that
+// conversion serves every v with |v| < 240, outside (0.875, 1) 2^-6 and
+// normal or larger; the rest goes to e4m3_encode_fast: |v| >= 240 (the
+// reference saturates to 448 from 240 on; NaN and Inf), the subnormal codes
+// that would carry into the normals (the reference stays at code 7), zeros
+// and binary32 denormals (sign handling).  Checked on all 2^32 inputs.
+__device__ __forceinline__ uint32_t e4m3_encode_ref_hw(float v) {
+    const uint32_t a = __float_as_uint(v) & 0x7FFFFFFFu;
+    const bool slow = a >= 0x43700000u || (a > 0x3C600000u && a < 0x3C800000u) || a < 0x00800000u;
+    return slow ? e4m3_encode_fast(__float_as_uint(v)) : e4m3_encode_hw(v);
+}
+
 __device__ __forceinline__ uint32_t e4m3_byte(float v, bool hw) {
-    return hw ? e4m3_encode_hw(v) : e4m3_encode_fast(__float_as_uint(v));
+    return hw ? e4m3_encode_hw(v) : e4m3_encode_ref_hw(v);
+}
+
+// four scaled elements -> four E4M3 bytes, little-endian in a word
+__device__ __forceinline__ uint32_t e4m3_word(const float4& v, const InvScale& s, bool hw) {
+    return e4m3_byte(mul_round_f64(v.x, s), hw) | (e4m3_byte(mul_round_f64(v.y, s), hw) << 8) |
+           (e4m3_byte(mul_round_f64(v.z, s), hw) << 16) | (e4m3_byte(mul_round_f64(v.w, s), hw) << 24);
 }
 
 // SCALE: 0 none (quantize_fp8_e4m3, matmul.tkv:60-66), 1 per tensor, 2 per
@@ -561,12 +655,17 @@ __global__ void fp8_encode_rows_kernel(const float* __restrict__ x, uint8_t* __r
         if (VEC) {
             const float4* xr = reinterpret_cast<const float4*>(x + r * cols);
             uint32_t* qr = reinterpret_cast<uint32_t*>(q + r * cols);
-            for (int64_t c = lane; c < cols / 4; c += 32) {
-                const float4 v = __ldcs(xr + c);
-                qr[c] = e4m3_byte(mul_round_f64(v.x, s), HW) | (e4m3_byte(mul_round_f64(v.y, s), HW) << 8) |
-                        (e4m3_byte(mul_round_f64(v.z, s), HW) << 16) |
-                        (e4m3_byte(mul_round_f64(v.w, s), HW) << 24);
+            const int64_t n4 = cols / 4;
+            int64_t c = lane;
+            // four 16-byte loads in flight per lane before any is encoded
+            for (; c + 96 < n4; c += 128) {
+                float4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) v[u] = __ldcs(xr + c + 32 * u);
+#pragma unroll
+                for (int u = 0; u < 4; u++) qr[c + 32 * u] = e4m3_word(v[u], s, HW);
             }
+            for (; c < n4; c += 32) qr[c] = e4m3_word(__ldcs(xr + c), s, HW);
             continue;
         }
         for (int64_t c = lane; c < cols; c += 32) {

@@ -72,13 +72,12 @@ struct Session {
     // split Q, K and V^T, fp16 bits (tensor-core attention), and their head scales
     uint16_t *qh = nullptr, *ql = nullptr, *kh = nullptr, *kl = nullptr, *vh = nullptr, *vl = nullptr;
     int* kv_exp = nullptr;
-    // exact int8 context: per layer and head max |V| (written by c_attn), the
-    // attention's fix-up list and its two counters (zero between launches)
+    // exact int8 context: per layer and V column max |V| (written by c_attn),
+    // the attention's fix-up list and its three counters (zero between launches)
     uint32_t* vmax = nullptr;
-    int* fix_n = nullptr;       // rows, units, finished fix-up CTAs
-    int4* fix_list = nullptr;   // [fix_cap] undecided rows
-    int4* fix_units = nullptr;  // [fix_cap] their attention units
-    double* fix_acc = nullptr;  // [fix_cap][kAttnFixAccWords] binary64 row accumulators
+    int* fix_n = nullptr;       // rows, rows taken by the fix-up, finished fix-up CTAs
+    int4* fix_list = nullptr;   // [fix_cap] rows with undecided int8 columns
+    uint2* fix_mask = nullptr;  // [fix_cap] those columns
     int fix_cap = 0;
     float *x = nullptr, *qkv = nullptr, *hf = nullptr, *xf = nullptr, *xf_last = nullptr, *logits = nullptr;
     size_t logits_cap = 0;
@@ -219,16 +218,11 @@ int gemm(Session& s, const int8_t* A, const Lin& l, const float* scale_a, float*
 int attention(Session& s, int layer, float* out, int8_t* outq, const float* qscale, uint32_t* amax) {
     if (s.attn_tc) {  // K / V^T hi-lo come from the c_attn epilogue
         AttnFix fx;
-        fx.vmax = s.vmax + static_cast<size_t>(layer) * s.heads;
+        fx.vmax = s.vmax + static_cast<size_t>(layer) * s.d;
         fx.list = s.fix_list;
-        fx.units = s.fix_units;
+        fx.mask = s.fix_mask;
         fx.n = s.fix_n;
-        fx.acc = s.fix_acc;
         fx.cap = s.fix_cap;
-        fx.ucap = s.fix_cap;
-        int longest = 1;
-        for (int i = 0; i < s.nseg; i++) longest = std::max(longest, s.seg_host[i + 1] - s.seg_host[i]);
-        fx.max_keys = longest;
         return launch_attention_tc(s.qkv, s.qh, s.ql, s.kh, s.kl, s.vh, s.vl, s.kv_exp, s.T, s.tiles, s.split, s.ntiles, s.comb, s.ncomb,
                                    s.d, s.heads, out, outq, qscale, amax, s.part_o, s.part_ml, s.counters, s.st, &fx);
     }
@@ -279,7 +273,7 @@ int enqueue_layers(Session& s, bool calibrating) {
     if (s.attn_tc && s.ncomb > 0)  // merge counters start at 0 (a run that stopped early may leave them set)
         TVQ_CUDA(cudaMemsetAsync(s.counters, 0, sizeof(int) * static_cast<size_t>(s.ncomb) * s.heads, s.st));
     if (s.attn_tc)  // head maxima of V (atomicMax from c_attn) and the fix-up counters start at 0
-        TVQ_CUDA(cudaMemsetAsync(s.vmax, 0, sizeof(uint32_t) * (static_cast<size_t>(s.layers) * s.heads + 4), s.st));
+        TVQ_CUDA(cudaMemsetAsync(s.vmax, 0, sizeof(uint32_t) * (static_cast<size_t>(s.layers) * s.d + 4), s.st));
     for (int l = 0; l < s.layers; l++) {
         LayerW& w = s.L[l];
         float* sc = s.act_scale + 4 * l;
@@ -296,7 +290,7 @@ int enqueue_layers(Session& s, bool calibrating) {
         }
         // c_attn: qkv = dequant(aq Wqkv) + b
         STEP(gemm(s, s.aq, w.lin[0], sc + 0, s.qkv, nullptr, nullptr, nullptr, nullptr, TVQ_ACT_NONE, s.attn_tc,
-                  s.vmax + static_cast<size_t>(l) * s.heads));
+                  s.vmax + static_cast<size_t>(l) * s.d));
         STEP(mark(s, ST_GEMM_QKV));
         // causal attention -> int8 context (attn c_proj input)
         if (calibrating) {
@@ -523,16 +517,14 @@ int tvq_session_create(int device, int64_t vocab, int64_t d_model, int64_t n_hea
         STEP(s->alloc(&s->err, 1));
         STEP(s->alloc(&s->kv_exp, static_cast<size_t>(3 * n_heads)));
         // head maxima of V per layer, then the fix-up lists' three counters
-        STEP(s->alloc(&s->vmax, static_cast<size_t>(std::max<int64_t>(n_layers, 1) * n_heads + 4)));
-        s->fix_n = reinterpret_cast<int*>(s->vmax + std::max<int64_t>(n_layers, 1) * n_heads);
-        TVQ_CUDA(cudaMemset(s->vmax, 0, sizeof(uint32_t) * (std::max<int64_t>(n_layers, 1) * n_heads + 4)));
-        // undecided int8 rows of one attention launch: about 1 % of the
-        // (token, head) rows at GPT-2 scales; room for 12.5 %
-        s->fix_cap = static_cast<int>(std::min<int64_t>(std::max<int64_t>(4096, max_tokens * n_heads / 8), INT32_MAX / 66));
+        STEP(s->alloc(&s->vmax, static_cast<size_t>(std::max<int64_t>(n_layers, 1) * d_model + 4)));
+        s->fix_n = reinterpret_cast<int*>(s->vmax + std::max<int64_t>(n_layers, 1) * d_model);
+        TVQ_CUDA(cudaMemset(s->vmax, 0, sizeof(uint32_t) * (std::max<int64_t>(n_layers, 1) * d_model + 4)));
+        // (token, head) rows of one attention launch with undecided int8
+        // columns: about 2 % at GPT-2 scales; room for 12.5 %
+        s->fix_cap = static_cast<int>(std::min<int64_t>(std::max<int64_t>(4096, max_tokens * n_heads / 8), INT32_MAX / 16));
         STEP(s->alloc(&s->fix_list, static_cast<size_t>(s->fix_cap)));
-        STEP(s->alloc(&s->fix_units, static_cast<size_t>(s->fix_cap)));
-        STEP(s->alloc(&s->fix_acc, static_cast<size_t>(s->fix_cap) * kAttnFixAccWords));
-        TVQ_CUDA(cudaMemset(s->fix_acc, 0, sizeof(double) * static_cast<size_t>(s->fix_cap) * kAttnFixAccWords));
+        STEP(s->alloc(&s->fix_mask, static_cast<size_t>(s->fix_cap)));
         TVQ_CUDA(cudaMemset(s->err, 0, sizeof(int)));
         std::lock_guard<std::mutex> lk(g_mu);
         *handle = g_next++;
@@ -991,34 +983,28 @@ int tvq_dev_attention(const float* qkv, const int64_t* seg, int64_t n_seg, int64
         // fp16 Q / K / V^T hi + lo (n4 halves each), then 3 heads exponents
         // and 3 heads amax words
         const size_t n4 = std::max<size_t>((static_cast<size_t>(attention_tc_pitch(T)) * d + 7) & ~size_t(7), 8);
-        // + the exact-int8 fix-up lists (rows and units, 16-byte entries), their
-        // accumulators and three counters
+        // + the exact-int8 fix-up list (16-byte rows, 8-byte column masks)
+        // and three counters
         const int64_t fcap = outq ? std::max<int64_t>(4096, static_cast<int64_t>(T) * n_heads / 8) : 0;
-        TVQ_CHECK(fcap <= INT32_MAX / 66, TVQ_ERR_UNSUPPORTED, "too many tokens x heads for the int8 fix-up lists");
+        TVQ_CHECK(fcap <= INT32_MAX / 16, TVQ_ERR_UNSUPPORTED, "too many tokens x heads for the int8 fix-up lists");
         uint16_t* kv = nullptr;
-        const size_t kv_bytes = (sizeof(uint16_t) * 6 * n4 + sizeof(int) * 6 * n_heads + 4 * sizeof(int) + 15) & ~size_t(15);
-        const size_t acc_bytes = sizeof(double) * static_cast<size_t>(fcap) * kAttnFixAccWords;
+        const size_t kv_bytes =
+            (sizeof(uint16_t) * 6 * n4 + sizeof(int) * 6 * n_heads + 4 * sizeof(int) + sizeof(uint32_t) * d + 15) &
+            ~size_t(15);
         TVQ_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&kv),
-                                 kv_bytes + acc_bytes + 2 * sizeof(int4) * static_cast<size_t>(fcap), st));
+                                 kv_bytes + (sizeof(int4) + sizeof(uint2)) * static_cast<size_t>(fcap), st));
         int* kv_exp = reinterpret_cast<int*>(kv + 6 * n4);
         uint32_t* kv_amax = reinterpret_cast<uint32_t*>(kv_exp + 3 * n_heads);
         AttnFix fx;
-        fx.vmax = kv_amax + 2 * n_heads;  // the V part's exact head maxima (launch_split_kv)
         fx.n = reinterpret_cast<int*>(kv_amax + 3 * n_heads);
-        fx.acc = reinterpret_cast<double*>(reinterpret_cast<char*>(kv) + kv_bytes);
-        fx.list = reinterpret_cast<int4*>(reinterpret_cast<char*>(kv) + kv_bytes + acc_bytes);
-        fx.units = fx.list + fcap;
+        uint32_t* vcol = reinterpret_cast<uint32_t*>(fx.n + 4);  // each V column's max |V| (launch_split_kv)
+        fx.vmax = vcol;
+        fx.list = reinterpret_cast<int4*>(reinterpret_cast<char*>(kv) + kv_bytes);
+        fx.mask = reinterpret_cast<uint2*>(fx.list + fcap);
         fx.cap = static_cast<int>(fcap);
-        fx.ucap = static_cast<int>(fcap);
-        int64_t longest = 1;
-        for (int64_t i = 0; i < n_seg; i++) longest = std::max<int64_t>(longest, seg[i + 1] - seg[i]);
-        fx.max_keys = static_cast<int>(longest);
-        if (fcap) {
-            TVQ_CUDA(cudaMemsetAsync(fx.n, 0, 3 * sizeof(int), st));
-            TVQ_CUDA(cudaMemsetAsync(fx.acc, 0, acc_bytes, st));
-        }
+        if (fcap) TVQ_CUDA(cudaMemsetAsync(fx.n, 0, 3 * sizeof(int), st));
         int r = launch_split_kv(qkv, T, static_cast<int>(d), kv, kv + n4, kv + 2 * n4, kv + 3 * n4, kv + 4 * n4,
-                                kv + 5 * n4, kv_exp, kv_amax, st);
+                                kv + 5 * n4, kv_exp, kv_amax, st, fcap ? vcol : nullptr);
         if (!r)
             r = launch_attention_tc(qkv, kv, kv + n4, kv + 2 * n4, kv + 3 * n4, kv + 4 * n4, kv + 5 * n4, kv_exp, T,
                                     tiles_dev, tiles_dev + n,
