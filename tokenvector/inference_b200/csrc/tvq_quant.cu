@@ -394,34 +394,38 @@ __global__ void rowwise_kernel(const float* __restrict__ x, int8_t* __restrict__
 }
 
 // Modes 0 and 2 for rows of 1025 .. 8192 floats (cols % 4 == 0, 16-byte
-// aligned rows): a 512-thread block takes its rows one at a time, and the
-// rows stream into a ring of `ns` (3 or 4) shared-memory slots by 1-D bulk
+// aligned rows): a 256-thread block takes its rows one at a time, and the
+// rows stream into a ring of ROW_SLOTS shared-memory slots by 1-D bulk
 // copies (the TMA engine; warp 0 issues up to 8 KB per lane, completion on
 // the slot's mbarrier), so HBM never waits for the arithmetic and each
-// element is read once.  The steps of consecutive rows overlap: while all
-// warps quantize row i with its scale, the block has already reduced row
-// i + 1's max |x| and warp 0 forms row i + 1's scale (two binary64
-// divisions) -- no warp waits for that serial step.  Same scale and
-// quantize arithmetic as rowwise_kernel.  Every wait is bounded
+// element is read once.  Per row: max |x| (one block reduction), the scale,
+// the quantize.  Mode 0 (calibrate_per_channel_minmax + quantize) forms the
+// scale in every thread without binary64: fl32(fl64(amax / 127)) is the
+// correctly rounded f32 quotient (an f64 quotient by 127 repeats a 7-bit
+// pattern, so it never lands on an f32 rounding midpoint), and the fast
+// quantize needs only fl32(1 / scale) (quant_fast_t); the binary64 1/scale
+// is formed in the rare near-tie path.  Mode 2 (dynamic, scale kept in
+// binary64) takes its scale from warp 0.  Every wait is bounded
 // (DEVERR_TIMEOUT_ROWS).
-constexpr int ROW_THREADS = 512;      // two blocks per SM: 32 warps
+constexpr int ROW_THREADS = 256;      // four blocks per SM (rows up to 6400 floats): 32 warps
 constexpr uint32_t ROW_CHUNK = 8192;  // bytes per bulk copy
-constexpr int ROW_MAX_SLOTS = 4;
+constexpr int ROW_SLOTS = 2;
 
 template <int MODE>
-__global__ void __launch_bounds__(ROW_THREADS, 2) rowwise_pipe_kernel(const float* __restrict__ x, int8_t* __restrict__ q,
+__global__ void __launch_bounds__(ROW_THREADS, 4) rowwise_pipe_kernel(const float* __restrict__ x, int8_t* __restrict__ q,
                                                                       float* __restrict__ scales, int64_t rows,
-                                                                      int64_t cols, int ns, int* err) {
-    extern __shared__ __align__(128) float4 rbuf[];  // [ns][cols / 4]
+                                                                      int64_t cols, int* err) {
+    extern __shared__ __align__(128) float4 rbuf[];  // [ROW_SLOTS][cols / 4]
     __shared__ float red[ROW_THREADS / 32];
-    __shared__ InvScale row_qs[2];  // by row parity
-    __shared__ __align__(8) uint64_t full[ROW_MAX_SLOTS];
+    __shared__ InvScale row_qs;
+    __shared__ __align__(8) uint64_t full[ROW_SLOTS];
     const int tid = threadIdx.x;
     const int n4 = static_cast<int>(cols / 4);
     const uint32_t row_bytes = static_cast<uint32_t>(cols) * 4u;
     const int64_t step = gridDim.x;
     if (tid == 0) {
-        for (int s = 0; s < ns; s++) mbar_init(&full[s], 1);
+#pragma unroll
+        for (int s = 0; s < ROW_SLOTS; s++) mbar_init(&full[s], 1);
         fence_barrier_init();
     }
     __syncthreads();
@@ -439,9 +443,16 @@ __global__ void __launch_bounds__(ROW_THREADS, 2) rowwise_pipe_kernel(const floa
             bulk_load(reinterpret_cast<char*>(rbuf + static_cast<int64_t>(slot) * n4) + off,
                       reinterpret_cast<const char*>(x + r * cols) + off, min(ROW_CHUNK, row_bytes - off), &full[slot]);
     };
-    // this thread's part of row j's max |x|, then the warp's, into red[]
-    auto amax_part = [&](int j) {
-        const float4* row = rbuf + static_cast<int64_t>(j % ns) * n4;
+    int64_t r = blockIdx.x;
+#pragma unroll
+    for (int s = 0; s < ROW_SLOTS - 1; s++) issue(r + s * step, s);
+    for (int i = 0; r < rows; i++, r += step) {
+        const int slot = i % ROW_SLOTS;
+        const bool ok = mbar_wait(&full[slot], static_cast<uint32_t>(i / ROW_SLOTS) & 1u, err, DEVERR_TIMEOUT_ROWS);
+        // every thread is past the previous row (its slot is free, red[] too)
+        if (!__syncthreads_and(ok)) return;  // the error word holds the cause
+        issue(r + (ROW_SLOTS - 1) * step, (i + ROW_SLOTS - 1) % ROW_SLOTS);
+        const float4* row = rbuf + static_cast<int64_t>(slot) * n4;
         float am = 0.0f;
         for (int c = tid; c < n4; c += ROW_THREADS) {
             const float4 v = row[c];
@@ -449,57 +460,43 @@ __global__ void __launch_bounds__(ROW_THREADS, 2) rowwise_pipe_kernel(const floa
         }
         am = warp_max(am);
         if ((tid & 31) == 0) red[tid >> 5] = am;
-    };
-    // warp 0, after the block barrier that follows amax_part(j): row j's
-    // scale (stored) and 1/scale (for the quantize of row j)
-    auto row_scale = [&](int j, int64_t rj) {
-        const float am = warp_max(tid < ROW_THREADS / 32 ? red[tid] : 0.0f);
-        if (tid != 0) return;
-        double amd = am;
-        if (amd < 0.00000001) amd = 0.00000001;
+        __syncthreads();
+#pragma unroll
+        for (int w = 0; w < ROW_THREADS / 32; w++) am = fmaxf(am, red[w]);
+        float sc, hi;
         if (MODE == 0) {
-            const float x0 = reinterpret_cast<const float*>(rbuf + static_cast<int64_t>(j % ns) * n4)[0];
-            const bool poisoned = (x0 != x0);  // NaN first element poisons min/max
-            const float sc = poisoned ? __int_as_float(0x7FC00000) : __double2float_rn(amd / 127.0);
-            scales[rj] = sc;
-            row_qs[j & 1] = make_inv_scale(static_cast<double>(sc));
+            const float x0 = reinterpret_cast<const float*>(row)[0];
+            if (x0 != x0) {  // NaN first element poisons min/max
+                sc = __int_as_float(0x7FC00000);
+            } else if (static_cast<double>(am) < 0.00000001) {
+                sc = __double2float_rn(0.00000001 / 127.0);
+            } else {
+                sc = __fdiv_rn(am, 127.0f);  // = fl32(fl64(am / 127)), see above
+            }
+            hi = (static_cast<double>(sc) > 0.00000001) ? __frcp_rn(sc) : __double2float_rn(1.0 / 0.00000001);
+            if (sc != sc) hi = sc;  // NaN scale: NaN products -> 0
+            if (tid == 0) scales[r] = sc;
         } else {
-            const double sc = amd / 127.0;
-            scales[rj] = __double2float_rn(sc);
-            row_qs[j & 1] = make_inv_from_inv(1.0 / sc);
+            if (tid == 0) {
+                double amd = am;
+                if (amd < 0.00000001) amd = 0.00000001;
+                const double scd = amd / 127.0;
+                scales[r] = __double2float_rn(scd);
+                row_qs = make_inv_from_inv(1.0 / scd);
+            }
+            __syncthreads();
+            hi = row_qs.hi;
+            sc = 0.0f;
         }
-    };
-    int64_t r = blockIdx.x;
-    if (r >= rows) return;
-    for (int s = 0; s < ns - 1; s++) issue(r + s * step, s);
-    {  // row 0 of this block: its scale before the loop
-        const bool ok = mbar_wait(&full[0], 0u, err, DEVERR_TIMEOUT_ROWS);
-        if (!__syncthreads_and(ok)) return;  // the error word holds the cause
-        amax_part(0);
-        __syncthreads();
-        if (tid < 32) row_scale(0, r);
-    }
-    for (int i = 0; r < rows; i++, r += step) {
-        const int64_t rn = r + step;  // row i + 1 (block-uniform)
-        bool ok = true;
-        if (rn < rows) ok = mbar_wait(&full[(i + 1) % ns], static_cast<uint32_t>((i + 1) / ns) & 1u, err,
-                                      DEVERR_TIMEOUT_ROWS);
-        // every thread is past row i - 1 (its slot is free) and row i's scale is published
-        if (!__syncthreads_and(ok)) return;
-        issue(r + (ns - 1) * step, (i + ns - 1) % ns);
-        if (rn < rows) amax_part(i + 1);
-        __syncthreads();
-        if (rn < rows && tid < 32) row_scale(i + 1, rn);
-        const InvScale qs = row_qs[i & 1];
-        const float4* row = rbuf + static_cast<int64_t>(i % ns) * n4;
         uint32_t* qr = reinterpret_cast<uint32_t*>(q + r * cols);
         for (int c = tid; c < n4; c += ROW_THREADS) {
             const float4 v = row[c];
             float t0, t1, t2, t3;
-            const bool fast = quant_fast_t(v.x, qs.hi, t0) & quant_fast_t(v.y, qs.hi, t1) &
-                              quant_fast_t(v.z, qs.hi, t2) & quant_fast_t(v.w, qs.hi, t3);
+            const bool fast = quant_fast_t(v.x, hi, t0) & quant_fast_t(v.y, hi, t1) & quant_fast_t(v.z, hi, t2) &
+                              quant_fast_t(v.w, hi, t3);
             uint32_t w = pack_q4(t0, t1, t2, t3);
             if (!fast) {  // rare: the binary64 expression decides
+                const InvScale qs = (MODE == 0) ? make_inv_scale(static_cast<double>(sc)) : row_qs;
                 char4 o;
                 o.x = quant_exact(v.x, qs);
                 o.y = quant_exact(v.y, qs);
@@ -519,26 +516,24 @@ int launch_rowwise(int mode, const float* x, int8_t* q, float* scales, int64_t r
     const bool vec = (cols % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(q) & 3) == 0);
     if (mode != 1 && vec && cols > 1024 && cols <= 8192) {
-        // four ring slots while two blocks still fit an SM (227 KB), else three
-        const size_t row_b = static_cast<size_t>(cols) * 4;
-        const int ns = (2 * (4 * row_b + 2048) <= 227 * 1024) ? 4 : 3;
-        const size_t smem = static_cast<size_t>(ns) * row_b;
-        // the ring: at most 4 slots of 7136 floats (114 KB) or 3 of 8192 (96 KB)
-        constexpr int kRingMax = 114 * 1024 + 1024;
+        const size_t smem = static_cast<size_t>(ROW_SLOTS) * static_cast<size_t>(cols) * 4;  // <= 96 KB
         static int attr_done[64] = {0};  // per device
         int dev = 0;
         TVQ_CUDA(cudaGetDevice(&dev));
         if (dev < 64 && !attr_done[dev]) {
-            TVQ_CUDA(cudaFuncSetAttribute(rowwise_pipe_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRingMax));
-            TVQ_CUDA(cudaFuncSetAttribute(rowwise_pipe_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRingMax));
+            TVQ_CUDA(cudaFuncSetAttribute(rowwise_pipe_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          ROW_SLOTS * 8192 * 4));
+            TVQ_CUDA(cudaFuncSetAttribute(rowwise_pipe_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          ROW_SLOTS * 8192 * 4));
             attr_done[dev] = 1;
         }
         int rc = 0;
         DeviceState* ds = device_state(&rc);
         if (!ds) return rc;
-        const int g = grid_for(rows * ROW_THREADS, ROW_THREADS, 2);
-        if (mode == 0) rowwise_pipe_kernel<0><<<g, ROW_THREADS, smem, st>>>(x, q, scales, rows, cols, ns, ds->d_error);
-        else rowwise_pipe_kernel<2><<<g, ROW_THREADS, smem, st>>>(x, q, scales, rows, cols, ns, ds->d_error);
+        const int per_sm = static_cast<int>(std::min<size_t>(4, (227 * 1024) / (smem + 1024)));
+        const int g = grid_for(rows * ROW_THREADS, ROW_THREADS, per_sm);
+        if (mode == 0) rowwise_pipe_kernel<0><<<g, ROW_THREADS, smem, st>>>(x, q, scales, rows, cols, ds->d_error);
+        else rowwise_pipe_kernel<2><<<g, ROW_THREADS, smem, st>>>(x, q, scales, rows, cols, ds->d_error);
         TVQ_CUDA(cudaGetLastError());
         return TVQ_OK;
     }
