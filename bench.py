@@ -100,7 +100,8 @@ def attention_roofline(per_stage_ms, bf16, src, n_layers, T=SEQ, hd=64, heads=12
     achieved = flops / t / 1e12
     peak = bf16
     return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-            "traffic": None, "kernel": "attention_tc_kernel (FP16 hi/lo operands, partial merge in-kernel), per layer",
+            "traffic": None, "kernel": "attention_tc_kernel (FP16 hi/lo operands, partial merge in-kernel) + "
+                                       "attention_fix_kernel (binary64 recompute of the undecided int8 columns), per layer",
             "peak_source": "dense FP16 = %s bf16" % src, "products_per_useful_product": 3}
 
 
@@ -783,9 +784,9 @@ def run_ours(args, rank, world, local):
         else:
             roof = {"bound": "tensor", "achieved": ops / t / 1e12, "peak": int8_peak, "unit": "TOPS"}
         roof["frac"] = roof["achieved"] / roof["peak"]
-        # dram__bytes_read + dram__bytes_write of one c_fc launch inside the
-        # forward (ncu, profiles/gemm_i8_gpt2_124m.md); outputs stay in L2
-        roof["traffic"] = None  # DRAM bytes come from ncu captures, not from this run
+        # dram__bytes_read + dram__bytes_write of a launch come from an ncu
+        # capture of the same kernel, not from this run
+        roof["traffic"] = None
         roof["kernel"] = "gemm_tc_kernel<I8> (%s, M=%d, N,K of the layer)" % (dom, T)
         roof["peak_source"] = "%s HBM copy bandwidth; INT8 peak: %s" % (src, int8_src)
         kernels = {}
