@@ -298,7 +298,7 @@ TVQ_API int tvq_dev_layernorm(const float* x, const float* gamma, const float* b
  * [T, 3d] rows [Q|K|V]; out f32 [T, d] and/or outq int8 (scale qscale_dev).
  * tiles_dev: device scratch of tiles_cap entries of 4 x int32, 16-byte
  * aligned; a call needs one entry per 64-row query tile, or with head dim 64
- * (tensor-core kernel, 3xTF32 products) two per 128-row tile -- at most
+ * (tensor-core kernel, FP16 hi/lo products) two per 128-row tile -- at most
  * ceil(len / 64) + 1 entries per sequence either way.  fp32-accurate: within
  * 1e-4 relative / 2e-6 absolute of the f64 oracle. */
 TVQ_API int tvq_dev_attention(const float* qkv, const int64_t* seg, int64_t n_seg, int64_t d, int64_t n_heads,
@@ -311,8 +311,8 @@ TVQ_API int tvq_dev_attention(const float* qkv, const int64_t* seg, int64_t n_se
  * (every GPU that loads it holds it until exit), so at most 32768 tiles of
  * 64 tokens per sequence fit in one call; larger calls fail with
  * TVQ_ERR_SIZE.  The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress), so make it before any stream capture.  All
- * calls share the array: calls that overlap on the GPU race on it.  No
+ * address (cudaGetSymbolAddress) once.  All calls share the array: calls
+ * that overlap on the GPU race on it.  No
  * cudaMalloc or cudaFree is called.  The tile list is copied into the array
  * from host memory, so the call blocks the calling thread until the work
  * already queued on `stream` has finished.  It always runs the fp32 SIMT

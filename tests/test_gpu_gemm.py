@@ -320,3 +320,32 @@ def test_f16_split_gemm_is_fp32_accurate(m, n, k):
     rel = err / (mag + 1e-300)
     assert np.all(rel <= 2.0 ** -18), float(rel.max())
     assert rel.max() <= max(4.0 * e32.max(), 2.0 ** -22), (rel.max(), e32.max())
+
+
+def test_matmul_fp8_config3_grid_worst_error(capsys):
+    """BASELINE config 3 (FP8 E4M3 PTQ GEMM, GPT-2-medium widths): activations
+    N(0,1) with 0.1 % outliers x20, weights N(0,0.02), per-tensor / per-channel
+    scales amax/448.  Over the (K, N) grid and M up to 1024, the worst error
+    relative to sum |a w| sa sw, the fraction of E4M3 subnormal operands, and
+    the share of the tolerance the OCP-vs-reference subnormal decode takes;
+    every element within the stated tolerance."""
+    lines = []
+    for (k, n) in [(1024, 3072), (1024, 4096), (4096, 1024)]:
+        for m in (1, 16, 128, 1024):
+            A, W, sa, sw = _fp8_operands(m, n, k, 7 * m + n + k)
+            Y = np.empty(m * n, np.float32)
+            M.matmul_fp8_e4m3(A, W, None, Y, m, n, k, float(sa[0]), sw)
+            ref = O.matmul_fp8_e4m3(A, W, None, float(sa[0]), sw).astype(np.float64)
+            err = np.abs(Y.reshape(m, n).astype(np.float64) - ref)
+            tol = _fp8_tol(A, W, sa, sw) + np.abs(ref) * 2.0 ** -23
+            assert np.all(err <= tol), (m, n, k, float((err / tol).max()))
+            da = np.abs(O.dequantize_fp8_e4m3(A).astype(np.float64))
+            dw = np.abs(O.dequantize_fp8_e4m3(W).astype(np.float64))
+            mag = (da @ dw.T) * float(sa[0]) * sw.astype(np.float64)[None, :]
+            sub_a = float((((A & 0x78) == 0) & ((A & 0x7) != 0)).mean())
+            sub_w = float((((W & 0x78) == 0) & ((W & 0x7) != 0)).mean())
+            lines.append("fp8 config3 m=%d n=%d k=%d: max err/sum|aw| %.3g, max err/tol %.3g, subnormal bytes "
+                         "A %.2f%% W %.2f%%" % (m, n, k, float((err / (mag + 1e-30)).max()),
+                                                  float((err / tol).max()), 100 * sub_a, 100 * sub_w))
+    with capsys.disabled():
+        print("\n" + "\n".join(lines))
