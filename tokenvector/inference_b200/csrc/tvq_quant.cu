@@ -448,9 +448,18 @@ __global__ void __launch_bounds__(ROW_THREADS, 4) rowwise_pipe_kernel(const floa
     for (int s = 0; s < ROW_SLOTS - 1; s++) issue(r + s * step, s);
     for (int i = 0; r < rows; i++, r += step) {
         const int slot = i % ROW_SLOTS;
-        const bool ok = mbar_wait(&full[slot], static_cast<uint32_t>(i / ROW_SLOTS) & 1u, err, DEVERR_TIMEOUT_ROWS);
+        const uint32_t par = static_cast<uint32_t>(i / ROW_SLOTS) & 1u;
+        const bool ok = mbar_wait(&full[slot], par, err, DEVERR_TIMEOUT_ROWS);
         // every thread is past the previous row (its slot is free, red[] too)
-        if (!__syncthreads_and(ok)) return;  // the error word holds the cause
+        if (!__syncthreads_and(ok)) {  // the error word holds the cause
+            // the only copy in flight is this slot's (the next row is issued
+            // after this barrier): give it a bounded time to land, then leave
+            if (tid == 0) {
+                const uint64_t t0 = globaltimer_ns();
+                while (!mbar_try_wait(&full[slot], par) && globaltimer_ns() - t0 < 100000000ull) __nanosleep(1000);
+            }
+            return;
+        }
         issue(r + (ROW_SLOTS - 1) * step, (i + ROW_SLOTS - 1) % ROW_SLOTS);
         const float4* row = rbuf + static_cast<int64_t>(slot) * n4;
         float am = 0.0f;
