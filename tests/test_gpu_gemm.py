@@ -349,3 +349,67 @@ def test_matmul_fp8_config3_grid_worst_error(capsys):
                                                   float((err / tol).max()), 100 * sub_a, 100 * sub_w))
     with capsys.disabled():
         print("\n" + "\n".join(lines))
+
+
+def _dev_gemm(tA, tW, tb, tR, Y, Yq, m, n, k, sa, tsw, per_channel, act, so):
+    from tokenvector.inference_b200.quantization import _buf as B
+    N.call("tvq_dev_gemm", N.GEMM_I8, B.ptr(tA), B.ptr(tW), B.ptr(tb), B.ptr(tR), B.ptr(Y), B.ptr(Yq), m, n, k,
+           B.ptr(sa), B.ptr(tsw), per_channel, act, B.ptr(so), 0, B.stream_of(tA))
+
+
+@pytest.mark.parametrize("m,n,k,seed,nonfinite", [(1024, 3072, 768, 11, False), (200, 320, 768, 12, True),
+                                                  (130, 4096, 1600, 13, False), (1, 64, 16, 14, True),
+                                                  (300, 6400, 1600, 15, False)])
+def test_device_gemm_gelu_int8_only_exact(m, n, k, seed, nonfinite):
+    """GELU-erf -> int8 with no f32 output (the c_fc form of a static-scale
+    forward): every int8 is the reference's quantize (engine.tkv:216-226) of
+    the reference's GELU (tensor.tkv:165-190) of the reference's dequant
+    (matmul.tkv:28), elements near an int8 rounding boundary, saturated ones
+    and non-finite biases included."""
+    import torch
+    A, W = _mats(m, n, k, seed)
+    rng = np.random.default_rng(seed)
+    bias = (rng.standard_normal(n) * 0.5).astype(np.float32)
+    if nonfinite:
+        bias[:3] = [np.inf, -np.inf, np.nan]
+    sw = (rng.random(n) * 2e-4 + 1e-5).astype(np.float32)
+    sa_v, so_v = np.float32(0.05), np.float32(0.03)
+    dev = torch.device("cuda:0")
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    tA, tW, tb, tsw = t(A), t(W), t(bias), t(sw)
+    sa = torch.tensor([sa_v], dtype=torch.float32, device=dev)
+    so = torch.tensor([so_v], dtype=torch.float32, device=dev)
+    Yq = torch.empty((m, n), dtype=torch.int8, device=dev)
+    _dev_gemm(tA, tW, tb, None, None, Yq, m, n, k, sa, tsw, 1, N.ACT_GELU_ERF, so)
+    torch.cuda.synchronize()
+    base = O.matmul_int8_per_channel(A, W, bias, sa_v, sw)
+    want = O.quantize_int8_symmetric(O.gelu_erf_array(base), so_v)
+    got = Yq.cpu().numpy()
+    bad = np.argwhere(got != want)
+    assert bad.size == 0, "%d int8 values differ, first at %s: %d vs %d" % (
+        len(bad), tuple(bad[0]), got[tuple(bad[0])], want[tuple(bad[0])])
+    # the data reach the saturation bound and the rounding boundaries
+    assert (np.abs(want) == 127).any()
+
+
+@pytest.mark.parametrize("m,n,k,in_place", [(1024, 768, 3072, True), (1024, 768, 768, False), (77, 1600, 6400, True),
+                                            (300, 512, 64, False), (129, 4096, 1040, True)])
+def test_device_gemm_residual_f32_exact(m, n, k, in_place):
+    """Dequant + bias + residual with an f32 output only (the c_proj form of a
+    forward, the residual stream updated in place): fl32 of the reference's
+    f64 chain plus the residual, bit for bit."""
+    import torch
+    A, W = _mats(m, n, k, 21)
+    rng = np.random.default_rng(21)
+    bias = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    sw = (rng.random(n) * 2e-4 + 1e-5).astype(np.float32)
+    R = rng.standard_normal((m, n)).astype(np.float32)
+    dev = torch.device("cuda:0")
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    tA, tW, tb, tsw, tR = t(A), t(W), t(bias), t(sw), t(R)
+    sa = torch.tensor([0.02], dtype=torch.float32, device=dev)
+    Y = tR if in_place else torch.empty((m, n), dtype=torch.float32, device=dev)
+    _dev_gemm(tA, tW, tb, tR, Y, None, m, n, k, sa, tsw, 1, N.ACT_NONE, None)
+    torch.cuda.synchronize()
+    want = O.add(O.matmul_int8_per_channel(A, W, bias, np.float32(0.02), sw), R)
+    assert _same(Y.cpu().numpy(), want)

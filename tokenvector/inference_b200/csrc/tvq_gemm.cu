@@ -401,6 +401,29 @@ __device__ __forceinline__ void tile_coords(const KParams& p, int tile, int& mb,
     nb = r / gm;
 }
 
+// Lean epilogues: compile-time forms of the general epilogue for the two
+// GEMM shapes of a static-scale forward, picked by the host only when every
+// other output (amax, raw accumulators, attention operands, zero points) is
+// off and n is a multiple of 16:
+//   LEAN_GELU_Q8  y = fl32(fl64(acc * w[n]) + b[n]), GELU-erf, int8 out only
+//   LEAN_F32      y = fl32(fl64(acc * w[n]) + b[n]) (+ residual), f32 out only
+// with w[n] = fl64(sa * sw[n]) exact (per tensor, or per channel where
+// fl64(fl64(acc * sa) * sw) = fl64(acc * (sa * sw))).  Each epilogue warp
+// owns the 16-column chunks c = half + 4 i of its lane group's 32 rows: one
+// tcgen05.ld of 16 columns, then the row's 16 outputs go straight from the
+// lane's registers to global memory (16 int8 bytes or 64 f32 bytes per
+// lane, whole 32-byte sectors), with no shared-memory staging and no barrier
+// across warps (a warp's column scales and biases sit in its own shared-
+// memory slot, written by its own lanes).  GELU_Q8 decides every int8 value
+// in one test: the GELU error bound and the quantize margin together.
+//   LEAN_QKV      y as LEAN_F32 (no residual) for a c_attn GEMM, plus the
+//                 attention's fp16 hi / lo operands: Q and K row-major, V
+//                 transposed, each head scaled by 2^kv_exp, and each V
+//                 column's max |V| (the general epilogue's kv split)
+constexpr int LEAN_GELU_Q8 = 1;
+constexpr int LEAN_F32 = 2;
+constexpr int LEAN_QKV = 3;
+
 template <int KIND, int BN>
 __device__ __forceinline__ constexpr uint32_t make_idesc() {
     // instruction descriptor: [4,6) D format, [7,10) A format, [10,13) B
@@ -414,7 +437,7 @@ __device__ __forceinline__ constexpr uint32_t make_idesc() {
 
 // NSA / NSB operand parts per stage: 1, or 2 (high + low) for the split
 // GEMMs; GEMM_W4 splits A only.
-template <int KIND, int BN>
+template <int KIND, int BN, int LEAN = 0>
 struct Cfg {
     static constexpr int NSA = (split_kind(KIND) || KIND == GEMM_W4) ? 2 : 1;
     static constexpr int NSB = split_kind(KIND) ? 2 : 1;
@@ -423,22 +446,263 @@ struct Cfg {
     static constexpr uint32_t A_BYTES = BM * BK;                  // one part
     static constexpr uint32_t B_BYTES = BN * BK;
     static constexpr uint32_t STAGE_BYTES = NSA * A_BYTES + NSB * B_BYTES;
-    static constexpr int STAGES = (STAGE_BYTES * 8 <= 196608) ? 8 : 196608 / STAGE_BYTES;
+    // LEAN_F32 stages each warp's 32 x 16 f32 chunk in shared memory (2 KB
+    // per warp beside its 1 KB of column scales): the ring gives up stages
+    // to stay within 227 KB
+    static constexpr uint32_t LEAN_EXTRA = (LEAN == 2) ? 32768u : 0u;
+    static constexpr int STAGES =
+        LEAN_EXTRA ? ((232448u - 49152u - 2u * 2u * BN * 8u - 1536u) / STAGE_BYTES < 8u
+                          ? (232448u - 49152u - 2u * 2u * BN * 8u - 1536u) / STAGE_BYTES : 8)
+                   : (STAGE_BYTES * 8 <= 196608) ? 8 : 196608 / STAGE_BYTES;
     // TMEM accumulator buffers: 2 (tile i+1's MMAs overlap tile i's
     // epilogue), 4 for the short promotion units of the split kinds
     static constexpr int NACC = promoted_kind(KIND) ? 4 : 2;
     static constexpr uint32_t TMEM_COLS = NACC * BN;  // 128/256/512: powers of two
     static constexpr uint32_t RING = STAGES * STAGE_BYTES;
-    static constexpr uint32_t EPI = EpiOf<KIND>::EPI_WARPS * 32 * EpiOf<KIND>::CH * 4;  // per-warp 32 x CH f32 staging
+    static constexpr uint32_t EPI = EpiOf<KIND>::EPI_WARPS * 32 * EpiOf<KIND>::CH * 4 + LEAN_EXTRA;  // per-warp 32 x CH f32 staging
     static constexpr uint32_t COLS = 2 * 2 * BN * 8;  // per-column scale and bias of a tile (f64), double-buffered
     static constexpr uint32_t SMEM = RING + EPI + COLS + 1024 /*align*/ + 512 /*barriers*/;
 };
 
-template <int KIND, int BN>
+// The lean epilogue of one CTA (warps 4 .. 19; see LEAN_GELU_Q8 / LEAN_F32).
+// slots: the general epilogue's staging area, 1 KB per warp here (the f64
+// scale and bias of up to 64 columns).
+template <int KIND, int BN, int LEAN>
+__device__ __forceinline__ void lean_epilogue(const KParams& p, double* slots, uint64_t* tfull, uint64_t* tempty,
+                                              uint32_t tmem_base, int warp, int lane) {
+    using C = Cfg<KIND, BN, LEAN>;
+    constexpr int EPW = 4;             // warps per TMEM lane group
+    constexpr int LCH = 16;            // columns per chunk
+    constexpr int NCH = BN / (LCH * EPW);  // chunks per warp per tile
+    static_assert(NCH >= 1 && EpiOf<KIND>::EPI_WARPS == 16, "lean epilogue: 16 warps, BN >= 64");
+    static_assert(16 * 64 * 2 * 8 + (LEAN == LEAN_F32 ? 16 * 32 * LCH * 4 : 0) <= C::EPI,
+                  "lean epilogue slots exceed the staging area");
+    const int eg = warp & 3;
+    const int half = (warp - 4) >> 2;
+    double* ws = slots + (warp - 4) * 128;  // [64] scales, then [64] biases
+    double* bs = ws + 64;
+    // LEAN_F32: this warp's 32 x 16 f32 staging tile (after the 16 slots);
+    // float4 j of row r sits at slot j ^ ((r >> 1) & 3): conflict-free both
+    // ways (lane = row when written, 4 lanes per row when read)
+    float* stg = reinterpret_cast<float*>(slots + 16 * 128) + (warp - 4) * (32 * LCH);
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(eg * 32) << 16);
+    const float sa = __ldg(p.scale_a);
+    const float sw0 = __ldg(p.scales_w);
+    const bool per_channel = p.per_channel != 0;
+    InvScale qs{0.0, 0.0f, 0.0f};
+    float c1 = 0.0f;
+    if constexpr (LEAN == LEAN_GELU_Q8) {
+        qs = make_inv_scale(static_cast<double>(__ldg(p.scale_out)));
+        // an element is decided on the fast path when g hi lies farther than
+        // (|g| + 1) hi 2^-19 (the fast GELU's error, widened by 2^-10) plus
+        // 2^-14 (the product's rounding and hi's distance from 1/scale:
+        // quant_fast_t's 2^-15, and 2^-16 more) from a half-integer
+        c1 = qs.hi * 1.9092130661010742e-06f;  // hi 2^-19 (1 + 2^-10)
+    }
+    uint32_t tcount = 0;
+    for (int tile = blockIdx.x; tile < p.num_m_blocks * p.num_n_blocks; tile += gridDim.x, tcount++) {
+        const uint32_t b = tcount % C::NACC;
+        const uint32_t aph = (tcount / C::NACC) & 1u;
+        int mb, nb;
+        tile_coords(p, tile, mb, nb);
+        const int row = mb * BM + eg * 32 + lane;
+        const bool row_ok = row < p.m;
+        // this warp's column scales and biases (the previous tile's reads of
+        // the slot are done: same warp, program order)
+        __syncwarp();
+        for (int j = lane; j < LCH * NCH; j += 32) {
+            const int n = min(nb * BN + (half + EPW * (j / LCH)) * LCH + j % LCH, p.n - 1);
+            const float sw = per_channel ? __ldg(p.scales_w + n) : sw0;
+            ws[j] = static_cast<double>(sa) * static_cast<double>(sw);  // exact
+            bs[j] = static_cast<double>(p.bias ? __ldg(p.bias + n) : 0.0f);
+        }
+        __syncwarp();
+        // LEAN_F32 store layout: in step it, lane l holds float4 (l & 3) of
+        // row it * 8 + (l >> 2) of the warp's 32 rows
+        const int srow0 = mb * BM + eg * 32 + (lane >> 2);
+        float4 res[4];
+        const int n00 = nb * BN + half * LCH;
+        if (LEAN == LEAN_F32 && p.residual && n00 < p.n) {
+#pragma unroll
+            for (int it = 0; it < 4; it++) {
+                const int rr = srow0 + 8 * it;
+                if (rr < p.m)
+                    res[it] = *reinterpret_cast<const float4*>(p.residual + static_cast<int64_t>(rr) * p.n + n00 +
+                                                               4 * (lane & 3));
+            }
+        }
+        const bool got = mbar_wait(&tfull[b], aph, p.err, DEVERR_TIMEOUT_EPILOGUE);
+        if (!__all_sync(0xffffffffu, got)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int i = 0; i < NCH; i++) {
+            const int c = half + EPW * i;
+            const int n0 = nb * BN + c * LCH;
+            if (n0 >= p.n) break;  // warp-uniform; n is a multiple of 16
+            if (LEAN == LEAN_F32 && p.residual && i > 0) {  // chunk 0's came before the wait
+#pragma unroll
+                for (int it = 0; it < 4; it++) {
+                    const int rr = srow0 + 8 * it;
+                    if (rr < p.m)
+                        res[it] = *reinterpret_cast<const float4*>(p.residual + static_cast<int64_t>(rr) * p.n + n0 +
+                                                                   4 * (lane & 3));
+                }
+            }
+            uint32_t r[LCH];
+            tmem_ld16(lane_base + b * BN + c * LCH, r);
+            tmem_ld_wait();
+            // the reference's chain, matmul.tkv:5,14,28
+            float y[LCH];
+#pragma unroll
+            for (int j = 0; j < LCH; j += 2) {
+                const double2 w2 = *reinterpret_cast<const double2*>(ws + i * LCH + j);
+                const double2 b2 = *reinterpret_cast<const double2*>(bs + i * LCH + j);
+                const double a0 = (KIND == GEMM_I8) ? static_cast<double>(static_cast<int>(r[j]))
+                                                    : static_cast<double>(__uint_as_float(r[j]));
+                const double a1 = (KIND == GEMM_I8) ? static_cast<double>(static_cast<int>(r[j + 1]))
+                                                    : static_cast<double>(__uint_as_float(r[j + 1]));
+                y[j] = __double2float_rn(__dadd_rn(__dmul_rn(a0, w2.x), b2.x));
+                y[j + 1] = __double2float_rn(__dadd_rn(__dmul_rn(a1, w2.y), b2.y));
+            }
+            if constexpr (LEAN == LEAN_GELU_Q8) {
+                float g[LCH];
+#pragma unroll
+                for (int j = 0; j < LCH; j++) g[j] = y[j];
+#pragma unroll
+                for (int j = 0; j < LCH; j += 2) gelu_erf_x2(g[j], g[j + 1]);
+                constexpr float M = 12582912.0f;  // 1.5 * 2^23
+                float t[LCH];
+                bool ok = true;
+#pragma unroll
+                for (int j = 0; j < LCH; j++) {
+                    const float tt = fmaf(g[j], qs.hi, M);
+                    const float d = fmaf(g[j], qs.hi, -__fsub_rn(tt, M));  // g hi - round(g hi)
+                    const float m = fmaf(fabsf(g[j]), c1, c1 + 6.103515625e-05f);
+                    ok &= fabsf(fabsf(d) - 0.5f) >= m;  // false for NaN
+                    t[j] = fminf(fmaxf(tt, M - 127.0f), M + 127.0f);
+                }
+                if (!ok) {
+                    // an element near an int8 boundary (or not finite): the
+                    // reference's own GELU and quantize decide it (unrolled:
+                    // the arrays stay in registers)
+#pragma unroll
+                    for (int j = 0; j < LCH; j++) {
+                        const float tt = fmaf(g[j], qs.hi, M);
+                        const float d = fmaf(g[j], qs.hi, -__fsub_rn(tt, M));
+                        const float m = fmaf(fabsf(g[j]), c1, c1 + 6.103515625e-05f);
+                        if (!(fabsf(fabsf(d) - 0.5f) >= m))
+                            t[j] = M + static_cast<float>(quant_exact(gelu_erf_ref(y[j]), qs));
+                    }
+                }
+                if (row_ok) {
+                    uint4 o;
+                    o.x = pack_q4(t[0], t[1], t[2], t[3]);
+                    o.y = pack_q4(t[4], t[5], t[6], t[7]);
+                    o.z = pack_q4(t[8], t[9], t[10], t[11]);
+                    o.w = pack_q4(t[12], t[13], t[14], t[15]);
+                    *reinterpret_cast<uint4*>(p.Yq + static_cast<int64_t>(row) * p.n + n0) = o;
+                }
+            } else if constexpr (LEAN == LEAN_QKV) {
+                if (row_ok) {
+                    float4* dst = reinterpret_cast<float4*>(p.Y + static_cast<int64_t>(row) * p.n + n0);
+#pragma unroll
+                    for (int q = 0; q < 4; q++) dst[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+                }
+                const int part = n0 / p.kvd;  // 0 Q, 1 K, 2 V (a chunk lies inside one 64-column head)
+                const int cc = n0 - part * p.kvd;
+                const int hh = cc / 64;
+                const int sh = kv_head_exp(p.kv_bound, p.kvd / 64, part, hh, sa);
+                const float kvf = exp2i(sh);
+                if (mb == 0 && eg == 0 && lane == 0 && cc % 64 == 0)
+                    p.kv_exp[part * (p.kvd / 64) + hh] = sh;  // one writer per head
+                if (part < 2) {
+                    uint32_t h[LCH / 2], l[LCH / 2];
+#pragma unroll
+                    for (int j = 0; j < LCH; j += 2) split_h2_pair(y[j] * kvf, y[j + 1] * kvf, h[j / 2], l[j / 2]);
+                    if (row_ok) {
+                        const int64_t ko = static_cast<int64_t>(row) * p.kvd + cc;
+                        uint4* dh = reinterpret_cast<uint4*>((part ? p.kh : p.qh) + ko);
+                        uint4* dl = reinterpret_cast<uint4*>((part ? p.kl : p.ql) + ko);
+                        dh[0] = make_uint4(h[0], h[1], h[2], h[3]);
+                        dh[1] = make_uint4(h[4], h[5], h[6], h[7]);
+                        dl[0] = make_uint4(l[0], l[1], l[2], l[3]);
+                        dl[1] = make_uint4(l[4], l[5], l[6], l[7]);
+                    }
+                } else {
+                    if (row_ok) {
+                        // V^T: column n0 + j is a row of V^T; lanes (consecutive
+                        // tokens) write consecutive addresses
+                        const int64_t vo = static_cast<int64_t>(cc) * p.vt_pitch + row;
+#pragma unroll
+                        for (int j = 0; j < LCH; j++) {
+                            const float v = y[j] * kvf;
+                            const __half hv = __float2half_rn(v);
+                            p.vth[vo + static_cast<int64_t>(j) * p.vt_pitch] = hv;
+                            p.vtl[vo + static_cast<int64_t>(j) * p.vt_pitch] = __float2half_rn(__fsub_rn(v, __half2float(hv)));
+                        }
+                    }
+                    if (p.kv_vmax) {
+                        // max over the warp's 32 rows of each of the 16 columns:
+                        // four rounds that each keep half the columns (lane bits
+                        // 16, 8, 4, 2 pick them), then lane bit 1
+                        float v[LCH];
+#pragma unroll
+                        for (int j = 0; j < LCH; j++) v[j] = row_ok ? fabsf(y[j]) : 0.0f;
+#pragma unroll
+                        for (int rd = 0, hn = LCH / 2; rd < 4; rd++, hn >>= 1) {
+                            const bool upper = (lane >> (4 - rd)) & 1;
+#pragma unroll
+                            for (int i2 = 0; i2 < LCH / 2; i2++) {
+                                if (i2 < hn) {
+                                    const float keep = upper ? v[i2 + hn] : v[i2];
+                                    const float send = upper ? v[i2] : v[i2 + hn];
+                                    v[i2] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 16 >> rd));
+                                }
+                            }
+                        }
+                        const float vm = fmaxf(v[0], __shfl_xor_sync(0xffffffffu, v[0], 1));
+                        const int cj = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+                        if ((lane & 1) == 0) atomicMax(p.kv_vmax + cc + cj, __float_as_uint(vm));
+                    }
+                }
+            } else {
+                // transpose through the warp's staging tile, then 8 rows x 64
+                // bytes per store (the residual was loaded in that layout;
+                // each element is read before the same lane stores it)
+                __syncwarp();  // the previous chunk's staging reads are done
+#pragma unroll
+                for (int q = 0; q < 4; q++)
+                    *reinterpret_cast<float4*>(stg + lane * LCH + 4 * (q ^ ((lane >> 1) & 3))) =
+                        make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+                __syncwarp();
+#pragma unroll
+                for (int it = 0; it < 4; it++) {
+                    const int rl = 8 * it + (lane >> 2), c4 = lane & 3;
+                    float4 v = *reinterpret_cast<const float4*>(stg + rl * LCH + 4 * (c4 ^ ((rl >> 1) & 3)));
+                    const int rr = srow0 + 8 * it;
+                    if (rr < p.m) {
+                        if (p.residual) {
+                            v.x = __fadd_rn(v.x, res[it].x);
+                            v.y = __fadd_rn(v.y, res[it].y);
+                            v.z = __fadd_rn(v.z, res[it].z);
+                            v.w = __fadd_rn(v.w, res[it].w);
+                        }
+                        *reinterpret_cast<float4*>(p.Y + static_cast<int64_t>(rr) * p.n + n0 + 4 * c4) = v;
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[b]);
+    }
+}
+
+template <int KIND, int BN, int LEAN>
 __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, KParams p) {
-    using C = Cfg<KIND, BN>;
+    using C = Cfg<KIND, BN, LEAN>;
     using E = EpiOf<KIND>;
     constexpr int STAGES = C::STAGES;
     constexpr int NSA = C::NSA, NSB = C::NSB;
@@ -617,7 +881,11 @@ __global__ void __launch_bounds__(EpiOf<KIND>::THREADS, 1)
             umma_commit(drain);
             mbar_wait(drain, 0, p.err, DEVERR_TIMEOUT_DRAIN);
         }
-    } else if (warp >= 4) {
+    } else if (LEAN != 0 && warp >= 4) {
+        if constexpr (LEAN != 0)
+            lean_epilogue<KIND, BN, LEAN>(p, reinterpret_cast<double*>(smem + C::RING), tfull, tempty, tmem_base, warp,
+                                          lane);
+    } else if (LEAN == 0 && warp >= 4) {
         // ------------------------------------------------ epilogue
         // phase 1: lane = row, CH consecutive columns from TMEM -> the
         //          reference epilogue in binary64, its own operations
@@ -1059,14 +1327,14 @@ int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box
     return TVQ_OK;
 }
 
-template <int KIND, int BN>
+template <int KIND, int BN, int LEAN = 0>
 int launch_tc(const KParams& p, const GemmArgs& g, int grid, cudaStream_t st) {
-    using C = Cfg<KIND, BN>;
+    using C = Cfg<KIND, BN, LEAN>;
     static int attr_done[64] = {0};  // per device
     int dev = 0;
     TVQ_CUDA(cudaGetDevice(&dev));
     if (dev < 64 && !attr_done[dev]) {
-        TVQ_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<KIND, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        TVQ_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<KIND, BN, LEAN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(C::SMEM)));
         attr_done[dev] = 1;
     }
@@ -1078,7 +1346,7 @@ int launch_tc(const KParams& p, const GemmArgs& g, int grid, cudaStream_t st) {
     if (rc) return rc;
     if (C::NSA == 1) ma2 = ma;
     if (C::NSB == 1) mb2 = mb;
-    return launch_pdl(gemm_tc_kernel<KIND, BN>, dim3(grid), dim3(EpiOf<KIND>::THREADS), C::SMEM, st, ma, mb, ma2, mb2, p);
+    return launch_pdl(gemm_tc_kernel<KIND, BN, LEAN>, dim3(grid), dim3(EpiOf<KIND>::THREADS), C::SMEM, st, ma, mb, ma2, mb2, p);
 }
 
 // Round a float to the TF32 grid (10 explicit mantissa bits), half away
@@ -1290,6 +1558,25 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     rc = get_encoder();
     if (rc) return rc;
 
+    // The lean epilogue where every output but the one it writes is off
+    // (TVQ_GEMM_LEAN=0 keeps the general one: A/B checks and tuning).
+    int lean = 0;
+    {
+        static const bool lean_off = [] {
+            const char* e = getenv("TVQ_GEMM_LEAN");
+            return e && atoi(e) == 0;
+        }();
+        const bool fold_ok = !g.per_channel || g.kind == GEMM_F8 || g.k < 33283;
+        const bool plain = (g.kind == GEMM_I8 || g.kind == GEMM_F8) && !acc_only && !asym && !g.acc_out &&
+                           !g.amax && !g.kh && g.n % 16 == 0 && fold_ok && !lean_off;
+        if (plain && g.kind == GEMM_I8 && g.act == TVQ_ACT_GELU_ERF && g.Yq && !g.Y && !g.residual) lean = LEAN_GELU_Q8;
+        if (plain && g.act == TVQ_ACT_NONE && g.Y && !g.Yq) lean = LEAN_F32;
+        // the c_attn form with the attention operands (the checks below
+        // still apply to g.kh)
+        const bool plain_kv = g.kind == GEMM_I8 && !acc_only && !asym && !g.acc_out && !g.amax && g.kh &&
+                              g.n % 16 == 0 && fold_ok && !lean_off;
+        if (plain_kv && g.act == TVQ_ACT_NONE && g.Y && !g.Yq && !g.residual) lean = LEAN_QKV;
+    }
     // Tile width: the widest N tile that still gives every SM a tile.
     int bn = g.force_bn;
     if (bn == 0) {  // TVQ_GEMM_BN=64|128|256 pins the tile width (tuning)
@@ -1334,11 +1621,31 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     const int tiles = p.num_m_blocks * p.num_n_blocks;
     const int grid = std::min(tiles, ds->sm_count);
     if (g.kind == GEMM_I8) {
+        if (lean == LEAN_GELU_Q8) {
+            if (bn == 256) return launch_tc<GEMM_I8, 256, LEAN_GELU_Q8>(p, g, grid, st);
+            if (bn == 128) return launch_tc<GEMM_I8, 128, LEAN_GELU_Q8>(p, g, grid, st);
+            return launch_tc<GEMM_I8, 64, LEAN_GELU_Q8>(p, g, grid, st);
+        }
+        if (lean == LEAN_F32) {
+            if (bn == 256) return launch_tc<GEMM_I8, 256, LEAN_F32>(p, g, grid, st);
+            if (bn == 128) return launch_tc<GEMM_I8, 128, LEAN_F32>(p, g, grid, st);
+            return launch_tc<GEMM_I8, 64, LEAN_F32>(p, g, grid, st);
+        }
+        if (lean == LEAN_QKV) {
+            if (bn == 256) return launch_tc<GEMM_I8, 256, LEAN_QKV>(p, g, grid, st);
+            if (bn == 128) return launch_tc<GEMM_I8, 128, LEAN_QKV>(p, g, grid, st);
+            return launch_tc<GEMM_I8, 64, LEAN_QKV>(p, g, grid, st);
+        }
         if (bn == 256) return launch_tc<GEMM_I8, 256>(p, g, grid, st);
         if (bn == 128) return launch_tc<GEMM_I8, 128>(p, g, grid, st);
         return launch_tc<GEMM_I8, 64>(p, g, grid, st);
     }
     if (g.kind == GEMM_F8) {
+        if (lean == LEAN_F32) {
+            if (bn == 256) return launch_tc<GEMM_F8, 256, LEAN_F32>(p, g, grid, st);
+            if (bn == 128) return launch_tc<GEMM_F8, 128, LEAN_F32>(p, g, grid, st);
+            return launch_tc<GEMM_F8, 64, LEAN_F32>(p, g, grid, st);
+        }
         if (bn == 256) return launch_tc<GEMM_F8, 256>(p, g, grid, st);
         if (bn == 128) return launch_tc<GEMM_F8, 128>(p, g, grid, st);
         return launch_tc<GEMM_F8, 64>(p, g, grid, st);
