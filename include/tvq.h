@@ -447,6 +447,27 @@ TVQ_API int tvq_session_calibrate(int64_t handle, const int64_t* ids, int ids_on
  * as the one-launch LM head). */
 TVQ_API int tvq_session_forward(int64_t handle, const int64_t* ids, int ids_on_device, float* logits,
                                 int64_t logits_len, int logits_on_device, void* stream);
+/* tvq_session_forward with host logits, queued without waiting: the call
+ * returns once the work is on `stream` (NULL: the session's own), so calls
+ * can be issued back to back and the next forward's body runs while this
+ * one's logits cross PCIe (the copy, ~206 MB per 1024-token step of GPT-2
+ * 124M, bounds the blocking form).  Before the LM head overwrites a range of
+ * the device logits, the stream waits until the previous call's copy of that
+ * range is done.  ids: host (pinned for an asynchronous copy) or device;
+ * logits: host memory (pinned), left untouched by the caller until
+ * tvq_session_wait returns.  No counterpart in the reference: its
+ * InferenceSession.run (session.tkv:3403-3436) is synchronous; each call's
+ * logits are those of tvq_session_forward on the same ids. */
+TVQ_API int tvq_session_forward_async(int64_t handle, const int64_t* ids, int ids_on_device, float* logits,
+                                      int64_t logits_len, void* stream);
+/* Makes `stream` wait (without blocking the host) until every logits copy
+ * queued by the session so far is done. */
+TVQ_API int tvq_session_join(int64_t handle, void* stream);
+/* tvq_session_join, then blocks until `stream` reaches that point and
+ * reports a device error of the queued calls (bad token ids and the like).
+ * Call it before reading the host logits and before any other call on the
+ * session. */
+TVQ_API int tvq_session_wait(int64_t handle, void* stream);
 TVQ_API int tvq_session_logits(int64_t handle, float** logits_dev, int64_t* rows, int64_t* cols);
 /* The transformer blocks alone (a CUDA graph of their own) on hidden states
  * x f32 [T, d_model] (T = the prepared layout's tokens; host or device; NULL

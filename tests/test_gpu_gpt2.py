@@ -275,6 +275,42 @@ def test_host_logits_chunked_lm_head_matches_device_forward(lengths):
     assert np.array_equal(got2.view(np.uint32), dev.view(np.uint32))
 
 
+@pytest.mark.parametrize("lengths", [[600], [100, 60]])
+def test_forward_async_back_to_back_matches_blocking_forward(lengths):
+    """Forwards queued back to back with tvq_session_forward_async, three
+    different id sets into two alternating pinned host buffers (the second
+    call's LM head waits for the first call's copies of the rows it
+    overwrites): every call's logits are the same bits as the blocking
+    forward of its ids; chunked (600 tokens) and one-launch (160) LM head."""
+    import torch
+    cfg = _small_cfg()
+    w = GPT2Weights.random(cfg, seed=12)
+    seg = segments_from_lengths(lengths)
+    T = int(seg[-1])
+    id_sets = [_ids(T, cfg.vocab, 20 + i) for i in range(3)]
+    s = GPT2Session(w, max_tokens=1024)
+    try:
+        s.prepare(seg)
+        s.calibrate(_ids(T, cfg.vocab, 3))
+        want = [s.forward(ids) for ids in id_sets]
+        rows, V = s.logits_shape()
+        ids_pin = [torch.from_numpy(ids).pin_memory() for ids in id_sets]
+        bufs = [torch.full((rows * V,), float("nan"), dtype=torch.float32).pin_memory() for _ in range(2)]
+        got = []
+        for i in range(3):
+            if i == 2:  # buffer 0 is reused: its first call must be done
+                s.wait()
+                got.append(bufs[0].numpy().reshape(rows, V).copy())
+            s.forward_async(ids_pin[i].data_ptr(), bufs[i % 2].data_ptr(), rows * V)
+        s.wait()
+        got.append(bufs[1].numpy().reshape(rows, V).copy())
+        got.append(bufs[0].numpy().reshape(rows, V).copy())
+    finally:
+        s.close()
+    for g, wnt in zip(got, want):
+        assert np.array_equal(g.view(np.uint32), wnt.view(np.uint32))
+
+
 def _assert_flip_bounded(got, ref, rows_frac=0.02):
     """Hidden states / logits within the flip-aware bounds of the module
     docstring: mean |diff| < 2e-4, at most rows_frac of the rows above 2e-3,

@@ -94,6 +94,9 @@ SIGNATURES = {
     "tvq_session_prepare": (i32, [i64, P, i64, i32]),
     "tvq_session_calibrate": (i32, [i64, P, i32, i32]),
     "tvq_session_forward": (i32, [i64, P, i32, P, i64, i32, P]),
+    "tvq_session_forward_async": (i32, [i64, P, i32, P, i64, P]),
+    "tvq_session_join": (i32, [i64, P]),
+    "tvq_session_wait": (i32, [i64, P]),
     "tvq_session_logits": (i32, [i64, P, P, P]),
     "tvq_session_run_layers": (i32, [i64, P, i32, P, i32, i32, P]),
     "tvq_dev_quantize_int4_grouped": (i32, [P, i64, i64, i64, P, P, P, P]),

@@ -534,7 +534,9 @@ __device__ __forceinline__ void lean_epilogue(const KParams& p, double* slots, u
         const bool got = mbar_wait(&tfull[b], aph, p.err, DEVERR_TIMEOUT_EPILOGUE);
         if (!__all_sync(0xffffffffu, got)) break;
         tc_fence_after();
-#pragma unroll
+        // not unrolled: the chunk body (with its rare exact path) stays small
+        // in the instruction cache; i only offsets shared memory and TMEM
+#pragma unroll 1
         for (int i = 0; i < NCH; i++) {
             const int c = half + EPW * i;
             const int n0 = nb * BN + c * LCH;

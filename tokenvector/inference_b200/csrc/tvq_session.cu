@@ -94,8 +94,9 @@ struct Session {
     int64_t extra_launches = 0;               // kernels launched beside that graph (LM head chunks)
     // host-bound logits: the copy stream and its events (created on first use)
     cudaStream_t cp = nullptr;
-    std::vector<cudaEvent_t> chunk_ev;
-    cudaEvent_t copies_done = nullptr;
+    std::vector<cudaEvent_t> chunk_ev;   // chunk c's logits are computed (on st)
+    std::vector<cudaEvent_t> copied_ev;  // chunk c's rows have been copied out (on cp)
+    cudaEvent_t copies_done = nullptr;   // every copy queued so far is done (on cp)
     // optional stage events recorded inside the captured graph (profiling)
     bool profile = false;
     std::vector<cudaEvent_t> ev;
@@ -116,6 +117,7 @@ struct Session {
         drop_graphs();
         for (cudaEvent_t e : ev) cudaEventDestroy(e);
         for (cudaEvent_t e : chunk_ev) cudaEventDestroy(e);
+        for (cudaEvent_t e : copied_ev) cudaEventDestroy(e);
         if (copies_done) cudaEventDestroy(copies_done);
         if (cp) cudaStreamDestroy(cp);
         for (void* p : allocs) cudaFree(p);
@@ -454,6 +456,60 @@ int capture(Session& s, int mode) {
     e = cudaGraphInstantiate(&s.gexec[mode], g, 0);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+    return TVQ_OK;
+}
+
+// Queue one forward whose logits go to host memory, with every copy on the
+// session's copy stream: the ids copy and the body on st, then the LM head
+// (in row chunks when there are enough rows, each chunk's copy overlapping
+// the next chunk), and copies_done recorded after the last copy.  Before
+// the LM head overwrites a range of the device logits, st waits until the
+// previous call's copy of that range is done, so calls can be queued back
+// to back (the next forward's body runs while this one's logits cross PCIe).
+int enqueue_host_logits(Session& s, const int64_t* ids, int ids_on_device, float* logits, cudaStream_t st) {
+    const int chunk_rows = logit_chunk_rows();
+    const bool chunked = s.logits_mode == 0 && chunk_rows > 0 && s.T >= 2 * chunk_rows && !s.profile;
+    const int nch = chunked ? (s.T + chunk_rows - 1) / chunk_rows : 1;
+    if (chunked && !s.gexec[M_BODY]) STEP(capture(s, M_BODY));
+    if (!chunked && !s.gexec[M_FORWARD]) STEP(capture(s, M_FORWARD));
+    if (!s.cp) TVQ_CUDA(cudaStreamCreateWithFlags(&s.cp, cudaStreamNonBlocking));
+    if (!s.copies_done) TVQ_CUDA(cudaEventCreateWithFlags(&s.copies_done, cudaEventDisableTiming));
+    while (static_cast<int>(s.chunk_ev.size()) < nch) {
+        cudaEvent_t e = nullptr, f = nullptr;
+        TVQ_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        s.chunk_ev.push_back(e);
+        TVQ_CUDA(cudaEventCreateWithFlags(&f, cudaEventDisableTiming));
+        s.copied_ev.push_back(f);
+    }
+    if (ids)
+        TVQ_CUDA(cudaMemcpyAsync(s.ids, ids, sizeof(int64_t) * s.T,
+                                 ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+    const int rows_all = static_cast<int>(s.logits_rows());
+    if (!chunked) {
+        // the LM head is inside the captured forward: it may not start
+        // before the previous call's copy has read the device logits
+        TVQ_CUDA(cudaStreamWaitEvent(st, s.copied_ev[0], 0));
+        TVQ_CUDA(cudaGraphLaunch(s.gexec[M_FORWARD], st));
+    } else {
+        TVQ_CUDA(cudaGraphLaunch(s.gexec[M_BODY], st));
+    }
+    for (int c = 0; c < nch; c++) {
+        const int r0 = chunked ? c * chunk_rows : 0;
+        const int rows = chunked ? std::min(s.T - r0, chunk_rows) : rows_all;
+        if (chunked) {
+            TVQ_CUDA(cudaStreamWaitEvent(st, s.copied_ev[c], 0));  // no-op before the first copy
+            STEP(launch_lm_head(s, r0, rows, st));
+        }
+        TVQ_CUDA(cudaEventRecord(s.chunk_ev[c], st));
+        TVQ_CUDA(cudaStreamWaitEvent(s.cp, s.chunk_ev[c], 0));
+        const size_t off = static_cast<size_t>(r0) * s.vocab;
+        TVQ_CUDA(cudaMemcpyAsync(logits + off, s.logits + off, static_cast<size_t>(rows) * s.vocab * sizeof(float),
+                                 cudaMemcpyDeviceToHost, s.cp));
+        TVQ_CUDA(cudaEventRecord(s.copied_ev[c], s.cp));
+    }
+    TVQ_CUDA(cudaEventRecord(s.copies_done, s.cp));
+    s.last_mode = chunked ? M_BODY : M_FORWARD;
+    s.extra_launches = chunked ? nch : 0;
     return TVQ_OK;
 }
 
@@ -826,35 +882,12 @@ int tvq_session_forward(int64_t handle, const int64_t* ids, int ids_on_device, f
         // captured body, and each chunk's rows are copied out on a second
         // stream while the next chunk computes (the copy, not the GEMM,
         // bounds this call)
-        if (!S->gexec[M_BODY]) STEP(capture(*S, M_BODY));
-        const int nch = (S->T + chunk_rows - 1) / chunk_rows;
-        if (!S->cp) TVQ_CUDA(cudaStreamCreateWithFlags(&S->cp, cudaStreamNonBlocking));
-        if (!S->copies_done) TVQ_CUDA(cudaEventCreateWithFlags(&S->copies_done, cudaEventDisableTiming));
-        while (static_cast<int>(S->chunk_ev.size()) < nch) {
-            cudaEvent_t e = nullptr;
-            TVQ_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-            S->chunk_ev.push_back(e);
-        }
-        if (ids)
-            TVQ_CUDA(cudaMemcpyAsync(S->ids, ids, sizeof(int64_t) * S->T,
-                                     ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
-        TVQ_CUDA(cudaGraphLaunch(S->gexec[M_BODY], st));
-        for (int c = 0; c < nch; c++) {
-            const int r0 = c * chunk_rows, rows = std::min(S->T - r0, chunk_rows);
-            STEP(launch_lm_head(*S, r0, rows, st));
-            TVQ_CUDA(cudaEventRecord(S->chunk_ev[c], st));
-            TVQ_CUDA(cudaStreamWaitEvent(S->cp, S->chunk_ev[c], 0));
-            const size_t off = static_cast<size_t>(r0) * S->vocab;
-            TVQ_CUDA(cudaMemcpyAsync(logits + off, S->logits + off, static_cast<size_t>(rows) * S->vocab * sizeof(float),
-                                     cudaMemcpyDeviceToHost, S->cp));
-        }
-        TVQ_CUDA(cudaEventRecord(S->copies_done, S->cp));
+        STEP(enqueue_host_logits(*S, ids, ids_on_device, logits, st));
         TVQ_CUDA(cudaStreamWaitEvent(st, S->copies_done, 0));
-        S->last_mode = M_BODY;
-        S->extra_launches = nch;
         return check_err(*S, st);
     }
     if (!S->gexec[M_FORWARD]) STEP(capture(*S, M_FORWARD));
+    if (S->copies_done) TVQ_CUDA(cudaStreamWaitEvent(st, S->copies_done, 0));  // a queued call's copies read the logits
     if (ids)
         TVQ_CUDA(cudaMemcpyAsync(S->ids, ids, sizeof(int64_t) * S->T,
                                  ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
@@ -866,6 +899,31 @@ int tvq_session_forward(int64_t handle, const int64_t* ids, int ids_on_device, f
                                  logits_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
     if ((ids && !ids_on_device) || (logits && !logits_on_device)) return check_err(*S, st);
     return TVQ_OK;
+}
+
+int tvq_session_forward_async(int64_t handle, const int64_t* ids, int ids_on_device, float* logits, int64_t logits_len,
+                              void* stream) {
+    SESSION(handle)
+    STEP(check_ready(*S));
+    TVQ_CHECK(logits, TVQ_ERR_INVALID, "a host logits buffer is required");
+    const size_t out_elems = static_cast<size_t>(S->logits_rows()) * S->vocab;
+    TVQ_CHECK(logits_len >= static_cast<int64_t>(out_elems), TVQ_ERR_SIZE, "logits buffer too small");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : S->st;
+    return enqueue_host_logits(*S, ids, ids_on_device, logits, st);
+}
+
+int tvq_session_join(int64_t handle, void* stream) {
+    SESSION(handle)
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : S->st;
+    if (S->copies_done) TVQ_CUDA(cudaStreamWaitEvent(st, S->copies_done, 0));
+    return TVQ_OK;
+}
+
+int tvq_session_wait(int64_t handle, void* stream) {
+    SESSION(handle)
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : S->st;
+    if (S->copies_done) TVQ_CUDA(cudaStreamWaitEvent(st, S->copies_done, 0));
+    return check_err(*S, st);
 }
 
 int tvq_session_run_layers(int64_t handle, const float* x, int x_on_device, float* y, int y_on_device, int dynamic,

@@ -302,6 +302,24 @@ class GPT2Session(_Session):
         N.call("tvq_session_forward", self.handle, _p(ids), 0, _p(out), out.size, 0, None)
         return out
 
+    def forward_async(self, ids_ptr: int, logits_ptr: int, logits_len: int, stream_ptr=None, ids_on_device=False):
+        """Queue a forward whose logits go to host memory and return at once
+        (raw pointers: pinned host ids or device ids, pinned host logits of
+        at least logits_len floats); wait() before reading the logits.
+        Consecutive calls overlap one forward's compute with the previous
+        one's logits copy."""
+        N.call("tvq_session_forward_async", self.handle, C.c_void_p(ids_ptr), 1 if ids_on_device else 0,
+               C.c_void_p(logits_ptr), logits_len, C.c_void_p(stream_ptr) if stream_ptr else None)
+
+    def join(self, stream_ptr=None):
+        """The stream waits (the host does not) for every queued logits copy."""
+        N.call("tvq_session_join", self.handle, C.c_void_p(stream_ptr) if stream_ptr else None)
+
+    def wait(self, stream_ptr=None):
+        """Block until every queued forward and its logits copy are done;
+        raises on a device error of those calls."""
+        N.call("tvq_session_wait", self.handle, C.c_void_p(stream_ptr) if stream_ptr else None)
+
     def forward_device(self, ids_dev_ptr=None, logits_dev_ptr=None, stream_ptr=None):
         """Asynchronous forward on device buffers (ints are raw pointers)."""
         N.call("tvq_session_forward", self.handle, C.c_void_p(ids_dev_ptr) if ids_dev_ptr else None, 1,
