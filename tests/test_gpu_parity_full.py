@@ -362,6 +362,45 @@ def test_config4_ragged_sample(gpt2_124m):
     assert np.allclose(last, got[seg[1:] - 1], rtol=1e-5, atol=1e-6)
 
 
+def test_config4_large_packed_batch_grouped_fixup():
+    """A packed batch large enough (13,312 tokens x 12 heads) that the exact
+    int8 fix-up of the attention context runs several rows per CTA at once
+    (the row-group form of a config-4 step): GPT-2 124M widths, two blocks,
+    ragged requests of 32 to 1024 tokens, the oracle's scales of a calibration pass on the same
+    layout; hidden states after both blocks bit for bit."""
+    import torch
+    cfg = GPT2Config(vocab=512, d_model=768, n_heads=12, n_layers=2, d_ffn=3072, max_pos=1024)
+    w = GPT2Weights.random(cfg, seed=5)
+    qw = OG.quantize_weights(w.layers)
+    rng = np.random.default_rng(45)
+    lengths = []
+    while sum(lengths) < 13312 - 1056:
+        lengths.append(int(rng.integers(32, 1025)))
+    lengths += [(13312 - sum(lengths)) // 2, 13312 - sum(lengths) - (13312 - sum(lengths)) // 2]
+    assert sum(lengths) == 13312 and all(32 <= v <= 1024 for v in lengths), lengths
+    seg = segments_from_lengths(lengths)
+    T = int(seg[-1])
+    assert T * cfg.n_heads >= 1024 * torch.cuda.get_device_properties(0).multi_processor_count
+    calib = rng.integers(0, cfg.vocab, T).astype(np.int64)
+    ids = rng.integers(0, cfg.vocab, T).astype(np.int64)
+    cal = OG.Calibrator(cfg.n_layers)
+    OG.blocks(w.layers, O.embed(calib, OG.positions(seg), w.wte, w.wpe), seg, calibrator=cal, qweights=qw,
+              n_heads=cfg.n_heads, eps=cfg.eps)
+    scales = cal.scales()
+    s = GPT2Session(w, max_tokens=T)
+    try:
+        s.prepare(seg, logits_mode=1)
+        s.set_act_scales(scales)
+        s.forward(ids)
+        hid = _hidden(s, T, cfg.d_model)
+    finally:
+        s.close()
+    x = O.embed(ids, OG.positions(seg), w.wte, w.wpe)
+    href = OG.blocks(w.layers, x, seg, scales=scales, qweights=qw, n_heads=cfg.n_heads, eps=cfg.eps)
+    nbad = int((hid.view(np.uint32) != href.view(np.uint32)).sum())
+    assert nbad == 0, (nbad, float(np.abs(hid - href).max()))
+
+
 def test_config5_three_xl_blocks_two_sequences():
     """Config 5's layer stack at the XL widths (d 1600, 25 heads, ffn 6400):
     three blocks on two 1024-token sequences of N(0,1) hidden states.  Every

@@ -894,18 +894,35 @@ constexpr int FIX_LPK = 4;                 // lanes per key
 constexpr int FIX_KPS = 32 / FIX_LPK;      // keys per warp step
 constexpr int FIX_UNROLL = 1;              // steps per load group (two groups in flight)
 constexpr int FIX_MAXC = 4;                // undecided columns per pass
+// RG row groups per CTA, each of FIX_THREADS / RG threads working on its
+// own row (its own reductions and a named barrier of its own): one group
+// (all 16 warps on a row) when the list is short and its rows long, as in
+// one 1024-token sequence; several when the list holds tens of thousands of
+// rows (a packed batch of requests), so that more rows have loads in flight.
+template <int RG>
 __global__ void __launch_bounds__(FIX_THREADS, 1) attention_fix_kernel(const float* __restrict__ qkv,
                                                                        const int4* __restrict__ rows,
                                                                        const uint2* __restrict__ masks, int* fix_n,
                                                                        int cap, int d, float* __restrict__ out,
                                                                        int8_t* __restrict__ outq,
                                                                        const float* __restrict__ qscale) {
+    static_assert(RG == 1 || RG == 2 || RG == 4 || RG == 8, "1, 2, 4 or 8 row groups");
     griddep_wait();
-    constexpr int NW = FIX_THREADS / 32;
-    constexpr int GK = NW * FIX_KPS * FIX_UNROLL;  // keys per load group of the whole block
-    __shared__ double red[NW][1 + FIX_MAXC];
-    __shared__ int next_row;
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    constexpr int NW = FIX_THREADS / 32 / RG;      // warps per row group
+    constexpr int GK = NW * FIX_KPS * FIX_UNROLL;  // keys per load group of a row group
+    __shared__ double red_all[RG][NW][1 + FIX_MAXC];
+    __shared__ int next_row_all[RG];
+    const int grp = static_cast<int>(threadIdx.x) / (32 * NW);
+    const int tid = static_cast<int>(threadIdx.x) - grp * 32 * NW, lane = tid & 31, wid = tid >> 5;
+    auto red = red_all[grp];
+    int& next_row = next_row_all[grp];
+    // the row group's barrier (named barrier 1 + grp; the whole CTA for one group)
+    auto gsync = [&]() {
+        if (RG == 1)
+            __syncthreads();
+        else
+            named_bar_sync(1 + grp, 32 * NW);
+    };
     constexpr int DPL = HD / FIX_LPK;  // dimensions per lane
     const int sub = lane & (FIX_LPK - 1), kq = lane / FIX_LPK;  // dimensions [DPL sub, DPL sub + DPL) of key slot kq
     const int n = min(*reinterpret_cast<const volatile int*>(fix_n), cap);
@@ -914,9 +931,9 @@ __global__ void __launch_bounds__(FIX_THREADS, 1) attention_fix_kernel(const flo
     // rows are taken from a counter (fix_n[1]) as CTAs become free: their key
     // counts range from 1 to the sequence length
     while (true) {
-        __syncthreads();  // next_row and red[] are free
+        gsync();  // next_row and red[] are free
         if (tid == 0) next_row = atomicAdd(fix_n + 1, 1);
-        __syncthreads();
+        gsync();
         const int ri = next_row;
         if (ri >= n) break;
         const int4 rw = rows[ri];
@@ -1024,13 +1041,13 @@ __global__ void __launch_bounds__(FIX_THREADS, 1) attention_fix_kernel(const flo
 #pragma unroll
                 for (int t = 0; t < FIX_MAXC; t++) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
             }
-            __syncthreads();  // red[] is free
+            gsync();  // red[] is free
             if (lane == 0) {
                 red[wid][0] = l;
 #pragma unroll
                 for (int t = 0; t < FIX_MAXC; t++) red[wid][1 + t] = acc[t];
             }
-            __syncthreads();
+            gsync();
             if (tid < nc) {
                 double lt = 0.0, at = 0.0;
 #pragma unroll
@@ -1047,7 +1064,7 @@ __global__ void __launch_bounds__(FIX_THREADS, 1) attention_fix_kernel(const flo
     }
     // the last CTA to finish resets the list for the next launch
     __syncthreads();
-    if (tid == 0) {
+    if (threadIdx.x == 0) {
         __threadfence();
         if (atomicAdd(fix_n + 2, 1) == static_cast<int>(gridDim.x) - 1) {
             fix_n[0] = 0;
@@ -1199,7 +1216,13 @@ int launch_attention_tc(const float* qkv, const void* qh, const void* ql, const 
     if (rc || !fixing) return rc;
     // the listed rows' undecided columns (the list length is known on the
     // device only: a persistent grid of a few CTAs per SM)
-    return launch_pdl(attention_fix_kernel, dim3(ds->sm_count), dim3(FIX_THREADS), 0, st, qkv,
+    // row groups per CTA from the layout (the list length itself is known on
+    // the device only): about 1-2 % of the (token, head) rows are listed, so
+    // a layout with more than ~16 of them per SM and group splits the CTA
+    const int64_t row_heads = static_cast<int64_t>(T) * nheads;
+    const int rg = row_heads >= 1024LL * ds->sm_count ? 4 : 1;
+    auto kern = rg == 4 ? attention_fix_kernel<4> : attention_fix_kernel<1>;
+    return launch_pdl(kern, dim3(ds->sm_count), dim3(FIX_THREADS), 0, st, qkv,
                       static_cast<const int4*>(fix->list), static_cast<const uint2*>(fix->mask), fix->n, fix->cap, d,
                       out, outq, qscale);
 }

@@ -159,6 +159,13 @@ __device__ __forceinline__ float mul_round_exact(float x, const InvScale& s) {
     return ok ? y : mul_round_slow(x, s.d);  // zero, tiny, huge, or near a midpoint
 }
 
+// An int32 as a binary64, exactly, without the conversion unit: the double
+// with high word 0x43300000 and low word a + 2^31 (a with its sign bit
+// flipped) is 2^52 + 2^31 + a, and subtracting 2^52 + 2^31 is exact.
+__device__ __forceinline__ double i32_to_f64(uint32_t a) {
+    return __hiloint2double(0x43300000, static_cast<int>(a ^ 0x80000000u)) - 4503601774854144.0;
+}
+
 // ---- pairs of floats in one 64-bit register for the f32x2 arithmetic of
 // sm_100: two independent IEEE binary32 operations per instruction, with
 // the rounding of the scalar forms (.rn unless named).

@@ -179,8 +179,8 @@ __device__ __forceinline__ void gelu_erf_x2(float& v0, float& v1) {
     P = f2_fma(P, T, f2_pack(0.254829592f, 0.254829592f));
     P = f2_mul(P, T);
     float m0, m1;
-    f2_unpack(f2_mul(f2_neg(AX), AX), m0, m1);
-    const uint64_t NEX = f2_pack(-__expf(m0), -__expf(m1));
+    f2_unpack(f2_mul(AX, AX), m0, m1);  // -(ax ax) below: the same bits as (-ax) ax
+    const uint64_t NEX = f2_pack(-__expf(-m0), -__expf(-m1));
     uint64_t E = f2_fma(NEX, P, f2_pack(1.0f, 1.0f));
     E ^= X & 0x8000000080000000ull;  // erf is odd
     f2_unpack(f2_mul(f2_mul(f2_pack(0.5f, 0.5f), V), f2_add(f2_pack(1.0f, 1.0f), E)), v0, v1);
@@ -446,10 +446,10 @@ struct Cfg {
     static constexpr uint32_t A_BYTES = BM * BK;                  // one part
     static constexpr uint32_t B_BYTES = BN * BK;
     static constexpr uint32_t STAGE_BYTES = NSA * A_BYTES + NSB * B_BYTES;
-    // LEAN_F32 stages each warp's 32 x 16 f32 chunk in shared memory (2 KB
+    // LEAN_F32 and LEAN_QKV stage each warp's 32 x 16 f32 chunk in shared memory (2 KB
     // per warp beside its 1 KB of column scales): the ring gives up stages
     // to stay within 227 KB
-    static constexpr uint32_t LEAN_EXTRA = (LEAN == 2) ? 32768u : 0u;
+    static constexpr uint32_t LEAN_EXTRA = (LEAN == 2 || LEAN == 3) ? 32768u : 0u;
     static constexpr int STAGES =
         LEAN_EXTRA ? ((232448u - 49152u - 2u * 2u * BN * 8u - 1536u) / STAGE_BYTES < 8u
                           ? (232448u - 49152u - 2u * 2u * BN * 8u - 1536u) / STAGE_BYTES : 8)
@@ -475,13 +475,13 @@ __device__ __forceinline__ void lean_epilogue(const KParams& p, double* slots, u
     constexpr int LCH = 16;            // columns per chunk
     constexpr int NCH = BN / (LCH * EPW);  // chunks per warp per tile
     static_assert(NCH >= 1 && EpiOf<KIND>::EPI_WARPS == 16, "lean epilogue: 16 warps, BN >= 64");
-    static_assert(16 * 64 * 2 * 8 + (LEAN == LEAN_F32 ? 16 * 32 * LCH * 4 : 0) <= C::EPI,
+    static_assert(16 * 64 * 2 * 8 + (LEAN != LEAN_GELU_Q8 ? 16 * 32 * LCH * 4 : 0) <= C::EPI,
                   "lean epilogue slots exceed the staging area");
     const int eg = warp & 3;
     const int half = (warp - 4) >> 2;
     double* ws = slots + (warp - 4) * 128;  // [64] scales, then [64] biases
     double* bs = ws + 64;
-    // LEAN_F32: this warp's 32 x 16 f32 staging tile (after the 16 slots);
+    // LEAN_F32, LEAN_QKV: this warp's 32 x 16 f32 staging tile (after the 16 slots);
     // float4 j of row r sits at slot j ^ ((r >> 1) & 3): conflict-free both
     // ways (lane = row when written, 4 lanes per row when read)
     float* stg = reinterpret_cast<float*>(slots + 16 * 128) + (warp - 4) * (32 * LCH);
@@ -499,6 +499,33 @@ __device__ __forceinline__ void lean_epilogue(const KParams& p, double* slots, u
         // quant_fast_t's 2^-15, and 2^-16 more) from a half-integer
         c1 = qs.hi * 1.9092130661010742e-06f;  // hi 2^-19 (1 + 2^-10)
     }
+    // f32 chunk y (lane = row) to Y rows srow0 + 8 it (+ residual res[it],
+    // loaded in the store layout): transposed through the warp's staging
+    // tile, then 8 rows x 64 bytes per store (each staged element is read
+    // before the same lane stores it)
+    auto store_f32_staged = [&](const float (&y)[LCH], int srow0, int n0, const float4 (&res)[4], bool add_res) {
+        __syncwarp();  // the previous chunk's staging reads are done
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+            *reinterpret_cast<float4*>(stg + lane * LCH + 4 * (q ^ ((lane >> 1) & 3))) =
+                make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+        __syncwarp();
+#pragma unroll
+        for (int it = 0; it < 4; it++) {
+            const int rl = 8 * it + (lane >> 2), c4 = lane & 3;
+            float4 v = *reinterpret_cast<const float4*>(stg + rl * LCH + 4 * (c4 ^ ((rl >> 1) & 3)));
+            const int rr = srow0 + 8 * it;
+            if (rr < p.m) {
+                if (add_res) {
+                    v.x = __fadd_rn(v.x, res[it].x);
+                    v.y = __fadd_rn(v.y, res[it].y);
+                    v.z = __fadd_rn(v.z, res[it].z);
+                    v.w = __fadd_rn(v.w, res[it].w);
+                }
+                *reinterpret_cast<float4*>(p.Y + static_cast<int64_t>(rr) * p.n + n0 + 4 * c4) = v;
+            }
+        }
+    };
     uint32_t tcount = 0;
     for (int tile = blockIdx.x; tile < p.num_m_blocks * p.num_n_blocks; tile += gridDim.x, tcount++) {
         const uint32_t b = tcount % C::NACC;
@@ -559,10 +586,9 @@ __device__ __forceinline__ void lean_epilogue(const KParams& p, double* slots, u
             for (int j = 0; j < LCH; j += 2) {
                 const double2 w2 = *reinterpret_cast<const double2*>(ws + i * LCH + j);
                 const double2 b2 = *reinterpret_cast<const double2*>(bs + i * LCH + j);
-                const double a0 = (KIND == GEMM_I8) ? static_cast<double>(static_cast<int>(r[j]))
-                                                    : static_cast<double>(__uint_as_float(r[j]));
-                const double a1 = (KIND == GEMM_I8) ? static_cast<double>(static_cast<int>(r[j + 1]))
-                                                    : static_cast<double>(__uint_as_float(r[j + 1]));
+                const double a0 = (KIND == GEMM_I8) ? i32_to_f64(r[j]) : static_cast<double>(__uint_as_float(r[j]));
+                const double a1 =
+                    (KIND == GEMM_I8) ? i32_to_f64(r[j + 1]) : static_cast<double>(__uint_as_float(r[j + 1]));
                 y[j] = __double2float_rn(__dadd_rn(__dmul_rn(a0, w2.x), b2.x));
                 y[j + 1] = __double2float_rn(__dadd_rn(__dmul_rn(a1, w2.y), b2.y));
             }
@@ -575,13 +601,23 @@ __device__ __forceinline__ void lean_epilogue(const KParams& p, double* slots, u
                 constexpr float M = 12582912.0f;  // 1.5 * 2^23
                 float t[LCH];
                 bool ok = true;
+                const uint64_t HI2 = f2_pack(qs.hi, qs.hi), M2 = f2_pack(M, M);
 #pragma unroll
-                for (int j = 0; j < LCH; j++) {
-                    const float tt = fmaf(g[j], qs.hi, M);
-                    const float d = fmaf(g[j], qs.hi, -__fsub_rn(tt, M));  // g hi - round(g hi)
-                    const float m = fmaf(fabsf(g[j]), c1, c1 + 6.103515625e-05f);
-                    ok &= fabsf(fabsf(d) - 0.5f) >= m;  // false for NaN
-                    t[j] = fminf(fmaxf(tt, M - 127.0f), M + 127.0f);
+                for (int j = 0; j < LCH; j += 2) {
+                    // per element: tt = fl(g hi + M), r = tt - M (exact), d =
+                    // fl(g hi - r); two elements per f32x2 instruction
+                    const uint64_t G = f2_pack(g[j], g[j + 1]);
+                    const uint64_t TT = f2_fma(G, HI2, M2);
+                    const uint64_t D = f2_fma(G, HI2, f2_sub(M2, TT));
+                    float tt[2], d[2];
+                    f2_unpack(TT, tt[0], tt[1]);
+                    f2_unpack(D, d[0], d[1]);
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const float m = fmaf(fabsf(g[j + e]), c1, c1 + 6.103515625e-05f);
+                        ok &= fabsf(fabsf(d[e]) - 0.5f) >= m;  // false for NaN
+                        t[j + e] = fminf(fmaxf(tt[e], M - 127.0f), M + 127.0f);
+                    }
                 }
                 if (!ok) {
                     // an element near an int8 boundary (or not finite): the
@@ -605,11 +641,7 @@ __device__ __forceinline__ void lean_epilogue(const KParams& p, double* slots, u
                     *reinterpret_cast<uint4*>(p.Yq + static_cast<int64_t>(row) * p.n + n0) = o;
                 }
             } else if constexpr (LEAN == LEAN_QKV) {
-                if (row_ok) {
-                    float4* dst = reinterpret_cast<float4*>(p.Y + static_cast<int64_t>(row) * p.n + n0);
-#pragma unroll
-                    for (int q = 0; q < 4; q++) dst[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
-                }
+                store_f32_staged(y, srow0, n0, res, false);
                 const int part = n0 / p.kvd;  // 0 Q, 1 K, 2 V (a chunk lies inside one 64-column head)
                 const int cc = n0 - part * p.kvd;
                 const int hh = cc / 64;
@@ -668,30 +700,7 @@ __device__ __forceinline__ void lean_epilogue(const KParams& p, double* slots, u
                     }
                 }
             } else {
-                // transpose through the warp's staging tile, then 8 rows x 64
-                // bytes per store (the residual was loaded in that layout;
-                // each element is read before the same lane stores it)
-                __syncwarp();  // the previous chunk's staging reads are done
-#pragma unroll
-                for (int q = 0; q < 4; q++)
-                    *reinterpret_cast<float4*>(stg + lane * LCH + 4 * (q ^ ((lane >> 1) & 3))) =
-                        make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
-                __syncwarp();
-#pragma unroll
-                for (int it = 0; it < 4; it++) {
-                    const int rl = 8 * it + (lane >> 2), c4 = lane & 3;
-                    float4 v = *reinterpret_cast<const float4*>(stg + rl * LCH + 4 * (c4 ^ ((rl >> 1) & 3)));
-                    const int rr = srow0 + 8 * it;
-                    if (rr < p.m) {
-                        if (p.residual) {
-                            v.x = __fadd_rn(v.x, res[it].x);
-                            v.y = __fadd_rn(v.y, res[it].y);
-                            v.z = __fadd_rn(v.z, res[it].z);
-                            v.w = __fadd_rn(v.w, res[it].w);
-                        }
-                        *reinterpret_cast<float4*>(p.Y + static_cast<int64_t>(rr) * p.n + n0 + 4 * c4) = v;
-                    }
-                }
+                store_f32_staged(y, srow0, n0, res, p.residual != nullptr);
             }
         }
         tc_fence_before();
