@@ -54,6 +54,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "tvq_common.cuh"
 #include "tvq_exact.cuh"
@@ -1218,10 +1219,20 @@ int launch_attention_tc(const float* qkv, const void* qh, const void* ql, const 
     // device only: a persistent grid of a few CTAs per SM)
     // row groups per CTA from the layout (the list length itself is known on
     // the device only): about 1-2 % of the (token, head) rows are listed, so
-    // a layout with more than ~16 of them per SM and group splits the CTA
+    // a layout of at least 1024 (token, head) rows per SM splits the CTA
     const int64_t row_heads = static_cast<int64_t>(T) * nheads;
-    const int rg = row_heads >= 1024LL * ds->sm_count ? 4 : 1;
-    auto kern = rg == 4 ? attention_fix_kernel<4> : attention_fix_kernel<1>;
+    static const int env_rg = [] {  // TVQ_FIX_GROUPS=1|2|4|8 pins the row groups (tuning)
+        const char* e = getenv("TVQ_FIX_GROUPS");
+        const int v = e ? atoi(e) : 0;
+        return (v == 1 || v == 2 || v == 4 || v == 8) ? v : 0;
+    }();
+    // (measured at config 4, 131072 packed tokens x 12 heads, attention
+    // stage per step: 26.0 / 24.5 / 24.0 ms with 2 / 4 / 8 row groups)
+    const int rg = env_rg ? env_rg : row_heads >= 1024LL * ds->sm_count ? 8 : 1;
+    auto kern = rg == 8   ? attention_fix_kernel<8>
+                : rg == 4 ? attention_fix_kernel<4>
+                : rg == 2 ? attention_fix_kernel<2>
+                          : attention_fix_kernel<1>;
     return launch_pdl(kern, dim3(ds->sm_count), dim3(FIX_THREADS), 0, st, qkv,
                       static_cast<const int4*>(fix->list), static_cast<const uint2*>(fix->mask), fix->n, fix->cap, d,
                       out, outq, qscale);

@@ -245,20 +245,30 @@ __global__ void __launch_bounds__(32 * LNW)
     const float4* g4 = reinterpret_cast<const float4*>(g);
     const float4* b4 = reinterpret_cast<const float4*>(b);
     float am = 0.0f;
-    for (int t = blockIdx.x * RPB + (WPR == 1 ? warp : 0); t < T; t += gridDim.x * RPB) {
-        const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(t) * d);
-        float4 v[NV];
+    constexpr bool KEEP = 4 * NV <= 24;  // x in binary64 registers, else converted again
+    // a warp per row with x kept in binary64: the next row's loads are issued
+    // once this row's values have been copied out of v (a warp then has two
+    // rows in flight, which its registers would not allow otherwise)
+    constexpr bool PREFETCH = WPR == 1 && KEEP;
+    const int tstep = static_cast<int>(gridDim.x) * RPB;
+    float4 v[NV];
+    auto load_row = [&](int tt) {
+        const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(tt) * d);
 #pragma unroll
         for (int j = 0; j < NV; j++) {
             const int i = j * 32 * WPR + tid;
             v[j] = (i < d4) ? __ldcs(xr + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
+    };
+    const int t0 = static_cast<int>(blockIdx.x) * RPB + (WPR == 1 ? warp : 0);
+    if (PREFETCH && t0 < T) load_row(t0);
+    for (int t = t0; t < T; t += tstep) {
+        if (!PREFETCH) load_row(t);
         // statistics in binary64 as the reference (gpt2_ref.tkv:61-78):
         // mu = sum x / d, var = sum (x - mu)^2 / d, rstd = 1 / sqrt(var + eps),
         // y = fl32(((x - mu) * rstd) * g + b) (B200 runs FP64 at half the FP32
         // rate); the sums run as a tree instead of the reference's sequence.
         // Slots past the row hold 0 and add nothing to the sum.
-        constexpr bool KEEP = 4 * NV <= 24;  // x in binary64 registers, else converted again
         double xd[KEEP ? 4 * NV : 1];
         double sum = 0.0;
 #pragma unroll
@@ -272,6 +282,7 @@ __global__ void __launch_bounds__(32 * LNW)
             }
             sum = __dadd_rn(sum, __dadd_rn(__dadd_rn(a0, a1), __dadd_rn(a2, a3)));
         }
+        if (PREFETCH && t + tstep < T) load_row(t + tstep);  // v is not read again for this row
         if constexpr (WPR == 1) sum = ln_warp_sum_d(sum);
         else sum = ln_block_sum_d(sum, redd[0], lane, warp);
         // element k of float4 j in binary64 (kept, or converted again)
