@@ -9,6 +9,7 @@ repetitions), for tuning and for small profiler captures.
   python kernel_bench.py attention --m 1024 --n 768 --heads 12
   python kernel_bench.py quantize --m 1024 --n 768
   python kernel_bench.py gpt2       # stage times of the 124M forward
+  python kernel_bench.py packed --m 16384 --reps 3   # a config-4-like packed batch, 2 blocks
   python kernel_bench.py all        # the GPT-2 124M shapes
 """
 from __future__ import annotations
@@ -277,10 +278,45 @@ def bench_gpt2(reps=20):
     return out
 
 
+def bench_packed(tokens, layers=2, reps=5):
+    """A config-4-like packed batch on GPT-2 124M widths (d 768, 12 heads, ffn
+    3072) with `layers` blocks and a small vocabulary: ragged requests of
+    U[32, 1024] tokens (seed 7) up to about `tokens`, last-token logits.  One
+    calibration forward (eager, general GEMM epilogues), then static-scale
+    forwards (CUDA graph) timed with stage events off and on.  Launch order
+    for a capture: the calibration forward's kernels, then each forward's
+    embed, and per block LayerNorm, c_attn, attention, fix-up, attn c_proj,
+    LayerNorm, c_fc, mlp c_proj."""
+    import torch
+    from tokenvector.inference_b200.gpt2 import GPT2Config, GPT2Session, GPT2Weights, segments_from_lengths
+    cfg = GPT2Config(vocab=512, d_model=768, n_heads=12, n_layers=layers, d_ffn=3072, max_pos=1024)
+    w = GPT2Weights.random(cfg, seed=1)
+    rng = np.random.default_rng(7)
+    lengths = []
+    while sum(lengths) < tokens - 1024:
+        lengths.append(int(rng.integers(32, 1025)))
+    seg = segments_from_lengths(lengths)
+    T = int(seg[-1])
+    s = GPT2Session(w, max_tokens=T)
+    s.prepare(seg, logits_mode=1)
+    s.calibrate(rng.integers(0, cfg.vocab, T).astype(np.int64))
+    _, dev, st, flush = _env()
+    ids = torch.randint(0, cfg.vocab, (T,), dtype=torch.int64, device=dev)
+    out = {"kernel": "packed", "tokens": T, "requests": len(lengths), "layers": layers}
+    for prof in (False, True):
+        s.set_profiling(prof)
+        out["forward_us_profiling" if prof else "forward_us"] = _time(
+            torch, st, flush, lambda: s.forward_device(ids.data_ptr(), None, st.cuda_stream), reps)
+        if prof:
+            out["stages_ms"] = s.stage_times()
+    s.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["gemm", "lmhead", "hbm", "sweep", "layernorm", "quantize", "attention", "gpt2",
-                                     "all"])
+                                     "packed", "all"])
     ap.add_argument("--m", type=int, default=1024)
     ap.add_argument("--n", type=int, default=768)
     ap.add_argument("--k", type=int, default=768)
@@ -308,6 +344,8 @@ def main():
         res.append(bench_attention(a.m, a.n, a.heads, a.reps))
     elif a.what == "gpt2":
         res.append(bench_gpt2(a.reps))
+    elif a.what == "packed":
+        res.append(bench_packed(a.m, reps=a.reps))
     else:
         for (n, k, ep) in [(2304, 768, "f32"), (768, 768, "f32_residual"), (3072, 768, "gelu_q"),
                            (768, 3072, "f32_residual")]:

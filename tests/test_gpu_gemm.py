@@ -413,3 +413,30 @@ def test_device_gemm_residual_f32_exact(m, n, k, in_place):
     torch.cuda.synchronize()
     want = O.add(O.matmul_int8_per_channel(A, W, bias, np.float32(0.02), sw), R)
     assert _same(Y.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("m,n,k", [(1024, 3072, 768), (300, 6400, 1600), (1, 64, 16)])
+def test_device_gemm_gelu_f32_amax(m, n, k):
+    """GELU-erf with an f32 output and max |y| (the c_fc of a calibrating
+    forward and of per-call calibration): the outputs within the fast GELU's
+    tolerance of the reference GELU of the reference dequant, and the
+    recorded max |y| equal to the largest |y| written."""
+    import torch
+    from tokenvector.inference_b200.quantization import _buf as B
+    A, W = _mats(m, n, k, 31)
+    rng = np.random.default_rng(31)
+    bias = (rng.standard_normal(n) * 0.5).astype(np.float32)
+    sw = (rng.random(n) * 2e-4 + 1e-5).astype(np.float32)
+    dev = torch.device("cuda:0")
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    tA, tW, tb, tsw = t(A), t(W), t(bias), t(sw)
+    sa = torch.tensor([0.05], dtype=torch.float32, device=dev)
+    Y = torch.empty((m, n), dtype=torch.float32, device=dev)
+    amax = torch.zeros(1, dtype=torch.int32, device=dev)
+    N.call("tvq_dev_gemm", N.GEMM_I8, B.ptr(tA), B.ptr(tW), B.ptr(tb), None, B.ptr(Y), None, m, n, k,
+           B.ptr(sa), B.ptr(tsw), 1, N.ACT_GELU_ERF, None, B.ptr(amax), B.stream_of(tA))
+    torch.cuda.synchronize()
+    want = O.gelu_erf_array(O.matmul_int8_per_channel(A, W, bias, np.float32(0.05), sw))
+    got = Y.cpu().numpy()
+    assert np.allclose(got, want, rtol=2e-6, atol=2e-6)
+    assert amax.cpu().numpy().view(np.float32)[0] == np.abs(got).max()

@@ -420,9 +420,13 @@ __device__ __forceinline__ void tile_coords(const KParams& p, int tile, int& mb,
 //                 attention's fp16 hi / lo operands: Q and K row-major, V
 //                 transposed, each head scaled by 2^kv_exp, and each V
 //                 column's max |V| (the general epilogue's kv split)
+//   LEAN_GELU_F32 y as LEAN_F32 (no residual), GELU-erf, f32 out, optional
+//                 max |y| (the c_fc of a calibrating forward or of per-call
+//                 calibration: its quantize comes after)
 constexpr int LEAN_GELU_Q8 = 1;
 constexpr int LEAN_F32 = 2;
 constexpr int LEAN_QKV = 3;
+constexpr int LEAN_GELU_F32 = 4;
 
 template <int KIND, int BN>
 __device__ __forceinline__ constexpr uint32_t make_idesc() {
@@ -449,7 +453,7 @@ struct Cfg {
     // LEAN_F32 and LEAN_QKV stage each warp's 32 x 16 f32 chunk in shared memory (2 KB
     // per warp beside its 1 KB of column scales): the ring gives up stages
     // to stay within 227 KB
-    static constexpr uint32_t LEAN_EXTRA = (LEAN == 2 || LEAN == 3) ? 32768u : 0u;
+    static constexpr uint32_t LEAN_EXTRA = (LEAN == 2 || LEAN == 3 || LEAN == 4) ? 32768u : 0u;
     static constexpr int STAGES =
         LEAN_EXTRA ? ((232448u - 49152u - 2u * 2u * BN * 8u - 1536u) / STAGE_BYTES < 8u
                           ? (232448u - 49152u - 2u * 2u * BN * 8u - 1536u) / STAGE_BYTES : 8)
@@ -503,6 +507,7 @@ __device__ __forceinline__ void lean_epilogue(const KParams& p, double* slots, u
     // loaded in the store layout): transposed through the warp's staging
     // tile, then 8 rows x 64 bytes per store (each staged element is read
     // before the same lane stores it)
+    float amax = 0.0f;  // LEAN_GELU_F32: this lane's max |y| (rows past m excluded)
     auto store_f32_staged = [&](const float (&y)[LCH], int srow0, int n0, const float4 (&res)[4], bool add_res) {
         __syncwarp();  // the previous chunk's staging reads are done
 #pragma unroll
@@ -522,28 +527,56 @@ __device__ __forceinline__ void lean_epilogue(const KParams& p, double* slots, u
                     v.z = __fadd_rn(v.z, res[it].z);
                     v.w = __fadd_rn(v.w, res[it].w);
                 }
+                if (LEAN == LEAN_GELU_F32)
+                    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
                 *reinterpret_cast<float4*>(p.Y + static_cast<int64_t>(rr) * p.n + n0 + 4 * c4) = v;
             }
         }
     };
+    // this warp's column scales and biases of a tile: lane l holds columns l
+    // and l + 32 of the warp's LCH * NCH; loaded one tile ahead, so that
+    // their latency hides behind the current tile
+    constexpr int PPL = (LCH * NCH + 31) / 32;
+    float psw[PPL], pb[PPL];
+    auto load_params = [&](int t) {
+        int tmb, tnb;
+        tile_coords(p, t, tmb, tnb);
+#pragma unroll
+        for (int q = 0; q < PPL; q++) {
+            const int j = lane + 32 * q;
+            const int n = min(tnb * BN + (half + EPW * (j / LCH)) * LCH + j % LCH, p.n - 1);
+            psw[q] = per_channel ? __ldg(p.scales_w + n) : sw0;
+            pb[q] = p.bias ? __ldg(p.bias + n) : 0.0f;
+        }
+    };
+    // (the GELU -> int8 form loads them at its tile's start instead: the
+    // prefetch registers spill there and it measured 2-3 % slower)
+    constexpr bool PREF = LEAN != LEAN_GELU_Q8;
+    const int num_tiles = p.num_m_blocks * p.num_n_blocks;
+    if (PREF && static_cast<int>(blockIdx.x) < num_tiles) load_params(blockIdx.x);
     uint32_t tcount = 0;
-    for (int tile = blockIdx.x; tile < p.num_m_blocks * p.num_n_blocks; tile += gridDim.x, tcount++) {
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, tcount++) {
         const uint32_t b = tcount % C::NACC;
         const uint32_t aph = (tcount / C::NACC) & 1u;
         int mb, nb;
         tile_coords(p, tile, mb, nb);
         const int row = mb * BM + eg * 32 + lane;
         const bool row_ok = row < p.m;
-        // this warp's column scales and biases (the previous tile's reads of
-        // the slot are done: same warp, program order)
+        // this tile's column scales and biases into the warp's slot (the
+        // previous tile's reads of the slot are done: same warp, program
+        // order), then the next tile's loads
+        if (!PREF) load_params(tile);
         __syncwarp();
-        for (int j = lane; j < LCH * NCH; j += 32) {
-            const int n = min(nb * BN + (half + EPW * (j / LCH)) * LCH + j % LCH, p.n - 1);
-            const float sw = per_channel ? __ldg(p.scales_w + n) : sw0;
-            ws[j] = static_cast<double>(sa) * static_cast<double>(sw);  // exact
-            bs[j] = static_cast<double>(p.bias ? __ldg(p.bias + n) : 0.0f);
+#pragma unroll
+        for (int q = 0; q < PPL; q++) {
+            const int j = lane + 32 * q;
+            if (j < LCH * NCH) {
+                ws[j] = static_cast<double>(sa) * static_cast<double>(psw[q]);  // exact
+                bs[j] = static_cast<double>(pb[q]);
+            }
         }
         __syncwarp();
+        if (PREF && tile + static_cast<int>(gridDim.x) < num_tiles) load_params(tile + gridDim.x);
         // LEAN_F32 store layout: in step it, lane l holds float4 (l & 3) of
         // row it * 8 + (l >> 2) of the warp's 32 rows
         const int srow0 = mb * BM + eg * 32 + (lane >> 2);
@@ -556,6 +589,18 @@ __device__ __forceinline__ void lean_epilogue(const KParams& p, double* slots, u
                 if (rr < p.m)
                     res[it] = *reinterpret_cast<const float4*>(p.residual + static_cast<int64_t>(rr) * p.n + n00 +
                                                                4 * (lane & 3));
+            }
+        }
+        // LEAN_QKV: each chunk's head exponent (two global loads) before the
+        // accumulator wait, off the chunks' critical path
+        int kv_sh[NCH];
+        if constexpr (LEAN == LEAN_QKV) {
+#pragma unroll
+            for (int i = 0; i < NCH; i++) {
+                const int n0 = nb * BN + (half + EPW * i) * LCH;
+                const int part = min(n0, p.n - 1) / p.kvd;
+                const int hh = (min(n0, p.n - 1) - part * p.kvd) / 64;
+                kv_sh[i] = kv_head_exp(p.kv_bound, p.kvd / 64, part, hh, sa);
             }
         }
         const bool got = mbar_wait(&tfull[b], aph, p.err, DEVERR_TIMEOUT_EPILOGUE);
@@ -640,12 +685,19 @@ __device__ __forceinline__ void lean_epilogue(const KParams& p, double* slots, u
                     o.w = pack_q4(t[12], t[13], t[14], t[15]);
                     *reinterpret_cast<uint4*>(p.Yq + static_cast<int64_t>(row) * p.n + n0) = o;
                 }
+            } else if constexpr (LEAN == LEAN_GELU_F32) {
+#pragma unroll
+                for (int j = 0; j < LCH; j += 2) gelu_erf_x2(y[j], y[j + 1]);
+                store_f32_staged(y, srow0, n0, res, false);
             } else if constexpr (LEAN == LEAN_QKV) {
                 store_f32_staged(y, srow0, n0, res, false);
                 const int part = n0 / p.kvd;  // 0 Q, 1 K, 2 V (a chunk lies inside one 64-column head)
                 const int cc = n0 - part * p.kvd;
                 const int hh = cc / 64;
-                const int sh = kv_head_exp(p.kv_bound, p.kvd / 64, part, hh, sa);
+                int sh = kv_sh[0];  // kv_sh[i] (the loop is rolled: select, no local-memory index)
+#pragma unroll
+                for (int i2 = 1; i2 < NCH; i2++)
+                    if (i2 == i) sh = kv_sh[i2];
                 const float kvf = exp2i(sh);
                 if (mb == 0 && eg == 0 && lane == 0 && cc % 64 == 0)
                     p.kv_exp[part * (p.kvd / 64) + hh] = sh;  // one writer per head
@@ -706,6 +758,11 @@ __device__ __forceinline__ void lean_epilogue(const KParams& p, double* slots, u
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[b]);
+    }
+    if (LEAN == LEAN_GELU_F32 && p.amax) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (lane == 0) atomicMax(p.amax, __float_as_uint(amax));
     }
 }
 
@@ -1578,10 +1635,12 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
             return e && atoi(e) == 0;
         }();
         const bool fold_ok = !g.per_channel || g.kind == GEMM_F8 || g.k < 33283;
-        const bool plain = (g.kind == GEMM_I8 || g.kind == GEMM_F8) && !acc_only && !asym && !g.acc_out &&
-                           !g.amax && !g.kh && g.n % 16 == 0 && fold_ok && !lean_off;
+        const bool plain_amax = (g.kind == GEMM_I8 || g.kind == GEMM_F8) && !acc_only && !asym && !g.acc_out &&
+                                !g.kh && g.n % 16 == 0 && fold_ok && !lean_off;
+        const bool plain = plain_amax && !g.amax;
         if (plain && g.kind == GEMM_I8 && g.act == TVQ_ACT_GELU_ERF && g.Yq && !g.Y && !g.residual) lean = LEAN_GELU_Q8;
         if (plain && g.act == TVQ_ACT_NONE && g.Y && !g.Yq) lean = LEAN_F32;
+        if (plain_amax && g.act == TVQ_ACT_GELU_ERF && g.Y && !g.Yq && !g.residual) lean = LEAN_GELU_F32;
         // the c_attn form with the attention operands (the checks below
         // still apply to g.kh)
         const bool plain_kv = g.kind == GEMM_I8 && !acc_only && !asym && !g.acc_out && !g.amax && g.kh &&
@@ -1641,6 +1700,11 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
             if (bn == 256) return launch_tc<GEMM_I8, 256, LEAN_F32>(p, g, grid, st);
             if (bn == 128) return launch_tc<GEMM_I8, 128, LEAN_F32>(p, g, grid, st);
             return launch_tc<GEMM_I8, 64, LEAN_F32>(p, g, grid, st);
+        }
+        if (lean == LEAN_GELU_F32) {
+            if (bn == 256) return launch_tc<GEMM_I8, 256, LEAN_GELU_F32>(p, g, grid, st);
+            if (bn == 128) return launch_tc<GEMM_I8, 128, LEAN_GELU_F32>(p, g, grid, st);
+            return launch_tc<GEMM_I8, 64, LEAN_GELU_F32>(p, g, grid, st);
         }
         if (lean == LEAN_QKV) {
             if (bn == 256) return launch_tc<GEMM_I8, 256, LEAN_QKV>(p, g, grid, st);
